@@ -1,0 +1,218 @@
+"""Headline benchmark: aggregate training tokens/s of asynchronous data-parallel nodes, one per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config tiny] [--impl dt|reference]
+
+For N > 1 launch with ``python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ...``.
+Each rank is one Distrain node: the tiny preset (hidden 768, 12 layers, 12 heads / 4 KV heads, SwiGLU
+2048, vocab 32768) at seq 1024 x micro-batch 32, bf16 compute with fp32 master weights and AdamW
+state, synthetic uniform-random tokens from per-rank seeds, N(0, 0.02) init. Every ``push_every``
+steps each node compresses its delta (top-k 10% + per-block INT8 with error feedback) and the
+coordinator merges the pushed deltas with 0.9^staleness x tokens weights and applies them unscaled.
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by barrier + device synchronisation,
+timed with CUDA events on the training stream; the reported time is the max over ranks. A training
+step's working set (~12 GB of activations and state) is far larger than the 126 MB L2, so no L2
+flush is inserted. ``e2e`` repeats the K steps through the public node API with a pinned-host H2D
+copy of every step's tokens and a D2H read of every step's loss.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def _parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="tiny")
+    ap.add_argument("--impl", default="dt", choices=["dt", "reference"])
+    ap.add_argument("--push-every", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-push", action="store_true", help="train only (no compression / merge)")
+    return ap.parse_args()
+
+
+def reference_unavailable(args):
+    line = {"impl": "reference",
+            "unavailable": "the reference (frane/distrain) is a Rust/Burn workspace and this image has no cargo/rustc "
+                           "toolchain, so it cannot be built or run offline"}
+    print(json.dumps(line), flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region (rank 0, all visible GPUs)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path):
+        self.path = path
+        self.proc = None
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def main():
+    args = _parse()
+    if args.impl == "reference":
+        reference_unavailable(args)
+        return 0
+    import torch
+    import torch.distributed as dist
+    from distrain_b200.config import bench_config
+    from distrain_b200.parallel.node import InBoxNode
+    from distrain_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=300))
+    run = bench_config(args.config)
+    if args.push_every:
+        run.push_every = args.push_every
+    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=not args.no_push)
+    B, S = run.micro_batch, run.seq_len
+
+    # synthetic uniform-random tokens, per-rank seed, pinned ring of host batches
+    g = torch.Generator().manual_seed(1000 + rank)
+    ring = [torch.randint(0, run.model.vocab_size, (B, S), generator=g, dtype=torch.int32).pin_memory()
+            for _ in range(4)]
+    dev_batches = [r.to(dev) for r in ring]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (also captures the CUDA graph)
+    for i in range(args.warmup):
+        node.train_step_device(dev_batches[i % 4])
+    torch.cuda.synchronize()
+    barrier()
+
+    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out", f"bench_clocks_r{rank}.csv")) if rank == 0 else None
+    if clocks:
+        os.makedirs(os.path.dirname(clocks.path), exist_ok=True)
+        clocks.start()
+        time.sleep(0.5)
+
+    ops._lib.LAUNCHES[0] = 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        node.train_step_device(dev_batches[i % 4])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = ops._lib.LAUNCHES[0]
+    ms = e0.elapsed_time(e1)
+
+    e2e_ms = None
+    if not args.no_e2e:
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        losses = node.train_steps_e2e(ring, args.steps)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = f0.elapsed_time(f1)
+    clk = clocks.stop() if clocks else None
+
+    t = torch.tensor([ms, e2e_ms or 0.0, float(launches)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms_max, launches = t[0].item(), t[1].item(), int(t[2].item())
+    node.close()
+    tokens_per_step = B * S
+    value = tokens_per_step * world * args.steps / (ms / 1e3)
+    if rank == 0:
+        out = {
+            "metric": "train tokens/sec (aggregate over GPUs, max-over-ranks time)",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (uniform-random token ids, per-rank seeds; random-init N(0,0.02) weights)",
+            "config": {"model": f"{run.name} preset ({run.model.param_count()/1e6:.1f}M params)",
+                       "global_batch": B * world, "seq_len": S, "parallelism": f"async-dp{world} (1 node per GPU)",
+                       "push_every": run.push_every if not args.no_push else None,
+                       "compression": f"top-k {run.compression.top_k_fraction:.0%} + INT8 block "
+                                      f"{run.compression.int8_block} + error feedback",
+                       "l2": "per-step working set (~12 GB) >> 126 MB L2; no flush"},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if e2e_ms is not None:
+            out["e2e"] = {"value": round(tokens_per_step * world * args.steps / (e2e_ms_max / 1e3), 1),
+                          "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 4}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,380 @@
+// Persistent tcgen05 GEMM for sm_100a:   C[M,N] (op)= alpha * sum_k A[m,k] * B[n,k]
+//
+// * Operands are bf16 in global memory, staged by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
+//   cluster multicast) into a STAGES-deep shared-memory ring; each operand may be K-major
+//   (k contiguous) or MN-major (m / n contiguous), which covers forward (X W^T), data-gradient
+//   (dY W) and weight-gradient (dY^T X) products without any transpose pass.
+// * One elected thread of warp 1 issues tcgen05.mma (M=128, N=BN, K=16, fp32 accumulate) into one
+//   of two TMEM accumulators; tcgen05.commit releases shared-memory stages and hands finished
+//   accumulators to the epilogue, so the epilogue of tile i overlaps the main loop of tile i+1.
+// * Warps 2..5 drain TMEM with tcgen05.ld (32 lanes x 32 columns per load) and write bf16, fp32,
+//   or fp32 atomically-added results (the latter for split-K and gradient accumulation).
+// * Tiles are visited by a persistent grid (one CTA per SM) in grouped order for L2 reuse.
+// Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its in-flight TMA loads and
+// MMAs, frees TMEM and returns with dt_error_word set.
+#include "common.cuh"
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int NUM_THREADS = 192;
+constexpr int GROUP_M = 16;
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ATOMIC = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  int num_kb;
+  int split_k, kb_per_split;
+  int tiles_m, tiles_n;
+  int epi;
+  float alpha;
+  void* C;
+  long long ldc;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  int group = GROUP_M * tiles_n;
+  int g = tile / group;
+  int first_m = g * GROUP_M;
+  int gm = min(tiles_m - first_m, GROUP_M);
+  int within = tile - g * group;
+  mb = first_m + within % gm;
+  nb = within / gm;
+}
+
+template <int BN, int A_MN, int B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::STAGES;
+  uint64_t* tfull = bars + 2 * C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* consumed = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_units = args.tiles_m * args.tiles_n * args.split_k;
+
+  if (warp == 0) {
+    // ───────────── TMA producer ─────────────
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+        int s = unit % args.split_k, tile = unit / args.split_k;
+        int mb, nb;
+        tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+        int m0 = mb * BM, n0 = nb * BN;
+        int kb0 = s * args.kb_per_split, kb1 = min(kb0 + args.kb_per_split, args.num_kb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, DT_ERR_TIMEOUT_EMPTY, 100, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * (64 * BK * 2), &tmA, &full[stage], m0 + 64 * j, kb * BK);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, kb * BK);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
+          }
+          ++issued;
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded) for every issued-but-unconsumed stage so no TMA write lands after exit.
+        for (int i = *consumed; i < issued; ++i) {
+          uint64_t t0 = dt_globaltimer();
+          while (!mbar_try_wait(&full[i % C::STAGES], (i / C::STAGES) & 1)) {
+            if (dt_globaltimer() - t0 > 20000000ull) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ───────────── MMA issuer ─────────────
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x, ++local) {
+        int s = unit % args.split_k;
+        int kb0 = s * args.kb_per_split, kb1 = min(kb0 + args.kb_per_split, args.num_kb);
+        int acc = local & 1;
+        uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, DT_ERR_TIMEOUT_TMEM, 200, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, DT_ERR_TIMEOUT_FULL, 201, abort_flag)) { ok = false; break; }
+          *consumed = *consumed + 1;
+          tc_fence_after();
+          uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad = A_MN ? umma_smem_desc_sw128(a_addr + k * 2048, 64 * BK * 2, 1024)
+                               : umma_smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            uint64_t bd = B_MN ? umma_smem_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
+                               : umma_smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok && issued_any) {
+        // Make sure every issued MMA has retired before TMEM is released.
+        umma_commit(drain);
+        uint64_t t0 = dt_globaltimer();
+        while (!mbar_try_wait(drain, 0)) {
+          if (dt_globaltimer() - t0 > 20000000ull) break;
+        }
+      }
+    }
+  } else {
+    // ───────────── Epilogue: warps 2..5 ─────────────
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    int local = 0;
+    for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
+      int tile = unit / args.split_k;
+      int mb, nb;
+      tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
+      int acc = local & 1;
+      uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, DT_ERR_TIMEOUT_TMEM, 300, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * BM + quad * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= args.N) continue;
+        const bool full_cols = (col0 + 32 <= args.N);
+        if (args.epi == EPI_BF16) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0;
+          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16(__uint_as_float(r[8 * v + 0]) * args.alpha, __uint_as_float(r[8 * v + 1]) * args.alpha);
+              w.y = pack_bf16(__uint_as_float(r[8 * v + 2]) * args.alpha, __uint_as_float(r[8 * v + 3]) * args.alpha);
+              w.z = pack_bf16(__uint_as_float(r[8 * v + 4]) * args.alpha, __uint_as_float(r[8 * v + 5]) * args.alpha);
+              w.w = pack_bf16(__uint_as_float(r[8 * v + 6]) * args.alpha, __uint_as_float(r[8 * v + 7]) * args.alpha);
+              reinterpret_cast<uint4*>(out)[v] = w;
+            }
+          } else {
+            for (int j = 0; j < 32 && col0 + j < args.N; ++j) out[j] = __float2bfloat16(__uint_as_float(r[j]) * args.alpha);
+          }
+        } else if (args.epi == EPI_F32) {
+          float* out = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              reinterpret_cast<float4*>(out)[v] =
+                  make_float4(__uint_as_float(r[4 * v]) * args.alpha, __uint_as_float(r[4 * v + 1]) * args.alpha,
+                              __uint_as_float(r[4 * v + 2]) * args.alpha, __uint_as_float(r[4 * v + 3]) * args.alpha);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < args.N; ++j) out[j] = __uint_as_float(r[j]) * args.alpha;
+          }
+        } else {
+          float* out = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              atomicAdd(reinterpret_cast<float4*>(out) + v,
+                        make_float4(__uint_as_float(r[4 * v]) * args.alpha, __uint_as_float(r[4 * v + 1]) * args.alpha,
+                                    __uint_as_float(r[4 * v + 2]) * args.alpha, __uint_as_float(r[4 * v + 3]) * args.alpha));
+          } else {
+            for (int j = 0; j < 32 && col0 + j < args.N; ++j) atomicAdd(out + j, __uint_as_float(r[j]) * args.alpha);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ───────────────────────────── host side ─────────────────────────────
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? 0 : -1;
+}
+
+// bf16 2-D tensor map over a row-major [outer, inner] matrix with row stride `ld` elements.
+int make_map(CUtensorMap* m, const void* ptr, long long inner, long long outer, long long ld, int box_inner,
+             int box_outer) {
+  if (get_encode()) return -2;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+int g_num_sms = 0;
+
+template <int BN, int A_MN, int B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+  using C = Cfg<BN>;
+  auto k = gemm_tc_kernel<BN, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    DT_CUDA_RET(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set = true;
+  }
+  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+// C[M,N] (op)= alpha * A[M,K] . B[N,K]^T
+//   a_mn = 0: A(m,k) at A[m*lda + k];  a_mn = 1: A(m,k) at A[k*lda + m]
+//   b_mn = 0: B(n,k) at B[n*ldb + k];  b_mn = 1: B(n,k) at B[k*ldb + n]
+//   epi: 0 bf16 store, 1 fp32 store, 2 fp32 atomic add;  split_k > 1 requires epi == 2.
+//   bn: 128 or 256 (0 = choose).  Returns 0 or a CUDA / argument error code.
+DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp,
+                        long long ldc, int M, int N, int K, int epi, float alpha, int split_k, int bn,
+                        cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((lda % 8) || (ldb % 8) || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15)) return -10;
+  if (split_k > 1 && epi != EPI_F32_ATOMIC) return -11;
+  if (!g_num_sms) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  if (bn != 128 && bn != 256) bn = (N <= 128) ? 128 : 256;
+  GemmArgs a;
+  a.M = M; a.N = N; a.K = K;
+  a.num_kb = (K + BK - 1) / BK;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (N + bn - 1) / bn;
+  int tiles = a.tiles_m * a.tiles_n;
+  if (split_k <= 0) {
+    // Auto split-K: enough work units to cover every SM when the tile count alone does not.
+    split_k = 1;
+    if (epi == EPI_F32_ATOMIC) {
+      while (tiles * split_k < g_num_sms && split_k * 2 <= a.num_kb / 4) split_k *= 2;
+    }
+  }
+  split_k = split_k < 1 ? 1 : (split_k > a.num_kb ? a.num_kb : split_k);
+  a.kb_per_split = (a.num_kb + split_k - 1) / split_k;
+  a.split_k = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
+  a.epi = epi;
+  a.alpha = alpha;
+  a.C = Cp;
+  a.ldc = ldc;
+
+  CUtensorMap ta, tb;
+  int rc;
+  rc = a_mn ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
+  if (rc) return rc;
+  rc = b_mn ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
+  if (rc) return rc;
+
+  int units = tiles * a.split_k;
+  int grid = units < g_num_sms ? units : g_num_sms;
+  if (bn == 256) {
+    if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, a, grid, stream);
+    if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, a, grid, stream);
+    if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, a, grid, stream);
+    return launch<256, 1, 1>(ta, tb, a, grid, stream);
+  } else {
+    if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, a, grid, stream);
+    if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, a, grid, stream);
+    if (a_mn && !b_mn) return launch<128, 1, 0>(ta, tb, a, grid, stream);
+    return launch<128, 1, 1>(ta, tb, a, grid, stream);
+  }
+}

@@ -1,0 +1,211 @@
+// RMSNorm forward/backward with the residual add, the embedding gather and the tied-head output
+// scale fused in, plus the embedding-gradient scatter-add.
+//
+// Reference semantics (core/model/src/model.rs:51-59): y = x * rsqrt(mean(x^2) + eps) * w, computed
+// in fp32. The residual stream is kept in fp32; the normalised output feeds the GEMMs in bf16.
+//
+// Layout: rows = B*T tokens, H columns; token row m = b*T + t reads token ids[b*S + t] (the model
+// input drops the last token of each length-S sequence, model.rs:791-794).
+#include "common.cuh"
+
+namespace {
+
+constexpr int ROWS_BWD = 32;  // rows per block in the backward (amortises dw atomics)
+
+// One block per row, each thread owns VPT float4 column groups.
+template <int VPT>
+__global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ br,
+                                       const float* __restrict__ emb, const int* __restrict__ ids, int T, int S,
+                                       const float* __restrict__ w, const float* __restrict__ scale,
+                                       float* __restrict__ out_resid, __nv_bfloat16* __restrict__ y,
+                                       float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float sh[32];
+  const long long row = blockIdx.x;
+  const float* src;
+  if (emb) {
+    long long b = row / T, t = row - b * T;
+    src = emb + (long long)ids[b * S + t] * H;
+  } else {
+    src = x + row * H;
+  }
+  float4 v[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    int c = (threadIdx.x + i * blockDim.x) * 4;
+    if (c < H) {
+      float4 a = *reinterpret_cast<const float4*>(src + c);
+      if (br) {
+        uint2 bb = *reinterpret_cast<const uint2*>(br + row * H + c);
+        float2 b0 = unpack_bf16(bb.x), b1 = unpack_bf16(bb.y);
+        a.x += b0.x; a.y += b0.y; a.z += b1.x; a.w += b1.y;
+      }
+      v[i] = a;
+      ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+      if (out_resid) *reinterpret_cast<float4*>(out_resid + row * H + c) = a;
+    } else {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  float tot = block_sum(ss, sh);
+  float r = rsqrtf(tot / (float)H + eps);
+  if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+  float s = scale ? *scale : 1.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    int c = (threadIdx.x + i * blockDim.x) * 4;
+    if (c < H) {
+      float4 ww = *reinterpret_cast<const float4*>(w + c);
+      uint2 o;
+      o.x = pack_bf16(v[i].x * r * ww.x * s, v[i].y * r * ww.y * s);
+      o.y = pack_bf16(v[i].z * r * ww.z * s, v[i].w * r * ww.w * s);
+      *reinterpret_cast<uint2*>(y + row * H + c) = o;
+    }
+  }
+}
+
+// Backward. Block handles ROWS_BWD rows; thread owns VPT float4 column groups.
+//   dy_eff = dy * s        (s = *scale if given, else 1)
+//   xhat   = x * rstd
+//   dx     = rstd * (dy_eff*w - xhat * mean(dy_eff*w*xhat))
+//   dresid_out = dresid_in + dx   (dresid_in may alias dresid_out or be null); optional bf16 copy
+//   dw    += sum_rows dy_eff * xhat                    (atomic, fp32)
+//   dscale+= sum_rows sum_cols dy * xhat * w           (atomic, fp32; only if scale given)
+template <int VPT>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
+                                   const float* __restrict__ rstd, const float* __restrict__ w,
+                                   const float* __restrict__ scale, const float* dresid_in, float* dresid_out,
+                                   __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw,
+                                   float* __restrict__ dscale, int M, int H) {
+  __shared__ float sh[32];
+  float4 wv[VPT], dwacc[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    int c = (threadIdx.x + i * blockDim.x) * 4;
+    wv[i] = (c < H) ? *reinterpret_cast<const float4*>(w + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    dwacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float s = scale ? *scale : 1.f;
+  float ds_acc = 0.f;
+  const int r0 = blockIdx.x * ROWS_BWD;
+  for (int rr = 0; rr < ROWS_BWD; ++rr) {
+    const long long row = r0 + rr;
+    if (row >= M) break;
+    const float rs = rstd[row];
+    float4 g[VPT], xh[VPT];
+    float dot = 0.f, dsd = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      int c = (threadIdx.x + i * blockDim.x) * 4;
+      if (c < H) {
+        uint2 bb = *reinterpret_cast<const uint2*>(dy + row * H + c);
+        float2 a = unpack_bf16(bb.x), b = unpack_bf16(bb.y);
+        float4 xv = *reinterpret_cast<const float4*>(x + row * H + c);
+        xh[i] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
+        g[i] = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
+        dot += g[i].x * wv[i].x * xh[i].x + g[i].y * wv[i].y * xh[i].y + g[i].z * wv[i].z * xh[i].z +
+               g[i].w * wv[i].w * xh[i].w;
+        if (dscale) dsd += a.x * xh[i].x * wv[i].x + a.y * xh[i].y * wv[i].y + b.x * xh[i].z * wv[i].z + b.y * xh[i].w * wv[i].w;
+        dwacc[i].x += g[i].x * xh[i].x; dwacc[i].y += g[i].y * xh[i].y;
+        dwacc[i].z += g[i].z * xh[i].z; dwacc[i].w += g[i].w * xh[i].w;
+      } else {
+        g[i] = xh[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mean = block_sum(dot, sh) / (float)H;
+    ds_acc += dsd;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      int c = (threadIdx.x + i * blockDim.x) * 4;
+      if (c < H) {
+        float4 d = make_float4(rs * (g[i].x * wv[i].x - xh[i].x * mean), rs * (g[i].y * wv[i].y - xh[i].y * mean),
+                               rs * (g[i].z * wv[i].z - xh[i].z * mean), rs * (g[i].w * wv[i].w - xh[i].w * mean));
+        if (dresid_in) {
+          float4 p = *reinterpret_cast<const float4*>(dresid_in + row * H + c);
+          d.x += p.x; d.y += p.y; d.z += p.z; d.w += p.w;
+        }
+        *reinterpret_cast<float4*>(dresid_out + row * H + c) = d;
+        if (dresid16) {
+          uint2 o;
+          o.x = pack_bf16(d.x, d.y);
+          o.y = pack_bf16(d.z, d.w);
+          *reinterpret_cast<uint2*>(dresid16 + row * H + c) = o;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    int c = (threadIdx.x + i * blockDim.x) * 4;
+    if (c < H) atomicAdd(reinterpret_cast<float4*>(dw + c), dwacc[i]);
+  }
+  if (dscale) {
+    float t = block_sum(ds_acc, sh);
+    if (threadIdx.x == 0) atomicAdd(dscale, t);
+  }
+}
+
+// dE[ids[row]] += g[row]   (fp32, float4 atomics)
+__global__ void embedding_bwd_kernel(const float* __restrict__ g, const int* __restrict__ ids, int T, int S,
+                                     float* __restrict__ dE, int M, int H) {
+  long long row = blockIdx.x;
+  long long b = row / T, t = row - b * T;
+  const float* src = g + row * H;
+  float* dst = dE + (long long)ids[b * S + t] * H;
+  for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4)
+    atomicAdd(reinterpret_cast<float4*>(dst + c), *reinterpret_cast<const float4*>(src + c));
+}
+
+int threads_for(int H, int vpt) {
+  int n = (H / 4 + vpt - 1) / vpt;
+  n = ((n + 31) / 32) * 32;
+  return n < 32 ? 32 : n;
+}
+
+}  // namespace
+
+// resid_out = (emb ? emb[ids] : x) + br ;  y = bf16(rmsnorm(resid_out) * w * scale)
+DT_API int dt_add_rmsnorm_fwd(const float* x, const void* br, const float* emb, const int* ids, int T, int S,
+                              const float* w, const float* scale, float* out_resid, void* y, float* rstd, int M,
+                              int H, float eps, cudaStream_t st) {
+  if (H % 4) return -10;
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(br);
+  __nv_bfloat16* yy = reinterpret_cast<__nv_bfloat16*>(y);
+  if (H <= 4096) {
+    int th = threads_for(H, 1);
+    add_rmsnorm_fwd_kernel<1><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps);
+  } else if (H <= 8192) {
+    int th = threads_for(H, 2);
+    add_rmsnorm_fwd_kernel<2><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps);
+  } else {
+    return -11;
+  }
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, const float* w, const float* scale,
+                          const float* dresid_in, float* dresid_out, void* dresid16, float* dw, float* dscale, int M,
+                          int H, cudaStream_t st) {
+  if (H % 4) return -10;
+  int blocks = (M + ROWS_BWD - 1) / ROWS_BWD;
+  const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(dy);
+  if (H <= 4096) {
+    rmsnorm_bwd_kernel<1><<<blocks, threads_for(H, 1), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out,
+                                                                reinterpret_cast<__nv_bfloat16*>(dresid16), dw,
+                                                                dscale, M, H);
+  } else if (H <= 8192) {
+    rmsnorm_bwd_kernel<2><<<blocks, threads_for(H, 2), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out,
+                                                                reinterpret_cast<__nv_bfloat16*>(dresid16), dw,
+                                                                dscale, M, H);
+  } else {
+    return -11;
+  }
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_embedding_bwd(const float* g, const int* ids, int T, int S, float* dE, int M, int H, cudaStream_t st) {
+  if (H % 4) return -10;
+  int th = H / 4 < 256 ? ((H / 4 + 31) / 32) * 32 : 256;
+  embedding_bwd_kernel<<<M, th, 0, st>>>(g, ids, T, S, dE, M, H);
+  return (int)cudaGetLastError();
+}

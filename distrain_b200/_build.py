@@ -1,0 +1,143 @@
+"""In-tree native build: CUDA kernel library (sm_100a) and C++ runtime library.
+
+* ``csrc/kernels/*.cu``  -> ``distrain_b200/lib/libdt_kernels.so``  (nvcc, ``-gencode arch=compute_100a,code=sm_100a``)
+* ``csrc/runtime/*.cpp`` -> ``distrain_b200/lib/libdt_runtime.so``  (g++, C++17, POSIX threads/sockets)
+
+Kernels are compiled as relocatable device code (``-rdc=true``) so the library-wide device error
+word defined in ``errors.cu`` is one object shared by every kernel. Objects are compiled in parallel into ``_build/`` and relinked only when a source or header changed.
+Neither library includes torch headers: they export a plain C ABI that Python binds with ctypes, so a
+kernel edit rebuilds in seconds and the same ``.so`` serves non-Python callers.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(ROOT, "csrc")
+LIBDIR = os.path.join(ROOT, "distrain_b200", "lib")
+BUILDDIR = os.path.join(ROOT, "_build")
+
+KERNELS_SO = os.path.join(LIBDIR, "libdt_kernels.so")
+RUNTIME_SO = os.path.join(LIBDIR, "libdt_runtime.so")
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _nvcc() -> str:
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if c and os.path.exists(c):
+            return c
+    raise RuntimeError("nvcc not found: the CUDA kernel library cannot be built")
+
+
+def _cuda_home() -> str:
+    return os.path.dirname(os.path.dirname(_nvcc()))
+
+
+def _newest(paths) -> float:
+    return max((os.path.getmtime(p) for p in paths), default=0.0)
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("build failed:\n" + " ".join(cmd) + "\n" + r.stdout)
+    return r.stdout
+
+
+def _compile_many(jobs, workers):
+    with cf.ThreadPoolExecutor(max_workers=workers) as ex:
+        futs = [ex.submit(_run, j) for j in jobs]
+        for f in futs:
+            f.result()
+
+
+def build_kernels(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
+    srcs = sorted(glob.glob(os.path.join(CSRC, "kernels", "*.cu")))
+    hdrs = glob.glob(os.path.join(CSRC, "kernels", "*.cuh")) + glob.glob(os.path.join(CSRC, "kernels", "*.h"))
+    os.makedirs(LIBDIR, exist_ok=True)
+    odir = os.path.join(BUILDDIR, "kernels")
+    os.makedirs(odir, exist_ok=True)
+    nvcc = _nvcc()
+    flags = ARCH_FLAGS + ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
+                          "--expt-relaxed-constexpr",
+                          "-I", os.path.join(CSRC, "kernels")] + list(extra_flags or [])
+    if os.environ.get("DT_BOUNDS_CHECK"):
+        flags.append("-DDT_BOUNDS_CHECK=1")
+    hdr_time = _newest(hdrs + [__file__])
+    jobs, objs = [], []
+    for s in srcs:
+        o = os.path.join(odir, os.path.basename(s) + ".o")
+        objs.append(o)
+        if force or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s), hdr_time):
+            jobs.append([nvcc] + flags + ["-c", s, "-o", o])
+    if jobs:
+        if verbose:
+            print(f"[build] nvcc {len(jobs)} kernel sources", file=sys.stderr)
+        _compile_many(jobs, min(len(jobs), os.cpu_count() or 4))
+    if jobs or force or not os.path.exists(KERNELS_SO) or os.path.getmtime(KERNELS_SO) < _newest(objs):
+        tmp = KERNELS_SO + ".tmp"
+        _run([nvcc] + ARCH_FLAGS + ["-shared", "-rdc=true", "-Xcompiler", "-fPIC", "-o", tmp] + objs)
+        os.replace(tmp, KERNELS_SO)
+    return KERNELS_SO
+
+
+def build_runtime(force: bool = False, verbose: bool = False) -> str:
+    srcs = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cpp")))
+    hdrs = glob.glob(os.path.join(CSRC, "runtime", "*.h")) + glob.glob(os.path.join(CSRC, "runtime", "*.hpp"))
+    os.makedirs(LIBDIR, exist_ok=True)
+    odir = os.path.join(BUILDDIR, "runtime")
+    os.makedirs(odir, exist_ok=True)
+    cxx = os.environ.get("CXX", "g++")
+    flags = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-function", "-pthread",
+             "-I", os.path.join(CSRC, "runtime")]
+    if os.environ.get("DT_SANITIZE"):
+        flags += ["-fsanitize=" + os.environ["DT_SANITIZE"], "-g", "-O1"]
+    hdr_time = _newest(hdrs + [__file__])
+    jobs, objs = [], []
+    for s in srcs:
+        o = os.path.join(odir, os.path.basename(s) + ".o")
+        objs.append(o)
+        if force or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s), hdr_time):
+            jobs.append([cxx] + flags + ["-c", s, "-o", o])
+    if not srcs:
+        return ""
+    if jobs:
+        if verbose:
+            print(f"[build] g++ {len(jobs)} runtime sources", file=sys.stderr)
+        _compile_many(jobs, min(len(jobs), os.cpu_count() or 4))
+    if jobs or force or not os.path.exists(RUNTIME_SO) or os.path.getmtime(RUNTIME_SO) < _newest(objs):
+        tmp = RUNTIME_SO + ".tmp"
+        link = [cxx, "-shared", "-pthread", "-o", tmp] + objs + ["-ldl"]
+        if os.environ.get("DT_SANITIZE"):
+            link.insert(1, "-fsanitize=" + os.environ["DT_SANITIZE"])
+        _run(link)
+        os.replace(tmp, RUNTIME_SO)
+    return RUNTIME_SO
+
+
+def kernels_stale() -> bool:
+    srcs = glob.glob(os.path.join(CSRC, "kernels", "*.cu")) + glob.glob(os.path.join(CSRC, "kernels", "*.cuh"))
+    return not os.path.exists(KERNELS_SO) or os.path.getmtime(KERNELS_SO) < _newest(srcs)
+
+
+def runtime_stale() -> bool:
+    srcs = glob.glob(os.path.join(CSRC, "runtime", "*.cpp")) + glob.glob(os.path.join(CSRC, "runtime", "*.h"))
+    return bool(srcs) and (not os.path.exists(RUNTIME_SO) or os.path.getmtime(RUNTIME_SO) < _newest(srcs))
+
+
+def build_all(force: bool = False, verbose: bool = True):
+    with cf.ThreadPoolExecutor(max_workers=2) as ex:
+        a = ex.submit(build_kernels, force, verbose)
+        b = ex.submit(build_runtime, force, verbose)
+        return a.result(), b.result()
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv)
+    print(KERNELS_SO, RUNTIME_SO)

@@ -1,0 +1,293 @@
+"""Node training engine: explicit forward + backward + AdamW over flat buffers, graph-capturable.
+
+One ``TrainEngine`` owns, for one model replica on one GPU:
+
+* ``master`` fp32 flat parameters, ``p16`` bf16 compute copy, ``grad`` fp32, AdamW ``m``/``v``;
+* every activation buffer of one micro-batch geometry (B sequences of S tokens), allocated once;
+* a device hyper-parameter block (lr, betas, eps, wd, step, bias corrections) and a device loss
+  scalar, so ``step()`` issues no host synchronisation and can be replayed from a CUDA graph.
+
+Per step (all on the current stream):
+  embed+RMSNorm -> L x [QKV GEMM, bias+RoPE, flash attention, O GEMM, add+RMSNorm, gate|up GEMM,
+  SwiGLU, down GEMM, add+RMSNorm] -> chunked tied LM head GEMM + cross-entropy (+ in-place dlogits)
+  -> backward in reverse (dgrad/wgrad tcgen05 GEMMs, norm/rope/swiglu/attention backward,
+  embedding scatter-add) -> per-tensor clip + AdamW (also refreshes ``p16``).
+
+The step mirrors the reference's continuous-loop step (node/cli/src/continuous.rs:598-637): loss on
+tokens[:, :-1] -> tokens[:, 1:], a NaN loss skips the optimiser update (decided on the device).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..ops import attention as attn_ops
+from ..config import ModelConfig, OptimConfig
+from .params import ParamLayout, init_flat
+from .oracle import rope_tables
+
+HP_LR, HP_B1, HP_B2, HP_EPS, HP_WD, HP_BC1, HP_BC2, HP_MAXNORM, HP_CLIP_GLOBAL, HP_STEP, HP_DO_UPDATE = range(11)
+
+
+class TrainEngine:
+    def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
+                 device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
+                 lm_chunk_rows: int = 8192, attn_impl: str = "dt"):
+        self.cfg = cfg
+        self.optim = optim or OptimConfig()
+        self.device = torch.device(device)
+        self.B, self.S = batch, seq_len
+        self.T = seq_len - 1
+        self.M = self.B * self.T
+        self.attn_impl = attn_impl
+        L = self.layout = ParamLayout(cfg)
+        H, F, d, nh, nkv, V = cfg.hidden_dim, cfg.ffn_hidden_dim, cfg.head_dim(), cfg.num_heads, cfg.num_kv_heads, cfg.vocab_size
+        self.H, self.F, self.d, self.nh, self.nkv, self.V = H, F, d, nh, nkv, V
+        self.W = (nh + 2 * nkv) * d
+        dev = self.device
+        f32, bf16 = torch.float32, torch.bfloat16
+        n = L.total
+        # ── parameters / optimizer state ──
+        self.master = torch.zeros(n, dtype=f32, device=dev)
+        self.p16 = torch.zeros(n, dtype=bf16, device=dev)
+        self.grad = torch.zeros(n, dtype=f32, device=dev)
+        self.m = torch.zeros(n, dtype=f32, device=dev)
+        self.v = torch.zeros(n, dtype=f32, device=dev)
+        self.cseg, self.cstart, self.cend, self.nseg = L.chunk_tables(dev)
+        self.norms = torch.zeros(self.nseg, dtype=f32, device=dev)
+        self.hp = torch.zeros(16, dtype=f32, device=dev)
+        self._hp_host = torch.zeros(16, dtype=f32).pin_memory() if dev.type == "cuda" else torch.zeros(16)
+        # ── inputs / outputs ──
+        self.ids = torch.zeros(batch, seq_len, dtype=torch.int32, device=dev)
+        self.loss = torch.zeros(4, dtype=f32, device=dev)  # [mean loss, nonfinite flag, -, -]
+        cos, sin = rope_tables(cfg, self.T)
+        self.cos, self.sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
+        # ── activations (saved for backward) ──
+        M, Lr = self.M, cfg.num_layers
+        self.resid_in = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
+        self.resid_mid = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
+        self.rstd1 = [torch.empty(M, dtype=f32, device=dev) for _ in range(Lr)]
+        self.rstd2 = [torch.empty(M, dtype=f32, device=dev) for _ in range(Lr)]
+        self.xn1 = [torch.empty(M, H, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.xn2 = [torch.empty(M, H, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.qkv = [torch.empty(M, self.W, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.attn = [torch.empty(M, nh * d, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.lse = [torch.empty(batch, nh, self.T, dtype=f32, device=dev) for _ in range(Lr)]
+        self.gu = [torch.empty(M, 2 * F, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.hact = [torch.empty(M, F, dtype=bf16, device=dev) for _ in range(Lr)]
+        self.resid_fin = torch.empty(M, H, dtype=f32, device=dev)
+        self.rstd_f = torch.empty(M, dtype=f32, device=dev)
+        self.xs = torch.empty(M, H, dtype=bf16, device=dev)
+        self.lm_chunk = min(lm_chunk_rows, M)
+        self.logits = torch.empty(self.lm_chunk, V, dtype=bf16, device=dev)
+        self.loss_rows = torch.empty(M, dtype=f32, device=dev)
+        # ── backward scratch ──
+        self.br = torch.empty(M, H, dtype=bf16, device=dev)
+        self.dresid = torch.empty(M, H, dtype=f32, device=dev)
+        self.g16 = torch.empty(M, H, dtype=bf16, device=dev)
+        self.dxs = torch.empty(M, H, dtype=bf16, device=dev)
+        self.dh = torch.empty(M, F, dtype=bf16, device=dev)
+        self.dgu = torch.empty(M, 2 * F, dtype=bf16, device=dev)
+        self.dattn = torch.empty(M, nh * d, dtype=bf16, device=dev)
+        self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
+        self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
+        self.delta = torch.empty(batch, nh, self.T, dtype=f32, device=dev)
+        # ── named views ──
+        self._bind_views()
+        if flat_init is None:
+            flat_init = init_flat(L, init_std, seed)
+        self.load_flat(flat_init)
+        self.graph = None
+        self.kernels_per_step = 0
+
+    # ───────────────────────── parameter views ─────────────────────────
+    def _bind_views(self):
+        L, cfg = self.layout, self.cfg
+        H, F, W, nh, d = self.H, self.F, self.W, self.nh, self.d
+
+        def trip(buf, prefix_dtype_views):
+            return prefix_dtype_views
+
+        self.pv, self.gv, self.wv = [], [], []
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}"
+            ent = {
+                "attn_norm": L.view(self.master, f"{p}.attn_norm.weight"),
+                "ffn_norm": L.view(self.master, f"{p}.ffn_norm.weight"),
+                "qkv_b": L.group_view(self.master, f"{p}.qkv_b") if cfg.qkv_bias else None,
+            }
+            gr = {
+                "attn_norm": L.view(self.grad, f"{p}.attn_norm.weight"),
+                "ffn_norm": L.view(self.grad, f"{p}.ffn_norm.weight"),
+                "qkv_b": L.group_view(self.grad, f"{p}.qkv_b") if cfg.qkv_bias else None,
+                "qkv_w": L.group_view(self.grad, f"{p}.qkv_w", (W, H)),
+                "o_w": L.group_view(self.grad, f"{p}.o_w", (H, nh * d)),
+                "gu_w": L.group_view(self.grad, f"{p}.gu_w", (2 * F, H)),
+                "down_w": L.group_view(self.grad, f"{p}.down_w", (H, F)),
+            }
+            w16 = {
+                "qkv_w": L.group_view(self.p16, f"{p}.qkv_w", (W, H)),
+                "o_w": L.group_view(self.p16, f"{p}.o_w", (H, nh * d)),
+                "gu_w": L.group_view(self.p16, f"{p}.gu_w", (2 * F, H)),
+                "down_w": L.group_view(self.p16, f"{p}.down_w", (H, F)),
+            }
+            self.pv.append(ent)
+            self.gv.append(gr)
+            self.wv.append(w16)
+        self.E = L.view(self.master, "embedding.embedding.weight")
+        self.E16 = L.view(self.p16, "embedding.embedding.weight")
+        self.gE = L.view(self.grad, "embedding.embedding.weight")
+        self.oscale = L.view(self.master, "embedding.output_scale")
+        self.g_oscale = L.view(self.grad, "embedding.output_scale")
+        self.fnorm = L.view(self.master, "final_norm.weight")
+        self.g_fnorm = L.view(self.grad, "final_norm.weight")
+
+    # ───────────────────────── state management ─────────────────────────
+    def load_flat(self, flat: torch.Tensor, reset_optimizer: bool = True):
+        """Replace master weights (e.g. a new global checkpoint) and optionally reset AdamW state."""
+        with torch.no_grad():
+            self.master.copy_(flat.to(self.device, non_blocking=True))
+            ops.cast_bf16(self.master, self.p16)
+            if reset_optimizer:
+                self.m.zero_()
+                self.v.zero_()
+                self.hp.zero_()
+                self._write_hp(self.optim.lr)
+
+    def _write_hp(self, lr: float):
+        o = self.optim
+        h = self._hp_host
+        h[HP_LR] = lr
+        h[HP_B1], h[HP_B2], h[HP_EPS], h[HP_WD] = o.beta1, o.beta2, o.eps, o.weight_decay
+        h[HP_MAXNORM] = o.grad_clip_norm
+        h[HP_CLIP_GLOBAL] = 1.0 if o.clip_global else 0.0
+        # copy only the configuration slots; step/bias-correction slots are device-owned
+        self.hp[:HP_BC1].copy_(h[:HP_BC1], non_blocking=True)
+        self.hp[HP_MAXNORM:HP_STEP].copy_(h[HP_MAXNORM:HP_STEP], non_blocking=True)
+
+    def set_lr(self, lr: float):
+        self._write_hp(lr)
+
+    def set_tokens(self, tokens: torch.Tensor):
+        self.ids.copy_(tokens, non_blocking=True)
+
+    # ───────────────────────── the step ─────────────────────────
+    def forward_backward(self):
+        cfg = self.cfg
+        M, H, F, T, S, W, d, nh, nkv, V = self.M, self.H, self.F, self.T, self.S, self.W, self.d, self.nh, self.nkv, self.V
+        eps = cfg.norm_eps
+        Lr = cfg.num_layers
+        self.grad.zero_()
+        # ── forward ──
+        ops.add_rmsnorm_fwd(emb=self.E, ids=self.ids, T=T, S=S, w=self.pv[0]["attn_norm"], out_resid=self.resid_in[0],
+                            y=self.xn1[0], rstd=self.rstd1[0], eps=eps, M=M, H=H)
+        for l in range(Lr):
+            pv, wv = self.pv[l], self.wv[l]
+            ops.linear_fwd(self.xn1[l], wv["qkv_w"], self.qkv[l])
+            ops.rope_fwd(self.qkv[l], pv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+            attn_ops.attention_fwd(self.qkv[l], self.attn[l], self.lse[l], B=self.B, T=T, nh=nh, nkv=nkv, d=d,
+                                   impl=self.attn_impl)
+            ops.linear_fwd(self.attn[l], wv["o_w"], self.br)
+            ops.add_rmsnorm_fwd(x=self.resid_in[l], br=self.br, w=pv["ffn_norm"], out_resid=self.resid_mid[l],
+                                y=self.xn2[l], rstd=self.rstd2[l], eps=eps, M=M, H=H)
+            ops.linear_fwd(self.xn2[l], wv["gu_w"], self.gu[l])
+            ops.swiglu_fwd(self.gu[l], self.hact[l], M=M, F=F)
+            ops.linear_fwd(self.hact[l], wv["down_w"], self.br)
+            if l + 1 < Lr:
+                ops.add_rmsnorm_fwd(x=self.resid_mid[l], br=self.br, w=self.pv[l + 1]["attn_norm"],
+                                    out_resid=self.resid_in[l + 1], y=self.xn1[l + 1], rstd=self.rstd1[l + 1], eps=eps,
+                                    M=M, H=H)
+            else:
+                ops.add_rmsnorm_fwd(x=self.resid_mid[l], br=self.br, w=self.fnorm, scale=self.oscale,
+                                    out_resid=self.resid_fin, y=self.xs, rstd=self.rstd_f, eps=eps, M=M, H=H)
+        # ── tied LM head + cross-entropy, chunked over rows; backward of the head fused per chunk ──
+        inv_m = 1.0 / M
+        for r0 in range(0, M, self.lm_chunk):
+            rows = min(self.lm_chunk, M - r0)
+            xs_c = self.xs[r0:r0 + rows]
+            lg = self.logits[:rows]
+            ops.gemm(xs_c, self.E16, lg, M=rows, N=V, K=H)
+            ops.ce_fwd_bwd(lg, self.ids, self.loss_rows[r0:r0 + rows], T=T, S=S, r0=r0, rows=rows, V=V,
+                           grad_scale=inv_m)
+            ops.gemm(lg, self.E16, self.dxs[r0:r0 + rows], M=rows, N=H, K=V, b_mn=True, ldb=H)
+            ops.gemm(lg, xs_c, self.gE, M=V, N=H, K=rows, a_mn=True, lda=V, b_mn=True, ldb=H, ldc=H,
+                     epi=ops.EPI_F32_ATOMIC)
+        ops.loss_reduce(self.loss_rows, M, inv_m, self.loss)
+        # ── backward ──
+        ops.rmsnorm_bwd(dy=self.dxs, x=self.resid_fin, rstd=self.rstd_f, w=self.fnorm, scale=self.oscale,
+                        dresid_out=self.dresid, dresid16=self.g16, dw=self.g_fnorm, dscale=self.g_oscale, M=M, H=H)
+        for l in reversed(range(Lr)):
+            pv, wv, gv = self.pv[l], self.wv[l], self.gv[l]
+            # FFN block
+            ops.linear_dgrad(self.g16, wv["down_w"], self.dh)
+            ops.linear_wgrad(self.g16, self.hact[l], gv["down_w"])
+            ops.swiglu_bwd(self.dh, self.gu[l], self.dgu, M=M, F=F)
+            ops.linear_dgrad(self.dgu, wv["gu_w"], self.br)
+            ops.linear_wgrad(self.dgu, self.xn2[l], gv["gu_w"])
+            ops.rmsnorm_bwd(dy=self.br, x=self.resid_mid[l], rstd=self.rstd2[l], w=pv["ffn_norm"],
+                            dresid_in=self.dresid, dresid_out=self.dresid, dresid16=self.g16, dw=gv["ffn_norm"],
+                            M=M, H=H)
+            # attention block
+            ops.linear_dgrad(self.g16, wv["o_w"], self.dattn)
+            ops.linear_wgrad(self.g16, self.attn[l], gv["o_w"])
+            attn_ops.attention_bwd(self.qkv[l], self.attn[l], self.dattn, self.lse[l], self.dqkv, self.dq_acc,
+                                   self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl)
+            ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+            ops.linear_dgrad(self.dqkv, wv["qkv_w"], self.br)
+            ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"])
+            ops.rmsnorm_bwd(dy=self.br, x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"],
+                            dresid_in=self.dresid, dresid_out=self.dresid, dresid16=self.g16 if l > 0 else None,
+                            dw=gv["attn_norm"], M=M, H=H)
+        ops.embedding_bwd(self.dresid, self.ids, self.gE, T=T, S=S, M=M, H=H)
+
+    def optimizer_step(self):
+        ops.adamw_step(self.master, self.grad, self.m, self.v, self.p16, self.cseg, self.cstart, self.cend,
+                       self.norms, self.hp, self.loss)
+
+    def step_kernels(self):
+        self.forward_backward()
+        self.optimizer_step()
+
+    # ───────────────────────── CUDA graph ─────────────────────────
+    def capture(self, warmup: int = 1):
+        """Capture one full train step (fwd+bwd+AdamW) as a CUDA graph; replay with ``replay()``."""
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        # warm-up on the side stream (loads modules, sets smem attributes) without touching weights
+        saved = (self.master.clone(), self.m.clone(), self.v.clone(), self.hp.clone())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.step_kernels()
+        torch.cuda.current_stream().wait_stream(s)
+        self.master.copy_(saved[0]); self.m.copy_(saved[1]); self.v.copy_(saved[2]); self.hp.copy_(saved[3])
+        ops.cast_bf16(self.master, self.p16)
+        del saved
+        g = torch.cuda.CUDAGraph()
+        from ..ops import _lib
+        n0 = _lib.LAUNCHES[0]
+        with torch.cuda.graph(g):
+            self.step_kernels()
+        self.kernels_per_step = _lib.LAUNCHES[0] - n0
+        self.graph = g
+        return g
+
+    def step(self):
+        if self.graph is not None:
+            self.graph.replay()
+            from ..ops import _lib
+            _lib.LAUNCHES[0] += self.kernels_per_step
+        else:
+            self.step_kernels()
+
+    def release_graph(self):
+        self.graph = None
+
+    # ───────────────────────── helpers ─────────────────────────
+    def state_dict(self):
+        return self.layout.to_state_dict(self.master)
+
+    def flops_per_step(self) -> float:
+        return self.cfg.flops_per_token(self.T) * self.M

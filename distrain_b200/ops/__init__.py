@@ -1,0 +1,115 @@
+"""Python entry points of the sm_100a kernel library.
+
+Each function takes torch tensors that already live on the GPU, launches the matching C-ABI
+launcher on the current stream and raises ``KernelError`` on any launch/argument failure.
+No function here allocates except where documented (``attention`` scratch is caller-provided).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import lib, check, stream_ptr, ptr, device_error, clear_device_error, KernelError  # noqa: F401
+
+EPI_BF16, EPI_F32, EPI_F32_ATOMIC = 0, 1, 2
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, *, M: int, N: int, K: int, a_mn: bool = False,
+         b_mn: bool = False, lda: int = None, ldb: int = None, ldc: int = None, epi: int = None,
+         alpha: float = 1.0, split_k: int = 0, bn: int = 0, stream=None):
+    """C[M,N] (op)= alpha * A[M,K] . B[N,K]^T on tcgen05 tensor cores.
+
+    ``a_mn`` False: A(m,k) = a[m*lda + k]; True: A(m,k) = a[k*lda + m]. Same for B with n.
+    ``epi``: EPI_BF16 (store bf16), EPI_F32 (store fp32), EPI_F32_ATOMIC (C += result, fp32; split-K allowed).
+    """
+    assert a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16
+    if epi is None:
+        epi = EPI_BF16 if c.dtype == torch.bfloat16 else EPI_F32
+    if lda is None:
+        lda = M if a_mn else K
+    if ldb is None:
+        ldb = N if b_mn else K
+    if ldc is None:
+        ldc = N
+    rc = lib().dt_gemm_bf16(a.data_ptr(), int(a_mn), lda, b.data_ptr(), int(b_mn), ldb, c.data_ptr(), ldc, M, N, K,
+                            epi, float(alpha), int(split_k), int(bn), stream_ptr(stream))
+    check(rc, "dt_gemm_bf16")
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, stream=None):
+    """out[M,N] = x[M,K] @ w[N,K]^T (bf16 in/out)."""
+    M, K = x.shape
+    N = w.shape[0]
+    gemm(x, w, out, M=M, N=N, K=K, stream=stream)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, dx: torch.Tensor, stream=None):
+    """dx[M,K] = dy[M,N] @ w[N,K]."""
+    M, N = dy.shape
+    K = w.shape[1]
+    gemm(dy, w, dx, M=M, N=K, K=N, b_mn=True, ldb=K, stream=stream)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, alpha: float = 1.0, stream=None):
+    """dw[N,K] += alpha * dy[M,N]^T @ x[M,K]   (fp32 accumulate, split-K as needed)."""
+    M, N = dy.shape
+    K = x.shape[1]
+    gemm(dy, x, dw, M=N, N=K, K=M, a_mn=True, lda=N, b_mn=True, ldb=K, ldc=K, epi=EPI_F32_ATOMIC, alpha=alpha,
+         stream=stream)
+
+
+def add_rmsnorm_fwd(*, y, rstd, w, eps, M, H, x=None, br=None, emb=None, ids=None, T=1, S=1, scale=None,
+                    out_resid=None, stream=None):
+    check(lib().dt_add_rmsnorm_fwd(ptr(x), ptr(br), ptr(emb), ptr(ids), T, S, ptr(w), ptr(scale), ptr(out_resid),
+                                   ptr(y), ptr(rstd), M, H, float(eps), stream_ptr(stream)), "dt_add_rmsnorm_fwd")
+
+
+def rmsnorm_bwd(*, dy, x, rstd, w, dresid_out, dw, M, H, scale=None, dresid_in=None, dresid16=None, dscale=None,
+                stream=None):
+    check(lib().dt_rmsnorm_bwd(ptr(dy), ptr(x), ptr(rstd), ptr(w), ptr(scale), ptr(dresid_in), ptr(dresid_out),
+                               ptr(dresid16), ptr(dw), ptr(dscale), M, H, stream_ptr(stream)), "dt_rmsnorm_bwd")
+
+
+def embedding_bwd(g, ids, dE, *, T, S, M, H, stream=None):
+    check(lib().dt_embedding_bwd(ptr(g), ptr(ids), T, S, ptr(dE), M, H, stream_ptr(stream)), "dt_embedding_bwd")
+
+
+def rope_fwd(qkv, bias, cos, sin, *, M, T, nh, nkv, d, stream=None):
+    check(lib().dt_rope_fwd(ptr(qkv), ptr(bias), ptr(cos), ptr(sin), M, T, nh, nkv, d, stream_ptr(stream)),
+          "dt_rope_fwd")
+
+
+def rope_bwd(dqkv, dbias, cos, sin, *, M, T, nh, nkv, d, stream=None):
+    check(lib().dt_rope_bwd(ptr(dqkv), ptr(dbias), ptr(cos), ptr(sin), M, T, nh, nkv, d, stream_ptr(stream)),
+          "dt_rope_bwd")
+
+
+def swiglu_fwd(gu, h, *, M, F, stream=None):
+    check(lib().dt_swiglu_fwd(ptr(gu), ptr(h), M, F, stream_ptr(stream)), "dt_swiglu_fwd")
+
+
+def swiglu_bwd(dh, gu, dgu, *, M, F, stream=None):
+    check(lib().dt_swiglu_bwd(ptr(dh), ptr(gu), ptr(dgu), M, F, stream_ptr(stream)), "dt_swiglu_bwd")
+
+
+def ce_fwd_bwd(logits, ids, loss_rows, *, T, S, r0, rows, V, ld=None, grad_scale=1.0, stream=None):
+    check(lib().dt_ce_fwd_bwd(ptr(logits), V if ld is None else ld, ptr(ids), T, S, r0, rows, ptr(loss_rows), V,
+                              float(grad_scale), stream_ptr(stream)), "dt_ce_fwd_bwd")
+
+
+def loss_reduce(loss_rows, n, scale, out, stream=None):
+    check(lib().dt_loss_reduce(ptr(loss_rows), n, float(scale), ptr(out), stream_ptr(stream)), "dt_loss_reduce")
+
+
+def adamw_step(p, g, m, v, p16, cseg, cstart, cend, norms, hp, loss_flag=None, stream=None):
+    check(lib().dt_adamw_step(ptr(p), ptr(g), ptr(m), ptr(v), ptr(p16), ptr(cseg), ptr(cstart), ptr(cend),
+                              cseg.numel(), ptr(norms), norms.numel(), ptr(hp), ptr(loss_flag), stream_ptr(stream)),
+          "dt_adamw_step")
+
+
+def seg_sqnorm(g, cseg, cstart, cend, norms, stream=None):
+    check(lib().dt_seg_sqnorm(ptr(g), ptr(cseg), ptr(cstart), ptr(cend), cseg.numel(), ptr(norms), norms.numel(),
+                              stream_ptr(stream)), "dt_seg_sqnorm")
+
+
+def cast_bf16(x, y, stream=None):
+    check(lib().dt_cast_bf16(ptr(x), ptr(y), x.numel(), stream_ptr(stream)), "dt_cast_bf16")

@@ -1,0 +1,95 @@
+"""Causal GQA attention over the fused QKV activation.
+
+``qkv`` is the [B*T, (nh+2nkv)*d] bf16 output of the QKV GEMM after bias+RoPE; query head h reads kv
+head h // (nh/nkv) (reference expand_kv_heads, model.rs:127-138, done here by indexing, never by
+materialising repeated K/V). ``out`` is [B*T, nh*d] bf16 (heads concatenated, the layout o_proj
+consumes); ``lse`` is the fp32 log-sum-exp [B, nh, T] saved for the backward.
+
+``impl="dt"`` runs the library's flash-attention kernels. ``impl="torch"`` is the plain-PyTorch
+formulation used only as a test oracle on small shapes.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import lib, check, stream_ptr, ptr, register, c_int, c_void, c_float
+
+_registered = False
+
+
+def _reg():
+    global _registered
+    if _registered:
+        return
+    register("dt_attn_fwd", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float, c_void])
+    register("dt_attn_bwd", [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
+                             c_int, c_float, c_void])
+    _registered = True
+
+
+def attention_fwd(qkv, out, lse, *, B, T, nh, nkv, d, impl="dt", stream=None):
+    scale = d ** -0.5
+    if impl == "torch":
+        o, l = _torch_fwd(qkv, B, T, nh, nkv, d)
+        out.copy_(o)
+        lse.copy_(l)
+        return
+    _reg()
+    check(lib().dt_attn_fwd(ptr(qkv), ptr(out), ptr(lse), B, T, nh, nkv, d, float(scale), stream_ptr(stream)),
+          "dt_attn_fwd")
+
+
+def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, *, B, T, nh, nkv, d, impl="dt", stream=None):
+    """dqkv <- gradients of q, k, v (same layout as qkv). ``dq_acc`` ([B*T, nh*d] fp32) and ``delta``
+    ([B, nh, T] fp32) are caller-provided scratch."""
+    scale = d ** -0.5
+    if impl == "torch":
+        dq, dk, dv = _torch_bwd(qkv, dout, B, T, nh, nkv, d)
+        W = (nh + 2 * nkv) * d
+        v = dqkv.view(B * T, W)
+        v[:, :nh * d].copy_(dq)
+        v[:, nh * d:(nh + nkv) * d].copy_(dk)
+        v[:, (nh + nkv) * d:].copy_(dv)
+        return
+    _reg()
+    check(lib().dt_attn_bwd(ptr(qkv), ptr(out), ptr(dout), ptr(lse), ptr(dqkv), ptr(dq_acc), ptr(delta), B, T, nh,
+                            nkv, d, float(scale), stream_ptr(stream)), "dt_attn_bwd")
+
+
+def _split(qkv, B, T, nh, nkv, d):
+    W = (nh + 2 * nkv) * d
+    x = qkv.view(B, T, W).float()
+    q = x[..., :nh * d].view(B, T, nh, d).transpose(1, 2)
+    k = x[..., nh * d:(nh + nkv) * d].view(B, T, nkv, d).transpose(1, 2)
+    v = x[..., (nh + nkv) * d:].view(B, T, nkv, d).transpose(1, 2)
+    return q, k, v
+
+
+def _torch_fwd(qkv, B, T, nh, nkv, d):
+    q, k, v = _split(qkv, B, T, nh, nkv, d)
+    g = nh // nkv
+    k = k.repeat_interleave(g, dim=1)
+    v = v.repeat_interleave(g, dim=1)
+    s = (q @ k.transpose(-1, -2)) * d ** -0.5
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool, device=qkv.device), 1)
+    s = s.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.softmax(s, dim=-1) @ v
+    return o.transpose(1, 2).reshape(B * T, nh * d).to(qkv.dtype), lse
+
+
+def _torch_bwd(qkv, dout, B, T, nh, nkv, d):
+    q, k, v = _split(qkv, B, T, nh, nkv, d)
+    q, k, v = q.requires_grad_(), k.requires_grad_(), v.requires_grad_()
+    with torch.enable_grad():
+        g = nh // nkv
+        kk = k.repeat_interleave(g, dim=1)
+        vv = v.repeat_interleave(g, dim=1)
+        s = (q @ kk.transpose(-1, -2)) * d ** -0.5
+        mask = torch.triu(torch.ones(T, T, dtype=torch.bool, device=qkv.device), 1)
+        s = s.masked_fill(mask, float("-inf"))
+        o = torch.softmax(s, dim=-1) @ vv
+        do = dout.view(B, T, nh, d).transpose(1, 2).float()
+        dq, dk, dv = torch.autograd.grad(o, (q, k, v), do)
+    f = lambda t, h: t.transpose(1, 2).reshape(B * T, h * d)
+    return f(dq, nh), f(dk, nkv), f(dv, nkv)

@@ -1,0 +1,89 @@
+"""In-box node runtime: one Distrain node per GPU process.
+
+``InBoxNode`` drives a ``TrainEngine`` through the reference's continuous-training semantics
+(node/cli/src/continuous.rs:379-675): train continuously, every ``push_every`` steps extract the
+round delta (round-start snapshot - current master), compress it with error feedback and hand it to
+the coordinator without stalling the training stream; when a new global checkpoint arrives, push the
+partial round, swap weights, reset AdamW and the error-feedback buffer, and start a new round.
+
+The data plane is device memory: compressed payloads sit in symmetric (peer-mapped) buffers that the
+coordinator's merge kernel reads over NVLink, and new checkpoints are written into every node's
+staging buffer by the coordinator's apply+broadcast kernel. The control plane (push metadata,
+versions, acknowledgements) goes through the process group's key-value store.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..config import RunConfig
+from ..models.engine import TrainEngine
+
+
+class InBoxNode:
+    def __init__(self, run: RunConfig, rank: int = 0, world: int = 1, device=None, enable_push: bool = True,
+                 attn_impl: str = None):
+        self.run = run
+        self.rank, self.world = rank, world
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        if attn_impl is None:
+            import os
+            attn_impl = os.environ.get("DT_ATTN_IMPL", "dt")
+        self.engine = TrainEngine(run.model, run.micro_batch, run.seq_len, optim=run.optim, device=self.device,
+                                  seed=run.seed, init_std=run.init_std, attn_impl=attn_impl)
+        self.enable_push = enable_push
+        self.step_count = 0
+        self.round_step = 0
+        self._graph_ready = False
+        self.sync = None
+        if enable_push:
+            from .inbox import InBoxSync
+            self.sync = InBoxSync(self, run, rank, world, self.device)
+
+    # ── training ──
+    def _ensure_graph(self):
+        if not self._graph_ready:
+            self.engine.capture()
+            self._graph_ready = True
+
+    def train_step_device(self, tokens_dev: torch.Tensor):
+        """One training step on tokens already resident on the device (no host sync)."""
+        self._ensure_graph()
+        if self.sync is not None:
+            self.sync.before_step()
+        self.engine.set_tokens(tokens_dev)
+        self.engine.step()
+        self.step_count += 1
+        self.round_step += 1
+        if self.sync is not None:
+            self.sync.after_step()
+
+    def train_steps_e2e(self, host_batches, steps: int):
+        """Public end-to-end loop: pinned-host tokens -> H2D -> step -> D2H loss read, every step.
+        The loss of step i is read on the host while step i+1 runs (one step of pipelining)."""
+        self._ensure_graph()
+        stream = torch.cuda.current_stream()
+        pinned_loss = torch.zeros(2, 4, dtype=torch.float32).pin_memory()
+        ev = [torch.cuda.Event(), torch.cuda.Event()]
+        losses = []
+        for i in range(steps):
+            if self.sync is not None:
+                self.sync.before_step()
+            self.engine.ids.copy_(host_batches[i % len(host_batches)], non_blocking=True)
+            self.engine.step()
+            pinned_loss[i % 2].copy_(self.engine.loss, non_blocking=True)
+            ev[i % 2].record(stream)
+            self.step_count += 1
+            self.round_step += 1
+            if self.sync is not None:
+                self.sync.after_step()
+            if i > 0:
+                ev[(i - 1) % 2].synchronize()
+                losses.append(float(pinned_loss[(i - 1) % 2][0]))
+        ev[(steps - 1) % 2].synchronize()
+        losses.append(float(pinned_loss[(steps - 1) % 2][0]))
+        return losses
+
+    def close(self):
+        if self.sync is not None:
+            self.sync.close()
+        self.engine.release_graph()

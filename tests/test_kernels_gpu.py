@@ -1,0 +1,273 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference of the same op."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from distrain_b200 import ops
+    return ops
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    ops = _ops()
+    ops.clear_device_error()
+    yield
+    torch.cuda.synchronize()
+    code, site = ops.device_error()
+    assert code == 0, f"device error {code} at site {site}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 200, 136), (1000, 768, 768), (256, 1280, 768),
+                                   (64, 40, 24)])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_bf16_out(M, N, K, a_mn, b_mn):
+    ops = _ops()
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    ref = A.float() @ B.float().t()
+    a_store = A.t().contiguous() if a_mn else A
+    b_store = B.t().contiguous() if b_mn else B
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a_store, b_store, C, M=M, N=N, K=K, a_mn=bool(a_mn), b_mn=bool(b_mn))
+    torch.cuda.synchronize()
+    assert _rel(C, ref) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("split_k", [1, 3, 0])
+def test_gemm_f32_atomic_splitk(bn, split_k):
+    ops = _ops()
+    torch.manual_seed(1)
+    M, N, K = 384, 512, 2048
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    C = torch.full((M, N), 1.0, device="cuda")
+    ops.gemm(A, B, C, M=M, N=N, K=K, epi=ops.EPI_F32_ATOMIC, split_k=split_k, bn=bn, alpha=0.5)
+    ref = 1.0 + 0.5 * (A.float() @ B.float().t())
+    torch.cuda.synchronize()
+    assert _rel(C, ref) < 1e-4
+
+
+def test_gemm_f32_store_and_large():
+    ops = _ops()
+    torch.manual_seed(2)
+    M, N, K = 4096, 4096, 1024
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    C = torch.empty(M, N, device="cuda")
+    ops.gemm(A, B, C, M=M, N=N, K=K, epi=ops.EPI_F32)
+    ref = A.float() @ B.float().t()
+    torch.cuda.synchronize()
+    assert _rel(C, ref) < 1e-4
+
+
+def test_linear_helpers():
+    ops = _ops()
+    torch.manual_seed(3)
+    M, N, K = 777, 384, 256
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(N, K, device="cuda").bfloat16()
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(N, K, device="cuda")
+    ops.linear_fwd(x, w, y)
+    ops.linear_dgrad(dy, w, dx)
+    ops.linear_wgrad(dy, x, dw)
+    torch.cuda.synchronize()
+    assert _rel(y, x.float() @ w.float().t()) < 1e-2
+    assert _rel(dx, dy.float() @ w.float()) < 1e-2
+    assert _rel(dw, dy.float().t() @ x.float()) < 1e-3
+
+
+@pytest.mark.parametrize("H", [64, 768, 2048, 5120])
+def test_add_rmsnorm_fwd_bwd(H):
+    ops = _ops()
+    torch.manual_seed(4)
+    M, eps = 97, 1e-5
+    x = torch.randn(M, H, device="cuda")
+    br = torch.randn(M, H, device="cuda").bfloat16()
+    w = torch.rand(H, device="cuda") + 0.5
+    scale = torch.tensor([1.7], device="cuda")
+    out_resid = torch.empty(M, H, device="cuda")
+    y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(M, device="cuda")
+    ops.add_rmsnorm_fwd(x=x, br=br, w=w, scale=scale, out_resid=out_resid, y=y, rstd=rstd, eps=eps, M=M, H=H)
+    r = x + br.float()
+    ref_y = r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + eps) * w * scale
+    torch.cuda.synchronize()
+    assert torch.allclose(out_resid, r)
+    assert _rel(y, ref_y) < 8e-3
+    # backward vs autograd
+    rr = r.clone().requires_grad_()
+    ww = w.clone().requires_grad_()
+    ss = scale.clone().requires_grad_()
+    out = rr * torch.rsqrt(rr.pow(2).mean(-1, keepdim=True) + eps) * ww * ss
+    dy = torch.randn(M, H, device="cuda").bfloat16()
+    out.backward(dy.float())
+    prev = torch.randn(M, H, device="cuda")
+    dres = prev.clone()
+    d16 = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(H, device="cuda")
+    ds = torch.zeros(1, device="cuda")
+    ops.rmsnorm_bwd(dy=dy, x=r, rstd=rstd, w=w, scale=scale, dresid_in=dres, dresid_out=dres, dresid16=d16, dw=dw,
+                    dscale=ds, M=M, H=H)
+    torch.cuda.synchronize()
+    assert _rel(dres, prev + rr.grad) < 1e-4
+    assert _rel(d16, prev + rr.grad) < 8e-3
+    assert _rel(dw, ww.grad) < 1e-4
+    assert _rel(ds, ss.grad) < 1e-4
+
+
+def test_embedding_gather_and_bwd():
+    ops = _ops()
+    torch.manual_seed(5)
+    B, S, V, H = 3, 17, 50, 64
+    T = S - 1
+    M = B * T
+    ids = torch.randint(0, V, (B, S), device="cuda", dtype=torch.int32)
+    E = torch.randn(V, H, device="cuda")
+    w = torch.ones(H, device="cuda")
+    resid = torch.empty(M, H, device="cuda")
+    y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(M, device="cuda")
+    ops.add_rmsnorm_fwd(emb=E, ids=ids, T=T, S=S, w=w, out_resid=resid, y=y, rstd=rstd, eps=1e-5, M=M, H=H)
+    ref = E[ids[:, :-1].long()].reshape(M, H)
+    g = torch.randn(M, H, device="cuda")
+    dE = torch.zeros(V, H, device="cuda")
+    ops.embedding_bwd(g, ids, dE, T=T, S=S, M=M, H=H)
+    ref_dE = torch.zeros(V, H, device="cuda").index_add_(0, ids[:, :-1].reshape(-1).long(), g)
+    torch.cuda.synchronize()
+    assert torch.allclose(resid, ref)
+    assert torch.allclose(dE, ref_dE, atol=1e-5)
+
+
+@pytest.mark.parametrize("nh,nkv,d", [(4, 2, 16), (12, 4, 64), (16, 4, 128)])
+def test_rope_fwd_bwd(nh, nkv, d):
+    from distrain_b200.models.oracle import apply_rope, rope_tables
+    from distrain_b200.config import ModelConfig
+    ops = _ops()
+    torch.manual_seed(6)
+    B, T = 2, 33
+    M, W = B * T, (nh + 2 * nkv) * d
+    cfg = ModelConfig(hidden_dim=nh * d, num_heads=nh, num_kv_heads=nkv, rope_theta=10000.0)
+    cos, sin = rope_tables(cfg, T)
+    cos, sin = cos.cuda(), sin.cuda()
+    qkv = torch.randn(M, W, device="cuda").bfloat16()
+    bias = torch.randn(W, device="cuda") * 0.1
+    x = (qkv.float() + bias).view(B, T, nh + 2 * nkv, d)
+    ref = torch.cat([apply_rope(x[:, :, :nh + nkv], cos, sin), x[:, :, nh + nkv:]], dim=2).reshape(M, W)
+    out = qkv.clone()
+    ops.rope_fwd(out, bias, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+    torch.cuda.synchronize()
+    assert _rel(out, ref) < 8e-3
+    # backward: gradient of sum(g * rope(x + b))
+    xx = (qkv.float()).view(B, T, nh + 2 * nkv, d).requires_grad_()
+    bb = bias.clone().requires_grad_()
+    y = xx + bb.view(nh + 2 * nkv, d)
+    y = torch.cat([apply_rope(y[:, :, :nh + nkv], cos, sin), y[:, :, nh + nkv:]], dim=2).reshape(M, W)
+    g = torch.randn(M, W, device="cuda").bfloat16()
+    y.backward(g.float())
+    dq = g.clone()
+    db = torch.zeros(W, device="cuda")
+    ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+    torch.cuda.synchronize()
+    assert _rel(dq, xx.grad.reshape(M, W)) < 8e-3
+    assert _rel(db, bb.grad) < 1e-4
+
+
+def test_swiglu_fwd_bwd():
+    ops = _ops()
+    torch.manual_seed(7)
+    M, F = 129, 256
+    gu = torch.randn(M, 2 * F, device="cuda").bfloat16()
+    h = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    ops.swiglu_fwd(gu, h, M=M, F=F)
+    g, u = gu.float()[:, :F].requires_grad_(), gu.float()[:, F:].requires_grad_()
+    ref = torch.nn.functional.silu(g) * u
+    dh = torch.randn(M, F, device="cuda").bfloat16()
+    ref.backward(dh.float())
+    dgu = torch.empty_like(gu)
+    ops.swiglu_bwd(dh, gu, dgu, M=M, F=F)
+    torch.cuda.synchronize()
+    assert _rel(h, ref) < 8e-3
+    assert _rel(dgu[:, :F], g.grad) < 1e-2
+    assert _rel(dgu[:, F:], u.grad) < 1e-2
+
+
+def test_cross_entropy():
+    ops = _ops()
+    torch.manual_seed(8)
+    B, S, V = 2, 9, 32768
+    T = S - 1
+    M = B * T
+    ids = torch.randint(0, V, (B, S), device="cuda", dtype=torch.int32)
+    z = (torch.randn(M, V, device="cuda") * 3).bfloat16()
+    zz = z.float().requires_grad_()
+    tgt = ids[:, 1:].reshape(-1).long()
+    loss = torch.nn.functional.cross_entropy(zz, tgt)
+    loss.backward()
+    rows = torch.empty(M, device="cuda")
+    zg = z.clone()
+    ops.ce_fwd_bwd(zg, ids, rows, T=T, S=S, r0=0, rows=M, V=V, grad_scale=1.0 / M)
+    out = torch.zeros(4, device="cuda")
+    ops.loss_reduce(rows, M, 1.0 / M, out)
+    torch.cuda.synchronize()
+    assert abs(out[0].item() - loss.item()) < 1e-3 * max(1.0, loss.item())
+    assert out[1].item() == 0.0
+    assert _rel(zg, zz.grad) < 1e-2
+
+
+def test_adamw_matches_reference():
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.models.oracle import AdamWRef
+    ops = _ops()
+    cfg = ModelConfig(hidden_dim=64, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=128, vocab_size=256)
+    L = ParamLayout(cfg)
+    flat = init_flat(L, 0.02, 0).cuda()
+    grads = torch.randn(L.total, device="cuda") * 0.5
+    for e in L.entries:
+        pass
+    mask = torch.zeros(L.total, dtype=torch.bool, device="cuda")
+    for e in L.entries:
+        mask[e.offset:e.offset + e.numel] = True
+    grads = grads * mask
+    p = flat.clone()
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    p16 = torch.empty(L.total, dtype=torch.bfloat16, device="cuda")
+    cseg, cstart, cend, nseg = L.chunk_tables("cuda")
+    norms = torch.zeros(nseg, device="cuda")
+    hp = torch.zeros(16, device="cuda")
+    hp[0], hp[1], hp[2], hp[3], hp[4], hp[7] = 1e-3, 0.9, 0.999, 1e-5, 0.1, 1.0
+    loss = torch.zeros(4, device="cuda")
+    ref_params = {k: t.clone() for k, t in L.views(flat.clone()).items()}
+    opt = AdamWRef(ref_params, lr=1e-3, clip=1.0)
+    for it in range(3):
+        ops.adamw_step(p, grads, m, v, p16, cseg, cstart, cend, norms, hp, loss)
+        for k, t in ref_params.items():
+            t.grad = L.view(grads, k).clone()
+        opt.step()
+    torch.cuda.synchronize()
+    got = L.views(p)
+    for k, t in ref_params.items():
+        assert torch.allclose(got[k], t, atol=1e-6, rtol=1e-5), k
+    assert torch.allclose(p16.float(), p.bfloat16().float())
+    # NaN loss flag skips the update
+    before = p.clone()
+    loss[1] = 1.0
+    ops.adamw_step(p, grads, m, v, p16, cseg, cstart, cend, norms, hp, loss)
+    torch.cuda.synchronize()
+    assert torch.equal(before, p)
