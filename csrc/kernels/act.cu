@@ -89,7 +89,7 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   // block combine (max then rescaled sum)
   int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   float wm = warp_max(m);
-  float ws = warp_sum(s * __expf(m - wm));
+  float ws = warp_sum(m == -INFINITY ? 0.f : s * __expf(m - wm));
   if (lane == 0) { sh_m[wid] = wm; sh[wid] = ws; }
   __syncthreads();
   int nw = blockDim.x >> 5;
@@ -97,7 +97,7 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
     float mm = lane < nw ? sh_m[lane] : -INFINITY;
     float ss = lane < nw ? sh[lane] : 0.f;
     float gm = warp_max(mm);
-    float gs = warp_sum(lane < nw ? ss * __expf(mm - gm) : 0.f);
+    float gs = warp_sum((lane < nw && mm != -INFINITY) ? ss * __expf(mm - gm) : 0.f);
     if (lane == 0) { sh_m[0] = gm; sh[0] = gs; }
   }
   __syncthreads();

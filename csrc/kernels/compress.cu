@@ -1,0 +1,413 @@
+// Fused delta compression for one node push, over the flat fp32 parameter buffer:
+//
+//   d   = snap - master + ef            (outer delta with error feedback; reference training.rs:50-61,
+//                                        compression.rs:68-79)
+//   snap= master                        (next round starts here)
+//   per tensor: k_s from the (adaptive, norm-proportional) budget   (compression.rs:128-159)
+//   keep the k_s largest |d| of each tensor, ties by ascending index (the reference's stable sort,
+//   compression.rs:162-167), emitted as ascending flat indices
+//   ef  = d with the kept entries zeroed  (residual of sparsification, compression.rs:82-88)
+//   values quantized to int8 with one absmax/127 fp32 scale per block of 256 kept values
+//   (per-tensor scale of the reference = a block spanning the whole tensor), round half away from zero
+//
+// Exact top-k uses a 3-level radix select on the IEEE bit pattern of |d| (bits 30..19, 18..7, 6..0),
+// with per-tensor histograms; the ordered compaction is a chunk-count / scan / write pass, so the
+// whole pipeline is a fixed number of linear passes with no sort.
+//
+// Launch split: dt_compress_begin (pass A) goes on the training stream because it reads the live
+// master weights; everything after it only touches `ef` and the payload and runs on a side stream.
+#include "common.cuh"
+
+namespace {
+
+constexpr int NB1 = 4096, NB2 = 4096, NB3 = 128;
+constexpr int SH1 = 19, SH2 = 7;
+constexpr int TPB = 256;
+
+struct SegState {
+  double sumsq;      // sum of d^2 over the segment
+  double kept_sq;    // sum of kept d^2
+  long long len;
+  long long k;       // elements to keep
+  unsigned prefix;   // resolved key prefix
+  long long krem;    // elements still to take inside the current prefix bin
+  unsigned tau;      // threshold key
+  long long take_eq; // elements with key == tau to keep (by index order)
+  float maxabs;
+  int nonfinite;
+};
+
+__device__ __forceinline__ unsigned keyof(float v) { return __float_as_uint(v) & 0x7fffffffu; }
+
+// Pass A: combined delta, snapshot refresh, per-segment stats, level-1 histogram.
+__global__ void pass_a_kernel(const float* __restrict__ master, float* __restrict__ snap, float* __restrict__ ef,
+                              const int* __restrict__ cseg, const long long* __restrict__ cstart,
+                              const long long* __restrict__ cend, SegState* seg, unsigned* __restrict__ hist1,
+                              int use_ef) {
+  __shared__ unsigned h[NB1];
+  __shared__ float shs[32];
+  for (int i = threadIdx.x; i < NB1; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int c = blockIdx.x, s = cseg[c];
+  float ss = 0.f, mx = 0.f;
+  int nf = 0;
+  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
+    float m = master[i];
+    float d = snap[i] - m + (use_ef ? ef[i] : 0.f);
+    snap[i] = m;
+    ef[i] = d;
+    if (!isfinite(d)) nf = 1;
+    ss += d * d;
+    mx = fmaxf(mx, fabsf(d));
+    atomicAdd(&h[keyof(d) >> SH1], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NB1; i += blockDim.x)
+    if (h[i]) atomicAdd(&hist1[(long long)s * NB1 + i], h[i]);
+  float tot = block_sum(ss, shs);
+  float m2 = mx;
+  for (int o = 16; o > 0; o >>= 1) m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(&seg[s].maxabs), __float_as_int(m2));
+  nf = __syncthreads_or(nf);
+  if (threadIdx.x == 0) {
+    atomicAdd(&seg[s].sumsq, (double)tot);
+    if (nf) seg[s].nonfinite = 1;
+  }
+}
+
+// Budget per segment (single block): adaptive (norm-proportional) or uniform, reference arithmetic.
+__global__ void budget_kernel(SegState* seg, int nseg, float k_fraction, int adaptive) {
+  __shared__ double tot_norm, tot_len;
+  if (threadIdx.x == 0) {
+    double tn = 0, tl = 0;
+    for (int s = 0; s < nseg; ++s) {
+      tn += sqrt(seg[s].sumsq);
+      tl += (double)seg[s].len;
+    }
+    tot_norm = tn;
+    tot_len = tl;
+  }
+  __syncthreads();
+  const double total_budget = ceil(tot_len * (double)k_fraction);
+  for (int s = threadIdx.x; s < nseg; s += blockDim.x) {
+    long long len = seg[s].len, k;
+    if (adaptive && tot_norm > 0.0) {
+      double frac = sqrt(seg[s].sumsq) / tot_norm;
+      k = (long long)ceil(total_budget * frac);
+      if (k < 1) k = 1;
+      if (k > len) k = len;
+    } else {
+      k = (long long)ceilf((float)len * k_fraction);
+      if (k < 1) k = 1;
+      if (k > len) k = len;
+    }
+    seg[s].k = k;
+    seg[s].krem = k;
+    seg[s].prefix = 0;
+  }
+}
+
+// Resolve one radix level for every segment: find the bin containing the krem-th largest key.
+// One warp per segment.
+__global__ void select_level_kernel(SegState* seg, int nseg, const unsigned* __restrict__ hist, int nbins,
+                                    int bits, int last) {
+  const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (s >= nseg) return;
+  const unsigned* hs = hist + (long long)s * nbins;
+  long long need = seg[s].krem;
+  // walk bins from the top in chunks of 32
+  long long above = 0;
+  int found = -1;
+  long long found_above = 0;
+  for (int base = nbins - 32; base >= 0 && found < 0; base -= 32) {
+    unsigned v = hs[base + lane];  // lane 31 = highest bin of this chunk
+    // inclusive suffix sum from the top within the chunk
+    unsigned suf = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      unsigned t = __shfl_down_sync(0xffffffffu, suf, o);
+      if (lane + o < 32) suf += t;
+    }
+    long long incl = above + suf;          // elements with bin >= base+lane
+    long long excl = incl - v;             // elements with bin >  base+lane
+    unsigned hit = __ballot_sync(0xffffffffu, incl >= need && excl < need);
+    if (hit) {
+      int l = 31 - __clz(hit);             // highest lane satisfying (there is exactly one)
+      found = base + l;
+      found_above = __shfl_sync(0xffffffffu, excl, l);
+    }
+    above += __shfl_sync(0xffffffffu, suf, 0);
+  }
+  if (lane == 0) {
+    if (found < 0) {  // need exceeds everything (cannot happen when k <= len); take everything
+      found = 0;
+      found_above = 0;
+    }
+    seg[s].prefix = (seg[s].prefix << bits) | (unsigned)found;
+    seg[s].krem = need - found_above;
+    if (last) {
+      seg[s].tau = seg[s].prefix;
+      seg[s].take_eq = seg[s].krem;
+    }
+  }
+}
+
+// Level-2/3 histogram over elements whose higher bits match the resolved prefix.
+template <int NB, int SHIFT_MATCH, int SHIFT_BIN>
+__global__ void hist_level_kernel(const float* __restrict__ ef, const int* __restrict__ cseg,
+                                  const long long* __restrict__ cstart, const long long* __restrict__ cend,
+                                  const SegState* seg, unsigned* __restrict__ hist) {
+  __shared__ unsigned h[NB];
+  for (int i = threadIdx.x; i < NB; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int c = blockIdx.x, s = cseg[c];
+  const unsigned pre = seg[s].prefix;
+  bool any = false;
+  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
+    unsigned k = keyof(ef[i]);
+    if ((k >> SHIFT_MATCH) == pre) {
+      atomicAdd(&h[(k >> SHIFT_BIN) & (NB - 1)], 1u);
+      any = true;
+    }
+  }
+  any = __syncthreads_or(any);
+  if (!any) return;
+  for (int i = threadIdx.x; i < NB; i += blockDim.x)
+    if (h[i]) atomicAdd(&hist[(long long)s * NB + i], h[i]);
+}
+
+// Per chunk: count of keys > tau and == tau.
+__global__ void count_kernel(const float* __restrict__ ef, const int* __restrict__ cseg,
+                             const long long* __restrict__ cstart, const long long* __restrict__ cend,
+                             const SegState* seg, long long* __restrict__ cnt_gt, long long* __restrict__ cnt_eq) {
+  const int c = blockIdx.x, s = cseg[c];
+  const unsigned tau = seg[s].tau;
+  unsigned gt = 0, eq = 0;
+  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
+    unsigned k = keyof(ef[i]);
+    gt += (k > tau);
+    eq += (k == tau);
+  }
+  __shared__ unsigned a[32], b[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    gt += __shfl_xor_sync(0xffffffffu, gt, o);
+    eq += __shfl_xor_sync(0xffffffffu, eq, o);
+  }
+  if ((threadIdx.x & 31) == 0) { a[threadIdx.x >> 5] = gt; b[threadIdx.x >> 5] = eq; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned tg = 0, te = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { tg += a[w]; te += b[w]; }
+    cnt_gt[c] = tg;
+    cnt_eq[c] = te;
+  }
+}
+
+// Single block: eq quota per chunk (in index order within each segment) and global output offsets.
+__global__ void scan_kernel(const int* __restrict__ cseg, int nchunks, const SegState* seg,
+                            const long long* __restrict__ cnt_gt, const long long* __restrict__ cnt_eq,
+                            long long* __restrict__ eq_take, long long* __restrict__ out_off,
+                            long long* __restrict__ total) {
+  if (threadIdx.x != 0) return;
+  long long off = 0, eq_seen = 0;
+  int cur = -1;
+  for (int c = 0; c < nchunks; ++c) {
+    int s = cseg[c];
+    if (s != cur) { cur = s; eq_seen = 0; }
+    long long quota = seg[s].take_eq - eq_seen;
+    if (quota < 0) quota = 0;
+    long long te = cnt_eq[c] < quota ? cnt_eq[c] : quota;
+    eq_seen += cnt_eq[c];
+    eq_take[c] = te;
+    out_off[c] = off;
+    off += cnt_gt[c] + te;
+  }
+  *total = off;
+}
+
+// Ordered compaction: writes (index, value) of kept entries in ascending index order, zeroes them in ef.
+__global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ cseg,
+                               const long long* __restrict__ cstart, const long long* __restrict__ cend,
+                               SegState* seg, const long long* __restrict__ eq_take,
+                               const long long* __restrict__ out_off, int* __restrict__ out_idx,
+                               float* __restrict__ out_val) {
+  __shared__ unsigned wsum_sel[TPB / 32], wsum_eq[TPB / 32];
+  __shared__ long long base_sel, base_eq;
+  __shared__ float shs[32];
+  const int c = blockIdx.x, s = cseg[c];
+  const unsigned tau = seg[s].tau;
+  const long long quota = eq_take[c];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) { base_sel = out_off[c]; base_eq = 0; }
+  __syncthreads();
+  float kept_sq = 0.f;
+  for (long long i0 = cstart[c]; i0 < cend[c]; i0 += blockDim.x) {
+    long long i = i0 + threadIdx.x;
+    bool valid = i < cend[c];
+    float d = valid ? ef[i] : 0.f;
+    unsigned k = keyof(d);
+    bool is_eq = valid && (k == tau);
+    bool is_gt = valid && (k > tau);
+    // rank among eq in this iteration
+    unsigned beq = __ballot_sync(0xffffffffu, is_eq);
+    unsigned eq_before_w = __popc(beq & ((1u << lane) - 1));
+    if (lane == 0) wsum_eq[wid] = __popc(beq);
+    __syncthreads();
+    unsigned eq_before = eq_before_w;
+    for (int w = 0; w < wid; ++w) eq_before += wsum_eq[w];
+    bool take = is_gt || (is_eq && (base_eq + eq_before) < quota);
+    unsigned bsel = __ballot_sync(0xffffffffu, take);
+    unsigned sel_before_w = __popc(bsel & ((1u << lane) - 1));
+    if (lane == 0) wsum_sel[wid] = __popc(bsel);
+    __syncthreads();
+    unsigned sel_before = sel_before_w;
+    unsigned tot_sel = 0, tot_eq = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      if (w < wid) sel_before += wsum_sel[w];
+      tot_sel += wsum_sel[w];
+      tot_eq += wsum_eq[w];
+    }
+    if (take) {
+      long long pos = base_sel + sel_before;
+      out_idx[pos] = (int)i;
+      out_val[pos] = d;
+      ef[i] = 0.f;
+      kept_sq += d * d;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { base_sel += tot_sel; base_eq += tot_eq; }
+    __syncthreads();
+  }
+  float t = block_sum(kept_sq, shs);
+  if (threadIdx.x == 0) atomicAdd(&seg[s].kept_sq, (double)t);
+}
+
+// Per block of `blk` kept values: absmax/127 scale (1 if all zero), round-half-away int8.
+__global__ void quant_kernel(const float* __restrict__ val, const long long* __restrict__ total, int blk,
+                             signed char* __restrict__ q, float* __restrict__ scales) {
+  __shared__ float sh[32];
+  const long long n = *total;
+  const long long b = blockIdx.x;
+  const long long s0 = b * blk;
+  if (s0 >= n) return;
+  const long long e = (s0 + blk < n) ? s0 + blk : n;
+  float mx = 0.f;
+  for (long long i = s0 + threadIdx.x; i < e; i += blockDim.x) mx = fmaxf(mx, fabsf(val[i]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) sh[0] = v;
+  }
+  __syncthreads();
+  const float amax = sh[0];
+  const float scale = amax == 0.f ? 1.f : amax / 127.f;
+  if (threadIdx.x == 0) scales[b] = scale;
+  for (long long i = s0 + threadIdx.x; i < e; i += blockDim.x) {
+    float r = roundf(val[i] / scale);
+    r = fminf(fmaxf(r, -127.f), 127.f);
+    q[i] = (signed char)r;
+  }
+}
+
+}  // namespace
+
+// ───────────────────────────── host API ─────────────────────────────
+// Workspace layout (device, caller-allocated, size from dt_compress_workspace_bytes):
+//   SegState[nseg] | hist1[nseg*NB1] | hist2[nseg*NB2] | hist3[nseg*NB3] |
+//   cnt_gt[nchunks] | cnt_eq[nchunks] | eq_take[nchunks] | out_off[nchunks] | total[1]
+struct WsPtrs {
+  SegState* seg;
+  unsigned *h1, *h2, *h3;
+  long long *gt, *eq, *take, *off, *total;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static WsPtrs carve(void* ws, int nseg, int nchunks) {
+  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
+  WsPtrs w;
+  w.seg = reinterpret_cast<SegState*>(p); p += align256(sizeof(SegState) * nseg);
+  w.h1 = reinterpret_cast<unsigned*>(p); p += align256(sizeof(unsigned) * (size_t)nseg * NB1);
+  w.h2 = reinterpret_cast<unsigned*>(p); p += align256(sizeof(unsigned) * (size_t)nseg * NB2);
+  w.h3 = reinterpret_cast<unsigned*>(p); p += align256(sizeof(unsigned) * (size_t)nseg * NB3);
+  w.gt = reinterpret_cast<long long*>(p); p += align256(8 * (size_t)nchunks);
+  w.eq = reinterpret_cast<long long*>(p); p += align256(8 * (size_t)nchunks);
+  w.take = reinterpret_cast<long long*>(p); p += align256(8 * (size_t)nchunks);
+  w.off = reinterpret_cast<long long*>(p); p += align256(8 * (size_t)nchunks);
+  w.total = reinterpret_cast<long long*>(p);
+  return w;
+}
+
+DT_API long long dt_compress_workspace_bytes(int nseg, int nchunks) {
+  return (long long)(align256(sizeof(SegState) * nseg) + align256(4ull * nseg * NB1) + align256(4ull * nseg * NB2) +
+                     align256(4ull * nseg * NB3) + 4 * align256(8ull * nchunks) + 256);
+}
+
+DT_API long long dt_compress_segstate_bytes() { return (long long)sizeof(SegState); }
+
+__global__ void seg_init_kernel(SegState* seg, const long long* __restrict__ seg_len, int nseg) {
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < nseg; s += gridDim.x * blockDim.x) {
+    SegState z = {};
+    z.len = seg_len[s];
+    seg[s] = z;
+  }
+}
+
+__global__ void export_stats_kernel(const SegState* seg, int nseg, const long long* total, double* out) {
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < nseg; s += gridDim.x * blockDim.x) {
+    out[s * 6 + 0] = seg[s].sumsq;
+    out[s * 6 + 1] = seg[s].kept_sq;
+    out[s * 6 + 2] = (double)seg[s].k;
+    out[s * 6 + 3] = (double)seg[s].maxabs;
+    out[s * 6 + 4] = (double)seg[s].nonfinite;
+    out[s * 6 + 5] = (double)seg[s].len;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) out[nseg * 6] = (double)*total;
+}
+
+// Pass A (training stream). seg_len: device array of per-segment element counts.
+DT_API int dt_compress_begin(const float* master, float* snap, float* ef, const int* cseg, const long long* cstart,
+                             const long long* cend, int nchunks, int nseg, const long long* seg_len, void* ws,
+                             int use_ef, cudaStream_t st) {
+  WsPtrs w = carve(ws, nseg, nchunks);
+  DT_CUDA_RET(cudaMemsetAsync(ws, 0, (size_t)dt_compress_workspace_bytes(nseg, nchunks), st));
+  seg_init_kernel<<<(nseg + 255) / 256, 256, 0, st>>>(w.seg, seg_len, nseg);
+  pass_a_kernel<<<nchunks, TPB, 0, st>>>(master, snap, ef, cseg, cstart, cend, w.seg, w.h1, use_ef);
+  return (int)cudaGetLastError();
+}
+
+// Everything after pass A (side stream). Writes out_idx/out_val (capacity entries) in ascending index
+// order, int8 + per-block scales when quant_block > 0, and the kept count into the workspace.
+DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstart, const long long* cend, int nchunks,
+                              int nseg, void* ws, float k_fraction, int adaptive, int* out_idx, float* out_val,
+                              signed char* out_q, float* out_scales, int quant_block, long long capacity,
+                              cudaStream_t st) {
+  WsPtrs w = carve(ws, nseg, nchunks);
+  budget_kernel<<<1, 256, 0, st>>>(w.seg, nseg, k_fraction, adaptive);
+  const int wpb = 8;
+  const int sblocks = (nseg + wpb - 1) / wpb;
+  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h1, NB1, 12, 0);
+  hist_level_kernel<NB2, SH1, SH2><<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.h2);
+  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h2, NB2, 12, 0);
+  hist_level_kernel<NB3, SH2, 0><<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.h3);
+  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h3, NB3, 7, 1);
+  count_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.gt, w.eq);
+  scan_kernel<<<1, 32, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
+  compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val);
+  if (quant_block > 0 && out_q) {
+    long long nblk = (capacity + quant_block - 1) / quant_block;
+    quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, quant_block, out_q, out_scales);
+  }
+  return (int)cudaGetLastError();
+}
+
+// Per-segment statistics into a device double array: [s*6 + {sumsq, kept_sq, k, maxabs, nonfinite, len}],
+// then the total kept count at [nseg*6].
+DT_API int dt_compress_export_stats(void* ws, int nseg, int nchunks, double* out, cudaStream_t st) {
+  WsPtrs w = carve(ws, nseg, nchunks);
+  export_stats_kernel<<<(nseg + 255) / 256, 256, 0, st>>>(w.seg, nseg, w.total, out);
+  return (int)cudaGetLastError();
+}

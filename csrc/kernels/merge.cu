@@ -1,0 +1,213 @@
+// Coordinator merge over device memory (reference coordinator/src/aggregation.rs:255-380):
+//
+//   pre-pass   per contribution: ||decoded delta||^2, max|x|, non-finite count   (validate_delta,
+//              compression.rs:388-424, and the 3x running-average norm clip inputs, aggregation.rs:310-328)
+//   accumulate acc[idx] += coef_c * q * scale[blk]   for every kept entry of every accepted contribution,
+//              coef_c = clip_c * w_c / sum(w) with w_c = tokens_c * 0.9^staleness_c (weighted_average_gpu,
+//              aggregation.rs:28-61). Payloads are read with plain loads straight out of each node's
+//              GPU memory (peer pointers of a symmetric allocation, NVLink P2P) - no staging copy.
+//   apply      v' = mu*v + acc ; theta -= lr*(mu*v' + acc)   (nesterov_step_gpu, aggregation.rs:64-105;
+//              lr 1, mu 0 => theta -= acc, the unscaled merged delta)
+//              fused with the fp32->bf16 cast and the broadcast of the new checkpoint into every
+//              node's staging buffers: one multimem.st per 16 bytes through an NVLS multicast object
+//              (or one store per peer when no multicast object exists), then acc is cleared.
+#include "common.cuh"
+
+namespace {
+
+struct Contrib {
+  const int* idx;            // kept flat indices (sparse) or null (dense)
+  const signed char* q;      // int8 values (quantised) or null
+  const float* val;          // fp32 values (unquantised sparse, or dense delta)
+  const float* scales;       // per-block scales (quantised)
+  long long count;           // kept entries (sparse) or length (dense)
+  int block;                 // quantisation block
+  int dense;
+  float coef;                // weight / total * clip scale
+  int pad;
+};
+
+__device__ __forceinline__ float contrib_value(const Contrib& c, long long i) {
+  if (c.q) return (float)__ldg(c.q + i) * __ldg(c.scales + i / c.block);
+  return __ldg(c.val + i);
+}
+
+__global__ void prepass_kernel(const Contrib* __restrict__ cs, int n, double* __restrict__ stats) {
+  // grid: (blocks per contribution, n); stats[c*3 + {sumsq, maxabs, nonfinite}]
+  __shared__ float shs[32];
+  const int c = blockIdx.y;
+  const Contrib C = cs[c];
+  float ss = 0.f, mx = 0.f;
+  int nf = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < C.count;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = contrib_value(C, i);
+    if (!isfinite(v)) { nf = 1; continue; }
+    ss += v * v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  float t = block_sum(ss, shs);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned long long*>(stats + c * 3 + 1),
+                                         (unsigned long long)__double_as_longlong((double)mx));
+  nf = __syncthreads_or(nf);
+  if (threadIdx.x == 0) {
+    atomicAdd(stats + c * 3 + 0, (double)t);
+    if (nf) atomicAdd(stats + c * 3 + 2, 1.0);
+  }
+}
+
+__global__ void accumulate_kernel(const Contrib* __restrict__ cs, int n, float* __restrict__ acc) {
+  const int c = blockIdx.y;
+  const Contrib C = cs[c];
+  if (C.coef == 0.f) return;
+  if (C.dense) {
+    const long long n4 = C.count / 4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+      float4 v = __ldg(reinterpret_cast<const float4*>(C.val) + i);
+      atomicAdd(reinterpret_cast<float4*>(acc) + i, make_float4(v.x * C.coef, v.y * C.coef, v.z * C.coef, v.w * C.coef));
+    }
+    for (long long i = n4 * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < C.count;
+         i += (long long)gridDim.x * blockDim.x)
+      atomicAdd(acc + i, __ldg(C.val + i) * C.coef);
+    return;
+  }
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < C.count; i += (long long)gridDim.x * blockDim.x) {
+    int j = __ldg(C.idx + i);
+    atomicAdd(acc + j, contrib_value(C, i) * C.coef);
+  }
+}
+
+__device__ __forceinline__ void mc_store_v4(void* mc_addr, float4 v) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+struct Dests {
+  float* stage32[8];
+  __nv_bfloat16* stage16[8];
+  int n;
+};
+
+// theta, vel, acc: local fp32 [n] (n a multiple of 4). Broadcast targets: multicast addresses
+// (mc32/mc16 non-null) or per-peer pointers in `d`.
+__global__ void apply_broadcast_kernel(float* __restrict__ theta, float* __restrict__ vel, float* __restrict__ acc,
+                                       long long n, float lr, float mu, float* mc32, __nv_bfloat16* mc16, Dests d,
+                                       int write_bf16) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    float4 a = reinterpret_cast<float4*>(acc)[i];
+    float4 t = reinterpret_cast<float4*>(theta)[i];
+    float* ap = &a.x;
+    float* tp = &t.x;
+    if (vel) {
+      float4 v = reinterpret_cast<float4*>(vel)[i];
+      float* vp = &v.x;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        vp[k] = mu * vp[k] + ap[k];
+        tp[k] -= lr * (mu * vp[k] + ap[k]);
+      }
+      reinterpret_cast<float4*>(vel)[i] = v;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tp[k] -= lr * ap[k];
+    }
+    reinterpret_cast<float4*>(theta)[i] = t;
+    reinterpret_cast<float4*>(acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint2 h;
+    h.x = pack_bf16(t.x, t.y);
+    h.y = pack_bf16(t.z, t.w);
+    if (mc32) {
+      mc_store_v4(reinterpret_cast<float4*>(mc32) + i, t);
+    } else {
+      for (int r = 0; r < d.n; ++r) reinterpret_cast<float4*>(d.stage32[r])[i] = t;
+    }
+    if (write_bf16) {
+      if (mc16) {
+        // two consecutive float4-index groups share one 16-byte bf16 store: pair threads via shuffle-free
+        // 8-byte stores are not multimem-capable, so use a v2.f32 multimem store of the packed pair
+        asm volatile("multimem.st.global.v2.f32 [%0], {%1, %2};" ::"l"(reinterpret_cast<uint2*>(mc16) + i),
+                     "f"(__uint_as_float(h.x)), "f"(__uint_as_float(h.y))
+                     : "memory");
+      } else {
+        for (int r = 0; r < d.n; ++r) reinterpret_cast<uint2*>(d.stage16[r])[i] = h;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+// Node side of a checkpoint swap: master <- stage32, p16 <- stage16 (or cast), snapshot <- master.
+__global__ void swap_in_kernel(const float* __restrict__ s32, const __nv_bfloat16* __restrict__ s16,
+                               float* __restrict__ master, __nv_bfloat16* __restrict__ p16, float* __restrict__ snap,
+                               long long n) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    float4 t = reinterpret_cast<const float4*>(s32)[i];
+    reinterpret_cast<float4*>(master)[i] = t;
+    if (snap) reinterpret_cast<float4*>(snap)[i] = t;
+    if (s16) {
+      reinterpret_cast<uint2*>(p16)[i] = reinterpret_cast<const uint2*>(s16)[i];
+    } else {
+      uint2 h;
+      h.x = pack_bf16(t.x, t.y);
+      h.y = pack_bf16(t.z, t.w);
+      reinterpret_cast<uint2*>(p16)[i] = h;
+    }
+  }
+}
+
+int grid_cap(long long work, int th, int cap) {
+  long long b = (work + th - 1) / th;
+  if (b > cap) b = cap;
+  return (int)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+DT_API long long dt_merge_contrib_bytes() { return (long long)sizeof(Contrib); }
+
+// contribs: device array of `n` Contrib descriptors (layout: see struct; sizeof from dt_merge_contrib_bytes).
+DT_API int dt_merge_prepass(const void* contribs, int n, long long max_count, double* stats, cudaStream_t st) {
+  if (n <= 0) return 0;
+  DT_CUDA_RET(cudaMemsetAsync(stats, 0, sizeof(double) * 3 * n, st));
+  dim3 grid(grid_cap(max_count, 256, 148 * 2), n);
+  prepass_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const Contrib*>(contribs), n, stats);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_merge_accumulate(const void* contribs, int n, long long max_count, float* acc, cudaStream_t st) {
+  if (n <= 0) return 0;
+  dim3 grid(grid_cap(max_count, 256, 148 * 4), n);
+  accumulate_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const Contrib*>(contribs), n, acc);
+  return (int)cudaGetLastError();
+}
+
+// stage32/stage16: host arrays of n_dest device pointers (peer-mapped), used when mc32 is null.
+DT_API int dt_merge_apply_broadcast(float* theta, float* vel, float* acc, long long n, float lr, float mu, void* mc32,
+                                    void* mc16, void* const* stage32, void* const* stage16, int n_dest,
+                                    int write_bf16, cudaStream_t st) {
+  if (n % 4) return -10;
+  if (n_dest > 8) return -11;
+  Dests d = {};
+  d.n = mc32 ? 0 : n_dest;
+  for (int r = 0; r < d.n; ++r) {
+    d.stage32[r] = reinterpret_cast<float*>(stage32[r]);
+    d.stage16[r] = stage16 ? reinterpret_cast<__nv_bfloat16*>(stage16[r]) : nullptr;
+  }
+  if (!mc32 && write_bf16 && !stage16) return -12;
+  apply_broadcast_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(
+      theta, vel, acc, n, lr, mu, reinterpret_cast<float*>(mc32), reinterpret_cast<__nv_bfloat16*>(mc16), d,
+      write_bf16);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_swap_in(const float* s32, const void* s16, float* master, void* p16, float* snap, long long n,
+                      cudaStream_t st) {
+  if (n % 4) return -10;
+  swap_in_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(s32, reinterpret_cast<const __nv_bfloat16*>(s16),
+                                                               master, reinterpret_cast<__nv_bfloat16*>(p16), snap, n);
+  return (int)cudaGetLastError();
+}

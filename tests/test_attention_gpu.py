@@ -1,0 +1,39 @@
+"""Flash attention kernels vs the plain fp32 PyTorch formulation (causal, GQA)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("B,T,nh,nkv,d", [(2, 64, 4, 2, 64), (2, 100, 4, 1, 64), (1, 257, 12, 4, 64),
+                                          (2, 130, 16, 4, 128), (3, 64, 4, 2, 16), (1, 1023, 12, 4, 64)])
+def test_attention_fwd_bwd(B, T, nh, nkv, d):
+    from distrain_b200.ops import attention as A
+    from distrain_b200 import ops
+    torch.manual_seed(0)
+    ops.clear_device_error()
+    W = (nh + 2 * nkv) * d
+    qkv = (torch.randn(B * T, W, device="cuda") * 1.5).bfloat16()
+    out = torch.empty(B * T, nh * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, nh, T, device="cuda")
+    A.attention_fwd(qkv, out, lse, B=B, T=T, nh=nh, nkv=nkv, d=d, impl="dt")
+    ref_o, ref_lse = A._torch_fwd(qkv, B, T, nh, nkv, d)
+    torch.cuda.synchronize()
+    assert _rel(out, ref_o) < 1e-2
+    assert (lse - ref_lse).abs().max().item() < 1e-2
+    dout = torch.randn(B * T, nh * d, device="cuda").bfloat16()
+    dqkv = torch.empty_like(qkv)
+    dq_acc = torch.empty(B * T, nh * d, device="cuda")
+    delta = torch.empty(B, nh, T, device="cuda")
+    A.attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, B=B, T=T, nh=nh, nkv=nkv, d=d, impl="dt")
+    dq, dk, dv = A._torch_bwd(qkv, dout, B, T, nh, nkv, d)
+    torch.cuda.synchronize()
+    assert _rel(dqkv[:, :nh * d], dq) < 2e-2
+    assert _rel(dqkv[:, nh * d:(nh + nkv) * d], dk) < 2e-2
+    assert _rel(dqkv[:, (nh + nkv) * d:], dv) < 2e-2
+    assert ops.device_error()[0] == 0

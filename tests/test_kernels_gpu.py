@@ -206,10 +206,11 @@ def test_swiglu_fwd_bwd():
     assert _rel(dgu[:, F:], u.grad) < 1e-2
 
 
-def test_cross_entropy():
+@pytest.mark.parametrize("V", [32768, 512, 256])
+def test_cross_entropy(V):
     ops = _ops()
     torch.manual_seed(8)
-    B, S, V = 2, 9, 32768
+    B, S = 2, 9
     T = S - 1
     M = B * T
     ids = torch.randint(0, V, (B, S), device="cuda", dtype=torch.int32)
@@ -238,8 +239,6 @@ def test_adamw_matches_reference():
     L = ParamLayout(cfg)
     flat = init_flat(L, 0.02, 0).cuda()
     grads = torch.randn(L.total, device="cuda") * 0.5
-    for e in L.entries:
-        pass
     mask = torch.zeros(L.total, dtype=torch.bool, device="cuda")
     for e in L.entries:
         mask[e.offset:e.offset + e.numel] = True
@@ -264,7 +263,7 @@ def test_adamw_matches_reference():
     got = L.views(p)
     for k, t in ref_params.items():
         assert torch.allclose(got[k], t, atol=1e-6, rtol=1e-5), k
-    assert torch.allclose(p16.float(), p.bfloat16().float())
+    assert torch.equal(p16[mask].float(), p[mask].bfloat16().float())
     # NaN loss flag skips the update
     before = p.clone()
     loss[1] = 1.0
