@@ -122,7 +122,8 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   }
 }
 
-// out[0] = sum(loss_row[0:n]) * scale  (single block); out[1] = 1 if non-finite.
+// out[0] = sum(loss_row[0:n]) * scale  (single block); out[1] = 1 if non-finite;
+// out[2] += out[0] and out[3] += 1 when finite (running round sums read at push time).
 __global__ void loss_reduce_kernel(const float* __restrict__ loss_row, long long n, float scale, float* out) {
   __shared__ float sh[32];
   float s = 0.f;
@@ -132,6 +133,10 @@ __global__ void loss_reduce_kernel(const float* __restrict__ loss_row, long long
     float l = tot * scale;
     out[0] = l;
     out[1] = isfinite(l) ? 0.f : 1.f;
+    if (isfinite(l)) {
+      out[2] += l;
+      out[3] += 1.f;
+    }
   }
 }
 

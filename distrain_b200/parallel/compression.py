@@ -1,0 +1,245 @@
+"""Delta compression: error feedback -> (adaptive) top-k -> INT8 -> payload.
+
+Two implementations of the same algorithm (reference core/model/src/compression.rs:57-382):
+
+* ``DeviceCompressor`` - the node's hot path: the fused sm_100a pipeline in ``csrc/kernels/compress.cu``
+  over the flat parameter buffer. ``begin()`` (on the training stream) forms d = snapshot - master + ef
+  and re-snapshots; ``finish()`` (on a side stream) selects, compacts, quantises and leaves a payload
+  (ascending flat indices, int8 values, fp32 per-block scales) in device memory.
+* ``compress_reference`` - a CPU restatement over a name->tensor dict, the oracle for tests and the
+  CPU node path; its output is the reference's ``SparseDelta`` (JSON/zstd codec in
+  ``utils/delta_codec.py``).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from ..config import CompressionConfig
+
+
+# ─────────────────────────────── CPU reference ───────────────────────────────
+def sparsify_topk(delta: Dict[str, torch.Tensor], k_fraction: float, adaptive: bool):
+    """Returns (sparse dense-shaped, indices, values) per tensor (compression.rs:128-184).
+    Ties are broken by ascending index (stable sort by |value| descending)."""
+    names = list(delta.keys())
+    norms = {n: math.sqrt(float((delta[n].double() ** 2).sum())) for n in names} if adaptive else {}
+    total_norm = sum(norms.values())
+    total_params = sum(delta[n].numel() for n in names)
+    kf32 = float(torch.tensor(k_fraction, dtype=torch.float32))
+    total_budget = math.ceil(total_params * kf32)
+    sparse, idxs, vals = {}, {}, {}
+    for n in names:
+        flat = delta[n].reshape(-1).float()
+        L = flat.numel()
+        if adaptive and total_norm > 0:
+            k = math.ceil(total_budget * (norms[n] / total_norm))
+            k = min(max(k, 1), L)
+        else:
+            k = max(int(math.ceil(float(torch.tensor(L, dtype=torch.float32) * torch.tensor(k_fraction,
+                                                                                            dtype=torch.float32)))), 1)
+            k = min(k, L)
+        order = torch.sort(flat.abs(), descending=True, stable=True).indices[:k]
+        order = torch.sort(order).values
+        v = flat[order]
+        sp = torch.zeros_like(flat)
+        sp[order] = v
+        sparse[n] = sp
+        idxs[n] = order.to(torch.int64)
+        vals[n] = v
+    return sparse, idxs, vals
+
+
+def quantize_int8(values: torch.Tensor, block: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """absmax/127 scale per block (block 0 = one scale for the whole vector), round half away from 0."""
+    v = values.float().reshape(-1)
+    n = v.numel()
+    if block <= 0:
+        block = max(n, 1)
+    nb = max((n + block - 1) // block, 1)
+    pad = nb * block - n
+    vp = torch.cat([v, v.new_zeros(pad)]) if pad else v
+    vb = vp.view(nb, block)
+    amax = vb.abs().amax(dim=1)
+    scale = torch.where(amax == 0, torch.ones_like(amax), amax / 127.0)
+    r = vb / scale[:, None]
+    q = torch.sign(r) * torch.floor(r.abs() + 0.5)
+    q = q.clamp(-127, 127).to(torch.int8).reshape(-1)[:n]
+    return q, scale
+
+
+def dequantize_int8(q: torch.Tensor, scale: torch.Tensor, block: int = 0) -> torch.Tensor:
+    n = q.numel()
+    if block <= 0:
+        block = max(n, 1)
+    idx = torch.arange(n) // block
+    return q.float() * scale[idx]
+
+
+@dataclass
+class SparseDeltaT:
+    """In-memory SparseDelta (compression.rs:92-104) with tensors instead of JSON lists."""
+    indices: Dict[str, torch.Tensor]
+    values: Dict[str, torch.Tensor]      # dequantised fp32 values, as the reference stores them
+    shapes: Dict[str, List[int]]
+    scales: Optional[Dict[str, float]]
+    config: CompressionConfig
+
+
+def compress_reference(delta: Dict[str, torch.Tensor], shapes: Dict[str, List[int]], cfg: CompressionConfig,
+                       ef: Dict[str, torch.Tensor]):
+    """Error feedback -> top-k -> per-tensor INT8 (reference semantics). Updates ``ef`` in place.
+    Returns (SparseDeltaT, stats dict)."""
+    combined = {n: delta[n].reshape(-1).float() + (ef[n].reshape(-1) if n in ef else 0) for n in delta}
+    dense_norm = math.sqrt(sum(float((t.double() ** 2).sum()) for t in combined.values()))
+    sparse, idxs, vals = sparsify_topk(combined, cfg.top_k_fraction, cfg.per_tensor_adaptive)
+    for n in combined:
+        ef[n] = combined[n] - sparse[n]
+    sparse_norm = math.sqrt(sum(float((t.double() ** 2).sum()) for t in sparse.values()))
+    kept = sum(int((t != 0).sum()) for t in sparse.values())
+    scales = None
+    if cfg.quantize_int8:
+        scales = {}
+        for n in vals:
+            q, s = quantize_int8(vals[n], 0)
+            vals[n] = dequantize_int8(q, s, 0)
+            scales[n] = float(s[0])
+    sd = SparseDeltaT(indices=idxs, values=vals, shapes=shapes, scales=scales, config=cfg)
+    total = sum(t.numel() for t in combined.values())
+    stats = {"dense_norm": dense_norm, "sparse_norm": sparse_norm,
+             "retention_ratio": sparse_norm / dense_norm if dense_norm > 0 else 0.0,
+             "top_k_fraction": cfg.top_k_fraction, "num_params_total": total, "num_params_kept": kept,
+             "raw_param_bytes": total * 4}
+    return sd, stats
+
+
+def reconstruct_dense(sd: SparseDeltaT) -> Dict[str, torch.Tensor]:
+    out = {}
+    for n, shape in sd.shapes.items():
+        numel = 1
+        for s in shape:
+            numel *= s
+        flat = torch.zeros(numel)
+        if n in sd.indices and sd.indices[n].numel():
+            flat[sd.indices[n].long()] = sd.values[n].float()
+        out[n] = flat
+    return out
+
+
+# ─────────────────────────────── device pipeline ───────────────────────────────
+class DeviceCompressor:
+    """Fused compress pipeline over a ``ParamLayout``'s flat buffer (one per node)."""
+
+    def __init__(self, layout, device, cfg: CompressionConfig, payload=None):
+        from ..ops import _lib
+        from ..ops._lib import c_int, c_void, c_ll, c_float
+        self.L = _lib.lib()
+        _lib.register("dt_compress_workspace_bytes", [c_int, c_int], restype=c_ll)
+        _lib.register("dt_compress_begin", [c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_void,
+                                            c_void, c_int, c_void])
+        _lib.register("dt_compress_finish", [c_void, c_void, c_void, c_void, c_int, c_int, c_void, c_float, c_int,
+                                             c_void, c_void, c_void, c_void, c_int, c_ll, c_void])
+        _lib.register("dt_compress_export_stats", [c_void, c_int, c_int, c_void, c_void])
+        self.layout, self.device, self.cfg = layout, torch.device(device), cfg
+        n = layout.total
+        self.cseg, self.cstart, self.cend, self.nseg = layout.chunk_tables(self.device)
+        self.nchunks = self.cseg.numel()
+        self.seg_len = torch.tensor([e.numel for e in layout.entries], dtype=torch.int64, device=self.device)
+        self.snap = torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.ef = torch.zeros(n, dtype=torch.float32, device=self.device)
+        wsb = self.L.dt_compress_workspace_bytes(self.nseg, self.nchunks)
+        self.ws = torch.zeros(wsb, dtype=torch.uint8, device=self.device)
+        self.stats_dev = torch.zeros(self.nseg * 6 + 1, dtype=torch.float64, device=self.device)
+        self.stats_host = torch.zeros(self.nseg * 6 + 1, dtype=torch.float64).pin_memory()
+        self.capacity = self.capacity_for(layout, cfg.top_k_fraction)
+        self.payload = payload or DevicePayload.allocate(self.capacity, cfg.int8_block if cfg.quantize_int8 else 0,
+                                                         self.device)
+
+    @staticmethod
+    def capacity_for(layout, k_fraction: float) -> int:
+        total = layout.num_params()
+        cap = math.ceil(total * float(k_fraction)) + len(layout.entries) + 16
+        return min(cap, total)
+
+    def reset(self, master: torch.Tensor):
+        """New checkpoint: snapshot <- master, error feedback cleared."""
+        self.snap.copy_(master)
+        self.ef.zero_()
+
+    def begin(self, master: torch.Tensor, stream=None):
+        from ..ops._lib import check, stream_ptr
+        check(self.L.dt_compress_begin(master.data_ptr(), self.snap.data_ptr(), self.ef.data_ptr(),
+                                       self.cseg.data_ptr(), self.cstart.data_ptr(), self.cend.data_ptr(),
+                                       self.nchunks, self.nseg, self.seg_len.data_ptr(), self.ws.data_ptr(), 1,
+                                       stream_ptr(stream)), "dt_compress_begin")
+
+    def finish(self, payload=None, stream=None, k_fraction: Optional[float] = None):
+        from ..ops._lib import check, stream_ptr
+        p = payload or self.payload
+        kf = self.cfg.top_k_fraction if k_fraction is None else k_fraction
+        qb = self.cfg.int8_block if self.cfg.quantize_int8 else 0
+        check(self.L.dt_compress_finish(self.ef.data_ptr(), self.cseg.data_ptr(), self.cstart.data_ptr(),
+                                        self.cend.data_ptr(), self.nchunks, self.nseg, self.ws.data_ptr(), float(kf),
+                                        int(self.cfg.per_tensor_adaptive), p.idx.data_ptr(), p.val.data_ptr(),
+                                        p.q.data_ptr() if qb else None, p.scales.data_ptr() if qb else None, qb,
+                                        p.capacity, stream_ptr(stream)), "dt_compress_finish")
+        check(self.L.dt_compress_export_stats(self.ws.data_ptr(), self.nseg, self.nchunks, self.stats_dev.data_ptr(),
+                                              stream_ptr(stream)), "dt_compress_export_stats")
+        self.stats_host.copy_(self.stats_dev, non_blocking=True)
+
+    def read_stats(self) -> dict:
+        """Call after the finish stream has been synchronised."""
+        s = self.stats_host
+        ns = self.nseg
+        seg = s[:ns * 6].view(ns, 6)
+        total_kept = int(s[ns * 6].item())
+        dense_sq, kept_sq = float(seg[:, 0].sum()), float(seg[:, 1].sum())
+        dense_norm, sparse_norm = math.sqrt(dense_sq), math.sqrt(kept_sq)
+        return {"dense_norm": dense_norm, "sparse_norm": sparse_norm,
+                "retention_ratio": sparse_norm / dense_norm if dense_norm > 0 else 0.0,
+                "num_params_total": self.layout.num_params(), "num_params_kept": total_kept,
+                "max_abs": float(seg[:, 3].max()), "nonfinite": bool(seg[:, 4].sum() > 0),
+                "k_per_tensor": seg[:, 2].long().tolist()}
+
+
+class DevicePayload:
+    """Compressed delta in device memory: idx int32[cap], val fp32[cap], q int8[cap], scales fp32[cap/blk].
+    Views into one allocation so the whole payload can live in a single symmetric (peer-mapped) buffer."""
+
+    def __init__(self, buf: torch.Tensor, capacity: int, block: int):
+        self.buf, self.capacity, self.block = buf, capacity, block
+        o = 0
+        def take(nbytes):
+            nonlocal o
+            s = o
+            o = (o + nbytes + 255) // 256 * 256
+            return s
+        oi = take(4 * capacity)
+        ov = take(4 * capacity)
+        oq = take(capacity)
+        nb = (capacity + block - 1) // block if block else 1
+        os_ = take(4 * nb)
+        self.idx = buf[oi:oi + 4 * capacity].view(torch.int32)
+        self.val = buf[ov:ov + 4 * capacity].view(torch.float32)
+        self.q = buf[oq:oq + capacity].view(torch.int8)
+        self.scales = buf[os_:os_ + 4 * nb].view(torch.float32)
+
+    @staticmethod
+    def nbytes(capacity: int, block: int) -> int:
+        nb = (capacity + block - 1) // block if block else 1
+        r = lambda x: (x + 255) // 256 * 256
+        return r(4 * capacity) + r(4 * capacity) + r(capacity) + r(4 * nb)
+
+    @classmethod
+    def allocate(cls, capacity: int, block: int, device) -> "DevicePayload":
+        buf = torch.zeros(cls.nbytes(capacity, block), dtype=torch.uint8, device=device)
+        return cls(buf, capacity, block)
+
+    def wire_bytes(self, count: int) -> int:
+        """Bytes a contribution of `count` kept entries occupies on the wire (idx + int8/fp32 + scales)."""
+        if self.block:
+            return count * 4 + count + ((count + self.block - 1) // self.block) * 4
+        return count * 8

@@ -1,0 +1,413 @@
+"""In-box asynchronous data plane: node push / coordinator merge / checkpoint swap over device memory.
+
+Every rank is one Distrain node; rank 0 additionally runs the coordinator. Per node:
+
+* ``payload`` - two slots of a symmetric (peer-mapped) buffer holding compressed deltas;
+* ``staging`` - two version-parity slots of a symmetric buffer (fp32 master + bf16 compute copy) that
+  the coordinator's apply kernel writes with NVLS ``multimem.st`` (or per-peer stores).
+
+Push (node, at a round boundary, reference continuous.rs:532-580): pass A of the compressor on the
+training stream (delta + error feedback + re-snapshot, ~0.2 ms), the rest of the compressor on a
+side stream into a free payload slot, then a background thread waits for it and posts the push
+metadata (the reference ``DeltaPush`` body plus where the payload lives) on the control bus.
+
+Merge (coordinator thread on rank 0): ingest pushes into the ``Accumulator`` (staleness, dedup,
+weights), and when the trigger fires run the peer-pull merge kernels on a low-priority stream;
+publish the new version. A payload slot is released once its contribution is merged, replaced or
+rejected; a node whose next slot is still in use defers the push by a step instead of blocking.
+
+Swap (node, reference continuous.rs:458-502): on a new version push the partial round, copy the
+staged checkpoint into the master / bf16 buffers, reset AdamW and the error-feedback buffer.
+"""
+from __future__ import annotations
+
+import json
+import os
+import queue
+import threading
+import time
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..config import RunConfig
+from ..protocol import Accumulator, DeltaPush, delta_path
+from .compression import DeviceCompressor, DevicePayload
+from .merge import Contribution, DeviceMerger
+
+
+# ─────────────────────────────── control bus ───────────────────────────────
+class LocalBus:
+    def __init__(self):
+        self.d: Dict[str, str] = {}
+        self.lock = threading.Lock()
+
+    def set(self, k, v):
+        with self.lock:
+            self.d[k] = v
+
+    def get(self, k, default=None):
+        with self.lock:
+            return self.d.get(k, default)
+
+
+class StoreBus:
+    """Key-value control plane over a TCPStore client of the job's rendezvous store."""
+
+    def __init__(self, prefix: str = "dtinbox/"):
+        host = os.environ.get("MASTER_ADDR", "127.0.0.1")
+        port = int(os.environ.get("MASTER_PORT", "29500"))
+        import datetime
+        self.store = dist.TCPStore(host, port, is_master=False, timeout=datetime.timedelta(seconds=60))
+        self.prefix = prefix
+        self.lock = threading.Lock()
+
+    def set(self, k, v):
+        with self.lock:
+            self.store.set(self.prefix + k, v)
+
+    def get(self, k, default=None):
+        with self.lock:
+            key = self.prefix + k
+            if not self.store.check([key]):
+                return default
+            return self.store.get(key).decode()
+
+
+def _symm_alloc(nbytes: int, device, world: int):
+    """Symmetric buffer: (local tensor, peer base pointers, multicast pointer)."""
+    if world == 1:
+        t = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        return t, [t.data_ptr()], 0, None
+    import torch.distributed._symmetric_memory as symm_mem
+    t = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+    t.zero_()
+    hdl = symm_mem.rendezvous(t, dist.group.WORLD.group_name)
+    mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
+    if os.environ.get("DT_NO_MULTICAST"):
+        mc = 0
+    return t, [int(p) for p in hdl.buffer_ptrs], mc, hdl
+
+
+class InBoxSync:
+    def __init__(self, node, run: RunConfig, rank: int, world: int, device):
+        self.node, self.run, self.rank, self.world = node, run, rank, world
+        self.device = torch.device(device)
+        eng = node.engine
+        self.eng = eng
+        self.layout = eng.layout
+        self.n = self.layout.total
+        self.node_id = f"node-{rank:02d}"
+        self.version = 0
+        self.seq = 0
+        self.round_tokens = 0
+        self.round_loss = []
+        self.first_round = True
+        self.round_t0 = time.time()
+        cfg = run.compression
+        self.comp_stream = torch.cuda.Stream(device=self.device)
+        # ── symmetric buffers ──
+        cap = DeviceCompressor.capacity_for(self.layout, max(cfg.top_k_fraction, 0.0))
+        blk = cfg.int8_block if cfg.quantize_int8 else 0
+        self.slot_bytes = (DevicePayload.nbytes(cap, blk) + 4095) // 4096 * 4096
+        self.pay_buf, self.pay_ptrs, _, self._pay_h = _symm_alloc(2 * self.slot_bytes, self.device, world)
+        self.slots = [DevicePayload(self.pay_buf[i * self.slot_bytes:(i + 1) * self.slot_bytes], cap, blk)
+                      for i in range(2)]
+        self.stage_bytes = (self.n * 6 + 4095) // 4096 * 4096
+        self.stage_buf, self.stage_ptrs, self.stage_mc, self._stage_h = _symm_alloc(2 * self.stage_bytes, self.device,
+                                                                                   world)
+        self.compressor = DeviceCompressor(self.layout, self.device, cfg, payload=self.slots[0])
+        self.compressor.reset(eng.master)
+        self.bus = LocalBus() if world == 1 else StoreBus()
+        self.inflight = None  # (seq, event, slot)
+        self.slot_seq = [-1, -1]
+        self.ef_ready = None
+        self.pending_posts: "queue.Queue" = queue.Queue()
+        self.stop = threading.Event()
+        self.poster = threading.Thread(target=self._post_loop, daemon=True)
+        self.poster.start()
+        self.latest_version = 0
+        self.coord = None
+        if rank == 0:
+            self.coord = InBoxCoordinator(self, run, world)
+        if world > 1:
+            dist.barrier()
+
+    # ─────────── helpers ───────────
+    def stage_views(self, version: int):
+        par = version % 2
+        base = par * self.stage_bytes
+        s32 = self.stage_buf[base:base + 4 * self.n].view(torch.float32)
+        s16 = self.stage_buf[base + 4 * self.n:base + 6 * self.n].view(torch.bfloat16)
+        return s32, s16
+
+    def stage_peer_ptrs(self, version: int):
+        par = version % 2
+        p32 = [p + par * self.stage_bytes for p in self.stage_ptrs]
+        p16 = [p + par * self.stage_bytes + 4 * self.n for p in self.stage_ptrs]
+        mc32 = self.stage_mc + par * self.stage_bytes if self.stage_mc else 0
+        mc16 = mc32 + 4 * self.n if mc32 else 0
+        return p32, p16, mc32, mc16
+
+    def _slot_free(self, slot: int) -> bool:
+        s = self.slot_seq[slot]
+        if s < 0:
+            return True
+        rel = self.bus.get(f"released/{self.rank}/{s}")
+        return rel is not None
+
+    # ─────────── step hooks ───────────
+    def before_step(self):
+        lv = self.bus.get("version") if (self.node.step_count % 4 == 0) else None
+        if lv is not None and int(lv) > self.version:
+            self._swap(int(lv))
+        # first-round linear warm-up of the inner lr (reference continuous.rs:588-596)
+        o = self.run.optim
+        warm = max(int(self.run.push_every * o.warmup_fraction), 2)
+        if self.first_round and self.node.round_step < warm:
+            self.eng.set_lr(o.lr * self.node.round_step / warm)
+        elif self.first_round and self.node.round_step == warm:
+            self.eng.set_lr(o.lr)
+
+    def after_step(self):
+        self.round_tokens += self.run.micro_batch * self.run.seq_len
+        if self.node.round_step >= self.run.push_every:
+            warm = max(int(self.run.push_every * self.run.optim.warmup_fraction), 2)
+            if self.first_round and self.node.round_step <= warm:
+                return
+            if self._push(partial=False):
+                self.first_round = False
+
+    def _push(self, partial: bool) -> bool:
+        slot = (self.seq + 1) % 2
+        if not self._slot_free(slot):
+            return False  # coordinator still holds that payload; try again next step
+        if self.inflight is not None and not self.inflight[1].query():
+            return False
+        seq = self.seq + 1
+        eng = self.eng
+        train = torch.cuda.current_stream()
+        if self.ef_ready is not None:
+            train.wait_event(self.ef_ready)
+        self.compressor.begin(eng.master, stream=train)   # pass A on the training stream
+        ev_a = torch.cuda.Event()
+        ev_a.record(train)
+        self.comp_stream.wait_event(ev_a)
+        self.compressor.finish(payload=self.slots[slot], stream=self.comp_stream)
+        ev_f = torch.cuda.Event()
+        ev_f.record(self.comp_stream)
+        self.ef_ready = ev_f
+        ev_l = torch.cuda.Event()
+        self.seq = seq
+        self.slot_seq[slot] = seq
+        steps = self.node.round_step
+        tokens = self.round_tokens
+        meta = DeltaPush(node_id=self.node_id, seq_num=seq, checkpoint_version=self.version, inner_steps=steps,
+                         delta_key=delta_path(self.version, self.node_id, seq), training_loss=0.0,
+                         tokens_processed=tokens, training_time_secs=time.time() - self.round_t0)
+        # round mean loss: device running sums (loss[2], loss[3]) copied after pass A, then reset
+        loss_h = torch.empty(2, dtype=torch.float32).pin_memory()
+        self.loss_hold = loss_h
+        with torch.cuda.stream(train):
+            loss_h.copy_(eng.loss[2:4], non_blocking=True)
+            eng.loss[2:4].zero_()
+            ev_l.record(train)
+        self.comp_stream.wait_event(ev_l)
+        ev_post = torch.cuda.Event()
+        ev_post.record(self.comp_stream)
+        self.inflight = (seq, ev_f, slot)
+        self.pending_posts.put((meta, ev_post, slot, loss_h))
+        self.node.round_step = 0
+        self.round_tokens = 0
+        self.round_t0 = time.time()
+        return True
+
+    def _post_loop(self):
+        torch.cuda.set_device(self.device)
+        while not self.stop.is_set():
+            try:
+                meta, ev, slot, loss_h = self.pending_posts.get(timeout=0.05)
+            except queue.Empty:
+                continue
+            ev.synchronize()
+            cnt = float(loss_h[1])
+            meta.training_loss = float(loss_h[0]) / cnt if cnt > 0 else 0.0
+            st = self.compressor.read_stats()
+            p = self.slots[slot]
+            meta.dense_norm, meta.sparse_norm = st["dense_norm"], st["sparse_norm"]
+            meta.compressed_bytes = p.wire_bytes(st["num_params_kept"])
+            body = meta.to_dict()
+            body["_slot"] = slot
+            body["_count"] = st["num_params_kept"]
+            body["_rank"] = self.rank
+            self.bus.set(f"push/{self.rank}/{meta.seq_num}", json.dumps(body))
+            self.bus.set(f"pushseq/{self.rank}", str(meta.seq_num))
+
+    def _swap(self, new_version: int):
+        if self.node.round_step > 0 and not self.first_round:
+            self._push(partial=True)
+        eng = self.eng
+        train = torch.cuda.current_stream()
+        s32, s16 = self.stage_views(new_version)
+        from ..ops._lib import check, stream_ptr, lib, register, c_void, c_ll
+        register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_void])
+        check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), eng.master.data_ptr(), eng.p16.data_ptr(),
+                               self.compressor.snap.data_ptr(), self.n, stream_ptr(train)), "dt_swap_in")
+        # AdamW is re-created on a checkpoint swap (reference continuous.rs:407-414)
+        eng.m.zero_()
+        eng.v.zero_()
+        eng.hp[9:11].zero_()
+        # error feedback reset at the checkpoint boundary, after any in-flight compression read it
+        ev = torch.cuda.Event()
+        ev.record(train)
+        self.comp_stream.wait_event(ev)
+        with torch.cuda.stream(self.comp_stream):
+            self.compressor.ef.zero_()
+        ev2 = torch.cuda.Event()
+        ev2.record(self.comp_stream)
+        self.ef_ready = ev2
+        self.version = new_version
+        self.node.round_step = 0
+        self.round_tokens = 0
+        self.round_t0 = time.time()
+        ev_done = torch.cuda.Event()
+        ev_done.record(train)
+        ev_done.synchronize()
+        self.bus.set(f"consumed/{self.rank}", str(new_version))
+
+    def close(self):
+        if self.coord is not None:
+            self.coord.close()
+        self.stop.set()
+        self.poster.join(timeout=5)
+        torch.cuda.synchronize()
+
+
+class _Shutdown(Exception):
+    pass
+
+
+class InBoxCoordinator:
+    """Coordinator thread on rank 0: ingest pushes, trigger merges, run the device merge, publish versions."""
+
+    def __init__(self, sync: InBoxSync, run: RunConfig, world: int):
+        self.sync, self.run, self.world = sync, run, world
+        self.bus = sync.bus if world == 1 else StoreBus()
+        self.acc = Accumulator(staleness_decay=run.staleness_decay, max_staleness=run.max_staleness,
+                               min_contributions=0, checkpoint_version=0)
+        for r in range(world):
+            self.acc.heartbeat(f"node-{r:02d}")
+        self.next_seq = [1] * world
+        self.payload_of: Dict[tuple, dict] = {}
+        stream = torch.cuda.Stream(device=sync.device, priority=0)
+        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
+        self.version = 0
+        self.merges: List[dict] = []
+        self.stop = threading.Event()
+        self.error: Optional[BaseException] = None
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def _release(self, rank: int, seq: int):
+        self.bus.set(f"released/{rank}/{seq}", "1")
+
+    def _ingest(self):
+        for r in range(self.world):
+            while True:
+                raw = self.bus.get(f"push/{r}/{self.next_seq[r]}")
+                if raw is None:
+                    break
+                body = json.loads(raw)
+                self.next_seq[r] += 1
+                push = DeltaPush.from_dict(body)
+                prev = [c for c in self.acc.state.contributions if c.node_id == push.node_id]
+                ok, reason = self.acc.push(push)
+                if ok:
+                    self.payload_of[(push.node_id, push.seq_num)] = body
+                    for c in prev:  # replaced by the newer push from the same node
+                        self._release(r, c.seq_num)
+                        self.payload_of.pop((c.node_id, c.seq_num), None)
+                else:
+                    self._release(r, push.seq_num)
+                self.acc.heartbeat(push.node_id)
+
+    def _contribution(self, c) -> Contribution:
+        body = self.payload_of[(c.node_id, c.seq_num)]
+        r, slot, count = body["_rank"], body["_slot"], body["_count"]
+        s = self.sync
+        p = s.slots[slot]
+        base_local = s.pay_buf.data_ptr()
+        peer = s.pay_ptrs[r]
+        off = lambda t: t.data_ptr() - base_local + peer
+        blk = p.block
+        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val),
+                            scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
+                            weight=c.weight, node_id=c.node_id, wire_bytes=p.wire_bytes(count))
+
+    def _wait_consumed(self, version: int, timeout: float = 30.0):
+        """Before writing staging parity of `version`, every node must have left version-2."""
+        need = version - 2
+        if need < 1:
+            return
+        t0 = time.time()
+        for r in range(self.world):
+            while int(self.bus.get(f"consumed/{r}", "0")) < need:
+                if self.stop.is_set():
+                    raise _Shutdown()
+                if time.time() - t0 > timeout:
+                    raise TimeoutError(f"node {r} did not consume version {need}")
+                time.sleep(0.001)
+
+    def _merge(self):
+        snap = self.acc.begin_merge()
+        try:
+            contribs = [self._contribution(c) for c in snap.contributions]
+            new_version = self.version + 1
+            self._wait_consumed(new_version)
+            p32, p16, mc32, mc16 = self.sync.stage_peer_ptrs(new_version)
+            t0 = time.time()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(self.merger.stream)
+            info = self.merger.merge(contribs, self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16, stage32=p32,
+                                     stage16=p16)
+            ev1.record(self.merger.stream)
+            ev1.synchronize()
+            info["device_ms"] = ev0.elapsed_time(ev1)
+            info["wall_ms"] = (time.time() - t0) * 1e3
+            info["version"] = new_version
+            info["n_contrib"] = len(contribs)
+            info["broadcast_bytes"] = self.sync.n * 6 * (1 if mc32 else self.world)
+            info["multicast"] = bool(mc32)
+            self.merges.append(info)
+            for c in snap.contributions:
+                r = int(c.node_id.split("-")[1])
+                self._release(r, c.seq_num)
+                self.payload_of.pop((c.node_id, c.seq_num), None)
+            self.version = new_version
+            tokens = sum(c.tokens_processed for c in snap.contributions)
+            self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
+            self.bus.set("version", str(new_version))
+        except BaseException:
+            self.acc.abort_merge()
+            raise
+
+    def _loop(self):
+        torch.cuda.set_device(self.sync.device)
+        try:
+            while not self.stop.is_set():
+                self._ingest()
+                if self.acc.ready():
+                    self._merge()
+                else:
+                    time.sleep(0.0005)
+        except _Shutdown:
+            pass
+        except BaseException as e:  # surfaced by close()
+            self.error = e
+
+    def close(self):
+        self.stop.set()
+        self.thread.join(timeout=30)
+        if self.error is not None:
+            raise RuntimeError(f"coordinator thread failed: {self.error!r}") from self.error

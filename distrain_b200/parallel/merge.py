@@ -1,0 +1,198 @@
+"""Coordinator merge: validate -> 3x running-average norm clip -> staleness x tokens weighted average ->
+outer (Nesterov) apply, reference coordinator/src/aggregation.rs:154-472.
+
+* ``merge_reference`` - CPU restatement over name->tensor dicts (oracle; also the CPU coordinator path).
+* ``DeviceMerger``   - the in-box path: contributions are compressed payloads that stay in each node's
+  GPU memory; the sm_100a kernels in ``csrc/kernels/merge.cu`` read them through peer pointers,
+  dequantise, weight and scatter-add into a local fp32 accumulator, then apply the update to the global
+  checkpoint and write it (fp32 + bf16) into every node's staging buffer in the same pass.
+"""
+from __future__ import annotations
+
+import math
+import struct
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from ..protocol import clip_scales, validate_stats
+
+
+# ─────────────────────────────── CPU reference ───────────────────────────────
+def validate_delta(delta: Dict[str, torch.Tensor]) -> Optional[str]:
+    if not delta:
+        return "Empty delta"
+    sumsq = 0.0
+    for name, v in delta.items():
+        v = v.float()
+        if torch.isnan(v).any():
+            return f"NaN in {name}"
+        if torch.isinf(v).any():
+            return f"Inf in {name}"
+        mx = float(v.abs().max()) if v.numel() else 0.0
+        if mx > 100.0:
+            return f"Magnitude too large in {name}: {mx:.1f}"
+        sumsq += float((v.double() ** 2).sum())
+    n = math.sqrt(sumsq)
+    if n > 1000.0:
+        return f"Total norm too large: {n:.1f}"
+    if n < 1e-10:
+        return f"Total norm near zero: {n:.2e}"
+    return None
+
+
+def weighted_average(deltas: Sequence[Tuple[Dict[str, torch.Tensor], float]]):
+    if not deltas:
+        return None
+    tot = sum(w for _, w in deltas)
+    if tot == 0:
+        return None
+    keys = list(deltas[0][0].keys())
+    out = {}
+    for k in keys:
+        acc = torch.zeros_like(deltas[0][0][k], dtype=torch.float32)
+        for d, w in deltas:
+            if k in d:
+                acc = acc + d[k].float() * float(w / tot)
+        out[k] = acc
+    return out
+
+
+def nesterov_step(ckpt: Dict[str, torch.Tensor], avg: Dict[str, torch.Tensor], velocity: Optional[Dict], lr: float,
+                  mu: float):
+    if velocity is None:
+        velocity = {k: torch.zeros_like(v) for k, v in avg.items()}
+    for k, p in ckpt.items():
+        if k in avg:
+            v = velocity[k] * mu + avg[k]
+            velocity[k] = v
+            ckpt[k] = p - (v * mu + avg[k]) * lr
+    return ckpt, velocity
+
+
+def merge_reference(ckpt: Dict[str, torch.Tensor], deltas: List[Dict[str, torch.Tensor]], weights: List[float],
+                    velocity=None, outer_lr: float = 1.0, outer_momentum: float = 0.0):
+    """Returns (new_ckpt, velocity, info). Order of ``deltas`` = arrival order (matters for clipping)."""
+    accepted, norms, rejected = [], [], 0
+    eff = []
+    for d, w in zip(deltas, weights):
+        if validate_delta(d) is not None:
+            rejected += 1
+            continue
+        n = math.sqrt(sum(float((t.double() ** 2).sum()) for t in d.values()))
+        e = n
+        if eff:
+            avg = sum(eff) / len(eff)
+            mx = avg * 3.0
+            if n > mx and n > 0:
+                s = mx / n
+                d = {k: t * s for k, t in d.items()}
+                e = mx
+        eff.append(e)
+        accepted.append((d, w))
+    avg = weighted_average(accepted)
+    if avg is None:
+        raise RuntimeError("No valid deltas to aggregate")
+    delta_norm = math.sqrt(sum(float((t.double() ** 2).sum()) for t in avg.values()))
+    new = {k: v.clone() for k, v in ckpt.items()}
+    new, velocity = nesterov_step(new, avg, velocity, outer_lr, outer_momentum)
+    return new, velocity, {"accepted": len(accepted), "rejected": rejected, "outer_delta_norm": delta_norm,
+                           "per_delta_norms": eff}
+
+
+# ─────────────────────────────── device merge ───────────────────────────────
+@dataclass
+class Contribution:
+    """One payload resident in (possibly another GPU's) device memory."""
+    idx_ptr: int
+    q_ptr: int
+    val_ptr: int
+    scales_ptr: int
+    count: int
+    block: int
+    dense: bool
+    weight: float
+    node_id: str = ""
+    wire_bytes: int = 0
+
+
+_CONTRIB_FMT = "<QQQQqiifi"  # matches struct Contrib in merge.cu (56 bytes)
+
+
+class DeviceMerger:
+    def __init__(self, n_params_padded: int, device, theta_init: torch.Tensor, momentum: float = 0.0,
+                 stream: Optional[torch.cuda.Stream] = None):
+        from ..ops import _lib
+        from ..ops._lib import c_int, c_void, c_ll, c_float
+        self.L = _lib.lib()
+        _lib.register("dt_merge_contrib_bytes", [], restype=c_ll)
+        _lib.register("dt_merge_prepass", [c_void, c_int, c_ll, c_void, c_void])
+        _lib.register("dt_merge_accumulate", [c_void, c_int, c_ll, c_void, c_void])
+        _lib.register("dt_merge_apply_broadcast", [c_void, c_void, c_void, c_ll, c_float, c_float, c_void, c_void,
+                                                   c_void, c_void, c_int, c_int, c_void])
+        assert self.L.dt_merge_contrib_bytes() == struct.calcsize(_CONTRIB_FMT)
+        self.device = torch.device(device)
+        self.n = n_params_padded
+        self.theta = theta_init.to(self.device, torch.float32).clone()
+        self.acc = torch.zeros(self.n, dtype=torch.float32, device=self.device)
+        self.vel = torch.zeros(self.n, dtype=torch.float32, device=self.device) if momentum else None
+        self.stream = stream or torch.cuda.Stream(device=self.device, priority=0)
+        self.stats = torch.zeros(3 * 64, dtype=torch.float64, device=self.device)
+        self.stats_host = torch.zeros(3 * 64, dtype=torch.float64).pin_memory()
+        self.desc = torch.zeros(64 * struct.calcsize(_CONTRIB_FMT), dtype=torch.uint8, device=self.device)
+        self.desc_host = torch.zeros_like(self.desc, device="cpu").pin_memory()
+
+    def _upload(self, contribs: List[Contribution], coefs: List[float]):
+        fmt = _CONTRIB_FMT
+        raw = b"".join(struct.pack(fmt, c.idx_ptr if not c.dense else 0, c.q_ptr, c.val_ptr, c.scales_ptr, c.count,
+                                   max(c.block, 1), int(c.dense), float(k), 0) for c, k in zip(contribs, coefs))
+        self.desc_host[:len(raw)].copy_(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
+        self.desc[:len(raw)].copy_(self.desc_host[:len(raw)], non_blocking=True)
+
+    def merge(self, contribs: List[Contribution], outer_lr: float, outer_momentum: float, mc32: int = 0,
+              mc16: int = 0, stage32: Sequence[int] = (), stage16: Sequence[int] = (), write_bf16: bool = True):
+        """Full merge on ``self.stream``; blocks the calling (coordinator) thread on the prepass only.
+        Returns an info dict (accepted, rejected, norms, nvlink bytes)."""
+        from ..ops._lib import check
+        import ctypes
+        n = len(contribs)
+        assert 0 < n <= 64
+        st = self.stream
+        sp = st.cuda_stream
+        maxc = max(c.count for c in contribs)
+        with torch.cuda.stream(st):
+            self._upload(contribs, [1.0] * n)
+            check(self.L.dt_merge_prepass(self.desc.data_ptr(), n, maxc, self.stats.data_ptr(), sp), "dt_merge_prepass")
+            self.stats_host[:3 * n].copy_(self.stats[:3 * n], non_blocking=True)
+        st.synchronize()
+        s = self.stats_host[:3 * n].view(n, 3).tolist()
+        valid, norms = [], []
+        reasons = []
+        for i, (sumsq, mx, nf) in enumerate(s):
+            r = validate_stats(sumsq, mx, nf > 0, empty=contribs[i].count == 0)
+            reasons.append(r)
+            if r is None:
+                valid.append(i)
+                norms.append(math.sqrt(sumsq))
+        if not valid:
+            raise RuntimeError("No valid deltas to aggregate: " + "; ".join(str(r) for r in reasons))
+        scales, eff = clip_scales(norms)
+        wsum = sum(contribs[i].weight for i in valid)
+        coefs = [0.0] * n
+        for j, i in enumerate(valid):
+            coefs[i] = contribs[i].weight / wsum * scales[j]
+        s32 = (ctypes.c_void_p * max(len(stage32), 1))(*stage32) if stage32 else None
+        s16 = (ctypes.c_void_p * max(len(stage16), 1))(*stage16) if stage16 else None
+        with torch.cuda.stream(st):
+            self._upload(contribs, coefs)
+            check(self.L.dt_merge_accumulate(self.desc.data_ptr(), n, maxc, self.acc.data_ptr(), sp),
+                  "dt_merge_accumulate")
+            check(self.L.dt_merge_apply_broadcast(self.theta.data_ptr(),
+                                                  self.vel.data_ptr() if self.vel is not None else None,
+                                                  self.acc.data_ptr(), self.n, float(outer_lr), float(outer_momentum),
+                                                  mc32 or None, mc16 or None, s32, s16, len(stage32),
+                                                  int(write_bf16), sp), "dt_merge_apply_broadcast")
+        pulled = sum(contribs[i].wire_bytes for i in range(n))
+        return {"accepted": len(valid), "rejected": n - len(valid), "reasons": reasons,
+                "per_delta_norms": eff, "coefs": coefs, "pulled_bytes": pulled}

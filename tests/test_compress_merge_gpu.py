@@ -1,0 +1,142 @@
+"""Fused compression and peer-pull merge kernels vs the CPU restatement of the reference algorithms."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _layout():
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout
+    cfg = ModelConfig(hidden_dim=64, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=128, vocab_size=512)
+    return ParamLayout(cfg)
+
+
+@pytest.mark.parametrize("k_fraction,adaptive", [(0.1, True), (0.01, True), (0.99, True), (0.1, False)])
+def test_device_compress_matches_reference(k_fraction, adaptive):
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor, sparsify_topk, quantize_int8
+    L = _layout()
+    dev = torch.device("cuda")
+    torch.manual_seed(0)
+    cfg = CompressionConfig(top_k_fraction=k_fraction, quantize_int8=True, per_tensor_adaptive=adaptive, int8_block=256)
+    comp = DeviceCompressor(L, dev, cfg)
+    snap = torch.zeros(L.total, device=dev)
+    mask = torch.zeros(L.total, dtype=torch.bool, device=dev)
+    for e in L.entries:
+        mask[e.offset:e.offset + e.numel] = True
+    delta = torch.randn(L.total, device=dev) * 1e-3 * mask
+    # per-tensor scale variety so the adaptive budget matters; a few exact ties
+    for i, e in enumerate(L.entries):
+        delta[e.offset:e.offset + e.numel] *= (1 + i % 5)
+    delta[L.entries[3].offset:L.entries[3].offset + 8] = 0.5
+    ef0 = torch.randn(L.total, device=dev) * 1e-4 * mask
+    comp.snap.copy_(snap)
+    comp.ef.copy_(ef0)
+    master = snap - delta
+    comp.begin(master)
+    comp.finish()
+    torch.cuda.synchronize()
+    st = comp.read_stats()
+    K = st["num_params_kept"]
+    p = comp.payload
+    idx = p.idx[:K].long().cpu()
+    vals = p.val[:K].cpu()
+    combined = (delta + ef0).cpu()
+    # reference selection per tensor
+    dd = {e.name: combined[e.offset:e.offset + e.numel] for e in L.entries}
+    _, ridx, rvals = sparsify_topk(dd, k_fraction, adaptive)
+    ref_idx = torch.cat([ridx[e.name] + e.offset for e in L.entries])
+    ref_val = torch.cat([rvals[e.name] for e in L.entries])
+    assert torch.equal(idx, ref_idx)
+    assert torch.equal(vals, ref_val)
+    assert torch.all(idx[1:] > idx[:-1])
+    # error feedback residual: combined with kept entries zeroed
+    ref_ef = combined.clone()
+    ref_ef[ref_idx] = 0
+    assert torch.equal(comp.ef.cpu(), ref_ef)
+    # snapshot refreshed to master
+    assert torch.equal(comp.snap, master)
+    # int8 blocks of 256 over the kept stream
+    q, sc = quantize_int8(ref_val, 256)
+    assert torch.equal(p.q[:K].cpu(), q)
+    assert torch.allclose(p.scales[:sc.numel()].cpu(), sc)
+    assert abs(st["dense_norm"] - float(combined.double().norm())) < 1e-6 * max(1, st["dense_norm"])
+
+
+def test_device_merge_matches_reference():
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload, dequantize_int8
+    from distrain_b200.parallel.merge import DeviceMerger, Contribution, merge_reference
+    L = _layout()
+    dev = torch.device("cuda")
+    torch.manual_seed(1)
+    theta = torch.randn(L.total, device=dev) * 0.02
+    cfg = CompressionConfig(top_k_fraction=0.2, quantize_int8=True, int8_block=256)
+    contribs, dense_deltas, weights = [], [], []
+    keep = []
+    scales_norm = [1.0, 1.0, 10.0]  # third delta is an outlier -> clipped to 3x running average
+    for i in range(3):
+        comp = DeviceCompressor(L, dev, cfg)
+        d = torch.zeros(L.total, device=dev)
+        for e in L.entries:
+            d[e.offset:e.offset + e.numel] = torch.randn(e.numel, device=dev) * 1e-3 * scales_norm[i]
+        comp.snap.copy_(theta)
+        comp.begin(theta - d)
+        comp.finish()
+        torch.cuda.synchronize()
+        K = comp.read_stats()["num_params_kept"]
+        p = comp.payload
+        keep.append(comp)
+        w = 1000.0 * (i + 1) * 0.9 ** i
+        weights.append(w)
+        contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                     scales_ptr=p.scales.data_ptr(), count=K, block=256, dense=False, weight=w,
+                                     wire_bytes=p.wire_bytes(K)))
+        deq = dequantize_int8(p.q[:K].cpu(), p.scales[:(K + 255) // 256].cpu(), 256)
+        dense = torch.zeros(L.total)
+        dense[p.idx[:K].long().cpu()] = deq
+        dense_deltas.append({e.name: dense[e.offset:e.offset + e.numel] for e in L.entries})
+    merger = DeviceMerger(L.total, dev, theta, momentum=0.0)
+    s32 = torch.zeros(L.total, device=dev)
+    s16 = torch.zeros(L.total, device=dev, dtype=torch.bfloat16)
+    info = merger.merge(contribs, 1.0, 0.0, stage32=[s32.data_ptr()], stage16=[s16.data_ptr()])
+    torch.cuda.synchronize()
+    ck = {e.name: theta[e.offset:e.offset + e.numel].cpu() for e in L.entries}
+    new, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=0.0)
+    got = merger.theta.cpu()
+    for e in L.entries:
+        assert torch.allclose(got[e.offset:e.offset + e.numel], new[e.name], atol=1e-7, rtol=1e-5), e.name
+    assert info["accepted"] == 3
+    assert info["per_delta_norms"][2] < info["per_delta_norms"][0] * 3.0001 * 2
+    assert torch.equal(s32, merger.theta)
+    assert torch.equal(s16, merger.theta.bfloat16())
+    assert float(merger.acc.abs().max()) == 0.0
+
+
+def test_inbox_single_gpu_protocol():
+    """One node + coordinator on one GPU: pushes, merges, version swaps, loss decreases."""
+    from distrain_b200.config import bench_config
+    from distrain_b200.parallel.node import InBoxNode
+    run = bench_config("micro")
+    run.model.vocab_size = 512
+    run.push_every = 6
+    run.optim.lr = 3e-3
+    node = InBoxNode(run, rank=0, world=1, device=torch.device("cuda"), enable_push=True)
+    g = torch.Generator().manual_seed(0)
+    batch = torch.randint(0, 512, (run.micro_batch, run.seq_len), generator=g, dtype=torch.int32).cuda()
+    losses = []
+    for i in range(60):
+        node.train_step_device(batch)
+        losses.append(node.engine.loss[0].item())
+    import time
+    time.sleep(0.5)
+    coord = node.sync.coord
+    assert len(coord.merges) >= 3, coord.merges
+    assert node.sync.version >= 2
+    m = coord.merges[-1]
+    assert m["accepted"] == 1 and m["pulled_bytes"] > 0
+    assert losses[-1] < losses[0]
+    node.close()
