@@ -179,6 +179,8 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms_max, launches = t[0].item(), t[1].item(), int(t[2].item())
+    merges = list(node.sync.coord.merges) if (node.sync is not None and node.sync.coord is not None) else []
+    versions = node.sync.version if node.sync is not None else 0
     node.close()
     tokens_per_step = B * S
     value = tokens_per_step * world * args.steps / (ms / 1e3)
@@ -205,6 +207,14 @@ def main():
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if merges:
+            dev_ms = sorted(m["device_ms"] for m in merges)
+            out["merge"] = {"count": len(merges), "node_version": versions,
+                            "device_ms_median": round(dev_ms[len(dev_ms) // 2], 3),
+                            "contributions_last": merges[-1]["n_contrib"],
+                            "pulled_bytes_last": merges[-1]["pulled_bytes"],
+                            "broadcast_bytes_last": merges[-1]["broadcast_bytes"],
+                            "multicast": merges[-1]["multicast"]}
         if e2e_ms is not None:
             out["e2e"] = {"value": round(tokens_per_step * world * args.steps / (e2e_ms_max / 1e3), 1),
                           "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 4}

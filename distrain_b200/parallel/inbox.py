@@ -94,6 +94,8 @@ class InBoxSync:
     def __init__(self, node, run: RunConfig, rank: int, world: int, device):
         self.node, self.run, self.rank, self.world = node, run, rank, world
         self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         eng = node.engine
         self.eng = eng
         self.layout = eng.layout

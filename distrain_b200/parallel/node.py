@@ -24,7 +24,9 @@ class InBoxNode:
                  attn_impl: str = None):
         self.run = run
         self.rank, self.world = rank, world
-        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         if attn_impl is None:
             import os
             attn_impl = os.environ.get("DT_ATTN_IMPL", "dt")
