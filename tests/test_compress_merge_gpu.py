@@ -134,7 +134,8 @@ def test_inbox_single_gpu_protocol():
     import time
     time.sleep(0.5)
     coord = node.sync.coord
-    assert len(coord.merges) >= 3, coord.merges
+    assert coord.error is None, repr(coord.error)
+    assert len(coord.merges) >= 3, (coord.merges, node.sync.seq, coord.next_seq, node.sync.bus.d)
     assert node.sync.version >= 2
     m = coord.merges[-1]
     assert m["accepted"] == 1 and m["pulled_bytes"] > 0

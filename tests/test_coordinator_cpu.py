@@ -1,0 +1,166 @@
+"""Coordinator: accumulator/trigger state machine (mocked clock) and the HTTP service on localhost
+with an FsStore (the reference has no coordinator tests; these restate state.rs / routes.rs /
+aggregation.rs behaviour)."""
+import datetime as dt
+import json
+import time
+
+import pytest
+import torch
+
+from distrain_b200 import protocol as P
+from distrain_b200.config import CoordinatorConfig, CompressionConfig, ModelConfig
+from distrain_b200.utils.storage import FsStore
+from distrain_b200.utils.checkpoint import load_safetensors_bytes
+from distrain_b200.utils.delta_codec import encode_sparse_delta
+from distrain_b200.parallel.compression import compress_reference
+
+
+def _push(node, seq, ver=0, tokens=1000, key=None, loss=5.0):
+    return P.DeltaPush(node_id=node, seq_num=seq, checkpoint_version=ver, inner_steps=10,
+                       delta_key=key or P.delta_path(ver, node, seq), training_loss=loss, tokens_processed=tokens,
+                       training_time_secs=1.0)
+
+
+def test_apply_delta_push_rules():
+    acc = P.AccumulatorState(checkpoint_version=12)
+    ok, r = P.apply_delta_push(acc, _push("a", 1, ver=1), 0.9, 10)
+    assert not ok and r == "Too stale: 11 > 10"
+    ok, _ = P.apply_delta_push(acc, _push("a", 1, ver=10, tokens=100), 0.9, 10)
+    assert ok and abs(acc.contributions[0].weight - 100 * 0.81) < 1e-9
+    ok, r = P.apply_delta_push(acc, _push("a", 1, ver=10), 0.9, 10)
+    assert not ok and r.startswith("Duplicate")
+    ok, _ = P.apply_delta_push(acc, _push("a", 2, ver=12, tokens=50), 0.9, 10)
+    assert ok and len(acc.contributions) == 1 and acc.contributions[0].seq_num == 2
+    assert acc.version == 2 and acc.first_contribution_at is not None
+
+
+def test_trigger_all_active_min_and_patience():
+    cs = P.CoordinatorPersistentState(heartbeats={"a": 1, "b": 1, "c": 1})
+    acc = P.AccumulatorState()
+    t0 = P.utcnow()
+    P.apply_delta_push(acc, _push("a", 1), 0.9, 10, now=t0)
+    assert not P.should_checkpoint(acc, 0, cs, now=t0)          # 1 < max(3//2, 2)
+    P.apply_delta_push(acc, _push("b", 1), 0.9, 10, now=t0)
+    assert not P.should_checkpoint(acc, 0, cs, now=t0 + dt.timedelta(seconds=10))
+    assert P.should_checkpoint(acc, 0, cs, now=t0 + dt.timedelta(seconds=61))   # cold-start patience 60 s
+    assert P.should_checkpoint(acc, 2, cs, now=t0) is False     # override met, but c missing and patience not over
+    P.apply_delta_push(acc, _push("c", 1), 0.9, 10, now=t0)
+    assert P.should_checkpoint(acc, 0, cs, now=t0)              # all active contributed
+    # patience from profiles: cluster max 1.2x, clamped to [30, 300]
+    cs2 = P.CoordinatorPersistentState(heartbeats={"a": 1, "b": 1, "x": 1},
+                                       node_profiles={"a": P.NodeProfile(expected_round_time=100.0),
+                                                      "b": P.NodeProfile(round_time_secs=110.0),
+                                                      "x": P.NodeProfile(expected_round_time=1000.0)})
+    acc2 = P.AccumulatorState()
+    P.apply_delta_push(acc2, _push("a", 1), 0.9, 10, now=t0)
+    P.apply_delta_push(acc2, _push("b", 1), 0.9, 10, now=t0)
+    assert not P.should_checkpoint(acc2, 0, cs2, now=t0 + dt.timedelta(seconds=131))
+    assert P.should_checkpoint(acc2, 0, cs2, now=t0 + dt.timedelta(seconds=132))
+
+
+def test_clip_scales_arrival_order():
+    s, e = P.clip_scales([1.0, 1.0, 10.0, 2.0])
+    assert s[:2] == [1.0, 1.0] and abs(s[2] - 0.3) < 1e-12 and s[3] == 1.0
+    assert e == [1.0, 1.0, 3.0, 2.0]
+
+
+def test_accumulator_carries_over_mid_merge_pushes():
+    a = P.Accumulator()
+    a.heartbeat("x")
+    a.push(_push("x", 1))
+    snap = a.begin_merge()
+    a.push(_push("y", 1))  # arrives during the merge
+    a.finish_merge(1, ["x"], 1000)
+    assert [c.node_id for c in a.state.contributions] == ["y"]
+    assert a.state.checkpoint_version == 1
+    assert a.state.contributions[0].weight == pytest.approx(1000 * 0.9)  # pushed against v0 -> staleness 1
+
+
+def test_wire_types_roundtrip_reference_shapes():
+    js = ('{"node_id":"n1","seq_num":3,"checkpoint_version":2,"inner_steps":5,"delta_key":"k","training_loss":1.5,'
+          '"tokens_processed":100,"training_time_secs":2.0}')
+    p = P.DeltaPush.from_json(js)
+    assert p.compressed_bytes is None and p.tokens_processed == 100
+    r = P.DeltaPushResponse(accepted=True, checkpoint_version=4).to_dict()
+    assert "reason" not in r
+    acc = P.AccumulatorState.from_dict({"checkpoint_version": 1, "contributions": [
+        {"node_id": "n", "seq_num": 1, "weight": 2.0, "checkpoint_version": 1, "inner_steps": 3,
+         "delta_key": "k", "received_at": "2025-01-02T03:04:05.123456789Z"}], "version": 7})
+    assert acc.contributions[0].tokens_processed == 0 and acc.first_contribution_at is None
+    assert P.AccumulatorState.from_dict(acc.to_dict()).to_dict() == acc.to_dict()
+    assert P.checkpoint_path(3) == "checkpoints/v3/model.safetensors"
+    assert P.delta_path(2, "n", 5) == "deltas/v2/n_5.delta.zst"
+    assert P.data_shard_path(7) == "data/shard_0007.bin"
+
+
+@pytest.fixture
+def service(tmp_path):
+    from distrain_b200.coordinator.service import CoordinatorService, bootstrap
+    store = FsStore(str(tmp_path))
+    cfg = ModelConfig(hidden_dim=32, num_layers=1, num_heads=2, num_kv_heads=1, ffn_hidden_dim=64, vocab_size=64)
+    layout, flat = bootstrap(store, cfg, seed=0)
+    ccfg = CoordinatorConfig(min_contributions=0, keep_versions=10)
+    svc = CoordinatorService(ccfg, store, flush_interval=3600)
+    port = svc.start(host="127.0.0.1", port=0, threads=4)
+    yield svc, store, layout, flat, port
+    svc.stop()
+
+
+def test_http_service_end_to_end(service):
+    from distrain_b200.coordinator.client import CoordinatorClient
+    svc, store, layout, flat, port = service
+    cl = CoordinatorClient(f"http://127.0.0.1:{port}")
+    assert cl.health()
+    reg = cl.register(P.RegisterRequest(gpu_model="B200", gpu_memory_gb=180.0, bandwidth_mbps=1e5, node_id="n1",
+                                        hardware={"gpu_model": "B200", "vram_mb": 183359,
+                                                  "device_type": "DiscreteGpu", "cpu_cores": 8, "ram_mb": 1000,
+                                                  "expected_round_time_secs": 30.0}))
+    assert reg.node_id == "n1" and reg.status == "Active" and reg.training_params["lr_max"] == 3e-4
+    cl.register(P.RegisterRequest(gpu_model="B200", gpu_memory_gb=180.0, bandwidth_mbps=1e5, node_id="n2"))
+    for n in ("n1", "n2"):
+        hb = cl.heartbeat(P.HeartbeatRequest(node_id=n, checkpoint_version=0))
+    assert hb.active_nodes == 2 and hb.latest_version == 0 and not hb.should_abort
+    # two nodes push reference-format deltas through the upload proxy
+    sd0 = layout.to_state_dict(flat)
+    shapes = {k: list(v.shape) for k, v in sd0.items()}
+    for i, n in enumerate(("n1", "n2")):
+        torch.manual_seed(i)
+        delta = {k: torch.randn(v.numel()) * 1e-3 for k, v in sd0.items()}
+        sd, stats = compress_reference(delta, shapes, CompressionConfig(top_k_fraction=0.2), {})
+        key = P.delta_path(0, n, 1)
+        cl.upload(key, encode_sparse_delta(sd))
+        r = cl.push_delta(_push(n, 1, ver=0, key=key, tokens=1000 * (i + 1)))
+        assert r.accepted
+    for _ in range(200):
+        if cl.get_latest_checkpoint().version == 1:
+            break
+        time.sleep(0.05)
+    assert cl.get_latest_checkpoint().version == 1, svc.last_error
+    new = load_safetensors_bytes(cl.download(P.checkpoint_path(1)))
+    assert set(new) == set(sd0)
+    meta = json.loads(cl.download(P.checkpoint_metadata_path(1)))
+    assert meta["contributions_accepted"] == 2 and meta["outer_lr"] == 1.0
+    hist = [json.loads(l) for l in store.get(P.stats_history_path()).decode().splitlines()]
+    assert [h["event"] for h in hist].count("delta_accepted") == 2 and hist[-1]["event"] == "checkpoint_produced"
+    st = cl.get_status()
+    assert st.checkpoint_version == 1 and st.accumulator_contributions == 0 and st.active_nodes == 2
+    m = cl.metrics()
+    assert "distrain_checkpoint_version 1" in m and "distrain_delta_pushes_accepted 2" in m
+    # after the merge the accumulator starts over: the same (node, seq) is accepted again at staleness 1,
+    # a repeat of it is a duplicate, and a push 11 versions behind is too stale
+    r = cl.push_delta(_push("n1", 1, ver=0))
+    assert r.accepted and r.checkpoint_version == 1
+    r = cl.push_delta(_push("n1", 1, ver=0))
+    assert not r.accepted and r.reason.startswith("Duplicate")
+    svc.acc.state.checkpoint_version = 12
+    r = cl.push_delta(_push("n2", 5, ver=1))
+    assert not r.accepted and r.reason == "Too stale: 11 > 10"
+    svc.acc.state.checkpoint_version = 1
+    svc.acc.state.contributions.clear()
+    # restart: state reloads from the store
+    svc.flush()
+    from distrain_b200.coordinator.service import CoordinatorService
+    svc2 = CoordinatorService(CoordinatorConfig(), store, flush_interval=3600)
+    assert svc2.acc.state.checkpoint_version == 1
+    assert svc2.acc.cs.total_tokens_trained == 3000
