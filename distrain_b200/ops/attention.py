@@ -5,7 +5,8 @@ head h // (nh/nkv) (reference expand_kv_heads, model.rs:127-138, done here by in
 materialising repeated K/V). ``out`` is [B*T, nh*d] bf16 (heads concatenated, the layout o_proj
 consumes); ``lse`` is the fp32 log-sum-exp [B, nh, T] saved for the backward.
 
-``impl="dt"`` runs the library's flash-attention kernels. ``impl="torch"`` is the plain-PyTorch
+``impl="dt"`` runs the library's flash-attention kernels (tcgen05 forward for d = 64 / 128, mma.sync
+otherwise); ``impl="mma"`` forces the mma.sync forward. ``impl="torch"`` is the plain-PyTorch
 formulation used only as a test oracle on small shapes.
 """
 from __future__ import annotations
@@ -24,7 +25,15 @@ def _reg():
     register("dt_attn_fwd", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float, c_void])
     register("dt_attn_bwd", [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
                              c_int, c_float, c_void])
+    register("dt_attn_fwd_tc", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float, c_void])
     _registered = True
+
+
+def fwd_kernel_for(d: int, impl: str) -> str:
+    """Which forward kernel runs: tcgen05 ('tc') for head dims 64 / 128, the mma.sync kernel otherwise."""
+    if impl == "dt":
+        return "tc" if d in (64, 128) else "mma"
+    return impl
 
 
 def attention_fwd(qkv, out, lse, *, B, T, nh, nkv, d, impl="dt", stream=None):
@@ -35,6 +44,11 @@ def attention_fwd(qkv, out, lse, *, B, T, nh, nkv, d, impl="dt", stream=None):
         lse.copy_(l)
         return
     _reg()
+    kind = fwd_kernel_for(d, impl)
+    if kind == "tc":
+        check(lib().dt_attn_fwd_tc(ptr(qkv), ptr(out), ptr(lse), B, T, nh, nkv, d, float(scale), stream_ptr(stream)),
+              "dt_attn_fwd_tc")
+        return
     check(lib().dt_attn_fwd(ptr(qkv), ptr(out), ptr(lse), B, T, nh, nkv, d, float(scale), stream_ptr(stream)),
           "dt_attn_fwd")
 

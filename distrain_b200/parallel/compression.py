@@ -188,7 +188,8 @@ class DeviceCompressor:
                                         p.capacity, stream_ptr(stream)), "dt_compress_finish")
         check(self.L.dt_compress_export_stats(self.ws.data_ptr(), self.nseg, self.nchunks, self.stats_dev.data_ptr(),
                                               stream_ptr(stream)), "dt_compress_export_stats")
-        self.stats_host.copy_(self.stats_dev, non_blocking=True)
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+            self.stats_host.copy_(self.stats_dev, non_blocking=True)
 
     def read_stats(self) -> dict:
         """Call after the finish stream has been synchronised."""

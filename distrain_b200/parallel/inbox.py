@@ -308,6 +308,7 @@ class InBoxCoordinator:
         self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
         self.version = 0
         self.merges: List[dict] = []
+        self.failed: List[str] = []
         self.stop = threading.Event()
         self.error: Optional[BaseException] = None
         self.thread = threading.Thread(target=self._loop, daemon=True)
@@ -392,9 +393,21 @@ class InBoxCoordinator:
             tokens = sum(c.tokens_processed for c in snap.contributions)
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
             self.bus.set("version", str(new_version))
-        except BaseException:
+        except _Shutdown:
             self.acc.abort_merge()
             raise
+        except Exception as e:
+            # like a failed reference aggregation: count it, drop the contributions of this attempt
+            # (their payload slots are released) and keep serving
+            self.failed.append(repr(e))
+            for c in snap.contributions:
+                r = int(c.node_id.split("-")[1])
+                self._release(r, c.seq_num)
+                self.payload_of.pop((c.node_id, c.seq_num), None)
+            self.acc.state.contributions = [c for c in self.acc.state.contributions
+                                            if (c.node_id, c.seq_num) not in {(x.node_id, x.seq_num)
+                                                                             for x in snap.contributions}]
+            self.acc.abort_merge()
 
     def _loop(self):
         torch.cuda.set_device(self.sync.device)

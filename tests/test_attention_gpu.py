@@ -37,3 +37,23 @@ def test_attention_fwd_bwd(B, T, nh, nkv, d):
     assert _rel(dqkv[:, nh * d:(nh + nkv) * d], dk) < 2e-2
     assert _rel(dqkv[:, (nh + nkv) * d:], dv) < 2e-2
     assert ops.device_error()[0] == 0
+
+
+@pytest.mark.parametrize("B,T,nh,nkv,d", [(2, 128, 4, 2, 64), (2, 100, 4, 1, 64), (1, 1023, 12, 4, 64),
+                                          (2, 300, 16, 4, 128), (1, 257, 8, 8, 128)])
+def test_attention_fwd_tcgen05(B, T, nh, nkv, d):
+    from distrain_b200.ops import attention as A
+    from distrain_b200 import ops
+    torch.manual_seed(1)
+    ops.clear_device_error()
+    W = (nh + 2 * nkv) * d
+    qkv = (torch.randn(B * T, W, device="cuda") * 2.0).bfloat16()
+    out = torch.full((B * T, nh * d), 7.0, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, nh, T, device="cuda")
+    assert A.fwd_kernel_for(d, "dt") == "tc"
+    A.attention_fwd(qkv, out, lse, B=B, T=T, nh=nh, nkv=nkv, d=d, impl="dt")
+    ref_o, ref_lse = A._torch_fwd(qkv, B, T, nh, nkv, d)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert _rel(out, ref_o) < 1e-2
+    assert (lse - ref_lse).abs().max().item() < 2e-2
