@@ -355,6 +355,8 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
     long long w256 = (tm * ((N + 255) / 256) + g_num_sms - 1) / g_num_sms;
     long long w128 = (tm * ((N + 127) / 128) + g_num_sms - 1) / g_num_sms;
     bn = (N <= 128 || w128 * 65 < w256 * 100) ? 128 : 256;
+    // accumulate / split-K problems fill the machine through K splits instead: keep the wide tile
+    if (epi == EPI_F32_ATOMIC && N > 128 && tm * ((N + 255) / 256) < g_num_sms) bn = 256;
   }
   GemmArgs a;
   a.M = M; a.N = N; a.K = K;

@@ -50,8 +50,7 @@ def test_attention_fwd_tcgen05(B, T, nh, nkv, d):
     qkv = (torch.randn(B * T, W, device="cuda") * 2.0).bfloat16()
     out = torch.full((B * T, nh * d), 7.0, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, nh, T, device="cuda")
-    assert A.fwd_kernel_for(d, "dt") == "tc"
-    A.attention_fwd(qkv, out, lse, B=B, T=T, nh=nh, nkv=nkv, d=d, impl="dt")
+    A.attention_fwd(qkv, out, lse, B=B, T=T, nh=nh, nkv=nkv, d=d, impl="tc")
     ref_o, ref_lse = A._torch_fwd(qkv, B, T, nh, nkv, d)
     torch.cuda.synchronize()
     assert ops.device_error()[0] == 0
