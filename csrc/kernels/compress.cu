@@ -411,3 +411,51 @@ DT_API int dt_compress_export_stats(void* ws, int nseg, int nchunks, double* out
   export_stats_kernel<<<(nseg + 255) / 256, 256, 0, st>>>(w.seg, nseg, w.total, out);
   return (int)cudaGetLastError();
 }
+
+// ───────────────────────────── allocation-free entry point ─────────────────────────────
+// dt_compress_noalloc: the same pipeline as dt_compress_begin + dt_compress_finish, for callers that
+// cannot allocate device memory themselves (see compress_noalloc.h). Its workspace is the file-scope
+// array below; host code never dereferences the array's name (on the host it is only a stand-in
+// symbol) - the device address comes from cudaGetSymbolAddress, resolved once per device.
+#include "compress_noalloc.h"
+#include <mutex>
+
+static __device__ __align__(256) unsigned char g_compress_scratch[DT_COMPRESS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+}  // namespace
+
+DT_API long long dt_compress_noalloc_scratch_bytes() { return (long long)DT_COMPRESS_NOALLOC_SCRATCH_BYTES; }
+
+DT_API int dt_compress_noalloc(const float* master, float* snap, float* ef, const int* cseg, const long long* cstart,
+                               const long long* cend, int nchunks, int nseg, const long long* seg_len,
+                               float k_fraction, int adaptive, int* out_idx, float* out_val, signed char* out_q,
+                               float* out_scales, int quant_block, long long capacity, double* stats_out,
+                               cudaStream_t st) {
+  const long long need = dt_compress_workspace_bytes(nseg, nchunks);
+  if (nseg <= 0 || nchunks <= 0 || need > (long long)DT_COMPRESS_NOALLOC_SCRATCH_BYTES) return -20;
+  int dev = 0;
+  DT_CUDA_RET(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return -21;
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_compress_scratch);
+      if (e != cudaSuccess) return (int)e;
+      g_scratch_ptr[dev] = p;
+    }
+    ws = g_scratch_ptr[dev];
+  }
+  // dt_compress_begin clears the whole workspace (histograms, counters) before use
+  int rc = dt_compress_begin(master, snap, ef, cseg, cstart, cend, nchunks, nseg, seg_len, ws, 1, st);
+  if (rc) return rc;
+  rc = dt_compress_finish(ef, cseg, cstart, cend, nchunks, nseg, ws, k_fraction, adaptive, out_idx, out_val, out_q,
+                          out_scales, quant_block, capacity, st);
+  if (rc) return rc;
+  if (stats_out) return dt_compress_export_stats(ws, nseg, nchunks, stats_out, st);
+  return 0;
+}
