@@ -1,6 +1,6 @@
 // HTTP/1.1 server core for the coordinator (reference coordinator/src/main.rs:126-137 serves the same
-// API with axum): POSIX sockets, one acceptor thread, a fixed worker pool, persistent (keep-alive)
-// connections, Content-Length bodies up to a configurable cap (512 MB in the reference), permissive
+// API with axum): POSIX sockets, one poller thread (accepts, and watches idle keep-alive connections),
+// a fixed worker pool that serves a connection only while it has a request, Content-Length bodies up to a configurable cap (512 MB in the reference), permissive
 // CORS (CorsLayer::permissive) including OPTIONS preflight. Requests are handed to a C callback that
 // routes them and fills the response through dtr_http_respond().
 #include <arpa/inet.h>
@@ -10,7 +10,10 @@
 #include <sys/socket.h>
 #include <unistd.h>
 
+#include <fcntl.h>
+
 #include <algorithm>
+#include <chrono>
 #include <atomic>
 #include <cerrno>
 #include <condition_variable>
@@ -34,6 +37,12 @@ struct Response {
 using Handler = void (*)(void* ctx, const char* method, const char* path, const char* body, long long body_len,
                          void* response);
 
+struct Conn {
+  int fd = -1;
+  std::string buf;  // bytes read past the last served request
+  std::chrono::steady_clock::time_point idle_since;
+};
+
 struct Server {
   int fd = -1;
   int port = 0;
@@ -45,7 +54,9 @@ struct Server {
   std::vector<std::thread> workers;
   std::mutex mu;
   std::condition_variable cv;
-  std::deque<int> queue;
+  std::deque<Conn*> queue;      // connections with data, waiting for a worker
+  std::vector<Conn*> idle;      // keep-alive connections watched by the poller
+  int wake[2] = {-1, -1};       // self-pipe: a worker parked a connection
   std::atomic<long long> served{0};
 };
 
@@ -122,11 +133,14 @@ void respond(int fd, const Response& r, bool keep_alive) {
   if (send_all(fd, h.data(), h.size())) send_all(fd, r.body.data(), r.body.size());
 }
 
-void serve_connection(Server* s, int fd) {
-  std::string buf;
-  while (!s->stop.load()) {
+// Serve the requests available on one connection. Returns true if the connection stays open
+// (keep-alive) and should go back to the poller, false if it was closed.
+bool serve_connection(Server* s, Conn* cn) {
+  const int fd = cn->fd;
+  std::string& buf = cn->buf;
+  do {
     size_t hend = 0;
-    if (!read_headers(fd, buf, hend, s->stop)) break;
+    if (!read_headers(fd, buf, hend, s->stop)) return false;
     std::string head = buf.substr(0, hend);
     buf.erase(0, hend);
     size_t le = head.find("\r\n");
@@ -134,7 +148,7 @@ void serve_connection(Server* s, int fd) {
     size_t sp1 = line.find(' '), sp2 = line.rfind(' ');
     if (sp1 == std::string::npos || sp2 == sp1) {
       respond(fd, Response{400, "text/plain", "bad request line"}, false);
-      break;
+      return false;
     }
     std::string method = line.substr(0, sp1), path = line.substr(sp1 + 1, sp2 - sp1 - 1);
     std::string version = line.substr(sp2 + 1);
@@ -157,19 +171,21 @@ void serve_connection(Server* s, int fd) {
     }
     if (chunked) {
       respond(fd, Response{411, "text/plain", "chunked bodies are not supported; send Content-Length"}, false);
-      break;
+      return false;
     }
     if (clen > s->max_body) {
       respond(fd, Response{413, "text/plain", "body exceeds limit"}, false);
-      break;
+      return false;
     }
     while ((long long)buf.size() < clen) {
+      struct pollfd pf{fd, POLLIN, 0};
+      int r = poll(&pf, 1, 30000);
+      if (r <= 0) return false;
       char tmp[1 << 16];
       ssize_t n = ::recv(fd, tmp, sizeof tmp, 0);
-      if (n <= 0) { keep_alive = false; break; }
+      if (n <= 0) return false;
       buf.append(tmp, (size_t)n);
     }
-    if ((long long)buf.size() < clen) break;
     std::string body = buf.substr(0, (size_t)clen);
     buf.erase(0, (size_t)clen);
     Response r;
@@ -181,39 +197,95 @@ void serve_connection(Server* s, int fd) {
     }
     respond(fd, r, keep_alive);
     s->served++;
-    if (!keep_alive) break;
+    if (!keep_alive) return false;
+  } while (buf.find("\r\n\r\n") != std::string::npos);  // pipelined request already buffered
+  return true;
+}
+
+void close_conn(Conn* c) {
+  ::close(c->fd);
+  delete c;
+}
+
+void park(Server* s, Conn* c) {
+  {
+    std::lock_guard<std::mutex> lk(s->mu);
+    c->idle_since = std::chrono::steady_clock::now();
+    s->idle.push_back(c);
   }
-  ::close(fd);
+  char b = 1;
+  (void)!::write(s->wake[1], &b, 1);
 }
 
 void worker_loop(Server* s) {
   while (true) {
-    int fd;
+    Conn* c;
     {
       std::unique_lock<std::mutex> lk(s->mu);
       s->cv.wait(lk, [&] { return s->stop.load() || !s->queue.empty(); });
       if (s->stop.load() && s->queue.empty()) return;
-      fd = s->queue.front();
+      c = s->queue.front();
       s->queue.pop_front();
     }
-    serve_connection(s, fd);
+    if (serve_connection(s, c) && !s->stop.load()) park(s, c);
+    else close_conn(c);
   }
 }
 
+// Poller: accepts connections and watches idle keep-alive connections; a connection with data (or a
+// hang-up) is handed to a worker, so idle clients never hold a worker thread.
 void accept_loop(Server* s) {
+  std::vector<pollfd> pfs;
+  std::vector<Conn*> watched;
   while (!s->stop.load()) {
-    struct pollfd pf{s->fd, POLLIN, 0};
-    int r = poll(&pf, 1, 100);
-    if (r <= 0) continue;
-    int c = ::accept(s->fd, nullptr, nullptr);
-    if (c < 0) continue;
-    int one = 1;
-    setsockopt(c, IPPROTO_TCP, TCP_NODELAY, &one, sizeof one);
+    pfs.clear();
+    watched.clear();
+    pfs.push_back({s->fd, POLLIN, 0});
+    pfs.push_back({s->wake[0], POLLIN, 0});
     {
       std::lock_guard<std::mutex> lk(s->mu);
-      s->queue.push_back(c);
+      auto now = std::chrono::steady_clock::now();
+      std::vector<Conn*> keep;
+      for (Conn* c : s->idle) {
+        if (now - c->idle_since > std::chrono::seconds(60)) { close_conn(c); continue; }
+        keep.push_back(c);
+      }
+      s->idle.swap(keep);
+      for (Conn* c : s->idle) {
+        pfs.push_back({c->fd, POLLIN, 0});
+        watched.push_back(c);
+      }
     }
-    s->cv.notify_one();
+    int r = poll(pfs.data(), pfs.size(), 100);
+    if (r <= 0) continue;
+    if (pfs[1].revents) {
+      char tmp[256];
+      while (::read(s->wake[0], tmp, sizeof tmp) > 0) {}
+    }
+    std::vector<Conn*> ready;
+    if (pfs[0].revents & POLLIN) {
+      int c = ::accept(s->fd, nullptr, nullptr);
+      if (c >= 0) {
+        int one = 1;
+        setsockopt(c, IPPROTO_TCP, TCP_NODELAY, &one, sizeof one);
+        Conn* cn = new Conn;
+        cn->fd = c;
+        std::lock_guard<std::mutex> lk(s->mu);
+        cn->idle_since = std::chrono::steady_clock::now();
+        s->idle.push_back(cn);  // served once it has data
+      }
+    }
+    for (size_t i = 2; i < pfs.size(); ++i)
+      if (pfs[i].revents) ready.push_back(watched[i - 2]);
+    if (!ready.empty()) {
+      std::lock_guard<std::mutex> lk(s->mu);
+      std::vector<Conn*> keep;
+      for (Conn* c : s->idle)
+        if (std::find(ready.begin(), ready.end(), c) == ready.end()) keep.push_back(c);
+      s->idle.swap(keep);
+      for (Conn* c : ready) s->queue.push_back(c);
+    }
+    for (size_t i = 0; i < ready.size(); ++i) s->cv.notify_one();
   }
 }
 
@@ -225,6 +297,9 @@ DT_API void* dtr_http_start(const char* host, int port, int nthreads, long long 
   s->handler = h;
   s->ctx = ctx;
   if (max_body > 0) s->max_body = max_body;
+  if (pipe(s->wake) != 0) { delete s; return nullptr; }
+  fcntl(s->wake[0], F_SETFL, O_NONBLOCK);
+  fcntl(s->wake[1], F_SETFL, O_NONBLOCK);
   s->fd = ::socket(AF_INET, SOCK_STREAM, 0);
   int one = 1;
   setsockopt(s->fd, SOL_SOCKET, SO_REUSEADDR, &one, sizeof one);
@@ -235,6 +310,8 @@ DT_API void* dtr_http_start(const char* host, int port, int nthreads, long long 
   else inet_pton(AF_INET, host, &a.sin_addr);
   if (::bind(s->fd, (sockaddr*)&a, sizeof a) != 0 || ::listen(s->fd, 256) != 0) {
     ::close(s->fd);
+    ::close(s->wake[0]);
+    ::close(s->wake[1]);
     delete s;
     return nullptr;
   }
@@ -267,9 +344,13 @@ DT_API void dtr_http_stop(void* h) {
     if (t.joinable()) t.join();
   {
     std::lock_guard<std::mutex> lk(s->mu);
-    for (int fd : s->queue) ::close(fd);
+    for (Conn* c : s->queue) close_conn(c);
+    for (Conn* c : s->idle) close_conn(c);
     s->queue.clear();
+    s->idle.clear();
   }
   ::close(s->fd);
+  ::close(s->wake[0]);
+  ::close(s->wake[1]);
   delete s;
 }

@@ -1,0 +1,292 @@
+"""Node runtime over the coordinator HTTP API + object store (reference node/cli/src/continuous.rs).
+
+Three concurrent activities, as in the reference (continuous.rs:74-344, 379-675):
+* checkpoint manager - polls GET /checkpoint/latest every ``poll_secs``, downloads new checkpoints;
+* uploader           - compresses each finished round (EF -> top-k -> INT8), uploads it to the store
+                       (or through the coordinator's /upload proxy), then POST /delta; measures upload
+                       bandwidth for the bandwidth-adaptive policy (raw if it fits a 10 s budget, else
+                       adaptive_top_k, trainer.rs:33-70) and recommends H_mini for ~10 s uploads;
+* training loop      - continuous steps; every ``h_mini`` steps it snapshots the round delta and hands it
+                       to the uploader without waiting; on a new checkpoint it pushes the partial round,
+                       swaps weights and restarts AdamW and error feedback; heartbeat every 10 steps.
+
+Backends: ``cpu`` (fp32 oracle model + reference AdamW, the micro-test configuration) and ``cuda``
+(the sm_100a ``TrainEngine``).
+"""
+from __future__ import annotations
+
+import math
+import queue
+import threading
+import time
+from typing import Callable, Dict, List, Optional
+
+import torch
+
+from .. import protocol as P
+from ..config import CompressionConfig, ModelConfig, OptimConfig
+from ..coordinator.client import CoordinatorClient
+from ..models.params import ParamLayout
+from ..utils.checkpoint import load_safetensors_bytes
+from ..utils.delta_codec import encode_sparse_delta
+from .compression import compress_reference
+
+
+def adaptive_top_k(loss: float, max_delta_bytes: Optional[int], raw_param_bytes: int) -> float:
+    """Loss-based retention, capped by the bandwidth budget (reference trainer.rs:33-70)."""
+    if loss > 20.0:
+        k = 0.50
+    elif loss > 10.0:
+        k = 0.60
+    elif loss > 7.0:
+        k = 0.70
+    elif loss > 5.0:
+        k = 0.75
+    else:
+        k = 0.80
+    if max_delta_bytes is not None:
+        mx = max_delta_bytes / (raw_param_bytes * 0.5) if raw_param_bytes > 0 else k
+        k = max(min(k, mx), 0.01)
+    return k
+
+
+class CpuBackend:
+    """fp32 oracle model + reference-semantics AdamW on the host."""
+
+    def __init__(self, cfg: ModelConfig, optim: OptimConfig):
+        from ..models import oracle
+        self.oracle, self.cfg, self.optim = oracle, cfg, optim
+        self.layout = ParamLayout(cfg)
+        self.params: Dict[str, torch.Tensor] = {}
+        self.opt = None
+
+    def load(self, sd: Dict[str, torch.Tensor]):
+        self.params = {k: v.detach().clone().float().requires_grad_() for k, v in sd.items()}
+        o = self.optim
+        self.opt = self.oracle.AdamWRef(self.params, lr=o.lr, betas=(o.beta1, o.beta2), eps=o.eps,
+                                        weight_decay=o.weight_decay, clip=o.grad_clip_norm, clip_global=o.clip_global)
+
+    def state(self) -> Dict[str, torch.Tensor]:
+        return {k: v.detach().clone() for k, v in self.params.items()}
+
+    def loss(self, tokens: torch.Tensor) -> float:
+        with torch.no_grad():
+            return float(self.oracle.lm_loss(self.params, self.cfg, tokens.long()).item())
+
+    def step(self, tokens: torch.Tensor, lr: float) -> float:
+        loss = self.oracle.lm_loss(self.params, self.cfg, tokens.long())
+        if not math.isfinite(loss.item()):
+            for p in self.params.values():
+                p.grad = None
+            return float("nan")
+        loss.backward()
+        self.opt.step(lr)
+        return float(loss.item())
+
+
+class CudaBackend:
+    """The sm_100a training engine (fp32 master, bf16 compute)."""
+
+    def __init__(self, cfg: ModelConfig, optim: OptimConfig, batch: int, seq_len: int, device):
+        from ..models.engine import TrainEngine
+        self.eng = TrainEngine(cfg, batch, seq_len, optim=optim, device=device)
+        self.layout = self.eng.layout
+        self.cfg = cfg
+
+    def load(self, sd):
+        flat = torch.zeros(self.layout.total)
+        self.layout.load_state_dict(flat, sd)
+        self.eng.load_flat(flat)
+
+    def state(self):
+        return self.layout.to_state_dict(self.eng.master)
+
+    def step(self, tokens, lr):
+        self.eng.set_lr(lr)
+        self.eng.set_tokens(tokens.to(self.eng.device, non_blocking=True))
+        self.eng.step()
+        return float(self.eng.loss[0].item())
+
+
+class HttpNode:
+    def __init__(self, coordinator_url: str, store, model_cfg: ModelConfig, batch: int, seq_len: int,
+                 h_mini: int = 50, optim: Optional[OptimConfig] = None, compression: Optional[CompressionConfig] = None,
+                 device: str = "cpu", node_id: Optional[str] = None, data: Optional[Callable[[], torch.Tensor]] = None,
+                 poll_secs: float = 5.0, use_upload_proxy: bool = False, bandwidth_adaptive: bool = False,
+                 heartbeat_every: int = 10):
+        self.client = CoordinatorClient(coordinator_url)
+        self.store = store
+        self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
+        self.optim = optim or OptimConfig()
+        self.comp = compression or CompressionConfig(top_k_fraction=0.1)
+        self.dev = device
+        self.backend = CpuBackend(model_cfg, self.optim) if device == "cpu" else \
+            CudaBackend(model_cfg, self.optim, batch, seq_len, device)
+        self.data = data
+        self.poll_secs, self.use_proxy, self.bw_adaptive = poll_secs, use_upload_proxy, bandwidth_adaptive
+        self.hb_every = heartbeat_every
+        self.node_id = node_id
+        self.version = -1
+        self.seq = 0
+        self.global_step = 0
+        self.stop = threading.Event()
+        self.new_ckpt: "queue.Queue" = queue.Queue()
+        self.up_q: "queue.Queue" = queue.Queue()
+        self.bandwidth_bps = 0.0
+        self.recommended_h_mini = h_mini
+        self.log: List[dict] = []
+        self.pushes: List[dict] = []
+        self.errors: List[str] = []
+        self._ef: Dict[str, torch.Tensor] = {}
+        self._ef_gen = 0        # bumped by the training loop at each checkpoint swap
+        self._ef_gen_seen = 0   # generation the uploader's error buffer belongs to
+        self._threads: List[threading.Thread] = []
+
+    # ─────────── lifecycle ───────────
+    def register(self, gpu_model: str = "cpu", vram_gb: float = 0.0):
+        req = P.RegisterRequest(gpu_model=gpu_model, gpu_memory_gb=vram_gb, bandwidth_mbps=0.0, node_id=self.node_id,
+                                hardware={"gpu_model": gpu_model, "vram_mb": int(vram_gb * 1024),
+                                          "device_type": "Cpu" if self.dev == "cpu" else "DiscreteGpu",
+                                          "cpu_cores": 1, "ram_mb": 0, "h_mini": self.h_mini,
+                                          "batch_size": self.batch})
+        r = self.client.register(req)
+        self.node_id = r.node_id
+        return r
+
+    def _load_version(self, v: int):
+        return load_safetensors_bytes(self.store.get(P.checkpoint_path(v)))
+
+    def _ckpt_manager(self):
+        while not self.stop.wait(self.poll_secs):
+            try:
+                info = self.client.get_latest_checkpoint()
+                if info.version > self.version:
+                    self.new_ckpt.put((info.version, self._load_version(info.version)))
+            except Exception as e:
+                self.errors.append(f"ckpt: {e}")
+
+    def _uploader(self):
+        while not self.stop.is_set() or not self.up_q.empty():
+            try:
+                pkg = self.up_q.get(timeout=0.05)
+            except queue.Empty:
+                continue
+            try:
+                self._compress_upload_push(pkg)
+            except Exception as e:
+                self.errors.append(f"upload: {e}")
+
+    def _compress_upload_push(self, pkg):
+        delta, shapes, push, mean_loss, ef_generation = pkg
+        if ef_generation != self._ef_gen_seen:   # error feedback restarts at a checkpoint boundary
+            self._ef, self._ef_gen_seen = {}, ef_generation
+        cfg = self.comp
+        raw_bytes = sum(t.numel() for t in delta.values()) * 4
+        if self.bw_adaptive and self.bandwidth_bps > 0:
+            budget = int(self.bandwidth_bps * 10)
+            trial_cfg = CompressionConfig(top_k_fraction=1.0, quantize_int8=False, zstd_level=cfg.zstd_level)
+            trial, _ = compress_reference(delta, shapes, trial_cfg, dict(self._ef))
+            if len(encode_sparse_delta(trial, trial_cfg.zstd_level)) <= budget:
+                cfg = trial_cfg
+            else:
+                cfg = CompressionConfig(top_k_fraction=adaptive_top_k(mean_loss, budget, raw_bytes),
+                                        quantize_int8=False, zstd_level=cfg.zstd_level)
+        sd, stats = compress_reference(delta, shapes, cfg, self._ef)
+        blob = encode_sparse_delta(sd, cfg.zstd_level)
+        t0 = time.time()
+        for attempt in range(5):   # 5 retries with backoff (continuous.rs:244-283)
+            try:
+                if self.use_proxy:
+                    self.client.upload(push.delta_key, blob)
+                else:
+                    self.store.put(push.delta_key, blob)
+                break
+            except Exception:
+                if attempt == 4:
+                    raise
+                time.sleep(2 ** attempt * 0.1)
+        secs = max(time.time() - t0, 1e-6)
+        self.bandwidth_bps = len(blob) / secs
+        self.recommended_h_mini = int(min(max(10.0 / secs * push.inner_steps, 10), 500))
+        push.compressed_bytes, push.dense_norm, push.sparse_norm = len(blob), stats["dense_norm"], stats["sparse_norm"]
+        resp = self.client.push_delta(push)
+        self.pushes.append({"seq": push.seq_num, "version": push.checkpoint_version, "accepted": resp.accepted,
+                            "reason": resp.reason, "bytes": len(blob), "retention": stats["retention_ratio"],
+                            "top_k": cfg.top_k_fraction})
+
+    # ─────────── training loop ───────────
+    def _build_push(self, start, steps, tokens, losses, t0):
+        cur = self.backend.state()
+        delta = {k: (start[k].reshape(-1) - cur[k].reshape(-1)).float() for k in start}
+        shapes = {k: list(v.shape) for k, v in start.items()}
+        self.seq += 1
+        mean_loss = sum(losses) / len(losses) if losses else 0.0
+        push = P.DeltaPush(node_id=self.node_id, seq_num=self.seq, checkpoint_version=self.version,
+                           inner_steps=steps, delta_key=P.delta_path(self.version, self.node_id, self.seq),
+                           training_loss=mean_loss, tokens_processed=tokens, training_time_secs=time.time() - t0)
+        self.up_q.put((delta, shapes, push, mean_loss, self._ef_gen))
+
+    def run(self, total_steps: int, stop_on_version: Optional[int] = None):
+        """Train ``total_steps`` steps continuously (or until ``stop_on_version`` is reached)."""
+        if self.node_id is None:
+            self.register()
+        if self.version < 0:
+            info = self.client.get_latest_checkpoint()
+            self.version = info.version
+            self.backend.load(self._load_version(info.version))
+        for fn in (self._ckpt_manager, self._uploader):
+            t = threading.Thread(target=fn, daemon=True)
+            t.start()
+            self._threads.append(t)
+        warm = max(int(self.h_mini * self.optim.warmup_fraction), 2)
+        first_round = True
+        start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+        loss_ema, loss_count = 0.0, 0
+        try:
+            while self.global_step < total_steps:
+                try:
+                    v, sd = self.new_ckpt.get_nowait()
+                except queue.Empty:
+                    v = None
+                if v is not None and v > self.version:
+                    if round_step > 0 and losses:
+                        self._build_push(start, round_step, round_tokens, losses, t0)
+                    self.backend.load(sd)          # fresh AdamW, like the reference's re-entered loop
+                    self._ef_gen += 1
+                    self.version = v
+                    start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+                    if stop_on_version is not None and v >= stop_on_version:
+                        break
+                if round_step >= self.h_mini:
+                    if not (first_round and round_step <= warm):
+                        self._build_push(start, round_step, round_tokens, losses, t0)
+                    start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+                    first_round = False
+                tokens = self.data()
+                lr = self.optim.lr * round_step / warm if (first_round and round_step < warm) else self.optim.lr
+                loss = self.backend.step(tokens, lr)
+                if not math.isfinite(loss):
+                    continue  # NaN loss: skip the update (continuous.rs:607-610)
+                if loss_count > 3 and loss > loss_ema * 3.0 and loss > loss_ema + 5.0:
+                    continue  # loss spike: skip (continuous.rs:613-621)
+                losses.append(loss)
+                loss_count += 1
+                loss_ema = loss if loss_count == 1 else loss_ema * 0.9 + loss * 0.1
+                round_step += 1
+                self.global_step += 1
+                round_tokens += self.batch * self.seq_len
+                self.log.append({"step": self.global_step, "loss": loss, "version": self.version, "lr": lr})
+                if self.global_step % self.hb_every == 0:
+                    threading.Thread(target=self._heartbeat, args=(round_step, loss), daemon=True).start()
+        finally:
+            self.stop.set()
+            for t in self._threads:
+                t.join(timeout=120)
+        return self.log
+
+    def _heartbeat(self, step, loss):
+        try:
+            self.client.heartbeat_sync(P.HeartbeatRequest(node_id=self.node_id, step=step, total_steps=self.h_mini,
+                                                          loss=loss, checkpoint_version=self.version))
+        except Exception:
+            pass  # heartbeat failures are non-fatal (continuous.rs:650-673)

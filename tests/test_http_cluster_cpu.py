@@ -1,0 +1,54 @@
+"""Multi-node without a cluster: coordinator HTTP service + two CPU nodes (fp32 oracle model),
+synthetic tokens, top-k 10% + INT8 deltas through the object store, pushes every few steps."""
+import threading
+
+import pytest
+import torch
+
+from distrain_b200.config import ModelConfig, CoordinatorConfig, CompressionConfig, OptimConfig
+from distrain_b200.coordinator.service import CoordinatorService, bootstrap
+from distrain_b200.parallel.http_node import HttpNode, adaptive_top_k
+from distrain_b200.utils.storage import FsStore
+
+
+def test_adaptive_top_k_reference_table():
+    assert adaptive_top_k(25.0, None, 0) == 0.5 and adaptive_top_k(6.0, None, 0) == 0.75
+    assert adaptive_top_k(4.0, None, 0) == 0.8
+    assert abs(adaptive_top_k(4.0, 10, 1000) - 0.02) < 1e-9 and adaptive_top_k(4.0, 1, 10 ** 9) == 0.01
+
+
+@pytest.mark.timeout(600)
+def test_two_cpu_nodes_and_coordinator(tmp_path):
+    cfg = ModelConfig(hidden_dim=64, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=128, vocab_size=512,
+                      max_seq_len=128, rope_theta=10000.0)
+    store = FsStore(str(tmp_path))
+    bootstrap(store, cfg, seed=0)
+    svc = CoordinatorService(CoordinatorConfig(min_contributions=0), store, flush_interval=3600)
+    port = svc.start(host="127.0.0.1", port=0, threads=4)
+    url = f"http://127.0.0.1:{port}"
+    # a fixed small token pool makes the loss drop visibly within a few dozen steps
+    pool = torch.randint(0, cfg.vocab_size, (8, 33), generator=torch.Generator().manual_seed(3), dtype=torch.int32)
+    nodes = []
+    for i in range(2):
+        g = torch.Generator().manual_seed(10 + i)
+        data = (lambda g=g: pool[torch.randint(0, 8, (4,), generator=g)])
+        n = HttpNode(url, store, cfg, batch=4, seq_len=33, h_mini=5, optim=OptimConfig(lr=3e-3),
+                     compression=CompressionConfig(top_k_fraction=0.1, quantize_int8=True), device="cpu",
+                     node_id=f"cpu-node-{i}", data=data, poll_secs=0.2)
+        n.register()
+        nodes.append(n)
+    th = [threading.Thread(target=n.run, args=(40,)) for n in nodes]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    svc.stop()
+    assert not svc.last_error, svc.last_error
+    assert all(not n.errors for n in nodes), [n.errors for n in nodes]
+    assert svc.acc.state.checkpoint_version >= 2
+    for n in nodes:
+        assert any(p["accepted"] for p in n.pushes)
+        first = sum(x["loss"] for x in n.log[:5]) / 5
+        last = sum(x["loss"] for x in n.log[-5:]) / 5
+        assert last < first, (first, last)
+        assert n.version >= 1
