@@ -1,0 +1,461 @@
+"""Command-line interface: ``python -m distrain_b200 <command>``.
+
+Node commands mirror the reference CLI (node/cli/src/main.rs:24-122): start, bootstrap, benchmark,
+status, config, eval, gpu-stress-test, baseline, generate. Service / tooling commands: coordinator
+(the HTTP coordinator, env-configured like coordinator/src/main.rs:141-188), prepare-data (the data-prep
+script's random-shard mode), micro-cluster (coordinator + N CPU node processes on one host).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import signal
+import subprocess
+import sys
+import time
+
+
+def _store(path_or_url: str):
+    from .utils.storage import open_store
+    return open_store(path_or_url)
+
+
+def _model_cfg(preset: str, vocab=None, seq=None, theta=None):
+    from .config import preset as get_preset, bench_config
+    if preset in ("micro-test-bench", "micro-bench"):
+        m = bench_config("micro").model
+    else:
+        m = get_preset(preset)
+    if vocab:
+        m.vocab_size = vocab
+    if seq:
+        m.max_seq_len = max(m.max_seq_len, seq)
+    if theta:
+        m.rope_theta = theta
+    return m
+
+
+def _infer_model_config(sd):
+    """Model hyper-parameters from checkpoint shapes (reference trainer.rs:837-906)."""
+    from .config import ModelConfig
+    V, H = sd["embedding.embedding.weight"].shape
+    L = 1 + max(int(k.split(".")[1]) for k in sd if k.startswith("layers."))
+    qd = sd["layers.0.attention.q_proj.weight"].shape[0]
+    kvd = sd["layers.0.attention.k_proj.weight"].shape[0]
+    F = sd["layers.0.ffn.gate_proj.weight"].shape[0]
+    for d in (128, 64, 32, 16):  # head_dim used by every preset
+        if qd % d == 0 and kvd % d == 0 and H % d == 0 and H // d == qd // d:
+            break
+    return ModelConfig(hidden_dim=H, num_layers=L, num_heads=qd // d, num_kv_heads=kvd // d, ffn_hidden_dim=F,
+                       vocab_size=V, qkv_bias="layers.0.attention.q_proj.bias" in sd)
+
+
+def _data_source(args, vocab, batch, seq, seed):
+    if getattr(args, "data_dir", None):
+        from .utils.data import ShardLoader
+        files = sorted(os.path.join(args.data_dir, f) for f in os.listdir(args.data_dir) if f.endswith(".bin"))
+        loader = ShardLoader(files, seq, batch, max_resident=8)
+        if getattr(args, "seek_seed", None) is not None:
+            loader.seek_by_seed(args.seek_seed)
+        return loader.next_batch
+    from .utils.data import SyntheticTokens
+    return SyntheticTokens(vocab, batch, seq, seed).next_batch
+
+
+# ─────────────────────────────── commands ───────────────────────────────
+def cmd_coordinator(args):
+    from .config import CoordinatorConfig
+    from .coordinator.service import CoordinatorService
+    cfg = CoordinatorConfig.from_env()
+    if args.port is not None:
+        cfg.port = args.port
+    store = _store(args.store)
+    svc = CoordinatorService(cfg, store, merge_device=args.merge_device)
+    port = svc.start(host=args.host or cfg.host)
+    print(json.dumps({"event": "coordinator_started", "port": port}), flush=True)
+    stop = []
+    signal.signal(signal.SIGTERM, lambda *a: stop.append(1))
+    try:
+        while not stop:
+            time.sleep(0.5)
+    except KeyboardInterrupt:
+        pass
+    svc.stop()
+
+
+def cmd_bootstrap(args):
+    from .coordinator.service import bootstrap
+    m = _model_cfg(args.preset, args.vocab, args.seq_len, args.rope_theta)
+    L, _ = bootstrap(_store(args.store), m, seed=args.seed)
+    print(json.dumps({"event": "bootstrapped", "version": 0, "params": L.num_params(), "model": m.to_dict()}))
+
+
+def cmd_start(args):
+    from .config import CompressionConfig, OptimConfig
+    from .parallel.http_node import HttpNode
+    from .utils.checkpoint import load_safetensors_bytes
+    from .coordinator.client import CoordinatorClient
+    from . import protocol as P
+    store = _store(args.store)
+    cl = CoordinatorClient(args.coordinator_url)
+    v = cl.get_latest_checkpoint().version
+    m = _infer_model_config(load_safetensors_bytes(store.get(P.checkpoint_path(v))))
+    if args.rope_theta:
+        m.rope_theta = args.rope_theta
+    m.max_seq_len = max(m.max_seq_len, args.seq_len)
+    device = "cpu" if args.cpu else (args.device or "cuda:0")
+    data = _data_source(args, m.vocab_size, args.batch_size, args.seq_len, args.seed)
+    node = HttpNode(args.coordinator_url, store, m, args.batch_size, args.seq_len, h_mini=args.h_mini,
+                    optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
+                                                                                 quantize_int8=not args.no_int8),
+                    device=device, node_id=args.node_id, data=data, poll_secs=args.poll_secs,
+                    bandwidth_adaptive=args.bandwidth_adaptive)
+    node.register(gpu_model="cpu" if device == "cpu" else "B200")
+    log = node.run(args.steps)
+    out = {"event": "node_done", "node_id": node.node_id, "steps": len(log), "version": node.version,
+           "first_loss": log[0]["loss"] if log else None, "last_loss": log[-1]["loss"] if log else None,
+           "pushes": len(node.pushes), "accepted": sum(p["accepted"] for p in node.pushes), "errors": node.errors}
+    if args.metrics_out:
+        with open(args.metrics_out, "w") as f:
+            for r in log:
+                f.write(json.dumps(r) + "\n")
+    print(json.dumps(out), flush=True)
+
+
+def cmd_status(args):
+    from .coordinator.client import CoordinatorClient
+    print(json.dumps(CoordinatorClient(args.coordinator_url).get_status().to_dict(), indent=2))
+
+
+def cmd_config(args):
+    from .config import TrainingParams
+    out = {"local_training_params": TrainingParams().to_dict()}
+    if args.coordinator_url:
+        from .coordinator.client import CoordinatorClient
+        out["coordinator"] = CoordinatorClient(args.coordinator_url).get_config()
+    print(json.dumps(out, indent=2))
+
+
+def _eval_loss(sd, cfg, batches, device):
+    import torch
+    from .models import oracle
+    p = {k: v.to(device) for k, v in sd.items()}
+    tot = 0.0
+    with torch.no_grad():
+        for b in batches:
+            tot += float(oracle.lm_loss(p, cfg, b.to(device).long()).item())
+    return tot / max(len(batches), 1)
+
+
+def cmd_eval(args):
+    import torch
+    from .utils.checkpoint import load_safetensors
+    res = []
+    for ck in args.checkpoints:
+        sd = load_safetensors(ck)
+        cfg = _infer_model_config(sd)
+        if args.rope_theta:
+            cfg.rope_theta = args.rope_theta
+        cfg.max_seq_len = max(cfg.max_seq_len, args.seq_len)
+        src = _data_source(args, cfg.vocab_size, args.batch_size, args.seq_len, args.seed)
+        batches = [src() for _ in range(args.batches)]
+        dev = args.device or ("cuda:0" if torch.cuda.is_available() else "cpu")
+        res.append({"checkpoint": ck, "loss": _eval_loss(sd, cfg, batches, dev), "batches": args.batches})
+    print(json.dumps(res, indent=2))
+
+
+def cmd_baseline(args):
+    """Single-device baseline (no coordinator, no compression), cosine LR with warmup, JSONL per step
+    (reference main.rs:1110-1216)."""
+    import torch
+    from .config import cosine_lr, OptimConfig
+    from .utils.checkpoint import load_safetensors
+    sd = load_safetensors(args.checkpoint)
+    cfg = _infer_model_config(sd)
+    if args.rope_theta:
+        cfg.rope_theta = args.rope_theta
+    cfg.max_seq_len = max(cfg.max_seq_len, args.seq_len)
+    src = _data_source(args, cfg.vocab_size, args.batch_size, args.seq_len, args.seed)
+    warm = int(args.steps * 0.2)
+    if args.cpu:
+        from .parallel.http_node import CpuBackend
+        be = CpuBackend(cfg, OptimConfig(lr=args.lr_max))
+        be.load(sd)
+        step = lambda toks, lr: be.step(toks, lr)
+    else:
+        from .models.engine import TrainEngine
+        from .models.params import ParamLayout
+        L = ParamLayout(cfg)
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, sd)
+        eng = TrainEngine(cfg, args.batch_size, args.seq_len, optim=OptimConfig(lr=args.lr_max),
+                          device=args.device or "cuda:0", flat_init=flat)
+
+        def step(toks, lr):
+            eng.set_lr(lr)
+            eng.set_tokens(toks.to(eng.device))
+            eng.step()
+            return float(eng.loss[0].item())
+    with open(args.output, "w") as f:
+        for s in range(args.steps):
+            lr = cosine_lr(s, warm, args.steps, args.lr_max, args.lr_max * 0.1)
+            loss = step(src(), lr)
+            f.write(json.dumps({"step": s + 1, "loss": loss, "lr": lr,
+                                "tokens": (s + 1) * args.batch_size * args.seq_len}) + "\n")
+    print(json.dumps({"event": "baseline_done", "steps": args.steps, "output": args.output}))
+
+
+def cmd_generate(args):
+    """Greedy / temperature sampling by full re-forward (the reference has no KV cache, main.rs:1416-1548)."""
+    import torch
+    from .models import oracle
+    from .utils.checkpoint import load_safetensors
+    sd = load_safetensors(args.checkpoint)
+    cfg = _infer_model_config(sd)
+    if args.rope_theta:
+        cfg.rope_theta = args.rope_theta
+    cfg.max_seq_len = max(cfg.max_seq_len, args.max_tokens + 64)
+    ids = [int(x) for x in args.prompt_ids.split(",")] if args.prompt_ids else [1]
+    tok = None
+    if args.tokenizer:
+        from tokenizers import Tokenizer
+        tok = Tokenizer.from_file(args.tokenizer)
+        ids = tok.encode(args.prompt).ids
+    g = torch.Generator().manual_seed(args.seed)
+    with torch.no_grad():
+        for _ in range(args.max_tokens):
+            x = torch.tensor([ids[-cfg.max_seq_len:]])
+            z = oracle.logits_fn(sd, cfg, x)[0, -1]
+            if args.temperature <= 0:
+                nxt = int(z.argmax())
+            else:
+                nxt = int(torch.multinomial(torch.softmax(z / args.temperature, -1), 1, generator=g))
+            ids.append(nxt)
+    print(json.dumps({"ids": ids, "text": tok.decode(ids) if tok else None}))
+
+
+def cmd_benchmark(args):
+    """Measure this device's training step time and the largest batch that fits (calibration)."""
+    import torch
+    from .config import bench_config
+    from .models.engine import TrainEngine
+    run = bench_config(args.preset)
+    eng = TrainEngine(run.model, args.batch_size or run.micro_batch, args.seq_len or run.seq_len,
+                      device=args.device or "cuda:0")
+    toks = torch.randint(0, run.model.vocab_size, (eng.B, eng.S), dtype=torch.int32, device=eng.device)
+    eng.set_tokens(toks)
+    eng.capture()
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        eng.step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    free, total = torch.cuda.mem_get_info()
+    print(json.dumps({"preset": args.preset, "batch": eng.B, "seq_len": eng.S, "ms_per_step": round(ms, 3),
+                      "tokens_per_sec": round(eng.B * eng.S / ms * 1e3, 1),
+                      "mem_used_gb": round((total - free) / 2 ** 30, 2), "mem_total_gb": round(total / 2 ** 30, 2)}))
+
+
+def cmd_gpu_stress_test(args):
+    """Child-process probe: one step at (batch, seq) from a checkpoint; exit 0 if it fits (trainer.rs:776-827)."""
+    import torch
+    from .utils.checkpoint import load_safetensors
+    from .models.engine import TrainEngine
+    from .models.params import ParamLayout
+    sd = load_safetensors(args.checkpoint)
+    cfg = _infer_model_config(sd)
+    cfg.max_seq_len = max(cfg.max_seq_len, args.seq_len)
+    try:
+        L = ParamLayout(cfg)
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, sd)
+        eng = TrainEngine(cfg, args.batch_size, args.seq_len, device=args.device or "cuda:0", flat_init=flat)
+        eng.set_tokens(torch.randint(0, cfg.vocab_size, (eng.B, eng.S), dtype=torch.int32, device=eng.device))
+        eng.step_kernels()
+        torch.cuda.synchronize()
+        ok = math.isfinite(eng.loss[0].item())
+    except torch.cuda.OutOfMemoryError:
+        ok = False
+    print(json.dumps({"batch_size": args.batch_size, "seq_len": args.seq_len, "fits": ok}))
+    sys.exit(0 if ok else 3)
+
+
+def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 256, device="cuda:0") -> int:
+    """Binary search of the largest batch that fits, each probe in a child process so an out-of-memory
+    failure cannot take down the caller (reference trainer.rs:733-834)."""
+    best = 0
+    while lo <= hi:
+        mid = (lo + hi) // 2
+        r = subprocess.run([sys.executable, "-m", "distrain_b200", "gpu-stress-test", checkpoint, "--batch-size",
+                            str(mid), "--seq-len", str(seq_len), "--device", device], capture_output=True)
+        if r.returncode == 0:
+            best, lo = mid, mid + 1
+        else:
+            hi = mid - 1
+    return best
+
+
+def cmd_prepare_data(args):
+    from .utils.data import prepare_random_shards
+    m = prepare_random_shards(args.output_dir, args.num_shards, args.tokens_per_shard, args.vocab, args.seed)
+    if args.upload_store:
+        st = _store(args.upload_store)
+        for f in os.listdir(args.output_dir):
+            key = "data/manifest.json" if f == "manifest.json" else f"data/{f}"
+            st.upload_from_file(os.path.join(args.output_dir, f), key)
+    print(json.dumps({"event": "prepared", "num_shards": m["num_shards"], "total_tokens": m["total_tokens"]}))
+
+
+def cmd_micro_cluster(args):
+    """Coordinator + N CPU node processes on the micro-test workload (vocab 32768, seq 128, batch 4,
+    theta 1e4, push every 20 steps, top-k 10% + INT8)."""
+    import tempfile
+    root = args.store or tempfile.mkdtemp(prefix="distrain-micro-")
+    env = dict(os.environ, PORT=str(args.port), MIN_CONTRIBUTIONS="0", OUTER_LR="1.0", OUTER_MOMENTUM="0.0")
+    py = [sys.executable, "-m", "distrain_b200"]
+    subprocess.run(py + ["bootstrap", "--preset", "micro-bench", "--store", root, "--seed", "0"], check=True, env=env)
+    coord = subprocess.Popen(py + ["coordinator", "--store", root, "--host", "127.0.0.1"], env=env,
+                             stdout=subprocess.PIPE, text=True)
+    coord.stdout.readline()
+    url = f"http://127.0.0.1:{args.port}"
+    nodes = [subprocess.Popen(py + ["start", "--coordinator-url", url, "--store", root, "--cpu", "--steps",
+                                    str(args.steps), "--batch-size", "4", "--seq-len", "128", "--h-mini", "20",
+                                    "--rope-theta", "10000", "--node-id", f"micro-{i}", "--seed", str(100 + i),
+                                    "--poll-secs", "1"], env=env, stdout=subprocess.PIPE, text=True)
+             for i in range(args.nodes)]
+    outs = [json.loads(n.communicate()[0].strip().splitlines()[-1]) for n in nodes]
+    coord.send_signal(signal.SIGTERM)
+    coord.wait(timeout=60)
+    print(json.dumps({"event": "micro_cluster_done", "store": root, "nodes": outs}))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="distrain_b200")
+    sp = ap.add_subparsers(dest="cmd", required=True)
+
+    p = sp.add_parser("coordinator", help="run the coordinator HTTP service")
+    p.add_argument("--store", required=True, help="object store: directory / file:// path, or http(s):// S3 endpoint")
+    p.add_argument("--host")
+    p.add_argument("--port", type=int)
+    p.add_argument("--merge-device", default="cpu")
+    p.set_defaults(fn=cmd_coordinator)
+
+    p = sp.add_parser("bootstrap", help="create and store checkpoint v0")
+    p.add_argument("--store", required=True)
+    p.add_argument("--preset", default="tiny")
+    p.add_argument("--vocab", type=int)
+    p.add_argument("--seq-len", type=int)
+    p.add_argument("--rope-theta", type=float)
+    p.add_argument("--seed", type=int, default=0)
+    p.set_defaults(fn=cmd_bootstrap)
+
+    p = sp.add_parser("start", help="run a training node against a coordinator")
+    p.add_argument("--coordinator-url", required=True)
+    p.add_argument("--store", required=True)
+    p.add_argument("--cpu", action="store_true")
+    p.add_argument("--device")
+    p.add_argument("--node-id")
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--batch-size", type=int, default=4)
+    p.add_argument("--seq-len", type=int, default=512)
+    p.add_argument("--h-mini", type=int, default=50)
+    p.add_argument("--lr", type=float, default=3e-4)
+    p.add_argument("--top-k", type=float, default=0.1)
+    p.add_argument("--no-int8", action="store_true")
+    p.add_argument("--bandwidth-adaptive", action="store_true")
+    p.add_argument("--data-dir")
+    p.add_argument("--seek-seed", type=int)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--rope-theta", type=float)
+    p.add_argument("--poll-secs", type=float, default=5.0)
+    p.add_argument("--metrics-out")
+    p.set_defaults(fn=cmd_start)
+
+    p = sp.add_parser("status", help="coordinator training status")
+    p.add_argument("--coordinator-url", required=True)
+    p.set_defaults(fn=cmd_status)
+
+    p = sp.add_parser("config", help="effective training parameters")
+    p.add_argument("--coordinator-url")
+    p.set_defaults(fn=cmd_config)
+
+    p = sp.add_parser("eval", help="loss of checkpoint(s) on data without training")
+    p.add_argument("checkpoints", nargs="+")
+    p.add_argument("--batches", type=int, default=50)
+    p.add_argument("--batch-size", type=int, default=4)
+    p.add_argument("--seq-len", type=int, default=512)
+    p.add_argument("--data-dir")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--device")
+    p.add_argument("--rope-theta", type=float)
+    p.set_defaults(fn=cmd_eval)
+
+    p = sp.add_parser("baseline", help="single-device baseline training, JSONL metrics")
+    p.add_argument("checkpoint")
+    p.add_argument("--data-dir")
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--output", default="baseline.jsonl")
+    p.add_argument("--cpu", action="store_true")
+    p.add_argument("--device")
+    p.add_argument("--batch-size", type=int, default=4)
+    p.add_argument("--seq-len", type=int, default=512)
+    p.add_argument("--lr-max", type=float, default=3e-4)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--rope-theta", type=float)
+    p.set_defaults(fn=cmd_baseline)
+
+    p = sp.add_parser("generate", help="sample tokens from a checkpoint")
+    p.add_argument("checkpoint")
+    p.add_argument("--prompt", default="The")
+    p.add_argument("--prompt-ids")
+    p.add_argument("--tokenizer")
+    p.add_argument("--max-tokens", type=int, default=32)
+    p.add_argument("--temperature", type=float, default=0.0)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--rope-theta", type=float)
+    p.set_defaults(fn=cmd_generate)
+
+    p = sp.add_parser("benchmark", help="step time / throughput of this device")
+    p.add_argument("--preset", default="tiny")
+    p.add_argument("--batch-size", type=int)
+    p.add_argument("--seq-len", type=int)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--device")
+    p.set_defaults(fn=cmd_benchmark)
+
+    p = sp.add_parser("gpu-stress-test", help="(internal) one-step fit probe for batch calibration")
+    p.add_argument("checkpoint")
+    p.add_argument("--batch-size", type=int, required=True)
+    p.add_argument("--seq-len", type=int, required=True)
+    p.add_argument("--device")
+    p.set_defaults(fn=cmd_gpu_stress_test)
+
+    p = sp.add_parser("prepare-data", help="write uint16 token shards + manifest (random test mode)")
+    p.add_argument("--output-dir", required=True)
+    p.add_argument("--num-shards", type=int, default=4)
+    p.add_argument("--tokens-per-shard", type=int, default=10_000_000)
+    p.add_argument("--vocab", type=int, default=32768)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--upload-store")
+    p.set_defaults(fn=cmd_prepare_data)
+
+    p = sp.add_parser("micro-cluster", help="coordinator + CPU nodes on the micro-test workload")
+    p.add_argument("--nodes", type=int, default=2)
+    p.add_argument("--steps", type=int, default=60)
+    p.add_argument("--port", type=int, default=18731)
+    p.add_argument("--store")
+    p.set_defaults(fn=cmd_micro_cluster)
+
+    args = ap.parse_args(argv)
+    args.fn(args)
+
+
+if __name__ == "__main__":
+    main()

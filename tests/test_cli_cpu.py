@@ -1,0 +1,52 @@
+"""CLI end to end on CPU: bootstrap, coordinator + two node processes on the micro-test workload,
+eval / baseline / generate / status / prepare-data."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PY = [sys.executable, "-m", "distrain_b200"]
+
+
+def run(args, **kw):
+    return subprocess.run(PY + args, cwd=ROOT, capture_output=True, text=True, timeout=600, **kw)
+
+
+@pytest.mark.timeout(900)
+def test_micro_cluster_processes(tmp_path):
+    r = run(["micro-cluster", "--nodes", "2", "--steps", "45", "--port", "18991", "--store", str(tmp_path / "s")])
+    assert r.returncode == 0, r.stderr[-3000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    for n in out["nodes"]:
+        assert n["steps"] == 45 and n["accepted"] >= 1 and not n["errors"], n
+        # uniform-random tokens: the loss sits at the entropy floor ln(32768) = 10.397 (no signal to learn)
+        assert abs(n["last_loss"] - 10.397) < 0.3 and n["version"] >= 1
+    assert os.path.exists(tmp_path / "s" / "distrain-training" / "checkpoints" / "v1" / "model.safetensors")
+
+
+def test_bootstrap_eval_baseline_generate(tmp_path):
+    st = str(tmp_path / "store")
+    r = run(["bootstrap", "--preset", "micro", "--store", st])
+    assert r.returncode == 0, r.stderr
+    ck = os.path.join(st, "distrain-training", "checkpoints", "v0", "model.safetensors")
+    r = run(["eval", ck, "--batches", "2", "--batch-size", "2", "--seq-len", "17", "--device", "cpu"])
+    assert r.returncode == 0, r.stderr
+    loss = json.loads(r.stdout)[0]["loss"]
+    assert abs(loss - 5.545) < 0.5  # ~ln(256) at init
+    out = str(tmp_path / "b.jsonl")
+    r = run(["baseline", ck, "--cpu", "--steps", "4", "--batch-size", "2", "--seq-len", "17", "--output", out])
+    assert r.returncode == 0, r.stderr
+    rows = [json.loads(l) for l in open(out)]
+    assert len(rows) == 4 and rows[0]["lr"] == 0.0 and rows[-1]["tokens"] == 4 * 2 * 17
+    r = run(["generate", ck, "--prompt-ids", "1,2,3", "--max-tokens", "5"])
+    assert r.returncode == 0, r.stderr
+    assert len(json.loads(r.stdout)["ids"]) == 8
+    r = run(["prepare-data", "--output-dir", str(tmp_path / "d"), "--num-shards", "2", "--tokens-per-shard", "1000",
+             "--vocab", "256"])
+    assert r.returncode == 0 and json.loads(r.stdout)["total_tokens"] == 2000
+    r = run(["eval", ck, "--batches", "1", "--batch-size", "2", "--seq-len", "17", "--data-dir", str(tmp_path / "d"),
+             "--device", "cpu"])
+    assert r.returncode == 0, r.stderr
