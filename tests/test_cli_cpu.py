@@ -37,10 +37,12 @@ def test_bootstrap_eval_baseline_generate(tmp_path):
     loss = json.loads(r.stdout)[0]["loss"]
     assert abs(loss - 5.545) < 0.5  # ~ln(256) at init
     out = str(tmp_path / "b.jsonl")
-    r = run(["baseline", ck, "--cpu", "--steps", "4", "--batch-size", "2", "--seq-len", "17", "--output", out])
+    r = run(["baseline", ck, "--cpu", "--steps", "10", "--batch-size", "2", "--seq-len", "17", "--output", out])
     assert r.returncode == 0, r.stderr
     rows = [json.loads(l) for l in open(out)]
-    assert len(rows) == 4 and rows[0]["lr"] == 0.0 and rows[-1]["tokens"] == 4 * 2 * 17
+    # 20% linear warm-up (2 steps) then cosine decay to 0.1 x lr_max
+    assert len(rows) == 10 and rows[0]["lr"] == 0.0 and rows[2]["lr"] == pytest.approx(3e-4)
+    assert rows[-1]["tokens"] == 10 * 2 * 17 and rows[-1]["lr"] < rows[2]["lr"]
     r = run(["generate", ck, "--prompt-ids", "1,2,3", "--max-tokens", "5"])
     assert r.returncode == 0, r.stderr
     assert len(json.loads(r.stdout)["ids"]) == 8
