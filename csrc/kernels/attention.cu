@@ -1,4 +1,5 @@
 // Causal GQA flash attention, forward and backward, bf16 in / fp32 softmax statistics.
+// LSE and delta rows are [B, nh, Tp] with Tp = T rounded up to a multiple of 4 (16-byte aligned rows).
 //
 // Reads q/k/v straight out of the fused QKV activation ([B*T, (nh+2nkv)*D], after bias+RoPE): query
 // head h uses kv head h / (nh/nkv) (reference expand_kv_heads, core/model/src/model.rs:127-138, by
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const __nv_bfloat16* __res
       for (int dt = 0; dt < D / 8; ++dt) {
         *reinterpret_cast<uint32_t*>(orow + dt * 8 + tig * 2) = pack_bf16(o[dt][2 * i] * inv, o[dt][2 * i + 1] * inv);
       }
-      if (tig == 0) lse[((long long)b * nh + h) * T + q] = (m_[i] + log2f(l)) * LN2;
+      if (tig == 0) lse[((long long)b * nh + h) * ((T + 3) & ~3) + q] = (m_[i] + log2f(l)) * LN2;
     }
   }
 }
@@ -249,7 +250,7 @@ __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, const
     }
   }
   const long long b = row / T, t = row % T;
-  delta[(b * nh + h) * T + t] = acc;
+  delta[(b * nh + h) * ((T + 3) & ~3) + t] = acc;
 }
 
 template <int D>
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(NT) attn_bwd_kernel(const __nv_bfloat16* __res
       cp_async_commit();
       if (threadIdx.x < 64) {
         int q = qb * BM + threadIdx.x;
-        long long idx = ((long long)b * nh + h) * T + q;
+        long long idx = ((long long)b * nh + h) * ((T + 3) & ~3) + q;
         slse[threadIdx.x] = (q < T) ? lse[idx] * LOG2E : INFINITY;
         sdel[threadIdx.x] = (q < T) ? delta[idx] : 0.f;
       }
@@ -468,5 +469,15 @@ DT_API int dt_attn_bwd(const void* qkv, const void* out, const void* dout, const
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   dq_convert_kernel<<<(unsigned)blocks, 256, 0, st>>>(dq_acc, dq, M, nh * D, (long long)(nh + 2 * nkv) * D);
+  return (int)cudaGetLastError();
+}
+
+// delta = rowsum(dO * O) per (row, head) into [B, nh, Tp] (the tcgen05 backward's pre-pass).
+DT_API int dt_attn_bwd_delta(const void* out, const void* dout, float* delta, int B, int T, int nh, int D,
+                             cudaStream_t st) {
+  if (D % 8) return -10;
+  long long items = (long long)B * T * nh;
+  attn_bwd_pre_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), delta, B, T, nh, D);
   return (int)cudaGetLastError();
 }

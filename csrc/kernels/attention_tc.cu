@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
           }
         }
       }
-      if (q < T) lse[((long long)b * nh + h) * T + q] = (m_run + log2f(l_run)) * LN2_F;
+      if (q < T) lse[((long long)b * nh + h) * ((T + 3) & ~3) + q] = (m_run + log2f(l_run)) * LN2_F;
     }
   }
 
@@ -342,5 +342,514 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
   if (nh % nkv) return -10;
   if (D == 64) return fwd_tc_launch<64>(qkv, out, lse, B, T, nh, nkv, scale, st);
   if (D == 128) return fwd_tc_launch<128>(qkv, out, lse, B, T, nh, nkv, scale, st);
+  return -11;
+}
+
+// ═══════════════════════════════ backward (tcgen05) ═══════════════════════════════
+// Two kernels, no atomics and no fp32 dQ scratch:
+//   attn_bwd_kv_tc: CTA = 128 keys of one kv head; loops over the kv group's query heads and the
+//     causal query blocks i >= key block. Per block: S^T = K Q^T and dP^T = V dO^T into TMEM;
+//     8 element-wise warps (thread = key row, half of the 128 query columns; the backward needs no row
+//     reduction) form P^T = exp2(S^T*c - LSE) and dS^T = P^T (dP^T - delta) in bf16 shared tiles;
+//     dV += P^T dO and dK += dS^T Q accumulate in TMEM; written once at the end.
+//   attn_bwd_q_tc: CTA = 128 queries of one head; loops over causal key blocks; recomputes S, dP,
+//     forms dS, accumulates dQ += dS K in TMEM; written once (bf16) into dqkv.
+// Every tile is loaded once in the 128-byte-swizzled [rows][64-column chunk] layout; the same bytes
+// serve as the K-major operand of one product and the MN-major operand of the other (Q, dO, K, and
+// the P^T / dS^T tiles, whose row-major [key][query] layout is also dS as an MN-major A operand).
+namespace {
+
+constexpr int BW_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 element-wise
+
+template <int D>
+struct KVCfg {
+  static constexpr int ST = (D == 64) ? 2 : 1;  // Q / dO stages
+  static constexpr int T = 128 * D * 2;         // one [128][D] bf16 tile
+  static constexpr int PT = 128 * 128 * 2;
+  static constexpr int SMEM = 2 * T + ST * 2 * T + 2 * PT + ST * 2 * 512 + 256;
+};
+
+template <int D>
+struct QCfg {
+  static constexpr int ST = (D == 64) ? 2 : 1;  // K / V stages
+  static constexpr int T = 128 * D * 2;
+  static constexpr int PT = 128 * 128 * 2;
+  static constexpr int SMEM = 2 * T + ST * 2 * T + PT + 256;
+};
+
+// K-major descriptor of K-step k (16 elements) in a [128 rows][D] swizzled tile made of 64-wide chunks.
+__device__ __forceinline__ uint64_t kdesc(uint32_t base, int k) {
+  return umma_smem_desc_sw128(base + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
+}
+// MN-major descriptor of K-step k (16 rows) of the same tile used with its columns as the N dimension.
+__device__ __forceinline__ uint64_t mndesc(uint32_t base, int k) {
+  return umma_smem_desc_sw128(base + k * 2048, 128 * 128, 1024);
+}
+
+struct WarpWait {
+  volatile int* abort_flag;
+  int lane;
+  __device__ bool operator()(uint64_t* bb, uint32_t par, int site) const {
+    int okl = 1;
+    if (lane == 0) okl = mbar_wait_bounded(bb, par, DT_ERR_TIMEOUT_TMEM, site, abort_flag) ? 1 : 0;
+    okl = __shfl_sync(0xffffffffu, okl, 0);
+    __syncwarp();
+    return okl != 0;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(BW_THREADS, 1)
+attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
+                      const __grid_constant__ CUtensorMap tmLSE, const __grid_constant__ CUtensorMap tmDEL,
+                      __nv_bfloat16* __restrict__ dqkv, int B, int T, int nh, int nkv, float scale) {
+  using C = KVCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 599);
+    return;
+  }
+  uint8_t* sK = smem_raw;
+  uint8_t* sV = sK + C::T;
+  uint8_t* sQ = sV + C::T;                  // [ST][T]
+  uint8_t* sDO = sQ + C::ST * C::T;         // [ST][T]
+  uint8_t* sP = sDO + C::ST * C::T;         // P^T  [128 keys][128 q]
+  uint8_t* sDS = sP + C::PT;                // dS^T [128 keys][128 q]
+  float* sLSE = reinterpret_cast<float*>(sDS + C::PT);  // [ST][128]
+  float* sDEL = sLSE + C::ST * 128;                     // [ST][128]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sDEL + C::ST * 128);
+  uint64_t* kv_full = bar;
+  uint64_t* qd_full = bar + 1;   // [2]
+  uint64_t* qd_empty = bar + 3;  // [2]
+  uint64_t* sdp_full = bar + 5;
+  uint64_t* s_free = bar + 6;
+  uint64_t* p_full = bar + 7;
+  uint64_t* mm_done = bar + 8;
+  uint64_t* drain = bar + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (T + 127) / 128;
+  const int kb = blockIdx.x % nkb;  // key block 0 has the most query blocks: scheduled first
+  const int bg = blockIdx.x / nkb;
+  const int g = bg % nkv, b = bg / nkv;
+  const int G = nh / nkv;
+  const int nqb = nkb;
+  const int iters = G * (nqb - kb);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
+    mbar_init(sdp_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(mm_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQKV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(kv_full, 2 * C::T);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_3d(sK + c * (128 * 128), &tmQKV, kv_full, (nh + g) * D + 64 * c, kb * 128, b);
+        tma_load_3d(sV + c * (128 * 128), &tmQKV, kv_full, (nh + nkv + g) * D + 64 * c, kb * 128, b);
+      }
+      for (int it = 0; it < iters; ++it) {
+        const int hh = it / (nqb - kb), i = kb + it % (nqb - kb), h = g * G + hh;
+        const int st = it % C::ST;
+        if (it >= C::ST &&
+            !mbar_wait_bounded(&qd_empty[st], ((it / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 500, abort_flag))
+          break;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * C::T + 2 * 512);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(sQ + st * C::T + c * (128 * 128), &tmQKV, &qd_full[st], h * D + 64 * c, i * 128, b);
+          tma_load_3d(sDO + st * C::T + c * (128 * 128), &tmDO, &qd_full[st], h * D + 64 * c, i * 128, b);
+        }
+        tma_load_2d(sLSE + st * 128, &tmLSE, &qd_full[st], i * 128, b * nh + h);
+        tma_load_2d(sDEL + st * 128, &tmDEL, &qd_full[st], i * 128, b * nh + h);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idKD = umma_idesc_bf16(128, D, 0, 1);
+      bool ok = mbar_wait_bounded(kv_full, 0, DT_ERR_TIMEOUT_FULL, 510, abort_flag);
+      bool issued = false;
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
+      for (int it = 0; it < iters && ok; ++it) {
+        const int st = it % C::ST;
+        if (!mbar_wait_bounded(&qd_full[st], (it / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 511, abort_flag)) { ok = false; break; }
+        if (it > 0 && !mbar_wait_bounded(s_free, (it - 1) & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ + st * C::T), aDO = smem_u32(sDO + st * C::T);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, kdesc(aK, k), kdesc(aQ, k), idSS, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aV, k), kdesc(aDO, k), idSS, k > 0 ? 1u : 0u);
+        issued = true;
+        umma_commit(sdp_full);
+        if (!mbar_wait_bounded(p_full, it & 1, DT_ERR_TIMEOUT_FULL, 513, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tDV, kdesc(aP, k), mndesc(aDO, k), idKD, (it > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tDK, kdesc(aDS, k), mndesc(aQ, k), idKD, (it > 0 || k > 0) ? 1u : 0u);
+        umma_commit(mm_done);
+        umma_commit(&qd_empty[st]);
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        uint64_t t0 = dt_globaltimer();
+        while (!mbar_try_wait(drain, 0)) if (dt_globaltimer() - t0 > 20000000ull) break;
+      }
+    }
+  } else {
+    // ───────────── element-wise warps: thread = key row r, query columns [hf*64, hf*64+64) ─────────────
+    const int ew = warp - 2, quad = warp & 3, hf = ew >> 2;
+    const int r = quad * 32 + lane;
+    const int key = kb * 128 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float sl2 = scale * LOG2E_F;
+    WarpWait wwait{abort_flag, lane};
+    bool ok = true;
+    for (int it = 0; it < iters; ++it) {
+      const int i = kb + it % (nqb - kb);
+      const int st = it % C::ST;
+      if (!wwait(sdp_full, it & 1, 520)) { ok = false; break; }
+      tc_fence_after();
+      const float* lse_s = sLSE + st * 128 + hf * 64;
+      const float* del_s = sDEL + st * 128 + hf * 64;
+      uint32_t pk[32], dk[32];  // packed bf16 pairs of P^T and dS^T for this thread's 64 columns
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tS + lane_off + hf * 64 + cc * 32, sv);
+        tmem_ld_32x32b_x32(tDP + lane_off + hf * 64 + cc * 32, dv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int cl = cc * 32 + e + u;
+            const int q = i * 128 + hf * 64 + cl;
+            const bool masked = (q < key) || (q >= T) || (key >= T);
+            const float p = masked ? 0.f : ex2_approx(__uint_as_float(sv[e + u]) * sl2 - lse_s[cl] * LOG2E_F);
+            pp[u] = p;
+            dd[u] = p * (__uint_as_float(dv[e + u]) - del_s[cl]);
+          }
+          pk[cc * 16 + e / 2] = pack_bf16(pp[0], pp[1]);
+          dk[cc * 16 + e / 2] = pack_bf16(dd[0], dd[1]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      // the previous block's dV / dK products must be done reading the P^T / dS^T tiles
+      if (it > 0 && !wwait(mm_done, (it - 1) & 1, 521)) { ok = false; break; }
+      uint8_t* prow = sP + hf * (128 * 128) + r * 128;
+      uint8_t* drow = sDS + hf * (128 * 128) + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int pos = (ch ^ (r & 7)) * 16;
+        *reinterpret_cast<uint4*>(prow + pos) = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        *reinterpret_cast<uint4*>(drow + pos) = make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // epilogue: dK (scaled) and dV rows of this key block
+    if (ok && wwait(mm_done, (iters - 1) & 1, 522)) {
+      tc_fence_after();
+      const long long W = (long long)(nh + 2 * nkv) * D;
+      __nv_bfloat16* krow = dqkv + ((long long)b * T + key) * W + (nh + g) * D + hf * (D / 2);
+      __nv_bfloat16* vrow = dqkv + ((long long)b * T + key) * W + (nh + nkv + g) * D + hf * (D / 2);
+#pragma unroll
+      for (int c0 = 0; c0 < D / 2; c0 += 32) {
+        uint32_t kv[32], vv[32];
+        tmem_ld_32x32b_x32(tDK + lane_off + hf * (D / 2) + c0, kv);
+        tmem_ld_32x32b_x32(tDV + lane_off + hf * (D / 2) + c0, vv);
+        tmem_ld_wait();
+        if (key < T) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 wk, wv;
+            wk.x = pack_bf16(__uint_as_float(kv[8 * v + 0]) * scale, __uint_as_float(kv[8 * v + 1]) * scale);
+            wk.y = pack_bf16(__uint_as_float(kv[8 * v + 2]) * scale, __uint_as_float(kv[8 * v + 3]) * scale);
+            wk.z = pack_bf16(__uint_as_float(kv[8 * v + 4]) * scale, __uint_as_float(kv[8 * v + 5]) * scale);
+            wk.w = pack_bf16(__uint_as_float(kv[8 * v + 6]) * scale, __uint_as_float(kv[8 * v + 7]) * scale);
+            wv.x = pack_bf16(__uint_as_float(vv[8 * v + 0]), __uint_as_float(vv[8 * v + 1]));
+            wv.y = pack_bf16(__uint_as_float(vv[8 * v + 2]), __uint_as_float(vv[8 * v + 3]));
+            wv.z = pack_bf16(__uint_as_float(vv[8 * v + 4]), __uint_as_float(vv[8 * v + 5]));
+            wv.w = pack_bf16(__uint_as_float(vv[8 * v + 6]), __uint_as_float(vv[8 * v + 7]));
+            *reinterpret_cast<uint4*>(krow + c0 + 8 * v) = wk;
+            *reinterpret_cast<uint4*>(vrow + c0 + 8 * v) = wv;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+template <int D>
+__global__ void __launch_bounds__(BW_THREADS, 1)
+attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
+                     const float* __restrict__ lse, const float* __restrict__ delta, __nv_bfloat16* __restrict__ dqkv,
+                     int B, int T, int nh, int nkv, float scale) {
+  using C = QCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 699);
+    return;
+  }
+  uint8_t* sQ = smem_raw;
+  uint8_t* sDO = sQ + C::T;
+  uint8_t* sK = sDO + C::T;         // [ST][T]
+  uint8_t* sV = sK + C::ST * C::T;  // [ST][T]
+  uint8_t* sDS = sV + C::ST * C::T; // dS [128 q][128 keys]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sDS + C::PT);
+  uint64_t* q_full = bar;
+  uint64_t* kv_full = bar + 1;   // [2]
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* sdp_full = bar + 5;
+  uint64_t* s_free = bar + 6;
+  uint64_t* p_full = bar + 7;
+  uint64_t* mm_done = bar + 8;
+  uint64_t* drain = bar + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = (T + 127) / 128;
+  const int qb = nqb - 1 - (blockIdx.x % nqb);  // long (late) query blocks first
+  const int bh = blockIdx.x / nqb;
+  const int h = bh % nh, b = bh / nh;
+  const int g = h / (nh / nkv);
+  const int nkb = qb + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    mbar_init(sdp_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(mm_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDQ = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQKV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(q_full, 2 * C::T);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_3d(sQ + c * (128 * 128), &tmQKV, q_full, h * D + 64 * c, qb * 128, b);
+        tma_load_3d(sDO + c * (128 * 128), &tmDO, q_full, h * D + 64 * c, qb * 128, b);
+      }
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % C::ST;
+        if (j >= C::ST &&
+            !mbar_wait_bounded(&kv_empty[st], ((j / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 600, abort_flag))
+          break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::T);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(sK + st * C::T + c * (128 * 128), &tmQKV, &kv_full[st], (nh + g) * D + 64 * c, j * 128, b);
+          tma_load_3d(sV + st * C::T + c * (128 * 128), &tmQKV, &kv_full[st], (nh + nkv + g) * D + 64 * c, j * 128, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idQD = umma_idesc_bf16(128, D, 0, 1);
+      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 610, abort_flag);
+      bool issued = false;
+      const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO), aDS = smem_u32(sDS);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j % C::ST;
+        if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 611, abort_flag)) { ok = false; break; }
+        if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sK + st * C::T), aV = smem_u32(sV + st * C::T);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, kdesc(aQ, k), kdesc(aK, k), idSS, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aDO, k), kdesc(aV, k), idSS, k > 0 ? 1u : 0u);
+        issued = true;
+        umma_commit(sdp_full);
+        if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 613, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tDQ, kdesc(aDS, k), mndesc(aK, k), idQD, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(mm_done);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        uint64_t t0 = dt_globaltimer();
+        while (!mbar_try_wait(drain, 0)) if (dt_globaltimer() - t0 > 20000000ull) break;
+      }
+    }
+  } else {
+    // ───────────── element-wise warps: thread = query row r, key columns [hf*64, hf*64+64) ─────────────
+    const int ew = warp - 2, quad = warp & 3, hf = ew >> 2;
+    const int r = quad * 32 + lane;
+    const int q = qb * 128 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const float sl2 = scale * LOG2E_F;
+    const int Tp = (T + 3) & ~3;
+    const long long ridx = ((long long)b * nh + h) * Tp + q;
+    const float lse2 = (q < T) ? lse[ridx] * LOG2E_F : 0.f;
+    const float dlt = (q < T) ? delta[ridx] : 0.f;
+    WarpWait wwait{abort_flag, lane};
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (!wwait(sdp_full, j & 1, 620)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t dk[32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tS + lane_off + hf * 64 + cc * 32, sv);
+        tmem_ld_32x32b_x32(tDP + lane_off + hf * 64 + cc * 32, dv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float dd[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = j * 128 + hf * 64 + cc * 32 + e + u;
+            const bool masked = (key > q) || (key >= T) || (q >= T);
+            const float p = masked ? 0.f : ex2_approx(__uint_as_float(sv[e + u]) * sl2 - lse2);
+            dd[u] = p * (__uint_as_float(dv[e + u]) - dlt);
+          }
+          dk[cc * 16 + e / 2] = pack_bf16(dd[0], dd[1]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      if (j > 0 && !wwait(mm_done, (j - 1) & 1, 621)) { ok = false; break; }
+      uint8_t* drow = sDS + hf * (128 * 128) + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(drow + (ch ^ (r & 7)) * 16) =
+            make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && wwait(mm_done, (nkb - 1) & 1, 622)) {
+      tc_fence_after();
+      const long long W = (long long)(nh + 2 * nkv) * D;
+      __nv_bfloat16* qrow = dqkv + ((long long)b * T + q) * W + h * D + hf * (D / 2);
+#pragma unroll
+      for (int c0 = 0; c0 < D / 2; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tDQ + lane_off + hf * (D / 2) + c0, o);
+        tmem_ld_wait();
+        if (q < T) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * scale, __uint_as_float(o[8 * v + 1]) * scale);
+            w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * scale, __uint_as_float(o[8 * v + 3]) * scale);
+            w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * scale, __uint_as_float(o[8 * v + 5]) * scale);
+            w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * scale, __uint_as_float(o[8 * v + 7]) * scale);
+            *reinterpret_cast<uint4*>(qrow + c0 + 8 * v) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// fp32 [rows, Tp] map with a {128, 1} box (LSE / delta slices of one query block).
+int rowvec_map(CUtensorMap* m, const float* p, long long rows, long long Tp) {
+  if (!g_enc) return -2;
+  cuuint64_t dims[2] = {(cuuint64_t)Tp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(Tp * 4)};
+  cuuint32_t box[2] = {128, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+template <int D>
+int bwd_tc_launch(const void* qkv, const void* dout, const float* lse, const float* delta, void* dqkv, int B, int T,
+                  int nh, int nkv, float scale, cudaStream_t st) {
+  long long W = (long long)(nh + 2 * nkv) * D;
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(lse) |
+       reinterpret_cast<uintptr_t>(delta)) & 15)
+    return -10;
+  const long long Tp = (T + 3) & ~3;
+  CUtensorMap mq, mdo, ml, md;
+  int rc = qkv_map(&mq, qkv, B, T, W);
+  if (!rc) rc = qkv_map(&mdo, dout, B, T, (long long)nh * D);
+  if (!rc) rc = rowvec_map(&ml, lse, (long long)B * nh, Tp);
+  if (!rc) rc = rowvec_map(&md, delta, (long long)B * nh, Tp);
+  if (rc) return rc;
+  static bool set = false;
+  if (!set) {
+    DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, KVCfg<D>::SMEM));
+    DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_q_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<D>::SMEM));
+    set = true;
+  }
+  const int nb = (T + 127) / 128;
+  auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv);
+  attn_bwd_kv_tc_kernel<D><<<B * nkv * nb, BW_THREADS, KVCfg<D>::SMEM, st>>>(mq, mdo, ml, md, dq, B, T, nh, nkv, scale);
+  DT_CUDA_RET(cudaGetLastError());
+  attn_bwd_q_tc_kernel<D><<<B * nh * nb, BW_THREADS, QCfg<D>::SMEM, st>>>(mq, mdo, lse, delta, dq, B, T, nh, nkv, scale);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+// tcgen05 backward (d = 64 / 128). `delta` must already hold rowsum(dO * O) (dt_attn_bwd_delta).
+DT_API int dt_attn_bwd_tc(const void* qkv, const void* dout, const float* lse, const float* delta, void* dqkv, int B,
+                          int T, int nh, int nkv, int D, float scale, cudaStream_t st) {
+  if (nh % nkv) return -10;
+  if (D == 64) return bwd_tc_launch<64>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st);
+  if (D == 128) return bwd_tc_launch<128>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st);
   return -11;
 }

@@ -76,11 +76,11 @@ def attn_cases(iters):
         W = (nh + 2 * nkv) * d
         qkv = torch.randn(B * T, W, device="cuda").bfloat16()
         o = torch.empty(B * T, nh * d, device="cuda", dtype=torch.bfloat16)
-        lse = torch.empty(B, nh, T, device="cuda")
+        lse = torch.empty(B, nh, A.lse_stride(T), device="cuda")
         do = torch.randn_like(o)
         dqkv = torch.empty_like(qkv)
         dqa = torch.empty(B * T, nh * d, device="cuda")
-        de = torch.empty(B, nh, T, device="cuda")
+        de = torch.empty(B, nh, A.lse_stride(T), device="cuda")
         fl = 4.0 * B * nh * T * T * d / 2  # causal
         ms_f = time_it(lambda: A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)
         ms_b = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)

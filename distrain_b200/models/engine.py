@@ -75,7 +75,8 @@ class TrainEngine:
         self.xn2 = [torch.empty(M, H, dtype=bf16, device=dev) for _ in range(Lr)]
         self.qkv = [torch.empty(M, self.W, dtype=bf16, device=dev) for _ in range(Lr)]
         self.attn = [torch.empty(M, nh * d, dtype=bf16, device=dev) for _ in range(Lr)]
-        self.lse = [torch.empty(batch, nh, self.T, dtype=f32, device=dev) for _ in range(Lr)]
+        Tp = attn_ops.lse_stride(self.T)
+        self.lse = [torch.empty(batch, nh, Tp, dtype=f32, device=dev) for _ in range(Lr)]
         self.gu = [torch.empty(M, 2 * F, dtype=bf16, device=dev) for _ in range(Lr)]
         self.hact = [torch.empty(M, F, dtype=bf16, device=dev) for _ in range(Lr)]
         self.resid_fin = torch.empty(M, H, dtype=f32, device=dev)
@@ -94,7 +95,7 @@ class TrainEngine:
         self.dattn = torch.empty(M, nh * d, dtype=bf16, device=dev)
         self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
         self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
-        self.delta = torch.empty(batch, nh, self.T, dtype=f32, device=dev)
+        self.delta = torch.empty(batch, nh, Tp, dtype=f32, device=dev)
         # ── named views ──
         self._bind_views()
         if flat_init is None:

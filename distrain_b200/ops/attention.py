@@ -18,6 +18,11 @@ from ._lib import lib, check, stream_ptr, ptr, register, c_int, c_void, c_float
 _registered = False
 
 
+def lse_stride(T: int) -> int:
+    """Row stride of the [B, nh, Tp] LSE / delta buffers: T rounded up to a multiple of 4 (16-byte rows)."""
+    return (T + 3) // 4 * 4
+
+
 def _reg():
     global _registered
     if _registered:
@@ -26,7 +31,17 @@ def _reg():
     register("dt_attn_bwd", [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
                              c_int, c_float, c_void])
     register("dt_attn_fwd_tc", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float, c_void])
+    register("dt_attn_bwd_delta", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_void])
+    register("dt_attn_bwd_tc", [c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float,
+                                c_void])
     _registered = True
+
+
+def bwd_kernel_for(d: int, impl: str) -> str:
+    """Backward for ``impl="dt"``: tcgen05 kernels for head dims 64 / 128, mma.sync otherwise."""
+    if impl == "dt":
+        return "tc" if d in (64, 128) else "mma"
+    return impl
 
 
 def fwd_kernel_for(d: int, impl: str) -> str:
@@ -43,7 +58,7 @@ def attention_fwd(qkv, out, lse, *, B, T, nh, nkv, d, impl="dt", stream=None):
     if impl == "torch":
         o, l = _torch_fwd(qkv, B, T, nh, nkv, d)
         out.copy_(o)
-        lse.copy_(l)
+        lse[..., :T].copy_(l)
         return
     _reg()
     kind = fwd_kernel_for(d, impl)
@@ -68,6 +83,12 @@ def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, *, B, T, nh, nkv, d,
         v[:, (nh + nkv) * d:].copy_(dv)
         return
     _reg()
+    if bwd_kernel_for(d, impl) == "tc" and d in (64, 128):
+        sp = stream_ptr(stream)
+        check(lib().dt_attn_bwd_delta(ptr(out), ptr(dout), ptr(delta), B, T, nh, d, sp), "dt_attn_bwd_delta")
+        check(lib().dt_attn_bwd_tc(ptr(qkv), ptr(dout), ptr(lse), ptr(delta), ptr(dqkv), B, T, nh, nkv, d,
+                                   float(scale), sp), "dt_attn_bwd_tc")
+        return
     check(lib().dt_attn_bwd(ptr(qkv), ptr(out), ptr(dout), ptr(lse), ptr(dqkv), ptr(dq_acc), ptr(delta), B, T, nh,
                             nkv, d, float(scale), stream_ptr(stream)), "dt_attn_bwd")
 
