@@ -122,6 +122,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
+      // another CTA already failed: give up now instead of serving out a full timeout per CTA
+      if (*reinterpret_cast<volatile int*>(&dt_error_word) != 0) {
+        if (abort_flag) *abort_flag = 1;
+        return false;
+      }
       if (dt_globaltimer() - t0 > DT_WAIT_NS) {
         dt_set_error(err, site);
         if (abort_flag) *abort_flag = 1;
