@@ -349,7 +349,7 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
 // Two kernels, no atomics and no fp32 dQ scratch:
 //   attn_bwd_kv_tc: CTA = 128 keys of one kv head; loops over the kv group's query heads and the
 //     causal query blocks i >= key block. Per block: S^T = K Q^T and dP^T = V dO^T into TMEM;
-//     8 element-wise warps (thread = key row, half of the 128 query columns; the backward needs no row
+//     16 element-wise warps (thread = key row, 32 of the 128 query columns; the backward needs no row
 //     reduction) form P^T = exp2(S^T*c - LSE) and dS^T = P^T (dP^T - delta) in bf16 shared tiles;
 //     dV += P^T dO and dK += dS^T Q accumulate in TMEM; written once at the end.
 //   attn_bwd_q_tc: CTA = 128 queries of one head; loops over causal key blocks; recomputes S, dP,
@@ -359,11 +359,16 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
 // the P^T / dS^T tiles, whose row-major [key][query] layout is also dS as an MN-major A operand).
 namespace {
 
-constexpr int BW_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 element-wise
+constexpr int BW_EW_WARPS = 16;
+constexpr int BW_THREADS = 64 + 32 * BW_EW_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2..17 element-wise
 
+// With two operand stages the MMA warp issues S/dP of the next block as soon as the element-wise
+// warps have read this block's S/dP out of TMEM, before this block's dV/dK (or dQ) products: the
+// tensor cores then work while P / dS of the next block are formed.
 template <int D>
 struct KVCfg {
   static constexpr int ST = (D == 64) ? 2 : 1;  // Q / dO stages
+  static constexpr bool EARLY = ST >= 2;
   static constexpr int T = 128 * D * 2;         // one [128][D] bf16 tile
   static constexpr int PT = 128 * 128 * 2;
   static constexpr int SMEM = 2 * T + ST * 2 * T + 2 * PT + ST * 2 * 512 + 256;
@@ -372,6 +377,7 @@ struct KVCfg {
 template <int D>
 struct QCfg {
   static constexpr int ST = (D == 64) ? 2 : 1;  // K / V stages
+  static constexpr bool EARLY = ST >= 2;
   static constexpr int T = 128 * D * 2;
   static constexpr int PT = 128 * 128 * 2;
   static constexpr int SMEM = 2 * T + ST * 2 * T + PT + 256;
@@ -397,6 +403,97 @@ struct WarpWait {
     return okl != 0;
   }
 };
+
+// One arrival per warp on a barrier initialised with the element-wise warp count.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+// Store 32 packed bf16 pairs' worth (32 columns) of row r into a [128 rows][2 x 64-column] 128-byte-
+// swizzled tile at column group cg (0..3).
+__device__ __forceinline__ void store_row32(uint8_t* tile, int r, int cg, const uint32_t (&v)[16]) {
+  uint8_t* row = tile + (cg >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(row + ((((cg & 1) << 2) + c) ^ (r & 7)) * 16) =
+        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+// kv kernel, 32 query columns of one key row: P^T = exp2(S^T*c - LSE*log2e), dS^T = P^T (dP^T - delta),
+// with LSE / delta per column (from shared memory). Columns e with !(lo <= e < hi) are zero (MASK).
+template <bool MASK>
+__device__ __forceinline__ void kv_block_math(const uint32_t (&sv)[32], const uint32_t (&dv)[32], const float* lse,
+                                              const float* del, float sl2, int lo, int hi, uint32_t (&pk)[16],
+                                              uint32_t (&dk)[16]) {
+  const uint64_t c2 = f2_pack(sl2, sl2), m2 = f2_pack(-LOG2E_F, -LOG2E_F);
+  const float4* l4 = reinterpret_cast<const float4*>(lse);
+  const float4* d4 = reinterpret_cast<const float4*>(del);
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    const float4 l = l4[v], dl = d4[v];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int e = 4 * v + 2 * h2;
+      const uint64_t nl = f2_mul(h2 ? f2_pack(l.z, l.w) : f2_pack(l.x, l.y), m2);
+      const float2 x = f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nl));
+      float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+      const uint64_t dd = f2_sub(f2_pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+                                 h2 ? f2_pack(dl.z, dl.w) : f2_pack(dl.x, dl.y));
+      float2 ds = f2_unpack(f2_mul(f2_pack(p0, p1), dd));
+      if (MASK) {
+        const bool v0 = (e >= lo) && (e < hi), v1 = (e + 1 >= lo) && (e + 1 < hi);
+        p0 = v0 ? p0 : 0.f;
+        ds.x = v0 ? ds.x : 0.f;
+        p1 = v1 ? p1 : 0.f;
+        ds.y = v1 ? ds.y : 0.f;
+      }
+      pk[e / 2] = pack_bf16(p0, p1);
+      dk[e / 2] = pack_bf16(ds.x, ds.y);
+    }
+  }
+}
+
+// q kernel, 32 key columns of one query row: dS = exp2(S*c - LSE*log2e) (dP - delta); LSE / delta are
+// this row's. Columns e >= hi are zero (MASK).
+template <bool MASK>
+__device__ __forceinline__ void q_block_math(const uint32_t (&sv)[32], const uint32_t (&dv)[32], float sl2,
+                                             float nlse2, float dlt, int hi, uint32_t (&dk)[16]) {
+  const uint64_t c2 = f2_pack(sl2, sl2), nl = f2_pack(nlse2, nlse2), d2 = f2_pack(dlt, dlt);
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    const float2 x = f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nl));
+    const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+    const uint64_t dd = f2_sub(f2_pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), d2);
+    float2 ds = f2_unpack(f2_mul(f2_pack(p0, p1), dd));
+    if (MASK) {
+      ds.x = (e < hi) ? ds.x : 0.f;
+      ds.y = (e + 1 < hi) ? ds.y : 0.f;
+    }
+    dk[e / 2] = pack_bf16(ds.x, ds.y);
+  }
+}
+
+// bf16 store of `n` (16 or 32) fp32 TMEM columns (times mul) of this thread's lane to dst.
+__device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, int n, float mul, bool valid,
+                                                 __nv_bfloat16* dst) {
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    uint32_t o[16];
+    tmem_ld_32x32b_x16(taddr + c0, o);
+    tmem_ld_wait();
+    if (valid) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        uint4 w;
+        w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * mul, __uint_as_float(o[8 * v + 1]) * mul);
+        w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * mul, __uint_as_float(o[8 * v + 3]) * mul);
+        w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * mul, __uint_as_float(o[8 * v + 5]) * mul);
+        w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * mul, __uint_as_float(o[8 * v + 7]) * mul);
+        *reinterpret_cast<uint4*>(dst + c0 + 8 * v) = w;
+      }
+    }
+  }
+}
 
 template <int D>
 __global__ void __launch_bounds__(BW_THREADS, 1)
@@ -442,8 +539,8 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
     mbar_init(sdp_full, 1);
-    mbar_init(s_free, 256);
-    mbar_init(p_full, 256);
+    mbar_init(s_free, BW_EW_WARPS);
+    mbar_init(p_full, BW_EW_WARPS);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -490,13 +587,12 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
     if (lane == 0) {
       constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idKD = umma_idesc_bf16(128, D, 0, 1);
-      bool ok = mbar_wait_bounded(kv_full, 0, DT_ERR_TIMEOUT_FULL, 510, abort_flag);
-      bool issued = false;
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
-      for (int it = 0; it < iters && ok; ++it) {
+      bool issued = false;
+      // S^T = K Q^T and dP^T = V dO^T of block `it`
+      auto issue_sdp = [&](int it) -> bool {
         const int st = it % C::ST;
-        if (!mbar_wait_bounded(&qd_full[st], (it / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 511, abort_flag)) { ok = false; break; }
-        if (it > 0 && !mbar_wait_bounded(s_free, (it - 1) & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&qd_full[st], (it / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 511, abort_flag)) return false;
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + st * C::T), aDO = smem_u32(sDO + st * C::T);
 #pragma unroll
@@ -505,8 +601,22 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
         for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aV, k), kdesc(aDO, k), idSS, k > 0 ? 1u : 0u);
         issued = true;
         umma_commit(sdp_full);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(kv_full, 0, DT_ERR_TIMEOUT_FULL, 510, abort_flag);
+      if (ok && C::EARLY && iters > 0) ok = issue_sdp(0);
+      for (int it = 0; it < iters && ok; ++it) {
+        const int st = it % C::ST;
+        if (!C::EARLY) {
+          if (it > 0 && !mbar_wait_bounded(s_free, (it - 1) & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
+          if (!issue_sdp(it)) { ok = false; break; }
+        } else if (it + 1 < iters) {
+          if (!mbar_wait_bounded(s_free, it & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
+          if (!issue_sdp(it + 1)) { ok = false; break; }
+        }
         if (!mbar_wait_bounded(p_full, it & 1, DT_ERR_TIMEOUT_FULL, 513, abort_flag)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ + st * C::T), aDO = smem_u32(sDO + st * C::T);
 #pragma unroll
         for (int k = 0; k < 8; ++k) umma_bf16(tDV, kdesc(aP, k), mndesc(aDO, k), idKD, (it > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
@@ -521,12 +631,13 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
       }
     }
   } else {
-    // ───────────── element-wise warps: thread = key row r, query columns [hf*64, hf*64+64) ─────────────
-    const int ew = warp - 2, quad = warp & 3, hf = ew >> 2;
+    // ───── element-wise warps: thread = key row r, query columns [cg*32, cg*32+32) ─────
+    const int ew = warp - 2, quad = warp & 3, cg = ew >> 2;
     const int r = quad * 32 + lane;
     const int key = kb * 128 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = scale * LOG2E_F;
+    const bool edge_k = (kb + 1) * 128 > T;
     WarpWait wwait{abort_flag, lane};
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
@@ -534,76 +645,39 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
       const int st = it % C::ST;
       if (!wwait(sdp_full, it & 1, 520)) { ok = false; break; }
       tc_fence_after();
-      const float* lse_s = sLSE + st * 128 + hf * 64;
-      const float* del_s = sDEL + st * 128 + hf * 64;
-      uint32_t pk[32], dk[32];  // packed bf16 pairs of P^T and dS^T for this thread's 64 columns
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      uint32_t pk[16], dk[16];
+      {
         uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tS + lane_off + hf * 64 + cc * 32, sv);
-        tmem_ld_32x32b_x32(tDP + lane_off + hf * 64 + cc * 32, dv);
+        tmem_ld_32x32b_x32(tS + lane_off + cg * 32, sv);
+        tmem_ld_32x32b_x32(tDP + lane_off + cg * 32, dv);
         tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pp[2], dd[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int cl = cc * 32 + e + u;
-            const int q = i * 128 + hf * 64 + cl;
-            const bool masked = (q < key) || (q >= T) || (key >= T);
-            const float p = masked ? 0.f : ex2_approx(__uint_as_float(sv[e + u]) * sl2 - lse_s[cl] * LOG2E_F);
-            pp[u] = p;
-            dd[u] = p * (__uint_as_float(dv[e + u]) - del_s[cl]);
-          }
-          pk[cc * 16 + e / 2] = pack_bf16(pp[0], pp[1]);
-          dk[cc * 16 + e / 2] = pack_bf16(dd[0], dd[1]);
+        const float* lse_s = sLSE + st * 128 + cg * 32;
+        const float* del_s = sDEL + st * 128 + cg * 32;
+        if (i == kb || edge_k || (i + 1) * 128 > T) {
+          const int qbase = i * 128 + cg * 32;
+          const int lo = key - qbase, hi = key < T ? T - qbase : 0;  // valid columns: lo <= e < hi
+          kv_block_math<true>(sv, dv, lse_s, del_s, sl2, lo, hi, pk, dk);
+        } else {
+          kv_block_math<false>(sv, dv, lse_s, del_s, sl2, 0, 32, pk, dk);
         }
       }
       tc_fence_before();
-      mbar_arrive(s_free);
+      warp_arrive(s_free, lane);
       // the previous block's dV / dK products must be done reading the P^T / dS^T tiles
       if (it > 0 && !wwait(mm_done, (it - 1) & 1, 521)) { ok = false; break; }
-      uint8_t* prow = sP + hf * (128 * 128) + r * 128;
-      uint8_t* drow = sDS + hf * (128 * 128) + r * 128;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const int pos = (ch ^ (r & 7)) * 16;
-        *reinterpret_cast<uint4*>(prow + pos) = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        *reinterpret_cast<uint4*>(drow + pos) = make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
-      }
+      store_row32(sP, r, cg, pk);
+      store_row32(sDS, r, cg, dk);
       fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
+      warp_arrive(p_full, lane);
     }
-    // epilogue: dK (scaled) and dV rows of this key block
+    // epilogue: dK (scaled) and dV rows of this key block, D/4 columns per thread
     if (ok && wwait(mm_done, (iters - 1) & 1, 522)) {
       tc_fence_after();
       const long long W = (long long)(nh + 2 * nkv) * D;
-      __nv_bfloat16* krow = dqkv + ((long long)b * T + key) * W + (nh + g) * D + hf * (D / 2);
-      __nv_bfloat16* vrow = dqkv + ((long long)b * T + key) * W + (nh + nkv + g) * D + hf * (D / 2);
-#pragma unroll
-      for (int c0 = 0; c0 < D / 2; c0 += 32) {
-        uint32_t kv[32], vv[32];
-        tmem_ld_32x32b_x32(tDK + lane_off + hf * (D / 2) + c0, kv);
-        tmem_ld_32x32b_x32(tDV + lane_off + hf * (D / 2) + c0, vv);
-        tmem_ld_wait();
-        if (key < T) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 wk, wv;
-            wk.x = pack_bf16(__uint_as_float(kv[8 * v + 0]) * scale, __uint_as_float(kv[8 * v + 1]) * scale);
-            wk.y = pack_bf16(__uint_as_float(kv[8 * v + 2]) * scale, __uint_as_float(kv[8 * v + 3]) * scale);
-            wk.z = pack_bf16(__uint_as_float(kv[8 * v + 4]) * scale, __uint_as_float(kv[8 * v + 5]) * scale);
-            wk.w = pack_bf16(__uint_as_float(kv[8 * v + 6]) * scale, __uint_as_float(kv[8 * v + 7]) * scale);
-            wv.x = pack_bf16(__uint_as_float(vv[8 * v + 0]), __uint_as_float(vv[8 * v + 1]));
-            wv.y = pack_bf16(__uint_as_float(vv[8 * v + 2]), __uint_as_float(vv[8 * v + 3]));
-            wv.z = pack_bf16(__uint_as_float(vv[8 * v + 4]), __uint_as_float(vv[8 * v + 5]));
-            wv.w = pack_bf16(__uint_as_float(vv[8 * v + 6]), __uint_as_float(vv[8 * v + 7]));
-            *reinterpret_cast<uint4*>(krow + c0 + 8 * v) = wk;
-            *reinterpret_cast<uint4*>(vrow + c0 + 8 * v) = wv;
-          }
-        }
-      }
+      __nv_bfloat16* krow = dqkv + ((long long)b * T + key) * W + (nh + g) * D + cg * (D / 4);
+      __nv_bfloat16* vrow = dqkv + ((long long)b * T + key) * W + (nh + nkv + g) * D + cg * (D / 4);
+      tmem_row_to_bf16(tDK + lane_off + cg * (D / 4), D / 4, scale, key < T, krow);
+      tmem_row_to_bf16(tDV + lane_off + cg * (D / 4), D / 4, 1.f, key < T, vrow);
     }
   }
   tc_fence_before();
@@ -652,8 +726,8 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
     mbar_init(sdp_full, 1);
-    mbar_init(s_free, 256);
-    mbar_init(p_full, 256);
+    mbar_init(s_free, BW_EW_WARPS);
+    mbar_init(p_full, BW_EW_WARPS);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -697,13 +771,12 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
     if (lane == 0) {
       constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idQD = umma_idesc_bf16(128, D, 0, 1);
-      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 610, abort_flag);
-      bool issued = false;
       const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO), aDS = smem_u32(sDS);
-      for (int j = 0; j < nkb && ok; ++j) {
+      bool issued = false;
+      // S = Q K^T and dP = dO V^T of key block j
+      auto issue_sdp = [&](int j) -> bool {
         const int st = j % C::ST;
-        if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 611, abort_flag)) { ok = false; break; }
-        if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 611, abort_flag)) return false;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + st * C::T), aV = smem_u32(sV + st * C::T);
 #pragma unroll
@@ -712,8 +785,22 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
         for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aDO, k), kdesc(aV, k), idSS, k > 0 ? 1u : 0u);
         issued = true;
         umma_commit(sdp_full);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 610, abort_flag);
+      if (ok && C::EARLY) ok = issue_sdp(0);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j % C::ST;
+        if (!C::EARLY) {
+          if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
+          if (!issue_sdp(j)) { ok = false; break; }
+        } else if (j + 1 < nkb) {
+          if (!mbar_wait_bounded(s_free, j & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
+          if (!issue_sdp(j + 1)) { ok = false; break; }
+        }
         if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 613, abort_flag)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t aK = smem_u32(sK + st * C::T);
 #pragma unroll
         for (int k = 0; k < 8; ++k) umma_bf16(tDQ, kdesc(aDS, k), mndesc(aK, k), idQD, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(mm_done);
@@ -726,74 +813,48 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
       }
     }
   } else {
-    // ───────────── element-wise warps: thread = query row r, key columns [hf*64, hf*64+64) ─────────────
-    const int ew = warp - 2, quad = warp & 3, hf = ew >> 2;
+    // ───── element-wise warps: thread = query row r, key columns [cg*32, cg*32+32) ─────
+    const int ew = warp - 2, quad = warp & 3, cg = ew >> 2;
     const int r = quad * 32 + lane;
     const int q = qb * 128 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = scale * LOG2E_F;
     const int Tp = (T + 3) & ~3;
     const long long ridx = ((long long)b * nh + h) * Tp + q;
-    const float lse2 = (q < T) ? lse[ridx] * LOG2E_F : 0.f;
+    const float nlse2 = (q < T) ? -lse[ridx] * LOG2E_F : 0.f;
     const float dlt = (q < T) ? delta[ridx] : 0.f;
+    const bool edge_q = (qb + 1) * 128 > T;
     WarpWait wwait{abort_flag, lane};
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
       if (!wwait(sdp_full, j & 1, 620)) { ok = false; break; }
       tc_fence_after();
-      uint32_t dk[32];
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      uint32_t dk[16];
+      {
         uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tS + lane_off + hf * 64 + cc * 32, sv);
-        tmem_ld_32x32b_x32(tDP + lane_off + hf * 64 + cc * 32, dv);
+        tmem_ld_32x32b_x32(tS + lane_off + cg * 32, sv);
+        tmem_ld_32x32b_x32(tDP + lane_off + cg * 32, dv);
         tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float dd[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = j * 128 + hf * 64 + cc * 32 + e + u;
-            const bool masked = (key > q) || (key >= T) || (q >= T);
-            const float p = masked ? 0.f : ex2_approx(__uint_as_float(sv[e + u]) * sl2 - lse2);
-            dd[u] = p * (__uint_as_float(dv[e + u]) - dlt);
-          }
-          dk[cc * 16 + e / 2] = pack_bf16(dd[0], dd[1]);
+        if (j == qb || edge_q || (j + 1) * 128 > T) {
+          const int kbase = j * 128 + cg * 32;
+          const int hi = q < T ? min(q - kbase + 1, T - kbase) : 0;  // valid columns: e < hi
+          q_block_math<true>(sv, dv, sl2, nlse2, dlt, hi, dk);
+        } else {
+          q_block_math<false>(sv, dv, sl2, nlse2, dlt, 32, dk);
         }
       }
       tc_fence_before();
-      mbar_arrive(s_free);
+      warp_arrive(s_free, lane);
       if (j > 0 && !wwait(mm_done, (j - 1) & 1, 621)) { ok = false; break; }
-      uint8_t* drow = sDS + hf * (128 * 128) + r * 128;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(drow + (ch ^ (r & 7)) * 16) =
-            make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+      store_row32(sDS, r, cg, dk);
       fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
+      warp_arrive(p_full, lane);
     }
     if (ok && wwait(mm_done, (nkb - 1) & 1, 622)) {
       tc_fence_after();
       const long long W = (long long)(nh + 2 * nkv) * D;
-      __nv_bfloat16* qrow = dqkv + ((long long)b * T + q) * W + h * D + hf * (D / 2);
-#pragma unroll
-      for (int c0 = 0; c0 < D / 2; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(tDQ + lane_off + hf * (D / 2) + c0, o);
-        tmem_ld_wait();
-        if (q < T) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * scale, __uint_as_float(o[8 * v + 1]) * scale);
-            w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * scale, __uint_as_float(o[8 * v + 3]) * scale);
-            w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * scale, __uint_as_float(o[8 * v + 5]) * scale);
-            w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * scale, __uint_as_float(o[8 * v + 7]) * scale);
-            *reinterpret_cast<uint4*>(qrow + c0 + 8 * v) = w;
-          }
-        }
-      }
+      __nv_bfloat16* qrow = dqkv + ((long long)b * T + q) * W + h * D + cg * (D / 4);
+      tmem_row_to_bf16(tDQ + lane_off + cg * (D / 4), D / 4, scale, q < T, qrow);
     }
   }
   tc_fence_before();
