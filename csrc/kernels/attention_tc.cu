@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
 PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
 std::once_flag g_enc_once;
 
-int qkv_map(CUtensorMap* m, const void* qkv, int B, int T, long long W) {
+int qkv_map(CUtensorMap* m, const void* qkv, int B, int T, long long W, int rows = 128) {
   std::call_once(g_enc_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -307,7 +307,7 @@ int qkv_map(CUtensorMap* m, const void* qkv, int B, int T, long long W) {
   if (!g_enc) return -2;
   cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)(W * 2), (cuuint64_t)(W * 2 * T)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(qkv), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -348,48 +348,78 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
 // ═══════════════════════════════ backward (tcgen05) ═══════════════════════════════
 // Two kernels, no atomics and no fp32 dQ scratch:
 //   attn_bwd_kv_tc: CTA = 128 keys of one kv head; loops over the kv group's query heads and the
-//     causal query blocks i >= key block. Per block: S^T = K Q^T and dP^T = V dO^T into TMEM;
+//     causal 128-query blocks. Per block: S^T = K Q^T and dP^T = V dO^T (128 x 128, fp32) into TMEM;
 //     16 element-wise warps (thread = key row, 32 of the 128 query columns; the backward needs no row
-//     reduction) form P^T = exp2(S^T*c - LSE) and dS^T = P^T (dP^T - delta) in bf16 shared tiles;
-//     dV += P^T dO and dK += dS^T Q accumulate in TMEM; written once at the end.
-//   attn_bwd_q_tc: CTA = 128 queries of one head; loops over causal key blocks; recomputes S, dP,
-//     forms dS, accumulates dQ += dS K in TMEM; written once (bf16) into dqkv.
-// Every tile is loaded once in the 128-byte-swizzled [rows][64-column chunk] layout; the same bytes
-// serve as the K-major operand of one product and the MN-major operand of the other (Q, dO, K, and
-// the P^T / dS^T tiles, whose row-major [key][query] layout is also dS as an MN-major A operand).
+//     reduction) form P^T = exp2(S^T*c - LSE) and dS^T = P^T (dP^T - delta) as bf16 pairs stored back
+//     into the S^T columns the thread has just read; dV += P^T dO and dK += dS^T Q take them as TMEM A
+//     operands and accumulate in TMEM; written once at the end.
+//   attn_bwd_q_tc: CTA = 128 queries of one head; loops over the causal 128-key blocks; recomputes S
+//     and dP (Q and dO held in TMEM as A operands), forms dS in TMEM, accumulates dQ += dS K.
+// Cost model (measured): a tcgen05.mma with M = 128 costs the tensor core about N/2 clocks, but one
+// issuing thread cannot issue much faster than one per ~50 clocks, so products are kept N = 128 wide
+// where the shapes allow and the issue loop does no descriptor arithmetic beyond constant adds. At
+// d = 64 S^T is double-buffered in TMEM (columns: S 2 x 128, dP 128, dV 64, dK 64) so the tensor cores
+// compute block i+1 while block i's exponentials (16 results / clock / SM) run; at d = 128 the
+// accumulators take the room of the second buffer.
+// Tiles arrive by TMA in the 128-byte-swizzled [64-column chunk][rows][128 B] layout; the same bytes
+// serve as the K-major operand of one product and the MN-major operand of the other (Q, dO, K).
+
+// Optional event trace (build with -DDT_ATTN_TRACE): SM clock of each pipeline event of one CTA,
+// slot = event * 64 + iteration, read back by a profiling harness.
+#ifdef DT_ATTN_TRACE
+__device__ unsigned long long g_attn_trace[8 * 64];
+__device__ int g_attn_trace_block;
+#define ATTN_TRACE(ev, it)                                  \
+  do {                                                      \
+    if ((int)blockIdx.x == g_attn_trace_block && (it) < 64) \
+      g_attn_trace[(ev) * 64 + (it)] = clock64();           \
+  } while (0)
+#else
+#define ATTN_TRACE(ev, it) \
+  do {                     \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int BW_EW_WARPS = 16;
 constexpr int BW_THREADS = 64 + 32 * BW_EW_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2..17 element-wise
 
-// With two operand stages the MMA warp issues S/dP of the next block as soon as the element-wise
-// warps have read this block's S/dP out of TMEM, before this block's dV/dK (or dQ) products: the
-// tensor cores then work while P / dS of the next block are formed.
 template <int D>
 struct KVCfg {
-  static constexpr int ST = (D == 64) ? 2 : 1;  // Q / dO stages
-  static constexpr bool EARLY = ST >= 2;
-  static constexpr int T = 128 * D * 2;         // one [128][D] bf16 tile
-  static constexpr int PT = 128 * 128 * 2;
-  static constexpr int SMEM = 2 * T + ST * 2 * T + 2 * PT + ST * 2 * 512 + 256;
+  static constexpr int NSB = (D == 64) ? 2 : 1;  // S^T buffers in TMEM
+  static constexpr int ST = (D == 64) ? 4 : 2;   // Q / dO stages
+  static constexpr int TT = 128 * D * 2;         // one [128][D] bf16 tile
+  static constexpr int SMEM = 2 * TT + ST * 2 * TT + ST * 2 * 512 + 256;
+  // TMEM columns
+  static constexpr int C_DP = NSB * 128, C_DV = C_DP + 128, C_DK = C_DV + D;
+  static_assert(C_DK + D <= 512, "kv TMEM budget");
 };
 
 template <int D>
 struct QCfg {
-  static constexpr int ST = (D == 64) ? 2 : 1;  // K / V stages
-  static constexpr bool EARLY = ST >= 2;
-  static constexpr int T = 128 * D * 2;
-  static constexpr int PT = 128 * 128 * 2;
-  static constexpr int SMEM = 2 * T + ST * 2 * T + PT + 256;
+  static constexpr int NSB = (D == 64) ? 2 : 1;  // S buffers in TMEM
+  static constexpr int ST = (D == 64) ? 4 : 2;   // K / V stages
+  static constexpr int TT = 128 * D * 2;
+  static constexpr int SMEM = 2 * TT + ST * 2 * TT + 256;
+  static constexpr int C_DP = NSB * 128, C_DQ = C_DP + 128, C_Q = C_DQ + D, C_DO = C_Q + D / 2;
+  static_assert(C_DO + D / 2 <= 512, "q TMEM budget");
 };
 
-// K-major descriptor of K-step k (16 elements) in a [128 rows][D] swizzled tile made of 64-wide chunks.
-__device__ __forceinline__ uint64_t kdesc(uint32_t base, int k) {
-  return umma_smem_desc_sw128(base + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
-}
-// MN-major descriptor of K-step k (16 rows) of the same tile used with its columns as the N dimension.
-__device__ __forceinline__ uint64_t mndesc(uint32_t base, int k) {
-  return umma_smem_desc_sw128(base + k * 2048, 128 * 128, 1024);
+static_assert(KVCfg<64>::SMEM <= 232448 && KVCfg<128>::SMEM <= 232448, "kv backward shared memory");
+static_assert(QCfg<64>::SMEM <= 232448 && QCfg<128>::SMEM <= 232448, "q backward shared memory");
+
+// Descriptor offsets (in 16-byte units) of K-step k within a [128 rows][D] swizzled tile of 64-wide
+// chunks: K-major (16 elements along the row) and MN-major (16 rows) use.
+__host__ __device__ constexpr uint64_t koff(int k) { return (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4); }
+__host__ __device__ constexpr uint64_t mnoff(int k) { return (uint64_t)((k * 2048) >> 4); }
+__device__ __forceinline__ uint64_t kdesc0(uint32_t base) { return umma_smem_desc_sw128(base, 16, 1024); }
+__device__ __forceinline__ uint64_t mndesc0(uint32_t base) { return umma_smem_desc_sw128(base, 128 * 128, 1024); }
+// TMEM A operand of K-step k of a bf16 tile written by the element-wise threads: thread group cg holds
+// elements [32cg, 32cg+32) as 16 packed columns at buf + 32cg + half*16; K-step k is group k>>1's
+// columns (k&1)*8 .. +8.
+__device__ __forceinline__ uint32_t pcol(uint32_t buf, int half, int k) {
+  return buf + (k >> 1) * 32 + half * 16 + (k & 1) * 8;
 }
 
 struct WarpWait {
@@ -410,18 +440,29 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
   if (lane == 0) mbar_arrive(bar);
 }
 
-// Store 32 packed bf16 pairs' worth (32 columns) of row r into a [128 rows][2 x 64-column] 128-byte-
-// swizzled tile at column group cg (0..3).
-__device__ __forceinline__ void store_row32(uint8_t* tile, int r, int cg, const uint32_t (&v)[16]) {
-  uint8_t* row = tile + (cg >> 1) * (128 * 128) + r * 128;
+// Copy row r, elements [cg*D/4, (cg+1)*D/4) of a swizzled [128][D] bf16 shared tile into TMEM as packed
+// pairs (column = element / 2) at tdst + lane offset: the tile becomes a TMEM A operand.
+template <int D>
+__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, int cg, uint32_t tdst) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
-    *reinterpret_cast<uint4*>(row + ((((cg & 1) << 2) + c) ^ (r & 7)) * 16) =
-        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  for (int u = 0; u < D / 32; u += 2) {
+    uint32_t v[8];
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const int e0 = cg * (D / 4) + (u + w) * 8;
+      const uint4 x = *reinterpret_cast<const uint4*>(tile + (e0 >> 6) * (128 * 128) + r * 128 +
+                                                      ((((e0 & 63) >> 3) ^ (r & 7)) << 4));
+      v[4 * w] = x.x;
+      v[4 * w + 1] = x.y;
+      v[4 * w + 2] = x.z;
+      v[4 * w + 3] = x.w;
+    }
+    tmem_st_32x32b_x8(tdst + (cg * (D / 4) + u * 8) / 2, v);
+  }
 }
 
 // kv kernel, 32 query columns of one key row: P^T = exp2(S^T*c - LSE*log2e), dS^T = P^T (dP^T - delta),
-// with LSE / delta per column (from shared memory). Columns e with !(lo <= e < hi) are zero (MASK).
+// LSE / delta per column (shared memory). Columns e outside [lo, hi) are zero (MASK).
 template <bool MASK>
 __device__ __forceinline__ void kv_block_math(const uint32_t (&sv)[32], const uint32_t (&dv)[32], const float* lse,
                                               const float* del, float sl2, int lo, int hi, uint32_t (&pk)[16],
@@ -454,8 +495,8 @@ __device__ __forceinline__ void kv_block_math(const uint32_t (&sv)[32], const ui
   }
 }
 
-// q kernel, 32 key columns of one query row: dS = exp2(S*c - LSE*log2e) (dP - delta); LSE / delta are
-// this row's. Columns e >= hi are zero (MASK).
+// q kernel, 32 key columns of one query row: dS = exp2(S*c - LSE*log2e) (dP - delta) with this row's
+// LSE / delta. Columns e >= hi are zero (MASK).
 template <bool MASK>
 __device__ __forceinline__ void q_block_math(const uint32_t (&sv)[32], const uint32_t (&dv)[32], float sl2,
                                              float nlse2, float dlt, int hi, uint32_t (&dk)[16]) {
@@ -474,7 +515,7 @@ __device__ __forceinline__ void q_block_math(const uint32_t (&sv)[32], const uin
   }
 }
 
-// bf16 store of `n` (16 or 32) fp32 TMEM columns (times mul) of this thread's lane to dst.
+// bf16 store of `n` (a multiple of 16) fp32 TMEM columns (times mul) of this thread's lane to dst.
 __device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, int n, float mul, bool valid,
                                                  __nv_bfloat16* dst) {
   for (int c0 = 0; c0 < n; c0 += 16) {
@@ -507,23 +548,22 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
     return;
   }
   uint8_t* sK = smem_raw;
-  uint8_t* sV = sK + C::T;
-  uint8_t* sQ = sV + C::T;                  // [ST][T]
-  uint8_t* sDO = sQ + C::ST * C::T;         // [ST][T]
-  uint8_t* sP = sDO + C::ST * C::T;         // P^T  [128 keys][128 q]
-  uint8_t* sDS = sP + C::PT;                // dS^T [128 keys][128 q]
-  float* sLSE = reinterpret_cast<float*>(sDS + C::PT);  // [ST][128]
-  float* sDEL = sLSE + C::ST * 128;                     // [ST][128]
+  uint8_t* sV = sK + C::TT;
+  uint8_t* sQ = sV + C::TT;             // [ST][TT]
+  uint8_t* sDO = sQ + C::ST * C::TT;    // [ST][TT]
+  float* sLSE = reinterpret_cast<float*>(sDO + C::ST * C::TT);  // [ST][128]
+  float* sDEL = sLSE + C::ST * 128;                             // [ST][128]
   uint64_t* bar = reinterpret_cast<uint64_t*>(sDEL + C::ST * 128);
   uint64_t* kv_full = bar;
-  uint64_t* qd_full = bar + 1;   // [2]
-  uint64_t* qd_empty = bar + 3;  // [2]
-  uint64_t* sdp_full = bar + 5;
-  uint64_t* s_free = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* mm_done = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* qd_full = bar + 1;               // [ST]
+  uint64_t* qd_empty = bar + 1 + C::ST;      // [ST]
+  uint64_t* s_full = bar + 1 + 2 * C::ST;    // [2] S^T of a buffer computed
+  uint64_t* p_full = s_full + 2;             // [2] P^T / dS^T of a buffer written
+  uint64_t* dp_full = s_full + 4;            // dP^T computed
+  uint64_t* dp_free = s_full + 5;            // dP^T read by the element-wise warps
+  uint64_t* mm_done = s_full + 6;
+  uint64_t* drain = s_full + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -532,15 +572,18 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
   const int bg = blockIdx.x / nkb;
   const int g = bg % nkv, b = bg / nkv;
   const int G = nh / nkv;
-  const int nqb = nkb;
-  const int iters = G * (nqb - kb);
+  const int nper = nkb - kb;  // causal query blocks kb..nkb-1
+  const int iters = G * nper;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
-    mbar_init(sdp_full, 1);
-    mbar_init(s_free, BW_EW_WARPS);
-    mbar_init(p_full, BW_EW_WARPS);
+    for (int i = 0; i < C::ST; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], BW_EW_WARPS);
+    }
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, BW_EW_WARPS);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -555,75 +598,100 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
+  const uint32_t tDP = tmem + C::C_DP, tDV = tmem + C::C_DV, tDK = tmem + C::C_DK;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQKV);
       tma_prefetch_desc(&tmDO);
-      mbar_arrive_expect_tx(kv_full, 2 * C::T);
+      mbar_arrive_expect_tx(kv_full, 2 * C::TT);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         tma_load_3d(sK + c * (128 * 128), &tmQKV, kv_full, (nh + g) * D + 64 * c, kb * 128, b);
         tma_load_3d(sV + c * (128 * 128), &tmQKV, kv_full, (nh + nkv + g) * D + 64 * c, kb * 128, b);
       }
       for (int it = 0; it < iters; ++it) {
-        const int hh = it / (nqb - kb), i = kb + it % (nqb - kb), h = g * G + hh;
+        const int hh = it / nper, i = kb + it % nper, h = g * G + hh;
         const int st = it % C::ST;
         if (it >= C::ST &&
             !mbar_wait_bounded(&qd_empty[st], ((it / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 500, abort_flag))
           break;
-        mbar_arrive_expect_tx(&qd_full[st], 2 * C::T + 2 * 512);
+        mbar_arrive_expect_tx(&qd_full[st], 2 * C::TT + 2 * 512);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sQ + st * C::T + c * (128 * 128), &tmQKV, &qd_full[st], h * D + 64 * c, i * 128, b);
-          tma_load_3d(sDO + st * C::T + c * (128 * 128), &tmDO, &qd_full[st], h * D + 64 * c, i * 128, b);
+          tma_load_3d(sQ + st * C::TT + c * (128 * 128), &tmQKV, &qd_full[st], h * D + 64 * c, i * 128, b);
+          tma_load_3d(sDO + st * C::TT + c * (128 * 128), &tmDO, &qd_full[st], h * D + 64 * c, i * 128, b);
         }
         tma_load_2d(sLSE + st * 128, &tmLSE, &qd_full[st], i * 128, b * nh + h);
         tma_load_2d(sDEL + st * 128, &tmDEL, &qd_full[st], i * 128, b * nh + h);
+        ATTN_TRACE(0, it);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idKD = umma_idesc_bf16(128, D, 0, 1);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), aDS = smem_u32(sDS);
+      const uint64_t dK0 = kdesc0(smem_u32(sK)), dV0 = kdesc0(smem_u32(sV));
+      const uint64_t dQ0 = kdesc0(smem_u32(sQ)), dDO0 = kdesc0(smem_u32(sDO));
+      const uint64_t mQ0 = mndesc0(smem_u32(sQ)), mDO0 = mndesc0(smem_u32(sDO));
+      constexpr uint64_t STG = (uint64_t)(C::TT >> 4);  // stage stride in descriptor units
       bool issued = false;
-      // S^T = K Q^T and dP^T = V dO^T of block `it`
-      auto issue_sdp = [&](int it) -> bool {
-        const int st = it % C::ST;
-        if (!mbar_wait_bounded(&qd_full[st], (it / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 511, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ + st * C::T), aDO = smem_u32(sDO + st * C::T);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, kdesc(aK, k), kdesc(aQ, k), idSS, k > 0 ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aV, k), kdesc(aDO, k), idSS, k > 0 ? 1u : 0u);
-        issued = true;
-        umma_commit(sdp_full);
-        return true;
+      auto wait_stage = [&](int it) -> bool {
+        return mbar_wait_bounded(&qd_full[it % C::ST], (it / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 511, abort_flag);
       };
-      bool ok = mbar_wait_bounded(kv_full, 0, DT_ERR_TIMEOUT_FULL, 510, abort_flag);
-      if (ok && C::EARLY && iters > 0) ok = issue_sdp(0);
-      for (int it = 0; it < iters && ok; ++it) {
-        const int st = it % C::ST;
-        if (!C::EARLY) {
-          if (it > 0 && !mbar_wait_bounded(s_free, (it - 1) & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
-          if (!issue_sdp(it)) { ok = false; break; }
-        } else if (it + 1 < iters) {
-          if (!mbar_wait_bounded(s_free, it & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
-          if (!issue_sdp(it + 1)) { ok = false; break; }
-        }
-        if (!mbar_wait_bounded(p_full, it & 1, DT_ERR_TIMEOUT_FULL, 513, abort_flag)) { ok = false; break; }
+      // S^T = K Q^T of block `it` into buffer it % NSB
+      auto issue_s = [&](int it) {
+        const uint64_t q = dQ0 + (uint64_t)(it % C::ST) * STG;
+        const uint32_t tS = tmem + (it % C::NSB) * 128;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, dK0 + koff(k), q + koff(k), idSS, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[it % C::NSB]);
+        issued = true;
+      };
+      // dP^T = V dO^T of block `it`
+      auto issue_dp = [&](int it) {
+        const uint64_t o = dDO0 + (uint64_t)(it % C::ST) * STG;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, dV0 + koff(k), o + koff(k), idSS, k > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+        ATTN_TRACE(1, it);
+      };
+      bool ok = mbar_wait_bounded(kv_full, 0, DT_ERR_TIMEOUT_FULL, 510, abort_flag) && wait_stage(0);
+      if (ok) {
         tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ + st * C::T), aDO = smem_u32(sDO + st * C::T);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) umma_bf16(tDV, kdesc(aP, k), mndesc(aDO, k), idKD, (it > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) umma_bf16(tDK, kdesc(aDS, k), mndesc(aQ, k), idKD, (it > 0 || k > 0) ? 1u : 0u);
-        umma_commit(mm_done);
-        umma_commit(&qd_empty[st]);
+        issue_s(0);
+        issue_dp(0);
       }
+      for (int it = 0; it < iters && ok; ++it) {
+        const int st = it % C::ST, bb = it % C::NSB;
+        const bool more = it + 1 < iters;
+        if (more) {
+          if (!wait_stage(it + 1)) { ok = false; break; }
+          tc_fence_after();
+          // a free second buffer: S^T of the next block runs while this block's exponentials do
+          if (C::NSB == 2) issue_s(it + 1);
+          if (!mbar_wait_bounded(dp_free, it & 1, DT_ERR_TIMEOUT_TMEM, 512, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          if (C::NSB == 2) issue_dp(it + 1);
+        }
+        if (!mbar_wait_bounded(&p_full[bb], (it / C::NSB) & 1, DT_ERR_TIMEOUT_FULL, 513, abort_flag)) { ok = false; break; }
+        ATTN_TRACE(2, it);
+        tc_fence_after();
+        const uint32_t tS = tmem + bb * 128;
+        const uint64_t mq = mQ0 + (uint64_t)st * STG, mo = mDO0 + (uint64_t)st * STG;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          umma_bf16_ts(tDV, pcol(tS, 0, k), mo + mnoff(k), idKD, (it > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tDK, pcol(tS, 1, k), mq + mnoff(k), idKD, (it > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&qd_empty[st]);
+        ATTN_TRACE(7, it);
+        if (C::NSB == 1 && more) {  // the single buffer is free once dV / dK of this block are issued
+          issue_s(it + 1);
+          issue_dp(it + 1);
+        }
+      }
+      if (ok) umma_commit(mm_done);
       if (!ok && issued) {
         umma_commit(drain);
         uint64_t t0 = dt_globaltimer();
@@ -631,7 +699,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
       }
     }
   } else {
-    // ───── element-wise warps: thread = key row r, query columns [cg*32, cg*32+32) ─────
+    // ───── element-wise warps: thread = key row r, query columns [cg*32, cg*32+32) of the block ─────
     const int ew = warp - 2, quad = warp & 3, cg = ew >> 2;
     const int r = quad * 32 + lane;
     const int key = kb * 128 + r;
@@ -640,17 +708,23 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
     const bool edge_k = (kb + 1) * 128 > T;
     WarpWait wwait{abort_flag, lane};
     bool ok = true;
-    for (int it = 0; it < iters; ++it) {
-      const int i = kb + it % (nqb - kb);
-      const int st = it % C::ST;
-      if (!wwait(sdp_full, it & 1, 520)) { ok = false; break; }
-      tc_fence_after();
+    for (int it = 0; it < iters && ok; ++it) {
+      const int i = kb + it % nper;
+      const int st = it % C::ST, bb = it % C::NSB;
+      const uint32_t tS = tmem + bb * 128 + lane_off + cg * 32;
       uint32_t pk[16], dk[16];
       {
         uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tS + lane_off + cg * 32, sv);
+        if (!wwait(&s_full[bb], (it / C::NSB) & 1, 520)) { ok = false; break; }
+        tc_fence_after();
+        tmem_ld_32x32b_x32(tS, sv);
+        if (!wwait(dp_full, it & 1, 521)) { ok = false; break; }
+        if (warp == 2 && lane == 0) ATTN_TRACE(3, it);
+        tc_fence_after();
         tmem_ld_32x32b_x32(tDP + lane_off + cg * 32, dv);
         tmem_ld_wait();
+        tc_fence_before();
+        warp_arrive(dp_free, lane);
         const float* lse_s = sLSE + st * 128 + cg * 32;
         const float* del_s = sDEL + st * 128 + cg * 32;
         if (i == kb || edge_k || (i + 1) * 128 > T) {
@@ -661,17 +735,15 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
           kv_block_math<false>(sv, dv, lse_s, del_s, sl2, 0, 32, pk, dk);
         }
       }
+      tmem_st_32x32b_x16(tS, pk);
+      tmem_st_32x32b_x16(tS + 16, dk);
+      tmem_st_wait();
       tc_fence_before();
-      warp_arrive(s_free, lane);
-      // the previous block's dV / dK products must be done reading the P^T / dS^T tiles
-      if (it > 0 && !wwait(mm_done, (it - 1) & 1, 521)) { ok = false; break; }
-      store_row32(sP, r, cg, pk);
-      store_row32(sDS, r, cg, dk);
-      fence_proxy_async_smem();
-      warp_arrive(p_full, lane);
+      if (warp == 2 && lane == 0) ATTN_TRACE(4, it);
+      warp_arrive(&p_full[bb], lane);
     }
     // epilogue: dK (scaled) and dV rows of this key block, D/4 columns per thread
-    if (ok && wwait(mm_done, (iters - 1) & 1, 522)) {
+    if (ok && wwait(mm_done, 0, 522)) {
       tc_fence_after();
       const long long W = (long long)(nh + 2 * nkv) * D;
       __nv_bfloat16* krow = dqkv + ((long long)b * T + key) * W + (nh + g) * D + cg * (D / 4);
@@ -698,20 +770,21 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
     return;
   }
   uint8_t* sQ = smem_raw;
-  uint8_t* sDO = sQ + C::T;
-  uint8_t* sK = sDO + C::T;         // [ST][T]
-  uint8_t* sV = sK + C::ST * C::T;  // [ST][T]
-  uint8_t* sDS = sV + C::ST * C::T; // dS [128 q][128 keys]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sDS + C::PT);
+  uint8_t* sDO = sQ + C::TT;
+  uint8_t* sK = sDO + C::TT;          // [ST][TT]
+  uint8_t* sV = sK + C::ST * C::TT;   // [ST][TT]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + C::ST * C::TT);
   uint64_t* q_full = bar;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* sdp_full = bar + 5;
-  uint64_t* s_free = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* mm_done = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* kv_full = bar + 1;               // [ST]
+  uint64_t* kv_empty = bar + 1 + C::ST;      // [ST]
+  uint64_t* s_full = bar + 1 + 2 * C::ST;    // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* dp_full = s_full + 4;
+  uint64_t* dp_free = s_full + 5;
+  uint64_t* qt_full = s_full + 6;            // Q / dO copied into TMEM
+  uint64_t* mm_done = s_full + 7;
+  uint64_t* drain = s_full + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -720,14 +793,18 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
   const int bh = blockIdx.x / nqb;
   const int h = bh % nh, b = bh / nh;
   const int g = h / (nh / nkv);
-  const int nkb = qb + 1;
+  const int njb = qb + 1;  // causal key blocks 0..qb
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-    mbar_init(sdp_full, 1);
-    mbar_init(s_free, BW_EW_WARPS);
-    mbar_init(p_full, BW_EW_WARPS);
+    for (int i = 0; i < C::ST; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], BW_EW_WARPS);
+    }
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, BW_EW_WARPS);
+    mbar_init(qt_full, BW_EW_WARPS);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -742,28 +819,28 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tDP = tmem + 128, tDQ = tmem + 256;
+  const uint32_t tDP = tmem + C::C_DP, tDQ = tmem + C::C_DQ, tQ = tmem + C::C_Q, tDO = tmem + C::C_DO;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQKV);
       tma_prefetch_desc(&tmDO);
-      mbar_arrive_expect_tx(q_full, 2 * C::T);
+      mbar_arrive_expect_tx(q_full, 2 * C::TT);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         tma_load_3d(sQ + c * (128 * 128), &tmQKV, q_full, h * D + 64 * c, qb * 128, b);
         tma_load_3d(sDO + c * (128 * 128), &tmDO, q_full, h * D + 64 * c, qb * 128, b);
       }
-      for (int j = 0; j < nkb; ++j) {
+      for (int j = 0; j < njb; ++j) {
         const int st = j % C::ST;
         if (j >= C::ST &&
             !mbar_wait_bounded(&kv_empty[st], ((j / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 600, abort_flag))
           break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * C::T);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::TT);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sK + st * C::T + c * (128 * 128), &tmQKV, &kv_full[st], (nh + g) * D + 64 * c, j * 128, b);
-          tma_load_3d(sV + st * C::T + c * (128 * 128), &tmQKV, &kv_full[st], (nh + nkv + g) * D + 64 * c, j * 128, b);
+          tma_load_3d(sK + st * C::TT + c * (128 * 128), &tmQKV, &kv_full[st], (nh + g) * D + 64 * c, j * 128, b);
+          tma_load_3d(sV + st * C::TT + c * (128 * 128), &tmQKV, &kv_full[st], (nh + nkv + g) * D + 64 * c, j * 128, b);
         }
       }
     }
@@ -771,41 +848,56 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
     if (lane == 0) {
       constexpr uint32_t idSS = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idQD = umma_idesc_bf16(128, D, 0, 1);
-      const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO), aDS = smem_u32(sDS);
+      const uint64_t dK0 = kdesc0(smem_u32(sK)), dV0 = kdesc0(smem_u32(sV)), mK0 = mndesc0(smem_u32(sK));
+      constexpr uint64_t STG = (uint64_t)(C::TT >> 4);
       bool issued = false;
-      // S = Q K^T and dP = dO V^T of key block j
-      auto issue_sdp = [&](int j) -> bool {
-        const int st = j % C::ST;
-        if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 611, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * C::T), aV = smem_u32(sV + st * C::T);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, kdesc(aQ, k), kdesc(aK, k), idSS, k > 0 ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_bf16(tDP, kdesc(aDO, k), kdesc(aV, k), idSS, k > 0 ? 1u : 0u);
-        issued = true;
-        umma_commit(sdp_full);
-        return true;
+      auto wait_stage = [&](int j) -> bool {
+        return mbar_wait_bounded(&kv_full[j % C::ST], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 611, abort_flag);
       };
-      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 610, abort_flag);
-      if (ok && C::EARLY) ok = issue_sdp(0);
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j % C::ST;
-        if (!C::EARLY) {
-          if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
-          if (!issue_sdp(j)) { ok = false; break; }
-        } else if (j + 1 < nkb) {
-          if (!mbar_wait_bounded(s_free, j & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
-          if (!issue_sdp(j + 1)) { ok = false; break; }
-        }
-        if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 613, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * C::T);
+      auto issue_s = [&](int j) {  // S = Q K^T of key block j into buffer j % NSB
+        const uint64_t kk = dK0 + (uint64_t)(j % C::ST) * STG;
+        const uint32_t tS = tmem + (j % C::NSB) * 128;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_bf16(tDQ, kdesc(aDS, k), mndesc(aK, k), idQD, (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(mm_done);
-        umma_commit(&kv_empty[st]);
+        for (int k = 0; k < D / 16; ++k) umma_bf16_ts(tS, tQ + k * 8, kk + koff(k), idSS, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[j % C::NSB]);
+        issued = true;
+      };
+      auto issue_dp = [&](int j) {  // dP = dO V^T of key block j
+        const uint64_t vv = dV0 + (uint64_t)(j % C::ST) * STG;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_bf16_ts(tDP, tDO + k * 8, vv + koff(k), idSS, k > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+      };
+      bool ok = mbar_wait_bounded(qt_full, 0, DT_ERR_TIMEOUT_FULL, 610, abort_flag) && wait_stage(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
       }
+      for (int j = 0; j < njb && ok; ++j) {
+        const int st = j % C::ST, bb = j % C::NSB;
+        const bool more = j + 1 < njb;
+        if (more) {
+          if (!wait_stage(j + 1)) { ok = false; break; }
+          tc_fence_after();
+          if (C::NSB == 2) issue_s(j + 1);
+          if (!mbar_wait_bounded(dp_free, j & 1, DT_ERR_TIMEOUT_TMEM, 612, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          if (C::NSB == 2) issue_dp(j + 1);
+        }
+        if (!mbar_wait_bounded(&p_full[bb], (j / C::NSB) & 1, DT_ERR_TIMEOUT_FULL, 613, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tS = tmem + bb * 128;
+        const uint64_t mk = mK0 + (uint64_t)st * STG;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16_ts(tDQ, pcol(tS, 0, k), mk + mnoff(k), idQD, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&kv_empty[st]);
+        if (C::NSB == 1 && more) {
+          issue_s(j + 1);
+          issue_dp(j + 1);
+        }
+      }
+      if (ok) umma_commit(mm_done);
       if (!ok && issued) {
         umma_commit(drain);
         uint64_t t0 = dt_globaltimer();
@@ -813,7 +905,7 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
       }
     }
   } else {
-    // ───── element-wise warps: thread = query row r, key columns [cg*32, cg*32+32) ─────
+    // ───── element-wise warps: thread = query row r, key columns [cg*32, cg*32+32) of the block ─────
     const int ew = warp - 2, quad = warp & 3, cg = ew >> 2;
     const int r = quad * 32 + lane;
     const int q = qb * 128 + r;
@@ -825,16 +917,29 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
     const float dlt = (q < T) ? delta[ridx] : 0.f;
     const bool edge_q = (qb + 1) * 128 > T;
     WarpWait wwait{abort_flag, lane};
-    bool ok = true;
-    for (int j = 0; j < nkb; ++j) {
-      if (!wwait(sdp_full, j & 1, 620)) { ok = false; break; }
-      tc_fence_after();
+    bool ok = wwait(q_full, 0, 623);
+    if (ok) {
+      tile_row_to_tmem<D>(sQ, r, cg, tQ + lane_off);
+      tile_row_to_tmem<D>(sDO, r, cg, tDO + lane_off);
+      tmem_st_wait();
+      tc_fence_before();
+      warp_arrive(qt_full, lane);
+    }
+    for (int j = 0; j < njb && ok; ++j) {
+      const int bb = j % C::NSB;
+      const uint32_t tS = tmem + bb * 128 + lane_off + cg * 32;
       uint32_t dk[16];
       {
         uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tS + lane_off + cg * 32, sv);
+        if (!wwait(&s_full[bb], (j / C::NSB) & 1, 620)) { ok = false; break; }
+        tc_fence_after();
+        tmem_ld_32x32b_x32(tS, sv);
+        if (!wwait(dp_full, j & 1, 621)) { ok = false; break; }
+        tc_fence_after();
         tmem_ld_32x32b_x32(tDP + lane_off + cg * 32, dv);
         tmem_ld_wait();
+        tc_fence_before();
+        warp_arrive(dp_free, lane);
         if (j == qb || edge_q || (j + 1) * 128 > T) {
           const int kbase = j * 128 + cg * 32;
           const int hi = q < T ? min(q - kbase + 1, T - kbase) : 0;  // valid columns: e < hi
@@ -843,14 +948,12 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
           q_block_math<false>(sv, dv, sl2, nlse2, dlt, 32, dk);
         }
       }
+      tmem_st_32x32b_x16(tS, dk);
+      tmem_st_wait();
       tc_fence_before();
-      warp_arrive(s_free, lane);
-      if (j > 0 && !wwait(mm_done, (j - 1) & 1, 621)) { ok = false; break; }
-      store_row32(sDS, r, cg, dk);
-      fence_proxy_async_smem();
-      warp_arrive(p_full, lane);
+      warp_arrive(&p_full[bb], lane);
     }
-    if (ok && wwait(mm_done, (nkb - 1) & 1, 622)) {
+    if (ok && wwait(mm_done, 0, 622)) {
       tc_fence_after();
       const long long W = (long long)(nh + 2 * nkv) * D;
       __nv_bfloat16* qrow = dqkv + ((long long)b * T + q) * W + h * D + cg * (D / 4);
