@@ -145,52 +145,69 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const f
   }
 }
 
-// Warp-per-row backward (H = 128 * VEC): no block-wide barrier per row; dw partials are kept per warp
-// and reduced across the block's warps through shared memory before one atomic per column.
+// Warp-per-row backward (H = 128 * VEC): no block-wide barrier per row. All three row loads (dy, x,
+// dresid_in) are issued before the row's reduction so each warp keeps ~7.5 KB (H = 768) in flight, and
+// w and the per-warp dw partials live in shared memory so two 256-thread blocks fit per SM (<= 128
+// registers); the partials are reduced across the block's warps before one atomic per column.
+// Blocks per SM: 2 while a row's loads fit 128 registers (VEC <= 8); wider rows keep one block, whose
+// 8 warps already hold >= 80 KB in flight.
 template <int VEC>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
+constexpr int rms_bwd_blocks() { return VEC <= 8 ? 2 : 1; }
+
+template <int VEC>
+__global__ void __launch_bounds__(256, rms_bwd_blocks<VEC>()) rmsnorm_bwd_warp_kernel(
     const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ rstd,
     const float* __restrict__ w, const float* __restrict__ scale, const float* dresid_in, float* dresid_out,
     __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw, float* __restrict__ dscale, int M, int H) {
-  extern __shared__ float red[];  // [8 warps][H]
+  extern __shared__ float red[];  // [8 warps][H] dw partials, then w [H]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const float s = scale ? *scale : 1.f;
-  float4 wv[VEC], acc[VEC];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    wv[i] = *reinterpret_cast<const float4*>(w + (i * 32 + lane) * 4);
-    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  float* sw = red + 8 * H;
+  float* acc = red + wid * H;
+  for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4)
+    *reinterpret_cast<float4*>(sw + c) = *reinterpret_cast<const float4*>(w + c);
+  for (int c = threadIdx.x * 4; c < 8 * H; c += blockDim.x * 4)
+    *reinterpret_cast<float4*>(red + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
   float ds_acc = 0.f;
   const int gw = blockIdx.x * 8 + wid, nw = gridDim.x * 8;
   for (long long row = gw; row < M; row += nw) {
     const float rs = rstd[row];
-    float4 g[VEC], xh[VEC];
+    uint2 graw[VEC];
+    float4 xh[VEC], pin[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      graw[i] = *reinterpret_cast<const uint2*>(dy + row * H + c);
+      xh[i] = *reinterpret_cast<const float4*>(x + row * H + c);
+      if (dresid_in) pin[i] = *reinterpret_cast<const float4*>(dresid_in + row * H + c);
+    }
     float dot = 0.f, dsd = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 4;
-      uint2 bb = *reinterpret_cast<const uint2*>(dy + row * H + c);
-      float2 a = unpack_bf16(bb.x), b = unpack_bf16(bb.y);
-      float4 xv = *reinterpret_cast<const float4*>(x + row * H + c);
-      xh[i] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
-      g[i] = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
-      dot += g[i].x * wv[i].x * xh[i].x + g[i].y * wv[i].y * xh[i].y + g[i].z * wv[i].z * xh[i].z +
-             g[i].w * wv[i].w * xh[i].w;
-      if (dscale) dsd += a.x * xh[i].x * wv[i].x + a.y * xh[i].y * wv[i].y + b.x * xh[i].z * wv[i].z + b.y * xh[i].w * wv[i].w;
-      acc[i].x += g[i].x * xh[i].x; acc[i].y += g[i].y * xh[i].y;
-      acc[i].z += g[i].z * xh[i].z; acc[i].w += g[i].w * xh[i].w;
+      const float4 wv = *reinterpret_cast<const float4*>(sw + c);
+      const float2 a = unpack_bf16(graw[i].x), b = unpack_bf16(graw[i].y);
+      xh[i] = make_float4(xh[i].x * rs, xh[i].y * rs, xh[i].z * rs, xh[i].w * rs);
+      const float4 g = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
+      dot += g.x * wv.x * xh[i].x + g.y * wv.y * xh[i].y + g.z * wv.z * xh[i].z + g.w * wv.w * xh[i].w;
+      if (dscale) dsd += a.x * xh[i].x * wv.x + a.y * xh[i].y * wv.y + b.x * xh[i].z * wv.z + b.y * xh[i].w * wv.w;
+      float4 av = *reinterpret_cast<float4*>(acc + c);
+      av.x += g.x * xh[i].x; av.y += g.y * xh[i].y;
+      av.z += g.z * xh[i].z; av.w += g.w * xh[i].w;
+      *reinterpret_cast<float4*>(acc + c) = av;
     }
     const float mean = warp_sum(dot) / (float)H;
     ds_acc += dsd;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 4;
-      float4 d = make_float4(rs * (g[i].x * wv[i].x - xh[i].x * mean), rs * (g[i].y * wv[i].y - xh[i].y * mean),
-                             rs * (g[i].z * wv[i].z - xh[i].z * mean), rs * (g[i].w * wv[i].w - xh[i].w * mean));
+      const float4 wv = *reinterpret_cast<const float4*>(sw + c);
+      const float2 a = unpack_bf16(graw[i].x), b = unpack_bf16(graw[i].y);
+      float4 d = make_float4(rs * (a.x * s * wv.x - xh[i].x * mean), rs * (a.y * s * wv.y - xh[i].y * mean),
+                             rs * (b.x * s * wv.z - xh[i].z * mean), rs * (b.y * s * wv.w - xh[i].w * mean));
       if (dresid_in) {
-        float4 p = *reinterpret_cast<const float4*>(dresid_in + row * H + c);
-        d.x += p.x; d.y += p.y; d.z += p.z; d.w += p.w;
+        d.x += pin[i].x; d.y += pin[i].y; d.z += pin[i].z; d.w += pin[i].w;
       }
       *reinterpret_cast<float4*>(dresid_out + row * H + c) = d;
       if (dresid16) {
@@ -201,8 +218,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
       }
     }
   }
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) *reinterpret_cast<float4*>(red + wid * H + (i * 32 + lane) * 4) = acc[i];
   __syncthreads();
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     float t = 0.f;
@@ -264,8 +279,9 @@ DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, con
   auto d16 = reinterpret_cast<__nv_bfloat16*>(dresid16);
   if (H % 128 == 0 && H <= 2048) {
     int wb = (M + 7) / 8;
-    if (wb > 148 * 4) wb = 148 * 4;
-    size_t sm = sizeof(float) * 8 * H;
+    const int per_sm = (H / 128) <= 8 ? 2 : 1;
+    if (wb > 148 * per_sm) wb = 148 * per_sm;
+    size_t sm = sizeof(float) * 9 * H;
 #define DT_RMS_WARP(V)                                                                                       \
   case V:                                                                                                   \
     if (sm > 48 * 1024) cudaFuncSetAttribute(rmsnorm_bwd_warp_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \

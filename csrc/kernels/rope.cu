@@ -8,7 +8,10 @@
 
 namespace {
 
-constexpr int ROWS = 16;
+// Block = (items, ry <= RY_MAX) threads over ROWS_F (forward) / ROWS_B (backward) rows; ry rows are
+// processed in parallel. The backward reduces the bias gradient over the block's rows through shared
+// memory and issues one atomic per column per block (64 rows), not per 16 rows and thread.
+constexpr int RY_MAX = 4, ROWS_F = 16, ROWS_B = 64;
 
 // Work items per row, in units of 8 elements: P8 = (nh+nkv) * d/16 rotation groups (8 pairs each),
 // then V8 = nkv * d/8 groups of v elements.
@@ -39,10 +42,11 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
   const int g_per_head = half / 8;
   const int P8 = (nh + nkv) * g_per_head, V8 = nkv * d / 8, items = P8 + V8;
   const int vbase = (nh + nkv) * d;
-  const int j = threadIdx.x;  // one item per thread (blockDim >= items, host-checked)
-  if (j >= items) return;
-  int c0, c1 = -1, i0 = 0;
-  if (j < P8) {
+  const int j = threadIdx.x, y = threadIdx.y, RY = blockDim.y;  // one item per thread (blockDim.x >= items, host-checked)
+  const bool active = j < items;
+  int c0 = 0, c1 = -1, i0 = 0;
+  if (!active) {
+  } else if (j < P8) {
     int head = j / g_per_head, g = j - head * g_per_head;
     i0 = g * 8;
     c0 = head * d + i0;
@@ -56,11 +60,12 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
   float b0[8], b1[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    b0[k] = (!BWD && bias) ? bias[c0 + k] : 0.f;
+    b0[k] = (!BWD && bias && active) ? bias[c0 + k] : 0.f;
     b1[k] = (!BWD && bias && c1 >= 0) ? bias[c1 + k] : 0.f;
   }
-  const int r0 = blockIdx.x * ROWS;
-  for (int rr = 0; rr < ROWS; ++rr) {
+  const int rows = BWD ? ROWS_B : ROWS_F;
+  const long long r0 = (long long)blockIdx.x * rows;
+  for (int rr = y; rr < rows && active; rr += RY) {
     const long long row = r0 + rr;
     if (row >= M) break;
     const int t = (int)(row % T);
@@ -103,10 +108,22 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
     store8(p + c1, o1);
   }
   if (BWD && dbias) {
+    extern __shared__ float red[];  // [RY][blockDim.x][16]
+    float* mine = red + ((size_t)y * blockDim.x + j) * 16;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      atomicAdd(dbias + c0 + k, acc0[k]);
-      if (c1 >= 0) atomicAdd(dbias + c1 + k, acc1[k]);
+      mine[k] = acc0[k];
+      mine[8 + k] = acc1[k];
+    }
+    __syncthreads();
+    if (y == 0 && active) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float t = 0.f;
+        for (int yy = 0; yy < RY; ++yy) t += red[((size_t)yy * blockDim.x + j) * 16 + k];
+        if (k < 8) atomicAdd(dbias + c0 + k, t);
+        else if (c1 >= 0) atomicAdd(dbias + c1 + k - 8, t);
+      }
     }
   }
 }
@@ -119,10 +136,19 @@ static int rope_launch(bool bwd, void* qkv, const float* bias, float* dbias, con
   int items = (nh + nkv) * (d / 16) + nkv * d / 8;
   int th = ((items + 31) / 32) * 32;
   if (th > 1024) return -11;
-  int blocks = (M + ROWS - 1) / ROWS;
+  int ry = RY_MAX;  // row lanes: the block stays <= 1024 threads and its reduction buffer <= 48 KB
+  while (ry > 1 && (th * ry > 1024 || sizeof(float) * 16 * th * ry > 48 * 1024)) ry /= 2;
+  if (th * ry > 1024 || sizeof(float) * 16 * th * ry > 48 * 1024) return -11;
+  const int rows = bwd ? ROWS_B : ROWS_F;
+  int blocks = (M + rows - 1) / rows;
   auto p = reinterpret_cast<__nv_bfloat16*>(qkv);
-  if (bwd) rope_kernel<true><<<blocks, th, 0, st>>>(p, nullptr, dbias, cosT, sinT, M, T, nh, nkv, d);
-  else rope_kernel<false><<<blocks, th, 0, st>>>(p, bias, nullptr, cosT, sinT, M, T, nh, nkv, d);
+  dim3 blk(th, ry);
+  if (bwd) {
+    size_t sm = sizeof(float) * 16 * th * ry;
+    rope_kernel<true><<<blocks, blk, sm, st>>>(p, nullptr, dbias, cosT, sinT, M, T, nh, nkv, d);
+  } else {
+    rope_kernel<false><<<blocks, blk, 0, st>>>(p, bias, nullptr, cosT, sinT, M, T, nh, nkv, d);
+  }
   return (int)cudaGetLastError();
 }
 
