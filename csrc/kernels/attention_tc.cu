@@ -1,20 +1,29 @@
-// Causal GQA flash-attention forward on the 5th-generation tensor cores (tcgen05 + TMEM), d = 64 / 128.
+// Causal GQA flash attention on the 5th-generation tensor cores (tcgen05 + TMEM), d = 64 / 128.
 //
 // Same contract as the mma.sync kernels in attention.cu (q/k/v read from the fused QKV activation,
-// query head h uses kv head h / (nh/nkv), out [B*T, nh*D] bf16, lse [B, nh, T] fp32 natural log).
+// query head h uses kv head h / (nh/nkv), out [B*T, nh*D] bf16, lse [B, nh, Tp] fp32 natural log with
+// Tp = T rounded up to a multiple of 4 so every row starts 16-byte aligned).
 //
-// One CTA = 128 query rows of one (batch, head); 6 warps:
+// Cost model behind the layouts (measured on B200): a tcgen05.mma with M = 128 costs the tensor core
+// about N/2 clocks, but a single issuing thread does not issue much faster than one per ~50 clocks, so
+// products are kept N = 128 wide where the shapes allow, the issue loops only add constants to
+// precomputed descriptors, and two CTAs share an SM where TMEM allows (two issuers). The softmax side
+// is bound by the exp2 unit (16 results / clock / SM).
+//
+// Forward. One CTA = 128 query rows of one (batch, head); 10 warps:
 //   warp 0     TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring (3-D tensor map
 //              [B, T, W] so rows past T are zero-filled per sequence; no cluster multicast)
-//   warp 1     single-thread tcgen05.mma issuer: S = Q K^T (M=128, N=128) into TMEM, then
-//              O += P V (M=128, N=D, K=128) with P from shared memory and V as an MN-major operand
-//   warps 2-5  softmax: thread i owns query row i = TMEM lane i. Two passes over S (max, then
-//              exp2 / row-sum / bf16 P written in the 128-byte-swizzled K-major layout the MMA reads).
-//              The running max is only raised when it grows by more than 8 (log2 units); O in TMEM is
-//              rescaled (tcgen05.ld/st) only then, otherwise P is taken against the stale max (values
-//              stay <= 2^8, exact after normalisation).
-// TMEM: S at columns [0,128), O at [128, 128+D) -> 256 columns, so two CTAs share an SM (d = 64) and
-// one CTA's softmax overlaps the other's MMAs. Every mbarrier wait is bounded.
+//   warp 1     single-thread tcgen05.mma issuer: S = Q K^T (N = 128) into TMEM; O += P V with P a TMEM
+//              A operand and V an MN-major shared operand. S of block j+1 is issued as soon as the
+//              softmax warps have read S of block j, before P V of block j.
+//   warps 2-9  softmax: two threads per query row (TMEM lane), 64 columns each; the row max is
+//              exchanged through shared memory once per block. The running
+//              max is only raised when it grows by more than 8 (log2 units); O in TMEM is rescaled
+//              (tcgen05.ld/st) only then, otherwise P is taken against the stale max (values stay
+//              <= 2^8, exact after normalisation). The pair exchanges through per-quarter mbarriers
+//              (bounded waits), not a named barrier, so a warp that gives up cannot strand its partner.
+// TMEM: S [0,128), O [128,128+D), P (bf16 pairs) [128+D, 192+D): 256 columns at d = 64, so two CTAs
+// share an SM and one CTA's softmax overlaps the other's products. Every mbarrier wait is bounded.
 #include "common.cuh"
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -22,49 +31,111 @@
 
 namespace {
 
-constexpr int BQ = 128, BKV = 128, NTH = 192;
+constexpr int BQ = 128, BKV = 128;
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float LN2_F = 0.6931471805599453f;
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
-template <int D>
-struct FCfg {
-  static constexpr int QB = BQ * D * 2;        // Q tile bytes
-  static constexpr int KB = BKV * D * 2;       // K tile bytes
-  static constexpr int VB = BKV * D * 2;       // V tile bytes
-  static constexpr int PB = BQ * BKV * 2;      // P tile bytes
-  static constexpr int STAGES = 2;
-  // no alignment slack: with no static shared memory the dynamic window starts 1024-aligned
-  // (checked at run time), which keeps two d=64 CTAs within one SM's 228 KB
-  static constexpr int SMEM = QB + STAGES * (KB + VB) + PB + 256;
-  static constexpr int TMEM_COLS = 256;
+// Descriptor offsets (in 16-byte units) of K-step k within a [128 rows][D] swizzled tile of 64-wide
+// chunks: K-major (16 elements along the row) and MN-major (16 rows) use.
+__host__ __device__ constexpr uint64_t koff(int k) { return (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4); }
+__host__ __device__ constexpr uint64_t mnoff(int k) { return (uint64_t)((k * 2048) >> 4); }
+__device__ __forceinline__ uint64_t kdesc0(uint32_t base) { return umma_smem_desc_sw128(base, 16, 1024); }
+__device__ __forceinline__ uint64_t mndesc0(uint32_t base) { return umma_smem_desc_sw128(base, 128 * 128, 1024); }
+
+struct WarpWait {
+  volatile int* abort_flag;
+  int lane;
+  __device__ bool operator()(uint64_t* bb, uint32_t par, int site) const {
+    int okl = 1;
+    if (lane == 0) okl = mbar_wait_bounded(bb, par, DT_ERR_TIMEOUT_TMEM, site, abort_flag) ? 1 : 0;
+    okl = __shfl_sync(0xffffffffu, okl, 0);
+    __syncwarp();
+    return okl != 0;
+  }
 };
 
+// One arrival per warp on a barrier initialised with the number of arriving warps.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+// bf16 store of `n` (a multiple of 16) fp32 TMEM columns (times mul) of this thread's lane to dst.
+__device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, int n, float mul, bool valid,
+                                                 __nv_bfloat16* dst) {
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    uint32_t o[16];
+    tmem_ld_32x32b_x16(taddr + c0, o);
+    tmem_ld_wait();
+    if (valid) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        uint4 w;
+        w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * mul, __uint_as_float(o[8 * v + 1]) * mul);
+        w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * mul, __uint_as_float(o[8 * v + 3]) * mul);
+        w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * mul, __uint_as_float(o[8 * v + 5]) * mul);
+        w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * mul, __uint_as_float(o[8 * v + 7]) * mul);
+        *reinterpret_cast<uint4*>(dst + c0 + 8 * v) = w;
+      }
+    }
+  }
+}
+
+// In-place scale of `n` (a multiple of 16) fp32 TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_row_scale(uint32_t taddr, int n, float mul) {
+  for (int c0 = 0; c0 < n; c0 += 16) {
+    uint32_t o[16];
+    tmem_ld_32x32b_x16(taddr + c0, o);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * mul);
+    tmem_st_32x32b_x16(taddr + c0, o);
+  }
+  tmem_st_wait();
+}
+
+constexpr int FWD_SM_WARPS = 8;                    // softmax warps: two per TMEM lane quarter
+constexpr int FWD_THREADS = 64 + 32 * FWD_SM_WARPS;
+
 template <int D>
-__global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV,
-                                                              __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
-                                                              int B, int T, int nh, int nkv, float scale) {
+struct FCfg {
+  static constexpr int CTAS = (D == 64) ? 2 : 1;   // CTAs per SM
+  static constexpr int ST = 2;                     // K / V stages
+  static constexpr int TT = 128 * D * 2;           // one [128][D] bf16 tile
+  static constexpr int SMEM = TT + ST * 2 * TT + 4 * 128 * 4 + 2 * 128 * 4 + 256;
+  static constexpr int TMEM_COLS = (D == 64) ? 256 : 512;
+  static constexpr int C_O = 128, C_P = 128 + D;
+  static_assert(C_P + 64 <= TMEM_COLS, "forward TMEM budget");
+};
+static_assert(2 * (FCfg<64>::SMEM + 1024) <= 233472 && FCfg<128>::SMEM <= 232448, "forward shared memory");
+
+template <int D>
+__global__ void __launch_bounds__(FWD_THREADS, FCfg<D>::CTAS)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __restrict__ out,
+                   float* __restrict__ lse, int B, int T, int nh, int nkv, float scale) {
   using C = FCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA; nothing allocated yet
     if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 499);
     return;
   }
-  uint8_t* sm = smem_raw;
-  uint8_t* sQ = sm;
-  uint8_t* sK = sQ + C::QB;                 // [STAGES][KB]
-  uint8_t* sV = sK + C::STAGES * C::KB;     // [STAGES][VB]
-  uint8_t* sP = sV + C::STAGES * C::VB;     // [PB]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + C::PB);
+  uint8_t* sQ = smem_raw;
+  uint8_t* sK = sQ + C::TT;             // [ST][TT]
+  uint8_t* sV = sK + C::ST * C::TT;     // [ST][TT]
+  float* sMax = reinterpret_cast<float*>(sV + C::ST * C::TT);  // [2 parity][2 halves][128 rows]
+  float* sL = sMax + 4 * 128;                                  // [2 halves][128 rows]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sL + 2 * 128);
   uint64_t* q_full = bar;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* s_full = bar + 5;
-  uint64_t* s_free = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* pv_done = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* kv_full = bar + 1;           // [ST]
+  uint64_t* kv_empty = bar + 1 + C::ST;  // [ST]
+  uint64_t* s_full = bar + 1 + 2 * C::ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = s_full + 3;
+  uint64_t* drain = s_full + 4;
+  uint64_t* xch = s_full + 5;  // [4 quarters][3]: row-max exchange (block parity 0 / 1), row-sum exchange
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 5 + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -77,12 +148,13 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < C::ST; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
+    mbar_init(s_free, FWD_SM_WARPS);
+    mbar_init(p_full, FWD_SM_WARPS);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 12; ++i) mbar_init(&xch[i], 2);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -95,23 +167,25 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + C::C_O, tP = tmem + C::C_P;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQKV);
       const int xq = h * D, xk = (nh + g) * D, xv = (nh + nkv + g) * D;
-      mbar_arrive_expect_tx(q_full, C::QB);
+      mbar_arrive_expect_tx(q_full, C::TT);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) tma_load_3d(sQ + c * (BQ * 128), &tmQKV, q_full, xq + 64 * c, qb * BQ, b);
       for (int j = 0; j < nkb; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait_bounded(&kv_empty[st], ((j >> 1) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], C::KB + C::VB);
+        const int st = j % C::ST;
+        if (j >= C::ST &&
+            !mbar_wait_bounded(&kv_empty[st], ((j / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag))
+          break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::TT);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sK + st * C::KB + c * (BKV * 128), &tmQKV, &kv_full[st], xk + 64 * c, j * BKV, b);
-          tma_load_3d(sV + st * C::VB + c * (BKV * 128), &tmQKV, &kv_full[st], xv + 64 * c, j * BKV, b);
+          tma_load_3d(sK + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xk + 64 * c, j * BKV, b);
+          tma_load_3d(sV + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xv + 64 * c, j * BKV, b);
         }
       }
     }
@@ -119,40 +193,38 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
     if (lane == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(BQ, BKV, 0, 0);
       constexpr uint32_t idO = umma_idesc_bf16(BQ, D, 0, 1);
-      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 410, abort_flag);
-      const uint32_t aq = smem_u32(sQ);
+      constexpr uint64_t STG = (uint64_t)(C::TT >> 4);
+      const uint64_t dQ0 = kdesc0(smem_u32(sQ)), dK0 = kdesc0(smem_u32(sK)), mV0 = mndesc0(smem_u32(sV));
       bool issued = false;
-      auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait_bounded(p_full, jj & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) return false;
+      auto issue_s = [&](int j) -> bool {  // S = Q K^T of key block j
+        if (!mbar_wait_bounded(&kv_full[j % C::ST], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 411, abort_flag))
+          return false;
         tc_fence_after();
-        const uint32_t ap = smem_u32(sP), bv = smem_u32(sV + (jj & 1) * C::VB);
+        const uint64_t kk = dK0 + (uint64_t)(j % C::ST) * STG;
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k) {
-          uint64_t ad = umma_smem_desc_sw128(ap + (k >> 2) * (BQ * 128) + (k & 3) * 32, 16, 1024);
-          uint64_t bd = umma_smem_desc_sw128(bv + k * 2048, BKV * 128, 1024);
-          umma_bf16(tO, ad, bd, idO, (jj > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[jj & 1]);
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, dQ0 + koff(k), kk + koff(k), idS, k > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        issued = true;
         return true;
       };
+      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 410, abort_flag) && issue_s(0);
       for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait_bounded(&kv_full[st], (j >> 1) & 1, DT_ERR_TIMEOUT_FULL, 411, abort_flag)) { ok = false; break; }
-        if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1, DT_ERR_TIMEOUT_TMEM, 412, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t bk = smem_u32(sK + st * C::KB);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          uint64_t ad = umma_smem_desc_sw128(aq + (k >> 2) * (BQ * 128) + (k & 3) * 32, 16, 1024);
-          uint64_t bd = umma_smem_desc_sw128(bk + (k >> 2) * (BKV * 128) + (k & 3) * 32, 16, 1024);
-          umma_bf16(tS, ad, bd, idS, k > 0 ? 1u : 0u);
+        const int st = j % C::ST;
+        if (j + 1 < nkb) {
+          // S of the next block once the softmax warps have read this block's S out of TMEM
+          if (!mbar_wait_bounded(s_free, j & 1, DT_ERR_TIMEOUT_TMEM, 412, abort_flag) || !issue_s(j + 1)) {
+            ok = false;
+            break;
+          }
         }
-        issued = true;
-        umma_commit(s_full);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t vv = mV0 + (uint64_t)st * STG;
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k) umma_bf16_ts(tO, tP + k * 8, vv + mnoff(k), idO, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[st]);
       }
-      if (ok) ok = issue_pv(nkb - 1);
       if (!ok && issued) {
         umma_commit(drain);
         uint64_t t0 = dt_globaltimer();
@@ -160,130 +232,93 @@ __global__ void __launch_bounds__(NTH, 1) attn_fwd_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // ───────────── softmax warps: row r = TMEM lane r ─────────────
-    const int quad = warp & 3;
+    // ───── softmax warps: row r = TMEM lane r, key columns [cg*64, cg*64+64) of each block ─────
+    const int sw = warp - 2, quad = warp & 3, cg = sw >> 2;
     const int r = quad * 32 + lane;
     const int q = qb * BQ + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = scale * LOG2E_F;
-    float m_run = -INFINITY, l_run = 0.f;
+    const uint64_t sl2v = f2_pack(sl2, sl2);
+    float m_run = -INFINITY, l_part = 0.f;
+    WarpWait wwait{abort_flag, lane};
     bool ok = true;
-    // one lane waits, the warp follows: keeps every lane on the same path around warp-collective TMEM ops
-    auto wwait = [&](uint64_t* bb, uint32_t par, int site) -> bool {
-      int okl = 1;
-      if (lane == 0) okl = mbar_wait_bounded(bb, par, DT_ERR_TIMEOUT_TMEM, site, abort_flag) ? 1 : 0;
-      okl = __shfl_sync(0xffffffffu, okl, 0);
-      __syncwarp();
-      return okl != 0;
-    };
-    for (int j = 0; j < nkb; ++j) {
+    for (int j = 0; j < nkb && ok; ++j) {
       if (!wwait(s_full, j & 1, 420)) { ok = false; break; }
       tc_fence_after();
-      const int key0 = j * BKV;
-      const bool diag = (j == qb);
-      // pass A: row max over the 128 scores (masked)
+      uint32_t sv[64];
+      tmem_ld_32x32b_x32(tS + lane_off + cg * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(tS + lane_off + cg * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      warp_arrive(s_free, lane);
+      const int key0 = j * BKV + cg * 64;
+      const bool need_mask = (j == qb) || (j + 1) * BKV > T;
+      // valid columns e < hi (causal key <= q, key < T); rows q >= T have none
+      const int hi = need_mask ? (q < T ? min(q - key0 + 1, T - key0) : 0) : 64;
       float mx = -INFINITY;
+      if (need_mask) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t v[2][32];
-        tmem_ld_32x32b_x32(tS + lane_off + h2 * 64, v[0]);
-        tmem_ld_32x32b_x32(tS + lane_off + h2 * 64 + 32, v[1]);
-        tmem_ld_wait();
+        for (int e = 0; e < 64; ++e) mx = (e < hi) ? fmaxf(mx, __uint_as_float(sv[e])) : mx;
+      } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int key = key0 + h2 * 64 + c;
-          float sv = __uint_as_float(v[c >> 5][c & 31]) * sl2;
-          if ((diag && key > q) || key >= T) sv = -INFINITY;
-          mx = fmaxf(mx, sv);
-        }
+        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
       }
+      // row max over both halves (partner warp: same lane quarter, other column half)
+      float* mbuf = sMax + (j & 1) * 256;
+      mbuf[cg * 128 + r] = mx;
+      warp_arrive(&xch[quad * 3 + (j & 1)], lane);
+      if (!wwait(&xch[quad * 3 + (j & 1)], (j >> 1) & 1, 423)) { ok = false; break; }
+      mx = fmaxf(mx, mbuf[(cg ^ 1) * 128 + r]);
+      const float m_new = mx * sl2;  // -inf when the row has no valid key yet
       // stale-max policy: raise the reference max only when it grows by more than the threshold
       float m_use = m_run;
       bool resc = false;
-      if (mx > m_run + RESCALE_THRESHOLD || m_run == -INFINITY) {
-        m_use = mx;
+      if (m_new > m_run + RESCALE_THRESHOLD || m_run == -INFINITY) {
+        m_use = m_new;
         resc = (m_run != -INFINITY);
       }
       const float m_safe = (m_use == -INFINITY) ? 0.f : m_use;
       const float alpha = resc ? ex2_approx(m_run - m_use) : 1.f;
-      // P buffer and O are busy until the previous P.V has completed
+      const uint64_t nm = f2_pack(-m_safe, -m_safe);
+      uint32_t pk[32];
+      uint64_t rs2 = f2_pack(0.f, 0.f);
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) {
+        const float2 x = f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2v, nm));
+        float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+        if (need_mask) {
+          p0 = (e < hi) ? p0 : 0.f;
+          p1 = (e + 1 < hi) ? p1 : 0.f;
+        }
+        rs2 = f2_add(rs2, f2_pack(p0, p1));
+        pk[e / 2] = pack_bf16(p0, p1);
+      }
+      const float2 rs = f2_unpack(rs2);
+      l_part = l_part * alpha + (rs.x + rs.y);
+      m_run = m_use;
+      // P and O are busy until the previous P V has completed
       if (j > 0 && !wwait(pv_done, (j - 1) & 1, 421)) { ok = false; break; }
       tc_fence_after();
-      // pass B: p = exp2(s - m), row sum, bf16 P tile in the swizzled K-major layout
-      float rs = 0.f;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t v[2][32];
-        tmem_ld_32x32b_x32(tS + lane_off + h2 * 64, v[0]);
-        tmem_ld_32x32b_x32(tS + lane_off + h2 * 64 + 32, v[1]);
-        tmem_ld_wait();
-        if (h2 == 1) {
-          tc_fence_before();
-          mbar_arrive(s_free);  // S fully in registers: the next Q K^T may overwrite it
-        }
-        uint8_t* prow = sP + h2 * (BQ * 128) + r * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          float pv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int c = ch * 8 + e;
-            const int key = key0 + h2 * 64 + c;
-            float sv = __uint_as_float(v[c >> 5][c & 31]) * sl2;
-            float p = ((diag && key > q) || key >= T) ? 0.f : ex2_approx(sv - m_safe);
-            pv[e] = p;
-            rs += p;
-          }
-          uint4 w;
-          w.x = pack_bf16(pv[0], pv[1]);
-          w.y = pack_bf16(pv[2], pv[3]);
-          w.z = pack_bf16(pv[4], pv[5]);
-          w.w = pack_bf16(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) * 16)) = w;
-        }
-      }
-      l_run = l_run * alpha + rs;
-      m_run = m_use;
-      // rescale O (warp-collective TMEM access; lanes that need no rescale multiply by 1)
-      if (__any_sync(0xffffffffu, resc) && j > 0) {
-#pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tO + lane_off + c0, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st_32x32b_x32(tO + lane_off + c0, o);
-        }
-        tmem_st_wait();
-      }
-      fence_proxy_async_smem();
+      if (__any_sync(0xffffffffu, resc)) tmem_row_scale(tO + lane_off + cg * (D / 2), D / 2, alpha);
+      tmem_st_32x32b_x16(tP + lane_off + cg * 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+      tmem_st_32x32b_x16(tP + lane_off + cg * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      warp_arrive(p_full, lane);
     }
-    // epilogue: O / l -> bf16 rows of `out`, lse
+    // epilogue: O / l -> bf16 rows of `out` (this half's D/2 columns), lse
     if (ok && wwait(pv_done, (nkb - 1) & 1, 422)) {
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = out + ((long long)b * T + q) * ((long long)nh * D) + h * D;
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(tO + lane_off + c0, o);
-        tmem_ld_wait();
-        if (q < T) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-            w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-            w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-            w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c0 + 8 * v) = w;
-          }
-        }
-      }
-      if (q < T) lse[((long long)b * nh + h) * ((T + 3) & ~3) + q] = (m_run + log2f(l_run)) * LN2_F;
+      sL[cg * 128 + r] = l_part;
+      warp_arrive(&xch[quad * 3 + 2], lane);
+      ok = wwait(&xch[quad * 3 + 2], 0, 424);
+    }
+    if (ok) {
+      const float l = l_part + sL[(cg ^ 1) * 128 + r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = out + ((long long)b * T + q) * ((long long)nh * D) + h * D + cg * (D / 2);
+      tmem_row_to_bf16(tO + lane_off + cg * (D / 2), D / 2, inv, q < T, orow);
+      if (cg == 0 && q < T) lse[((long long)b * nh + h) * ((T + 3) & ~3) + q] = (m_run + log2f(l)) * LN2_F;
     }
   }
 
@@ -329,8 +364,8 @@ int fwd_tc_launch(const void* qkv, void* out, float* lse, int B, int T, int nh, 
     set = true;
   }
   int nqb = (T + BQ - 1) / BQ;
-  attn_fwd_tc_kernel<D><<<B * nh * nqb, NTH, C::SMEM, st>>>(m, reinterpret_cast<__nv_bfloat16*>(out), lse, B, T, nh,
-                                                             nkv, scale);
+  attn_fwd_tc_kernel<D><<<B * nh * nqb, FWD_THREADS, C::SMEM, st>>>(m, reinterpret_cast<__nv_bfloat16*>(out), lse, B,
+                                                                     T, nh, nkv, scale);
   return (int)cudaGetLastError();
 }
 
@@ -355,9 +390,7 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
 //     operands and accumulate in TMEM; written once at the end.
 //   attn_bwd_q_tc: CTA = 128 queries of one head; loops over the causal 128-key blocks; recomputes S
 //     and dP (Q and dO held in TMEM as A operands), forms dS in TMEM, accumulates dQ += dS K.
-// Cost model (measured): a tcgen05.mma with M = 128 costs the tensor core about N/2 clocks, but one
-// issuing thread cannot issue much faster than one per ~50 clocks, so products are kept N = 128 wide
-// where the shapes allow and the issue loop does no descriptor arithmetic beyond constant adds. At
+// Products are kept N = 128 wide where the shapes allow (see the cost model at the top). At
 // d = 64 S^T is double-buffered in TMEM (columns: S 2 x 128, dP 128, dV 64, dK 64) so the tensor cores
 // compute block i+1 while block i's exponentials (16 results / clock / SM) run; at d = 128 the
 // accumulators take the room of the second buffer.
@@ -409,35 +442,11 @@ struct QCfg {
 static_assert(KVCfg<64>::SMEM <= 232448 && KVCfg<128>::SMEM <= 232448, "kv backward shared memory");
 static_assert(QCfg<64>::SMEM <= 232448 && QCfg<128>::SMEM <= 232448, "q backward shared memory");
 
-// Descriptor offsets (in 16-byte units) of K-step k within a [128 rows][D] swizzled tile of 64-wide
-// chunks: K-major (16 elements along the row) and MN-major (16 rows) use.
-__host__ __device__ constexpr uint64_t koff(int k) { return (uint64_t)(((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4); }
-__host__ __device__ constexpr uint64_t mnoff(int k) { return (uint64_t)((k * 2048) >> 4); }
-__device__ __forceinline__ uint64_t kdesc0(uint32_t base) { return umma_smem_desc_sw128(base, 16, 1024); }
-__device__ __forceinline__ uint64_t mndesc0(uint32_t base) { return umma_smem_desc_sw128(base, 128 * 128, 1024); }
 // TMEM A operand of K-step k of a bf16 tile written by the element-wise threads: thread group cg holds
 // elements [32cg, 32cg+32) as 16 packed columns at buf + 32cg + half*16; K-step k is group k>>1's
 // columns (k&1)*8 .. +8.
 __device__ __forceinline__ uint32_t pcol(uint32_t buf, int half, int k) {
   return buf + (k >> 1) * 32 + half * 16 + (k & 1) * 8;
-}
-
-struct WarpWait {
-  volatile int* abort_flag;
-  int lane;
-  __device__ bool operator()(uint64_t* bb, uint32_t par, int site) const {
-    int okl = 1;
-    if (lane == 0) okl = mbar_wait_bounded(bb, par, DT_ERR_TIMEOUT_TMEM, site, abort_flag) ? 1 : 0;
-    okl = __shfl_sync(0xffffffffu, okl, 0);
-    __syncwarp();
-    return okl != 0;
-  }
-};
-
-// One arrival per warp on a barrier initialised with the element-wise warp count.
-__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
-  __syncwarp();
-  if (lane == 0) mbar_arrive(bar);
 }
 
 // Copy row r, elements [cg*D/4, (cg+1)*D/4) of a swizzled [128][D] bf16 shared tile into TMEM as packed
@@ -512,27 +521,6 @@ __device__ __forceinline__ void q_block_math(const uint32_t (&sv)[32], const uin
       ds.y = (e + 1 < hi) ? ds.y : 0.f;
     }
     dk[e / 2] = pack_bf16(ds.x, ds.y);
-  }
-}
-
-// bf16 store of `n` (a multiple of 16) fp32 TMEM columns (times mul) of this thread's lane to dst.
-__device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, int n, float mul, bool valid,
-                                                 __nv_bfloat16* dst) {
-  for (int c0 = 0; c0 < n; c0 += 16) {
-    uint32_t o[16];
-    tmem_ld_32x32b_x16(taddr + c0, o);
-    tmem_ld_wait();
-    if (valid) {
-#pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        uint4 w;
-        w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * mul, __uint_as_float(o[8 * v + 1]) * mul);
-        w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * mul, __uint_as_float(o[8 * v + 3]) * mul);
-        w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * mul, __uint_as_float(o[8 * v + 5]) * mul);
-        w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * mul, __uint_as_float(o[8 * v + 7]) * mul);
-        *reinterpret_cast<uint4*>(dst + c0 + 8 * v) = w;
-      }
-    }
   }
 }
 
