@@ -29,6 +29,39 @@
 #include <cudaTypedefs.h>
 #include <mutex>
 
+// Optional event trace (build with -DDT_ATTN_TRACE): SM clock of each pipeline event of one CTA,
+// slot = event * 64 + iteration, read back by a profiling harness.
+#ifdef DT_ATTN_TRACE
+__device__ unsigned long long g_attn_trace[8 * 64];
+__device__ int g_attn_trace_block;
+__device__ unsigned long long g_cta_trace[4 * 65536];  // per CTA: start ns, setup-done ns, end ns, SM id
+__device__ __forceinline__ void cta_trace(int slot) {
+  if (threadIdx.x == 0 && blockIdx.x < 65536) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_cta_trace[blockIdx.x * 4 + slot] = t;
+    if (slot == 2) {
+      unsigned sm;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+      g_cta_trace[blockIdx.x * 4 + 3] = sm;
+    }
+  }
+}
+#define CTA_TRACE(slot) cta_trace(slot)
+#define ATTN_TRACE(ev, it)                                  \
+  do {                                                      \
+    if ((int)blockIdx.x == g_attn_trace_block && (it) < 64) \
+      g_attn_trace[(ev) * 64 + (it)] = clock64();           \
+  } while (0)
+#else
+#define ATTN_TRACE(ev, it) \
+  do {                     \
+  } while (0)
+#define CTA_TRACE(slot) \
+  do {                  \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int BQ = 128, BKV = 128;
@@ -116,6 +149,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
                    float* __restrict__ lse, int B, int T, int nh, int nkv, float scale) {
   using C = FCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  CTA_TRACE(0);
   if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA; nothing allocated yet
     if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 499);
     return;
@@ -168,6 +202,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + C::C_O, tP = tmem + C::C_P;
+  CTA_TRACE(1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -204,6 +239,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) umma_bf16(tS, dQ0 + koff(k), kk + koff(k), idS, k > 0 ? 1u : 0u);
         umma_commit(s_full);
+        ATTN_TRACE(0, j);
         issued = true;
         return true;
       };
@@ -218,6 +254,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
           }
         }
         if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) { ok = false; break; }
+        ATTN_TRACE(1, j);
         tc_fence_after();
         const uint64_t vv = mV0 + (uint64_t)st * STG;
 #pragma unroll
@@ -244,6 +281,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       if (!wwait(s_full, j & 1, 420)) { ok = false; break; }
+      if (warp == 2 && lane == 0) ATTN_TRACE(2, j);
       tc_fence_after();
       uint32_t sv[64];
       tmem_ld_32x32b_x32(tS + lane_off + cg * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -269,6 +307,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
       warp_arrive(&xch[quad * 3 + (j & 1)], lane);
       if (!wwait(&xch[quad * 3 + (j & 1)], (j >> 1) & 1, 423)) { ok = false; break; }
       mx = fmaxf(mx, mbuf[(cg ^ 1) * 128 + r]);
+      if (warp == 2 && lane == 0) ATTN_TRACE(3, j);
       const float m_new = mx * sl2;  // -inf when the row has no valid key yet
       // stale-max policy: raise the reference max only when it grows by more than the threshold
       float m_use = m_run;
@@ -296,8 +335,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
       const float2 rs = f2_unpack(rs2);
       l_part = l_part * alpha + (rs.x + rs.y);
       m_run = m_use;
+      if (warp == 2 && lane == 0) ATTN_TRACE(4, j);
       // P and O are busy until the previous P V has completed
       if (j > 0 && !wwait(pv_done, (j - 1) & 1, 421)) { ok = false; break; }
+      if (warp == 2 && lane == 0) ATTN_TRACE(5, j);
       tc_fence_after();
       if (__any_sync(0xffffffffu, resc)) tmem_row_scale(tO + lane_off + cg * (D / 2), D / 2, alpha);
       tmem_st_32x32b_x16(tP + lane_off + cg * 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
@@ -305,6 +346,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
       tmem_st_wait();
       tc_fence_before();
       warp_arrive(p_full, lane);
+      if (warp == 2 && lane == 0) ATTN_TRACE(6, j);
     }
     // epilogue: O / l -> bf16 rows of `out` (this half's D/2 columns), lse
     if (ok && wwait(pv_done, (nkb - 1) & 1, 422)) {
@@ -326,6 +368,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+  CTA_TRACE(2);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
@@ -397,21 +440,6 @@ DT_API int dt_attn_fwd_tc(const void* qkv, void* out, float* lse, int B, int T, 
 // Tiles arrive by TMA in the 128-byte-swizzled [64-column chunk][rows][128 B] layout; the same bytes
 // serve as the K-major operand of one product and the MN-major operand of the other (Q, dO, K).
 
-// Optional event trace (build with -DDT_ATTN_TRACE): SM clock of each pipeline event of one CTA,
-// slot = event * 64 + iteration, read back by a profiling harness.
-#ifdef DT_ATTN_TRACE
-__device__ unsigned long long g_attn_trace[8 * 64];
-__device__ int g_attn_trace_block;
-#define ATTN_TRACE(ev, it)                                  \
-  do {                                                      \
-    if ((int)blockIdx.x == g_attn_trace_block && (it) < 64) \
-      g_attn_trace[(ev) * 64 + (it)] = clock64();           \
-  } while (0)
-#else
-#define ATTN_TRACE(ev, it) \
-  do {                     \
-  } while (0)
-#endif
 
 namespace {
 

@@ -1,6 +1,11 @@
 """Kernel microbenchmarks: CUDA-event timing of the hot sm_100a kernels on the tiny/small preset shapes.
 
-    python -m distrain_b200.bench_kernels [--only gemm|attn|norm|compress|merge|all] [--iters N] [--json]
+    python -m distrain_b200.bench_kernels [--only gemm|attn|norm|compress|merge|all] [--case SUBSTR] [--iters N]
+                                          [--warmup W] [--json]
+
+``--case`` keeps only the cases whose name contains SUBSTR (e.g. ``gate_up_fwd``, ``attn_fwd_d64``,
+``rmsnorm_bwd``, ``compress_10``, ``merge_10``); with ``--iters 1 --warmup 1`` a case launches its kernel twice, which
+is what a single-launch profiler capture wants.
 
 Each case runs warm-up launches, then ``iters`` launches between two events on the launching stream
 (synchronised on both sides); inputs are resized so every case reads more than the 126 MB L2, or the
@@ -29,7 +34,16 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
-def time_it(fn, iters=20, warmup=3):
+_CASE = None
+_WARMUP = 3
+
+
+def want(name: str) -> bool:
+    return _CASE is None or _CASE in name
+
+
+def time_it(fn, iters=20, warmup=None):
+    warmup = _WARMUP if warmup is None else min(warmup, _WARMUP)
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -56,6 +70,8 @@ def gemm_cases(iters):
         ("lm_head_dgrad_chunk", 8192, 768, 32768, 0, 1, 0), ("square_8192", 8192, 8192, 8192, 0, 0, 0),
     ]
     for name, m, n, k, a_mn, b_mn, epi in shapes:
+        if not want(name):
+            continue
         A = torch.randn(k if a_mn else m, m if a_mn else k, device="cuda").bfloat16()
         B = torch.randn(k if b_mn else n, n if b_mn else k, device="cuda").bfloat16()
         C = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16 if epi == 0 else torch.float32)
@@ -73,6 +89,9 @@ def attn_cases(iters):
     pk = peaks()
     out = []
     for (B, T, nh, nkv, d) in [(32, 1023, 12, 4, 64), (8, 2047, 16, 4, 128)]:
+        do_f, do_b = want(f"attn_fwd_d{d}"), want(f"attn_bwd_d{d}")
+        if not (do_f or do_b):
+            continue
         W = (nh + 2 * nkv) * d
         qkv = torch.randn(B * T, W, device="cuda").bfloat16()
         o = torch.empty(B * T, nh * d, device="cuda", dtype=torch.bfloat16)
@@ -82,9 +101,13 @@ def attn_cases(iters):
         dqa = torch.empty(B * T, nh * d, device="cuda")
         de = torch.empty(B, nh, A.lse_stride(T), device="cuda")
         fl = 4.0 * B * nh * T * T * d / 2  # causal
-        ms_f = time_it(lambda: A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)
-        ms_b = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d), iters)
+        A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d)  # valid LSE for the backward
+        ms_f = time_it(lambda: A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d), iters) if do_f else None
+        ms_b = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d),
+                       iters) if do_b else None
         for nm, ms, f in (("fwd", ms_f, fl), ("bwd", ms_b, 2.5 * fl)):
+            if ms is None:
+                continue
             tf = f / (ms * 1e-3) / 1e12
             out.append({"kernel": f"attn_{nm}", "case": f"B{B} T{T} h{nh}/{nkv} d{d}", "ms": round(ms, 4),
                         "tflops": round(tf, 1), f"frac_of_{pk['src']}_bf16": round(tf / pk["bf16_tflops"], 3)})
@@ -101,10 +124,17 @@ def norm_cases(iters):
     r = torch.empty(M, H, device="cuda")
     y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
     rs = torch.empty(M, device="cuda")
-    ms = time_it(lambda: ops.add_rmsnorm_fwd(x=x, br=br, w=w, out_resid=r, y=y, rstd=rs, eps=1e-5, M=M, H=H), iters)
-    byt = M * H * (4 + 2 + 4 + 2)
-    out = [{"kernel": "add_rmsnorm_fwd", "case": f"{M}x{H}", "ms": round(ms, 4), "gbs": round(byt / ms / 1e6, 1),
-            f"frac_of_{pk['src']}_hbm": round(byt / ms / 1e6 / pk["hbm_gbs"], 3)}]
+    out = []
+    if want("add_rmsnorm_fwd") or want("rmsnorm_bwd"):
+        ms = time_it(lambda: ops.add_rmsnorm_fwd(x=x, br=br, w=w, out_resid=r, y=y, rstd=rs, eps=1e-5, M=M, H=H),
+                     iters)
+        byt = M * H * (4 + 2 + 4 + 2)
+        if want("add_rmsnorm_fwd"):
+            out.append({"kernel": "add_rmsnorm_fwd", "case": f"{M}x{H}", "ms": round(ms, 4),
+                        "gbs": round(byt / ms / 1e6, 1),
+                        f"frac_of_{pk['src']}_hbm": round(byt / ms / 1e6 / pk["hbm_gbs"], 3)})
+    if not want("rmsnorm_bwd"):
+        return out
     dres = torch.zeros(M, H, device="cuda")
     d16 = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
     dw = torch.zeros(H, device="cuda")
@@ -123,6 +153,8 @@ def compress_cases(iters):
     pk = peaks()
     out = []
     for name, k in (("tiny", 0.01), ("tiny", 0.10), ("tiny", 0.99)):
+        if not want(f"compress_{round(k * 100)}"):
+            continue
         L = ParamLayout(preset(name))
         comp = DeviceCompressor(L, torch.device("cuda"), CompressionConfig(top_k_fraction=k, int8_block=256))
         master = torch.randn(L.total, device="cuda") * 1e-2
@@ -133,12 +165,60 @@ def compress_cases(iters):
     return out
 
 
+def merge_cases(iters):
+    """Coordinator merge of 8 compressed deltas of the tiny model held in this GPU's memory (the same
+    kernels read peer memory in the multi-GPU run): prepass (validation norms) + weighted dequant
+    scatter-add + apply with fp32 / bf16 writes to one destination's staging buffers. Reported per
+    merge, including the host round trip of the prepass."""
+    from distrain_b200.config import preset, CompressionConfig
+    from distrain_b200.models.params import ParamLayout
+    from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
+    from distrain_b200.parallel.merge import DeviceMerger, Contribution
+    out = []
+    L = ParamLayout(preset("tiny"))
+    dev = torch.device("cuda")
+    for k in (0.01, 0.10, 0.99):
+        if not want(f"merge_{round(k * 100)}"):
+            continue
+        comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=k, int8_block=256))
+        master = torch.randn(L.total, device=dev) * 1e-2
+        pays, contribs = [], []
+        for i in range(8):
+            comp.reset(master)
+            comp.begin(master - torch.randn_like(master) * 1e-4)
+            p = DevicePayload.allocate(comp.capacity, 256, dev)
+            comp.finish(payload=p)
+            torch.cuda.synchronize()
+            cnt = int(comp.stats_host[comp.nseg * 6].item())
+            pays.append(p)
+            contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                         scales_ptr=p.scales.data_ptr(), count=cnt, block=256, dense=False,
+                                         weight=1000.0 * (i + 1), wire_bytes=cnt * 5 + (cnt + 255) // 256 * 4))
+        m = DeviceMerger(L.total, dev, master)
+        s32 = torch.empty(L.total, device=dev)  # one destination node's staging buffers (fp32 master, bf16)
+        s16 = torch.empty(L.total, device=dev, dtype=torch.bfloat16)
+
+        def run():
+            m.merge(contribs, 1.0, 0.0, stage32=[s32.data_ptr()], stage16=[s16.data_ptr()])
+            m.stream.synchronize()
+        ms = time_it(run, iters, warmup=2)
+        wire = sum(c.wire_bytes for c in contribs)
+        out.append({"kernel": "merge_pipeline", "case": f"8 x tiny {L.num_params() / 1e6:.0f}M top-k {k:.0%}",
+                    "ms": round(ms, 3), "payload_mb": round(wire / 1e6, 1)})
+        del comp, m, pays, s32, s16
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="all")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--case", default=None)
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args()
+    global _CASE, _WARMUP
+    _CASE, _WARMUP = a.case, a.warmup
     sys.path.insert(0, ROOT)
     res = []
     sel = a.only.split(",")
@@ -150,6 +230,8 @@ def main():
         res += norm_cases(a.iters)
     if "all" in sel or "compress" in sel:
         res += compress_cases(a.iters)
+    if "all" in sel or "merge" in sel:
+        res += merge_cases(a.iters)
     from distrain_b200 import ops
     code, site = ops.device_error()
     for r in res:
