@@ -23,6 +23,7 @@ namespace {
 constexpr int NB1 = 4096, NB2 = 4096, NB3 = 128;
 constexpr int SH1 = 19, SH2 = 7;
 constexpr int TPB = 256;
+constexpr int UNR = 4;  // elements per thread per loop iteration in the streaming passes
 
 struct SegState {
   double sumsq;      // sum of d^2 over the segment
@@ -33,11 +34,51 @@ struct SegState {
   long long krem;    // elements still to take inside the current prefix bin
   unsigned tau;      // threshold key
   long long take_eq; // elements with key == tau to keep (by index order)
+  long long eq_base; // scan scratch: global count of key == tau entries before the segment's first chunk
   float maxabs;
   int nonfinite;
 };
 
 __device__ __forceinline__ unsigned keyof(float v) { return __float_as_uint(v) & 0x7fffffffu; }
+
+// Histogram increment aggregated over the warp: lanes that hit the same bin are counted by one atomic.
+// Deltas of one tensor have similar magnitudes and crowd into a few bins, where per-lane shared atomics
+// would serialise 32-fold. Every lane of the warp must call it (inactive lanes with valid = false).
+__device__ __forceinline__ void hist_add_warp(unsigned* h, unsigned bin, bool valid) {
+  const unsigned key = valid ? bin : 0xffffffffu;
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  if (valid && (threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&h[bin], (unsigned)__popc(peers));
+}
+
+// Exclusive block scan of two counters (blockDim.x a multiple of 32, <= 1024); returns the block totals.
+__device__ __forceinline__ void block_scan2(long long a, long long b, long long& ea, long long& eb, long long& ta,
+                                            long long& tb, long long* sh /* [2][33] */) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  long long ia = a, ib = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long xa = __shfl_up_sync(0xffffffffu, ia, o), xb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) { ia += xa; ib += xb; }
+  }
+  if (lane == 31) { sh[wid] = ia; sh[33 + wid] = ib; }
+  __syncthreads();
+  if (wid == 0) {
+    long long va = lane < nw ? sh[lane] : 0, vb = lane < nw ? sh[33 + lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long xa = __shfl_up_sync(0xffffffffu, va, o), xb = __shfl_up_sync(0xffffffffu, vb, o);
+      if (lane >= o) { va += xa; vb += xb; }
+    }
+    if (lane < nw) { sh[lane] = va; sh[33 + lane] = vb; }  // inclusive warp prefixes
+  }
+  __syncthreads();
+  const long long wa = wid ? sh[wid - 1] : 0, wb = wid ? sh[33 + wid - 1] : 0;
+  ea = wa + ia - a;
+  eb = wb + ib - b;
+  ta = sh[nw - 1];
+  tb = sh[33 + nw - 1];
+  __syncthreads();  // sh may be reused by the caller's next scan
+}
 
 // Pass A: combined delta, snapshot refresh, per-segment stats, level-1 histogram.
 __global__ void pass_a_kernel(const float* __restrict__ master, float* __restrict__ snap, float* __restrict__ ef,
@@ -51,15 +92,32 @@ __global__ void pass_a_kernel(const float* __restrict__ master, float* __restric
   const int c = blockIdx.x, s = cseg[c];
   float ss = 0.f, mx = 0.f;
   int nf = 0;
-  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
-    float m = master[i];
-    float d = snap[i] - m + (use_ef ? ef[i] : 0.f);
-    snap[i] = m;
-    ef[i] = d;
-    if (!isfinite(d)) nf = 1;
-    ss += d * d;
-    mx = fmaxf(mx, fabsf(d));
-    atomicAdd(&h[keyof(d) >> SH1], 1u);
+  const long long e = cend[c];
+  // UNR elements per thread per iteration, all loads issued before any use (memory-level parallelism)
+  for (long long i0 = cstart[c]; i0 < e; i0 += (long long)blockDim.x * UNR) {
+    float m[UNR], sv[UNR], ev[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const long long i = i0 + u * blockDim.x + threadIdx.x;
+      const bool valid = i < e;
+      m[u] = valid ? master[i] : 0.f;
+      sv[u] = valid ? snap[i] : 0.f;
+      ev[u] = (valid && use_ef) ? ef[i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const long long i = i0 + u * blockDim.x + threadIdx.x;
+      const bool valid = i < e;
+      const float d = sv[u] - m[u] + ev[u];
+      if (valid) {
+        snap[i] = m[u];
+        ef[i] = d;
+        if (!isfinite(d)) nf = 1;
+        ss += d * d;
+        mx = fmaxf(mx, fabsf(d));
+      }
+      hist_add_warp(h, keyof(d) >> SH1, valid);
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < NB1; i += blockDim.x)
@@ -163,11 +221,19 @@ __global__ void hist_level_kernel(const float* __restrict__ ef, const int* __res
   const int c = blockIdx.x, s = cseg[c];
   const unsigned pre = seg[s].prefix;
   bool any = false;
-  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
-    unsigned k = keyof(ef[i]);
-    if ((k >> SHIFT_MATCH) == pre) {
-      atomicAdd(&h[(k >> SHIFT_BIN) & (NB - 1)], 1u);
-      any = true;
+  const long long e = cend[c];
+  for (long long i0 = cstart[c]; i0 < e; i0 += (long long)blockDim.x * UNR) {
+    unsigned k[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const long long i = i0 + u * blockDim.x + threadIdx.x;
+      k[u] = i < e ? keyof(ef[i]) : 0xffffffffu;  // never matches a prefix (bit 31 set)
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const bool hit = (k[u] >> SHIFT_MATCH) == pre;
+      any |= hit;
+      if (__any_sync(0xffffffffu, hit)) hist_add_warp(h, (k[u] >> SHIFT_BIN) & (NB - 1), hit);
     }
   }
   any = __syncthreads_or(any);
@@ -183,10 +249,20 @@ __global__ void count_kernel(const float* __restrict__ ef, const int* __restrict
   const int c = blockIdx.x, s = cseg[c];
   const unsigned tau = seg[s].tau;
   unsigned gt = 0, eq = 0;
-  for (long long i = cstart[c] + threadIdx.x; i < cend[c]; i += blockDim.x) {
-    unsigned k = keyof(ef[i]);
-    gt += (k > tau);
-    eq += (k == tau);
+  const long long e = cend[c];
+  for (long long i0 = cstart[c]; i0 < e; i0 += (long long)blockDim.x * UNR) {
+    unsigned k[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const long long i = i0 + u * blockDim.x + threadIdx.x;
+      k[u] = i < e ? keyof(ef[i]) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const long long i = i0 + u * blockDim.x + threadIdx.x;
+      gt += (i < e) && (k[u] > tau);
+      eq += (i < e) && (k[u] == tau);
+    }
   }
   __shared__ unsigned a[32], b[32];
   for (int o = 16; o > 0; o >>= 1) {
@@ -203,80 +279,97 @@ __global__ void count_kernel(const float* __restrict__ ef, const int* __restrict
   }
 }
 
-// Single block: eq quota per chunk (in index order within each segment) and global output offsets.
-__global__ void scan_kernel(const int* __restrict__ cseg, int nchunks, const SegState* seg,
-                            const long long* __restrict__ cnt_gt, const long long* __restrict__ cnt_eq,
-                            long long* __restrict__ eq_take, long long* __restrict__ out_off,
-                            long long* __restrict__ total) {
-  if (threadIdx.x != 0) return;
-  long long off = 0, eq_seen = 0;
-  int cur = -1;
-  for (int c = 0; c < nchunks; ++c) {
-    int s = cseg[c];
-    if (s != cur) { cur = s; eq_seen = 0; }
-    long long quota = seg[s].take_eq - eq_seen;
-    if (quota < 0) quota = 0;
-    long long te = cnt_eq[c] < quota ? cnt_eq[c] : quota;
-    eq_seen += cnt_eq[c];
-    eq_take[c] = te;
-    out_off[c] = off;
-    off += cnt_gt[c] + te;
+// Single block (1024 threads, each owning a contiguous run of chunks): eq quota per chunk (ties taken in
+// index order within each segment) and global output offsets, as two block scans.
+__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ cseg, int nchunks, SegState* seg,
+                                                    const long long* __restrict__ cnt_gt,
+                                                    const long long* __restrict__ cnt_eq,
+                                                    long long* __restrict__ eq_take, long long* __restrict__ out_off,
+                                                    long long* __restrict__ total) {
+  __shared__ long long sh[66];
+  const int per = (nchunks + blockDim.x - 1) / blockDim.x;
+  const int c0 = min((int)threadIdx.x * per, nchunks), c1 = min(c0 + per, nchunks);
+  // 1) global exclusive prefix of the eq counts; the prefix at a segment's first chunk is its base
+  long long eqs = 0;
+  for (int c = c0; c < c1; ++c) eqs += cnt_eq[c];
+  long long ex, dummy, tot_eq, tot_dummy;
+  block_scan2(eqs, 0, ex, dummy, tot_eq, tot_dummy, sh);
+  for (int c = c0; c < c1; ++c) {
+    eq_take[c] = ex;  // eq entries of all chunks before c (temporary)
+    if (c == 0 || cseg[c - 1] != cseg[c]) seg[cseg[c]].eq_base = ex;
+    ex += cnt_eq[c];
   }
-  *total = off;
+  __syncthreads();
+  // 2) eq entries this chunk may take, then the global exclusive prefix of kept entries
+  long long kept = 0;
+  for (int c = c0; c < c1; ++c) {
+    const int s = cseg[c];
+    long long q = seg[s].take_eq - (eq_take[c] - seg[s].eq_base);
+    q = q < 0 ? 0 : (q > cnt_eq[c] ? cnt_eq[c] : q);
+    eq_take[c] = q;
+    kept += cnt_gt[c] + q;
+  }
+  long long off, tot;
+  block_scan2(kept, 0, off, dummy, tot, tot_dummy, sh);
+  for (int c = c0; c < c1; ++c) {
+    out_off[c] = off;
+    off += cnt_gt[c] + eq_take[c];
+  }
+  if (threadIdx.x == 0) *total = tot;
 }
 
 // Ordered compaction: writes (index, value) of kept entries in ascending index order, zeroes them in ef.
+// Each thread owns CR consecutive elements per round; one block scan of (keys > tau, keys == tau) counts
+// per round gives every thread its output position and its share of the chunk's eq quota.
+constexpr int CR = 16;
 __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ cseg,
                                const long long* __restrict__ cstart, const long long* __restrict__ cend,
                                SegState* seg, const long long* __restrict__ eq_take,
                                const long long* __restrict__ out_off, int* __restrict__ out_idx,
                                float* __restrict__ out_val) {
-  __shared__ unsigned wsum_sel[TPB / 32], wsum_eq[TPB / 32];
-  __shared__ long long base_sel, base_eq;
+  __shared__ long long sh[66];
   __shared__ float shs[32];
   const int c = blockIdx.x, s = cseg[c];
   const unsigned tau = seg[s].tau;
   const long long quota = eq_take[c];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (threadIdx.x == 0) { base_sel = out_off[c]; base_eq = 0; }
-  __syncthreads();
+  const long long e = cend[c];
+  long long base_sel = out_off[c], eq_seen = 0;
   float kept_sq = 0.f;
-  for (long long i0 = cstart[c]; i0 < cend[c]; i0 += blockDim.x) {
-    long long i = i0 + threadIdx.x;
-    bool valid = i < cend[c];
-    float d = valid ? ef[i] : 0.f;
-    unsigned k = keyof(d);
-    bool is_eq = valid && (k == tau);
-    bool is_gt = valid && (k > tau);
-    // rank among eq in this iteration
-    unsigned beq = __ballot_sync(0xffffffffu, is_eq);
-    unsigned eq_before_w = __popc(beq & ((1u << lane) - 1));
-    if (lane == 0) wsum_eq[wid] = __popc(beq);
-    __syncthreads();
-    unsigned eq_before = eq_before_w;
-    for (int w = 0; w < wid; ++w) eq_before += wsum_eq[w];
-    bool take = is_gt || (is_eq && (base_eq + eq_before) < quota);
-    unsigned bsel = __ballot_sync(0xffffffffu, take);
-    unsigned sel_before_w = __popc(bsel & ((1u << lane) - 1));
-    if (lane == 0) wsum_sel[wid] = __popc(bsel);
-    __syncthreads();
-    unsigned sel_before = sel_before_w;
-    unsigned tot_sel = 0, tot_eq = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-      if (w < wid) sel_before += wsum_sel[w];
-      tot_sel += wsum_sel[w];
-      tot_eq += wsum_eq[w];
+  for (long long r0 = cstart[c]; r0 < e; r0 += (long long)blockDim.x * CR) {
+    const long long i0 = r0 + (long long)threadIdx.x * CR;
+    float v[CR];
+    unsigned gtm = 0, eqm = 0;
+#pragma unroll
+    for (int j = 0; j < CR; ++j) {
+      const long long i = i0 + j;
+      v[j] = i < e ? ef[i] : 0.f;
+      const unsigned k = keyof(v[j]);
+      if (i < e && k > tau) gtm |= 1u << j;
+      if (i < e && k == tau) eqm |= 1u << j;
     }
-    if (take) {
-      long long pos = base_sel + sel_before;
-      out_idx[pos] = (int)i;
-      out_val[pos] = d;
-      ef[i] = 0.f;
-      kept_sq += d * d;
+    long long gpre, epre, gtot, etot;
+    block_scan2(__popc(gtm), __popc(eqm), gpre, epre, gtot, etot, sh);
+    const long long qrem = quota - eq_seen;  // ties this chunk may still take, in index order
+    const long long eq_before = qrem <= 0 ? 0 : (epre < qrem ? epre : qrem);
+    long long allow = qrem - epre;
+    long long pos = base_sel + gpre + eq_before;
+#pragma unroll
+    for (int j = 0; j < CR; ++j) {
+      bool take = (gtm >> j) & 1u;
+      if (((eqm >> j) & 1u) && allow > 0) {
+        take = true;
+        --allow;
+      }
+      if (take) {
+        out_idx[pos] = (int)(i0 + j);
+        out_val[pos] = v[j];
+        ef[i0 + j] = 0.f;
+        kept_sq += v[j] * v[j];
+        ++pos;
+      }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) { base_sel += tot_sel; base_eq += tot_eq; }
-    __syncthreads();
+    base_sel += gtot + (qrem <= 0 ? 0 : (etot < qrem ? etot : qrem));
+    eq_seen += etot;
   }
   float t = block_sum(kept_sq, shs);
   if (threadIdx.x == 0) atomicAdd(&seg[s].kept_sq, (double)t);
@@ -395,7 +488,7 @@ DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstar
   hist_level_kernel<NB3, SH2, 0><<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.h3);
   select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h3, NB3, 7, 1);
   count_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.gt, w.eq);
-  scan_kernel<<<1, 32, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
+  scan_kernel<<<1, 1024, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
   compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val);
   if (quant_block > 0 && out_q) {
     long long nblk = (capacity + quant_block - 1) / quant_block;

@@ -27,6 +27,8 @@ struct Contrib {
   int pad;
 };
 
+constexpr int MUNR = 4;
+
 __device__ __forceinline__ float contrib_value(const Contrib& c, long long i) {
   if (c.q) return (float)__ldg(c.q + i) * __ldg(c.scales + i / c.block);
   return __ldg(c.val + i);
@@ -39,12 +41,21 @@ __global__ void prepass_kernel(const Contrib* __restrict__ cs, int n, double* __
   const Contrib C = cs[c];
   float ss = 0.f, mx = 0.f;
   int nf = 0;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < C.count;
-       i += (long long)gridDim.x * blockDim.x) {
-    float v = contrib_value(C, i);
-    if (!isfinite(v)) { nf = 1; continue; }
-    ss += v * v;
-    mx = fmaxf(mx, fabsf(v));
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  // MUNR independent elements per thread per iteration: all loads in flight before any use
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < C.count; i0 += stride * MUNR) {
+    float v[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      v[u] = i < C.count ? contrib_value(C, i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      if (!isfinite(v[u])) { nf = 1; continue; }
+      ss += v[u] * v[u];
+      mx = fmaxf(mx, fabsf(v[u]));
+    }
   }
   float t = block_sum(ss, shs);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -72,9 +83,19 @@ __global__ void accumulate_kernel(const Contrib* __restrict__ cs, int n, float* 
       atomicAdd(acc + i, __ldg(C.val + i) * C.coef);
     return;
   }
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < C.count; i += (long long)gridDim.x * blockDim.x) {
-    int j = __ldg(C.idx + i);
-    atomicAdd(acc + j, contrib_value(C, i) * C.coef);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < C.count; i0 += stride * MUNR) {
+    int j[MUNR];
+    float v[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      j[u] = i < C.count ? __ldg(C.idx + i) : -1;
+      v[u] = i < C.count ? contrib_value(C, i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u)
+      if (j[u] >= 0) atomicAdd(acc + j[u], v[u] * C.coef);
   }
 }
 
