@@ -39,6 +39,9 @@ def _parse():
     ap.add_argument("--push-every", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-push", action="store_true", help="train only (no compression / merge)")
+    ap.add_argument("--sync", default="inbox", choices=["inbox", "nccl"],
+                    help="inbox: compressed deltas, peer-pull merge kernel, NVLS broadcast (the product); "
+                         "nccl: comparison arm, dense fp32 delta all-reduce every push")
     return ap.parse_args()
 
 
@@ -123,7 +126,11 @@ def main():
     run = bench_config(args.config)
     if args.push_every:
         run.push_every = args.push_every
-    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=not args.no_push)
+    nccl_arm = args.sync == "nccl" and not args.no_push
+    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=not args.no_push and not nccl_arm)
+    if nccl_arm:
+        from distrain_b200.parallel.nccl_baseline import NcclDenseSync
+        node.sync = NcclDenseSync(node, run, rank, world, dev)
     B, S = run.micro_batch, run.seq_len
 
     # synthetic uniform-random tokens, per-rank seed, pinned ring of host batches
@@ -179,7 +186,10 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms_max, launches = t[0].item(), t[1].item(), int(t[2].item())
-    merges = list(node.sync.coord.merges) if (node.sync is not None and node.sync.coord is not None) else []
+    if nccl_arm:
+        merges = node.sync.merges
+    else:
+        merges = list(node.sync.coord.merges) if (node.sync is not None and node.sync.coord is not None) else []
     versions = node.sync.version if node.sync is not None else 0
     node.close()
     tokens_per_step = B * S
@@ -199,10 +209,13 @@ def main():
             "dtype": "bf16",
             "data": "synthetic (uniform-random token ids, per-rank seeds; random-init N(0,0.02) weights)",
             "config": {"model": f"{run.name} preset ({run.model.param_count()/1e6:.1f}M params)",
-                       "global_batch": B * world, "seq_len": S, "parallelism": f"async-dp{world} (1 node per GPU)",
+                       "global_batch": B * world, "seq_len": S,
+                       "parallelism": (f"sync-dp{world} (NCCL all-reduce of dense fp32 deltas every push)"
+                                       if nccl_arm else f"async-dp{world} (1 node per GPU)"),
                        "push_every": run.push_every if not args.no_push else None,
-                       "compression": f"top-k {run.compression.top_k_fraction:.0%} + INT8 block "
-                                      f"{run.compression.int8_block} + error feedback",
+                       "compression": ("none (dense fp32 delta)" if nccl_arm else
+                                       f"top-k {run.compression.top_k_fraction:.0%} + INT8 block "
+                                       f"{run.compression.int8_block} + error feedback"),
                        "l2": "per-step working set (~12 GB) >> 126 MB L2; no flush"},
             "gpu_launches": launches,
             "clocks": clk,
@@ -215,6 +228,8 @@ def main():
                             "pulled_bytes_last": merges[-1]["pulled_bytes"],
                             "broadcast_bytes_last": merges[-1]["broadcast_bytes"],
                             "multicast": merges[-1]["multicast"]}
+            if nccl_arm:
+                out["merge"]["allreduce_bytes"] = merges[-1]["allreduce_bytes"]
         if e2e_ms is not None:
             out["e2e"] = {"value": round(tokens_per_step * world * args.steps / (e2e_ms_max / 1e3), 1),
                           "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 4}

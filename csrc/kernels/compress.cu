@@ -135,15 +135,26 @@ __global__ void pass_a_kernel(const float* __restrict__ master, float* __restric
 
 // Budget per segment (single block): adaptive (norm-proportional) or uniform, reference arithmetic.
 __global__ void budget_kernel(SegState* seg, int nseg, float k_fraction, int adaptive) {
+  // The norm total is summed in segment order by one thread (the reference's order, so k per tensor is
+  // bit-identical to it); the block only stages the square roots in shared memory.
+  __shared__ double buf[256];
   __shared__ double tot_norm, tot_len;
-  if (threadIdx.x == 0) {
-    double tn = 0, tl = 0;
-    for (int s = 0; s < nseg; ++s) {
-      tn += sqrt(seg[s].sumsq);
-      tl += (double)seg[s].len;
+  if (threadIdx.x == 0) { tot_norm = 0.0; tot_len = 0.0; }
+  for (int base = 0; base < nseg; base += 256) {
+    __syncthreads();
+    const int s = base + threadIdx.x;
+    if (threadIdx.x < 256 && s < nseg) buf[threadIdx.x] = sqrt(seg[s].sumsq);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int cnt = min(256, nseg - base);
+      double tn = tot_norm, tl = tot_len;
+      for (int i = 0; i < cnt; ++i) {
+        tn += buf[i];
+        tl += (double)seg[base + i].len;
+      }
+      tot_norm = tn;
+      tot_len = tl;
     }
-    tot_norm = tn;
-    tot_len = tl;
   }
   __syncthreads();
   const double total_budget = ceil(tot_len * (double)k_fraction);
@@ -165,42 +176,44 @@ __global__ void budget_kernel(SegState* seg, int nseg, float k_fraction, int ada
   }
 }
 
-// Resolve one radix level for every segment: find the bin containing the krem-th largest key.
-// One warp per segment.
-__global__ void select_level_kernel(SegState* seg, int nseg, const unsigned* __restrict__ hist, int nbins,
-                                    int bits, int last) {
-  const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+// Resolve one radix level for every segment: find the bin holding the krem-th largest key. One block per
+// segment; thread t owns PER consecutive bins counted from the top, all loaded at once, and a block scan
+// of the per-thread sums locates the crossing thread, which walks its own bins.
+template <int NB, int NT>
+__global__ void __launch_bounds__(NT) select_level_kernel(SegState* seg, int nseg, const unsigned* __restrict__ hist,
+                                                          int bits, int last) {
+  constexpr int PER = NB / NT;
+  __shared__ long long sh[66];
+  const int s = blockIdx.x;
   if (s >= nseg) return;
-  const unsigned* hs = hist + (long long)s * nbins;
-  long long need = seg[s].krem;
-  // walk bins from the top in chunks of 32
-  long long above = 0;
+  const unsigned* hs = hist + (long long)s * NB;
+  unsigned local[PER];
+  long long tsum = 0;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    local[u] = hs[NB - 1 - (threadIdx.x * PER + u)];
+    tsum += local[u];
+  }
+  long long above, dummy, total, tdummy;
+  block_scan2(tsum, 0, above, dummy, total, tdummy, sh);
+  const long long need = seg[s].krem;
   int found = -1;
   long long found_above = 0;
-  for (int base = nbins - 32; base >= 0 && found < 0; base -= 32) {
-    unsigned v = hs[base + lane];  // lane 31 = highest bin of this chunk
-    // inclusive suffix sum from the top within the chunk
-    unsigned suf = v;
-    for (int o = 1; o < 32; o <<= 1) {
-      unsigned t = __shfl_down_sync(0xffffffffu, suf, o);
-      if (lane + o < 32) suf += t;
+  if (above < need && need <= above + tsum) {
+    long long acc = above;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      if (found < 0 && acc + local[u] >= need) {
+        found = NB - 1 - (threadIdx.x * PER + u);
+        found_above = acc;
+      }
+      acc += local[u];
     }
-    long long incl = above + suf;          // elements with bin >= base+lane
-    long long excl = incl - v;             // elements with bin >  base+lane
-    unsigned hit = __ballot_sync(0xffffffffu, incl >= need && excl < need);
-    if (hit) {
-      int l = 31 - __clz(hit);             // highest lane satisfying (there is exactly one)
-      found = base + l;
-      found_above = __shfl_sync(0xffffffffu, excl, l);
-    }
-    above += __shfl_sync(0xffffffffu, suf, 0);
+  } else if (threadIdx.x == 0 && total < need) {  // need exceeds everything (cannot happen when k <= len)
+    found = 0;
+    found_above = 0;
   }
-  if (lane == 0) {
-    if (found < 0) {  // need exceeds everything (cannot happen when k <= len); take everything
-      found = 0;
-      found_above = 0;
-    }
+  if (found >= 0) {
     seg[s].prefix = (seg[s].prefix << bits) | (unsigned)found;
     seg[s].krem = need - found_above;
     if (last) {
@@ -480,13 +493,11 @@ DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstar
                               cudaStream_t st) {
   WsPtrs w = carve(ws, nseg, nchunks);
   budget_kernel<<<1, 256, 0, st>>>(w.seg, nseg, k_fraction, adaptive);
-  const int wpb = 8;
-  const int sblocks = (nseg + wpb - 1) / wpb;
-  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h1, NB1, 12, 0);
+  select_level_kernel<NB1, 256><<<nseg, 256, 0, st>>>(w.seg, nseg, w.h1, 12, 0);
   hist_level_kernel<NB2, SH1, SH2><<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.h2);
-  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h2, NB2, 12, 0);
+  select_level_kernel<NB2, 256><<<nseg, 256, 0, st>>>(w.seg, nseg, w.h2, 12, 0);
   hist_level_kernel<NB3, SH2, 0><<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.h3);
-  select_level_kernel<<<sblocks, 32 * wpb, 0, st>>>(w.seg, nseg, w.h3, NB3, 7, 1);
+  select_level_kernel<NB3, 128><<<nseg, 128, 0, st>>>(w.seg, nseg, w.h3, 7, 1);
   count_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.gt, w.eq);
   scan_kernel<<<1, 1024, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
   compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val);

@@ -12,6 +12,7 @@
 //              node's staging buffers: one multimem.st per 16 bytes through an NVLS multicast object
 //              (or one store per peer when no multicast object exists), then acc is cleared.
 #include "common.cuh"
+#include <cstring>
 
 namespace {
 
@@ -26,6 +27,14 @@ struct Contrib {
   float coef;                // weight / total * clip scale
   int pad;
 };
+static_assert(sizeof(Contrib) == 56, "Contrib layout is shared with the host packer");
+
+// The descriptor table travels as a kernel parameter (64 x 56 B < 4 KB): it is captured at launch, so no
+// device copy of it can be read before its upload has landed.
+constexpr int MAX_CONTRIB = 64;
+struct ContribTable {
+  Contrib c[MAX_CONTRIB];
+};
 
 constexpr int MUNR = 4;
 
@@ -34,11 +43,11 @@ __device__ __forceinline__ float contrib_value(const Contrib& c, long long i) {
   return __ldg(c.val + i);
 }
 
-__global__ void prepass_kernel(const Contrib* __restrict__ cs, int n, double* __restrict__ stats) {
+__global__ void prepass_kernel(const __grid_constant__ ContribTable cs, int n, double* __restrict__ stats) {
   // grid: (blocks per contribution, n); stats[c*3 + {sumsq, maxabs, nonfinite}]
   __shared__ float shs[32];
   const int c = blockIdx.y;
-  const Contrib C = cs[c];
+  const Contrib& C = cs.c[c];
   float ss = 0.f, mx = 0.f;
   int nf = 0;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -68,9 +77,9 @@ __global__ void prepass_kernel(const Contrib* __restrict__ cs, int n, double* __
   }
 }
 
-__global__ void accumulate_kernel(const Contrib* __restrict__ cs, int n, float* __restrict__ acc) {
+__global__ void accumulate_kernel(const __grid_constant__ ContribTable cs, int n, float* __restrict__ acc) {
   const int c = blockIdx.y;
-  const Contrib C = cs[c];
+  const Contrib& C = cs.c[c];
   if (C.coef == 0.f) return;
   if (C.dense) {
     const long long n4 = C.count / 4;
@@ -191,18 +200,25 @@ int grid_cap(long long work, int th, int cap) {
 DT_API long long dt_merge_contrib_bytes() { return (long long)sizeof(Contrib); }
 
 // contribs: device array of `n` Contrib descriptors (layout: see struct; sizeof from dt_merge_contrib_bytes).
+// `contribs`: HOST array of n packed Contrib records (n <= 64), copied into the launch parameters.
 DT_API int dt_merge_prepass(const void* contribs, int n, long long max_count, double* stats, cudaStream_t st) {
   if (n <= 0) return 0;
+  if (n > MAX_CONTRIB) return -13;
   DT_CUDA_RET(cudaMemsetAsync(stats, 0, sizeof(double) * 3 * n, st));
   dim3 grid(grid_cap(max_count, 256, 148 * 2), n);
-  prepass_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const Contrib*>(contribs), n, stats);
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  prepass_kernel<<<grid, 256, 0, st>>>(tab, n, stats);
   return (int)cudaGetLastError();
 }
 
 DT_API int dt_merge_accumulate(const void* contribs, int n, long long max_count, float* acc, cudaStream_t st) {
   if (n <= 0) return 0;
+  if (n > MAX_CONTRIB) return -13;
   dim3 grid(grid_cap(max_count, 256, 148 * 4), n);
-  accumulate_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const Contrib*>(contribs), n, acc);
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  accumulate_kernel<<<grid, 256, 0, st>>>(tab, n, acc);
   return (int)cudaGetLastError();
 }
 

@@ -1,0 +1,183 @@
+"""Merge microbenchmark on one NVSwitch box: N nodes' compressed deltas -> coordinator merge -> checkpoint
+broadcast, against an NCCL all-reduce of the same deltas in dense fp32.
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 --master-port P \\
+        -m distrain_b200.bench_merge [--models tiny,small] [--topk 0.01,0.1,0.99] [--iters 5] [--warmup 2]
+
+Per (model, top-k), every iteration:
+  1. every rank compresses a synthetic round delta (fixed random snapshot vs master, error feedback
+     cleared) into its symmetric (peer-mapped) payload buffer: pass A + radix top-k + ordered
+     compaction + INT8 block 256;
+  2. rank 0 (the coordinator) pulls all N payloads over NVLink with the merge kernels (prepass norms and
+     validation with its host round trip, weighted dequant scatter-add into fp32), applies the update and
+     writes the new checkpoint (fp32 master + bf16 copy) into every rank's staging buffer with NVLS
+     multimem stores (per-peer stores when the box offers no multicast object).
+Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, total = their
+sum (the steps are separated by barriers). Bytes over NVLink: payloads pulled from the N-1 peers plus the
+checkpoint stored through the multicast object (each GPU receives it once).
+Comparison arm per model: delta = snapshot - master, ncclAllReduce(AVG) of the n fp32 values, the same
+apply and bf16 cast on every rank; max over ranks. One JSON line per case on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _max_over_ranks(x: float, dev) -> float:
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, dev):
+    from .config import preset, CompressionConfig
+    from .models.params import ParamLayout
+    from .parallel.compression import DeviceCompressor, DevicePayload
+    from .parallel.merge import DeviceMerger, Contribution
+    from .parallel.inbox import _symm_alloc
+    from . import ops
+
+    L = ParamLayout(preset(name))
+    n = L.total
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    master = torch.randn(n, device=dev, generator=g) * 0.02
+    snap = master + torch.randn(n, device=dev, generator=g) * 1e-3
+    cap_max = DeviceCompressor.capacity_for(L, max(topks))
+    pay_bytes = (DevicePayload.nbytes(cap_max, 256) + 4095) // 4096 * 4096
+    pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes, dev, world)
+    stage_bytes = (n * 6 + 4095) // 4096 * 4096
+    stage_buf, stage_ptrs, stage_mc, _stage_h = _symm_alloc(stage_bytes, dev, world)
+    p32 = [p for p in stage_ptrs]
+    p16 = [p + n * 4 for p in stage_ptrs]
+    mc32 = stage_mc or 0
+    mc16 = (stage_mc + n * 4) if stage_mc else 0
+    merger = DeviceMerger(n, dev, snap, momentum=0.0) if rank == 0 else None
+    results = []
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for k in topks:
+        cap = DeviceCompressor.capacity_for(L, k)
+        payload = DevicePayload(pay_buf[:DevicePayload.nbytes(cap, 256)], cap, 256)
+        comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=k, int8_block=256), payload=payload)
+        t_comp, t_merge, pulled, infos = [], [], 0, None
+        for it in range(warmup + iters):
+            comp.snap.copy_(snap)
+            comp.ef.zero_()
+            torch.cuda.synchronize()
+            barrier()
+            c0, c1 = _events()
+            c0.record()
+            comp.begin(master)
+            comp.finish()
+            c1.record()
+            torch.cuda.synchronize()
+            cnt = torch.tensor([int(comp.stats_host[comp.nseg * 6].item())], device=dev, dtype=torch.int64)
+            counts = [torch.zeros_like(cnt) for _ in range(world)]
+            if world > 1:
+                dist.all_gather(counts, cnt)
+            else:
+                counts = [cnt]
+            counts = [int(c.item()) for c in counts]
+            barrier()
+            mms = 0.0
+            if rank == 0:
+                base = pay_buf.data_ptr()
+                contribs = []
+                for r in range(world):
+                    off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
+                    contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q),
+                                                 val_ptr=off(payload.val), scales_ptr=off(payload.scales),
+                                                 count=counts[r], block=256, dense=False, weight=1.0,
+                                                 node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
+                m0, m1 = _events()
+                m0.record(merger.stream)
+                infos = merger.merge(contribs, 1.0, 0.0, mc32=mc32, mc16=mc16, stage32=p32, stage16=p16)
+                m1.record(merger.stream)
+                merger.stream.synchronize()
+                mms = m0.elapsed_time(m1)
+                pulled = sum(c.wire_bytes for c in contribs[1:])
+            barrier()
+            if it >= warmup:
+                t_comp.append(c0.elapsed_time(c1))
+                t_merge.append(mms)
+        cms = _max_over_ranks(sorted(t_comp)[len(t_comp) // 2], dev)
+        mms = _max_over_ranks(sorted(t_merge)[len(t_merge) // 2], dev)
+        if rank == 0:
+            results.append({"bench": "compress_merge_broadcast", "model": name, "params": L.num_params(),
+                            "n_nodes": world, "top_k": k, "compress_ms": round(cms, 3), "merge_ms": round(mms, 3),
+                            "total_ms": round(cms + mms, 3), "accepted": infos["accepted"],
+                            "payload_bytes_pulled_nvlink": pulled,
+                            "checkpoint_bytes_broadcast": n * 6, "broadcast": "nvls multimem" if mc32 else "per-peer",
+                            "timing": "CUDA events, median of iters, max over ranks"})
+        del comp, payload
+    # comparison arm: dense fp32 all-reduce of the same deltas
+    delta = torch.empty_like(master)
+    p16t = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    theta = torch.empty_like(master)
+    ts = []
+    for it in range(warmup + iters):
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = _events()
+        e0.record()
+        torch.sub(snap, master, out=delta)
+        if world > 1:
+            dist.all_reduce(delta, op=dist.ReduceOp.AVG)
+        theta.copy_(snap).sub_(delta)
+        ops.cast_bf16(theta, p16t)
+        e1.record()
+        torch.cuda.synchronize()
+        if it >= warmup:
+            ts.append(e0.elapsed_time(e1))
+    ams = _max_over_ranks(sorted(ts)[len(ts) // 2], dev)
+    if rank == 0:
+        results.append({"bench": "nccl_dense_allreduce", "model": name, "params": L.num_params(), "n_nodes": world,
+                        "total_ms": round(ams, 3), "allreduce_bytes_per_rank": n * 4,
+                        "bus_bytes_per_rank": int(2 * (world - 1) / world * n * 4),
+                        "timing": "CUDA events, median of iters, max over ranks"})
+    barrier()
+    return results
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--models", default="tiny,small")
+    ap.add_argument("--topk", default="0.01,0.1,0.99")
+    ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=2)
+    a = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=300))
+    topks = [float(x) for x in a.topk.split(",")]
+    for m in a.models.split(","):
+        for r in run_model(m, topks, a.iters, a.warmup, rank, world, dev):
+            print(json.dumps(r), flush=True)
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

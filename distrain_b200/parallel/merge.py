@@ -140,15 +140,27 @@ class DeviceMerger:
         self.stream = stream or torch.cuda.Stream(device=self.device, priority=0)
         self.stats = torch.zeros(3 * 64, dtype=torch.float64, device=self.device)
         self.stats_host = torch.zeros(3 * 64, dtype=torch.float64).pin_memory()
-        self.desc = torch.zeros(64 * struct.calcsize(_CONTRIB_FMT), dtype=torch.uint8, device=self.device)
-        self.desc_host = torch.zeros_like(self.desc, device="cpu").pin_memory()
 
-    def _upload(self, contribs: List[Contribution], coefs: List[float]):
+    def _pack(self, contribs: List[Contribution], coefs: List[float]):
+        """Host descriptor table (struct Contrib records), passed to the kernels as launch parameters."""
+        import ctypes
         fmt = _CONTRIB_FMT
         raw = b"".join(struct.pack(fmt, c.idx_ptr if not c.dense else 0, c.q_ptr, c.val_ptr, c.scales_ptr, c.count,
                                    max(c.block, 1), int(c.dense), float(k), 0) for c, k in zip(contribs, coefs))
-        self.desc_host[:len(raw)].copy_(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
-        self.desc[:len(raw)].copy_(self.desc_host[:len(raw)], non_blocking=True)
+        buf = ctypes.create_string_buffer(raw, len(raw))
+        self._keep = buf
+        return buf
+
+    def _prepass(self, contribs: List[Contribution], maxc: int):
+        from ..ops._lib import check
+        st = self.stream
+        n = len(contribs)
+        buf = self._pack(contribs, [1.0] * n)
+        with torch.cuda.stream(st):
+            check(self.L.dt_merge_prepass(buf, n, maxc, self.stats.data_ptr(), st.cuda_stream), "dt_merge_prepass")
+            self.stats_host[:3 * n].copy_(self.stats[:3 * n], non_blocking=True)
+        st.synchronize()
+        return self.stats_host[:3 * n].view(n, 3).tolist()
 
     def merge(self, contribs: List[Contribution], outer_lr: float, outer_momentum: float, mc32: int = 0,
               mc16: int = 0, stage32: Sequence[int] = (), stage16: Sequence[int] = (), write_bf16: bool = True):
@@ -161,12 +173,7 @@ class DeviceMerger:
         st = self.stream
         sp = st.cuda_stream
         maxc = max(c.count for c in contribs)
-        with torch.cuda.stream(st):
-            self._upload(contribs, [1.0] * n)
-            check(self.L.dt_merge_prepass(self.desc.data_ptr(), n, maxc, self.stats.data_ptr(), sp), "dt_merge_prepass")
-            self.stats_host[:3 * n].copy_(self.stats[:3 * n], non_blocking=True)
-        st.synchronize()
-        s = self.stats_host[:3 * n].view(n, 3).tolist()
+        s = self._prepass(contribs, maxc)
         valid, norms = [], []
         reasons = []
         for i, (sumsq, mx, nf) in enumerate(s):
@@ -184,10 +191,9 @@ class DeviceMerger:
             coefs[i] = contribs[i].weight / wsum * scales[j]
         s32 = (ctypes.c_void_p * max(len(stage32), 1))(*stage32) if stage32 else None
         s16 = (ctypes.c_void_p * max(len(stage16), 1))(*stage16) if stage16 else None
+        buf = self._pack(contribs, coefs)
         with torch.cuda.stream(st):
-            self._upload(contribs, coefs)
-            check(self.L.dt_merge_accumulate(self.desc.data_ptr(), n, maxc, self.acc.data_ptr(), sp),
-                  "dt_merge_accumulate")
+            check(self.L.dt_merge_accumulate(buf, n, maxc, self.acc.data_ptr(), sp), "dt_merge_accumulate")
             check(self.L.dt_merge_apply_broadcast(self.theta.data_ptr(),
                                                   self.vel.data_ptr() if self.vel is not None else None,
                                                   self.acc.data_ptr(), self.n, float(outer_lr), float(outer_momentum),
