@@ -133,6 +133,17 @@ DT_API int dt_adamw_step(float* p, const float* g, float* m, float* v, void* p16
   return (int)cudaGetLastError();
 }
 
+// Prepare + update only: `norms` already holds the per-segment squared gradient norms (e.g. summed over a
+// tensor-parallel group after dt_seg_sqnorm).
+DT_API int dt_adamw_apply(float* p, const float* g, float* m, float* v, void* p16, const int* cseg,
+                          const long long* cstart, const long long* cend, int nchunks, const float* norms, int nseg,
+                          float* hp, const float* loss_flag, cudaStream_t st) {
+  adam_prepare_kernel<<<1, 1, 0, st>>>(hp, loss_flag);
+  adamw_update_kernel<<<nchunks, 256, 0, st>>>(p, g, m, v, reinterpret_cast<__nv_bfloat16*>(p16), cseg, cstart, cend,
+                                               norms, nseg, hp);
+  return (int)cudaGetLastError();
+}
+
 DT_API int dt_seg_sqnorm(const float* g, const int* cseg, const long long* cstart, const long long* cend, int nchunks,
                          float* norms, int nseg, cudaStream_t st) {
   DT_CUDA_RET(cudaMemsetAsync(norms, 0, sizeof(float) * nseg, st));

@@ -136,6 +136,57 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ─────────────── tensor-parallel partial-sum hand-off (peer GPU -> this GPU) ───────────────
+// The peer's producer kernel stores its partial output into this GPU's receive buffer over NVLink and
+// then adds 1 to *arrivals (system-scope release). The k-th consumer kernel waits until arrivals
+// exceeds *consumed (read at its start by every block), reads the partial with L2-only loads, and its
+// last block to finish advances *consumed. Waits are bounded: on a timeout the block records an error
+// code in dt_error_word and skips its work instead of hanging.
+struct PeerWait {
+  const unsigned* arrivals;  // null: no peer partial
+  unsigned* consumed;
+  unsigned* done_blocks;     // zeroed scratch, returns to 0 after every launch
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Call from every thread of the block; returns false (block-uniform) if the partial never arrived.
+__device__ __forceinline__ bool peer_wait_begin(const PeerWait& w, int* sh_ok) {
+  if (!w.arrivals) return true;
+  if (threadIdx.x == 0) {
+    const unsigned target = *reinterpret_cast<volatile unsigned*>(w.consumed) + 1u;
+    int ok = 1;
+    if ((int)(ld_acquire_sys(w.arrivals) - target) < 0) {
+      const uint64_t t0 = dt_globaltimer();
+      while ((int)(ld_acquire_sys(w.arrivals) - target) < 0) {
+        if (*reinterpret_cast<volatile int*>(&dt_error_word) != 0 || dt_globaltimer() - t0 > DT_WAIT_NS) {
+          dt_set_error(DT_ERR_TIMEOUT_PEER, 900);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    *sh_ok = ok;
+  }
+  __syncthreads();
+  return *sh_ok != 0;
+}
+
+// Call from every thread of the block after its last read of the partial.
+__device__ __forceinline__ void peer_wait_end(const PeerWait& w) {
+  if (!w.arrivals) return;
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(w.done_blocks, 1u) == gridDim.x - 1) {
+    *w.done_blocks = 0u;
+    __threadfence();
+    atomicAdd(w.consumed, 1u);
+  }
+}
+
 // ───────────────────────────── TMA ─────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");

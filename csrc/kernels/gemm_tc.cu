@@ -36,6 +36,12 @@ struct GemmArgs {
   float alpha;
   void* C;
   long long ldc;
+  // Tensor-parallel partial-sum exchange (bf16 epilogue only): every output box is also TMA-stored
+  // into the peer GPU's receive buffer (tmCp, over NVLink); once all CTAs' stores have completed, the
+  // last CTA adds 1 to the peer's arrival counter with a system-scope release.
+  int peer;
+  unsigned* peer_arrivals;  // on the peer GPU
+  unsigned* done_ctas;      // local scratch counter, returns to 0 after every launch
 };
 
 template <int BN>
@@ -62,7 +68,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 template <int BN, int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmCp, GemmArgs args) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -265,6 +271,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (lane == 0) {
             if (args.epi == EPI_F32_ATOMIC) tma_reduce_add_2d(&tmC, stage, gcol, row0);
             else tma_store_2d(&tmC, stage, gcol, row0);
+            if (args.peer) tma_store_2d(&tmCp, stage, gcol, row0);
             bulk_commit();
           }
           pending = true;
@@ -281,6 +288,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (args.peer && threadIdx.x == 0) {
+    // every epilogue warp has waited for its bulk stores (wait_group 0) before the barrier above
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence_system();
+    if (atomicAdd(args.done_ctas, 1u) == gridDim.x - 1) {
+      *args.done_ctas = 0u;
+      __threadfence_system();
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(args.peer_arrivals) : "memory");
+    }
+  }
 }
 
 // ───────────────────────────── host side ─────────────────────────────
@@ -317,8 +334,8 @@ int make_map(CUtensorMap* m, const void* ptr, long long inner, long long outer, 
 int g_num_sms = 0;
 
 template <int BN, int A_MN, int B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int grid,
-           cudaStream_t st) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tcp,
+           const GemmArgs& a, int grid, cudaStream_t st) {
   using C = Cfg<BN>;
   auto k = gemm_tc_kernel<BN, A_MN, B_MN>;
   static bool attr_set = false;
@@ -326,20 +343,16 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
     DT_CUDA_RET(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, a);
+  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, tcp, a);
   return (int)cudaGetLastError();
 }
 
 }  // namespace
 
-// C[M,N] (op)= alpha * A[M,K] . B[N,K]^T
-//   a_mn = 0: A(m,k) at A[m*lda + k];  a_mn = 1: A(m,k) at A[k*lda + m]
-//   b_mn = 0: B(n,k) at B[n*ldb + k];  b_mn = 1: B(n,k) at B[k*ldb + n]
-//   epi: 0 bf16 store, 1 fp32 store, 2 fp32 atomic add;  split_k > 1 requires epi == 2.
-//   bn: 128 or 256 (0 = choose).  Returns 0 or a CUDA / argument error code.
-DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp,
-                        long long ldc, int M, int N, int K, int epi, float alpha, int split_k, int bn,
-                        cudaStream_t stream) {
+namespace {
+int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp, long long ldc,
+              int M, int N, int K, int epi, float alpha, int split_k, int bn, void* Cpeer, unsigned* peer_arrivals,
+              unsigned* done_ctas, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((lda % 8) || (ldb % 8) || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15)) return -10;
   if (split_k > 1 && epi != EPI_F32_ATOMIC) return -11;
@@ -378,13 +391,20 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
   a.alpha = alpha;
   a.C = Cp;
   a.ldc = ldc;
+  a.peer = Cpeer != nullptr;
+  a.peer_arrivals = peer_arrivals;
+  a.done_ctas = done_ctas;
+  if (a.peer && (epi != EPI_BF16 || !peer_arrivals || !done_ctas || (reinterpret_cast<uintptr_t>(Cpeer) & 15)))
+    return -13;
 
   if ((ldc % (epi == EPI_BF16 ? 8 : 4)) || (reinterpret_cast<uintptr_t>(Cp) & 15)) return -12;
-  CUtensorMap ta, tb, tcm;
+  CUtensorMap ta, tb, tcm, tcp;
   int rc;
   rc = (epi == EPI_BF16) ? make_map(&tcm, Cp, N, M, ldc, 64, 32, false, true)
                          : make_map(&tcm, Cp, N, M, ldc, 32, 32, true, true);
   if (rc) return rc;
+  tcp = tcm;
+  if (a.peer && (rc = make_map(&tcp, Cpeer, N, M, ldc, 64, 32, false, true))) return rc;
   rc = a_mn ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
   if (rc) return rc;
   rc = b_mn ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
@@ -393,14 +413,37 @@ DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, i
   int units = tiles * a.split_k;
   int grid = units < g_num_sms ? units : g_num_sms;
   if (bn == 256) {
-    if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, tcm, a, grid, stream);
-    if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, tcm, a, grid, stream);
-    if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, tcm, a, grid, stream);
-    return launch<256, 1, 1>(ta, tb, tcm, a, grid, stream);
+    if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, tcm, tcp, a, grid, stream);
+    if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    return launch<256, 1, 1>(ta, tb, tcm, tcp, a, grid, stream);
   } else {
-    if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, tcm, a, grid, stream);
-    if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, tcm, a, grid, stream);
-    if (a_mn && !b_mn) return launch<128, 1, 0>(ta, tb, tcm, a, grid, stream);
-    return launch<128, 1, 1>(ta, tb, tcm, a, grid, stream);
+    if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, tcm, tcp, a, grid, stream);
+    if (a_mn && !b_mn) return launch<128, 1, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    return launch<128, 1, 1>(ta, tb, tcm, tcp, a, grid, stream);
   }
+}
+}  // namespace
+
+// C[M,N] (op)= alpha * A[M,K] . B[N,K]^T
+//   a_mn = 0: A(m,k) at A[m*lda + k];  a_mn = 1: A(m,k) at A[k*lda + m]
+//   b_mn = 0: B(n,k) at B[n*ldb + k];  b_mn = 1: B(n,k) at B[k*ldb + n]
+//   epi: 0 bf16 store, 1 fp32 store, 2 fp32 atomic add;  split_k > 1 requires epi == 2.
+//   bn: 128 or 256 (0 = choose).  Returns 0 or a CUDA / argument error code.
+DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp,
+                        long long ldc, int M, int N, int K, int epi, float alpha, int split_k, int bn,
+                        cudaStream_t stream) {
+  return gemm_impl(A, a_mn, lda, B, b_mn, ldb, Cp, ldc, M, N, K, epi, alpha, split_k, bn, nullptr, nullptr, nullptr,
+                   stream);
+}
+
+// Same product (bf16 epilogue) whose every output box is also stored into `Cpeer` (a peer GPU's buffer of
+// the same shape and ldc, mapped into this process); when all boxes have landed the kernel adds 1 to
+// *peer_arrivals (on the peer) with a system-scope release. `done_ctas` is a zeroed local counter.
+DT_API int dt_gemm_bf16_peer(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp,
+                             long long ldc, int M, int N, int K, float alpha, int bn, void* Cpeer,
+                             unsigned* peer_arrivals, unsigned* done_ctas, cudaStream_t stream) {
+  return gemm_impl(A, a_mn, lda, B, b_mn, ldb, Cp, ldc, M, N, K, EPI_BF16, alpha, 1, bn, Cpeer, peer_arrivals,
+                   done_ctas, stream);
 }

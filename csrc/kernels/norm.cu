@@ -18,9 +18,15 @@ __global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_b
                                        const float* __restrict__ emb, const int* __restrict__ ids, int T, int S,
                                        const float* __restrict__ w, const float* __restrict__ scale,
                                        float* __restrict__ out_resid, __nv_bfloat16* __restrict__ y,
-                                       float* __restrict__ rstd_out, int H, float eps) {
+                                       float* __restrict__ rstd_out, int H, float eps,
+                                       const __nv_bfloat16* br2, PeerWait pw) {
   __shared__ float sh[32];
+  __shared__ int sh_ok;
   const long long row = blockIdx.x;
+  if (!peer_wait_begin(pw, &sh_ok)) {
+    peer_wait_end(pw);
+    return;
+  }
   const float* src;
   if (emb) {
     long long b = row / T, t = row - b * T;
@@ -37,6 +43,11 @@ __global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_b
       float4 a = *reinterpret_cast<const float4*>(src + c);
       if (br) {
         uint2 bb = *reinterpret_cast<const uint2*>(br + row * H + c);
+        float2 b0 = unpack_bf16(bb.x), b1 = unpack_bf16(bb.y);
+        a.x += b0.x; a.y += b0.y; a.z += b1.x; a.w += b1.y;
+      }
+      if (br2) {  // the tensor-parallel peer's partial (written over NVLink: L2-only load)
+        uint2 bb = __ldcg(reinterpret_cast<const uint2*>(br2 + row * H + c));
         float2 b0 = unpack_bf16(bb.x), b1 = unpack_bf16(bb.y);
         a.x += b0.x; a.y += b0.y; a.z += b1.x; a.w += b1.y;
       }
@@ -62,6 +73,7 @@ __global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_b
       *reinterpret_cast<uint2*>(y + row * H + c) = o;
     }
   }
+  peer_wait_end(pw);
 }
 
 // Backward. Block handles ROWS_BWD rows; thread owns VPT float4 column groups.
@@ -76,8 +88,14 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const f
                                    const float* __restrict__ rstd, const float* __restrict__ w,
                                    const float* __restrict__ scale, const float* dresid_in, float* dresid_out,
                                    __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw,
-                                   float* __restrict__ dscale, int M, int H) {
+                                   float* __restrict__ dscale, int M, int H, const __nv_bfloat16* dy2,
+                                   PeerWait pw) {
   __shared__ float sh[32];
+  __shared__ int sh_ok;
+  if (!peer_wait_begin(pw, &sh_ok)) {
+    peer_wait_end(pw);
+    return;
+  }
   float4 wv[VPT], dwacc[VPT];
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
@@ -100,6 +118,11 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const f
       if (c < H) {
         uint2 bb = *reinterpret_cast<const uint2*>(dy + row * H + c);
         float2 a = unpack_bf16(bb.x), b = unpack_bf16(bb.y);
+        if (dy2) {  // the tensor-parallel peer's partial data gradient
+          uint2 b2 = __ldcg(reinterpret_cast<const uint2*>(dy2 + row * H + c));
+          float2 a2 = unpack_bf16(b2.x), c2 = unpack_bf16(b2.y);
+          a.x += a2.x; a.y += a2.y; b.x += c2.x; b.y += c2.y;
+        }
         float4 xv = *reinterpret_cast<const float4*>(x + row * H + c);
         xh[i] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
         g[i] = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
@@ -143,6 +166,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const f
     float t = block_sum(ds_acc, sh);
     if (threadIdx.x == 0) atomicAdd(dscale, t);
   }
+  peer_wait_end(pw);
 }
 
 // Warp-per-row backward (H = 128 * VEC): no block-wide barrier per row. All three row loads (dy, x,
@@ -158,8 +182,14 @@ template <int VEC>
 __global__ void __launch_bounds__(256, rms_bwd_blocks<VEC>()) rmsnorm_bwd_warp_kernel(
     const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ rstd,
     const float* __restrict__ w, const float* __restrict__ scale, const float* dresid_in, float* dresid_out,
-    __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw, float* __restrict__ dscale, int M, int H) {
+    __nv_bfloat16* __restrict__ dresid16, float* __restrict__ dw, float* __restrict__ dscale, int M, int H,
+    const __nv_bfloat16* dy2, PeerWait pw) {
   extern __shared__ float red[];  // [8 warps][H] dw partials, then w [H]
+  __shared__ int sh_ok;
+  if (!peer_wait_begin(pw, &sh_ok)) {
+    peer_wait_end(pw);
+    return;
+  }
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const float s = scale ? *scale : 1.f;
   float* sw = red + 8 * H;
@@ -179,6 +209,13 @@ __global__ void __launch_bounds__(256, rms_bwd_blocks<VEC>()) rmsnorm_bwd_warp_k
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 4;
       graw[i] = *reinterpret_cast<const uint2*>(dy + row * H + c);
+      if (dy2) {  // the tensor-parallel peer's partial data gradient, summed in fp32 then kept as bf16x2
+        const uint2 b2 = __ldcg(reinterpret_cast<const uint2*>(dy2 + row * H + c));
+        const float2 a0 = unpack_bf16(graw[i].x), a1 = unpack_bf16(graw[i].y);
+        const float2 c0 = unpack_bf16(b2.x), c1 = unpack_bf16(b2.y);
+        graw[i].x = pack_bf16(a0.x + c0.x, a0.y + c0.y);
+        graw[i].y = pack_bf16(a1.x + c1.x, a1.y + c1.y);
+      }
       xh[i] = *reinterpret_cast<const float4*>(x + row * H + c);
       if (dresid_in) pin[i] = *reinterpret_cast<const float4*>(dresid_in + row * H + c);
     }
@@ -230,6 +267,7 @@ __global__ void __launch_bounds__(256, rms_bwd_blocks<VEC>()) rmsnorm_bwd_warp_k
     float t = block_sum(ds_acc, sh);
     if (threadIdx.x == 0) atomicAdd(dscale, t);
   }
+  peer_wait_end(pw);
 }
 
 // dE[ids[row]] += g[row]   (fp32, float4 atomics)
@@ -251,31 +289,34 @@ int threads_for(int H, int vpt) {
 
 }  // namespace
 
-// resid_out = (emb ? emb[ids] : x) + br ;  y = bf16(rmsnorm(resid_out) * w * scale)
-DT_API int dt_add_rmsnorm_fwd(const float* x, const void* br, const float* emb, const int* ids, int T, int S,
-                              const float* w, const float* scale, float* out_resid, void* y, float* rstd, int M,
-                              int H, float eps, cudaStream_t st) {
+namespace {
+
+int add_rmsnorm_impl(const float* x, const void* br, const void* br2, const float* emb, const int* ids, int T, int S,
+                     const float* w, const float* scale, float* out_resid, void* y, float* rstd, int M, int H, float eps,
+                     PeerWait pw, cudaStream_t st) {
   if (H % 4) return -10;
   const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(br);
+  const __nv_bfloat16* b2 = reinterpret_cast<const __nv_bfloat16*>(br2);
   __nv_bfloat16* yy = reinterpret_cast<__nv_bfloat16*>(y);
   if (H <= 4096) {
     int th = threads_for(H, 1);
-    add_rmsnorm_fwd_kernel<1><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps);
+    add_rmsnorm_fwd_kernel<1><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps, b2, pw);
   } else if (H <= 8192) {
     int th = threads_for(H, 2);
-    add_rmsnorm_fwd_kernel<2><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps);
+    add_rmsnorm_fwd_kernel<2><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps, b2, pw);
   } else {
     return -11;
   }
   return (int)cudaGetLastError();
 }
 
-DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, const float* w, const float* scale,
-                          const float* dresid_in, float* dresid_out, void* dresid16, float* dw, float* dscale, int M,
-                          int H, cudaStream_t st) {
+int rmsnorm_bwd_impl(const void* dy, const void* dy2, const float* x, const float* rstd, const float* w,
+                     const float* scale, const float* dresid_in, float* dresid_out, void* dresid16, float* dw,
+                     float* dscale, int M, int H, PeerWait pw, cudaStream_t st) {
   if (H % 4) return -10;
   int blocks = (M + ROWS_BWD - 1) / ROWS_BWD;
   const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(dy);
+  const __nv_bfloat16* d2 = reinterpret_cast<const __nv_bfloat16*>(dy2);
   auto d16 = reinterpret_cast<__nv_bfloat16*>(dresid16);
   if (H % 128 == 0 && H <= 2048) {
     int wb = (M + 7) / 8;
@@ -285,7 +326,8 @@ DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, con
 #define DT_RMS_WARP(V)                                                                                       \
   case V:                                                                                                   \
     if (sm > 48 * 1024) cudaFuncSetAttribute(rmsnorm_bwd_warp_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm); \
-    rmsnorm_bwd_warp_kernel<V><<<wb, 256, sm, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out, d16, dw, dscale, M, H); \
+    rmsnorm_bwd_warp_kernel<V><<<wb, 256, sm, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out, d16, dw, dscale, M, H, \
+                                                    d2, pw);                                                 \
     return (int)cudaGetLastError();
     switch (H / 128) {
       DT_RMS_WARP(1) DT_RMS_WARP(2) DT_RMS_WARP(3) DT_RMS_WARP(4) DT_RMS_WARP(5) DT_RMS_WARP(6) DT_RMS_WARP(8)
@@ -295,17 +337,50 @@ DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, con
 #undef DT_RMS_WARP
   }
   if (H <= 4096) {
-    rmsnorm_bwd_kernel<1><<<blocks, threads_for(H, 1), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out,
-                                                                reinterpret_cast<__nv_bfloat16*>(dresid16), dw,
-                                                                dscale, M, H);
+    rmsnorm_bwd_kernel<1><<<blocks, threads_for(H, 1), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out, d16, dw,
+                                                                dscale, M, H, d2, pw);
   } else if (H <= 8192) {
-    rmsnorm_bwd_kernel<2><<<blocks, threads_for(H, 2), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out,
-                                                                reinterpret_cast<__nv_bfloat16*>(dresid16), dw,
-                                                                dscale, M, H);
+    rmsnorm_bwd_kernel<2><<<blocks, threads_for(H, 2), 0, st>>>(d, x, rstd, w, scale, dresid_in, dresid_out, d16, dw,
+                                                                dscale, M, H, d2, pw);
   } else {
     return -11;
   }
   return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+// resid_out = (emb ? emb[ids] : x) + br ;  y = bf16(rmsnorm(resid_out) * w * scale)
+DT_API int dt_add_rmsnorm_fwd(const float* x, const void* br, const float* emb, const int* ids, int T, int S,
+                              const float* w, const float* scale, float* out_resid, void* y, float* rstd, int M,
+                              int H, float eps, cudaStream_t st) {
+  return add_rmsnorm_impl(x, br, nullptr, emb, ids, T, S, w, scale, out_resid, y, rstd, M, H, eps, PeerWait{}, st);
+}
+
+// Tensor-parallel form: resid_out = x + br + br2 with br2 the peer's partial in this GPU's receive buffer,
+// waited for through the arrival / consumed counters (PeerWait).
+DT_API int dt_add_rmsnorm_fwd_tp(const float* x, const void* br, const void* br2, const float* w, const float* scale,
+                                 float* out_resid, void* y, float* rstd, int M, int H, float eps,
+                                 const unsigned* arrivals, unsigned* consumed, unsigned* done_blocks,
+                                 cudaStream_t st) {
+  return add_rmsnorm_impl(x, br, br2, nullptr, nullptr, 1, 1, w, scale, out_resid, y, rstd, M, H, eps,
+                          PeerWait{arrivals, consumed, done_blocks}, st);
+}
+
+DT_API int dt_rmsnorm_bwd(const void* dy, const float* x, const float* rstd, const float* w, const float* scale,
+                          const float* dresid_in, float* dresid_out, void* dresid16, float* dw, float* dscale, int M,
+                          int H, cudaStream_t st) {
+  return rmsnorm_bwd_impl(dy, nullptr, x, rstd, w, scale, dresid_in, dresid_out, dresid16, dw, dscale, M, H,
+                          PeerWait{}, st);
+}
+
+// Tensor-parallel form: dy + dy2 with dy2 the peer's partial data gradient in the receive buffer.
+DT_API int dt_rmsnorm_bwd_tp(const void* dy, const void* dy2, const float* x, const float* rstd, const float* w,
+                             const float* scale, const float* dresid_in, float* dresid_out, void* dresid16, float* dw,
+                             float* dscale, int M, int H, const unsigned* arrivals, unsigned* consumed,
+                             unsigned* done_blocks, cudaStream_t st) {
+  return rmsnorm_bwd_impl(dy, dy2, x, rstd, w, scale, dresid_in, dresid_out, dresid16, dw, dscale, M, H,
+                          PeerWait{arrivals, consumed, done_blocks}, st);
 }
 
 DT_API int dt_embedding_bwd(const float* g, const int* ids, int T, int S, float* dE, int M, int H, cudaStream_t st) {

@@ -15,6 +15,12 @@ Per step (all on the current stream):
 
 The step mirrors the reference's continuous-loop step (node/cli/src/continuous.rs:598-637): loss on
 tokens[:, :-1] -> tokens[:, 1:], a NaN loss skips the optimiser update (decided on the device).
+
+Options: ``tp`` (a ``parallel.tensor_parallel.TensorParallel``) runs this replica split over a
+tensor-parallel group (local heads / FFN rows; all-reduces after the row-parallel GEMMs in the forward
+and the column-parallel data-gradient GEMMs in the backward; group-summed clip norms). ``act_ckpt``
+keeps only each block's input residual and recomputes the block's forward (norm, QKV, RoPE, attention,
+o_proj, norm, gate|up, SwiGLU) right before its backward, with one set of block buffers.
 """
 from __future__ import annotations
 
@@ -35,16 +41,20 @@ HP_LR, HP_B1, HP_B2, HP_EPS, HP_WD, HP_BC1, HP_BC2, HP_MAXNORM, HP_CLIP_GLOBAL, 
 class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
-                 lm_chunk_rows: int = 8192, attn_impl: str = "dt"):
+                 lm_chunk_rows: int = 8192, attn_impl: str = "dt", tp=None, act_ckpt: bool = False):
         self.cfg = cfg
+        self.tp = tp
+        self.act_ckpt = act_ckpt
+        tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
         self.optim = optim or OptimConfig()
         self.device = torch.device(device)
         self.B, self.S = batch, seq_len
         self.T = seq_len - 1
         self.M = self.B * self.T
         self.attn_impl = attn_impl
-        L = self.layout = ParamLayout(cfg)
-        H, F, d, nh, nkv, V = cfg.hidden_dim, cfg.ffn_hidden_dim, cfg.head_dim(), cfg.num_heads, cfg.num_kv_heads, cfg.vocab_size
+        L = self.layout = ParamLayout(cfg, tp_rank, tp_size)
+        # local (per tensor-parallel rank) head counts and FFN width
+        H, F, d, nh, nkv, V = cfg.hidden_dim, L.F, cfg.head_dim(), L.nh, L.nkv, cfg.vocab_size
         self.H, self.F, self.d, self.nh, self.nkv, self.V = H, F, d, nh, nkv, V
         self.W = (nh + 2 * nkv) * d
         dev = self.device
@@ -67,18 +77,24 @@ class TrainEngine:
         self.cos, self.sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
         # ── activations (saved for backward) ──
         M, Lr = self.M, cfg.num_layers
-        self.resid_in = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
-        self.resid_mid = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
-        self.rstd1 = [torch.empty(M, dtype=f32, device=dev) for _ in range(Lr)]
-        self.rstd2 = [torch.empty(M, dtype=f32, device=dev) for _ in range(Lr)]
-        self.xn1 = [torch.empty(M, H, dtype=bf16, device=dev) for _ in range(Lr)]
-        self.xn2 = [torch.empty(M, H, dtype=bf16, device=dev) for _ in range(Lr)]
-        self.qkv = [torch.empty(M, self.W, dtype=bf16, device=dev) for _ in range(Lr)]
-        self.attn = [torch.empty(M, nh * d, dtype=bf16, device=dev) for _ in range(Lr)]
         Tp = attn_ops.lse_stride(self.T)
-        self.lse = [torch.empty(batch, nh, Tp, dtype=f32, device=dev) for _ in range(Lr)]
-        self.gu = [torch.empty(M, 2 * F, dtype=bf16, device=dev) for _ in range(Lr)]
-        self.hact = [torch.empty(M, F, dtype=bf16, device=dev) for _ in range(Lr)]
+        # with activation checkpointing every block shares one set of buffers (index 0)
+        nb = 1 if act_ckpt else Lr
+
+        def per_block(make):
+            bufs = [make() for _ in range(nb)]
+            return bufs * Lr if act_ckpt else bufs
+        self.resid_in = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
+        self.resid_mid = per_block(lambda: torch.empty(M, H, dtype=f32, device=dev))
+        self.rstd1 = per_block(lambda: torch.empty(M, dtype=f32, device=dev))
+        self.rstd2 = per_block(lambda: torch.empty(M, dtype=f32, device=dev))
+        self.xn1 = per_block(lambda: torch.empty(M, H, dtype=bf16, device=dev))
+        self.xn2 = per_block(lambda: torch.empty(M, H, dtype=bf16, device=dev))
+        self.qkv = per_block(lambda: torch.empty(M, self.W, dtype=bf16, device=dev))
+        self.attn = per_block(lambda: torch.empty(M, nh * d, dtype=bf16, device=dev))
+        self.lse = per_block(lambda: torch.empty(batch, nh, Tp, dtype=f32, device=dev))
+        self.gu = per_block(lambda: torch.empty(M, 2 * F, dtype=bf16, device=dev))
+        self.hact = per_block(lambda: torch.empty(M, F, dtype=bf16, device=dev))
         self.resid_fin = torch.empty(M, H, dtype=f32, device=dev)
         self.rstd_f = torch.empty(M, dtype=f32, device=dev)
         self.xs = torch.empty(M, H, dtype=bf16, device=dev)
@@ -96,10 +112,17 @@ class TrainEngine:
         self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
         self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
         self.delta = torch.empty(batch, nh, Tp, dtype=f32, device=dev)
+        if tp is not None:
+            from ..parallel.tensor_parallel import norm_weights
+            self.norm_w = norm_weights(L, dev)
         # ── named views ──
         self._bind_views()
         if flat_init is None:
-            flat_init = init_flat(L, init_std, seed)
+            if tp is not None and tp.size > 1:
+                from ..parallel.tensor_parallel import init_flat_tp
+                flat_init = init_flat_tp(L, init_std, seed, device=dev)
+            else:
+                flat_init = init_flat(L, init_std, seed)
         self.load_flat(flat_init)
         self.graph = None
         self.kernels_per_step = 0
@@ -181,6 +204,8 @@ class TrainEngine:
         M, H, F, T, S, W, d, nh, nkv, V = self.M, self.H, self.F, self.T, self.S, self.W, self.d, self.nh, self.nkv, self.V
         eps = cfg.norm_eps
         Lr = cfg.num_layers
+        if self._tp_active() and self.tp.fused:
+            self.tp.begin_step(4 * Lr + ((Lr - 1) if self.act_ckpt else 0))
         self.grad.zero_()
         # ── forward ──
         ops.add_rmsnorm_fwd(emb=self.E, ids=self.ids, T=T, S=S, w=self.pv[0]["attn_norm"], out_resid=self.resid_in[0],
@@ -191,19 +216,17 @@ class TrainEngine:
             ops.rope_fwd(self.qkv[l], pv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
             attn_ops.attention_fwd(self.qkv[l], self.attn[l], self.lse[l], B=self.B, T=T, nh=nh, nkv=nkv, d=d,
                                    impl=self.attn_impl)
-            ops.linear_fwd(self.attn[l], wv["o_w"], self.br)
-            ops.add_rmsnorm_fwd(x=self.resid_in[l], br=self.br, w=pv["ffn_norm"], out_resid=self.resid_mid[l],
-                                y=self.xn2[l], rstd=self.rstd2[l], eps=eps, M=M, H=H)
+            self._row_parallel_add_norm(self.attn[l], wv["o_w"], x=self.resid_in[l], w=pv["ffn_norm"],
+                                        out_resid=self.resid_mid[l], y=self.xn2[l], rstd=self.rstd2[l])
             ops.linear_fwd(self.xn2[l], wv["gu_w"], self.gu[l])
             ops.swiglu_fwd(self.gu[l], self.hact[l], M=M, F=F)
-            ops.linear_fwd(self.hact[l], wv["down_w"], self.br)
             if l + 1 < Lr:
-                ops.add_rmsnorm_fwd(x=self.resid_mid[l], br=self.br, w=self.pv[l + 1]["attn_norm"],
-                                    out_resid=self.resid_in[l + 1], y=self.xn1[l + 1], rstd=self.rstd1[l + 1], eps=eps,
-                                    M=M, H=H)
+                self._row_parallel_add_norm(self.hact[l], wv["down_w"], x=self.resid_mid[l],
+                                            w=self.pv[l + 1]["attn_norm"], out_resid=self.resid_in[l + 1],
+                                            y=self.xn1[l + 1], rstd=self.rstd1[l + 1])
             else:
-                ops.add_rmsnorm_fwd(x=self.resid_mid[l], br=self.br, w=self.fnorm, scale=self.oscale,
-                                    out_resid=self.resid_fin, y=self.xs, rstd=self.rstd_f, eps=eps, M=M, H=H)
+                self._row_parallel_add_norm(self.hact[l], wv["down_w"], x=self.resid_mid[l], w=self.fnorm,
+                                            scale=self.oscale, out_resid=self.resid_fin, y=self.xs, rstd=self.rstd_f)
         # ── tied LM head + cross-entropy, chunked over rows; backward of the head fused per chunk ──
         inv_m = 1.0 / M
         for r0 in range(0, M, self.lm_chunk):
@@ -222,29 +245,92 @@ class TrainEngine:
                         dresid_out=self.dresid, dresid16=self.g16, dw=self.g_fnorm, dscale=self.g_oscale, M=M, H=H)
         for l in reversed(range(Lr)):
             pv, wv, gv = self.pv[l], self.wv[l], self.gv[l]
+            if self.act_ckpt and l + 1 < Lr:  # the last block's buffers are still live from the forward
+                self._recompute_block(l)
             # FFN block
             ops.linear_dgrad(self.g16, wv["down_w"], self.dh)
             ops.linear_wgrad(self.g16, self.hact[l], gv["down_w"])
             ops.swiglu_bwd(self.dh, self.gu[l], self.dgu, M=M, F=F)
-            ops.linear_dgrad(self.dgu, wv["gu_w"], self.br)
-            ops.linear_wgrad(self.dgu, self.xn2[l], gv["gu_w"])
-            ops.rmsnorm_bwd(dy=self.br, x=self.resid_mid[l], rstd=self.rstd2[l], w=pv["ffn_norm"],
-                            dresid_in=self.dresid, dresid_out=self.dresid, dresid16=self.g16, dw=gv["ffn_norm"],
-                            M=M, H=H)
+            self._col_parallel_dgrad_norm_bwd(
+                self.dgu, wv["gu_w"], lambda: ops.linear_wgrad(self.dgu, self.xn2[l], gv["gu_w"]),
+                x=self.resid_mid[l], rstd=self.rstd2[l], w=pv["ffn_norm"], dresid_in=self.dresid,
+                dresid_out=self.dresid, dresid16=self.g16, dw=gv["ffn_norm"])
             # attention block
             ops.linear_dgrad(self.g16, wv["o_w"], self.dattn)
             ops.linear_wgrad(self.g16, self.attn[l], gv["o_w"])
             attn_ops.attention_bwd(self.qkv[l], self.attn[l], self.dattn, self.lse[l], self.dqkv, self.dq_acc,
                                    self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl)
             ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
-            ops.linear_dgrad(self.dqkv, wv["qkv_w"], self.br)
-            ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"])
-            ops.rmsnorm_bwd(dy=self.br, x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"],
-                            dresid_in=self.dresid, dresid_out=self.dresid, dresid16=self.g16 if l > 0 else None,
-                            dw=gv["attn_norm"], M=M, H=H)
+            self._col_parallel_dgrad_norm_bwd(
+                self.dqkv, wv["qkv_w"], lambda: ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"]),
+                x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"], dresid_in=self.dresid,
+                dresid_out=self.dresid, dresid16=self.g16 if l > 0 else None, dw=gv["attn_norm"])
         ops.embedding_bwd(self.dresid, self.ids, self.gE, T=T, S=S, M=M, H=H)
 
+    def _tp_active(self) -> bool:
+        return self.tp is not None and self.tp.size > 1
+
+    def _row_parallel_add_norm(self, a, w16, *, x, w, y, rstd, out_resid=None, scale=None):
+        """br = a @ w16^T (summed over the tensor-parallel group), then resid = x + br, y = rmsnorm(resid)."""
+        M, H, eps = self.M, self.H, self.cfg.norm_eps
+        if self._tp_active() and self.tp.fused:
+            tp = self.tp
+            slot = tp.next_slot()
+            ops.linear_peer(a, w16, self.br, tp.peer_recv_ptr(slot), tp.peer_arrivals, tp.done_ctas)
+            ops.add_rmsnorm_fwd_tp(x=x, br=self.br, br2=tp.recv(slot), w=w, scale=scale, out_resid=out_resid, y=y,
+                                   rstd=rstd, eps=eps, M=M, H=H, arrivals=tp.arrivals, consumed=tp.consumed,
+                                   done_blocks=tp.done_blocks)
+            return
+        ops.linear_fwd(a, w16, self.br)
+        if self._tp_active():
+            self.tp.allreduce_(self.br)
+        ops.add_rmsnorm_fwd(x=x, br=self.br, w=w, scale=scale, out_resid=out_resid, y=y, rstd=rstd, eps=eps, M=M,
+                            H=H)
+
+    def _col_parallel_dgrad_norm_bwd(self, dy, w16, between, *, x, rstd, w, dresid_in, dresid_out, dresid16, dw):
+        """br = dy @ w16 (summed over the group), ``between()`` (independent work that overlaps the
+        exchange), then the RMSNorm backward taking br as its incoming gradient."""
+        M, H = self.M, self.H
+        if self._tp_active() and self.tp.fused:
+            tp = self.tp
+            slot = tp.next_slot()
+            ops.linear_peer(dy, w16, self.br, tp.peer_recv_ptr(slot), tp.peer_arrivals, tp.done_ctas, dgrad=True)
+            between()
+            ops.rmsnorm_bwd_tp(dy=self.br, dy2=tp.recv(slot), x=x, rstd=rstd, w=w, dresid_in=dresid_in,
+                               dresid_out=dresid_out, dresid16=dresid16, dw=dw, M=M, H=H, arrivals=tp.arrivals,
+                               consumed=tp.consumed, done_blocks=tp.done_blocks)
+            return
+        ops.linear_dgrad(dy, w16, self.br)
+        if self._tp_active():
+            self.tp.allreduce_(self.br)
+        between()
+        ops.rmsnorm_bwd(dy=self.br, x=x, rstd=rstd, w=w, dresid_in=dresid_in, dresid_out=dresid_out,
+                        dresid16=dresid16, dw=dw, M=M, H=H)
+
+    def _recompute_block(self, l: int):
+        """Forward of block l from its saved input residual, into the shared block buffers."""
+        cfg = self.cfg
+        M, H, F, T, d, nh, nkv = self.M, self.H, self.F, self.T, self.d, self.nh, self.nkv
+        pv, wv = self.pv[l], self.wv[l]
+        eps = cfg.norm_eps
+        ops.add_rmsnorm_fwd(x=self.resid_in[l], w=pv["attn_norm"], y=self.xn1[l], rstd=self.rstd1[l], eps=eps,
+                            M=M, H=H)
+        ops.linear_fwd(self.xn1[l], wv["qkv_w"], self.qkv[l])
+        ops.rope_fwd(self.qkv[l], pv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+        attn_ops.attention_fwd(self.qkv[l], self.attn[l], self.lse[l], B=self.B, T=T, nh=nh, nkv=nkv, d=d,
+                               impl=self.attn_impl)
+        self._row_parallel_add_norm(self.attn[l], wv["o_w"], x=self.resid_in[l], w=pv["ffn_norm"],
+                                    out_resid=self.resid_mid[l], y=self.xn2[l], rstd=self.rstd2[l])
+        ops.linear_fwd(self.xn2[l], wv["gu_w"], self.gu[l])
+        ops.swiglu_fwd(self.gu[l], self.hact[l], M=M, F=F)
+
     def optimizer_step(self):
+        if self.tp is not None and self.tp.size > 1:
+            ops.seg_sqnorm(self.grad, self.cseg, self.cstart, self.cend, self.norms)
+            self.tp.sum_norms_(self.norms, self.norm_w)
+            ops.adamw_apply(self.master, self.grad, self.m, self.v, self.p16, self.cseg, self.cstart, self.cend,
+                            self.norms, self.hp, self.loss)
+            return
         ops.adamw_step(self.master, self.grad, self.m, self.v, self.p16, self.cseg, self.cstart, self.cend,
                        self.norms, self.hp, self.loss)
 

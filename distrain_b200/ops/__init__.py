@@ -57,6 +57,35 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, alpha: flo
          stream=stream)
 
 
+def linear_peer(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, peer_out: int, peer_arrivals: int,
+                done_ctas: int, *, dgrad: bool = False, stream=None):
+    """Row-parallel forward (``dgrad`` False: out = a @ w^T) or column-parallel data gradient (``dgrad`` True:
+    out = a @ w) whose every output box is also stored into the tensor-parallel peer's receive buffer
+    ``peer_out`` (a device address on the peer GPU), then signalled on ``peer_arrivals``."""
+    M = a.shape[0]
+    if dgrad:
+        N, K, b_mn, ldb = w.shape[1], w.shape[0], 1, w.shape[1]
+    else:
+        N, K, b_mn, ldb = w.shape[0], w.shape[1], 0, w.shape[1]
+    check(lib().dt_gemm_bf16_peer(ptr(a), 0, K, ptr(w), b_mn, ldb, ptr(out), N, M, N, K, 1.0, 0, peer_out,
+                                  peer_arrivals, done_ctas, stream_ptr(stream)), "dt_gemm_bf16_peer")
+
+
+def add_rmsnorm_fwd_tp(*, x, br, br2, w, y, rstd, eps, M, H, arrivals, consumed, done_blocks, scale=None,
+                       out_resid=None, stream=None):
+    """resid_out = x + br + br2 (br2: the peer's partial, waited for on the counters); y = rmsnorm(...)."""
+    check(lib().dt_add_rmsnorm_fwd_tp(ptr(x), ptr(br), ptr(br2), ptr(w), ptr(scale), ptr(out_resid), ptr(y),
+                                      ptr(rstd), M, H, float(eps), arrivals, consumed, done_blocks,
+                                      stream_ptr(stream)), "dt_add_rmsnorm_fwd_tp")
+
+
+def rmsnorm_bwd_tp(*, dy, dy2, x, rstd, w, dresid_out, dw, M, H, arrivals, consumed, done_blocks, scale=None,
+                   dresid_in=None, dresid16=None, dscale=None, stream=None):
+    check(lib().dt_rmsnorm_bwd_tp(ptr(dy), ptr(dy2), ptr(x), ptr(rstd), ptr(w), ptr(scale), ptr(dresid_in),
+                                  ptr(dresid_out), ptr(dresid16), ptr(dw), ptr(dscale), M, H, arrivals, consumed,
+                                  done_blocks, stream_ptr(stream)), "dt_rmsnorm_bwd_tp")
+
+
 def add_rmsnorm_fwd(*, y, rstd, w, eps, M, H, x=None, br=None, emb=None, ids=None, T=1, S=1, scale=None,
                     out_resid=None, stream=None):
     check(lib().dt_add_rmsnorm_fwd(ptr(x), ptr(br), ptr(emb), ptr(ids), T, S, ptr(w), ptr(scale), ptr(out_resid),
@@ -104,6 +133,13 @@ def adamw_step(p, g, m, v, p16, cseg, cstart, cend, norms, hp, loss_flag=None, s
     check(lib().dt_adamw_step(ptr(p), ptr(g), ptr(m), ptr(v), ptr(p16), ptr(cseg), ptr(cstart), ptr(cend),
                               cseg.numel(), ptr(norms), norms.numel(), ptr(hp), ptr(loss_flag), stream_ptr(stream)),
           "dt_adamw_step")
+
+
+def adamw_apply(p, g, m, v, p16, cseg, cstart, cend, norms, hp, loss_flag=None, stream=None):
+    """AdamW prepare + update with precomputed per-segment squared norms (tensor-parallel clipping)."""
+    check(lib().dt_adamw_apply(ptr(p), ptr(g), ptr(m), ptr(v), ptr(p16), ptr(cseg), ptr(cstart), ptr(cend),
+                               cseg.numel(), ptr(norms), norms.numel(), ptr(hp), ptr(loss_flag), stream_ptr(stream)),
+          "dt_adamw_apply")
 
 
 def seg_sqnorm(g, cseg, cstart, cend, norms, stream=None):

@@ -27,6 +27,12 @@ _SIGS = {
     "dt_device_sm_count": [c_int],
     "dt_gemm_bf16": [c_void, c_int, c_ll, c_void, c_int, c_ll, c_void, c_ll, c_int, c_int, c_int, c_int, c_float,
                      c_int, c_int, c_void],
+    "dt_gemm_bf16_peer": [c_void, c_int, c_ll, c_void, c_int, c_ll, c_void, c_ll, c_int, c_int, c_int, c_float, c_int,
+                          c_void, c_void, c_void, c_void],
+    "dt_add_rmsnorm_fwd_tp": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_float,
+                              c_void, c_void, c_void, c_void],
+    "dt_rmsnorm_bwd_tp": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void,
+                          c_int, c_int, c_void, c_void, c_void, c_void],
     "dt_add_rmsnorm_fwd": [c_void, c_void, c_void, c_void, c_int, c_int, c_void, c_void, c_void, c_void, c_void,
                            c_int, c_int, c_float, c_void],
     "dt_rmsnorm_bwd": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int,
@@ -40,6 +46,8 @@ _SIGS = {
     "dt_loss_reduce": [c_void, c_ll, c_float, c_void, c_void],
     "dt_adamw_step": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_void, c_int, c_void,
                       c_void, c_void],
+    "dt_adamw_apply": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_void, c_int, c_void,
+                       c_void, c_void],
     "dt_seg_sqnorm": [c_void, c_void, c_void, c_void, c_int, c_void, c_int, c_void],
     "dt_cast_bf16": [c_void, c_void, c_ll, c_void],
 }
@@ -52,7 +60,7 @@ class KernelError(RuntimeError):
 # Kernel launches issued through this library (incremented per launcher call by the number of
 # kernels that launcher starts); a CUDA-graph replay adds the count recorded at capture.
 LAUNCHES = [0]
-_KERNELS_PER_CALL = {"dt_adamw_step": 3, "dt_seg_sqnorm": 1, "dt_get_error": 0, "dt_clear_error": 0}
+_KERNELS_PER_CALL = {"dt_adamw_step": 3, "dt_adamw_apply": 2, "dt_seg_sqnorm": 1, "dt_get_error": 0, "dt_clear_error": 0}
 
 
 def lib():
