@@ -39,6 +39,8 @@ def _parse():
     ap.add_argument("--push-every", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-push", action="store_true", help="train only (no compression / merge)")
+    ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
+                    help="tensor-parallel partial-sum exchange: fused GEMM-epilogue peer stores, or NCCL all-reduce")
     ap.add_argument("--sync", default="inbox", choices=["inbox", "nccl"],
                     help="inbox: compressed deltas, peer-pull merge kernel, NVLS broadcast (the product); "
                          "nccl: comparison arm, dense fp32 delta all-reduce every push")
@@ -127,14 +129,32 @@ def main():
     if args.push_every:
         run.push_every = args.push_every
     nccl_arm = args.sync == "nccl" and not args.no_push
-    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=not args.no_push and not nccl_arm)
+    # tensor parallelism: node k = ranks [k*tp, (k+1)*tp); its shards are averaged across nodes by the
+    # groups of ranks that hold the same shard
+    tp_size = run.tp if (run.tp > 1 and world % run.tp == 0) else 1
+    tp, dp_group = None, None
+    if tp_size > 1:
+        from distrain_b200.parallel.tensor_parallel import TensorParallel
+        nodes = world // tp_size
+        tp_groups = [dist.new_group([k * tp_size + i for i in range(tp_size)]) for k in range(nodes)]
+        dp_groups = [dist.new_group([k * tp_size + i for k in range(nodes)]) for i in range(tp_size)]
+        tp = TensorParallel(tp_groups[rank // tp_size], rank % tp_size, tp_size, mode=args.tp_mode,
+                            rows=run.micro_batch * (run.seq_len - 1), hidden=run.model.hidden_dim, device=dev)
+        dp_group = dp_groups[rank % tp_size]
+        if not (args.no_push or nccl_arm):
+            print("note: the in-box compressed-delta protocol runs one node per GPU; with tensor parallelism the "
+                  "nodes are synchronised by the NCCL dense-delta arm", file=sys.stderr)
+            nccl_arm = True
+    node_rank, n_nodes = rank // tp_size, world // tp_size
+    node = InBoxNode(run, rank=node_rank, world=n_nodes, device=dev,
+                     enable_push=not args.no_push and not nccl_arm, tp=tp)
     if nccl_arm:
         from distrain_b200.parallel.nccl_baseline import NcclDenseSync
-        node.sync = NcclDenseSync(node, run, rank, world, dev)
+        node.sync = NcclDenseSync(node, run, node_rank, n_nodes, dev, group=dp_group)
     B, S = run.micro_batch, run.seq_len
 
-    # synthetic uniform-random tokens, per-rank seed, pinned ring of host batches
-    g = torch.Generator().manual_seed(1000 + rank)
+    # synthetic uniform-random tokens, per-node seed (the ranks of one tensor-parallel node share them)
+    g = torch.Generator().manual_seed(1000 + node_rank)
     ring = [torch.randint(0, run.model.vocab_size, (B, S), generator=g, dtype=torch.int32).pin_memory()
             for _ in range(4)]
     dev_batches = [r.to(dev) for r in ring]
@@ -193,7 +213,7 @@ def main():
     versions = node.sync.version if node.sync is not None else 0
     node.close()
     tokens_per_step = B * S
-    value = tokens_per_step * world * args.steps / (ms / 1e3)
+    value = tokens_per_step * n_nodes * args.steps / (ms / 1e3)
     if rank == 0:
         out = {
             "metric": "train tokens/sec (aggregate over GPUs, max-over-ranks time)",
@@ -209,9 +229,11 @@ def main():
             "dtype": "bf16",
             "data": "synthetic (uniform-random token ids, per-rank seeds; random-init N(0,0.02) weights)",
             "config": {"model": f"{run.name} preset ({run.model.param_count()/1e6:.1f}M params)",
-                       "global_batch": B * world, "seq_len": S,
-                       "parallelism": (f"sync-dp{world} (NCCL all-reduce of dense fp32 deltas every push)"
-                                       if nccl_arm else f"async-dp{world} (1 node per GPU)"),
+                       "global_batch": B * n_nodes, "seq_len": S,
+                       "parallelism": ((f"tp{tp_size} ({args.tp_mode} exchange) x " if tp_size > 1 else "") +
+                                       (f"sync-dp{n_nodes} (NCCL all-reduce of dense fp32 deltas every push)"
+                                        if nccl_arm else f"async-dp{n_nodes} (1 node per GPU)")),
+                       "activation_checkpointing": run.activation_checkpointing,
                        "push_every": run.push_every if not args.no_push else None,
                        "compression": ("none (dense fp32 delta)" if nccl_arm else
                                        f"top-k {run.compression.top_k_fraction:.0%} + INT8 block "
@@ -231,7 +253,7 @@ def main():
             if nccl_arm:
                 out["merge"]["allreduce_bytes"] = merges[-1]["allreduce_bytes"]
         if e2e_ms is not None:
-            out["e2e"] = {"value": round(tokens_per_step * world * args.steps / (e2e_ms_max / 1e3), 1),
+            out["e2e"] = {"value": round(tokens_per_step * n_nodes * args.steps / (e2e_ms_max / 1e3), 1),
                           "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 4}
         print(json.dumps(out), flush=True)
     if world > 1:

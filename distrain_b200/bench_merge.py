@@ -4,10 +4,14 @@ broadcast, against an NCCL all-reduce of the same deltas in dense fp32.
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 --master-port P \\
         -m distrain_b200.bench_merge [--models tiny,small] [--topk 0.01,0.1,0.99] [--iters 5] [--warmup 2]
 
+Inputs (per rank seed): a delta of i.i.d. N(0, 1e-4^2) entries over the preset's parameter layout (the
+snapshot minus the master weights) and an error-feedback buffer of the same distribution; staleness drawn
+uniformly from {0, 1, 2, 3} and token counts uniformly from [1e5, 1e6], giving the merge weights
+tokens * 0.9^staleness.
+
 Per (model, top-k), every iteration:
-  1. every rank compresses a synthetic round delta (fixed random snapshot vs master, error feedback
-     cleared) into its symmetric (peer-mapped) payload buffer: pass A + radix top-k + ordered
-     compaction + INT8 block 256;
+  1. every rank compresses its delta (+ error feedback) into its symmetric (peer-mapped) payload buffer:
+     pass A + radix top-k + ordered compaction + INT8 block 256;
   2. rank 0 (the coordinator) pulls all N payloads over NVLink with the merge kernels (prepass norms and
      validation with its host round trip, weighted dequant scatter-add into fp32), applies the update and
      writes the new checkpoint (fp32 master + bf16 copy) into every rank's staging buffer with NVLS
@@ -15,8 +19,9 @@ Per (model, top-k), every iteration:
 Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, total = their
 sum (the steps are separated by barriers). Bytes over NVLink: payloads pulled from the N-1 peers plus the
 checkpoint stored through the multicast object (each GPU receives it once).
-Comparison arm per model: delta = snapshot - master, ncclAllReduce(AVG) of the n fp32 values, the same
-apply and bf16 cast on every rank; max over ranks. One JSON line per case on rank 0.
+Comparison arm per model: delta = snapshot - master scaled by its merge weight, ncclAllReduce(SUM) of the
+n fp32 values, the same apply and bf16 cast on every rank; max over ranks. One JSON line per case on
+rank 0.
 """
 from __future__ import annotations
 
@@ -53,7 +58,12 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     n = L.total
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     master = torch.randn(n, device=dev, generator=g) * 0.02
-    snap = master + torch.randn(n, device=dev, generator=g) * 1e-3
+    snap = master + torch.randn(n, device=dev, generator=g) * 1e-4
+    ef0 = torch.randn(n, device=dev, generator=g) * 1e-4
+    hg = torch.Generator().manual_seed(4321)  # same draws on every rank
+    stale = torch.randint(0, 4, (world,), generator=hg).tolist()
+    tokens = torch.randint(100_000, 1_000_001, (world,), generator=hg).tolist()
+    weights = [t * 0.9 ** s for t, s in zip(tokens, stale)]
     cap_max = DeviceCompressor.capacity_for(L, max(topks))
     pay_bytes = (DevicePayload.nbytes(cap_max, 256) + 4095) // 4096 * 4096
     pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes, dev, world)
@@ -77,7 +87,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         t_comp, t_merge, pulled, infos = [], [], 0, None
         for it in range(warmup + iters):
             comp.snap.copy_(snap)
-            comp.ef.zero_()
+            comp.ef.copy_(ef0)
             torch.cuda.synchronize()
             barrier()
             c0, c1 = _events()
@@ -102,7 +112,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                     off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
                     contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q),
                                                  val_ptr=off(payload.val), scales_ptr=off(payload.scales),
-                                                 count=counts[r], block=256, dense=False, weight=1.0,
+                                                 count=counts[r], block=256, dense=False, weight=weights[r],
                                                  node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
                 m0, m1 = _events()
                 m0.record(merger.stream)
@@ -123,6 +133,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                             "total_ms": round(cms + mms, 3), "accepted": infos["accepted"],
                             "payload_bytes_pulled_nvlink": pulled,
                             "checkpoint_bytes_broadcast": n * 6, "broadcast": "nvls multimem" if mc32 else "per-peer",
+                            "staleness": stale, "tokens": tokens,
                             "timing": "CUDA events, median of iters, max over ranks"})
         del comp, payload
     # comparison arm: dense fp32 all-reduce of the same deltas
@@ -136,8 +147,9 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         e0, e1 = _events()
         e0.record()
         torch.sub(snap, master, out=delta)
+        delta.mul_(weights[rank] / sum(weights))  # the same staleness x tokens weights, then a plain sum
         if world > 1:
-            dist.all_reduce(delta, op=dist.ReduceOp.AVG)
+            dist.all_reduce(delta, op=dist.ReduceOp.SUM)
         theta.copy_(snap).sub_(delta)
         ops.cast_bf16(theta, p16t)
         e1.record()

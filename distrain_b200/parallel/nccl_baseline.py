@@ -24,8 +24,11 @@ from .. import ops
 
 
 class NcclDenseSync:
-    def __init__(self, node, run, rank: int, world: int, device, outer_lr: float = 1.0):
+    def __init__(self, node, run, rank: int, world: int, device, outer_lr: float = 1.0, group=None):
+        # world: number of replicas averaged; group: their process group (with tensor parallelism, the
+        # ranks holding the same shard of every replica)
         self.node, self.run, self.rank, self.world = node, run, rank, world
+        self.group = group
         self.eng = node.engine
         self.outer_lr = float(outer_lr)
         self.snap = self.eng.master.clone()
@@ -56,7 +59,7 @@ class NcclDenseSync:
         e0.record(train)
         torch.sub(self.snap, eng.master, out=self.delta)
         if self.world > 1:
-            dist.all_reduce(self.delta, op=dist.ReduceOp.AVG)
+            dist.all_reduce(self.delta, op=dist.ReduceOp.AVG, group=self.group)
         eng.master.copy_(self.snap).sub_(self.delta, alpha=self.outer_lr)
         self.snap.copy_(eng.master)
         ops.cast_bf16(eng.master, eng.p16)

@@ -21,7 +21,7 @@ from ..models.engine import TrainEngine
 
 class InBoxNode:
     def __init__(self, run: RunConfig, rank: int = 0, world: int = 1, device=None, enable_push: bool = True,
-                 attn_impl: str = None):
+                 attn_impl: str = None, tp=None):
         self.run = run
         self.rank, self.world = rank, world
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -30,8 +30,10 @@ class InBoxNode:
         if attn_impl is None:
             import os
             attn_impl = os.environ.get("DT_ATTN_IMPL", "dt")
+        # tp: a TensorParallel group (this node = one model replica split over the group's GPUs)
         self.engine = TrainEngine(run.model, run.micro_batch, run.seq_len, optim=run.optim, device=self.device,
-                                  seed=run.seed, init_std=run.init_std, attn_impl=attn_impl)
+                                  seed=run.seed, init_std=run.init_std, attn_impl=attn_impl, tp=tp,
+                                  act_ckpt=run.activation_checkpointing)
         self.enable_push = enable_push
         self.step_count = 0
         self.round_step = 0
