@@ -378,10 +378,23 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
   a.tiles_n = (N + bn - 1) / bn;
   int tiles = a.tiles_m * a.tiles_n;
   if (split_k <= 0) {
-    // Auto split-K: enough work units to cover every SM when the tile count alone does not.
+    // Auto split-K (accumulating epilogue only): the smallest split whose work units fill >= 90 % of the
+    // last wave of the persistent grid (units / (waves * SMs)), keeping >= 8 K-blocks per split; without
+    // one, the split with the best fill. A power-of-two rule lands e.g. 96 tiles on 192 units = 1.3 waves.
     split_k = 1;
     if (epi == EPI_F32_ATOMIC) {
-      while (tiles * split_k < g_num_sms && split_k * 2 <= a.num_kb / 4) split_k *= 2;
+      auto fill = [&](int sk) {
+        const long long u = (long long)tiles * sk;
+        return (double)u / (double)(((u + g_num_sms - 1) / g_num_sms) * g_num_sms);
+      };
+      int best = 1;
+      double best_fill = fill(1);
+      for (int sk = 1; sk <= 32 && a.num_kb / sk >= 8; ++sk) {
+        const double f = fill(sk);
+        if (f >= 0.9) { best = sk; break; }
+        if (f > best_fill + 1e-9) { best = sk; best_fill = f; }
+      }
+      split_k = best;
     }
   }
   split_k = split_k < 1 ? 1 : (split_k > a.num_kb ? a.num_kb : split_k);

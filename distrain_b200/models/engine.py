@@ -41,7 +41,7 @@ HP_LR, HP_B1, HP_B2, HP_EPS, HP_WD, HP_BC1, HP_BC2, HP_MAXNORM, HP_CLIP_GLOBAL, 
 class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
-                 lm_chunk_rows: int = 8192, attn_impl: str = "dt", tp=None, act_ckpt: bool = False):
+                 lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False):
         self.cfg = cfg
         self.tp = tp
         self.act_ckpt = act_ckpt
@@ -343,15 +343,15 @@ class TrainEngine:
         """Capture one full train step (fwd+bwd+AdamW) as a CUDA graph; replay with ``replay()``."""
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream())
-        # warm-up on the side stream (loads modules, sets smem attributes) without touching weights
-        saved = (self.master.clone(), self.m.clone(), self.v.clone(), self.hp.clone())
+        # warm-up on the side stream (loads modules, sets smem attributes) without touching weights or
+        # optimizer state: the step's loss is marked non-finite, so the optimizer kernels run but skip
+        # the update exactly as for a NaN step (no copies of the state: large presets have no room)
         with torch.cuda.stream(s):
             for _ in range(warmup):
-                self.step_kernels()
+                self.forward_backward()
+                self.loss[1].fill_(1.0)
+                self.optimizer_step()
         torch.cuda.current_stream().wait_stream(s)
-        self.master.copy_(saved[0]); self.m.copy_(saved[1]); self.v.copy_(saved[2]); self.hp.copy_(saved[3])
-        ops.cast_bf16(self.master, self.p16)
-        del saved
         g = torch.cuda.CUDAGraph()
         from ..ops import _lib
         n0 = _lib.LAUNCHES[0]

@@ -74,16 +74,28 @@ class StoreBus:
                 return default
             return self.store.get(key).decode()
 
+    def wait_get(self, k, timeout: float = 60.0):
+        """Blocking read of a key another process is about to set."""
+        t0 = time.time()
+        while True:
+            v = self.get(k)
+            if v is not None:
+                return v
+            if time.time() - t0 > timeout:
+                raise TimeoutError(f"control bus key {self.prefix + k} not set within {timeout} s")
+            time.sleep(0.0005)
 
-def _symm_alloc(nbytes: int, device, world: int):
-    """Symmetric buffer: (local tensor, peer base pointers, multicast pointer)."""
+
+def _symm_alloc(nbytes: int, device, world: int, group=None):
+    """Symmetric buffer over `group` (default: the world): (local tensor, peer base pointers by group rank,
+    multicast pointer)."""
     if world == 1:
         t = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         return t, [t.data_ptr()], 0, None
     import torch.distributed._symmetric_memory as symm_mem
     t = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
     t.zero_()
-    hdl = symm_mem.rendezvous(t, dist.group.WORLD.group_name)
+    hdl = symm_mem.rendezvous(t, (group or dist.group.WORLD).group_name)
     mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
     if os.environ.get("DT_NO_MULTICAST"):
         mc = 0
@@ -91,8 +103,19 @@ def _symm_alloc(nbytes: int, device, world: int):
 
 
 class InBoxSync:
-    def __init__(self, node, run: RunConfig, rank: int, world: int, device):
+    """One node's side of the protocol for one parameter shard.
+
+    Without tensor parallelism a node is one GPU and there is one shard. With tensor parallelism
+    (``n_shards`` = TP size) every rank of a node runs its own instance for its shard over ``dp_group``
+    (the ranks holding that shard on every node): payloads, staging buffers and slot bookkeeping are per
+    shard; the coordinator of shard 0 decides merges and publishes a plan that the coordinators of the
+    other shards execute with the same coefficients (validation and norm clipping on the full-delta
+    norms summed over shards); the ranks of one node swap to a new version at the same step."""
+
+    def __init__(self, node, run: RunConfig, rank: int, world: int, device, shard: int = 0, n_shards: int = 1,
+                 dp_group=None):
         self.node, self.run, self.rank, self.world = node, run, rank, world
+        self.shard, self.n_shards, self.dp_group = shard, n_shards, dp_group
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
@@ -113,15 +136,17 @@ class InBoxSync:
         cap = DeviceCompressor.capacity_for(self.layout, max(cfg.top_k_fraction, 0.0))
         blk = cfg.int8_block if cfg.quantize_int8 else 0
         self.slot_bytes = (DevicePayload.nbytes(cap, blk) + 4095) // 4096 * 4096
-        self.pay_buf, self.pay_ptrs, _, self._pay_h = _symm_alloc(2 * self.slot_bytes, self.device, world)
+        self.pay_buf, self.pay_ptrs, _, self._pay_h = _symm_alloc(2 * self.slot_bytes, self.device, world, dp_group)
         self.slots = [DevicePayload(self.pay_buf[i * self.slot_bytes:(i + 1) * self.slot_bytes], cap, blk)
                       for i in range(2)]
         self.stage_bytes = (self.n * 6 + 4095) // 4096 * 4096
         self.stage_buf, self.stage_ptrs, self.stage_mc, self._stage_h = _symm_alloc(2 * self.stage_bytes, self.device,
-                                                                                   world)
+                                                                                   world, dp_group)
         self.compressor = DeviceCompressor(self.layout, self.device, cfg, payload=self.slots[0])
         self.compressor.reset(eng.master)
-        self.bus = LocalBus() if world == 1 else StoreBus()
+        multi = world * n_shards > 1
+        self.bus = StoreBus(f"dtinbox/s{shard}/" if n_shards > 1 else "dtinbox/") if multi else LocalBus()
+        self.shared = self.bus if n_shards == 1 else StoreBus("dtinbox/shared/")
         self.inflight = None  # (seq, event, slot)
         self.slot_seq = [-1, -1]
         self.ef_ready = None
@@ -132,8 +157,8 @@ class InBoxSync:
         self.latest_version = 0
         self.coord = None
         if rank == 0:
-            self.coord = InBoxCoordinator(self, run, world)
-        if world > 1:
+            self.coord = InBoxCoordinator(self, run, world) if shard == 0 else ShardFollower(self, run, world)
+        if world * n_shards > 1:
             dist.barrier()
 
     # ─────────── helpers ───────────
@@ -161,7 +186,19 @@ class InBoxSync:
 
     # ─────────── step hooks ───────────
     def before_step(self):
-        lv = self.bus.get("version") if (self.node.step_count % 4 == 0) else None
+        lv = None
+        if self.node.step_count % 4 == 0:
+            if self.n_shards == 1:
+                lv = self.bus.get("version")
+            else:
+                # the ranks of one node swap at the same step: shard 0 decides, the others read its decision
+                key = f"swap/{self.rank}/{self.node.step_count}"
+                if self.shard == 0:
+                    lv = self.shared.get("version")
+                    self.shared.set(key, lv if lv is not None else "-1")
+                else:
+                    lv = self.shared.wait_get(key)
+                    lv = None if lv == "-1" else lv
         if lv is not None and int(lv) > self.version:
             self._swap(int(lv))
         # first-round linear warm-up of the inner lr (reference continuous.rs:588-596)
@@ -178,8 +215,27 @@ class InBoxSync:
             warm = max(int(self.run.push_every * self.run.optim.warmup_fraction), 2)
             if self.first_round and self.node.round_step <= warm:
                 return
-            if self._push(partial=False):
+            if self._push_agreed():
                 self.first_round = False
+
+    def _push_agreed(self, partial: bool = False) -> bool:
+        """Push now if this shard can (one shard), or as shard 0 decides for every shard of the node, so
+        the shards' rounds cover the same steps and carry the same sequence numbers."""
+        if self.n_shards == 1:
+            return self._push(partial=partial)
+        key = f"pushdec/{self.rank}/{self.node.step_count}/{int(partial)}"
+        if self.shard == 0:
+            ok = self._push(partial=partial)
+            self.shared.set(key, "1" if ok else "0")
+            return ok
+        if self.shared.wait_get(key) != "1":
+            return False
+        t0 = time.time()
+        while not self._push(partial=partial):  # the slot is released for every shard at once
+            if time.time() - t0 > 60:
+                raise TimeoutError("payload slot of this shard not released")
+            time.sleep(0.0005)
+        return True
 
     def _push(self, partial: bool) -> bool:
         slot = (self.seq + 1) % 2
@@ -248,7 +304,7 @@ class InBoxSync:
 
     def _swap(self, new_version: int):
         if self.node.round_step > 0 and not self.first_round:
-            self._push(partial=True)
+            self._push_agreed(partial=True)
         eng = self.eng
         train = torch.cuda.current_stream()
         s32, s16 = self.stage_views(new_version)
@@ -295,7 +351,12 @@ class InBoxCoordinator:
 
     def __init__(self, sync: InBoxSync, run: RunConfig, world: int):
         self.sync, self.run, self.world = sync, run, world
-        self.bus = sync.bus if world == 1 else StoreBus()
+        ns = sync.n_shards
+        self.bus = sync.bus if isinstance(sync.bus, LocalBus) else StoreBus(sync.bus.prefix)
+        # every shard's bus (slot releases, consumed versions) and the cross-shard bus (plans)
+        self.shard_buses = [self.bus] if ns == 1 else [StoreBus(f"dtinbox/s{t}/") for t in range(ns)]
+        self.shared = self.bus if ns == 1 else StoreBus("dtinbox/shared/")
+        self.attempt = 0
         self.acc = Accumulator(staleness_decay=run.staleness_decay, max_staleness=run.max_staleness,
                                min_contributions=0, checkpoint_version=0)
         for r in range(world):
@@ -315,7 +376,8 @@ class InBoxCoordinator:
         self.thread.start()
 
     def _release(self, rank: int, seq: int):
-        self.bus.set(f"released/{rank}/{seq}", "1")
+        for b in self.shard_buses:
+            b.set(f"released/{rank}/{seq}", "1")
 
     def _ingest(self):
         for r in range(self.world):
@@ -356,13 +418,14 @@ class InBoxCoordinator:
         if need < 1:
             return
         t0 = time.time()
-        for r in range(self.world):
-            while int(self.bus.get(f"consumed/{r}", "0")) < need:
-                if self.stop.is_set():
-                    raise _Shutdown()
-                if time.time() - t0 > timeout:
-                    raise TimeoutError(f"node {r} did not consume version {need}")
-                time.sleep(0.001)
+        for b in self.shard_buses:
+            for r in range(self.world):
+                while int(b.get(f"consumed/{r}", "0")) < need:
+                    if self.stop.is_set():
+                        raise _Shutdown()
+                    if time.time() - t0 > timeout:
+                        raise TimeoutError(f"node {r} did not consume version {need}")
+                    time.sleep(0.001)
 
     def _merge(self):
         snap = self.acc.begin_merge()
@@ -374,10 +437,35 @@ class InBoxCoordinator:
             t0 = time.time()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(self.merger.stream)
-            info = self.merger.merge(contribs, self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16, stage32=p32,
-                                     stage16=p16)
+            ns = self.sync.n_shards
+            self.attempt += 1
+            att = self.attempt
+            if ns > 1:  # the other shards' coordinators run the same merge on their shards
+                self.shared.set(f"plan/{att}", json.dumps({"version": new_version, "members": [
+                    [c.node_id, c.seq_num] for c in snap.contributions]}))
+            stats = self.merger.prepass(contribs)
+            if ns > 1:  # validation and clipping see the full delta: sum the shards' squares
+                for t in range(1, ns):
+                    st = json.loads(self.shared.wait_get(f"stats/{att}/{t}", 120))
+                    for i, (ss, mx, nf) in enumerate(st):
+                        stats[i][0] += ss
+                        stats[i][1] = max(stats[i][1], mx)
+                        stats[i][2] = max(stats[i][2], nf)
+            try:
+                coefs, info = self.merger.plan(contribs, stats)
+            except Exception:
+                if ns > 1:
+                    self.shared.set(f"coefs/{att}", "abort")
+                raise
+            if ns > 1:
+                self.shared.set(f"coefs/{att}", json.dumps(coefs))
+            self.merger.accumulate_apply(contribs, coefs, self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16, stage32=p32,
+                                         stage16=p16)
+            info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
             ev1.record(self.merger.stream)
             ev1.synchronize()
+            for t in range(1, ns):
+                self.shared.wait_get(f"merged/{att}/{t}", 120)
             info["device_ms"] = ev0.elapsed_time(ev1)
             info["wall_ms"] = (time.time() - t0) * 1e3
             info["version"] = new_version
@@ -392,7 +480,7 @@ class InBoxCoordinator:
             self.version = new_version
             tokens = sum(c.tokens_processed for c in snap.contributions)
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
-            self.bus.set("version", str(new_version))
+            self.shared.set("version", str(new_version))
         except _Shutdown:
             self.acc.abort_merge()
             raise
@@ -428,3 +516,73 @@ class InBoxCoordinator:
         self.thread.join(timeout=30)
         if self.error is not None:
             raise RuntimeError(f"coordinator thread failed: {self.error!r}") from self.error
+
+
+class ShardFollower:
+    """Coordinator thread for shard t > 0 (on node 0's rank of that shard): executes the merge plans of the
+    shard-0 coordinator on this shard's payloads - prepass, report the stats, wait for the shared
+    coefficients, accumulate + apply + broadcast into this shard's staging buffers, report completion.
+    Slot releases and version publication are the shard-0 coordinator's."""
+
+    def __init__(self, sync: InBoxSync, run: RunConfig, world: int):
+        self.sync, self.run, self.world = sync, run, world
+        self.bus = StoreBus(sync.bus.prefix)
+        self.shared = StoreBus("dtinbox/shared/")
+        stream = torch.cuda.Stream(device=sync.device, priority=-100)
+        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
+        self.attempt = 0
+        self.merges: List[dict] = []
+        self.failed: List[str] = []
+        self.stop = threading.Event()
+        self.error: Optional[BaseException] = None
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def _contribution(self, node_id: str, seq: int) -> Contribution:
+        r = int(node_id.split("-")[1])
+        body = json.loads(self.bus.wait_get(f"push/{r}/{seq}", 120))
+        s = self.sync
+        p = s.slots[body["_slot"]]
+        base_local = s.pay_buf.data_ptr()
+        peer = s.pay_ptrs[r]
+        off = lambda t: t.data_ptr() - base_local + peer
+        blk = p.block
+        count = body["_count"]
+        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val),
+                            scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
+                            weight=1.0, node_id=node_id, wire_bytes=p.wire_bytes(count))
+
+    def _one(self, att: int, plan: dict):
+        v = plan["version"]
+        contribs = [self._contribution(nid, seq) for nid, seq in plan["members"]]
+        p32, p16, mc32, mc16 = self.sync.stage_peer_ptrs(v)
+        stats = self.merger.prepass(contribs)
+        self.shared.set(f"stats/{att}/{self.sync.shard}", json.dumps(stats))
+        c = self.shared.wait_get(f"coefs/{att}", 120)
+        if c == "abort":
+            self.failed.append(f"attempt {att} aborted by shard 0")
+            return
+        self.merger.accumulate_apply(contribs, json.loads(c), self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16,
+                                     stage32=p32, stage16=p16)
+        self.merger.stream.synchronize()
+        self.merges.append({"version": v, "n_contrib": len(contribs)})
+        self.shared.set(f"merged/{att}/{self.sync.shard}", "1")
+
+    def _loop(self):
+        torch.cuda.set_device(self.sync.device)
+        try:
+            while not self.stop.is_set():
+                raw = self.shared.get(f"plan/{self.attempt + 1}")
+                if raw is None:
+                    time.sleep(0.0005)
+                    continue
+                self.attempt += 1
+                self._one(self.attempt, json.loads(raw))
+        except BaseException as e:  # surfaced by close()
+            self.error = e
+
+    def close(self):
+        self.stop.set()
+        self.thread.join(timeout=30)
+        if self.error is not None:
+            raise RuntimeError(f"shard coordinator thread failed: {self.error!r}") from self.error

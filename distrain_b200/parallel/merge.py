@@ -162,21 +162,20 @@ class DeviceMerger:
         st.synchronize()
         return self.stats_host[:3 * n].view(n, 3).tolist()
 
-    def merge(self, contribs: List[Contribution], outer_lr: float, outer_momentum: float, mc32: int = 0,
-              mc16: int = 0, stage32: Sequence[int] = (), stage16: Sequence[int] = (), write_bf16: bool = True):
-        """Full merge on ``self.stream``; blocks the calling (coordinator) thread on the prepass only.
-        Returns an info dict (accepted, rejected, norms, nvlink bytes)."""
-        from ..ops._lib import check
-        import ctypes
+    def prepass(self, contribs: List[Contribution]) -> List[List[float]]:
+        """Per-contribution [sum of squares, max |x|, non-finite flag] of the dequantised payloads; blocks the
+        calling (coordinator) thread until they are on the host."""
         n = len(contribs)
         assert 0 < n <= 64
-        st = self.stream
-        sp = st.cuda_stream
-        maxc = max(c.count for c in contribs)
-        s = self._prepass(contribs, maxc)
-        valid, norms = [], []
-        reasons = []
-        for i, (sumsq, mx, nf) in enumerate(s):
+        return self._prepass(contribs, max(c.count for c in contribs))
+
+    @staticmethod
+    def plan(contribs: List[Contribution], stats: List[List[float]]):
+        """Validation, norm clipping in arrival order and weighting from (possibly shard-combined) stats:
+        returns (coefficient per contribution, info). Raises when no contribution is valid."""
+        n = len(contribs)
+        valid, norms, reasons = [], [], []
+        for i, (sumsq, mx, nf) in enumerate(stats):
             r = validate_stats(sumsq, mx, nf > 0, empty=contribs[i].count == 0)
             reasons.append(r)
             if r is None:
@@ -189,6 +188,19 @@ class DeviceMerger:
         coefs = [0.0] * n
         for j, i in enumerate(valid):
             coefs[i] = contribs[i].weight / wsum * scales[j]
+        return coefs, {"accepted": len(valid), "rejected": n - len(valid), "reasons": reasons,
+                       "per_delta_norms": eff, "coefs": coefs}
+
+    def accumulate_apply(self, contribs: List[Contribution], coefs: List[float], outer_lr: float,
+                         outer_momentum: float, mc32: int = 0, mc16: int = 0, stage32: Sequence[int] = (),
+                         stage16: Sequence[int] = (), write_bf16: bool = True):
+        """Weighted dequant scatter-add of every payload, then apply + broadcast, enqueued on the merge stream."""
+        from ..ops._lib import check
+        import ctypes
+        n = len(contribs)
+        st = self.stream
+        sp = st.cuda_stream
+        maxc = max(c.count for c in contribs)
         s32 = (ctypes.c_void_p * max(len(stage32), 1))(*stage32) if stage32 else None
         s16 = (ctypes.c_void_p * max(len(stage16), 1))(*stage16) if stage16 else None
         buf = self._pack(contribs, coefs)
@@ -199,6 +211,13 @@ class DeviceMerger:
                                                   self.acc.data_ptr(), self.n, float(outer_lr), float(outer_momentum),
                                                   mc32 or None, mc16 or None, s32, s16, len(stage32),
                                                   int(write_bf16), sp), "dt_merge_apply_broadcast")
-        pulled = sum(contribs[i].wire_bytes for i in range(n))
-        return {"accepted": len(valid), "rejected": n - len(valid), "reasons": reasons,
-                "per_delta_norms": eff, "coefs": coefs, "pulled_bytes": pulled}
+
+    def merge(self, contribs: List[Contribution], outer_lr: float, outer_momentum: float, mc32: int = 0,
+              mc16: int = 0, stage32: Sequence[int] = (), stage16: Sequence[int] = (), write_bf16: bool = True):
+        """Full merge on ``self.stream``; blocks the calling (coordinator) thread on the prepass only.
+        Returns an info dict (accepted, rejected, norms, nvlink bytes)."""
+        n = len(contribs)
+        coefs, info = self.plan(contribs, self.prepass(contribs))
+        self.accumulate_apply(contribs, coefs, outer_lr, outer_momentum, mc32, mc16, stage32, stage16, write_bf16)
+        info["pulled_bytes"] = sum(contribs[i].wire_bytes for i in range(n))
+        return info
