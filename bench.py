@@ -37,6 +37,7 @@ def _parse():
     ap.add_argument("--config", default="tiny")
     ap.add_argument("--impl", default="dt", choices=["dt", "reference"])
     ap.add_argument("--push-every", type=int, default=None)
+    ap.add_argument("--tp", type=int, default=None, help="tensor-parallel size per node (default: the preset's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-push", action="store_true", help="train only (no compression / merge)")
     ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
@@ -128,6 +129,8 @@ def main():
     run = bench_config(args.config)
     if args.push_every:
         run.push_every = args.push_every
+    if args.tp:
+        run.tp = args.tp
     nccl_arm = args.sync == "nccl" and not args.no_push
     # tensor parallelism: node k = ranks [k*tp, (k+1)*tp); its shards are averaged across nodes by the
     # groups of ranks that hold the same shard
@@ -141,13 +144,11 @@ def main():
         tp = TensorParallel(tp_groups[rank // tp_size], rank % tp_size, tp_size, mode=args.tp_mode,
                             rows=run.micro_batch * (run.seq_len - 1), hidden=run.model.hidden_dim, device=dev)
         dp_group = dp_groups[rank % tp_size]
-        if not (args.no_push or nccl_arm):
-            print("note: the in-box compressed-delta protocol runs one node per GPU; with tensor parallelism the "
-                  "nodes are synchronised by the NCCL dense-delta arm", file=sys.stderr)
-            nccl_arm = True
     node_rank, n_nodes = rank // tp_size, world // tp_size
+    # with tensor parallelism every rank runs the protocol for its shard over its dp group
     node = InBoxNode(run, rank=node_rank, world=n_nodes, device=dev,
-                     enable_push=not args.no_push and not nccl_arm, tp=tp)
+                     enable_push=not args.no_push and not nccl_arm, tp=tp,
+                     shard=rank % tp_size, n_shards=tp_size, dp_group=dp_group)
     if nccl_arm:
         from distrain_b200.parallel.nccl_baseline import NcclDenseSync
         node.sync = NcclDenseSync(node, run, node_rank, n_nodes, dev, group=dp_group)

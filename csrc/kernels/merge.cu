@@ -170,20 +170,29 @@ __global__ void apply_broadcast_kernel(float* __restrict__ theta, float* __restr
 }
 
 // Node side of a checkpoint swap: master <- stage32, p16 <- stage16 (or cast), snapshot <- master.
+// Checkpoint swap. rebase == 0: master = snap = staged fp32, p16 = staged bf16 (or its cast).
+// rebase == 1: the steps trained since the last push are carried onto the new checkpoint:
+// master = staged + (master - snap), snap = staged, p16 = bf16(master).
 __global__ void swap_in_kernel(const float* __restrict__ s32, const __nv_bfloat16* __restrict__ s16,
                                float* __restrict__ master, __nv_bfloat16* __restrict__ p16, float* __restrict__ snap,
-                               long long n) {
+                               long long n, int rebase) {
   const long long n4 = n / 4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     float4 t = reinterpret_cast<const float4*>(s32)[i];
-    reinterpret_cast<float4*>(master)[i] = t;
+    float4 w = t;
+    if (rebase) {
+      const float4 m = reinterpret_cast<const float4*>(master)[i];
+      const float4 o = reinterpret_cast<const float4*>(snap)[i];
+      w = make_float4(t.x + (m.x - o.x), t.y + (m.y - o.y), t.z + (m.z - o.z), t.w + (m.w - o.w));
+    }
+    reinterpret_cast<float4*>(master)[i] = w;
     if (snap) reinterpret_cast<float4*>(snap)[i] = t;
-    if (s16) {
+    if (s16 && !rebase) {
       reinterpret_cast<uint2*>(p16)[i] = reinterpret_cast<const uint2*>(s16)[i];
     } else {
       uint2 h;
-      h.x = pack_bf16(t.x, t.y);
-      h.y = pack_bf16(t.z, t.w);
+      h.x = pack_bf16(w.x, w.y);
+      h.y = pack_bf16(w.z, w.w);
       reinterpret_cast<uint2*>(p16)[i] = h;
     }
   }
@@ -242,9 +251,11 @@ DT_API int dt_merge_apply_broadcast(float* theta, float* vel, float* acc, long l
 }
 
 DT_API int dt_swap_in(const float* s32, const void* s16, float* master, void* p16, float* snap, long long n,
-                      cudaStream_t st) {
+                      int rebase, cudaStream_t st) {
   if (n % 4) return -10;
+  if (rebase && !snap) return -11;
   swap_in_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(s32, reinterpret_cast<const __nv_bfloat16*>(s16),
-                                                               master, reinterpret_cast<__nv_bfloat16*>(p16), snap, n);
+                                                               master, reinterpret_cast<__nv_bfloat16*>(p16), snap, n,
+                                                               rebase);
   return (int)cudaGetLastError();
 }

@@ -60,6 +60,9 @@ def main():
     ap.add_argument("--data", default="markov", choices=["markov", "uniform"])
     ap.add_argument("--push-every", type=int, default=None)
     ap.add_argument("--eval-batches", type=int, default=4)
+    ap.add_argument("--swap-mode", default=None, choices=["push_partial", "rebase"])
+    ap.add_argument("--ef-on-swap", default=None, choices=["keep", "reset"])
+    ap.add_argument("--keep-optimizer", action="store_true", help="keep the AdamW state across checkpoint swaps")
     a = ap.parse_args()
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from distrain_b200.config import bench_config
@@ -77,6 +80,12 @@ def main():
     run = bench_config(a.config)
     if a.push_every:
         run.push_every = a.push_every
+    if a.swap_mode:
+        run.swap_mode = a.swap_mode
+    if a.ef_on_swap:
+        run.ef_on_swap = a.ef_on_swap
+    if a.keep_optimizer:
+        run.reset_optimizer_on_swap = False
     node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=world > 1)
     B, S, V = run.micro_batch, run.seq_len, run.model.vocab_size
     mk = (lambda seed: MarkovTokens(V, B, S, seed)) if a.data == "markov" else \
@@ -116,6 +125,9 @@ def main():
                "tokens_total": a.steps * B * (S - 1) * world, "heldout_loss_max": round(float(held[0]), 4),
                "heldout_loss_mean": round(float(held[1]), 4), "train_loss_last20": round(sum(tail) / len(tail), 4),
                "merges": merges, "global_version": version, "push_every": run.push_every if world > 1 else None}
+        if world > 1:
+            out.update(swap_mode=run.swap_mode, ef_on_swap=run.ef_on_swap,
+                       reset_optimizer_on_swap=run.reset_optimizer_on_swap)
         if a.data == "markov":
             out["entropy_floor"] = round(gen.entropy(), 4)
         else:

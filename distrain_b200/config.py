@@ -294,6 +294,17 @@ class RunConfig(_Json):
     max_staleness: int = 10
     init_std: float = 0.02
     seed: int = 0
+    # What a node does with the steps it trained since its last push when a new checkpoint arrives:
+    # "push_partial" pushes them as a partial round and replaces its weights with the checkpoint (the
+    # reference node, continuous.rs:458-502); "rebase" carries them onto the new checkpoint
+    # (weights = checkpoint + (weights - round start)) and keeps the round going, so every push covers
+    # `push_every` steps even when checkpoints arrive within a step of a push.
+    swap_mode: str = "push_partial"
+    # error-feedback buffer at a checkpoint swap: "keep" (the reference node keeps 100%,
+    # continuous.rs:489-493) or "reset"
+    ef_on_swap: str = "keep"
+    # re-create the inner AdamW state at a swap (the reference node does, continuous.rs:407-414)
+    reset_optimizer_on_swap: bool = True
 
 
 def bench_config(name: str) -> RunConfig:

@@ -16,8 +16,9 @@ weights), and when the trigger fires run the peer-pull merge kernels on a top-pr
 publish the new version. A payload slot is released once its contribution is merged, replaced or
 rejected; a node whose next slot is still in use defers the push by a step instead of blocking.
 
-Swap (node, reference continuous.rs:458-502): on a new version push the partial round, copy the
-staged checkpoint into the master / bf16 buffers, reset AdamW and the error-feedback buffer.
+Swap (node, reference continuous.rs:458-502): on a new version push the partial round and copy the
+staged checkpoint into the master / bf16 buffers (or, with ``swap_mode="rebase"``, carry the steps since
+the last push onto it); re-create AdamW; keep (reference) or clear the error-feedback buffer.
 """
 from __future__ import annotations
 
@@ -303,32 +304,36 @@ class InBoxSync:
             self.bus.set(f"pushseq/{self.rank}", str(meta.seq_num))
 
     def _swap(self, new_version: int):
-        if self.node.round_step > 0 and not self.first_round:
+        run = self.run
+        rebase = run.swap_mode == "rebase"
+        if not rebase and self.node.round_step > 0 and not self.first_round:
             self._push_agreed(partial=True)
         eng = self.eng
         train = torch.cuda.current_stream()
         s32, s16 = self.stage_views(new_version)
-        from ..ops._lib import check, stream_ptr, lib, register, c_void, c_ll
-        register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_void])
+        from ..ops._lib import check, stream_ptr, lib, register, c_void, c_ll, c_int
+        register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
         check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), eng.master.data_ptr(), eng.p16.data_ptr(),
-                               self.compressor.snap.data_ptr(), self.n, stream_ptr(train)), "dt_swap_in")
-        # AdamW is re-created on a checkpoint swap (reference continuous.rs:407-414)
-        eng.m.zero_()
-        eng.v.zero_()
-        eng.hp[9:11].zero_()
-        # error feedback reset at the checkpoint boundary, after any in-flight compression read it
-        ev = torch.cuda.Event()
-        ev.record(train)
-        self.comp_stream.wait_event(ev)
-        with torch.cuda.stream(self.comp_stream):
-            self.compressor.ef.zero_()
-        ev2 = torch.cuda.Event()
-        ev2.record(self.comp_stream)
-        self.ef_ready = ev2
+                               self.compressor.snap.data_ptr(), self.n, int(rebase), stream_ptr(train)), "dt_swap_in")
+        if run.reset_optimizer_on_swap:  # AdamW re-created (reference continuous.rs:407-414)
+            eng.m.zero_()
+            eng.v.zero_()
+            eng.hp[9:11].zero_()
+        if run.ef_on_swap == "reset":
+            # cleared after any in-flight compression has read it
+            ev = torch.cuda.Event()
+            ev.record(train)
+            self.comp_stream.wait_event(ev)
+            with torch.cuda.stream(self.comp_stream):
+                self.compressor.ef.zero_()
+            ev2 = torch.cuda.Event()
+            ev2.record(self.comp_stream)
+            self.ef_ready = ev2
         self.version = new_version
-        self.node.round_step = 0
-        self.round_tokens = 0
-        self.round_t0 = time.time()
+        if not rebase:  # a new round starts at the checkpoint; a rebased round keeps counting
+            self.node.round_step = 0
+            self.round_tokens = 0
+            self.round_t0 = time.time()
         ev_done = torch.cuda.Event()
         ev_done.record(train)
         ev_done.synchronize()

@@ -4,7 +4,7 @@
 (node/cli/src/continuous.rs:379-675): train continuously, every ``push_every`` steps extract the
 round delta (round-start snapshot - current master), compress it with error feedback and hand it to
 the coordinator without stalling the training stream; when a new global checkpoint arrives, push the
-partial round, swap weights, reset AdamW and the error-feedback buffer, and start a new round.
+partial round (or rebase it onto the checkpoint), swap weights, re-create AdamW, and start a new round.
 
 The data plane is device memory: compressed payloads sit in symmetric (peer-mapped) buffers that the
 coordinator's merge kernel reads over NVLink, and new checkpoints are written into every node's
@@ -21,7 +21,7 @@ from ..models.engine import TrainEngine
 
 class InBoxNode:
     def __init__(self, run: RunConfig, rank: int = 0, world: int = 1, device=None, enable_push: bool = True,
-                 attn_impl: str = None, tp=None):
+                 attn_impl: str = None, tp=None, shard: int = 0, n_shards: int = 1, dp_group=None):
         self.run = run
         self.rank, self.world = rank, world
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -30,7 +30,9 @@ class InBoxNode:
         if attn_impl is None:
             import os
             attn_impl = os.environ.get("DT_ATTN_IMPL", "dt")
-        # tp: a TensorParallel group (this node = one model replica split over the group's GPUs)
+        # tp: a TensorParallel group (this node = one model replica split over the group's GPUs); rank and
+        # world then count nodes, and this process runs the protocol for parameter shard `shard` of
+        # `n_shards` over `dp_group` (the ranks that hold that shard on every node)
         self.engine = TrainEngine(run.model, run.micro_batch, run.seq_len, optim=run.optim, device=self.device,
                                   seed=run.seed, init_std=run.init_std, attn_impl=attn_impl, tp=tp,
                                   act_ckpt=run.activation_checkpointing)
@@ -41,7 +43,8 @@ class InBoxNode:
         self.sync = None
         if enable_push:
             from .inbox import InBoxSync
-            self.sync = InBoxSync(self, run, rank, world, self.device)
+            self.sync = InBoxSync(self, run, rank, world, self.device, shard=shard, n_shards=n_shards,
+                                  dp_group=dp_group)
 
     # ── training ──
     def _ensure_graph(self):

@@ -141,3 +141,57 @@ def test_inbox_single_gpu_protocol():
     assert m["accepted"] == 1 and m["pulled_bytes"] > 0
     assert losses[-1] < losses[0]
     node.close()
+
+
+@pytest.mark.parametrize("rebase", [0, 1])
+def test_swap_in_kernel(rebase):
+    """Checkpoint swap against its fp32 definition: replace (master = snap = staged) or rebase
+    (master = staged + master - snap, snap = staged), bf16 copy of the new master."""
+    from distrain_b200.ops._lib import lib, register, check, c_void, c_ll, c_int, stream_ptr
+    register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
+    n = 1 << 20
+    g = torch.Generator(device="cuda").manual_seed(5)
+    s32 = torch.randn(n, device="cuda", generator=g)
+    s16 = s32.bfloat16()
+    master = torch.randn(n, device="cuda", generator=g)
+    snap = master - 1e-3 * torch.randn(n, device="cuda", generator=g)
+    want = (s32.double() + (master.double() - snap.double())).float() if rebase else s32.clone()
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), master.data_ptr(), p16.data_ptr(), snap.data_ptr(), n,
+                           rebase, stream_ptr(torch.cuda.current_stream())), "dt_swap_in")
+    torch.cuda.synchronize()
+    assert torch.allclose(master, want, atol=1e-6, rtol=1e-6)
+    assert torch.equal(snap, s32)
+    assert torch.equal(p16, master.bfloat16())
+
+
+@pytest.mark.parametrize("swap_mode,ef_on_swap", [("push_partial", "keep"), ("rebase", "keep"),
+                                                  ("push_partial", "reset")])
+def test_inbox_swap_policies(swap_mode, ef_on_swap):
+    """The swap policies run the protocol end to end on one GPU (rebase keeps whole rounds: every push
+    after the first covers push_every steps)."""
+    from distrain_b200.config import bench_config
+    from distrain_b200.parallel.node import InBoxNode
+    run = bench_config("micro")
+    run.model.vocab_size = 512
+    run.push_every = 6
+    run.optim.lr = 3e-3
+    run.swap_mode, run.ef_on_swap = swap_mode, ef_on_swap
+    node = InBoxNode(run, rank=0, world=1, device=torch.device("cuda"), enable_push=True)
+    g = torch.Generator().manual_seed(0)
+    batch = torch.randint(0, 512, (run.micro_batch, run.seq_len), generator=g, dtype=torch.int32).cuda()
+    losses = []
+    for i in range(60):
+        node.train_step_device(batch)
+        losses.append(node.engine.loss[0].item())
+    import json
+    import time
+    time.sleep(0.5)
+    coord = node.sync.coord
+    assert coord.error is None, repr(coord.error)
+    assert len(coord.merges) >= 3 and node.sync.version >= 2
+    assert losses[-1] < losses[0]
+    if swap_mode == "rebase":
+        steps = [json.loads(node.sync.bus.get(f"push/0/{s}"))["inner_steps"] for s in range(1, node.sync.seq + 1)]
+        assert all(s >= run.push_every for s in steps), steps
+    node.close()
