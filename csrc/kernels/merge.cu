@@ -2,15 +2,17 @@
 //
 //   pre-pass   per contribution: ||decoded delta||^2, max|x|, non-finite count   (validate_delta,
 //              compression.rs:388-424, and the 3x running-average norm clip inputs, aggregation.rs:310-328)
-//   accumulate acc[idx] += coef_c * q * scale[blk]   for every kept entry of every accepted contribution,
+//   accumulate dst[idx] += coef_c * q * scale[blk]   for every kept entry of every accepted contribution,
 //              coef_c = clip_c * w_c / sum(w) with w_c = tokens_c * 0.9^staleness_c (weighted_average_gpu,
 //              aggregation.rs:28-61). Payloads are read with plain loads straight out of each node's
 //              GPU memory (peer pointers of a symmetric allocation, NVLink P2P) - no staging copy.
-//   apply      v' = mu*v + acc ; theta -= lr*(mu*v' + acc)   (nesterov_step_gpu, aggregation.rs:64-105;
-//              lr 1, mu 0 => theta -= acc, the unscaled merged delta)
-//              fused with the fp32->bf16 cast and the broadcast of the new checkpoint into every
-//              node's staging buffers: one multimem.st per 16 bytes through an NVLS multicast object
-//              (or one store per peer when no multicast object exists), then acc is cleared.
+//              Without outer momentum (the reference's setting, aggregation.rs:364) dst is the checkpoint
+//              itself and coef_c carries the factor -outer_lr: theta -= lr * merged delta, in place, with
+//              no dense accumulator.
+//   broadcast  the new fp32 checkpoint into every node's staging buffer: one multimem.st per 16 bytes
+//              through an NVLS multicast object (or one store per peer when no multicast object exists).
+//   apply      (outer momentum only) v' = mu*v + acc ; theta -= lr*(mu*v' + acc) (nesterov_step_gpu,
+//              aggregation.rs:64-105) fused with the broadcast; acc is cleared.
 #include "common.cuh"
 #include <cstring>
 
@@ -116,15 +118,22 @@ __device__ __forceinline__ void mc_store_v4(void* mc_addr, float4 v) {
 
 struct Dests {
   float* stage32[8];
-  __nv_bfloat16* stage16[8];
   int n;
 };
 
-// theta, vel, acc: local fp32 [n] (n a multiple of 4). Broadcast targets: multicast addresses
-// (mc32/mc16 non-null) or per-peer pointers in `d`.
+__device__ __forceinline__ void store_dests(float* mc32, const Dests& d, const float* self, long long i, float4 t) {
+  if (mc32) {
+    mc_store_v4(reinterpret_cast<float4*>(mc32) + i, t);
+  } else {
+    for (int r = 0; r < d.n; ++r)
+      if (d.stage32[r] != self) reinterpret_cast<float4*>(d.stage32[r])[i] = t;
+  }
+}
+
+// theta, vel, acc: local fp32 [n] (n a multiple of 4). Broadcast targets: a multicast address (mc32
+// non-null) or per-peer pointers in `d`.
 __global__ void apply_broadcast_kernel(float* __restrict__ theta, float* __restrict__ vel, float* __restrict__ acc,
-                                       long long n, float lr, float mu, float* mc32, __nv_bfloat16* mc16, Dests d,
-                                       int write_bf16) {
+                                       long long n, float lr, float mu, float* mc32, Dests d) {
   const long long n4 = n / 4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     float4 a = reinterpret_cast<float4*>(acc)[i];
@@ -146,24 +155,27 @@ __global__ void apply_broadcast_kernel(float* __restrict__ theta, float* __restr
     }
     reinterpret_cast<float4*>(theta)[i] = t;
     reinterpret_cast<float4*>(acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    uint2 h;
-    h.x = pack_bf16(t.x, t.y);
-    h.y = pack_bf16(t.z, t.w);
-    if (mc32) {
-      mc_store_v4(reinterpret_cast<float4*>(mc32) + i, t);
-    } else {
-      for (int r = 0; r < d.n; ++r) reinterpret_cast<float4*>(d.stage32[r])[i] = t;
+    store_dests(mc32, d, theta, i, t);
+  }
+  __threadfence_system();
+}
+
+// theta (already updated in place) -> every node's staging buffer. When theta is this GPU's own staging
+// buffer, the multicast store rewrites the local copy with the value just read from it.
+__global__ void broadcast_kernel(const float* __restrict__ theta, long long n, float* mc32, Dests d) {
+  const long long n4 = n / 4;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < n4; i0 += stride * MUNR) {
+    float4 t[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < n4) t[u] = reinterpret_cast<const float4*>(theta)[i];
     }
-    if (write_bf16) {
-      if (mc16) {
-        // two consecutive float4-index groups share one 16-byte bf16 store: pair threads via shuffle-free
-        // 8-byte stores are not multimem-capable, so use a v2.f32 multimem store of the packed pair
-        asm volatile("multimem.st.global.v2.f32 [%0], {%1, %2};" ::"l"(reinterpret_cast<uint2*>(mc16) + i),
-                     "f"(__uint_as_float(h.x)), "f"(__uint_as_float(h.y))
-                     : "memory");
-      } else {
-        for (int r = 0; r < d.n; ++r) reinterpret_cast<uint2*>(d.stage16[r])[i] = h;
-      }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < n4) store_dests(mc32, d, theta, i, t[u]);
     }
   }
   __threadfence_system();
@@ -172,10 +184,14 @@ __global__ void apply_broadcast_kernel(float* __restrict__ theta, float* __restr
 // Node side of a checkpoint swap: master <- stage32, p16 <- stage16 (or cast), snapshot <- master.
 // Checkpoint swap. rebase == 0: master = snap = staged fp32, p16 = staged bf16 (or its cast).
 // rebase == 1: the steps trained since the last push are carried onto the new checkpoint:
-// master = staged + (master - snap), snap = staged, p16 = bf16(master).
+// master = staged + (master - snap), snap = staged.
+// ef != nullptr folds the error-feedback residual (the part of this node's delta not transmitted yet,
+// in "subtract to apply" convention) into the weights: master -= ef, ef = 0. The next delta then
+// carries the residual by itself, so what a node transmits is unchanged while it trains on its own
+// full progress. p16 = bf16(master) whenever master differs from the staged checkpoint.
 __global__ void swap_in_kernel(const float* __restrict__ s32, const __nv_bfloat16* __restrict__ s16,
                                float* __restrict__ master, __nv_bfloat16* __restrict__ p16, float* __restrict__ snap,
-                               long long n, int rebase) {
+                               float* __restrict__ ef, long long n, int rebase) {
   const long long n4 = n / 4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     float4 t = reinterpret_cast<const float4*>(s32)[i];
@@ -185,9 +201,14 @@ __global__ void swap_in_kernel(const float* __restrict__ s32, const __nv_bfloat1
       const float4 o = reinterpret_cast<const float4*>(snap)[i];
       w = make_float4(t.x + (m.x - o.x), t.y + (m.y - o.y), t.z + (m.z - o.z), t.w + (m.w - o.w));
     }
+    if (ef) {
+      const float4 e = reinterpret_cast<const float4*>(ef)[i];
+      w = make_float4(w.x - e.x, w.y - e.y, w.z - e.z, w.w - e.w);
+      reinterpret_cast<float4*>(ef)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     reinterpret_cast<float4*>(master)[i] = w;
     if (snap) reinterpret_cast<float4*>(snap)[i] = t;
-    if (s16 && !rebase) {
+    if (s16 && !rebase && !ef) {
       reinterpret_cast<uint2*>(p16)[i] = reinterpret_cast<const uint2*>(s16)[i];
     } else {
       uint2 h;
@@ -231,31 +252,41 @@ DT_API int dt_merge_accumulate(const void* contribs, int n, long long max_count,
   return (int)cudaGetLastError();
 }
 
-// stage32/stage16: host arrays of n_dest device pointers (peer-mapped), used when mc32 is null.
-DT_API int dt_merge_apply_broadcast(float* theta, float* vel, float* acc, long long n, float lr, float mu, void* mc32,
-                                    void* mc16, void* const* stage32, void* const* stage16, int n_dest,
-                                    int write_bf16, cudaStream_t st) {
-  if (n % 4) return -10;
+// stage32: host array of n_dest device pointers (peer-mapped), used when mc32 is null.
+static int make_dests(Dests& d, void* mc32, void* const* stage32, int n_dest) {
   if (n_dest > 8) return -11;
-  Dests d = {};
+  d = Dests{};
   d.n = mc32 ? 0 : n_dest;
-  for (int r = 0; r < d.n; ++r) {
-    d.stage32[r] = reinterpret_cast<float*>(stage32[r]);
-    d.stage16[r] = stage16 ? reinterpret_cast<__nv_bfloat16*>(stage16[r]) : nullptr;
-  }
-  if (!mc32 && write_bf16 && !stage16) return -12;
-  apply_broadcast_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(
-      theta, vel, acc, n, lr, mu, reinterpret_cast<float*>(mc32), reinterpret_cast<__nv_bfloat16*>(mc16), d,
-      write_bf16);
+  if (!mc32 && (!stage32 || n_dest <= 0)) return -12;
+  for (int r = 0; r < d.n; ++r) d.stage32[r] = reinterpret_cast<float*>(stage32[r]);
+  return 0;
+}
+
+DT_API int dt_merge_apply_broadcast(float* theta, float* vel, float* acc, long long n, float lr, float mu, void* mc32,
+                                    void* const* stage32, int n_dest, cudaStream_t st) {
+  if (n % 4) return -10;
+  Dests d;
+  if (int e = make_dests(d, mc32, stage32, n_dest)) return e;
+  apply_broadcast_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(theta, vel, acc, n, lr, mu,
+                                                                        reinterpret_cast<float*>(mc32), d);
   return (int)cudaGetLastError();
 }
 
-DT_API int dt_swap_in(const float* s32, const void* s16, float* master, void* p16, float* snap, long long n,
-                      int rebase, cudaStream_t st) {
+DT_API int dt_merge_broadcast(const float* theta, long long n, void* mc32, void* const* stage32, int n_dest,
+                              cudaStream_t st) {
   if (n % 4) return -10;
-  if (rebase && !snap) return -11;
+  Dests d;
+  if (int e = make_dests(d, mc32, stage32, n_dest)) return e;
+  broadcast_kernel<<<grid_cap(n / 4 / MUNR, 256, 148 * 8), 256, 0, st>>>(theta, n, reinterpret_cast<float*>(mc32), d);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_swap_in(const float* s32, const void* s16, float* master, void* p16, float* snap, float* ef,
+                      long long n, int rebase, cudaStream_t st) {
+  if (n % 4) return -10;
+  if ((rebase || ef) && !snap) return -11;
   swap_in_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(s32, reinterpret_cast<const __nv_bfloat16*>(s16),
-                                                               master, reinterpret_cast<__nv_bfloat16*>(p16), snap, n,
-                                                               rebase);
+                                                               master, reinterpret_cast<__nv_bfloat16*>(p16), snap, ef,
+                                                               n, rebase);
   return (int)cudaGetLastError();
 }

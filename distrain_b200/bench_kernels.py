@@ -168,7 +168,7 @@ def compress_cases(iters):
 def merge_cases(iters):
     """Coordinator merge of 8 compressed deltas of the tiny model held in this GPU's memory (the same
     kernels read peer memory in the multi-GPU run): prepass (validation norms) + weighted dequant
-    scatter-add + apply with fp32 / bf16 writes to one destination's staging buffers. Reported per
+    scatter-add into the checkpoint + fp32 broadcast to one destination's staging buffer. Reported per
     merge, including the host round trip of the prepass."""
     from distrain_b200.config import preset, CompressionConfig
     from distrain_b200.models.params import ParamLayout
@@ -195,17 +195,16 @@ def merge_cases(iters):
                                          scales_ptr=p.scales.data_ptr(), count=cnt, block=256, dense=False,
                                          weight=1000.0 * (i + 1), wire_bytes=cnt * 5 + (cnt + 255) // 256 * 4))
         m = DeviceMerger(L.total, dev, master)
-        s32 = torch.empty(L.total, device=dev)  # one destination node's staging buffers (fp32 master, bf16)
-        s16 = torch.empty(L.total, device=dev, dtype=torch.bfloat16)
+        s32 = torch.empty(L.total, device=dev)  # one destination node's staging buffer
 
         def run():
-            m.merge(contribs, 1.0, 0.0, stage32=[s32.data_ptr()], stage16=[s16.data_ptr()])
+            m.merge(contribs, 1.0, stage32=[s32.data_ptr()])
             m.stream.synchronize()
         ms = time_it(run, iters, warmup=2)
         wire = sum(c.wire_bytes for c in contribs)
         out.append({"kernel": "merge_pipeline", "case": f"8 x tiny {L.num_params() / 1e6:.0f}M top-k {k:.0%}",
                     "ms": round(ms, 3), "payload_mb": round(wire / 1e6, 1)})
-        del comp, m, pays, s32, s16
+        del comp, m, pays, s32
     return out
 
 

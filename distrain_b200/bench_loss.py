@@ -61,8 +61,12 @@ def main():
     ap.add_argument("--push-every", type=int, default=None)
     ap.add_argument("--eval-batches", type=int, default=4)
     ap.add_argument("--swap-mode", default=None, choices=["push_partial", "rebase"])
-    ap.add_argument("--ef-on-swap", default=None, choices=["keep", "reset"])
-    ap.add_argument("--keep-optimizer", action="store_true", help="keep the AdamW state across checkpoint swaps")
+    ap.add_argument("--ef-on-swap", default=None, choices=["keep", "reset", "fold"])
+    ap.add_argument("--reset-optimizer", default=None, choices=["yes", "no"],
+                    help="re-create the AdamW state at checkpoint swaps (the reference node does)")
+    ap.add_argument("--topk", type=float, default=None, help="top-k fraction of the delta compression")
+    ap.add_argument("--sync", default="inbox", choices=["inbox", "nccl"],
+                    help="inbox: the compressed asynchronous protocol; nccl: dense synchronous delta averaging")
     a = ap.parse_args()
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from distrain_b200.config import bench_config
@@ -84,9 +88,14 @@ def main():
         run.swap_mode = a.swap_mode
     if a.ef_on_swap:
         run.ef_on_swap = a.ef_on_swap
-    if a.keep_optimizer:
-        run.reset_optimizer_on_swap = False
-    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=world > 1)
+    if a.reset_optimizer:
+        run.reset_optimizer_on_swap = a.reset_optimizer == "yes"
+    if a.topk:
+        run.compression.top_k_fraction = a.topk
+    node = InBoxNode(run, rank=rank, world=world, device=dev, enable_push=world > 1 and a.sync == "inbox")
+    if world > 1 and a.sync == "nccl":
+        from distrain_b200.parallel.nccl_baseline import NcclDenseSync
+        node.sync = NcclDenseSync(node, run, rank, world, dev)
     B, S, V = run.micro_batch, run.seq_len, run.model.vocab_size
     mk = (lambda seed: MarkovTokens(V, B, S, seed)) if a.data == "markov" else \
         (lambda seed: SyntheticTokens(V, B, S, seed))
@@ -97,7 +106,12 @@ def main():
         losses.extend(node.train_steps_e2e([ring[i % 2]], 1))
         ring[i % 2] = gen.next_batch().pin_memory()  # next batch prepared while the GPU runs
     torch.cuda.synchronize()
-    merges = len(node.sync.coord.merges) if (node.sync is not None and node.sync.coord is not None) else 0
+    merges = 0
+    if node.sync is not None:
+        if a.sync == "nccl":
+            merges = len(node.sync.merges)
+        elif node.sync.coord is not None:
+            merges = len(node.sync.coord.merges)
     version = node.sync.version if node.sync is not None else 0
     if node.sync is not None:
         node.sync.close()
@@ -126,8 +140,10 @@ def main():
                "heldout_loss_mean": round(float(held[1]), 4), "train_loss_last20": round(sum(tail) / len(tail), 4),
                "merges": merges, "global_version": version, "push_every": run.push_every if world > 1 else None}
         if world > 1:
-            out.update(swap_mode=run.swap_mode, ef_on_swap=run.ef_on_swap,
-                       reset_optimizer_on_swap=run.reset_optimizer_on_swap)
+            out.update(sync=a.sync, reset_optimizer_on_swap=run.reset_optimizer_on_swap)
+            if a.sync == "inbox":
+                out.update(swap_mode=run.swap_mode, ef_on_swap=run.ef_on_swap,
+                           top_k=run.compression.top_k_fraction)
         if a.data == "markov":
             out["entropy_floor"] = round(gen.entropy(), 4)
         else:

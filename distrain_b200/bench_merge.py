@@ -13,8 +13,8 @@ Per (model, top-k), every iteration:
   1. every rank compresses its delta (+ error feedback) into its symmetric (peer-mapped) payload buffer:
      pass A + radix top-k + ordered compaction + INT8 block 256;
   2. rank 0 (the coordinator) pulls all N payloads over NVLink with the merge kernels (prepass norms and
-     validation with its host round trip, weighted dequant scatter-add into fp32), applies the update and
-     writes the new checkpoint (fp32 master + bf16 copy) into every rank's staging buffer with NVLS
+     validation with its host round trip, weighted dequant scatter-add straight into its fp32 checkpoint,
+     which is its own staging buffer) and writes the new fp32 checkpoint into every rank's staging buffer with NVLS
      multimem stores (per-peer stores when the box offers no multicast object).
 Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, total = their
 sum (the steps are separated by barriers). Bytes over NVLink: payloads pulled from the N-1 peers plus the
@@ -67,13 +67,12 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     cap_max = DeviceCompressor.capacity_for(L, max(topks))
     pay_bytes = (DevicePayload.nbytes(cap_max, 256) + 4095) // 4096 * 4096
     pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes, dev, world)
-    stage_bytes = (n * 6 + 4095) // 4096 * 4096
+    stage_bytes = (n * 4 + 4095) // 4096 * 4096
     stage_buf, stage_ptrs, stage_mc, _stage_h = _symm_alloc(stage_bytes, dev, world)
     p32 = [p for p in stage_ptrs]
-    p16 = [p + n * 4 for p in stage_ptrs]
     mc32 = stage_mc or 0
-    mc16 = (stage_mc + n * 4) if stage_mc else 0
-    merger = DeviceMerger(n, dev, snap, momentum=0.0) if rank == 0 else None
+    merger = (DeviceMerger(n, dev, snap, momentum=0.0, theta_buffer=stage_buf[:n * 4].view(torch.float32))
+              if rank == 0 else None)
     results = []
 
     def barrier():
@@ -116,7 +115,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                                                  node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
                 m0, m1 = _events()
                 m0.record(merger.stream)
-                infos = merger.merge(contribs, 1.0, 0.0, mc32=mc32, mc16=mc16, stage32=p32, stage16=p16)
+                infos = merger.merge(contribs, 1.0, mc32=mc32, stage32=p32)
                 m1.record(merger.stream)
                 merger.stream.synchronize()
                 mms = m0.elapsed_time(m1)
@@ -132,7 +131,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                             "n_nodes": world, "top_k": k, "compress_ms": round(cms, 3), "merge_ms": round(mms, 3),
                             "total_ms": round(cms + mms, 3), "accepted": infos["accepted"],
                             "payload_bytes_pulled_nvlink": pulled,
-                            "checkpoint_bytes_broadcast": n * 6, "broadcast": "nvls multimem" if mc32 else "per-peer",
+                            "checkpoint_bytes_broadcast": n * 4, "broadcast": "nvls multimem" if mc32 else "per-peer",
                             "staleness": stale, "tokens": tokens,
                             "timing": "CUDA events, median of iters, max over ranks"})
         del comp, payload

@@ -294,17 +294,25 @@ class RunConfig(_Json):
     max_staleness: int = 10
     init_std: float = 0.02
     seed: int = 0
-    # What a node does with the steps it trained since its last push when a new checkpoint arrives:
-    # "push_partial" pushes them as a partial round and replaces its weights with the checkpoint (the
-    # reference node, continuous.rs:458-502); "rebase" carries them onto the new checkpoint
-    # (weights = checkpoint + (weights - round start)) and keeps the round going, so every push covers
-    # `push_every` steps even when checkpoints arrive within a step of a push.
-    swap_mode: str = "push_partial"
-    # error-feedback buffer at a checkpoint swap: "keep" (the reference node keeps 100%,
-    # continuous.rs:489-493) or "reset"
-    ef_on_swap: str = "keep"
-    # re-create the inner AdamW state at a swap (the reference node does, continuous.rs:407-414)
-    reset_optimizer_on_swap: bool = True
+    # What a node does at a checkpoint swap. The reference node (continuous.rs:458-502) pushes the steps
+    # trained since its last push as a partial round, replaces its weights with the checkpoint, keeps
+    # its error-feedback buffer and re-creates AdamW: swap_mode="push_partial", ef_on_swap="keep",
+    # reset_optimizer_on_swap=True. On one box a merge lands within a step or two of the pushes, so that
+    # turns every push into a cascade of few-step partial rounds and optimizer restarts. The defaults
+    # here, chosen on the held-out loss at matched tokens (2 nodes x 300 steps of the tiny preset on a
+    # learnable Markov source: 1.67 against 2.35 for the reference's choices; dense NCCL averaging
+    # 1.67 with optimizer restarts, 1.55 without):
+    #   swap_mode "rebase": carry the steps since the last push onto the checkpoint
+    #     (weights = checkpoint + (weights - round start)) and keep the round going, so every push
+    #     covers push_every steps;
+    #   ef_on_swap "fold": clear the error-feedback buffer at the boundary by moving its residual into
+    #     the weights (weights -= residual); the next delta transmits it, while the node trains on all
+    #     of its own progress ("keep" and "reset" are the other choices);
+    #   reset_optimizer_on_swap False: keep the AdamW moments.
+    payload_slots: int = 2  # compressed-delta buffers per node (1 halves that memory; pushes then wait for the merge)
+    swap_mode: str = "rebase"
+    ef_on_swap: str = "fold"
+    reset_optimizer_on_swap: bool = False
 
 
 def bench_config(name: str) -> RunConfig:
@@ -322,7 +330,7 @@ def bench_config(name: str) -> RunConfig:
                          compression=CompressionConfig(top_k_fraction=0.99, int8_block=256))
     if name in ("large", "13b"):
         return RunConfig(name="large", model=preset("large"), seq_len=2048, micro_batch=4, push_every=100,
-                         tp=2, activation_checkpointing=True)
+                         tp=2, activation_checkpointing=True, payload_slots=1)
     if name in ("medium", "7b"):
         return RunConfig(name="medium", model=preset("medium"), seq_len=2048, micro_batch=4, push_every=100,
                          activation_checkpointing=True)

@@ -2,9 +2,11 @@
 
 Every rank is one Distrain node; rank 0 additionally runs the coordinator. Per node:
 
-* ``payload`` - two slots of a symmetric (peer-mapped) buffer holding compressed deltas;
-* ``staging`` - two version-parity slots of a symmetric buffer (fp32 master + bf16 compute copy) that
-  the coordinator's apply kernel writes with NVLS ``multimem.st`` (or per-peer stores).
+* ``payload`` - one or two slots of a symmetric (peer-mapped) buffer holding compressed deltas;
+* ``staging`` - one fp32 checkpoint slot in a symmetric buffer that the coordinator's broadcast kernel
+  writes with NVLS ``multimem.st`` (or per-peer stores); on the coordinator's rank the slot is the global
+  checkpoint itself, which the merge updates in place. The coordinator writes version v only after every
+  node has swapped to v-1.
 
 Push (node, at a round boundary, reference continuous.rs:532-580): pass A of the compressor on the
 training stream (delta + error feedback + re-snapshot, ~0.2 ms), the rest of the compressor on a
@@ -18,7 +20,8 @@ rejected; a node whose next slot is still in use defers the push by a step inste
 
 Swap (node, reference continuous.rs:458-502): on a new version push the partial round and copy the
 staged checkpoint into the master / bf16 buffers (or, with ``swap_mode="rebase"``, carry the steps since
-the last push onto it); re-create AdamW; keep (reference) or clear the error-feedback buffer.
+the last push onto it); re-create AdamW; keep (reference), clear, or fold into the weights the
+error-feedback residual.
 """
 from __future__ import annotations
 
@@ -137,11 +140,17 @@ class InBoxSync:
         cap = DeviceCompressor.capacity_for(self.layout, max(cfg.top_k_fraction, 0.0))
         blk = cfg.int8_block if cfg.quantize_int8 else 0
         self.slot_bytes = (DevicePayload.nbytes(cap, blk) + 4095) // 4096 * 4096
-        self.pay_buf, self.pay_ptrs, _, self._pay_h = _symm_alloc(2 * self.slot_bytes, self.device, world, dp_group)
+        # payload slots: with two, a node can push again while the coordinator still holds its previous
+        # payload; one is enough when pushes are far apart (and saves ~9 bytes per kept entry)
+        self.n_slots = max(1, int(run.payload_slots))
+        self.pay_buf, self.pay_ptrs, _, self._pay_h = _symm_alloc(self.n_slots * self.slot_bytes, self.device, world,
+                                                                  dp_group)
         self.slots = [DevicePayload(self.pay_buf[i * self.slot_bytes:(i + 1) * self.slot_bytes], cap, blk)
-                      for i in range(2)]
-        self.stage_bytes = (self.n * 6 + 4095) // 4096 * 4096
-        self.stage_buf, self.stage_ptrs, self.stage_mc, self._stage_h = _symm_alloc(2 * self.stage_bytes, self.device,
+                      for i in range(self.n_slots)]
+        # one fp32 checkpoint slot per node (the swap derives the bf16 copy); the coordinator's own slot is
+        # its global checkpoint, updated in place by the merge
+        self.stage_bytes = (self.n * 4 + 4095) // 4096 * 4096
+        self.stage_buf, self.stage_ptrs, self.stage_mc, self._stage_h = _symm_alloc(self.stage_bytes, self.device,
                                                                                    world, dp_group)
         self.compressor = DeviceCompressor(self.layout, self.device, cfg, payload=self.slots[0])
         self.compressor.reset(eng.master)
@@ -149,7 +158,7 @@ class InBoxSync:
         self.bus = StoreBus(f"dtinbox/s{shard}/" if n_shards > 1 else "dtinbox/") if multi else LocalBus()
         self.shared = self.bus if n_shards == 1 else StoreBus("dtinbox/shared/")
         self.inflight = None  # (seq, event, slot)
-        self.slot_seq = [-1, -1]
+        self.slot_seq = [-1] * self.n_slots
         self.ef_ready = None
         self.pending_posts: "queue.Queue" = queue.Queue()
         self.stop = threading.Event()
@@ -163,20 +172,13 @@ class InBoxSync:
             dist.barrier()
 
     # ─────────── helpers ───────────
-    def stage_views(self, version: int):
-        par = version % 2
-        base = par * self.stage_bytes
-        s32 = self.stage_buf[base:base + 4 * self.n].view(torch.float32)
-        s16 = self.stage_buf[base + 4 * self.n:base + 6 * self.n].view(torch.bfloat16)
-        return s32, s16
+    def stage_view(self) -> torch.Tensor:
+        """This node's fp32 checkpoint slot (on the coordinator's rank: the global checkpoint)."""
+        return self.stage_buf[:4 * self.n].view(torch.float32)
 
-    def stage_peer_ptrs(self, version: int):
-        par = version % 2
-        p32 = [p + par * self.stage_bytes for p in self.stage_ptrs]
-        p16 = [p + par * self.stage_bytes + 4 * self.n for p in self.stage_ptrs]
-        mc32 = self.stage_mc + par * self.stage_bytes if self.stage_mc else 0
-        mc16 = mc32 + 4 * self.n if mc32 else 0
-        return p32, p16, mc32, mc16
+    def stage_peer_ptrs(self):
+        """(every node's slot by group rank, multicast address of the slots or 0)."""
+        return list(self.stage_ptrs), self.stage_mc or 0
 
     def _slot_free(self, slot: int) -> bool:
         s = self.slot_seq[slot]
@@ -239,7 +241,7 @@ class InBoxSync:
         return True
 
     def _push(self, partial: bool) -> bool:
-        slot = (self.seq + 1) % 2
+        slot = (self.seq + 1) % self.n_slots
         if not self._slot_free(slot):
             return False  # coordinator still holds that payload; try again next step
         if self.inflight is not None and not self.inflight[1].query():
@@ -310,11 +312,15 @@ class InBoxSync:
             self._push_agreed(partial=True)
         eng = self.eng
         train = torch.cuda.current_stream()
-        s32, s16 = self.stage_views(new_version)
+        s32 = self.stage_view()
+        fold = run.ef_on_swap == "fold"
+        if fold and self.ef_ready is not None:
+            train.wait_event(self.ef_ready)  # the in-flight compression has written the residual
         from ..ops._lib import check, stream_ptr, lib, register, c_void, c_ll, c_int
-        register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
-        check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), eng.master.data_ptr(), eng.p16.data_ptr(),
-                               self.compressor.snap.data_ptr(), self.n, int(rebase), stream_ptr(train)), "dt_swap_in")
+        register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
+        check(lib().dt_swap_in(s32.data_ptr(), None, eng.master.data_ptr(), eng.p16.data_ptr(),
+                               self.compressor.snap.data_ptr(), self.compressor.ef.data_ptr() if fold else None,
+                               self.n, int(rebase), stream_ptr(train)), "dt_swap_in")
         if run.reset_optimizer_on_swap:  # AdamW re-created (reference continuous.rs:407-414)
             eng.m.zero_()
             eng.v.zero_()
@@ -371,7 +377,8 @@ class InBoxCoordinator:
         # highest priority: the training graph keeps every SM busy with persistent GEMMs, so merge
         # kernels must be first in line whenever blocks retire or they starve for seconds
         stream = torch.cuda.Stream(device=sync.device, priority=-100)
-        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
+        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
+                                   theta_buffer=sync.stage_view())
         self.version = 0
         self.merges: List[dict] = []
         self.failed: List[str] = []
@@ -418,8 +425,9 @@ class InBoxCoordinator:
                             weight=c.weight, node_id=c.node_id, wire_bytes=p.wire_bytes(count))
 
     def _wait_consumed(self, version: int, timeout: float = 30.0):
-        """Before writing staging parity of `version`, every node must have left version-2."""
-        need = version - 2
+        """Before the merge writes `version` into the single checkpoint slot (in place on this GPU, by
+        broadcast on the others), every node of every shard must have swapped to version-1."""
+        need = version - 1
         if need < 1:
             return
         t0 = time.time()
@@ -438,7 +446,7 @@ class InBoxCoordinator:
             contribs = [self._contribution(c) for c in snap.contributions]
             new_version = self.version + 1
             self._wait_consumed(new_version)
-            p32, p16, mc32, mc16 = self.sync.stage_peer_ptrs(new_version)
+            p32, mc32 = self.sync.stage_peer_ptrs()
             t0 = time.time()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(self.merger.stream)
@@ -464,8 +472,7 @@ class InBoxCoordinator:
                 raise
             if ns > 1:
                 self.shared.set(f"coefs/{att}", json.dumps(coefs))
-            self.merger.accumulate_apply(contribs, coefs, self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16, stage32=p32,
-                                         stage16=p16)
+            self.merger.accumulate_apply(contribs, coefs, self.run.outer_lr, mc32=mc32, stage32=p32)
             info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
             ev1.record(self.merger.stream)
             ev1.synchronize()
@@ -475,7 +482,7 @@ class InBoxCoordinator:
             info["wall_ms"] = (time.time() - t0) * 1e3
             info["version"] = new_version
             info["n_contrib"] = len(contribs)
-            info["broadcast_bytes"] = self.sync.n * 6 * (1 if mc32 else self.world)
+            info["broadcast_bytes"] = self.sync.n * 4 * (1 if mc32 else self.world - 1)
             info["multicast"] = bool(mc32)
             self.merges.append(info)
             for c in snap.contributions:
@@ -534,7 +541,8 @@ class ShardFollower:
         self.bus = StoreBus(sync.bus.prefix)
         self.shared = StoreBus("dtinbox/shared/")
         stream = torch.cuda.Stream(device=sync.device, priority=-100)
-        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream)
+        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
+                                   theta_buffer=sync.stage_view())
         self.attempt = 0
         self.merges: List[dict] = []
         self.failed: List[str] = []
@@ -560,15 +568,14 @@ class ShardFollower:
     def _one(self, att: int, plan: dict):
         v = plan["version"]
         contribs = [self._contribution(nid, seq) for nid, seq in plan["members"]]
-        p32, p16, mc32, mc16 = self.sync.stage_peer_ptrs(v)
+        p32, mc32 = self.sync.stage_peer_ptrs()
         stats = self.merger.prepass(contribs)
         self.shared.set(f"stats/{att}/{self.sync.shard}", json.dumps(stats))
         c = self.shared.wait_get(f"coefs/{att}", 120)
         if c == "abort":
             self.failed.append(f"attempt {att} aborted by shard 0")
             return
-        self.merger.accumulate_apply(contribs, json.loads(c), self.run.outer_lr, 0.0, mc32=mc32, mc16=mc16,
-                                     stage32=p32, stage16=p16)
+        self.merger.accumulate_apply(contribs, json.loads(c), self.run.outer_lr, mc32=mc32, stage32=p32)
         self.merger.stream.synchronize()
         self.merges.append({"version": v, "n_contrib": len(contribs)})
         self.shared.set(f"merged/{att}/{self.sync.shard}", "1")

@@ -121,8 +121,18 @@ _CONTRIB_FMT = "<QQQQqiifi"  # matches struct Contrib in merge.cu (56 bytes)
 
 
 class DeviceMerger:
-    def __init__(self, n_params_padded: int, device, theta_init: torch.Tensor, momentum: float = 0.0,
-                 stream: Optional[torch.cuda.Stream] = None):
+    """Device merge of compressed payloads into the global checkpoint ``theta``.
+
+    ``theta_buffer``: an fp32 [n] tensor that holds the checkpoint and is updated in place (the in-box
+    coordinator passes its own staging buffer, so the checkpoint exists once on that GPU); it is
+    initialised from ``theta_init`` when that is given too. Without ``theta_buffer`` theta is a copy of
+    ``theta_init``. With ``momentum`` 0 (the reference's outer step, coordinator/src/aggregation.rs:364)
+    the weighted dequantised values are scatter-added straight into theta; otherwise through an fp32
+    accumulator and a velocity buffer (Nesterov, aggregation.rs:64-105)."""
+
+    def __init__(self, n_params_padded: int, device, theta_init: Optional[torch.Tensor] = None,
+                 momentum: float = 0.0, stream: Optional[torch.cuda.Stream] = None,
+                 theta_buffer: Optional[torch.Tensor] = None):
         from ..ops import _lib
         from ..ops._lib import c_int, c_void, c_ll, c_float
         self.L = _lib.lib()
@@ -130,12 +140,20 @@ class DeviceMerger:
         _lib.register("dt_merge_prepass", [c_void, c_int, c_ll, c_void, c_void])
         _lib.register("dt_merge_accumulate", [c_void, c_int, c_ll, c_void, c_void])
         _lib.register("dt_merge_apply_broadcast", [c_void, c_void, c_void, c_ll, c_float, c_float, c_void, c_void,
-                                                   c_void, c_void, c_int, c_int, c_void])
+                                                   c_int, c_void])
+        _lib.register("dt_merge_broadcast", [c_void, c_ll, c_void, c_void, c_int, c_void])
         assert self.L.dt_merge_contrib_bytes() == struct.calcsize(_CONTRIB_FMT)
         self.device = torch.device(device)
         self.n = n_params_padded
-        self.theta = theta_init.to(self.device, torch.float32).clone()
-        self.acc = torch.zeros(self.n, dtype=torch.float32, device=self.device)
+        if theta_buffer is not None:
+            assert theta_buffer.dtype == torch.float32 and theta_buffer.numel() == self.n
+            self.theta = theta_buffer
+            if theta_init is not None:
+                self.theta.copy_(theta_init)
+        else:
+            self.theta = theta_init.to(self.device, torch.float32).clone()
+        self.momentum = float(momentum)
+        self.acc = torch.zeros(self.n, dtype=torch.float32, device=self.device) if momentum else None
         self.vel = torch.zeros(self.n, dtype=torch.float32, device=self.device) if momentum else None
         self.stream = stream or torch.cuda.Stream(device=self.device, priority=0)
         self.stats = torch.zeros(3 * 64, dtype=torch.float64, device=self.device)
@@ -192,9 +210,10 @@ class DeviceMerger:
                        "per_delta_norms": eff, "coefs": coefs}
 
     def accumulate_apply(self, contribs: List[Contribution], coefs: List[float], outer_lr: float,
-                         outer_momentum: float, mc32: int = 0, mc16: int = 0, stage32: Sequence[int] = (),
-                         stage16: Sequence[int] = (), write_bf16: bool = True):
-        """Weighted dequant scatter-add of every payload, then apply + broadcast, enqueued on the merge stream."""
+                         mc32: int = 0, stage32: Sequence[int] = ()):
+        """Weighted dequant scatter-add of every payload into the checkpoint, then the broadcast of the new
+        checkpoint (multicast address ``mc32``, or the peers' staging pointers ``stage32``), enqueued on the
+        merge stream."""
         from ..ops._lib import check
         import ctypes
         n = len(contribs)
@@ -202,22 +221,24 @@ class DeviceMerger:
         sp = st.cuda_stream
         maxc = max(c.count for c in contribs)
         s32 = (ctypes.c_void_p * max(len(stage32), 1))(*stage32) if stage32 else None
-        s16 = (ctypes.c_void_p * max(len(stage16), 1))(*stage16) if stage16 else None
-        buf = self._pack(contribs, coefs)
         with torch.cuda.stream(st):
-            check(self.L.dt_merge_accumulate(buf, n, maxc, self.acc.data_ptr(), sp), "dt_merge_accumulate")
-            check(self.L.dt_merge_apply_broadcast(self.theta.data_ptr(),
-                                                  self.vel.data_ptr() if self.vel is not None else None,
-                                                  self.acc.data_ptr(), self.n, float(outer_lr), float(outer_momentum),
-                                                  mc32 or None, mc16 or None, s32, s16, len(stage32),
-                                                  int(write_bf16), sp), "dt_merge_apply_broadcast")
+            if self.acc is None:  # theta -= lr * sum_c coef_c * x_c, in place
+                buf = self._pack(contribs, [-float(outer_lr) * k for k in coefs])
+                check(self.L.dt_merge_accumulate(buf, n, maxc, self.theta.data_ptr(), sp), "dt_merge_accumulate")
+                check(self.L.dt_merge_broadcast(self.theta.data_ptr(), self.n, mc32 or None, s32, len(stage32), sp),
+                      "dt_merge_broadcast")
+            else:
+                buf = self._pack(contribs, coefs)
+                check(self.L.dt_merge_accumulate(buf, n, maxc, self.acc.data_ptr(), sp), "dt_merge_accumulate")
+                check(self.L.dt_merge_apply_broadcast(self.theta.data_ptr(), self.vel.data_ptr(), self.acc.data_ptr(),
+                                                      self.n, float(outer_lr), self.momentum, mc32 or None, s32,
+                                                      len(stage32), sp), "dt_merge_apply_broadcast")
 
-    def merge(self, contribs: List[Contribution], outer_lr: float, outer_momentum: float, mc32: int = 0,
-              mc16: int = 0, stage32: Sequence[int] = (), stage16: Sequence[int] = (), write_bf16: bool = True):
+    def merge(self, contribs: List[Contribution], outer_lr: float, mc32: int = 0, stage32: Sequence[int] = ()):
         """Full merge on ``self.stream``; blocks the calling (coordinator) thread on the prepass only.
         Returns an info dict (accepted, rejected, norms, nvlink bytes)."""
         n = len(contribs)
         coefs, info = self.plan(contribs, self.prepass(contribs))
-        self.accumulate_apply(contribs, coefs, outer_lr, outer_momentum, mc32, mc16, stage32, stage16, write_bf16)
+        self.accumulate_apply(contribs, coefs, outer_lr, mc32, stage32)
         info["pulled_bytes"] = sum(contribs[i].wire_bytes for i in range(n))
         return info

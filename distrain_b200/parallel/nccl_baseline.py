@@ -7,8 +7,8 @@ checkpoint pushed back with NVLS multimem stores) is plain DiLoCo-style synchron
 collective: every ``push_every`` steps each rank forms its dense round delta delta = theta_start - theta,
 ``ncclAllReduce(AVG)`` averages it over all ranks on the training stream, every rank applies
 theta = theta_start - outer_lr * mean(delta) (outer lr 1, no momentum: the reference's merge with
-uniform weights, no staleness, no compression) and starts a new round with a fresh AdamW state, as the
-in-box node does on a checkpoint swap.
+uniform weights, no staleness, no compression) and starts a new round, with a fresh AdamW state when
+``run.reset_optimizer_on_swap`` is set, as the in-box node does on a checkpoint swap.
 
 It reuses the node's hook points (``before_step`` / ``after_step``) so the benchmark measures exactly
 the trainer plus this merge; ``merges`` holds the device time of each all-reduce + apply.
@@ -63,9 +63,10 @@ class NcclDenseSync:
         eng.master.copy_(self.snap).sub_(self.delta, alpha=self.outer_lr)
         self.snap.copy_(eng.master)
         ops.cast_bf16(eng.master, eng.p16)
-        eng.m.zero_()
-        eng.v.zero_()
-        eng.hp[9:11].zero_()
+        if self.run.reset_optimizer_on_swap:
+            eng.m.zero_()
+            eng.v.zero_()
+            eng.hp[9:11].zero_()
         e1.record(train)
         self._events.append((e0, e1))
         self.version += 1

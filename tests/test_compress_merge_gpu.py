@@ -66,7 +66,10 @@ def test_device_compress_matches_reference(k_fraction, adaptive):
     assert abs(st["dense_norm"] - float(combined.double().norm())) < 1e-6 * max(1, st["dense_norm"])
 
 
-def test_device_merge_matches_reference():
+@pytest.mark.parametrize("momentum,in_place", [(0.0, True), (0.0, False), (0.9, False)])
+def test_device_merge_matches_reference(momentum, in_place):
+    """Merge of three compressed payloads (one an outlier that gets clipped) against the fp32 reference
+    merge: in place into a staging-style buffer, into a private copy, and with Nesterov momentum."""
     from distrain_b200.config import CompressionConfig
     from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload, dequantize_int8
     from distrain_b200.parallel.merge import DeviceMerger, Contribution, merge_reference
@@ -99,21 +102,24 @@ def test_device_merge_matches_reference():
         dense = torch.zeros(L.total)
         dense[p.idx[:K].long().cpu()] = deq
         dense_deltas.append({e.name: dense[e.offset:e.offset + e.numel] for e in L.entries})
-    merger = DeviceMerger(L.total, dev, theta, momentum=0.0)
+    own = torch.zeros(L.total, device=dev) if in_place else None
+    merger = DeviceMerger(L.total, dev, theta, momentum=momentum, theta_buffer=own)
     s32 = torch.zeros(L.total, device=dev)
-    s16 = torch.zeros(L.total, device=dev, dtype=torch.bfloat16)
-    info = merger.merge(contribs, 1.0, 0.0, stage32=[s32.data_ptr()], stage16=[s16.data_ptr()])
+    dests = [s32.data_ptr()] + ([own.data_ptr()] if in_place else [])  # the own slot is skipped by the kernel
+    info = merger.merge(contribs, 1.0, stage32=dests)
     torch.cuda.synchronize()
     ck = {e.name: theta[e.offset:e.offset + e.numel].cpu() for e in L.entries}
-    new, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=0.0)
+    new, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=momentum)
     got = merger.theta.cpu()
     for e in L.entries:
         assert torch.allclose(got[e.offset:e.offset + e.numel], new[e.name], atol=1e-7, rtol=1e-5), e.name
     assert info["accepted"] == 3
     assert info["per_delta_norms"][2] < info["per_delta_norms"][0] * 3.0001 * 2
     assert torch.equal(s32, merger.theta)
-    assert torch.equal(s16, merger.theta.bfloat16())
-    assert float(merger.acc.abs().max()) == 0.0
+    if in_place:
+        assert merger.theta.data_ptr() == own.data_ptr()
+    if merger.acc is not None:
+        assert float(merger.acc.abs().max()) == 0.0
 
 
 def test_inbox_single_gpu_protocol():
@@ -143,30 +149,40 @@ def test_inbox_single_gpu_protocol():
     node.close()
 
 
-@pytest.mark.parametrize("rebase", [0, 1])
-def test_swap_in_kernel(rebase):
+@pytest.mark.parametrize("rebase,fold", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_swap_in_kernel(rebase, fold):
     """Checkpoint swap against its fp32 definition: replace (master = snap = staged) or rebase
-    (master = staged + master - snap, snap = staged), bf16 copy of the new master."""
+    (master = staged + master - snap, snap = staged), optionally folding the error-feedback residual into
+    the weights (master -= ef, ef = 0); bf16 copy of the new master."""
     from distrain_b200.ops._lib import lib, register, check, c_void, c_ll, c_int, stream_ptr
-    register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
+    register("dt_swap_in", [c_void, c_void, c_void, c_void, c_void, c_void, c_ll, c_int, c_void])
     n = 1 << 20
     g = torch.Generator(device="cuda").manual_seed(5)
     s32 = torch.randn(n, device="cuda", generator=g)
     s16 = s32.bfloat16()
     master = torch.randn(n, device="cuda", generator=g)
     snap = master - 1e-3 * torch.randn(n, device="cuda", generator=g)
-    want = (s32.double() + (master.double() - snap.double())).float() if rebase else s32.clone()
+    ef = 1e-3 * torch.randn(n, device="cuda", generator=g)
+    want = s32.double()
+    if rebase:
+        want = want + (master.double() - snap.double())
+    if fold:
+        want = want - ef.double()
+    want = want.float()
     p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
-    check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), master.data_ptr(), p16.data_ptr(), snap.data_ptr(), n,
-                           rebase, stream_ptr(torch.cuda.current_stream())), "dt_swap_in")
+    check(lib().dt_swap_in(s32.data_ptr(), s16.data_ptr(), master.data_ptr(), p16.data_ptr(), snap.data_ptr(),
+                           ef.data_ptr() if fold else None, n, rebase,
+                           stream_ptr(torch.cuda.current_stream())), "dt_swap_in")
     torch.cuda.synchronize()
     assert torch.allclose(master, want, atol=1e-6, rtol=1e-6)
     assert torch.equal(snap, s32)
     assert torch.equal(p16, master.bfloat16())
+    if fold:
+        assert float(ef.abs().max()) == 0.0
 
 
 @pytest.mark.parametrize("swap_mode,ef_on_swap", [("push_partial", "keep"), ("rebase", "keep"),
-                                                  ("push_partial", "reset")])
+                                                  ("push_partial", "reset"), ("rebase", "fold")])
 def test_inbox_swap_policies(swap_mode, ef_on_swap):
     """The swap policies run the protocol end to end on one GPU (rebase keeps whole rounds: every push
     after the first covers push_every steps)."""
