@@ -203,10 +203,11 @@ def main():
         e2e_ms = f0.elapsed_time(f1)
     clk = clocks.stop() if clocks else None
 
-    t = torch.tensor([ms, e2e_ms or 0.0, float(launches)], device=dev)
+    free_b, total_b = torch.cuda.mem_get_info(dev)
+    t = torch.tensor([ms, e2e_ms or 0.0, float(launches), float(total_b - free_b)], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms_max, launches = t[0].item(), t[1].item(), int(t[2].item())
+    ms, e2e_ms_max, launches, mem_used = t[0].item(), t[1].item(), int(t[2].item()), t[3].item()
     if nccl_arm:
         merges = node.sync.merges
     else:
@@ -239,7 +240,9 @@ def main():
                        "compression": ("none (dense fp32 delta)" if nccl_arm else
                                        f"top-k {run.compression.top_k_fraction:.0%} + INT8 block "
                                        f"{run.compression.int8_block} + error feedback"),
-                       "l2": "per-step working set (~12 GB) >> 126 MB L2; no flush"},
+                       "l2": (f"per-step working set >= {node.engine.layout.total * 18 / 1e9:.1f} GB (weights, "
+                              "gradients, AdamW state) >> 126 MB L2; no flush"),
+                       "device_memory_used_gb_max": round(mem_used / 1e9, 1)},
             "gpu_launches": launches,
             "clocks": clk,
         }
