@@ -331,6 +331,26 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ cseg
   if (threadIdx.x == 0) *total = tot;
 }
 
+// Kept indices are stored as 32-bit offsets within 2^31-element windows of the flat buffer (chunks never
+// straddle a window boundary); the payload records the position where each window's entries start, so a
+// reader adds (window << 31). Buffers below 2^31 elements have one window and plain indices.
+constexpr long long kWindowMask = (1LL << 31) - 1;
+constexpr int kMaxWindows = 8;
+
+__global__ void window_kernel(const long long* __restrict__ off, const long long* __restrict__ total,
+                              const int* __restrict__ win_chunk, int nwin, int nchunks, long long* __restrict__ out) {
+  const int k = threadIdx.x;
+  if (k >= kMaxWindows) return;
+  long long v = 0x7fffffffffffffffLL;  // no such window
+  if (k == 0) {
+    v = 0;
+  } else if (k < nwin) {
+    const int c = win_chunk[k];
+    v = c < nchunks ? off[c] : *total;
+  }
+  out[k] = v;
+}
+
 // Ordered compaction: writes (index, value) of kept entries in ascending index order, zeroes them in ef.
 // Each thread owns CR consecutive elements per round; one block scan of (keys > tau, keys == tau) counts
 // per round gives every thread its output position and its share of the chunk's eq quota.
@@ -374,7 +394,7 @@ __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ c
         --allow;
       }
       if (take) {
-        out_idx[pos] = (int)(i0 + j);
+        out_idx[pos] = (int)((i0 + j) & kWindowMask);  // index within its 2^31 window
         out_val[pos] = v[j];
         ef[i0 + j] = 0.f;
         kept_sq += v[j] * v[j];
@@ -490,7 +510,8 @@ DT_API int dt_compress_begin(const float* master, float* snap, float* ef, const 
 DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstart, const long long* cend, int nchunks,
                               int nseg, void* ws, float k_fraction, int adaptive, int* out_idx, float* out_val,
                               signed char* out_q, float* out_scales, int quant_block, long long capacity,
-                              cudaStream_t st) {
+                              const int* win_chunk, int nwin, long long* out_win, cudaStream_t st) {
+  if (nwin > kMaxWindows) return -21;
   WsPtrs w = carve(ws, nseg, nchunks);
   budget_kernel<<<1, 256, 0, st>>>(w.seg, nseg, k_fraction, adaptive);
   select_level_kernel<NB1, 256><<<nseg, 256, 0, st>>>(w.seg, nseg, w.h1, 12, 0);
@@ -501,6 +522,7 @@ DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstar
   count_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.gt, w.eq);
   scan_kernel<<<1, 1024, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
   compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val);
+  if (out_win) window_kernel<<<1, 32, 0, st>>>(w.off, w.total, win_chunk, nwin, nchunks, out_win);
   if (quant_block > 0 && out_q) {
     long long nblk = (capacity + quant_block - 1) / quant_block;
     quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, quant_block, out_q, out_scales);
@@ -557,8 +579,10 @@ DT_API int dt_compress_noalloc(const float* master, float* snap, float* ef, cons
   // dt_compress_begin clears the whole workspace (histograms, counters) before use
   int rc = dt_compress_begin(master, snap, ef, cseg, cstart, cend, nchunks, nseg, seg_len, ws, 1, st);
   if (rc) return rc;
+  // kept indices are window-relative (see window_kernel); this entry point serves buffers below 2^31
+  // elements, where they are plain flat indices
   rc = dt_compress_finish(ef, cseg, cstart, cend, nchunks, nseg, ws, k_fraction, adaptive, out_idx, out_val, out_q,
-                          out_scales, quant_block, capacity, st);
+                          out_scales, quant_block, capacity, nullptr, 1, nullptr, st);
   if (rc) return rc;
   if (stats_out) return dt_compress_export_stats(ws, nseg, nchunks, stats_out, st);
   return 0;

@@ -19,26 +19,48 @@
 namespace {
 
 struct Contrib {
-  const int* idx;            // kept flat indices (sparse) or null (dense)
+  const int* idx;            // kept indices, relative to their 2^31-element window (sparse), or null (dense)
   const signed char* q;      // int8 values (quantised) or null
   const float* val;          // fp32 values (unquantised sparse, or dense delta)
   const float* scales;       // per-block scales (quantised)
+  const long long* win;      // position where each index window starts (8 entries) or null (one window)
   long long count;           // kept entries (sparse) or length (dense)
   int block;                 // quantisation block
   int dense;
   float coef;                // weight / total * clip scale
   int pad;
 };
-static_assert(sizeof(Contrib) == 56, "Contrib layout is shared with the host packer");
+static_assert(sizeof(Contrib) == 64, "Contrib layout is shared with the host packer");
 
-// The descriptor table travels as a kernel parameter (64 x 56 B < 4 KB): it is captured at launch, so no
-// device copy of it can be read before its upload has landed.
+// The descriptor table travels as a kernel parameter (64 x 64 B; kernel parameters up to 32 KB): it is
+// captured at launch, so no device copy of it can be read before its upload has landed.
 constexpr int MAX_CONTRIB = 64;
 struct ContribTable {
   Contrib c[MAX_CONTRIB];
 };
 
 constexpr int MUNR = 4;
+
+// Window starts of a contribution (positions; int64 max = none), loaded once per thread.
+struct Windows {
+  long long start[7];  // starts of windows 1..7
+  int n;               // how many of them exist
+  __device__ __forceinline__ void load(const long long* win) {
+    n = 0;
+    if (!win) return;
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+      start[k] = __ldg(win + 1 + k);
+      if (start[k] != 0x7fffffffffffffffLL) n = k + 1;
+    }
+  }
+  // flat index of the entry at position p
+  __device__ __forceinline__ long long flat(int idx, long long p) const {
+    long long w = 0;
+    for (int k = 0; k < n; ++k) w += p >= start[k];
+    return (long long)idx + (w << 31);
+  }
+};
 
 __device__ __forceinline__ float contrib_value(const Contrib& c, long long i) {
   if (c.q) return (float)__ldg(c.q + i) * __ldg(c.scales + i / c.block);
@@ -94,6 +116,8 @@ __global__ void accumulate_kernel(const __grid_constant__ ContribTable cs, int n
       atomicAdd(acc + i, __ldg(C.val + i) * C.coef);
     return;
   }
+  Windows W;
+  W.load(C.win);
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < C.count; i0 += stride * MUNR) {
     int j[MUNR];
@@ -106,7 +130,7 @@ __global__ void accumulate_kernel(const __grid_constant__ ContribTable cs, int n
     }
 #pragma unroll
     for (int u = 0; u < MUNR; ++u)
-      if (j[u] >= 0) atomicAdd(acc + j[u], v[u] * C.coef);
+      if (j[u] >= 0) atomicAdd(acc + W.flat(j[u], i0 + u * stride), v[u] * C.coef);
   }
 }
 

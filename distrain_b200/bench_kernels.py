@@ -192,6 +192,7 @@ def merge_cases(iters):
             cnt = int(comp.stats_host[comp.nseg * 6].item())
             pays.append(p)
             contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                         win_ptr=p.win.data_ptr(),
                                          scales_ptr=p.scales.data_ptr(), count=cnt, block=256, dense=False,
                                          weight=1000.0 * (i + 1), wire_bytes=cnt * 5 + (cnt + 255) // 256 * 4))
         m = DeviceMerger(L.total, dev, master)

@@ -109,7 +109,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                 contribs = []
                 for r in range(world):
                     off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
-                    contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q),
+                    contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q), win_ptr=off(payload.win),
                                                  val_ptr=off(payload.val), scales_ptr=off(payload.scales),
                                                  count=counts[r], block=256, dense=False, weight=weights[r],
                                                  node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))

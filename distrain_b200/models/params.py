@@ -120,15 +120,19 @@ class ParamLayout:
                 v.copy_(src.reshape(v.shape).to(v.dtype))
 
     # ── optimizer chunk tables ──
+    WINDOW = 1 << 31  # compressed payloads store kept indices relative to windows of this many elements
+
     def chunk_tables(self, device, chunk: int = 32768):
         """(cseg, cstart, cend) int32/int64 device tensors: one segment per named tensor, chunks of
-        <= ``chunk`` elements with 4-aligned starts (the tail of a tensor may extend into padding)."""
+        <= ``chunk`` elements with 4-aligned starts (the tail of a tensor may extend into padding). No chunk
+        straddles a multiple of ``WINDOW``."""
         segs, starts, ends = [], [], []
+        W = self.WINDOW
         for si, e in enumerate(self.entries):
             s, end = e.offset, e.offset + e.numel
             i = s
             while i < end:
-                j = min(i + chunk, end)
+                j = min(i + chunk, end, (i // W + 1) * W)
                 segs.append(si)
                 starts.append(i)
                 ends.append(j)

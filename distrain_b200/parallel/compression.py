@@ -141,12 +141,19 @@ class DeviceCompressor:
         _lib.register("dt_compress_begin", [c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_void,
                                             c_void, c_int, c_void])
         _lib.register("dt_compress_finish", [c_void, c_void, c_void, c_void, c_int, c_int, c_void, c_float, c_int,
-                                             c_void, c_void, c_void, c_void, c_int, c_ll, c_void])
+                                             c_void, c_void, c_void, c_void, c_int, c_ll, c_void, c_int, c_void,
+                                             c_void])
         _lib.register("dt_compress_export_stats", [c_void, c_int, c_int, c_void, c_void])
         self.layout, self.device, self.cfg = layout, torch.device(device), cfg
         n = layout.total
         self.cseg, self.cstart, self.cend, self.nseg = layout.chunk_tables(self.device)
         self.nchunks = self.cseg.numel()
+        # first chunk of every 2^31-element index window (kept indices are stored window-relative)
+        W = layout.WINDOW
+        self.nwin = max(1, (layout.total + W - 1) // W)
+        starts = self.cstart.cpu()
+        win_chunk = [0] + [int(torch.searchsorted(starts, k * W)) for k in range(1, self.nwin)]
+        self.win_chunk = torch.tensor(win_chunk, dtype=torch.int32, device=self.device)
         self.seg_len = torch.tensor([e.numel for e in layout.entries], dtype=torch.int64, device=self.device)
         self.snap = torch.zeros(n, dtype=torch.float32, device=self.device)
         self.ef = torch.zeros(n, dtype=torch.float32, device=self.device)
@@ -185,7 +192,8 @@ class DeviceCompressor:
                                         self.cend.data_ptr(), self.nchunks, self.nseg, self.ws.data_ptr(), float(kf),
                                         int(self.cfg.per_tensor_adaptive), p.idx.data_ptr(), p.val.data_ptr(),
                                         p.q.data_ptr() if qb else None, p.scales.data_ptr() if qb else None, qb,
-                                        p.capacity, stream_ptr(stream)), "dt_compress_finish")
+                                        p.capacity, self.win_chunk.data_ptr(), self.nwin, p.win.data_ptr(),
+                                        stream_ptr(stream)), "dt_compress_finish")
         check(self.L.dt_compress_export_stats(self.ws.data_ptr(), self.nseg, self.nchunks, self.stats_dev.data_ptr(),
                                               stream_ptr(stream)), "dt_compress_export_stats")
         with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
@@ -207,8 +215,13 @@ class DeviceCompressor:
 
 
 class DevicePayload:
-    """Compressed delta in device memory: idx int32[cap], val fp32[cap], q int8[cap], scales fp32[cap/blk].
-    Views into one allocation so the whole payload can live in a single symmetric (peer-mapped) buffer."""
+    """Compressed delta in device memory: idx int32[cap], val fp32[cap], q int8[cap], scales fp32[cap/blk],
+    win int64[8]. Views into one allocation so the whole payload can live in a single symmetric (peer-mapped)
+    buffer. ``idx`` holds each kept index relative to its 2^31-element window; ``win[k]`` is the position
+    of the first entry of window k (int64 max for windows that do not exist), so the flat index of entry
+    p is idx[p] + (k << 31) with k the number of window starts <= p beyond the first."""
+
+    MAX_WINDOWS = 8
 
     def __init__(self, buf: torch.Tensor, capacity: int, block: int):
         self.buf, self.capacity, self.block = buf, capacity, block
@@ -223,6 +236,8 @@ class DevicePayload:
         oq = take(capacity)
         nb = (capacity + block - 1) // block if block else 1
         os_ = take(4 * nb)
+        ow = take(8 * self.MAX_WINDOWS)
+        self.win = buf[ow:ow + 8 * self.MAX_WINDOWS].view(torch.int64)
         self.idx = buf[oi:oi + 4 * capacity].view(torch.int32)
         self.val = buf[ov:ov + 4 * capacity].view(torch.float32)
         self.q = buf[oq:oq + capacity].view(torch.int8)
@@ -232,7 +247,15 @@ class DevicePayload:
     def nbytes(capacity: int, block: int) -> int:
         nb = (capacity + block - 1) // block if block else 1
         r = lambda x: (x + 255) // 256 * 256
-        return r(4 * capacity) + r(4 * capacity) + r(capacity) + r(4 * nb)
+        return r(4 * capacity) + r(4 * capacity) + r(capacity) + r(4 * nb) + r(8 * DevicePayload.MAX_WINDOWS)
+
+    def global_indices(self, count: int) -> torch.Tensor:
+        """Flat int64 indices of the first ``count`` kept entries."""
+        pos = torch.arange(count, device=self.idx.device, dtype=torch.int64)
+        k = torch.zeros_like(pos)
+        for w in self.win[1:].tolist():
+            k += (pos >= w).long()
+        return self.idx[:count].long() + (k << 31)
 
     @classmethod
     def allocate(cls, capacity: int, block: int, device) -> "DevicePayload":

@@ -420,7 +420,7 @@ class InBoxCoordinator:
         peer = s.pay_ptrs[r]
         off = lambda t: t.data_ptr() - base_local + peer
         blk = p.block
-        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val),
+        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
                             scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
                             weight=c.weight, node_id=c.node_id, wire_bytes=p.wire_bytes(count))
 
@@ -561,7 +561,7 @@ class ShardFollower:
         off = lambda t: t.data_ptr() - base_local + peer
         blk = p.block
         count = body["_count"]
-        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val),
+        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
                             scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
                             weight=1.0, node_id=node_id, wire_bytes=p.wire_bytes(count))
 

@@ -115,9 +115,10 @@ class Contribution:
     weight: float
     node_id: str = ""
     wire_bytes: int = 0
+    win_ptr: int = 0  # the payload's window starts (DevicePayload.win), 0 = one window
 
 
-_CONTRIB_FMT = "<QQQQqiifi"  # matches struct Contrib in merge.cu (56 bytes)
+_CONTRIB_FMT = "<QQQQQqiifi"  # matches struct Contrib in merge.cu (64 bytes)
 
 
 class DeviceMerger:
@@ -163,8 +164,9 @@ class DeviceMerger:
         """Host descriptor table (struct Contrib records), passed to the kernels as launch parameters."""
         import ctypes
         fmt = _CONTRIB_FMT
-        raw = b"".join(struct.pack(fmt, c.idx_ptr if not c.dense else 0, c.q_ptr, c.val_ptr, c.scales_ptr, c.count,
-                                   max(c.block, 1), int(c.dense), float(k), 0) for c, k in zip(contribs, coefs))
+        raw = b"".join(struct.pack(fmt, c.idx_ptr if not c.dense else 0, c.q_ptr, c.val_ptr, c.scales_ptr,
+                                   c.win_ptr if not c.dense else 0, c.count, max(c.block, 1), int(c.dense), float(k),
+                                   0) for c, k in zip(contribs, coefs))
         buf = ctypes.create_string_buffer(raw, len(raw))
         self._keep = buf
         return buf

@@ -85,7 +85,10 @@ def decode_dtz_dense(data: bytes) -> torch.Tensor:
 
 
 def payload_to_dtz(payload, count: int, total_params: int, zstd_level: int = 0) -> bytes:
-    """Serialise the first ``count`` entries of a device payload (DevicePayload) to DTZ1 bytes."""
+    """Serialise the first ``count`` entries of a device payload (DevicePayload) to DTZ1 bytes (flat int32
+    indices: layouts below 2^31 parameters; larger ones go through the per-tensor SparseDelta format)."""
+    if total_params >= 1 << 31:
+        raise ValueError("DTZ1 carries int32 flat indices; use payload_to_sparse_delta above 2^31 parameters")
     blk = payload.block
     if blk:
         nb = (count + blk - 1) // blk
@@ -100,7 +103,7 @@ def flat_to_named(dense: torch.Tensor, layout) -> Dict[str, torch.Tensor]:
 
 def payload_to_sparse_delta(payload, count: int, layout, cfg: CompressionConfig) -> SparseDeltaT:
     """Device payload -> reference SparseDelta (per-tensor indices; dequantised values)."""
-    idx = payload.idx[:count].long().cpu()
+    idx = payload.global_indices(count).cpu()
     if payload.block:
         q = payload.q[:count].float().cpu()
         sc = payload.scales[:(count + payload.block - 1) // payload.block].cpu()

@@ -96,6 +96,7 @@ def test_device_merge_matches_reference(momentum, in_place):
         w = 1000.0 * (i + 1) * 0.9 ** i
         weights.append(w)
         contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                     win_ptr=p.win.data_ptr(),
                                      scales_ptr=p.scales.data_ptr(), count=K, block=256, dense=False, weight=w,
                                      wire_bytes=p.wire_bytes(K)))
         deq = dequantize_int8(p.q[:K].cpu(), p.scales[:(K + 255) // 256].cpu(), 256)
