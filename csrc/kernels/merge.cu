@@ -205,6 +205,262 @@ __global__ void broadcast_kernel(const float* __restrict__ theta, long long n, f
   __threadfence_system();
 }
 
+// ───────────── distributed merge: every node merges one slice of the flat range ─────────────
+// Node r owns the flat range [a_r, b_r) (float4-aligned, about n/W elements). For a merge attempt `att`
+// every node:
+//   dm_range    finds, per member payload, the positions whose flat index falls in its range (payload
+//               indices ascend, so a 32-ary warp search over the peer's index array);
+//   dm_prepass  sums ||x||^2, max|x| and non-finite counts over those positions and adds them into rank
+//               0's stats with system-scope atomics; its last block releases rank 0's arrival counter;
+// rank 0 waits for W arrivals, the host validates / clips / weighs (the same rules as the single-GPU
+// merge) and dm_publish writes the coefficients into every node's control buffer and releases each
+// node's flag; then every node:
+//   dm_apply    waits for its flag, adds coef * x into its slice of the checkpoint (its own staging
+//               slot) - dense members fused in one pass, sparse ones by atomics;
+//   dm_broadcast writes its slice into every node's slot (multimem.st, or one store per peer) and
+//               releases rank 0's done counter.
+// Counters only grow (targets att * W), so no reset races between attempts. Every wait is bounded.
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded wait by one thread until *p >= target; false on timeout (error recorded at `site`).
+__device__ __forceinline__ bool wait_ge_u64(const unsigned long long* p, unsigned long long target, int site,
+                                           unsigned long long bound_ns = DT_WAIT_NS) {
+  if (ld_acquire_sys_u64(p) >= target) return true;
+  const uint64_t t0 = dt_globaltimer();
+  while (ld_acquire_sys_u64(p) < target) {
+    if (*reinterpret_cast<volatile int*>(&dt_error_word) != 0 || dt_globaltimer() - t0 > bound_ns) {
+      dt_set_error(DT_ERR_TIMEOUT_PEER, site);
+      return false;
+    }
+  }
+  return true;
+}
+
+// First position p in [0, count) with flat(p) >= x (count if none), by one warp.
+__device__ long long warp_lower_bound(const Contrib& C, const Windows& W, long long x) {
+  const int lane = threadIdx.x & 31;
+  long long L = 0, R = C.count;
+  while (R - L > 32) {
+    const long long step = (R - L + 31) / 32;
+    const long long p = L + lane * step;
+    const bool ge = p >= R || W.flat(__ldg(C.idx + p), p) >= x;
+    const unsigned m = __ballot_sync(0xffffffffu, ge);
+    if (m == 0) {
+      L = L + 31 * step + 1;
+    } else {
+      const int f = __ffs(m) - 1;
+      if (f == 0) {
+        R = L;
+      } else {
+        const long long nr = L + f * step;
+        L = L + (long long)(f - 1) * step + 1;
+        if (nr < R) R = nr;
+      }
+    }
+  }
+  const long long p = L + lane;
+  const bool ge = p >= R || W.flat(__ldg(C.idx + p), p) >= x;
+  const unsigned m = __ballot_sync(0xffffffffu, ge);
+  return m ? L + __ffs(m) - 1 : R;
+}
+
+__global__ void dm_range_kernel(const __grid_constant__ ContribTable cs, long long a, long long b,
+                                long long* __restrict__ ranges) {
+  const int c = blockIdx.x;
+  const Contrib& C = cs.c[c];
+  long long lo, hi;
+  if (C.dense) {
+    lo = a < C.count ? a : C.count;
+    hi = b < C.count ? b : C.count;
+  } else {
+    Windows W;
+    W.load(C.win);
+    lo = warp_lower_bound(C, W, a);
+    hi = warp_lower_bound(C, W, b);
+  }
+  if (threadIdx.x == 0) {
+    ranges[2 * c] = lo;
+    ranges[2 * c + 1] = hi;
+  }
+}
+
+__device__ __forceinline__ void last_block_release(unsigned* blocks_local, unsigned long long* counter) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atomicAdd(blocks_local, 1u) == total - 1) {
+      *blocks_local = 0u;
+      __threadfence_system();
+      red_release_sys_add_u64(counter, 1ull);
+    }
+  }
+}
+
+__global__ void dm_prepass_kernel(const __grid_constant__ ContribTable cs, const long long* __restrict__ ranges,
+                                  double* stats_dst, unsigned long long* arrivals_dst, unsigned* blocks_local) {
+  __shared__ float shs[32];
+  const int c = blockIdx.y;
+  const Contrib& C = cs.c[c];
+  const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
+  float ss = 0.f, mx = 0.f;
+  int nf = 0;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < hi; i0 += stride * MUNR) {
+    float v[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      v[u] = i < hi ? contrib_value(C, i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      if (!isfinite(v[u])) { nf = 1; continue; }
+      ss += v[u] * v[u];
+      mx = fmaxf(mx, fabsf(v[u]));
+    }
+  }
+  const float t = block_sum(ss, shs);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0 && mx > 0.f)
+    atomicMax_system(reinterpret_cast<unsigned long long*>(stats_dst + c * 3 + 1),
+                     (unsigned long long)__double_as_longlong((double)mx));
+  nf = __syncthreads_or(nf);
+  if (threadIdx.x == 0) {
+    if (t != 0.f) atomicAdd_system(stats_dst + c * 3 + 0, (double)t);
+    if (nf) atomicAdd_system(stats_dst + c * 3 + 2, 1.0);
+  }
+  last_block_release(blocks_local, arrivals_dst);
+}
+
+// One block waits for another node's step: the wait covers host work on that node (rank 0 plans on the
+// host between its statistics and its coefficients), so it is bounded by `bound_ns` rather than the
+// library-wide 2 s; the full grids launched after it on the same stream then find the flag set.
+__global__ void dm_wait_kernel(const unsigned long long* counter, unsigned long long target, int site,
+                               unsigned long long bound_ns) {
+  if (threadIdx.x == 0) wait_ge_u64(counter, target, site, bound_ns);
+}
+
+struct PeerFloats {
+  float* p[8];
+};
+struct PeerFlags {
+  unsigned long long* p[8];
+};
+
+__global__ void dm_publish_kernel(const float* __restrict__ coefs, int n, PeerFloats dst, PeerFlags flags, int W,
+                                  unsigned long long att) {
+  const int t = threadIdx.x;
+  if (t < n) {
+    const float v = coefs[t];
+    for (int r = 0; r < W; ++r) dst.p[r][t] = v;
+  }
+  __syncthreads();
+  if (t == 0) {
+    __threadfence_system();
+    for (int r = 0; r < W; ++r) st_release_sys_u64(flags.p[r], att);
+  }
+}
+
+// Block-uniform: waits for the coefficients of attempt `att` and stages them in shared memory.
+__device__ __forceinline__ bool dm_load_coefs(const unsigned long long* flag, unsigned long long att,
+                                              const float* coefs, int n, float* sh_coef, int* sh_ok) {
+  if (threadIdx.x == 0) {
+    int ok = wait_ge_u64(flag, att, 910) ? 1 : 0;
+    if (ok)
+      for (int c = 0; c < n; ++c) sh_coef[c] = *reinterpret_cast<const volatile float*>(coefs + c);
+    *sh_ok = ok;
+  }
+  __syncthreads();
+  return *sh_ok != 0;
+}
+
+__global__ void dm_apply_dense_kernel(const __grid_constant__ ContribTable cs, int n, long long a4, long long b4,
+                                      const float* coefs, const unsigned long long* flag, unsigned long long att,
+                                      float* __restrict__ theta) {
+  __shared__ float shc[MAX_CONTRIB];
+  __shared__ int ok;
+  if (!dm_load_coefs(flag, att, coefs, n, shc, &ok)) return;
+  for (long long i = a4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < b4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < n; ++c) {
+      const Contrib& C = cs.c[c];
+      const float k = shc[c];
+      if (!C.dense || k == 0.f || 4 * i >= C.count) continue;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(C.val) + i);
+      acc.x += k * v.x;
+      acc.y += k * v.y;
+      acc.z += k * v.z;
+      acc.w += k * v.w;
+    }
+    float4 t = reinterpret_cast<float4*>(theta)[i];
+    t.x += acc.x;
+    t.y += acc.y;
+    t.z += acc.z;
+    t.w += acc.w;
+    reinterpret_cast<float4*>(theta)[i] = t;
+  }
+}
+
+__global__ void dm_apply_sparse_kernel(const __grid_constant__ ContribTable cs, int n,
+                                       const long long* __restrict__ ranges, const float* coefs,
+                                       const unsigned long long* flag, unsigned long long att,
+                                       float* __restrict__ theta) {
+  __shared__ float shc[MAX_CONTRIB];
+  __shared__ int ok;
+  if (!dm_load_coefs(flag, att, coefs, n, shc, &ok)) return;
+  const int c = blockIdx.y;
+  const Contrib& C = cs.c[c];
+  const float k = shc[c];
+  if (C.dense || k == 0.f) return;
+  Windows W;
+  W.load(C.win);
+  const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < hi; i0 += stride * MUNR) {
+    int j[MUNR];
+    float v[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      j[u] = i < hi ? __ldg(C.idx + i) : -1;
+      v[u] = i < hi ? contrib_value(C, i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u)
+      if (j[u] >= 0) atomicAdd(theta + W.flat(j[u], i0 + u * stride), v[u] * k);
+  }
+}
+
+__global__ void dm_broadcast_kernel(const float* __restrict__ theta, long long a4, long long b4, float* mc32, Dests d,
+                                    unsigned long long* done_dst, unsigned* blocks_local) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = a4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < b4; i0 += stride * MUNR) {
+    float4 t[MUNR];
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < b4) t[u] = reinterpret_cast<const float4*>(theta)[i];
+    }
+#pragma unroll
+    for (int u = 0; u < MUNR; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < b4) store_dests(mc32, d, theta, i, t[u]);
+    }
+  }
+  last_block_release(blocks_local, done_dst);
+}
+
 // Node side of a checkpoint swap: master <- stage32, p16 <- stage16 (or cast), snapshot <- master.
 // Checkpoint swap. rebase == 0: master = snap = staged fp32, p16 = staged bf16 (or its cast).
 // rebase == 1: the steps trained since the last push are carried onto the new checkpoint:
@@ -312,5 +568,76 @@ DT_API int dt_swap_in(const float* s32, const void* s16, float* master, void* p1
   swap_in_kernel<<<grid_cap(n / 4, 256, 148 * 8), 256, 0, st>>>(s32, reinterpret_cast<const __nv_bfloat16*>(s16),
                                                                master, reinterpret_cast<__nv_bfloat16*>(p16), snap, ef,
                                                                n, rebase);
+  return (int)cudaGetLastError();
+}
+
+// ───────────────────────────── distributed merge entry points ─────────────────────────────
+// `contribs`: host table of n packed Contrib records (as dt_merge_prepass). Ranges scratch: 2*n int64.
+DT_API int dt_dm_range(const void* contribs, int n, long long a, long long b, long long* ranges, cudaStream_t st) {
+  if (n <= 0) return 0;
+  if (n > MAX_CONTRIB) return -13;
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  dm_range_kernel<<<n, 32, 0, st>>>(tab, a, b, ranges);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_dm_prepass(const void* contribs, int n, long long max_len, const long long* ranges, double* stats_dst,
+                         unsigned long long* arrivals_dst, unsigned* blocks_local, cudaStream_t st) {
+  if (n <= 0 || n > MAX_CONTRIB) return -13;
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  dim3 grid(grid_cap(max_len / MUNR + 1, 256, 148 * 2), n);
+  dm_prepass_kernel<<<grid, 256, 0, st>>>(tab, ranges, stats_dst, arrivals_dst, blocks_local);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_dm_wait(const unsigned long long* counter, unsigned long long target, int site,
+                      unsigned long long bound_ns, cudaStream_t st) {
+  dm_wait_kernel<<<1, 32, 0, st>>>(counter, target, site, bound_ns);
+  return (int)cudaGetLastError();
+}
+
+// coef_dsts / flag_dsts: host arrays of W device pointers (every node's coefficient buffer and flag).
+DT_API int dt_dm_publish(const float* coefs, int n, void* const* coef_dsts, void* const* flag_dsts, int W,
+                         unsigned long long att, cudaStream_t st) {
+  if (n <= 0 || n > MAX_CONTRIB || W <= 0 || W > 8) return -13;
+  PeerFloats d{};
+  PeerFlags f{};
+  for (int r = 0; r < W; ++r) {
+    d.p[r] = reinterpret_cast<float*>(coef_dsts[r]);
+    f.p[r] = reinterpret_cast<unsigned long long*>(flag_dsts[r]);
+  }
+  dm_publish_kernel<<<1, MAX_CONTRIB, 0, st>>>(coefs, n, d, f, W, att);
+  return (int)cudaGetLastError();
+}
+
+// Adds the weighted members into theta[a, b) (a, b multiples of 4) once the flag reaches `att`.
+DT_API int dt_dm_apply(const void* contribs, int n, long long max_len, const long long* ranges, long long a, long long b,
+                       const float* coefs, const unsigned long long* flag, unsigned long long att, float* theta,
+                       int has_dense, int has_sparse, cudaStream_t st) {
+  if (n <= 0 || n > MAX_CONTRIB) return -13;
+  if ((a | b) & 3) return -10;
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  if (has_dense && b > a)
+    dm_apply_dense_kernel<<<grid_cap((b - a) / 4, 256, 148 * 4), 256, 0, st>>>(tab, n, a / 4, b / 4, coefs, flag,
+                                                                                att, theta);
+  if (has_sparse) {
+    dim3 grid(grid_cap(max_len / MUNR + 1, 256, 148 * 4), n);
+    dm_apply_sparse_kernel<<<grid, 256, 0, st>>>(tab, n, ranges, coefs, flag, att, theta);
+  }
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_dm_broadcast(const float* theta, long long a, long long b, void* mc32, void* const* stage32, int n_dest,
+                           unsigned long long* done_dst, unsigned* blocks_local, cudaStream_t st) {
+  if ((a | b) & 3) return -10;
+  Dests d;
+  if (int e = make_dests(d, mc32, stage32, n_dest)) return e;
+  const long long n4 = (b - a) / 4;
+  dm_broadcast_kernel<<<grid_cap(n4 / MUNR + 1, 256, 148 * 4), 256, 0, st>>>(theta, a / 4, b / 4,
+                                                                             reinterpret_cast<float*>(mc32), d,
+                                                                             done_dst, blocks_local);
   return (int)cudaGetLastError();
 }

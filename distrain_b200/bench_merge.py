@@ -12,12 +12,15 @@ tokens * 0.9^staleness.
 Per (model, top-k), every iteration:
   1. every rank compresses its delta (+ error feedback) into its symmetric (peer-mapped) payload buffer:
      pass A + radix top-k + ordered compaction + INT8 block 256;
-  2. rank 0 (the coordinator) pulls all N payloads over NVLink with the merge kernels (prepass norms and
-     validation with its host round trip, weighted dequant scatter-add straight into its fp32 checkpoint,
-     which is its own staging buffer) and writes the new fp32 checkpoint into every rank's staging buffer with NVLS
-     multimem stores (per-peer stores when the box offers no multicast object).
-Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, total = their
-sum (the steps are separated by barriers). Bytes over NVLink: payloads pulled from the N-1 peers plus the
+  2. the distributed merge (every rank merges one slice of the flat range: pulls that slice of all N
+     payloads over NVLink, adds partial norms into rank 0's statistics, applies rank 0's coefficients to
+     its slice of the checkpoint - its own staging buffer - and writes the slice into every rank's
+     staging buffer with NVLS multimem stores, or per-peer stores without a multicast object);
+  3. for comparison, the single-coordinator merge of the same payloads (rank 0 pulls all of them,
+     scatter-adds into its checkpoint and broadcasts the whole checkpoint).
+Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, from before
+its phase 1 to after every rank's phase 3 (the three phases are separated by NCCL barriers, which are
+inside the timed interval), total = their sum. Bytes over NVLink: payloads pulled from the N-1 peers plus the
 checkpoint stored through the multicast object (each GPU receives it once).
 Comparison arm per model: delta = snapshot - master scaled by its merge weight, ncclAllReduce(SUM) of the
 n fp32 values, the same apply and bf16 cast on every rank; max over ranks. One JSON line per case on
@@ -50,7 +53,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     from .config import preset, CompressionConfig
     from .models.params import ParamLayout
     from .parallel.compression import DeviceCompressor, DevicePayload
-    from .parallel.merge import DeviceMerger, Contribution
+    from .parallel.merge import DeviceMerger, DistributedMerger, Contribution
     from .parallel.inbox import _symm_alloc
     from . import ops
 
@@ -71,8 +74,12 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     stage_buf, stage_ptrs, stage_mc, _stage_h = _symm_alloc(stage_bytes, dev, world)
     p32 = [p for p in stage_ptrs]
     mc32 = stage_mc or 0
-    merger = (DeviceMerger(n, dev, snap, momentum=0.0, theta_buffer=stage_buf[:n * 4].view(torch.float32))
-              if rank == 0 else None)
+    theta = stage_buf[:n * 4].view(torch.float32)
+    theta.copy_(snap)
+    ctl, ctl_ptrs, _, _ctl_h = _symm_alloc(DistributedMerger.CTL_BYTES, dev, world)
+    dm = DistributedMerger(rank, world, n, dev, theta, p32, mc32, ctl, ctl_ptrs)
+    single = DeviceMerger(n, dev, None, momentum=0.0, theta_buffer=theta) if rank == 0 else None
+    att = 0
     results = []
 
     def barrier():
@@ -83,7 +90,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         cap = DeviceCompressor.capacity_for(L, k)
         payload = DevicePayload(pay_buf[:DevicePayload.nbytes(cap, 256)], cap, 256)
         comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=k, int8_block=256), payload=payload)
-        t_comp, t_merge, pulled, infos = [], [], 0, None
+        t_comp, t_merge, t_single, pulled, infos = [], [], [], 0, None
         for it in range(warmup + iters):
             comp.snap.copy_(snap)
             comp.ef.copy_(ef0)
@@ -102,34 +109,61 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
             else:
                 counts = [cnt]
             counts = [int(c.item()) for c in counts]
-            barrier()
-            mms = 0.0
+            base = pay_buf.data_ptr()
+            contribs = []
+            for r in range(world):
+                off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
+                contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q), win_ptr=off(payload.win),
+                                             val_ptr=off(payload.val), scales_ptr=off(payload.scales),
+                                             count=counts[r], block=256, dense=False, weight=weights[r],
+                                             node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
+            pulled = sum(c.wire_bytes for c in contribs[1:])
+            # distributed merge: every rank merges its slice (timed on rank 0, which waits for all slices)
+            att += 1
             if rank == 0:
-                base = pay_buf.data_ptr()
-                contribs = []
-                for r in range(world):
-                    off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
-                    contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q), win_ptr=off(payload.win),
-                                                 val_ptr=off(payload.val), scales_ptr=off(payload.scales),
-                                                 count=counts[r], block=256, dense=False, weight=weights[r],
-                                                 node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
-                m0, m1 = _events()
-                m0.record(merger.stream)
-                infos = merger.merge(contribs, 1.0, mc32=mc32, stage32=p32)
-                m1.record(merger.stream)
-                merger.stream.synchronize()
-                mms = m0.elapsed_time(m1)
-                pulled = sum(c.wire_bytes for c in contribs[1:])
+                dm.reset_stats()
+            barrier()
+            m0, m1 = _events()
+            m0.record(dm.stream)
+            dm.prepass(contribs)           # phase 1: every rank, partial statistics into rank 0's
+            dm.check("prepass")
+            barrier()
+            if rank == 0:                  # phase 2: rank 0 plans and publishes the coefficients
+                infos, failure = dm.plan_publish(contribs, 1.0, att)
+                dm.check("publish")
+                assert failure is None, failure
+            barrier()
+            dm.apply(contribs, att)        # phase 3: every rank, its slice + broadcast
+            dm.check("apply")
+            barrier()
+            if rank == 0:
+                dm.finish(att)
+            m1.record(dm.stream)
+            dm.stream.synchronize()
+            mms = m0.elapsed_time(m1) if rank == 0 else 0.0
+            barrier()
+            # single-coordinator merge of the same payloads (rank 0 pulls everything and broadcasts)
+            sms = 0.0
+            if rank == 0:
+                s0, s1 = _events()
+                s0.record(single.stream)
+                single.merge(contribs, 1.0, mc32=mc32, stage32=p32)
+                s1.record(single.stream)
+                single.stream.synchronize()
+                sms = s0.elapsed_time(s1)
             barrier()
             if it >= warmup:
                 t_comp.append(c0.elapsed_time(c1))
                 t_merge.append(mms)
+                t_single.append(sms)
         cms = _max_over_ranks(sorted(t_comp)[len(t_comp) // 2], dev)
         mms = _max_over_ranks(sorted(t_merge)[len(t_merge) // 2], dev)
+        sms = _max_over_ranks(sorted(t_single)[len(t_single) // 2], dev)
         if rank == 0:
             results.append({"bench": "compress_merge_broadcast", "model": name, "params": L.num_params(),
                             "n_nodes": world, "top_k": k, "compress_ms": round(cms, 3), "merge_ms": round(mms, 3),
-                            "total_ms": round(cms + mms, 3), "accepted": infos["accepted"],
+                            "total_ms": round(cms + mms, 3), "merge": f"distributed over {world} GPUs",
+                            "single_coordinator_merge_ms": round(sms, 3), "accepted": infos["accepted"],
                             "payload_bytes_pulled_nvlink": pulled,
                             "checkpoint_bytes_broadcast": n * 4, "broadcast": "nvls multimem" if mc32 else "per-peer",
                             "staleness": stale, "tokens": tokens,

@@ -38,7 +38,7 @@ import torch.distributed as dist
 from ..config import RunConfig
 from ..protocol import Accumulator, DeltaPush, delta_path
 from .compression import DeviceCompressor, DevicePayload
-from .merge import Contribution, DeviceMerger
+from .merge import Contribution, DeviceMerger, DistributedMerger
 
 
 # ─────────────────────────────── control bus ───────────────────────────────
@@ -154,6 +154,16 @@ class InBoxSync:
                                                                                    world, dp_group)
         self.compressor = DeviceCompressor(self.layout, self.device, cfg, payload=self.slots[0])
         self.compressor.reset(eng.master)
+        # without tensor parallelism every node merges one slice of the checkpoint (DistributedMerger);
+        # every node's slot starts as the (identical) initial weights
+        self.dm = None
+        if n_shards == 1:
+            self.ctl, self.ctl_ptrs, _, self._ctl_h = _symm_alloc(DistributedMerger.CTL_BYTES, self.device, world,
+                                                                  dp_group)
+            self.stage_view().copy_(eng.master)
+            self.dm = DistributedMerger(rank, world, self.n, self.device, self.stage_view(), self.stage_ptrs,
+                                        self.stage_mc, self.ctl, self.ctl_ptrs,
+                                        stream=torch.cuda.Stream(device=self.device, priority=-100))
         multi = world * n_shards > 1
         self.bus = StoreBus(f"dtinbox/s{shard}/" if n_shards > 1 else "dtinbox/") if multi else LocalBus()
         self.shared = self.bus if n_shards == 1 else StoreBus("dtinbox/shared/")
@@ -166,8 +176,14 @@ class InBoxSync:
         self.poster.start()
         self.latest_version = 0
         self.coord = None
+        self.dm_error: Optional[BaseException] = None
+        self.dm_thread = None
         if rank == 0:
             self.coord = InBoxCoordinator(self, run, world) if shard == 0 else ShardFollower(self, run, world)
+        elif self.dm is not None:
+            self.dm_thread = threading.Thread(target=self._dm_loop, daemon=True)
+            self.dm_thread.start()
+        torch.cuda.synchronize(self.device)
         if world * n_shards > 1:
             dist.barrier()
 
@@ -345,12 +361,71 @@ class InBoxSync:
         ev_done.synchronize()
         self.bus.set(f"consumed/{self.rank}", str(new_version))
 
+    def member_contribution(self, m) -> Contribution:
+        """A merge member [rank, slot, count, block, weight] as seen from this node (peer pointers)."""
+        r, slot, count, blk, weight = m[:5]
+        p = self.slots[slot]
+        base_local = self.pay_buf.data_ptr()
+        peer = self.pay_ptrs[r]
+        off = lambda t: t.data_ptr() - base_local + peer
+        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
+                            scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
+                            weight=weight, wire_bytes=p.wire_bytes(count))
+
+    def _poll(self, key: str, alt: Optional[str] = None, timeout: float = 120.0):
+        """Wait for `key` (or `alt`) on the control bus; returns (which key, value)."""
+        t0 = time.time()
+        while not self.stop.is_set():
+            v = self.bus.get(key)
+            if v is not None:
+                return key, v
+            if alt is not None:
+                v = self.bus.get(alt)
+                if v is not None:
+                    return alt, v
+            if time.time() - t0 > timeout:
+                raise TimeoutError(f"control bus key {key} not set within {timeout} s")
+            time.sleep(0.0001)
+        raise _Shutdown()
+
+    def _dm_loop(self):
+        """Nodes other than rank 0: run this node's share of every merge attempt rank 0 announces
+        (phase 1 prepass, then - once rank 0 has published the coefficients - phase 3 apply)."""
+        torch.cuda.set_device(self.device)
+        att = 0
+        try:
+            while not self.stop.is_set():
+                raw = self.bus.get(f"dm/{att + 1}")
+                if raw is None:
+                    time.sleep(0.0001)
+                    continue
+                att += 1
+                plan = json.loads(raw)
+                contribs = [self.member_contribution(m) for m in plan["members"]]
+                self.dm.prepass(contribs)
+                self.dm.check("prepass")
+                self.bus.set(f"dmpre/{att}/{self.rank}", "1")
+                which, _ = self._poll(f"dmcoef/{att}", f"dmabort/{att}")
+                if which.startswith("dmabort"):
+                    continue
+                self.dm.apply(contribs, att)
+                self.dm.check("apply")
+                self.bus.set(f"dmdone/{att}/{self.rank}", "1")
+        except _Shutdown:
+            pass
+        except BaseException as e:  # surfaced by close()
+            self.dm_error = e
+
     def close(self):
         if self.coord is not None:
             self.coord.close()
         self.stop.set()
         self.poster.join(timeout=5)
+        if self.dm_thread is not None:
+            self.dm_thread.join(timeout=30)
         torch.cuda.synchronize()
+        if self.dm_error is not None:
+            raise RuntimeError(f"distributed merge worker failed: {self.dm_error!r}") from self.dm_error
 
 
 class _Shutdown(Exception):
@@ -375,10 +450,13 @@ class InBoxCoordinator:
         self.next_seq = [1] * world
         self.payload_of: Dict[tuple, dict] = {}
         # highest priority: the training graph keeps every SM busy with persistent GEMMs, so merge
-        # kernels must be first in line whenever blocks retire or they starve for seconds
-        stream = torch.cuda.Stream(device=sync.device, priority=-100)
-        self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
-                                   theta_buffer=sync.stage_view())
+        # kernels must be first in line whenever blocks retire or they starve for seconds (the distributed
+        # merger has its own such stream)
+        self.merger = None
+        if sync.dm is None:
+            stream = torch.cuda.Stream(device=sync.device, priority=-100)
+            self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
+                                       theta_buffer=sync.stage_view())
         self.version = 0
         self.merges: List[dict] = []
         self.failed: List[str] = []
@@ -441,6 +519,8 @@ class InBoxCoordinator:
                     time.sleep(0.001)
 
     def _merge(self):
+        if self.sync.dm is not None:
+            return self._merge_distributed()
         snap = self.acc.begin_merge()
         try:
             contribs = [self._contribution(c) for c in snap.contributions]
@@ -499,6 +579,91 @@ class InBoxCoordinator:
         except Exception as e:
             # like a failed reference aggregation: count it, drop the contributions of this attempt
             # (their payload slots are released) and keep serving
+            self.failed.append(repr(e))
+            for c in snap.contributions:
+                r = int(c.node_id.split("-")[1])
+                self._release(r, c.seq_num)
+                self.payload_of.pop((c.node_id, c.seq_num), None)
+            self.acc.state.contributions = [c for c in self.acc.state.contributions
+                                            if (c.node_id, c.seq_num) not in {(x.node_id, x.seq_num)
+                                                                             for x in snap.contributions}]
+            self.acc.abort_merge()
+
+    def _wait_key(self, key: str, timeout: float = 120.0):
+        t0 = time.time()
+        while self.bus.get(key) is None:
+            if self.stop.is_set():
+                raise _Shutdown()
+            if time.time() - t0 > timeout:
+                raise TimeoutError(f"control bus key {key} not set within {timeout} s")
+            time.sleep(0.0001)
+
+    def _merge_distributed(self):
+        """Merge with every node working on its slice (DistributedMerger): announce the members on the bus,
+        run this node's share plus the plan, publish the version."""
+        snap = self.acc.begin_merge()
+        try:
+            contribs = [self._contribution(c) for c in snap.contributions]
+            members = []
+            for c in snap.contributions:
+                body = self.payload_of[(c.node_id, c.seq_num)]
+                members.append([body["_rank"], body["_slot"], body["_count"],
+                                self.sync.slots[body["_slot"]].block, c.weight])
+            new_version = self.version + 1
+            self._wait_consumed(new_version)
+            dm = self.sync.dm
+            self.attempt += 1
+            att = self.attempt
+            dm.reset_stats()
+            t0 = time.time()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(dm.stream)
+            W = self.world
+            if W > 1:
+                self.bus.set(f"dm/{att}", json.dumps({"version": new_version, "members": members}))
+            try:
+                dm.prepass(contribs)
+                dm.check("prepass")
+                for r in range(1, W):
+                    self._wait_key(f"dmpre/{att}/{r}")
+                info, failure = dm.plan_publish(contribs, self.run.outer_lr, att)
+                dm.check("publish")
+            except BaseException:
+                if W > 1:
+                    self.bus.set(f"dmabort/{att}", "1")
+                raise
+            if W > 1:
+                self.bus.set(f"dmcoef/{att}", "1")
+            dm.apply(contribs, att)
+            dm.check("apply")
+            for r in range(1, W):
+                self._wait_key(f"dmdone/{att}/{r}")
+            dm.finish(att)
+            if failure is not None:
+                raise failure
+            ev1.record(dm.stream)
+            ev1.synchronize()
+            info["device_ms"] = ev0.elapsed_time(ev1)
+            info["wall_ms"] = (time.time() - t0) * 1e3
+            info["version"] = new_version
+            info["n_contrib"] = len(contribs)
+            mc = bool(self.sync.stage_mc)
+            info["broadcast_bytes"] = self.sync.n * 4 * (1 if mc else max(self.world - 1, 1))
+            info["multicast"] = mc
+            info["distributed"] = self.world
+            self.merges.append(info)
+            for c in snap.contributions:
+                r = int(c.node_id.split("-")[1])
+                self._release(r, c.seq_num)
+                self.payload_of.pop((c.node_id, c.seq_num), None)
+            self.version = new_version
+            tokens = sum(c.tokens_processed for c in snap.contributions)
+            self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
+            self.shared.set("version", str(new_version))
+        except _Shutdown:
+            self.acc.abort_merge()
+            raise
+        except Exception as e:
             self.failed.append(repr(e))
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])

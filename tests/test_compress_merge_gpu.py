@@ -212,3 +212,47 @@ def test_inbox_swap_policies(swap_mode, ef_on_swap):
         steps = [json.loads(node.sync.bus.get(f"push/0/{s}"))["inner_steps"] for s in range(1, node.sync.seq + 1)]
         assert all(s >= run.push_every for s in steps), steps
     node.close()
+
+
+def test_distributed_merger_single_node_matches_reference():
+    """The distributed merger with one node (its slice is the whole range) against the fp32 reference."""
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor, dequantize_int8
+    from distrain_b200.parallel.merge import DistributedMerger, Contribution, merge_reference
+    L = _layout()
+    dev = torch.device("cuda")
+    torch.manual_seed(2)
+    theta0 = torch.randn(L.total, device=dev) * 0.02
+    cfg = CompressionConfig(top_k_fraction=0.2, quantize_int8=True, int8_block=256)
+    contribs, dense_deltas, weights, keep = [], [], [], []
+    for i, sc in enumerate([1.0, 4.0]):
+        comp = DeviceCompressor(L, dev, cfg)
+        d = torch.randn(L.total, device=dev) * 1e-3 * sc
+        comp.snap.copy_(theta0)
+        comp.begin(theta0 - d)
+        comp.finish()
+        torch.cuda.synchronize()
+        K = comp.read_stats()["num_params_kept"]
+        p = comp.payload
+        keep.append(comp)
+        w = 1000.0 / (i + 1)
+        weights.append(w)
+        contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                     scales_ptr=p.scales.data_ptr(), win_ptr=p.win.data_ptr(), count=K, block=256,
+                                     dense=False, weight=w))
+        deq = dequantize_int8(p.q[:K].cpu(), p.scales[:(K + 255) // 256].cpu(), 256)
+        dense = torch.zeros(L.total)
+        dense[p.global_indices(K).cpu()] = deq
+        dense_deltas.append({e.name: dense[e.offset:e.offset + e.numel] for e in L.entries})
+    theta = theta0.clone()
+    ctl = torch.zeros(DistributedMerger.CTL_BYTES, dtype=torch.uint8, device=dev)
+    dm = DistributedMerger(0, 1, L.total, dev, theta, [theta.data_ptr()], 0, ctl, [ctl.data_ptr()])
+    ck = {e.name: theta0[e.offset:e.offset + e.numel].cpu() for e in L.entries}
+    for att in (1, 2):
+        dm.reset_stats()
+        info = dm.run_local(contribs, 1.0, att)
+        ck, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=0.0)
+        got = theta.cpu()
+        for e in L.entries:
+            assert torch.allclose(got[e.offset:e.offset + e.numel], ck[e.name], atol=1e-7, rtol=1e-5), (att, e.name)
+        assert info["accepted"] == 2

@@ -85,4 +85,6 @@ def test_windowed_payload_and_merge():
     m.stream.synchronize()
     torch.testing.assert_close(theta[gi], -p.val[:K], rtol=0, atol=0)
     assert float(theta.abs().sum()) == pytest.approx(float(p.val[:K].abs().double().sum()), rel=1e-5)
-    assert torch.equal(dst, theta)
+    diff = (dst != theta).nonzero().flatten()
+    assert diff.numel() == 0, (f"{diff.numel()} broadcast mismatches, first {diff[:4].tolist()} last "
+                               f"{diff[-4:].tolist()}; dst {dst[diff[:4]].tolist()} theta {theta[diff[:4]].tolist()}")
