@@ -107,6 +107,7 @@ def test_device_merge_matches_reference(momentum, in_place):
     merger = DeviceMerger(L.total, dev, theta, momentum=momentum, theta_buffer=own)
     s32 = torch.zeros(L.total, device=dev)
     dests = [s32.data_ptr()] + ([own.data_ptr()] if in_place else [])  # the own slot is skipped by the kernel
+    torch.cuda.synchronize()  # the merger's stream does not wait for the default stream's fills
     info = merger.merge(contribs, 1.0, stage32=dests)
     torch.cuda.synchronize()
     ck = {e.name: theta[e.offset:e.offset + e.numel].cpu() for e in L.entries}
@@ -247,6 +248,7 @@ def test_distributed_merger_single_node_matches_reference():
     theta = theta0.clone()
     ctl = torch.zeros(DistributedMerger.CTL_BYTES, dtype=torch.uint8, device=dev)
     dm = DistributedMerger(0, 1, L.total, dev, theta, [theta.data_ptr()], 0, ctl, [ctl.data_ptr()])
+    torch.cuda.synchronize()
     ck = {e.name: theta0[e.offset:e.offset + e.numel].cpu() for e in L.entries}
     for att in (1, 2):
         dm.reset_stats()

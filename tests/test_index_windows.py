@@ -81,6 +81,7 @@ def test_windowed_payload_and_merge():
     c = Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=0, val_ptr=p.val.data_ptr(), scales_ptr=0, count=K, block=0,
                      dense=False, weight=1.0, win_ptr=p.win.data_ptr())
     dst = torch.zeros(n, device=dev)
+    torch.cuda.synchronize()  # the merger's stream does not wait for the default stream's fills
     m.accumulate_apply([c], [1.0], 1.0, stage32=[dst.data_ptr()])
     m.stream.synchronize()
     torch.testing.assert_close(theta[gi], -p.val[:K], rtol=0, atol=0)
