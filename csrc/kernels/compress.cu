@@ -409,8 +409,10 @@ __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ c
 }
 
 // Per block of `blk` kept values: absmax/127 scale (1 if all zero), round-half-away int8.
+// `wire` (3 doubles): statistics of the dequantised values as they go on the wire - sum of squares,
+// max |x| (as ordered bits), non-finite blocks - which the coordinator validates and clips on.
 __global__ void quant_kernel(const float* __restrict__ val, const long long* __restrict__ total, int blk,
-                             signed char* __restrict__ q, float* __restrict__ scales) {
+                             signed char* __restrict__ q, float* __restrict__ scales, double* __restrict__ wire) {
   __shared__ float sh[32];
   const long long n = *total;
   const long long b = blockIdx.x;
@@ -431,10 +433,23 @@ __global__ void quant_kernel(const float* __restrict__ val, const long long* __r
   const float amax = sh[0];
   const float scale = amax == 0.f ? 1.f : amax / 127.f;
   if (threadIdx.x == 0) scales[b] = scale;
+  float ss = 0.f, dmax = 0.f;
   for (long long i = s0 + threadIdx.x; i < e; i += blockDim.x) {
     float r = roundf(val[i] / scale);
     r = fminf(fmaxf(r, -127.f), 127.f);
     q[i] = (signed char)r;
+    const float dq = r * scale;
+    ss += dq * dq;
+    dmax = fmaxf(dmax, fabsf(dq));
+  }
+  __syncthreads();  // sh reused
+  const float tss = block_sum(ss, sh);
+  for (int o = 16; o > 0; o >>= 1) dmax = fmaxf(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
+  if ((threadIdx.x & 31) == 0 && dmax > 0.f)
+    atomicMax(reinterpret_cast<unsigned long long*>(wire + 1), (unsigned long long)__double_as_longlong((double)dmax));
+  if (threadIdx.x == 0) {
+    atomicAdd(wire, (double)tss);
+    if (!isfinite(amax)) atomicAdd(wire + 2, 1.0);
   }
 }
 
@@ -443,7 +458,7 @@ __global__ void quant_kernel(const float* __restrict__ val, const long long* __r
 // ───────────────────────────── host API ─────────────────────────────
 // Workspace layout (device, caller-allocated, size from dt_compress_workspace_bytes):
 //   SegState[nseg] | hist1[nseg*NB1] | hist2[nseg*NB2] | hist3[nseg*NB3] |
-//   cnt_gt[nchunks] | cnt_eq[nchunks] | eq_take[nchunks] | out_off[nchunks] | total[1]
+//   cnt_gt[nchunks] | cnt_eq[nchunks] | eq_take[nchunks] | out_off[nchunks] | total[1] wire[3] (doubles)
 struct WsPtrs {
   SegState* seg;
   unsigned *h1, *h2, *h3;
@@ -491,7 +506,13 @@ __global__ void export_stats_kernel(const SegState* seg, int nseg, const long lo
     out[s * 6 + 4] = (double)seg[s].nonfinite;
     out[s * 6 + 5] = (double)seg[s].len;
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) out[nseg * 6] = (double)*total;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    out[nseg * 6] = (double)*total;
+    const double* wire = reinterpret_cast<const double*>(total + 1);  // quantised pushes only
+    out[nseg * 6 + 1] = wire[0];
+    out[nseg * 6 + 2] = wire[1];
+    out[nseg * 6 + 3] = wire[2];
+  }
 }
 
 // Pass A (training stream). seg_len: device array of per-segment element counts.
@@ -525,13 +546,32 @@ DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstar
   if (out_win) window_kernel<<<1, 32, 0, st>>>(w.off, w.total, win_chunk, nwin, nchunks, out_win);
   if (quant_block > 0 && out_q) {
     long long nblk = (capacity + quant_block - 1) / quant_block;
-    quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, quant_block, out_q, out_scales);
+    quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, quant_block, out_q, out_scales,
+                                                 reinterpret_cast<double*>(w.total + 1));
   }
   return (int)cudaGetLastError();
 }
 
+// Raw push (no selection): the whole delta + error feedback formed by pass A leaves as dense fp32 and the
+// error-feedback buffer is cleared (nothing is left behind). n: a multiple of 4.
+__global__ void raw_kernel(float* __restrict__ ef, float* __restrict__ out, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    reinterpret_cast<float4*>(out)[i] = reinterpret_cast<const float4*>(ef)[i];
+    reinterpret_cast<float4*>(ef)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+DT_API int dt_compress_raw(float* ef, float* out, long long n, cudaStream_t st) {
+  if (n % 4) return -10;
+  long long b = (n / 4 + 255) / 256;
+  if (b > 148 * 8) b = 148 * 8;
+  raw_kernel<<<(unsigned)(b < 1 ? 1 : b), 256, 0, st>>>(ef, out, n / 4);
+  return (int)cudaGetLastError();
+}
+
 // Per-segment statistics into a device double array: [s*6 + {sumsq, kept_sq, k, maxabs, nonfinite, len}],
-// then the total kept count at [nseg*6].
+// then the total kept count at [nseg*6] and the dequantised wire statistics {sum of squares, max |x|,
+// non-finite} at [nseg*6 + 1..3] (zero unless the push was quantised).
 DT_API int dt_compress_export_stats(void* ws, int nseg, int nchunks, double* out, cudaStream_t st) {
   WsPtrs w = carve(ws, nseg, nchunks);
   export_stats_kernel<<<(nseg + 255) / 256, 256, 0, st>>>(w.seg, nseg, w.total, out);

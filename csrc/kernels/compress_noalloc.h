@@ -18,7 +18,7 @@
 //    threads - race on it; serialise them (one stream, one caller at a time).
 //  * No cudaMalloc, cudaFree or allocating library routine is called.
 //  * Arguments and outputs are those of dt_compress_begin + dt_compress_finish (one stream), plus
-//    optional per-segment statistics (dt_compress_export_stats layout) in stats_out.
+//    optional per-segment statistics (dt_compress_export_stats layout: nseg * 6 + 4 doubles) in stats_out.
 //  * Returns 0, a CUDA error code, or -20 (problem exceeds the scratch), -21 (device ordinal >= 64).
 #pragma once
 #include <cuda_runtime.h>

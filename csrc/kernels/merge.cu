@@ -206,20 +206,18 @@ __global__ void broadcast_kernel(const float* __restrict__ theta, long long n, f
 }
 
 // ───────────── distributed merge: every node merges one slice of the flat range ─────────────
-// Node r owns the flat range [a_r, b_r) (float4-aligned, about n/W elements). For a merge attempt `att`
-// every node:
-//   dm_range    finds, per member payload, the positions whose flat index falls in its range (payload
-//               indices ascend, so a 32-ary warp search over the peer's index array);
-//   dm_prepass  sums ||x||^2, max|x| and non-finite counts over those positions and adds them into rank
-//               0's stats with system-scope atomics; its last block releases rank 0's arrival counter;
-// rank 0 waits for W arrivals, the host validates / clips / weighs (the same rules as the single-GPU
-// merge) and dm_publish writes the coefficients into every node's control buffer and releases each
-// node's flag; then every node:
-//   dm_apply    waits for its flag, adds coef * x into its slice of the checkpoint (its own staging
-//               slot) - dense members fused in one pass, sparse ones by atomics;
+// Node r owns the flat range [a_r, b_r) (float4-aligned, about n/W elements). Rank 0 plans the attempt on
+// the host from the statistics every node reported with its push (validation, clipping, weights) and
+// announces members and coefficients; then every node:
+//   dm_range    finds, per sparse member payload, the positions whose flat index falls in its range
+//               (payload indices ascend, so a 32-ary warp search over the peer's index array);
+//   dm_apply    adds coef * x into its slice of the checkpoint (its own staging slot) - dense members
+//               fused in one pass, sparse ones by atomics;
 //   dm_broadcast writes its slice into every node's slot (multimem.st, or one store per peer) and
 //               releases rank 0's done counter.
-// Counters only grow (targets att * W), so no reset races between attempts. Every wait is bounded.
+// Each payload is read once, by the node that owns the slice. Cross-node ordering is on the host (the
+// announcement before the kernels, a completion key after them); rank 0's final bounded wait on the
+// done counter (target att * W, counters only grow) checks that every slice landed.
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -227,9 +225,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 }
 __device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // Bounded wait by one thread until *p >= target; false on timeout (error recorded at `site`).
 __device__ __forceinline__ bool wait_ge_u64(const unsigned long long* p, unsigned long long target, int site,
@@ -306,90 +301,23 @@ __device__ __forceinline__ void last_block_release(unsigned* blocks_local, unsig
   }
 }
 
-__global__ void dm_prepass_kernel(const __grid_constant__ ContribTable cs, const long long* __restrict__ ranges,
-                                  double* stats_dst, unsigned long long* arrivals_dst, unsigned* blocks_local) {
-  __shared__ float shs[32];
-  const int c = blockIdx.y;
-  const Contrib& C = cs.c[c];
-  const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
-  float ss = 0.f, mx = 0.f;
-  int nf = 0;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i0 = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < hi; i0 += stride * MUNR) {
-    float v[MUNR];
-#pragma unroll
-    for (int u = 0; u < MUNR; ++u) {
-      const long long i = i0 + u * stride;
-      v[u] = i < hi ? contrib_value(C, i) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < MUNR; ++u) {
-      if (!isfinite(v[u])) { nf = 1; continue; }
-      ss += v[u] * v[u];
-      mx = fmaxf(mx, fabsf(v[u]));
-    }
-  }
-  const float t = block_sum(ss, shs);
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0 && mx > 0.f)
-    atomicMax_system(reinterpret_cast<unsigned long long*>(stats_dst + c * 3 + 1),
-                     (unsigned long long)__double_as_longlong((double)mx));
-  nf = __syncthreads_or(nf);
-  if (threadIdx.x == 0) {
-    if (t != 0.f) atomicAdd_system(stats_dst + c * 3 + 0, (double)t);
-    if (nf) atomicAdd_system(stats_dst + c * 3 + 2, 1.0);
-  }
-  last_block_release(blocks_local, arrivals_dst);
-}
-
-// One block waits for another node's step: the wait covers host work on that node (rank 0 plans on the
-// host between its statistics and its coefficients), so it is bounded by `bound_ns` rather than the
-// library-wide 2 s; the full grids launched after it on the same stream then find the flag set.
+// Rank 0's final check that every node's slice landed (the host has already seen every node's completion,
+// so this returns at once unless a slice went missing; bounded either way).
 __global__ void dm_wait_kernel(const unsigned long long* counter, unsigned long long target, int site,
                                unsigned long long bound_ns) {
   if (threadIdx.x == 0) wait_ge_u64(counter, target, site, bound_ns);
 }
 
-struct PeerFloats {
-  float* p[8];
-};
-struct PeerFlags {
-  unsigned long long* p[8];
-};
-
-__global__ void dm_publish_kernel(const float* __restrict__ coefs, int n, PeerFloats dst, PeerFlags flags, int W,
-                                  unsigned long long att) {
-  const int t = threadIdx.x;
-  if (t < n) {
-    const float v = coefs[t];
-    for (int r = 0; r < W; ++r) dst.p[r][t] = v;
-  }
+// Coefficients of the attempt (this node's control buffer, written by the host on the same stream).
+__device__ __forceinline__ void dm_load_coefs(const float* coefs, int n, float* sh_coef) {
+  if (threadIdx.x < n) sh_coef[threadIdx.x] = coefs[threadIdx.x];
   __syncthreads();
-  if (t == 0) {
-    __threadfence_system();
-    for (int r = 0; r < W; ++r) st_release_sys_u64(flags.p[r], att);
-  }
-}
-
-// Block-uniform: waits for the coefficients of attempt `att` and stages them in shared memory.
-__device__ __forceinline__ bool dm_load_coefs(const unsigned long long* flag, unsigned long long att,
-                                              const float* coefs, int n, float* sh_coef, int* sh_ok) {
-  if (threadIdx.x == 0) {
-    int ok = wait_ge_u64(flag, att, 910) ? 1 : 0;
-    if (ok)
-      for (int c = 0; c < n; ++c) sh_coef[c] = *reinterpret_cast<const volatile float*>(coefs + c);
-    *sh_ok = ok;
-  }
-  __syncthreads();
-  return *sh_ok != 0;
 }
 
 __global__ void dm_apply_dense_kernel(const __grid_constant__ ContribTable cs, int n, long long a4, long long b4,
-                                      const float* coefs, const unsigned long long* flag, unsigned long long att,
-                                      float* __restrict__ theta) {
+                                      const float* coefs, float* __restrict__ theta) {
   __shared__ float shc[MAX_CONTRIB];
-  __shared__ int ok;
-  if (!dm_load_coefs(flag, att, coefs, n, shc, &ok)) return;
+  dm_load_coefs(coefs, n, shc);
   for (long long i = a4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < b4;
        i += (long long)gridDim.x * blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -414,11 +342,9 @@ __global__ void dm_apply_dense_kernel(const __grid_constant__ ContribTable cs, i
 
 __global__ void dm_apply_sparse_kernel(const __grid_constant__ ContribTable cs, int n,
                                        const long long* __restrict__ ranges, const float* coefs,
-                                       const unsigned long long* flag, unsigned long long att,
                                        float* __restrict__ theta) {
   __shared__ float shc[MAX_CONTRIB];
-  __shared__ int ok;
-  if (!dm_load_coefs(flag, att, coefs, n, shc, &ok)) return;
+  dm_load_coefs(coefs, n, shc);
   const int c = blockIdx.y;
   const Contrib& C = cs.c[c];
   const float k = shc[c];
@@ -582,50 +508,24 @@ DT_API int dt_dm_range(const void* contribs, int n, long long a, long long b, lo
   return (int)cudaGetLastError();
 }
 
-DT_API int dt_dm_prepass(const void* contribs, int n, long long max_len, const long long* ranges, double* stats_dst,
-                         unsigned long long* arrivals_dst, unsigned* blocks_local, cudaStream_t st) {
-  if (n <= 0 || n > MAX_CONTRIB) return -13;
-  ContribTable tab;
-  memcpy(tab.c, contribs, sizeof(Contrib) * n);
-  dim3 grid(grid_cap(max_len / MUNR + 1, 256, 148 * 2), n);
-  dm_prepass_kernel<<<grid, 256, 0, st>>>(tab, ranges, stats_dst, arrivals_dst, blocks_local);
-  return (int)cudaGetLastError();
-}
-
 DT_API int dt_dm_wait(const unsigned long long* counter, unsigned long long target, int site,
                       unsigned long long bound_ns, cudaStream_t st) {
   dm_wait_kernel<<<1, 32, 0, st>>>(counter, target, site, bound_ns);
   return (int)cudaGetLastError();
 }
 
-// coef_dsts / flag_dsts: host arrays of W device pointers (every node's coefficient buffer and flag).
-DT_API int dt_dm_publish(const float* coefs, int n, void* const* coef_dsts, void* const* flag_dsts, int W,
-                         unsigned long long att, cudaStream_t st) {
-  if (n <= 0 || n > MAX_CONTRIB || W <= 0 || W > 8) return -13;
-  PeerFloats d{};
-  PeerFlags f{};
-  for (int r = 0; r < W; ++r) {
-    d.p[r] = reinterpret_cast<float*>(coef_dsts[r]);
-    f.p[r] = reinterpret_cast<unsigned long long*>(flag_dsts[r]);
-  }
-  dm_publish_kernel<<<1, MAX_CONTRIB, 0, st>>>(coefs, n, d, f, W, att);
-  return (int)cudaGetLastError();
-}
-
-// Adds the weighted members into theta[a, b) (a, b multiples of 4) once the flag reaches `att`.
+// Adds the weighted members into theta[a, b) (a, b multiples of 4); coefs: this node's device copy.
 DT_API int dt_dm_apply(const void* contribs, int n, long long max_len, const long long* ranges, long long a, long long b,
-                       const float* coefs, const unsigned long long* flag, unsigned long long att, float* theta,
-                       int has_dense, int has_sparse, cudaStream_t st) {
+                       const float* coefs, float* theta, int has_dense, int has_sparse, cudaStream_t st) {
   if (n <= 0 || n > MAX_CONTRIB) return -13;
   if ((a | b) & 3) return -10;
   ContribTable tab;
   memcpy(tab.c, contribs, sizeof(Contrib) * n);
   if (has_dense && b > a)
-    dm_apply_dense_kernel<<<grid_cap((b - a) / 4, 256, 148 * 4), 256, 0, st>>>(tab, n, a / 4, b / 4, coefs, flag,
-                                                                                att, theta);
+    dm_apply_dense_kernel<<<grid_cap((b - a) / 4, 256, 148 * 4), 256, 0, st>>>(tab, n, a / 4, b / 4, coefs, theta);
   if (has_sparse) {
     dim3 grid(grid_cap(max_len / MUNR + 1, 256, 148 * 4), n);
-    dm_apply_sparse_kernel<<<grid, 256, 0, st>>>(tab, n, ranges, coefs, flag, att, theta);
+    dm_apply_sparse_kernel<<<grid, 256, 0, st>>>(tab, n, ranges, coefs, theta);
   }
   return (int)cudaGetLastError();
 }

@@ -11,16 +11,18 @@ tokens * 0.9^staleness.
 
 Per (model, top-k), every iteration:
   1. every rank compresses its delta (+ error feedback) into its symmetric (peer-mapped) payload buffer:
-     pass A + radix top-k + ordered compaction + INT8 block 256;
-  2. the distributed merge (every rank merges one slice of the flat range: pulls that slice of all N
-     payloads over NVLink, adds partial norms into rank 0's statistics, applies rank 0's coefficients to
-     its slice of the checkpoint - its own staging buffer - and writes the slice into every rank's
-     staging buffer with NVLS multimem stores, or per-peer stores without a multicast object);
+     pass A + radix top-k + ordered compaction + INT8 block 256 (or, for "raw", pass A and the dense fp32
+     delta);
+  2. the distributed merge: validation, clipping and weights from the statistics every node reports with
+     its push, then every rank merges one slice of the flat range - pulls that slice of all N payloads
+     over NVLink, adds it into its slice of the checkpoint (its own staging buffer) and writes the slice
+     into every rank's staging buffer with NVLS multimem stores, or per-peer stores without a multicast
+     object;
   3. for comparison, the single-coordinator merge of the same payloads (rank 0 pulls all of them,
      scatter-adds into its checkpoint and broadcasts the whole checkpoint).
-Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, from before
-its phase 1 to after every rank's phase 3 (the three phases are separated by NCCL barriers, which are
-inside the timed interval), total = their sum. Bytes over NVLink: payloads pulled from the N-1 peers plus the
+Timed with CUDA events on the launching streams: compress = max over ranks, merge = rank 0, from the
+start of its slice to its check that every rank's slice landed (an NCCL barrier, inside the timed
+interval, separates the two), total = their sum. Bytes over NVLink: payloads pulled from the N-1 peers plus the
 checkpoint stored through the multicast object (each GPU receives it once).
 Comparison arm per model: delta = snapshot - master scaled by its merge weight, ncclAllReduce(SUM) of the
 n fp32 values, the same apply and bf16 cast on every rank; max over ranks. One JSON line per case on
@@ -67,8 +69,12 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     stale = torch.randint(0, 4, (world,), generator=hg).tolist()
     tokens = torch.randint(100_000, 1_000_001, (world,), generator=hg).tolist()
     weights = [t * 0.9 ** s for t, s in zip(tokens, stale)]
-    cap_max = DeviceCompressor.capacity_for(L, max(topks))
-    pay_bytes = (DevicePayload.nbytes(cap_max, 256) + 4095) // 4096 * 4096
+    ks = [k for k in topks if k != "raw"]
+    cap_max = DeviceCompressor.capacity_for(L, max(ks)) if ks else 1
+    need = DevicePayload.nbytes(cap_max, 256)
+    if "raw" in topks:
+        need = max(need, 4 * n)
+    pay_bytes = (need + 4095) // 4096 * 4096
     pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes, dev, world)
     stage_bytes = (n * 4 + 4095) // 4096 * 4096
     stage_buf, stage_ptrs, stage_mc, _stage_h = _symm_alloc(stage_bytes, dev, world)
@@ -87,9 +93,12 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
             dist.barrier()
 
     for k in topks:
-        cap = DeviceCompressor.capacity_for(L, k)
+        raw = k == "raw"
+        cap = DeviceCompressor.capacity_for(L, 0.01 if raw else k)
         payload = DevicePayload(pay_buf[:DevicePayload.nbytes(cap, 256)], cap, 256)
-        comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=k, int8_block=256), payload=payload)
+        comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=0.01 if raw else k, int8_block=256),
+                                payload=payload)
+        raw_view = pay_buf[:4 * n].view(torch.float32) if raw else None
         t_comp, t_merge, t_single, pulled, infos = [], [], [], 0, None
         for it in range(warmup + iters):
             comp.snap.copy_(snap)
@@ -99,42 +108,45 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
             c0, c1 = _events()
             c0.record()
             comp.begin(master)
-            comp.finish()
+            if raw:
+                comp.finish_raw(raw_view)
+            else:
+                comp.finish()
             c1.record()
             torch.cuda.synchronize()
-            cnt = torch.tensor([int(comp.stats_host[comp.nseg * 6].item())], device=dev, dtype=torch.int64)
-            counts = [torch.zeros_like(cnt) for _ in range(world)]
+            kept = n if raw else int(comp.stats_host[comp.nseg * 6].item())
+            wire = comp.read_stats(raw=raw)["wire"]
+            cnt = torch.tensor([kept] + wire, device=dev, dtype=torch.float64)
+            got = [torch.zeros_like(cnt) for _ in range(world)]
             if world > 1:
-                dist.all_gather(counts, cnt)
+                dist.all_gather(got, cnt)
             else:
-                counts = [cnt]
-            counts = [int(c.item()) for c in counts]
+                got = [cnt]
+            counts = [int(g[0].item()) for g in got]
+            stats = [g[1:].tolist() for g in got]  # what each node reports with its push
             base = pay_buf.data_ptr()
             contribs = []
             for r in range(world):
                 off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
+                if raw:
+                    contribs.append(Contribution(idx_ptr=0, q_ptr=0, val_ptr=off(raw_view), scales_ptr=0, count=n,
+                                                 block=0, dense=True, weight=weights[r], node_id=f"node-{r:02d}",
+                                                 wire_bytes=4 * n))
+                    continue
                 contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q), win_ptr=off(payload.win),
                                              val_ptr=off(payload.val), scales_ptr=off(payload.scales),
                                              count=counts[r], block=256, dense=False, weight=weights[r],
                                              node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
             pulled = sum(c.wire_bytes for c in contribs[1:])
-            # distributed merge: every rank merges its slice (timed on rank 0, which waits for all slices)
+            # distributed merge: every rank plans from the reported statistics (the same on every rank),
+            # merges its slice and broadcasts it; rank 0 checks that every slice landed
+            coefs, infos = DeviceMerger.plan(contribs, stats)
             att += 1
-            if rank == 0:
-                dm.reset_stats()
             barrier()
             m0, m1 = _events()
             m0.record(dm.stream)
-            dm.prepass(contribs)           # phase 1: every rank, partial statistics into rank 0's
-            dm.check("prepass")
-            barrier()
-            if rank == 0:                  # phase 2: rank 0 plans and publishes the coefficients
-                infos, failure = dm.plan_publish(contribs, 1.0, att)
-                dm.check("publish")
-                assert failure is None, failure
-            barrier()
-            dm.apply(contribs, att)        # phase 3: every rank, its slice + broadcast
-            dm.check("apply")
+            dm.apply(contribs, coefs, 1.0)
+            dm.check()
             barrier()
             if rank == 0:
                 dm.finish(att)
@@ -142,12 +154,13 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
             dm.stream.synchronize()
             mms = m0.elapsed_time(m1) if rank == 0 else 0.0
             barrier()
-            # single-coordinator merge of the same payloads (rank 0 pulls everything and broadcasts)
+            # single-coordinator merge of the same payloads (rank 0 pulls all of them, scatter-adds into its
+            # checkpoint and broadcasts the whole of it)
             sms = 0.0
             if rank == 0:
                 s0, s1 = _events()
                 s0.record(single.stream)
-                single.merge(contribs, 1.0, mc32=mc32, stage32=p32)
+                single.accumulate_apply(contribs, coefs, 1.0, mc32=mc32, stage32=p32)
                 s1.record(single.stream)
                 single.stream.synchronize()
                 sms = s0.elapsed_time(s1)
@@ -202,7 +215,9 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--models", default="tiny,small")
-    ap.add_argument("--topk", default="0.01,0.1,0.99")
+    ap.add_argument("--topk", default="0.01,0.1,0.99,raw",
+                    help="top-k fractions; 'raw' = the dense fp32 delta (what the bandwidth-adaptive policy sends "
+                         "when it fits the upload budget, as it always does over NVLink)")
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     a = ap.parse_args()
@@ -214,7 +229,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=300))
-    topks = [float(x) for x in a.topk.split(",")]
+    topks = [x if x == "raw" else float(x) for x in a.topk.split(",")]
     for m in a.models.split(","):
         for r in run_model(m, topks, a.iters, a.warmup, rank, world, dev):
             print(json.dumps(r), flush=True)

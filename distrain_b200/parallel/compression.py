@@ -129,6 +129,41 @@ def reconstruct_dense(sd: SparseDeltaT) -> Dict[str, torch.Tensor]:
     return out
 
 
+def adaptive_top_k(loss: float, max_delta_bytes: Optional[int], raw_param_bytes: int) -> float:
+    """Loss-based retention, capped by the bandwidth budget (reference trainer.rs:33-70)."""
+    if loss > 20.0:
+        k = 0.50
+    elif loss > 10.0:
+        k = 0.60
+    elif loss > 7.0:
+        k = 0.70
+    elif loss > 5.0:
+        k = 0.75
+    else:
+        k = 0.80
+    if max_delta_bytes is not None:
+        mx = max_delta_bytes / (raw_param_bytes * 0.5) if raw_param_bytes > 0 else k
+        k = max(min(k, mx), 0.01)
+    return k
+
+
+def adaptive_push_mode(bandwidth_adaptive: bool, bandwidth_bps: float, raw_bytes: int, last_loss: float,
+                       cfg: CompressionConfig):
+    """(kind, top-k fraction, int8 block) of a push (reference continuous.rs:190-219): without the
+    bandwidth-adaptive policy, the configured top-k; with it and no measured bandwidth, the loss-based
+    top-k (quantised as configured); with a bandwidth under which the raw delta moves within the 10 s
+    budget, raw (dense fp32); otherwise an unquantised top-k capped by that budget."""
+    qb = cfg.int8_block if cfg.quantize_int8 else 0
+    if not bandwidth_adaptive:
+        return "topk", cfg.top_k_fraction, qb
+    if bandwidth_bps <= 0.0:
+        return "topk", adaptive_top_k(last_loss, None, 0), qb
+    budget = bandwidth_bps * 10.0
+    if raw_bytes <= budget:
+        return "raw", 1.0, 0
+    return "topk", adaptive_top_k(last_loss, int(budget), raw_bytes), 0
+
+
 # ─────────────────────────────── device pipeline ───────────────────────────────
 class DeviceCompressor:
     """Fused compress pipeline over a ``ParamLayout``'s flat buffer (one per node)."""
@@ -144,6 +179,7 @@ class DeviceCompressor:
                                              c_void, c_void, c_void, c_void, c_int, c_ll, c_void, c_int, c_void,
                                              c_void])
         _lib.register("dt_compress_export_stats", [c_void, c_int, c_int, c_void, c_void])
+        _lib.register("dt_compress_raw", [c_void, c_void, c_ll, c_void])
         self.layout, self.device, self.cfg = layout, torch.device(device), cfg
         n = layout.total
         self.cseg, self.cstart, self.cend, self.nseg = layout.chunk_tables(self.device)
@@ -183,11 +219,17 @@ class DeviceCompressor:
                                        self.nchunks, self.nseg, self.seg_len.data_ptr(), self.ws.data_ptr(), 1,
                                        stream_ptr(stream)), "dt_compress_begin")
 
-    def finish(self, payload=None, stream=None, k_fraction: Optional[float] = None):
+    def finish(self, payload=None, stream=None, k_fraction: Optional[float] = None,
+               quant_block: Optional[int] = None):
+        """Selection, compaction and (quant_block > 0) INT8 quantisation into ``payload``; ``k_fraction`` and
+        ``quant_block`` default to the configuration (quant_block 0: fp32 values, the payload's q and
+        scales untouched)."""
         from ..ops._lib import check, stream_ptr
         p = payload or self.payload
         kf = self.cfg.top_k_fraction if k_fraction is None else k_fraction
-        qb = self.cfg.int8_block if self.cfg.quantize_int8 else 0
+        qb = (self.cfg.int8_block if self.cfg.quantize_int8 else 0) if quant_block is None else quant_block
+        assert qb == 0 or p.block == qb, "payload laid out for another quantisation block"
+        assert math.ceil(self.layout.num_params() * kf) <= p.capacity or kf >= 1.0, "payload capacity"
         check(self.L.dt_compress_finish(self.ef.data_ptr(), self.cseg.data_ptr(), self.cstart.data_ptr(),
                                         self.cend.data_ptr(), self.nchunks, self.nseg, self.ws.data_ptr(), float(kf),
                                         int(self.cfg.per_tensor_adaptive), p.idx.data_ptr(), p.val.data_ptr(),
@@ -199,18 +241,42 @@ class DeviceCompressor:
         with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
             self.stats_host.copy_(self.stats_dev, non_blocking=True)
 
-    def read_stats(self) -> dict:
-        """Call after the finish stream has been synchronised."""
+    def finish_raw(self, out: torch.Tensor, stream=None):
+        """Raw push after ``begin``: the dense delta (+ error feedback) into ``out`` (fp32, >= n elements),
+        error feedback cleared. Statistics as for a top-k push (``read_stats(raw=True)``)."""
+        from ..ops._lib import check, stream_ptr
+        n = self.layout.total
+        assert out.dtype == torch.float32 and out.numel() >= n
+        check(self.L.dt_compress_export_stats(self.ws.data_ptr(), self.nseg, self.nchunks, self.stats_dev.data_ptr(),
+                                              stream_ptr(stream)), "dt_compress_export_stats")
+        check(self.L.dt_compress_raw(self.ef.data_ptr(), out.data_ptr(), n, stream_ptr(stream)), "dt_compress_raw")
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+            self.stats_host.copy_(self.stats_dev, non_blocking=True)
+
+    def read_stats(self, raw: bool = False, quantized: Optional[bool] = None) -> dict:
+        """Call after the finish stream has been synchronised. ``wire`` = [sum of squares, max |x|,
+        non-finite count] of the values exactly as they were sent (dequantised for INT8 pushes, the kept
+        fp32 values for unquantised ones, the whole delta for raw ones): what the coordinator validates
+        and clips on."""
         s = self.stats_host
         ns = self.nseg
         seg = s[:ns * 6].view(ns, 6)
         total_kept = int(s[ns * 6].item())
         dense_sq, kept_sq = float(seg[:, 0].sum()), float(seg[:, 1].sum())
+        max_abs, nonfinite = float(seg[:, 3].max()), float(seg[:, 4].sum())
+        if raw:
+            total_kept, kept_sq = self.layout.total, dense_sq
+        if quantized is None:
+            quantized = self.cfg.quantize_int8
+        if quantized and not raw:
+            wire = [float(s[ns * 6 + 1]), float(s[ns * 6 + 2]), float(s[ns * 6 + 3]) + nonfinite]
+        else:  # the largest |d| of a tensor is always kept, so max |kept| = max |d|
+            wire = [kept_sq, max_abs, nonfinite]
         dense_norm, sparse_norm = math.sqrt(dense_sq), math.sqrt(kept_sq)
         return {"dense_norm": dense_norm, "sparse_norm": sparse_norm,
                 "retention_ratio": sparse_norm / dense_norm if dense_norm > 0 else 0.0,
                 "num_params_total": self.layout.num_params(), "num_params_kept": total_kept,
-                "max_abs": float(seg[:, 3].max()), "nonfinite": bool(seg[:, 4].sum() > 0),
+                "max_abs": max_abs, "nonfinite": nonfinite > 0, "wire": wire,
                 "k_per_tensor": seg[:, 2].long().tolist()}
 
 
@@ -262,8 +328,15 @@ class DevicePayload:
         buf = torch.zeros(cls.nbytes(capacity, block), dtype=torch.uint8, device=device)
         return cls(buf, capacity, block)
 
-    def wire_bytes(self, count: int) -> int:
-        """Bytes a contribution of `count` kept entries occupies on the wire (idx + int8/fp32 + scales)."""
-        if self.block:
-            return count * 4 + count + ((count + self.block - 1) // self.block) * 4
+    def wire_bytes(self, count: int, block: Optional[int] = None) -> int:
+        """Bytes a contribution of `count` kept entries occupies on the wire (idx + int8/fp32 + scales);
+        `block` overrides the payload's quantisation block (0: fp32 values)."""
+        blk = self.block if block is None else block
+        if blk:
+            return count * 4 + count + ((count + blk - 1) // blk) * 4
         return count * 8
+
+    def raw(self, n: int) -> torch.Tensor:
+        """The slot read as a dense fp32 delta of n values (a raw push; the slot must hold 4n bytes)."""
+        assert self.buf.numel() >= 4 * n, "payload slot too small for a raw push"
+        return self.buf[:4 * n].view(torch.float32)

@@ -29,25 +29,7 @@ from ..coordinator.client import CoordinatorClient
 from ..models.params import ParamLayout
 from ..utils.checkpoint import load_safetensors_bytes
 from ..utils.delta_codec import encode_sparse_delta
-from .compression import compress_reference
-
-
-def adaptive_top_k(loss: float, max_delta_bytes: Optional[int], raw_param_bytes: int) -> float:
-    """Loss-based retention, capped by the bandwidth budget (reference trainer.rs:33-70)."""
-    if loss > 20.0:
-        k = 0.50
-    elif loss > 10.0:
-        k = 0.60
-    elif loss > 7.0:
-        k = 0.70
-    elif loss > 5.0:
-        k = 0.75
-    else:
-        k = 0.80
-    if max_delta_bytes is not None:
-        mx = max_delta_bytes / (raw_param_bytes * 0.5) if raw_param_bytes > 0 else k
-        k = max(min(k, mx), 0.01)
-    return k
+from .compression import adaptive_top_k, compress_reference  # noqa: F401 (adaptive_top_k re-exported)
 
 
 class CpuBackend:

@@ -26,6 +26,7 @@ error-feedback residual.
 from __future__ import annotations
 
 import json
+import math
 import os
 import queue
 import threading
@@ -37,7 +38,7 @@ import torch.distributed as dist
 
 from ..config import RunConfig
 from ..protocol import Accumulator, DeltaPush, delta_path
-from .compression import DeviceCompressor, DevicePayload
+from .compression import DeviceCompressor, DevicePayload, adaptive_push_mode
 from .merge import Contribution, DeviceMerger, DistributedMerger
 
 
@@ -137,9 +138,16 @@ class InBoxSync:
         cfg = run.compression
         self.comp_stream = torch.cuda.Stream(device=self.device)
         # ── symmetric buffers ──
-        cap = DeviceCompressor.capacity_for(self.layout, max(cfg.top_k_fraction, 0.0))
+        # bandwidth-adaptive pushes (reference continuous.rs:190-219) may be raw (dense fp32, n values) or
+        # loss-based top-k up to 80 %: size the slots for the largest
+        kmax = max(cfg.top_k_fraction, 0.80 if run.bandwidth_adaptive else 0.0)
+        cap = DeviceCompressor.capacity_for(self.layout, kmax)
         blk = cfg.int8_block if cfg.quantize_int8 else 0
-        self.slot_bytes = (DevicePayload.nbytes(cap, blk) + 4095) // 4096 * 4096
+        need = DevicePayload.nbytes(cap, blk)
+        if run.bandwidth_adaptive:
+            need = max(need, 4 * self.n)
+        self.slot_bytes = (need + 4095) // 4096 * 4096
+        self.last_loss = float(math.log(run.model.vocab_size))  # previous round's mean loss (adaptive top-k)
         # payload slots: with two, a node can push again while the coordinator still holds its previous
         # payload; one is enough when pushes are far apart (and saves ~9 bytes per kept entry)
         self.n_slots = max(1, int(run.payload_slots))
@@ -244,19 +252,29 @@ class InBoxSync:
             return self._push(partial=partial)
         key = f"pushdec/{self.rank}/{self.node.step_count}/{int(partial)}"
         if self.shard == 0:
-            ok = self._push(partial=partial)
-            self.shared.set(key, "1" if ok else "0")
+            mode = self.push_mode()
+            ok = self._push(partial=partial, mode=mode)
+            self.shared.set(key, json.dumps(list(mode)) if ok else "0")
             return ok
-        if self.shared.wait_get(key) != "1":
+        dec = self.shared.wait_get(key)
+        if dec == "0":
             return False
+        mode = tuple(json.loads(dec))
         t0 = time.time()
-        while not self._push(partial=partial):  # the slot is released for every shard at once
+        while not self._push(partial=partial, mode=mode):  # the slot is released for every shard at once
             if time.time() - t0 > 60:
                 raise TimeoutError("payload slot of this shard not released")
             time.sleep(0.0005)
         return True
 
-    def _push(self, partial: bool) -> bool:
+    def push_mode(self):
+        """(kind, top-k fraction, int8 block) of the next push (``adaptive_push_mode``); in the box the
+        measured bandwidth is the coordinator's payload pull rate over NVLink."""
+        bw = float(self.shared.get("bw", "0") or 0.0)
+        return adaptive_push_mode(self.run.bandwidth_adaptive, bw, 4 * self.layout.num_params(), self.last_loss,
+                                  self.run.compression)
+
+    def _push(self, partial: bool, mode=None) -> bool:
         slot = (self.seq + 1) % self.n_slots
         if not self._slot_free(slot):
             return False  # coordinator still holds that payload; try again next step
@@ -267,11 +285,15 @@ class InBoxSync:
         train = torch.cuda.current_stream()
         if self.ef_ready is not None:
             train.wait_event(self.ef_ready)
+        kind, kf, qb = mode or self.push_mode()
         self.compressor.begin(eng.master, stream=train)   # pass A on the training stream
         ev_a = torch.cuda.Event()
         ev_a.record(train)
         self.comp_stream.wait_event(ev_a)
-        self.compressor.finish(payload=self.slots[slot], stream=self.comp_stream)
+        if kind == "raw":
+            self.compressor.finish_raw(self.slots[slot].raw(self.n), stream=self.comp_stream)
+        else:
+            self.compressor.finish(payload=self.slots[slot], stream=self.comp_stream, k_fraction=kf, quant_block=qb)
         ev_f = torch.cuda.Event()
         ev_f.record(self.comp_stream)
         self.ef_ready = ev_f
@@ -294,7 +316,7 @@ class InBoxSync:
         ev_post = torch.cuda.Event()
         ev_post.record(self.comp_stream)
         self.inflight = (seq, ev_f, slot)
-        self.pending_posts.put((meta, ev_post, slot, loss_h))
+        self.pending_posts.put((meta, ev_post, slot, loss_h, kind, qb))
         self.node.round_step = 0
         self.round_tokens = 0
         self.round_t0 = time.time()
@@ -304,20 +326,26 @@ class InBoxSync:
         torch.cuda.set_device(self.device)
         while not self.stop.is_set():
             try:
-                meta, ev, slot, loss_h = self.pending_posts.get(timeout=0.05)
+                meta, ev, slot, loss_h, kind, qb = self.pending_posts.get(timeout=0.05)
             except queue.Empty:
                 continue
             ev.synchronize()
             cnt = float(loss_h[1])
             meta.training_loss = float(loss_h[0]) / cnt if cnt > 0 else 0.0
-            st = self.compressor.read_stats()
+            if cnt > 0:
+                self.last_loss = meta.training_loss
+            raw = kind == "raw"
+            st = self.compressor.read_stats(raw=raw, quantized=qb > 0)
             p = self.slots[slot]
             meta.dense_norm, meta.sparse_norm = st["dense_norm"], st["sparse_norm"]
-            meta.compressed_bytes = p.wire_bytes(st["num_params_kept"])
+            meta.compressed_bytes = 4 * st["num_params_kept"] if raw else p.wire_bytes(st["num_params_kept"], qb)
             body = meta.to_dict()
             body["_slot"] = slot
             body["_count"] = st["num_params_kept"]
             body["_rank"] = self.rank
+            body["_dense"] = int(raw)
+            body["_block"] = qb
+            body["_stats"] = st["wire"]  # what the coordinator validates and clips on
             self.bus.set(f"push/{self.rank}/{meta.seq_num}", json.dumps(body))
             self.bus.set(f"pushseq/{self.rank}", str(meta.seq_num))
 
@@ -362,35 +390,21 @@ class InBoxSync:
         self.bus.set(f"consumed/{self.rank}", str(new_version))
 
     def member_contribution(self, m) -> Contribution:
-        """A merge member [rank, slot, count, block, weight] as seen from this node (peer pointers)."""
-        r, slot, count, blk, weight = m[:5]
+        """A merge member [rank, slot, count, block, weight, dense] as seen from this node (peer pointers)."""
+        r, slot, count, blk, weight, dense = m[:6]
         p = self.slots[slot]
         base_local = self.pay_buf.data_ptr()
         peer = self.pay_ptrs[r]
         off = lambda t: t.data_ptr() - base_local + peer
+        if dense:
+            return Contribution(idx_ptr=0, q_ptr=0, val_ptr=off(p.raw(self.n)), scales_ptr=0, count=self.n, block=0,
+                                dense=True, weight=weight, wire_bytes=4 * count)
         return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
                             scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
-                            weight=weight, wire_bytes=p.wire_bytes(count))
-
-    def _poll(self, key: str, alt: Optional[str] = None, timeout: float = 120.0):
-        """Wait for `key` (or `alt`) on the control bus; returns (which key, value)."""
-        t0 = time.time()
-        while not self.stop.is_set():
-            v = self.bus.get(key)
-            if v is not None:
-                return key, v
-            if alt is not None:
-                v = self.bus.get(alt)
-                if v is not None:
-                    return alt, v
-            if time.time() - t0 > timeout:
-                raise TimeoutError(f"control bus key {key} not set within {timeout} s")
-            time.sleep(0.0001)
-        raise _Shutdown()
+                            weight=weight, wire_bytes=p.wire_bytes(count, blk))
 
     def _dm_loop(self):
-        """Nodes other than rank 0: run this node's share of every merge attempt rank 0 announces
-        (phase 1 prepass, then - once rank 0 has published the coefficients - phase 3 apply)."""
+        """Nodes other than rank 0: apply this node's slice of every merge attempt rank 0 announces."""
         torch.cuda.set_device(self.device)
         att = 0
         try:
@@ -401,18 +415,9 @@ class InBoxSync:
                     continue
                 att += 1
                 plan = json.loads(raw)
-                contribs = [self.member_contribution(m) for m in plan["members"]]
-                self.dm.prepass(contribs)
-                self.dm.check("prepass")
-                self.bus.set(f"dmpre/{att}/{self.rank}", "1")
-                which, _ = self._poll(f"dmcoef/{att}", f"dmabort/{att}")
-                if which.startswith("dmabort"):
-                    continue
-                self.dm.apply(contribs, att)
-                self.dm.check("apply")
+                self.dm.apply([self.member_contribution(m) for m in plan["members"]], plan["coefs"], plan["lr"])
+                self.dm.check()
                 self.bus.set(f"dmdone/{att}/{self.rank}", "1")
-        except _Shutdown:
-            pass
         except BaseException as e:  # surfaced by close()
             self.dm_error = e
 
@@ -489,18 +494,16 @@ class InBoxCoordinator:
                     self._release(r, push.seq_num)
                 self.acc.heartbeat(push.node_id)
 
+    def _member(self, body: dict, weight: float) -> list:
+        p = self.sync.slots[body["_slot"]]
+        return [body["_rank"], body["_slot"], body["_count"], body.get("_block", p.block), weight,
+                body.get("_dense", 0)]
+
     def _contribution(self, c) -> Contribution:
         body = self.payload_of[(c.node_id, c.seq_num)]
-        r, slot, count = body["_rank"], body["_slot"], body["_count"]
-        s = self.sync
-        p = s.slots[slot]
-        base_local = s.pay_buf.data_ptr()
-        peer = s.pay_ptrs[r]
-        off = lambda t: t.data_ptr() - base_local + peer
-        blk = p.block
-        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
-                            scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
-                            weight=c.weight, node_id=c.node_id, wire_bytes=p.wire_bytes(count))
+        out = self.sync.member_contribution(self._member(body, c.weight))
+        out.node_id = c.node_id
+        return out
 
     def _wait_consumed(self, version: int, timeout: float = 30.0):
         """Before the merge writes `version` into the single checkpoint slot (in place on this GPU, by
@@ -533,25 +536,24 @@ class InBoxCoordinator:
             ns = self.sync.n_shards
             self.attempt += 1
             att = self.attempt
+            # validation and clipping see the full delta: every shard's push reported the statistics of its
+            # payload; sum the squares, take the maxima
+            stats = []
+            for c in snap.contributions:
+                r = int(c.node_id.split("-")[1])
+                tot = [0.0, 0.0, 0.0]
+                for t in range(ns):
+                    if t == 0:
+                        body = self.payload_of[(c.node_id, c.seq_num)]
+                    else:
+                        body = json.loads(self.shard_buses[t].wait_get(f"push/{r}/{c.seq_num}", 120))
+                    ss, mx, nf = body["_stats"]
+                    tot = [tot[0] + ss, max(tot[1], mx), tot[2] + nf]
+                stats.append(tot)
+            coefs, info = self.merger.plan(contribs, stats)  # raises when no contribution is valid
             if ns > 1:  # the other shards' coordinators run the same merge on their shards
-                self.shared.set(f"plan/{att}", json.dumps({"version": new_version, "members": [
+                self.shared.set(f"plan/{att}", json.dumps({"version": new_version, "coefs": coefs, "members": [
                     [c.node_id, c.seq_num] for c in snap.contributions]}))
-            stats = self.merger.prepass(contribs)
-            if ns > 1:  # validation and clipping see the full delta: sum the shards' squares
-                for t in range(1, ns):
-                    st = json.loads(self.shared.wait_get(f"stats/{att}/{t}", 120))
-                    for i, (ss, mx, nf) in enumerate(st):
-                        stats[i][0] += ss
-                        stats[i][1] = max(stats[i][1], mx)
-                        stats[i][2] = max(stats[i][2], nf)
-            try:
-                coefs, info = self.merger.plan(contribs, stats)
-            except Exception:
-                if ns > 1:
-                    self.shared.set(f"coefs/{att}", "abort")
-                raise
-            if ns > 1:
-                self.shared.set(f"coefs/{att}", json.dumps(coefs))
             self.merger.accumulate_apply(contribs, coefs, self.run.outer_lr, mc32=mc32, stage32=p32)
             info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
             ev1.record(self.merger.stream)
@@ -565,6 +567,7 @@ class InBoxCoordinator:
             info["broadcast_bytes"] = self.sync.n * 4 * (1 if mc32 else self.world - 1)
             info["multicast"] = bool(mc32)
             self.merges.append(info)
+            self._publish_bandwidth(info)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)
@@ -589,6 +592,12 @@ class InBoxCoordinator:
                                                                              for x in snap.contributions}]
             self.acc.abort_merge()
 
+    def _publish_bandwidth(self, info: dict):
+        """Measured payload pull rate of this merge (bytes/s over its wall time), the in-box counterpart of
+        the reference node's measured upload bandwidth for bandwidth-adaptive compression."""
+        secs = max(info.get("wall_ms", 0.0), 1e-3) / 1e3
+        self.shared.set("bw", str(info.get("pulled_bytes", 0) / secs))
+
     def _wait_key(self, key: str, timeout: float = 120.0):
         t0 = time.time()
         while self.bus.get(key) is None:
@@ -607,40 +616,28 @@ class InBoxCoordinator:
             members = []
             for c in snap.contributions:
                 body = self.payload_of[(c.node_id, c.seq_num)]
-                members.append([body["_rank"], body["_slot"], body["_count"],
-                                self.sync.slots[body["_slot"]].block, c.weight])
+                members.append(self._member(body, c.weight))
             new_version = self.version + 1
             self._wait_consumed(new_version)
             dm = self.sync.dm
+            stats = [self.payload_of[(c.node_id, c.seq_num)]["_stats"] for c in snap.contributions]
+            coefs, info = DeviceMerger.plan(contribs, stats)  # raises when no contribution is valid
+            info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
             self.attempt += 1
             att = self.attempt
-            dm.reset_stats()
             t0 = time.time()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(dm.stream)
             W = self.world
+            lr = self.run.outer_lr
             if W > 1:
-                self.bus.set(f"dm/{att}", json.dumps({"version": new_version, "members": members}))
-            try:
-                dm.prepass(contribs)
-                dm.check("prepass")
-                for r in range(1, W):
-                    self._wait_key(f"dmpre/{att}/{r}")
-                info, failure = dm.plan_publish(contribs, self.run.outer_lr, att)
-                dm.check("publish")
-            except BaseException:
-                if W > 1:
-                    self.bus.set(f"dmabort/{att}", "1")
-                raise
-            if W > 1:
-                self.bus.set(f"dmcoef/{att}", "1")
-            dm.apply(contribs, att)
-            dm.check("apply")
+                self.bus.set(f"dm/{att}", json.dumps({"version": new_version, "members": members, "coefs": coefs,
+                                                      "lr": lr}))
+            dm.apply(contribs, coefs, lr)
+            dm.check()
             for r in range(1, W):
                 self._wait_key(f"dmdone/{att}/{r}")
             dm.finish(att)
-            if failure is not None:
-                raise failure
             ev1.record(dm.stream)
             ev1.synchronize()
             info["device_ms"] = ev0.elapsed_time(ev1)
@@ -652,6 +649,7 @@ class InBoxCoordinator:
             info["multicast"] = mc
             info["distributed"] = self.world
             self.merges.append(info)
+            self._publish_bandwidth(info)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)
@@ -697,9 +695,9 @@ class InBoxCoordinator:
 
 class ShardFollower:
     """Coordinator thread for shard t > 0 (on node 0's rank of that shard): executes the merge plans of the
-    shard-0 coordinator on this shard's payloads - prepass, report the stats, wait for the shared
-    coefficients, accumulate + apply + broadcast into this shard's staging buffers, report completion.
-    Slot releases and version publication are the shard-0 coordinator's."""
+    shard-0 coordinator (members and coefficients, planned on the full-delta statistics of all shards) on
+    this shard's payloads - accumulate + apply + broadcast into this shard's staging buffers - and reports
+    completion. Slot releases and version publication are the shard-0 coordinator's."""
 
     def __init__(self, sync: InBoxSync, run: RunConfig, world: int):
         self.sync, self.run, self.world = sync, run, world
@@ -719,28 +717,17 @@ class ShardFollower:
     def _contribution(self, node_id: str, seq: int) -> Contribution:
         r = int(node_id.split("-")[1])
         body = json.loads(self.bus.wait_get(f"push/{r}/{seq}", 120))
-        s = self.sync
-        p = s.slots[body["_slot"]]
-        base_local = s.pay_buf.data_ptr()
-        peer = s.pay_ptrs[r]
-        off = lambda t: t.data_ptr() - base_local + peer
-        blk = p.block
-        count = body["_count"]
-        return Contribution(idx_ptr=off(p.idx), q_ptr=off(p.q) if blk else 0, val_ptr=off(p.val), win_ptr=off(p.win),
-                            scales_ptr=off(p.scales) if blk else 0, count=count, block=blk, dense=False,
-                            weight=1.0, node_id=node_id, wire_bytes=p.wire_bytes(count))
+        p = self.sync.slots[body["_slot"]]
+        out = self.sync.member_contribution([r, body["_slot"], body["_count"], body.get("_block", p.block), 1.0,
+                                             body.get("_dense", 0)])
+        out.node_id = node_id
+        return out
 
     def _one(self, att: int, plan: dict):
         v = plan["version"]
         contribs = [self._contribution(nid, seq) for nid, seq in plan["members"]]
         p32, mc32 = self.sync.stage_peer_ptrs()
-        stats = self.merger.prepass(contribs)
-        self.shared.set(f"stats/{att}/{self.sync.shard}", json.dumps(stats))
-        c = self.shared.wait_get(f"coefs/{att}", 120)
-        if c == "abort":
-            self.failed.append(f"attempt {att} aborted by shard 0")
-            return
-        self.merger.accumulate_apply(contribs, json.loads(c), self.run.outer_lr, mc32=mc32, stage32=p32)
+        self.merger.accumulate_apply(contribs, plan["coefs"], self.run.outer_lr, mc32=mc32, stage32=p32)
         self.merger.stream.synchronize()
         self.merges.append({"version": v, "n_contrib": len(contribs)})
         self.shared.set(f"merged/{att}/{self.sync.shard}", "1")

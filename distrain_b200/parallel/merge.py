@@ -250,35 +250,32 @@ class DeviceMerger:
 
 class DistributedMerger:
     """This node's part of the distributed merge (merge.cu ``dm_*`` kernels): node r of W owns the flat
-    range [a_r, b_r) of the checkpoint. Every node pulls that range of each member payload over NVLink and
-    adds its partial norms into rank 0's statistics (phase 1); rank 0 validates, clips and weighs from
-    the summed statistics, as ``DeviceMerger.plan`` does, and writes the coefficients into every node's
-    control buffer (phase 2); every node updates its slice of the checkpoint in its own staging slot and
-    writes the slice into every node's slot, through NVLS multicast or per-peer stores (phase 3). The
-    payload traffic and the broadcast are spread over all W GPUs instead of funnelling through one.
-    The caller separates the phases with a cross-node synchronisation, so no kernel ever spins on
-    another node's host progress.
+    range [a_r, b_r) of the checkpoint. Rank 0 plans an attempt on the host from the statistics each node
+    reported with its push (``DeviceMerger.plan``: validation, clipping, weights) and announces members and
+    coefficients; every node then pulls its range of each member payload over NVLink, adds it into its
+    slice of the checkpoint in its own staging slot and writes the slice into every node's slot, through
+    NVLS multicast or per-peer stores (``apply``); rank 0 checks that all slices landed (``finish``).
+    Every payload is read once, by the node that owns the slice, and the broadcast is spread over all W
+    GPUs instead of funnelling through one. The caller orders the steps across nodes (announcement
+    before ``apply``, every node's completion before ``finish``), so no kernel waits on another node's
+    host progress.
 
     ``ctl``: this node's control buffer (``CTL_BYTES``, symmetric), ``ctl_ptrs``: every node's control
     buffer by rank; ``theta``: this node's fp32 staging slot (all slots hold the same checkpoint between
     merges); ``stage_ptrs`` / ``stage_mc``: every node's slot, and the multicast address (0 = none)."""
 
     CTL_BYTES = 8192
-    OFF_STATS, OFF_COEF, OFF_ARR, OFF_DONE, OFF_FLAG, OFF_BPRE, OFF_BBC, OFF_RANGES = (0, 2048, 2560, 2624, 2688,
-                                                                                       2752, 2816, 4096)
+    OFF_COEF, OFF_DONE, OFF_BBC, OFF_RANGES = 2048, 2624, 2816, 4096
 
     def __init__(self, rank: int, world: int, n: int, device, theta: torch.Tensor, stage_ptrs: Sequence[int],
                  stage_mc: int, ctl: torch.Tensor, ctl_ptrs: Sequence[int], stream: Optional[torch.cuda.Stream] = None):
         from ..ops import _lib
-        from ..ops._lib import c_int, c_void, c_ll, c_float
+        from ..ops._lib import c_int, c_void, c_ll
         self.L = _lib.lib()
         u64 = ctypes.c_ulonglong
         _lib.register("dt_dm_range", [c_void, c_int, c_ll, c_ll, c_void, c_void])
-        _lib.register("dt_dm_prepass", [c_void, c_int, c_ll, c_void, c_void, c_void, c_void, c_void])
         _lib.register("dt_dm_wait", [c_void, u64, c_int, u64, c_void])
-        _lib.register("dt_dm_publish", [c_void, c_int, c_void, c_void, c_int, u64, c_void])
-        _lib.register("dt_dm_apply", [c_void, c_int, c_ll, c_void, c_ll, c_ll, c_void, c_void, u64, c_void, c_int, c_int,
-                                      c_void])
+        _lib.register("dt_dm_apply", [c_void, c_int, c_ll, c_void, c_ll, c_ll, c_void, c_void, c_int, c_int, c_void])
         _lib.register("dt_dm_broadcast", [c_void, c_ll, c_ll, c_void, c_void, c_int, c_void, c_void, c_void])
         assert world <= 8 and ctl.numel() >= self.CTL_BYTES
         self.rank, self.world, self.n = rank, world, n
@@ -289,9 +286,8 @@ class DistributedMerger:
         self.base = ctl.data_ptr()
         self.a, self.b = self.range_of(rank)
         self.stream = stream or torch.cuda.Stream(device=self.device, priority=-100)
-        self.stats_host = torch.zeros(3 * 64, dtype=torch.float64).pin_memory()
         self.coef_host = torch.zeros(64, dtype=torch.float32).pin_memory()
-        self.coef_dev = torch.zeros(64, dtype=torch.float32, device=self.device)
+        self.coef_dev = ctl[self.OFF_COEF:self.OFF_COEF + 256].view(torch.float32)
         self._keep = None
 
     def range_of(self, r: int):
@@ -306,116 +302,52 @@ class DistributedMerger:
         self._keep = buf
         return buf
 
-    def reset_stats(self):
-        """Rank 0, before it announces an attempt: clear the statistics the nodes will add into."""
-        with torch.cuda.stream(self.stream):
-            self.ctl[self.OFF_STATS:self.OFF_STATS + 8 * 3 * 64].zero_()
-        self.stream.synchronize()
-
-    def _front(self, contribs, buf, stats_dst: int, arr_dst: int):
+    def apply(self, contribs: List[Contribution], coefs: Sequence[float], outer_lr: float):
+        """This node's slice: theta[a, b) -= outer_lr * sum_c coef_c * x_c, then its broadcast into every node's
+        slot; enqueued on ``self.stream``."""
         from ..ops._lib import check
-        sp = self.stream.cuda_stream
         n = len(contribs)
-        ranges = self.base + self.OFF_RANGES
+        assert 0 < n <= 64 and len(coefs) == n
+        buf = self._pack(contribs)
+        sp = self.stream.cuda_stream
+        has_dense = any(c.dense for c in contribs)
+        has_sparse = any(not c.dense for c in contribs)
         max_len = max(max((self.b - self.a) if c.dense else c.count // self.world + 1 for c in contribs), 1)
-        check(self.L.dt_dm_range(buf, n, self.a, self.b, ranges, sp), "dt_dm_range")
-        check(self.L.dt_dm_prepass(buf, n, max_len, ranges, stats_dst, arr_dst, self.base + self.OFF_BPRE, sp),
-              "dt_dm_prepass")
-        return max_len
-
-    def _max_len(self, contribs):
-        return max(max((self.b - self.a) if c.dense else c.count // self.world + 1 for c in contribs), 1)
-
-    # The attempt runs in three phases; the caller separates them with a cross-node synchronisation
-    # (control-bus keys in the in-box protocol, barriers in the microbenchmark), so no kernel waits on
-    # another node's host: (1) every node: ``prepass``; (2) rank 0: ``plan_publish``; (3) every node:
-    # ``apply``. Each call enqueues on ``self.stream``; synchronise it before signalling the phase done.
-    def prepass(self, contribs: List[Contribution]):
-        """Phase 1: this node's partial statistics, added into rank 0's."""
-        self._buf = self._pack(contribs)
-        r0 = self.ctl_ptrs[0]
-        with torch.cuda.stream(self.stream):
-            self._front(contribs, self._buf, r0 + self.OFF_STATS, r0 + self.OFF_ARR)
-
-    def plan_publish(self, contribs: List[Contribution], outer_lr: float, att: int, plan=None):
-        """Phase 2 (rank 0, after every node's phase 1): validation, clipping and weights from the summed
-        statistics, then the coefficients into every node's control buffer. Returns (info, failure):
-        a plan that raises publishes zero coefficients (the attempt still completes everywhere) and is
-        returned as `failure` for the caller to raise once phase 3 is done."""
-        from ..ops._lib import check
-        from .. import ops
-        plan = plan or (lambda st: DeviceMerger.plan(contribs, st))
-        n = len(contribs)
-        W = self.world
-        sp = self.stream.cuda_stream
-        with torch.cuda.stream(self.stream):
-            check(self.L.dt_dm_wait(self.base + self.OFF_ARR, att * W, 911, DT_WAIT_SHORT_NS, sp), "dt_dm_wait")
-            self.stats_host[:3 * n].copy_(self.ctl[self.OFF_STATS:self.OFF_STATS + 24 * n].view(torch.float64),
-                                          non_blocking=True)
-        self.stream.synchronize()
-        err = ops.device_error(self.stream)
-        if err[0]:
-            raise RuntimeError(f"distributed merge: device error {err} while gathering statistics")
-        stats = self.stats_host[:3 * n].view(n, 3).tolist()
-        failure = None
-        try:
-            coefs, info = plan(stats)
-        except Exception as e:
-            coefs, info, failure = [0.0] * n, {}, e
+        self.stream.synchronize()  # the pinned coefficient staging buffer is reused
         self.coef_host[:n] = torch.tensor([-float(outer_lr) * k for k in coefs], dtype=torch.float32)
         with torch.cuda.stream(self.stream):
             self.coef_dev[:n].copy_(self.coef_host[:n], non_blocking=True)
-            cd = (ctypes.c_void_p * W)(*[p + self.OFF_COEF for p in self.ctl_ptrs])
-            fd = (ctypes.c_void_p * W)(*[p + self.OFF_FLAG for p in self.ctl_ptrs])
-            check(self.L.dt_dm_publish(self.coef_dev.data_ptr(), n, cd, fd, W, att, sp), "dt_dm_publish")
-        info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
-        return info, failure
-
-    def apply(self, contribs: List[Contribution], att: int):
-        """Phase 3 (after rank 0's phase 2): this node's slice of the checkpoint, then its broadcast."""
-        from ..ops._lib import check
-        buf = self._pack(contribs)
-        sp = self.stream.cuda_stream
-        n = len(contribs)
-        has_dense = any(c.dense for c in contribs)
-        has_sparse = any(not c.dense for c in contribs)
-        with torch.cuda.stream(self.stream):
-            check(self.L.dt_dm_wait(self.base + self.OFF_FLAG, att, 913, DT_WAIT_SHORT_NS, sp), "dt_dm_wait")
-            check(self.L.dt_dm_apply(buf, n, self._max_len(contribs), self.base + self.OFF_RANGES, self.a, self.b,
-                                     self.base + self.OFF_COEF, self.base + self.OFF_FLAG, att, self.theta.data_ptr(),
-                                     int(has_dense), int(has_sparse), sp), "dt_dm_apply")
+            ranges = self.base + self.OFF_RANGES
+            if has_sparse:
+                check(self.L.dt_dm_range(buf, n, self.a, self.b, ranges, sp), "dt_dm_range")
+            check(self.L.dt_dm_apply(buf, n, max_len, ranges, self.a, self.b, self.coef_dev.data_ptr(),
+                                     self.theta.data_ptr(), int(has_dense), int(has_sparse), sp), "dt_dm_apply")
             dests = (ctypes.c_void_p * self.world)(*self.stage_ptrs)
             check(self.L.dt_dm_broadcast(self.theta.data_ptr(), self.a, self.b, self.stage_mc or None, dests,
                                          self.world, self.ctl_ptrs[0] + self.OFF_DONE, self.base + self.OFF_BBC, sp),
                   "dt_dm_broadcast")
 
-    def finish(self, att: int):
-        """Rank 0, after every node's phase 3: check that all slices landed."""
-        from ..ops._lib import check
+    def check(self, what: str = "apply"):
+        """Synchronise this node's merge stream; raise on a recorded device error."""
         from .. import ops
+        self.stream.synchronize()
+        err = ops.device_error(self.stream)
+        if err[0]:
+            raise RuntimeError(f"distributed merge ({what}): device error {err}")
+
+    def finish(self, att: int):
+        """Rank 0, after every node's ``apply`` of attempt ``att`` (the att-th on this merger) completed."""
+        from ..ops._lib import check
         with torch.cuda.stream(self.stream):
             check(self.L.dt_dm_wait(self.base + self.OFF_DONE, att * self.world, 912, DT_WAIT_SHORT_NS,
                                     self.stream.cuda_stream), "dt_dm_wait")
-        self.stream.synchronize()
-        err = ops.device_error(self.stream)
-        if err[0]:
-            raise RuntimeError(f"distributed merge: device error {err} while applying")
+        self.check("finish")
 
-    def check(self, phase: str):
-        """Synchronise this node's merge stream and raise on a recorded device error."""
-        from .. import ops
-        self.stream.synchronize()
-        err = ops.device_error(self.stream)
-        if err[0]:
-            raise RuntimeError(f"distributed merge ({phase}): device error {err}")
-
-    def run_local(self, contribs: List[Contribution], outer_lr: float, att: int, plan=None):
-        """All three phases on a single node (world 1)."""
+    def run_local(self, contribs: List[Contribution], stats: List[List[float]], outer_lr: float, att: int):
+        """The whole attempt on a single node (world 1): plan from ``stats``, apply, finish."""
         assert self.world == 1
-        self.prepass(contribs)
-        info, failure = self.plan_publish(contribs, outer_lr, att, plan)
-        self.apply(contribs, att)
+        coefs, info = DeviceMerger.plan(contribs, stats)
+        self.apply(contribs, coefs, outer_lr)
         self.finish(att)
-        if failure is not None:
-            raise failure
+        info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
         return info

@@ -64,6 +64,11 @@ def test_device_compress_matches_reference(k_fraction, adaptive):
     assert torch.equal(p.q[:K].cpu(), q)
     assert torch.allclose(p.scales[:sc.numel()].cpu(), sc)
     assert abs(st["dense_norm"] - float(combined.double().norm())) < 1e-6 * max(1, st["dense_norm"])
+    # statistics of the dequantised values as sent (what the coordinator validates and clips on)
+    deq = q.float() * sc[torch.arange(K) // 256]
+    ss, mx, nf = st["wire"]
+    assert abs(ss - float((deq.double() ** 2).sum())) < 1e-5 * ss
+    assert mx == pytest.approx(float(deq.abs().max()), rel=1e-6) and nf == 0
 
 
 @pytest.mark.parametrize("momentum,in_place", [(0.0, True), (0.0, False), (0.9, False)])
@@ -225,7 +230,7 @@ def test_distributed_merger_single_node_matches_reference():
     torch.manual_seed(2)
     theta0 = torch.randn(L.total, device=dev) * 0.02
     cfg = CompressionConfig(top_k_fraction=0.2, quantize_int8=True, int8_block=256)
-    contribs, dense_deltas, weights, keep = [], [], [], []
+    contribs, dense_deltas, weights, keep, stats = [], [], [], [], []
     for i, sc in enumerate([1.0, 4.0]):
         comp = DeviceCompressor(L, dev, cfg)
         d = torch.randn(L.total, device=dev) * 1e-3 * sc
@@ -233,7 +238,9 @@ def test_distributed_merger_single_node_matches_reference():
         comp.begin(theta0 - d)
         comp.finish()
         torch.cuda.synchronize()
-        K = comp.read_stats()["num_params_kept"]
+        st = comp.read_stats()
+        K = st["num_params_kept"]
+        stats.append(st["wire"])
         p = comp.payload
         keep.append(comp)
         w = 1000.0 / (i + 1)
@@ -251,10 +258,69 @@ def test_distributed_merger_single_node_matches_reference():
     torch.cuda.synchronize()
     ck = {e.name: theta0[e.offset:e.offset + e.numel].cpu() for e in L.entries}
     for att in (1, 2):
-        dm.reset_stats()
-        info = dm.run_local(contribs, 1.0, att)
+        info = dm.run_local(contribs, stats, 1.0, att)
         ck, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=0.0)
         got = theta.cpu()
         for e in L.entries:
             assert torch.allclose(got[e.offset:e.offset + e.numel], ck[e.name], atol=1e-7, rtol=1e-5), (att, e.name)
         assert info["accepted"] == 2
+
+
+def test_raw_push_kernel():
+    """Raw push: the dense delta + error feedback leaves as fp32, error feedback cleared, statistics of
+    the whole delta."""
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor
+    L = _layout()
+    dev = torch.device("cuda")
+    comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=0.1))
+    master = torch.randn(L.total, device=dev) * 0.02
+    d = torch.randn(L.total, device=dev) * 1e-3
+    e0 = torch.randn(L.total, device=dev) * 1e-4
+    comp.snap.copy_(master + d)
+    comp.ef.copy_(e0)
+    out = torch.empty(L.total, device=dev)
+    comp.begin(master)
+    comp.finish_raw(out)
+    torch.cuda.synchronize()
+    want = torch.zeros(L.total, device=dev)
+    for e in L.entries:
+        sl = slice(e.offset, e.offset + e.numel)
+        want[sl] = (master + d)[sl] - master[sl] + e0[sl]
+    for e in L.entries:
+        sl = slice(e.offset, e.offset + e.numel)
+        torch.testing.assert_close(out[sl], want[sl], rtol=0, atol=1e-7)
+    assert float(comp.ef.abs().max()) == 0.0
+    st = comp.read_stats(raw=True)
+    assert st["num_params_kept"] == L.total
+    assert abs(st["dense_norm"] - float(want.double().norm())) < 1e-6 * st["dense_norm"]
+    assert st["sparse_norm"] == st["dense_norm"]
+
+
+def test_inbox_bandwidth_adaptive_protocol():
+    """Bandwidth-adaptive pushes on one GPU: the first push is a loss-based top-k (no bandwidth measured
+    yet), later pushes are raw once the merge has measured the pull rate; merges apply them."""
+    import json
+    import time
+    from distrain_b200.config import bench_config
+    from distrain_b200.parallel.node import InBoxNode
+    run = bench_config("micro")
+    run.model.vocab_size = 512
+    run.push_every = 6
+    run.optim.lr = 3e-3
+    run.bandwidth_adaptive = True
+    node = InBoxNode(run, rank=0, world=1, device=torch.device("cuda"), enable_push=True)
+    g = torch.Generator().manual_seed(0)
+    batch = torch.randint(0, 512, (run.micro_batch, run.seq_len), generator=g, dtype=torch.int32).cuda()
+    losses = []
+    for i in range(60):
+        node.train_step_device(batch)
+        losses.append(node.engine.loss[0].item())
+    time.sleep(0.5)
+    coord = node.sync.coord
+    assert coord.error is None, repr(coord.error)
+    assert not coord.failed, coord.failed
+    bodies = [json.loads(node.sync.bus.get(f"push/0/{s}")) for s in range(1, node.sync.seq + 1)]
+    assert bodies[0]["_dense"] == 0 and any(b["_dense"] == 1 for b in bodies[1:]), [b["_dense"] for b in bodies]
+    assert len(coord.merges) >= 3 and losses[-1] < losses[0]
+    node.close()

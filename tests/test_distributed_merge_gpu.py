@@ -1,9 +1,10 @@
 """Distributed merge (every node merges one slice of the checkpoint) against the fp32 reference merge.
 
-Two spawned ranks on two GPUs each compress their own delta into a symmetric payload buffer; rank 0
-leads two merge attempts, rank 1 works; after each attempt both ranks' staging slots must hold the
-reference merge of both dequantised deltas (staleness-style weights, 3x-average norm clip) applied to the
-previous checkpoint. Skipped on a one-GPU box (the one-GPU case runs inside the in-box protocol tests)."""
+Two spawned ranks on two GPUs each compress their own delta into a symmetric payload buffer and report
+its statistics; both plan from them, merge their slice and broadcast it, twice; after each attempt both
+ranks' staging slots must hold the reference merge of both dequantised deltas (staleness-style weights,
+3x-average norm clip) applied to the previous checkpoint. Skipped on a one-GPU box (the one-GPU case is
+in test_compress_merge_gpu.py)."""
 import os
 import socket
 
@@ -28,7 +29,7 @@ def _rank(rank, port, out_dir):
     from distrain_b200.models.params import ParamLayout
     from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
     from distrain_b200.parallel.inbox import _symm_alloc
-    from distrain_b200.parallel.merge import Contribution, DistributedMerger
+    from distrain_b200.parallel.merge import Contribution, DeviceMerger, DistributedMerger
     from distrain_b200 import ops
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -50,11 +51,13 @@ def _rank(rank, port, out_dir):
     comp.begin(theta0 - delta)
     comp.finish()
     torch.cuda.synchronize()
-    K = comp.read_stats()["num_params_kept"]
-    cnt = torch.tensor([K], device=dev, dtype=torch.int64)
-    counts = [torch.zeros_like(cnt) for _ in range(W)]
-    dist.all_gather(counts, cnt)
-    counts = [int(c) for c in counts]
+    st = comp.read_stats()
+    K = st["num_params_kept"]
+    cnt = torch.tensor([K] + st["wire"], device=dev, dtype=torch.float64)
+    got = [torch.zeros_like(cnt) for _ in range(W)]
+    dist.all_gather(got, cnt)
+    counts = [int(g[0]) for g in got]
+    stats = [g[1:].tolist() for g in got]
     stage_buf, stage_ptrs, stage_mc, _h2 = _symm_alloc((n * 4 + 4095) // 4096 * 4096, dev, W)
     theta = stage_buf[:n * 4].view(torch.float32)
     theta.copy_(theta0)
@@ -72,20 +75,11 @@ def _rank(rank, port, out_dir):
     dist.barrier()
     slots, infos = [], []
     for att in (1, 2):
-        if rank == 0:
-            dm.reset_stats()
+        coefs, info = DeviceMerger.plan(contribs, stats)
+        infos.append(info)
         dist.barrier()
-        dm.prepass(contribs)
-        dm.check("prepass")
-        dist.barrier()
-        if rank == 0:
-            info, failure = dm.plan_publish(contribs, 1.0, att)
-            dm.check("publish")
-            assert failure is None
-            infos.append(info)
-        dist.barrier()
-        dm.apply(contribs, att)
-        dm.check("apply")
+        dm.apply(contribs, coefs, 1.0)
+        dm.check()
         dist.barrier()
         if rank == 0:
             dm.finish(att)
@@ -94,8 +88,7 @@ def _rank(rank, port, out_dir):
         if att == 1:
             diag = {"ranges": ctl[dm.OFF_RANGES:dm.OFF_RANGES + 16 * W].view(torch.int64).cpu().clone(),
                     "coefs": ctl[dm.OFF_COEF:dm.OFF_COEF + 4 * W].view(torch.float32).cpu().clone(),
-                    "stats": ctl[:24 * W].view(torch.float64).cpu().clone(), "a": dm.a, "b": dm.b,
-                    "mc": int(stage_mc or 0)}
+                    "stats": torch.tensor(stats), "a": dm.a, "b": dm.b, "mc": int(stage_mc or 0)}
     gi = payload.global_indices(K).cpu()
     deq = (payload.q[:K].float() * payload.scales[torch.arange(K, device=dev) // 256]).cpu()
     torch.save({"slots": slots, "idx": gi, "val": deq, "theta0": theta0.cpu(), "infos": infos, "diag": diag,

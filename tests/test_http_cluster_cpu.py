@@ -52,3 +52,14 @@ def test_two_cpu_nodes_and_coordinator(tmp_path):
         last = sum(x["loss"] for x in n.log[-5:]) / 5
         assert last < first, (first, last)
         assert n.version >= 1
+
+
+def test_adaptive_push_mode():
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import adaptive_push_mode
+    cfg = CompressionConfig(top_k_fraction=0.1, quantize_int8=True, int8_block=256)
+    assert adaptive_push_mode(False, 1e12, 400, 3.0, cfg) == ("topk", 0.1, 256)
+    assert adaptive_push_mode(True, 0.0, 400, 6.0, cfg) == ("topk", 0.75, 256)   # no bandwidth yet: loss-based
+    assert adaptive_push_mode(True, 100.0, 400, 3.0, cfg) == ("raw", 1.0, 0)     # 400 B within 10 s at 100 B/s
+    kind, k, qb = adaptive_push_mode(True, 10.0, 4000, 3.0, cfg)                  # budget 100 B of 4000 raw
+    assert kind == "topk" and qb == 0 and abs(k - 100 / 2000) < 1e-9
