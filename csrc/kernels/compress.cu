@@ -572,6 +572,8 @@ DT_API int dt_compress_raw(float* ef, float* out, long long n, cudaStream_t st) 
 // Per-segment statistics into a device double array: [s*6 + {sumsq, kept_sq, k, maxabs, nonfinite, len}],
 // then the total kept count at [nseg*6] and the dequantised wire statistics {sum of squares, max |x|,
 // non-finite} at [nseg*6 + 1..3] (zero unless the push was quantised).
+DT_API long long dt_compress_stats_len(int nseg) { return 6LL * nseg + 4; }
+
 DT_API int dt_compress_export_stats(void* ws, int nseg, int nchunks, double* out, cudaStream_t st) {
   WsPtrs w = carve(ws, nseg, nchunks);
   export_stats_kernel<<<(nseg + 255) / 256, 256, 0, st>>>(w.seg, nseg, w.total, out);

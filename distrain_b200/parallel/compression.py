@@ -180,6 +180,7 @@ class DeviceCompressor:
                                              c_void])
         _lib.register("dt_compress_export_stats", [c_void, c_int, c_int, c_void, c_void])
         _lib.register("dt_compress_raw", [c_void, c_void, c_ll, c_void])
+        _lib.register("dt_compress_stats_len", [c_int], restype=c_ll)
         self.layout, self.device, self.cfg = layout, torch.device(device), cfg
         n = layout.total
         self.cseg, self.cstart, self.cend, self.nseg = layout.chunk_tables(self.device)
@@ -195,8 +196,9 @@ class DeviceCompressor:
         self.ef = torch.zeros(n, dtype=torch.float32, device=self.device)
         wsb = self.L.dt_compress_workspace_bytes(self.nseg, self.nchunks)
         self.ws = torch.zeros(wsb, dtype=torch.uint8, device=self.device)
-        self.stats_dev = torch.zeros(self.nseg * 6 + 1, dtype=torch.float64, device=self.device)
-        self.stats_host = torch.zeros(self.nseg * 6 + 1, dtype=torch.float64).pin_memory()
+        nstat = self.L.dt_compress_stats_len(self.nseg)  # doubles dt_compress_export_stats writes
+        self.stats_dev = torch.zeros(nstat, dtype=torch.float64, device=self.device)
+        self.stats_host = torch.zeros(nstat, dtype=torch.float64).pin_memory()
         self.capacity = self.capacity_for(layout, cfg.top_k_fraction)
         self.payload = payload or DevicePayload.allocate(self.capacity, cfg.int8_block if cfg.quantize_int8 else 0,
                                                          self.device)

@@ -45,7 +45,7 @@ def test_noalloc_matches_allocating_entry_point_twice():
     ef = torch.zeros(layout.total, device=dev)
     cap = ref.capacity
     out = DevicePayload.allocate(cap, 256, dev)
-    stats = torch.zeros(ref.nseg * 6 + 4, dtype=torch.float64, device=dev)
+    stats = torch.zeros(ref.stats_dev.numel(), dtype=torch.float64, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
 
     for call in range(2):
