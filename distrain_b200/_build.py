@@ -121,6 +121,52 @@ def build_runtime(force: bool = False, verbose: bool = False) -> str:
     return RUNTIME_SO
 
 
+def sanitizer_cxx(sanitize: str):
+    """The first of $CXX and g++ that compiles and links a program with -fsanitize=<sanitize> (None if
+    neither does: a toolchain without the sanitizer runtime libraries)."""
+    seen = []
+    for c in (os.environ.get("CXX"), "g++"):
+        if not c or c in seen:
+            continue
+        seen.append(c)
+        try:
+            r = subprocess.run([c, "-fsanitize=" + sanitize, "-x", "c++", "-", "-o", os.devnull],
+                               input=b"int main(){return 0;}", capture_output=True, timeout=120)
+        except (OSError, subprocess.TimeoutExpired):
+            continue
+        if r.returncode == 0:
+            return c
+    return None
+
+
+def build_runtime_selftest(sanitize: str, tag: str) -> str:
+    """The runtime sources plus ``csrc/runtime/tests/selftest.cpp`` as one executable built with
+    ``-fsanitize=<sanitize>`` (e.g. "address,undefined" or "thread"); returns its path."""
+    srcs = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cpp"))) + [os.path.join(CSRC, "runtime", "tests",
+                                                                                     "selftest.cpp")]
+    hdrs = glob.glob(os.path.join(CSRC, "runtime", "*.hpp")) + glob.glob(os.path.join(CSRC, "runtime", "*.h"))
+    odir = os.path.join(BUILDDIR, "selftest-" + tag)
+    os.makedirs(odir, exist_ok=True)
+    cxx = sanitizer_cxx(sanitize)
+    if cxx is None:
+        raise RuntimeError(f"no C++ compiler here links -fsanitize={sanitize}")
+    flags = ["-O1", "-g", "-std=c++17", "-pthread", "-fno-omit-frame-pointer", "-fsanitize=" + sanitize,
+             "-I", os.path.join(CSRC, "runtime")]
+    hdr_time = _newest(hdrs + [__file__])
+    jobs, objs = [], []
+    for src in srcs:
+        o = os.path.join(odir, os.path.basename(src) + ".o")
+        objs.append(o)
+        if not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(src), hdr_time):
+            jobs.append([cxx] + flags + ["-c", src, "-o", o])
+    if jobs:
+        _compile_many(jobs, min(len(jobs), os.cpu_count() or 4))
+    exe = os.path.join(odir, "selftest")
+    if jobs or not os.path.exists(exe) or os.path.getmtime(exe) < _newest(objs):
+        _run([cxx, "-fsanitize=" + sanitize, "-pthread", "-o", exe] + objs + ["-ldl"])
+    return exe
+
+
 def kernels_stale() -> bool:
     srcs = glob.glob(os.path.join(CSRC, "kernels", "*.cu")) + glob.glob(os.path.join(CSRC, "kernels", "*.cuh"))
     return not os.path.exists(KERNELS_SO) or os.path.getmtime(KERNELS_SO) < _newest(srcs)
