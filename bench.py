@@ -114,6 +114,8 @@ def main():
     from distrain_b200.config import bench_config
     from distrain_b200.parallel.node import InBoxNode
     from distrain_b200 import ops
+    from distrain_b200.utils.tracing import nvtx, setup_logging
+    setup_logging()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -165,8 +167,9 @@ def main():
             dist.barrier()
 
     # warm-up (also captures the CUDA graph)
-    for i in range(args.warmup):
-        node.train_step_device(dev_batches[i % 4])
+    with nvtx("warmup"):
+        for i in range(args.warmup):
+            node.train_step_device(dev_batches[i % 4])
     torch.cuda.synchronize()
     barrier()
 
@@ -182,8 +185,9 @@ def main():
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for i in range(args.steps):
-        node.train_step_device(dev_batches[i % 4])
+    with nvtx("timed"):
+        for i in range(args.steps):
+            node.train_step_device(dev_batches[i % 4])
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -196,7 +200,8 @@ def main():
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
-        losses = node.train_steps_e2e(ring, args.steps)
+        with nvtx("timed_e2e"):
+            losses = node.train_steps_e2e(ring, args.steps)
         f1.record(stream)
         torch.cuda.synchronize()
         barrier()

@@ -454,6 +454,8 @@ def main(argv=None):
     p.set_defaults(fn=cmd_micro_cluster)
 
     args = ap.parse_args(argv)
+    from .utils.tracing import setup_logging
+    setup_logging(os.environ.get("DT_LOG", "info"))
     args.fn(args)
 
 

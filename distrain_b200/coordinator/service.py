@@ -14,6 +14,7 @@ from __future__ import annotations
 import ctypes
 import hashlib
 import json
+import logging
 import math
 import threading
 import time
@@ -37,6 +38,8 @@ VERSION = "0.1.0"
 _HANDLER = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_void_p,
                             ctypes.c_longlong, ctypes.c_void_p)
 
+
+log = logging.getLogger("distrain_b200.coordinator")
 
 class CoordinatorService:
     def __init__(self, cfg: CoordinatorConfig, store: ObjectStore, merge_device: str = "cpu",
@@ -302,6 +305,11 @@ class CoordinatorService:
         return d
 
     def _aggregate(self, snap: P.AccumulatorState):
+        from ..utils.tracing import nvtx
+        with nvtx("aggregate"):
+            return self._aggregate_impl(snap)
+
+    def _aggregate_impl(self, snap: P.AccumulatorState):
         t0 = time.time()
         try:
             new_version = snap.checkpoint_version + 1
@@ -339,6 +347,8 @@ class CoordinatorService:
                 self.store.put(P.optimizer_state_path(new_version),
                                save_velocity({k: v.cpu() for k, v in velocity.items()}))
             elapsed = time.time() - t0
+            log.info("aggregation v%d: %d accepted, %d rejected, outer delta norm %.4g, %.2f s", new_version,
+                     info["accepted"], rejected, info["outer_delta_norm"], elapsed)
             total_weight = sum(c.weight for c in snap.contributions)
             self.store.put_json(P.checkpoint_metadata_path(new_version), {
                 "version": new_version, "contributions_accepted": info["accepted"], "contributions_rejected": rejected,

@@ -341,6 +341,11 @@ class TrainEngine:
     # ───────────────────────── CUDA graph ─────────────────────────
     def capture(self, warmup: int = 1):
         """Capture one full train step (fwd+bwd+AdamW) as a CUDA graph; replay with ``replay()``."""
+        from ..utils.tracing import nvtx
+        with nvtx("capture"):
+            return self._capture(warmup)
+
+    def _capture(self, warmup: int = 1):
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream())
         # warm-up on the side stream (loads modules, sets smem attributes) without touching weights or

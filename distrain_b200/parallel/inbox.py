@@ -26,6 +26,7 @@ error-feedback residual.
 from __future__ import annotations
 
 import json
+import logging
 import math
 import os
 import queue
@@ -38,8 +39,12 @@ import torch.distributed as dist
 
 from ..config import RunConfig
 from ..protocol import Accumulator, DeltaPush, delta_path
+from ..utils.tracing import PhaseTimer, nvtx
 from .compression import DeviceCompressor, DevicePayload, adaptive_push_mode
 from .merge import Contribution, DeviceMerger, DistributedMerger
+
+
+log = logging.getLogger("distrain_b200.inbox")
 
 
 # ─────────────────────────────── control bus ───────────────────────────────
@@ -275,6 +280,10 @@ class InBoxSync:
                                   self.run.compression)
 
     def _push(self, partial: bool, mode=None) -> bool:
+        with nvtx("push"):
+            return self._push_impl(partial, mode)
+
+    def _push_impl(self, partial: bool, mode=None) -> bool:
         slot = (self.seq + 1) % self.n_slots
         if not self._slot_free(slot):
             return False  # coordinator still holds that payload; try again next step
@@ -350,6 +359,14 @@ class InBoxSync:
             self.bus.set(f"pushseq/{self.rank}", str(meta.seq_num))
 
     def _swap(self, new_version: int):
+        t0 = time.perf_counter()
+        with nvtx("swap"):
+            self._swap_impl(new_version)
+        log.info("node %s swap v%d -> v%d in %.1f ms", self.node_id, self.version_before_swap, new_version,
+                 (time.perf_counter() - t0) * 1e3)
+
+    def _swap_impl(self, new_version: int):
+        self.version_before_swap = self.version
         run = self.run
         rebase = run.swap_mode == "rebase"
         if not rebase and self.node.round_step > 0 and not self.first_round:
@@ -415,8 +432,10 @@ class InBoxSync:
                     continue
                 att += 1
                 plan = json.loads(raw)
-                self.dm.apply([self.member_contribution(m) for m in plan["members"]], plan["coefs"], plan["lr"])
-                self.dm.check()
+                with nvtx("merge/slice"):
+                    self.dm.apply([self.member_contribution(m) for m in plan["members"]], plan["coefs"],
+                                  plan["lr"])
+                    self.dm.check()
                 self.bus.set(f"dmdone/{att}/{self.rank}", "1")
         except BaseException as e:  # surfaced by close()
             self.dm_error = e
@@ -568,6 +587,8 @@ class InBoxCoordinator:
             info["multicast"] = bool(mc32)
             self.merges.append(info)
             self._publish_bandwidth(info)
+            log.info("merge v%d: %d contributions (%d accepted), %.1f MB pulled, %.2f ms", new_version,
+                     len(contribs), info.get("accepted", 0), info.get("pulled_bytes", 0) / 1e6, info["wall_ms"])
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)
@@ -583,6 +604,7 @@ class InBoxCoordinator:
             # like a failed reference aggregation: count it, drop the contributions of this attempt
             # (their payload slots are released) and keep serving
             self.failed.append(repr(e))
+            log.warning("merge failed: %r", e)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)
@@ -620,8 +642,10 @@ class InBoxCoordinator:
             new_version = self.version + 1
             self._wait_consumed(new_version)
             dm = self.sync.dm
-            stats = [self.payload_of[(c.node_id, c.seq_num)]["_stats"] for c in snap.contributions]
-            coefs, info = DeviceMerger.plan(contribs, stats)  # raises when no contribution is valid
+            timer = PhaseTimer("merge", log)
+            with timer.phase("plan"):
+                stats = [self.payload_of[(c.node_id, c.seq_num)]["_stats"] for c in snap.contributions]
+                coefs, info = DeviceMerger.plan(contribs, stats)  # raises when no contribution is valid
             info["pulled_bytes"] = sum(c.wire_bytes for c in contribs)
             self.attempt += 1
             att = self.attempt
@@ -630,14 +654,18 @@ class InBoxCoordinator:
             ev0.record(dm.stream)
             W = self.world
             lr = self.run.outer_lr
-            if W > 1:
-                self.bus.set(f"dm/{att}", json.dumps({"version": new_version, "members": members, "coefs": coefs,
-                                                      "lr": lr}))
-            dm.apply(contribs, coefs, lr)
-            dm.check()
-            for r in range(1, W):
-                self._wait_key(f"dmdone/{att}/{r}")
-            dm.finish(att)
+            with timer.phase("announce"):
+                if W > 1:
+                    self.bus.set(f"dm/{att}", json.dumps({"version": new_version, "members": members,
+                                                          "coefs": coefs, "lr": lr}))
+            with timer.phase("slice"):
+                dm.apply(contribs, coefs, lr)
+                dm.check()
+            with timer.phase("wait_slices"):
+                for r in range(1, W):
+                    self._wait_key(f"dmdone/{att}/{r}")
+                dm.finish(att)
+            info["phases_ms"] = timer.report(version=new_version, contributions=len(contribs))
             ev1.record(dm.stream)
             ev1.synchronize()
             info["device_ms"] = ev0.elapsed_time(ev1)
@@ -650,6 +678,8 @@ class InBoxCoordinator:
             info["distributed"] = self.world
             self.merges.append(info)
             self._publish_bandwidth(info)
+            log.info("merge v%d: %d contributions (%d accepted), %.1f MB pulled, %.2f ms", new_version,
+                     len(contribs), info.get("accepted", 0), info.get("pulled_bytes", 0) / 1e6, info["wall_ms"])
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)
@@ -663,6 +693,7 @@ class InBoxCoordinator:
             raise
         except Exception as e:
             self.failed.append(repr(e))
+            log.warning("merge failed: %r", e)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
                 self._release(r, c.seq_num)

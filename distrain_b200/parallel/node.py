@@ -17,6 +17,7 @@ import torch
 
 from ..config import RunConfig
 from ..models.engine import TrainEngine
+from ..utils.tracing import nvtx
 
 
 class InBoxNode:
@@ -55,14 +56,15 @@ class InBoxNode:
     def train_step_device(self, tokens_dev: torch.Tensor):
         """One training step on tokens already resident on the device (no host sync)."""
         self._ensure_graph()
-        if self.sync is not None:
-            self.sync.before_step()
-        self.engine.set_tokens(tokens_dev)
-        self.engine.step()
-        self.step_count += 1
-        self.round_step += 1
-        if self.sync is not None:
-            self.sync.after_step()
+        with nvtx("step"):
+            if self.sync is not None:
+                self.sync.before_step()
+            self.engine.set_tokens(tokens_dev)
+            self.engine.step()
+            self.step_count += 1
+            self.round_step += 1
+            if self.sync is not None:
+                self.sync.after_step()
 
     def train_steps_e2e(self, host_batches, steps: int):
         """Public end-to-end loop: pinned-host tokens -> H2D -> step -> D2H loss read, every step.
@@ -73,16 +75,17 @@ class InBoxNode:
         ev = [torch.cuda.Event(), torch.cuda.Event()]
         losses = []
         for i in range(steps):
-            if self.sync is not None:
-                self.sync.before_step()
-            self.engine.ids.copy_(host_batches[i % len(host_batches)], non_blocking=True)
-            self.engine.step()
-            pinned_loss[i % 2].copy_(self.engine.loss, non_blocking=True)
-            ev[i % 2].record(stream)
-            self.step_count += 1
-            self.round_step += 1
-            if self.sync is not None:
-                self.sync.after_step()
+            with nvtx("step"):
+                if self.sync is not None:
+                    self.sync.before_step()
+                self.engine.ids.copy_(host_batches[i % len(host_batches)], non_blocking=True)
+                self.engine.step()
+                pinned_loss[i % 2].copy_(self.engine.loss, non_blocking=True)
+                ev[i % 2].record(stream)
+                self.step_count += 1
+                self.round_step += 1
+                if self.sync is not None:
+                    self.sync.after_step()
             if i > 0:
                 ev[(i - 1) % 2].synchronize()
                 losses.append(float(pinned_loss[(i - 1) % 2][0]))
