@@ -310,6 +310,12 @@ class RunConfig(_Json):
     #     of its own progress ("keep" and "reset" are the other choices);
     #   reset_optimizer_on_swap False: keep the AdamW moments.
     payload_slots: int = 2  # compressed-delta buffers per node (1 halves that memory; pushes then wait for the merge)
+    # in-box checkpoint persistence: object-store directory ("" = off), every N versions, newest kept; resume
+    # starts every node from the newest stored version
+    checkpoint_store: str = ""
+    checkpoint_every: int = 0
+    keep_versions: int = 10
+    resume: bool = False
     swap_mode: str = "rebase"
     ef_on_swap: str = "fold"
     reset_optimizer_on_swap: bool = False

@@ -41,6 +41,7 @@ from ..config import RunConfig
 from ..protocol import Accumulator, DeltaPush, delta_path
 from ..utils.tracing import PhaseTimer, nvtx
 from .compression import DeviceCompressor, DevicePayload, adaptive_push_mode
+from .inbox_ckpt import CheckpointWriter, latest_version, resume_flat
 from .merge import Contribution, DeviceMerger, DistributedMerger
 
 
@@ -166,6 +167,20 @@ class InBoxSync:
         self.stage_buf, self.stage_ptrs, self.stage_mc, self._stage_h = _symm_alloc(self.stage_bytes, self.device,
                                                                                    world, dp_group)
         self.compressor = DeviceCompressor(self.layout, self.device, cfg, payload=self.slots[0])
+        # checkpoint store: resume from its newest version before anything copies the weights
+        self.store = None
+        self.resumed_version = 0
+        if run.checkpoint_store:
+            from ..utils.storage import FsStore
+            self.store = FsStore(run.checkpoint_store)
+            if run.resume:
+                v = latest_version(self.store, n_shards)
+                if v:
+                    eng.master.copy_(resume_flat(self.store, self.layout, v, shard, n_shards).to(self.device))
+                    from .. import ops
+                    ops.cast_bf16(eng.master, eng.p16)
+                    self.version = self.resumed_version = v
+                    log.info("node %s resumed from stored checkpoint v%d", self.node_id, v)
         self.compressor.reset(eng.master)
         # without tensor parallelism every node merges one slice of the checkpoint (DistributedMerger);
         # every node's slot starts as the (identical) initial weights
@@ -180,6 +195,8 @@ class InBoxSync:
         multi = world * n_shards > 1
         self.bus = StoreBus(f"dtinbox/s{shard}/" if n_shards > 1 else "dtinbox/") if multi else LocalBus()
         self.shared = self.bus if n_shards == 1 else StoreBus("dtinbox/shared/")
+        if self.resumed_version:
+            self.bus.set(f"consumed/{self.rank}", str(self.resumed_version))
         self.inflight = None  # (seq, event, slot)
         self.slot_seq = [-1] * self.n_slots
         self.ef_ready = None
@@ -468,7 +485,11 @@ class InBoxCoordinator:
         self.shared = self.bus if ns == 1 else StoreBus("dtinbox/shared/")
         self.attempt = 0
         self.acc = Accumulator(staleness_decay=run.staleness_decay, max_staleness=run.max_staleness,
-                               min_contributions=0, checkpoint_version=0)
+                               min_contributions=0, checkpoint_version=sync.resumed_version)
+        self.ckpt = None
+        if sync.store is not None and run.checkpoint_every > 0:
+            self.ckpt = CheckpointWriter(sync.store, sync.layout, run.checkpoint_every, run.keep_versions, 0,
+                                         sync.n_shards)
         for r in range(world):
             self.acc.heartbeat(f"node-{r:02d}")
         self.next_seq = [1] * world
@@ -481,7 +502,7 @@ class InBoxCoordinator:
             stream = torch.cuda.Stream(device=sync.device, priority=-100)
             self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
                                        theta_buffer=sync.stage_view())
-        self.version = 0
+        self.version = sync.resumed_version
         self.merges: List[dict] = []
         self.failed: List[str] = []
         self.stop = threading.Event()
@@ -597,6 +618,7 @@ class InBoxCoordinator:
             tokens = sum(c.tokens_processed for c in snap.contributions)
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
             self.shared.set("version", str(new_version))
+            self._maybe_store(new_version, info)
         except _Shutdown:
             self.acc.abort_merge()
             raise
@@ -613,6 +635,14 @@ class InBoxCoordinator:
                                             if (c.node_id, c.seq_num) not in {(x.node_id, x.seq_num)
                                                                              for x in snap.contributions}]
             self.acc.abort_merge()
+
+    def _maybe_store(self, version: int, info: dict):
+        """Persist a due version from this GPU's slot (before the next merge may overwrite it)."""
+        if self.ckpt is None or not self.ckpt.due(version):
+            return
+        stream = self.sync.dm.stream if self.sync.dm is not None else self.merger.stream
+        self.ckpt.snapshot(self.sync.stage_view(), version, stream,
+                           meta={"contributions_accepted": info.get("accepted"), "source": "in-box merge"})
 
     def _publish_bandwidth(self, info: dict):
         """Measured payload pull rate of this merge (bytes/s over its wall time), the in-box counterpart of
@@ -688,6 +718,7 @@ class InBoxCoordinator:
             tokens = sum(c.tokens_processed for c in snap.contributions)
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
             self.shared.set("version", str(new_version))
+            self._maybe_store(new_version, info)
         except _Shutdown:
             self.acc.abort_merge()
             raise
@@ -720,6 +751,8 @@ class InBoxCoordinator:
     def close(self):
         self.stop.set()
         self.thread.join(timeout=30)
+        if self.ckpt is not None:
+            self.ckpt.close()
         if self.error is not None:
             raise RuntimeError(f"coordinator thread failed: {self.error!r}") from self.error
 
@@ -737,6 +770,10 @@ class ShardFollower:
         stream = torch.cuda.Stream(device=sync.device, priority=-100)
         self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
                                    theta_buffer=sync.stage_view())
+        self.ckpt = None
+        if sync.store is not None and run.checkpoint_every > 0:
+            self.ckpt = CheckpointWriter(sync.store, sync.layout, run.checkpoint_every, run.keep_versions, sync.shard,
+                                         sync.n_shards)
         self.attempt = 0
         self.merges: List[dict] = []
         self.failed: List[str] = []
@@ -761,6 +798,8 @@ class ShardFollower:
         self.merger.accumulate_apply(contribs, plan["coefs"], self.run.outer_lr, mc32=mc32, stage32=p32)
         self.merger.stream.synchronize()
         self.merges.append({"version": v, "n_contrib": len(contribs)})
+        if self.ckpt is not None and self.ckpt.due(v):  # this shard's file, before the next merge writes
+            self.ckpt.snapshot(self.sync.stage_view(), v, self.merger.stream)
         self.shared.set(f"merged/{att}/{self.sync.shard}", "1")
 
     def _loop(self):
@@ -779,5 +818,7 @@ class ShardFollower:
     def close(self):
         self.stop.set()
         self.thread.join(timeout=30)
+        if self.ckpt is not None:
+            self.ckpt.close()
         if self.error is not None:
             raise RuntimeError(f"shard coordinator thread failed: {self.error!r}") from self.error

@@ -324,3 +324,45 @@ def test_inbox_bandwidth_adaptive_protocol():
     assert bodies[0]["_dense"] == 0 and any(b["_dense"] == 1 for b in bodies[1:]), [b["_dense"] for b in bodies]
     assert len(coord.merges) >= 3 and losses[-1] < losses[0]
     node.close()
+
+
+def test_inbox_checkpoint_store_and_resume(tmp_path):
+    """The one-GPU protocol stores every merged version in the reference layout; a restarted node resumes
+    from the newest one (weights, bf16 copy, version)."""
+    import time
+    from distrain_b200.config import bench_config
+    from distrain_b200.parallel.node import InBoxNode
+    from distrain_b200.parallel.inbox_ckpt import latest_version, resume_flat
+    from distrain_b200.utils.storage import FsStore
+    run = bench_config("micro")
+    run.model.vocab_size = 512
+    run.push_every = 6
+    run.optim.lr = 3e-3
+    run.checkpoint_store = str(tmp_path)
+    run.checkpoint_every = 1
+    run.keep_versions = 3
+    node = InBoxNode(run, rank=0, world=1, device=torch.device("cuda"), enable_push=True)
+    g = torch.Generator().manual_seed(0)
+    batch = torch.randint(0, 512, (run.micro_batch, run.seq_len), generator=g, dtype=torch.int32).cuda()
+    for i in range(40):
+        node.train_step_device(batch)
+    time.sleep(0.5)
+    merged = node.sync.coord.version
+    node.close()
+    store = FsStore(str(tmp_path))
+    v = latest_version(store)
+    assert v is not None and v == merged >= 2
+    flat = resume_flat(store, node.engine.layout, v)
+    assert torch.isfinite(flat).all()
+    del node
+    torch.cuda.empty_cache()
+    run.resume = True
+    node2 = InBoxNode(run, rank=0, world=1, device=torch.device("cuda"), enable_push=True)
+    assert node2.sync.version == v and node2.sync.coord.version == v
+    L = node2.engine.layout
+    for e in L.entries:
+        sl = slice(e.offset, e.offset + e.numel)
+        assert torch.equal(node2.engine.master[sl].cpu(), flat[sl]), e.name
+    assert torch.equal(node2.engine.p16, node2.engine.master.bfloat16())
+    node2.train_step_device(batch)
+    node2.close()
