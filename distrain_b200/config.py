@@ -316,6 +316,7 @@ class RunConfig(_Json):
     checkpoint_every: int = 0
     keep_versions: int = 10
     resume: bool = False
+    metrics_port: int = -1  # in-box coordinator's Prometheus /metrics (-1 = off, 0 = any free port)
     swap_mode: str = "rebase"
     ef_on_swap: str = "fold"
     reset_optimizer_on_swap: bool = False

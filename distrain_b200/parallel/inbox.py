@@ -490,6 +490,11 @@ class InBoxCoordinator:
         if sync.store is not None and run.checkpoint_every > 0:
             self.ckpt = CheckpointWriter(sync.store, sync.layout, run.checkpoint_every, run.keep_versions, 0,
                                          sync.n_shards)
+        from ..coordinator.metrics import Metrics, MetricsServer
+        self.metrics = Metrics()
+        self.metrics.registered_nodes = world
+        self.metrics.checkpoint_version = sync.resumed_version
+        self.metrics_server = MetricsServer(self.metrics, port=run.metrics_port) if run.metrics_port >= 0 else None
         for r in range(world):
             self.acc.heartbeat(f"node-{r:02d}")
         self.next_seq = [1] * world
@@ -525,6 +530,13 @@ class InBoxCoordinator:
                 push = DeltaPush.from_dict(body)
                 prev = [c for c in self.acc.state.contributions if c.node_id == push.node_id]
                 ok, reason = self.acc.push(push)
+                with self.metrics._lock:
+                    self.metrics.delta_pushes_total += 1
+                    if ok:
+                        self.metrics.delta_pushes_accepted += 1
+                    else:
+                        self.metrics.delta_pushes_rejected += 1
+                    self.metrics.accumulator_contributions = len(self.acc.state.contributions)
                 if ok:
                     self.payload_of[(push.node_id, push.seq_num)] = body
                     for c in prev:  # replaced by the newer push from the same node
@@ -619,6 +631,7 @@ class InBoxCoordinator:
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
             self.shared.set("version", str(new_version))
             self._maybe_store(new_version, info)
+            self._record(info)
         except _Shutdown:
             self.acc.abort_merge()
             raise
@@ -626,6 +639,7 @@ class InBoxCoordinator:
             # like a failed reference aggregation: count it, drop the contributions of this attempt
             # (their payload slots are released) and keep serving
             self.failed.append(repr(e))
+            self._record(None, failed=True)
             log.warning("merge failed: %r", e)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
@@ -635,6 +649,20 @@ class InBoxCoordinator:
                                             if (c.node_id, c.seq_num) not in {(x.node_id, x.seq_num)
                                                                              for x in snap.contributions}]
             self.acc.abort_merge()
+
+    def _record(self, info: Optional[dict], failed: bool = False):
+        with self.metrics._lock:
+            m = self.metrics
+            m.aggregations_total += 1
+            if failed:
+                m.aggregations_failed += 1
+                return
+            m.checkpoint_version = info["version"]
+            m.last_aggregation_secs = info.get("wall_ms", 0.0) / 1e3
+            m.merge_device_ms = info.get("device_ms", 0.0)
+            m.merge_pulled_bytes = info.get("pulled_bytes", 0)
+            m.accumulator_contributions = len(self.acc.state.contributions)
+            m.active_nodes = len(self.acc.cs.heartbeats)
 
     def _maybe_store(self, version: int, info: dict):
         """Persist a due version from this GPU's slot (before the next merge may overwrite it)."""
@@ -719,11 +747,13 @@ class InBoxCoordinator:
             self.acc.finish_merge(new_version, [c.node_id for c in snap.contributions], tokens)
             self.shared.set("version", str(new_version))
             self._maybe_store(new_version, info)
+            self._record(info)
         except _Shutdown:
             self.acc.abort_merge()
             raise
         except Exception as e:
             self.failed.append(repr(e))
+            self._record(None, failed=True)
             log.warning("merge failed: %r", e)
             for c in snap.contributions:
                 r = int(c.node_id.split("-")[1])
@@ -753,6 +783,8 @@ class InBoxCoordinator:
         self.thread.join(timeout=30)
         if self.ckpt is not None:
             self.ckpt.close()
+        if self.metrics_server is not None:
+            self.metrics_server.stop()
         if self.error is not None:
             raise RuntimeError(f"coordinator thread failed: {self.error!r}") from self.error
 
