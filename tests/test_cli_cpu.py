@@ -16,8 +16,18 @@ def run(args, **kw):
 
 
 @pytest.mark.timeout(900)
+def _free_port():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
 def test_micro_cluster_processes(tmp_path):
-    r = run(["micro-cluster", "--nodes", "2", "--steps", "45", "--port", "18991", "--store", str(tmp_path / "s")])
+    r = run(["micro-cluster", "--nodes", "2", "--steps", "45", "--port", str(_free_port()), "--store",
+             str(tmp_path / "s")])
     assert r.returncode == 0, r.stderr[-3000:]
     out = json.loads(r.stdout.strip().splitlines()[-1])
     for n in out["nodes"]:
