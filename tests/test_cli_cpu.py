@@ -33,7 +33,10 @@ def test_micro_cluster_processes(tmp_path):
     for n in out["nodes"]:
         assert n["steps"] == 45 and n["accepted"] >= 1 and not n["errors"], n
         # uniform-random tokens: the loss sits at the entropy floor ln(32768) = 10.397 (no signal to learn)
-        assert abs(n["last_loss"] - 10.397) < 0.3 and n["version"] >= 1
+        assert abs(n["last_loss"] - 10.397) < 0.3, n
+    # a node that finishes its steps before the first merge is published exits at version 0; the merge
+    # itself must have happened (at least one node swapped, and v1 is in the store)
+    assert max(n["version"] for n in out["nodes"]) >= 1, out["nodes"]
     assert os.path.exists(tmp_path / "s" / "distrain-training" / "checkpoints" / "v1" / "model.safetensors")
 
 
