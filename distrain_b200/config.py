@@ -317,6 +317,11 @@ class RunConfig(_Json):
     keep_versions: int = 10
     resume: bool = False
     metrics_port: int = -1  # in-box coordinator's Prometheus /metrics (-1 = off, 0 = any free port)
+    # inner lr: constant (default) or loss-based, lr_max * clamp(loss_ema / ln(vocab), 0.1, 1)
+    # (reference continuous.rs:586-596, LR_MODE=loss_based)
+    loss_based_lr: bool = False
+    # per-step watchdog: expected seconds per step (0 = off); a step stalled past max(6x, 300 s) is reported
+    watchdog_step_secs: float = 0.0
     swap_mode: str = "rebase"
     ef_on_swap: str = "fold"
     reset_optimizer_on_swap: bool = False

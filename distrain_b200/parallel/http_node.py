@@ -16,6 +16,7 @@ Backends: ``cpu`` (fp32 oracle model + reference AdamW, the micro-test configura
 from __future__ import annotations
 
 import math
+import os
 import queue
 import threading
 import time
@@ -30,6 +31,7 @@ from ..models.params import ParamLayout
 from ..utils.checkpoint import load_safetensors_bytes
 from ..utils.delta_codec import encode_sparse_delta
 from .compression import adaptive_top_k, compress_reference  # noqa: F401 (adaptive_top_k re-exported)
+from ..utils.watchdog import StepWatchdog, watchdog_limit
 
 
 class CpuBackend:
@@ -95,7 +97,8 @@ class HttpNode:
                  h_mini: int = 50, optim: Optional[OptimConfig] = None, compression: Optional[CompressionConfig] = None,
                  device: str = "cpu", node_id: Optional[str] = None, data: Optional[Callable[[], torch.Tensor]] = None,
                  poll_secs: float = 5.0, use_upload_proxy: bool = False, bandwidth_adaptive: bool = False,
-                 heartbeat_every: int = 10):
+                 heartbeat_every: int = 10, loss_based_lr: Optional[bool] = None,
+                 expected_step_secs: Optional[float] = None):
         self.client = CoordinatorClient(coordinator_url)
         self.store = store
         self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
@@ -107,6 +110,9 @@ class HttpNode:
         self.data = data
         self.poll_secs, self.use_proxy, self.bw_adaptive = poll_secs, use_upload_proxy, bandwidth_adaptive
         self.hb_every = heartbeat_every
+        # inner lr mode: constant (default) or loss-based (LR_MODE=loss_based, reference continuous.rs:586-596)
+        self.loss_based_lr = (os.environ.get("LR_MODE") == "loss_based") if loss_based_lr is None else loss_based_lr
+        self.expected_step_secs = expected_step_secs
         self.node_id = node_id
         self.version = -1
         self.seq = 0
@@ -224,8 +230,16 @@ class HttpNode:
         first_round = True
         start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
         loss_ema, loss_count = 0.0, 0
+        ln_vocab = math.log(self.cfg.vocab_size)
+        wd = None
+        if self.expected_step_secs is not None:  # per-step watchdog (reference trainer.rs:1098-1163)
+            wd = StepWatchdog(watchdog_limit(self.expected_step_secs), on_timeout=self._hung)
         try:
             while self.global_step < total_steps:
+                if wd is not None:
+                    wd.beat()
+                if self.stop.is_set():
+                    break
                 try:
                     v, sd = self.new_ckpt.get_nowait()
                 except queue.Empty:
@@ -245,7 +259,12 @@ class HttpNode:
                     start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
                     first_round = False
                 tokens = self.data()
-                lr = self.optim.lr * round_step / warm if (first_round and round_step < warm) else self.optim.lr
+                if first_round and round_step < warm:
+                    lr = self.optim.lr * round_step / warm
+                elif self.loss_based_lr and loss_ema > 0.0:
+                    lr = self.optim.lr * min(max(loss_ema / ln_vocab, 0.1), 1.0)
+                else:
+                    lr = self.optim.lr
                 loss = self.backend.step(tokens, lr)
                 if not math.isfinite(loss):
                     continue  # NaN loss: skip the update (continuous.rs:607-610)
@@ -261,10 +280,16 @@ class HttpNode:
                 if self.global_step % self.hb_every == 0:
                     threading.Thread(target=self._heartbeat, args=(round_step, loss), daemon=True).start()
         finally:
+            if wd is not None:
+                wd.close()
             self.stop.set()
             for t in self._threads:
                 t.join(timeout=120)
         return self.log
+
+    def _hung(self, stalled: float):
+        self.errors.append(f"GpuHung: no step for {stalled:.0f} s")
+        self.stop.set()
 
     def _heartbeat(self, step, loss):
         try:

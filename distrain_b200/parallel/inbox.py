@@ -154,6 +154,9 @@ class InBoxSync:
             need = max(need, 4 * self.n)
         self.slot_bytes = (need + 4095) // 4096 * 4096
         self.last_loss = float(math.log(run.model.vocab_size))  # previous round's mean loss (adaptive top-k)
+        self.loss_ema, self.loss_count = 0.0, 0  # loss-based inner lr (continuous.rs:586-630)
+        self.per_step_losses = False             # True once the e2e loop feeds every step's loss
+        self._lr_set = None
         # payload slots: with two, a node can push again while the coordinator still holds its previous
         # payload; one is enough when pushes are far apart (and saves ~9 bytes per kept entry)
         self.n_slots = max(1, int(run.payload_slots))
@@ -250,13 +253,30 @@ class InBoxSync:
                     lv = None if lv == "-1" else lv
         if lv is not None and int(lv) > self.version:
             self._swap(int(lv))
-        # first-round linear warm-up of the inner lr (reference continuous.rs:588-596)
+        # first-round linear warm-up of the inner lr (reference continuous.rs:588-596), then constant or
+        # loss-based
         o = self.run.optim
         warm = max(int(self.run.push_every * o.warmup_fraction), 2)
         if self.first_round and self.node.round_step < warm:
             self.eng.set_lr(o.lr * self.node.round_step / warm)
         elif self.first_round and self.node.round_step == warm:
             self.eng.set_lr(o.lr)
+            self._lr_set = o.lr
+        elif self.run.loss_based_lr and self.loss_ema > 0.0:
+            lr = o.lr * min(max(self.loss_ema / math.log(self.run.model.vocab_size), 0.1), 1.0)
+            if self._lr_set is None or abs(lr - self._lr_set) > 1e-3 * lr:
+                self.eng.set_lr(lr)
+                self._lr_set = lr
+
+    def observe_loss(self, loss: float):
+        """One step's (or, without per-step losses, one round's mean) training loss: the EMA behind the
+        loss-based inner lr, with the reference's spike rule (continuous.rs:613-630)."""
+        if not math.isfinite(loss):
+            return
+        if self.loss_count > 3 and loss > self.loss_ema * 3.0 and loss > self.loss_ema + 5.0:
+            return
+        self.loss_count += 1
+        self.loss_ema = loss if self.loss_count == 1 else self.loss_ema * 0.9 + loss * 0.1
 
     def after_step(self):
         self.round_tokens += self.run.micro_batch * self.run.seq_len
@@ -360,6 +380,8 @@ class InBoxSync:
             meta.training_loss = float(loss_h[0]) / cnt if cnt > 0 else 0.0
             if cnt > 0:
                 self.last_loss = meta.training_loss
+                if not self.per_step_losses:
+                    self.observe_loss(meta.training_loss)
             raw = kind == "raw"
             st = self.compressor.read_stats(raw=raw, quantized=qb > 0)
             p = self.slots[slot]

@@ -38,6 +38,12 @@ class InBoxNode:
                                   seed=run.seed, init_std=run.init_std, attn_impl=attn_impl, tp=tp,
                                   act_ckpt=run.activation_checkpointing)
         self.enable_push = enable_push
+        self.watchdog = None
+        if run.watchdog_step_secs > 0:
+            from ..utils.watchdog import StepWatchdog, watchdog_limit
+            self.hung = None
+            self.watchdog = StepWatchdog(watchdog_limit(run.watchdog_step_secs),
+                                         on_timeout=lambda s: setattr(self, "hung", s))
         self.step_count = 0
         self.round_step = 0
         self._graph_ready = False
@@ -61,6 +67,8 @@ class InBoxNode:
                 self.sync.before_step()
             self.engine.set_tokens(tokens_dev)
             self.engine.step()
+            if self.watchdog is not None:
+                self.watchdog.beat()
             self.step_count += 1
             self.round_step += 1
             if self.sync is not None:
@@ -88,12 +96,22 @@ class InBoxNode:
                     self.sync.after_step()
             if i > 0:
                 ev[(i - 1) % 2].synchronize()
-                losses.append(float(pinned_loss[(i - 1) % 2][0]))
+                self._observe(float(pinned_loss[(i - 1) % 2][0]), losses)
         ev[(steps - 1) % 2].synchronize()
-        losses.append(float(pinned_loss[(steps - 1) % 2][0]))
+        self._observe(float(pinned_loss[(steps - 1) % 2][0]), losses)
         return losses
 
+    def _observe(self, loss: float, losses: list):
+        losses.append(loss)
+        if self.watchdog is not None:
+            self.watchdog.beat()
+        if self.sync is not None and hasattr(self.sync, "observe_loss"):
+            self.sync.per_step_losses = True
+            self.sync.observe_loss(loss)
+
     def close(self):
+        if self.watchdog is not None:
+            self.watchdog.close()
         if self.sync is not None:
             self.sync.close()
         self.engine.release_graph()

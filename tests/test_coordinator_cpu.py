@@ -164,3 +164,21 @@ def test_http_service_end_to_end(service):
     svc2 = CoordinatorService(CoordinatorConfig(), store, flush_interval=3600)
     assert svc2.acc.state.checkpoint_version == 1
     assert svc2.acc.cs.total_tokens_trained == 3000
+
+
+def test_merge_is_permutation_invariant_without_clipping():
+    """The weighted merge is commutative (paper p.3 sec 3.1): with deltas of similar norm (no 3x clip fires)
+    any arrival order gives the same checkpoint within fp32 rounding. The clip itself uses the running
+    average in arrival order, as in the reference, so an outlier's scale can depend on the order."""
+    import itertools
+    from distrain_b200.parallel.merge import merge_reference
+    g = torch.Generator().manual_seed(0)
+    ck = {"a": torch.randn(300, generator=g), "b": torch.randn(7, 5, generator=g)}
+    deltas = [{k: torch.randn(v.shape, generator=g) * 1e-3 * (1 + 0.1 * i) for k, v in ck.items()} for i in range(4)]
+    weights = [1000.0, 750.0 * 0.9, 500.0 * 0.81, 2000.0]
+    base, _, _ = merge_reference(ck, deltas, weights)
+    for perm in itertools.permutations(range(4)):
+        got, _, info = merge_reference(ck, [deltas[i] for i in perm], [weights[i] for i in perm])
+        assert info["accepted"] == 4
+        for k in ck:
+            torch.testing.assert_close(got[k], base[k], rtol=1e-6, atol=1e-7)

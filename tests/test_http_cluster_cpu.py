@@ -63,3 +63,31 @@ def test_adaptive_push_mode():
     assert adaptive_push_mode(True, 100.0, 400, 3.0, cfg) == ("raw", 1.0, 0)     # 400 B within 10 s at 100 B/s
     kind, k, qb = adaptive_push_mode(True, 10.0, 4000, 3.0, cfg)                  # budget 100 B of 4000 raw
     assert kind == "topk" and qb == 0 and abs(k - 100 / 2000) < 1e-9
+
+
+def test_loss_based_inner_lr_and_watchdog(tmp_path):
+    """One CPU node with LR_MODE=loss_based: after the first-round warm-up every step's lr is
+    lr_max * clamp(loss_ema / ln(vocab), 0.1, 1) of the losses before it; the watchdog stays quiet."""
+    import math
+    cfg = ModelConfig(hidden_dim=32, num_layers=1, num_heads=2, num_kv_heads=1, ffn_hidden_dim=64, vocab_size=256,
+                      max_seq_len=64, rope_theta=10000.0)
+    store = FsStore(str(tmp_path))
+    bootstrap(store, cfg, seed=0)
+    svc = CoordinatorService(CoordinatorConfig(min_contributions=0), store, flush_interval=3600)
+    port = svc.start(host="127.0.0.1", port=0, threads=2)
+    g = torch.Generator().manual_seed(5)
+    n = HttpNode(f"http://127.0.0.1:{port}", store, cfg, batch=2, seq_len=17, h_mini=10, optim=OptimConfig(lr=1e-3),
+                 compression=CompressionConfig(top_k_fraction=0.1), device="cpu", node_id="lr-node",
+                 data=lambda: torch.randint(0, 256, (2, 17), generator=g, dtype=torch.int32), poll_secs=0.2,
+                 loss_based_lr=True, expected_step_secs=1.0)
+    n.register()
+    n.run(25)
+    svc.stop()
+    assert not n.errors, n.errors
+    warm = max(int(10 * 0.2), 2)
+    ema = 0.0
+    for i, row in enumerate(n.log):
+        if i >= warm and ema > 0:
+            want = 1e-3 * min(max(ema / math.log(256), 0.1), 1.0)
+            assert abs(row["lr"] - want) < 1e-12, (i, row["lr"], want)
+        ema = row["loss"] if i == 0 else ema * 0.9 + row["loss"] * 0.1
