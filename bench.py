@@ -115,6 +115,7 @@ def main():
     from distrain_b200.parallel.node import InBoxNode
     from distrain_b200 import ops
     from distrain_b200.utils.tracing import nvtx, setup_logging
+    from distrain_b200.roofline import step_roofline
     setup_logging()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -250,6 +251,8 @@ def main():
                        "device_memory_used_gb_max": round(mem_used / 1e9, 1)},
             "gpu_launches": launches,
             "clocks": clk,
+            # model FLOPs (6N + causal attention [+ recompute]) per GPU against the measured bf16 peaks
+            "roofline": step_roofline(run.model, S, value, world, run.activation_checkpointing),
         }
         if merges:
             dev_ms = sorted(m["device_ms"] for m in merges)

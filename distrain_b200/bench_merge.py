@@ -173,7 +173,11 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         mms = _max_over_ranks(sorted(t_merge)[len(t_merge) // 2], dev)
         sms = _max_over_ranks(sorted(t_single)[len(t_single) // 2], dev)
         if rank == 0:
+            from .roofline import distributed_merge_roofline
+            per_member = sum(c.wire_bytes for c in contribs) / len(contribs)
+            roof = distributed_merge_roofline(n, per_member, world, mms, multicast=bool(mc32))
             results.append({"bench": "compress_merge_broadcast", "model": name, "params": L.num_params(),
+                            "merge_roofline": roof,
                             "n_nodes": world, "top_k": k, "compress_ms": round(cms, 3), "merge_ms": round(mms, 3),
                             "total_ms": round(cms + mms, 3), "merge": f"distributed over {world} GPUs",
                             "single_coordinator_merge_ms": round(sms, 3), "accepted": infos["accepted"],
