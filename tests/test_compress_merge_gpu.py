@@ -347,8 +347,8 @@ def test_inbox_checkpoint_store_and_resume(tmp_path):
     for i in range(40):
         node.train_step_device(batch)
     time.sleep(0.5)
+    node.close()  # joins the coordinator (a merge in flight completes) and flushes the checkpoint writer
     merged = node.sync.coord.version
-    node.close()
     store = FsStore(str(tmp_path))
     v = latest_version(store)
     assert v is not None and v == merged >= 2
