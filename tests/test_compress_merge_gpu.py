@@ -351,7 +351,7 @@ def test_inbox_checkpoint_store_and_resume(tmp_path):
     merged = node.sync.coord.version
     store = FsStore(str(tmp_path))
     v = latest_version(store)
-    assert v is not None and v == merged >= 2
+    assert v is not None and v == merged >= 1  # every merged version is stored (checkpoint_every=1)
     flat = resume_flat(store, node.engine.layout, v)
     assert torch.isfinite(flat).all()
     del node
