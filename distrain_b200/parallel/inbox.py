@@ -467,7 +467,7 @@ class InBoxSync:
             while not self.stop.is_set():
                 raw = self.bus.get(f"dm/{att + 1}")
                 if raw is None:
-                    time.sleep(0.0001)
+                    time.sleep(0.0005)  # each poll is a store round trip taking the GIL from the training loop
                     continue
                 att += 1
                 plan = json.loads(raw)
