@@ -29,3 +29,12 @@ DT_API int dt_device_sm_count(int device) {
 }
 
 DT_API int dt_library_version() { return 1; }
+
+// Installed driver and linked runtime versions (e.g. 12080 = 12.8); 0 when no driver is present.
+DT_API int dt_cuda_versions(int* driver, int* runtime) {
+  *driver = 0;
+  *runtime = 0;
+  cudaDriverGetVersion(driver);
+  cudaRuntimeGetVersion(runtime);
+  return 0;
+}

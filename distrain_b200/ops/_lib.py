@@ -85,8 +85,25 @@ def lib():
             f.restype = c_int
         L.dt_cuda_error_string.restype = ctypes.c_char_p
         L.dt_cuda_error_string.argtypes = [c_int]
+        _check_driver(L)
         _LIB = L
         return L
+
+
+MIN_DRIVER = 12080  # sm_100a code needs a CUDA 12.8+ driver
+
+
+def _check_driver(L):
+    """Fail with a clear message when a GPU is present but its driver cannot run sm_100a code (the role the
+    reference's node/cli/cuda_compat.c plays for its own toolchain)."""
+    if not hasattr(L, "dt_cuda_versions"):
+        return
+    drv, rt = ctypes.c_int(0), ctypes.c_int(0)
+    L.dt_cuda_versions.argtypes = [ctypes.POINTER(c_int), ctypes.POINTER(c_int)]
+    L.dt_cuda_versions(ctypes.byref(drv), ctypes.byref(rt))
+    if 0 < drv.value < MIN_DRIVER:
+        raise KernelError(f"CUDA driver {drv.value // 1000}.{drv.value % 1000 // 10} is older than 12.8, the "
+                          f"minimum for sm_100a (B200) code built with CUDA {rt.value // 1000}.{rt.value % 1000 // 10}")
 
 
 def register(name: str, argtypes, restype=c_int):
