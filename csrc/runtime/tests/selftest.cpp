@@ -7,6 +7,7 @@
 //            plus a malformed request and a body above the limit
 //   codecs   safetensors save -> open -> read back, DTZ1 encode -> decode (int8 and fp32), SipHash /
 //            splitmix64 / shard assignment determinism, zstd round trip when the library is present
+//   sched    push acceptance / merge trigger / round-time rules of the coordinator
 //   loader   three uint16 shard files: synchronous reads across shard boundaries with wrap-around, then
 //            the prefetch thread filling caller buffers while this thread consumes them
 //
@@ -18,6 +19,7 @@
 #include <unistd.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -58,6 +60,10 @@ int dtr_loader_start_prefetch(void*, int32_t**, int);
 int dtr_loader_acquire(void*, int);
 void dtr_loader_release(void*, int);
 void dtr_loader_close(void*);
+int dts_accept_push(long long, long long, int, int, const char* const*, const long long*, const char*, long long,
+                    double, double, double*, char*, int);
+int dts_should_checkpoint(int, const char* const*, int, const char* const*, const double*, double, int);
+double dts_update_round_time(double, long long, long long);
 }
 
 #define CHECK(c)                                                     \
@@ -279,9 +285,32 @@ static void test_loader(const std::string& dir) {
   dtr_loader_close(L);
 }
 
+// ───────────────────────────── scheduler ─────────────────────────────
+static void test_scheduler() {
+  const char* nodes[2] = {"a", "b"};
+  long long seqs[2] = {3, 1};
+  double w = 0;
+  char why[128];
+  CHECK(dts_accept_push(10, 8, 5, 2, nodes, seqs, "c", 1, 1000.0, 0.9, &w, why, sizeof why) == 1);
+  CHECK(std::fabs(w - 1000.0 * 0.81) < 1e-9);
+  CHECK(dts_accept_push(10, 2, 5, 2, nodes, seqs, "c", 1, 1000.0, 0.9, &w, why, sizeof why) == 0);
+  CHECK(std::strncmp(why, "Too stale", 9) == 0);
+  CHECK(dts_accept_push(10, 10, 5, 2, nodes, seqs, "a", 3, 1000.0, 0.9, &w, why, 8) == 0);  // truncated reason
+  CHECK(std::strlen(why) < 8);
+  const char* active[3] = {"a", "b", "c"};
+  double times[3] = {100.0, std::nan(""), 40.0};
+  CHECK(dts_should_checkpoint(0, nodes, 3, active, times, 1000.0, 0) == 0);
+  CHECK(dts_should_checkpoint(2, nodes, 3, active, times, 10.0, 0) == 0);   // patience 120 s not elapsed
+  CHECK(dts_should_checkpoint(2, nodes, 3, active, times, 120.7, 0) == 1);
+  CHECK(dts_should_checkpoint(2, nodes, 2, active, times, 0.0, 0) == 1);    // every active node contributed
+  CHECK(dts_update_round_time(std::nan(""), -1, 100) != dts_update_round_time(std::nan(""), -1, 100));
+  CHECK(dts_update_round_time(std::nan(""), 100, 200) == 100.0);
+}
+
 int main(int argc, char** argv) {
   const std::string dir = argc > 1 ? argv[1] : "/tmp";
   test_codecs();
+  test_scheduler();
   test_loader(dir);
   test_http();
   std::printf("runtime selftest ok\n");

@@ -317,20 +317,31 @@ class CoordinatorPersistentState:
 
 
 # ─────────────────────────────── accumulator logic ───────────────────────────────
+def _cstrs(items):
+    import ctypes
+    arr = (ctypes.c_char_p * max(len(items), 1))(*[x.encode() for x in items])
+    return arr
+
+
 def apply_delta_push(acc: AccumulatorState, push: DeltaPush, staleness_decay: float, max_staleness: int,
                      now: Optional[_dt.datetime] = None):
-    """Returns (accepted, reason). Same rules and messages as the reference (state.rs:63-124)."""
+    """Returns (accepted, reason). The decision (staleness cap, dedup by seq_num, weight
+    tokens * decay^staleness; reference state.rs:63-124) is the runtime library's ``dts_accept_push``."""
+    import ctypes
+    from .utils.native import rt
     now = now or utcnow()
-    staleness = max(acc.checkpoint_version - push.checkpoint_version, 0)
-    if staleness > max_staleness:
-        return False, f"Too stale: {staleness} > {max_staleness}"
-    for c in acc.contributions:
-        if c.node_id == push.node_id and c.seq_num >= push.seq_num:
-            return False, f"Duplicate: existing seq_num {c.seq_num} >= {push.seq_num}"
-    weight = push.tokens_processed * staleness_decay ** staleness
+    nodes = _cstrs([c.node_id for c in acc.contributions])
+    seqs = (ctypes.c_longlong * max(len(acc.contributions), 1))(*[c.seq_num for c in acc.contributions])
+    weight = ctypes.c_double(0.0)
+    reason = ctypes.create_string_buffer(256)
+    ok = rt().dts_accept_push(acc.checkpoint_version, push.checkpoint_version, int(max_staleness),
+                              len(acc.contributions), nodes, seqs, push.node_id.encode(), push.seq_num,
+                              float(push.tokens_processed), float(staleness_decay), ctypes.byref(weight), reason, 256)
+    if not ok:
+        return False, reason.value.decode()
     acc.contributions = [c for c in acc.contributions if c.node_id != push.node_id]
     acc.contributions.append(ContributionMeta(
-        node_id=push.node_id, seq_num=push.seq_num, weight=weight, checkpoint_version=push.checkpoint_version,
+        node_id=push.node_id, seq_num=push.seq_num, weight=weight.value, checkpoint_version=push.checkpoint_version,
         inner_steps=push.inner_steps, tokens_processed=push.tokens_processed, delta_key=push.delta_key,
         received_at=now, training_loss=push.training_loss))
     if acc.first_contribution_at is None:
@@ -341,53 +352,39 @@ def apply_delta_push(acc: AccumulatorState, push: DeltaPush, staleness_decay: fl
 
 def should_checkpoint(acc: AccumulatorState, min_contributions_override: int, cs: CoordinatorPersistentState,
                       now: Optional[_dt.datetime] = None) -> bool:
-    """Patience-based trigger (state.rs:140-225)."""
-    n = len(acc.contributions)
-    if n == 0:
+    """Patience-based trigger (state.rs:140-225), decided by the runtime library's ``dts_should_checkpoint``."""
+    import ctypes
+    from .utils.native import rt
+    if not acc.contributions:
         return False
-    active = len(cs.heartbeats)
-    if min_contributions_override > 0:
-        min_required = min_contributions_override
-    elif active <= 1:
-        min_required = 1
-    else:
-        min_required = max(active // 2, 2)
-    if n < min_required:
-        return False
-    contributing = {c.node_id for c in acc.contributions}
-    active_contributed = sum(1 for nid in cs.heartbeats if nid in contributing)
-    if active > 0 and active_contributed >= active:
-        return True
     now = now or utcnow()
     elapsed = max((now - acc.first_contribution_at).total_seconds(), 0.0) if acc.first_contribution_at else 0.0
-    elapsed = float(int(elapsed))  # chrono num_seconds() truncates
+    active = list(cs.heartbeats)
     times = []
-    for nid, p in cs.node_profiles.items():
-        if nid in cs.heartbeats:
+    for nid in active:
+        p = cs.node_profiles.get(nid)
+        t = None
+        if p is not None:
             t = p.expected_round_time if p.expected_round_time is not None else p.round_time_secs
-            if t is not None:
-                times.append(t)
-    if not times:
-        patience = 60.0
-    else:
-        times.sort()
-        median = times[len(times) // 2]
-        cluster = [t for t in times if t <= median * 3.0]
-        cluster_max = cluster[-1] if cluster else median
-        patience = min(max(cluster_max * 1.2, 30.0), 300.0)
-    return elapsed >= patience
+        times.append(float("nan") if t is None else float(t))
+    tarr = (ctypes.c_double * max(len(times), 1))(*times)
+    return bool(rt().dts_should_checkpoint(len(acc.contributions), _cstrs([c.node_id for c in acc.contributions]),
+                                           len(active), _cstrs(active), tarr, float(elapsed),
+                                           int(min_contributions_override)))
 
 
 def update_round_time(cs: CoordinatorPersistentState, node_id: str, now_secs: Optional[int] = None):
-    """Round-time EMA 0.3/0.7 between consecutive pushes in (10, 600) s (routes.rs:244-263)."""
+    """Round-time EMA 0.3/0.7 between consecutive pushes in (10, 600) s (routes.rs:244-263), computed by the
+    runtime library's ``dts_update_round_time``."""
+    from .utils.native import rt
     now_secs = int(time.time()) if now_secs is None else now_secs
     p = cs.node_profiles.get(node_id)
     if p is None:
         return
-    if p.last_push_time is not None:
-        el = float(max(now_secs - p.last_push_time, 0))
-        if 10.0 < el < 600.0:
-            p.round_time_secs = el if p.round_time_secs is None else p.round_time_secs * 0.3 + el * 0.7
+    prev = float("nan") if p.round_time_secs is None else float(p.round_time_secs)
+    last = -1 if p.last_push_time is None else int(p.last_push_time)
+    new = rt().dts_update_round_time(prev, last, int(now_secs))
+    p.round_time_secs = None if math.isnan(new) else new
     p.last_push_time = now_secs
 
 

@@ -52,6 +52,10 @@ _SIGS = {
     "dtr_delta_config": ([c_void], c_char_p),
     "dtr_dtz_encode": ([c_ll, c_ll, c_void, c_void, c_void, c_void, c_int, c_int], c_void),
     "dtr_dtz_decode_dense": ([c_void, c_ll], c_void),
+    "dts_accept_push": ([c_ll, c_ll, c_int, c_int, c_void, c_void, c_char_p, c_ll, ctypes.c_double, ctypes.c_double,
+                         c_void, c_void, c_int], c_int),
+    "dts_should_checkpoint": ([c_int, c_void, c_int, c_void, c_void, ctypes.c_double, c_int], c_int),
+    "dts_update_round_time": ([ctypes.c_double, c_ll, c_ll], ctypes.c_double),
 }
 
 
