@@ -148,6 +148,15 @@ def main():
                             rows=run.micro_batch * (run.seq_len - 1), hidden=run.model.hidden_dim, device=dev)
         dp_group = dp_groups[rank % tp_size]
     node_rank, n_nodes = rank // tp_size, world // tp_size
+    if rank == 0:
+        from distrain_b200.memory import check_fits
+        fits, est = check_fits(run, torch.cuda.get_device_properties(dev).total_memory, n_nodes,
+                               protocol=not args.no_push)
+        if not fits:
+            print(f"warning: {run.name} needs ~{est['total'] / 1e9:.0f} GB per rank (engine {est['engine'] / 1e9:.0f}, "
+                  f"activations {est['activations'] / 1e9:.0f}, protocol {est['protocol'] / 1e9:.0f}); this GPU has "
+                  f"{torch.cuda.get_device_properties(dev).total_memory / 1e9:.0f} GB - use tensor parallelism "
+                  f"(--tp) or fewer payload slots", file=sys.stderr)
     # with tensor parallelism every rank runs the protocol for its shard over its dp group
     node = InBoxNode(run, rank=node_rank, world=n_nodes, device=dev,
                      enable_push=not args.no_push and not nccl_arm, tp=tp,

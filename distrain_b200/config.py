@@ -344,8 +344,9 @@ def bench_config(name: str) -> RunConfig:
         return RunConfig(name="large", model=preset("large"), seq_len=2048, micro_batch=4, push_every=100,
                          tp=2, activation_checkpointing=True, payload_slots=1)
     if name in ("medium", "7b"):
+        # 5.8 B parameters: with the protocol's buffers one GPU would need ~192 GB, so two GPUs per node
         return RunConfig(name="medium", model=preset("medium"), seq_len=2048, micro_batch=4, push_every=100,
-                         activation_checkpointing=True)
+                         tp=2, activation_checkpointing=True, payload_slots=1)
     raise KeyError(name)
 
 
