@@ -267,9 +267,8 @@ def main():
             dev_ms = sorted(m["device_ms"] for m in merges)
             out["merge"] = {"count": len(merges), "node_version": versions,
                             "ms_median": round(dev_ms[len(dev_ms) // 2], 3),
-                            "timing": ("CUDA events on the merge stream of rank 0, while the nodes train: from "
-                                       "the start of its slice to its check that every slice landed "
-                                       "(control-bus round trips included)") if not nccl_arm else
+                            "timing": ("CUDA events on rank 0's merge stream while the nodes train, host planning "
+                                       "and control-bus round trips between its kernels included") if not nccl_arm else
                                       "CUDA events around the NCCL all-reduce + apply on the training stream",
                             "contributions_last": merges[-1]["n_contrib"],
                             "pulled_bytes_last": merges[-1]["pulled_bytes"],
