@@ -38,6 +38,8 @@ def _parse():
     ap.add_argument("--impl", default="dt", choices=["dt", "reference"])
     ap.add_argument("--push-every", type=int, default=None)
     ap.add_argument("--tp", type=int, default=None, help="tensor-parallel size per node (default: the preset's)")
+    ap.add_argument("--clocks-csv", default=None,
+                    help="keep the nvidia-smi clock samples of the timed region in this CSV (default: a temp file)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-push", action="store_true", help="train only (no compression / merge)")
     ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
@@ -183,9 +185,16 @@ def main():
     torch.cuda.synchronize()
     barrier()
 
-    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out", f"bench_clocks_r{rank}.csv")) if rank == 0 else None
-    if clocks:
-        os.makedirs(os.path.dirname(clocks.path), exist_ok=True)
+    clocks = None
+    if rank == 0:
+        if args.clocks_csv:
+            path = args.clocks_csv
+            os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+        else:
+            import tempfile
+            fd, path = tempfile.mkstemp(prefix="dt_clocks_", suffix=".csv")
+            os.close(fd)
+        clocks = ClockSampler(path)
         clocks.start()
         time.sleep(0.5)
 
