@@ -209,6 +209,55 @@ def merge_cases(iters):
     return out
 
 
+def dm_cases(iters):
+    """The distributed merge's kernels on one GPU (one node owning the whole range, so no broadcast): per
+    merge, the range search over 8 payloads of the tiny model and the weighted dequant scatter-add into the
+    checkpoint. Plans come from the reported statistics (no device pass over the payloads)."""
+    from distrain_b200.config import preset, CompressionConfig
+    from distrain_b200.models.params import ParamLayout
+    from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
+    from distrain_b200.parallel.merge import DeviceMerger, DistributedMerger, Contribution
+    out = []
+    L = ParamLayout(preset("tiny"))
+    dev = torch.device("cuda")
+    for k in (0.01, 0.10, 0.99):
+        if not want(f"dm_{round(k * 100)}"):
+            continue
+        comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=k, int8_block=256))
+        master = torch.randn(L.total, device=dev) * 1e-2
+        pays, contribs, stats = [], [], []
+        for i in range(8):
+            comp.reset(master)
+            comp.begin(master - torch.randn_like(master) * 1e-4)
+            p = DevicePayload.allocate(comp.capacity, 256, dev)
+            comp.finish(payload=p)
+            torch.cuda.synchronize()
+            st = comp.read_stats()
+            cnt = st["num_params_kept"]
+            pays.append(p)
+            stats.append(st["wire"])
+            contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                         win_ptr=p.win.data_ptr(), scales_ptr=p.scales.data_ptr(), count=cnt,
+                                         block=256, dense=False, weight=1000.0 * (i + 1),
+                                         wire_bytes=p.wire_bytes(cnt)))
+        theta = master.clone()
+        ctl = torch.zeros(DistributedMerger.CTL_BYTES, dtype=torch.uint8, device=dev)
+        dm = DistributedMerger(0, 1, L.total, dev, theta, [theta.data_ptr()], 0, ctl, [ctl.data_ptr()])
+        coefs, _ = DeviceMerger.plan(contribs, stats)
+        torch.cuda.synchronize()
+
+        def run():
+            dm.apply(contribs, coefs, 1.0)
+            dm.stream.synchronize()
+        ms = time_it(run, iters, warmup=2)
+        wire = sum(c.wire_bytes for c in contribs)
+        out.append({"kernel": "dm_range_apply", "case": f"8 x tiny {L.num_params() / 1e6:.0f}M top-k {k:.0%}",
+                    "ms": round(ms, 3), "payload_mb": round(wire / 1e6, 1),
+                    "payload_gbs": round(wire / ms / 1e6, 1)})
+        del comp, dm, pays, theta
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="all")
@@ -232,6 +281,8 @@ def main():
         res += compress_cases(a.iters)
     if "all" in sel or "merge" in sel:
         res += merge_cases(a.iters)
+    if "all" in sel or "dm" in sel:
+        res += dm_cases(a.iters)
     from distrain_b200 import ops
     code, site = ops.device_error()
     for r in res:
