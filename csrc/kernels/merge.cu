@@ -387,6 +387,121 @@ __global__ void dm_broadcast_kernel(const float* __restrict__ theta, long long a
   last_block_release(blocks_local, done_dst);
 }
 
+// ───── fused tile merge: atomic-free apply + broadcast of one slice (alternative to dm_apply_* + dm_broadcast) ─────
+// The slice [a, b) is cut into tiles of DM_TILE elements. dm_tile_bounds_kernel records, for every member
+// payload, the position where each tile's entries start (bounds[c * (ntiles + 1) + t]); dm_tile_apply_kernel
+// then gives every tile to one CTA, which sums all members' entries of the tile into shared memory (shared
+// atomics only), adds the sum to the checkpoint once and writes the tile to every node. Every index is
+// range-checked, so malformed bounds can only skip work.
+constexpr int DM_TILE = 8192;
+
+__device__ __forceinline__ long long dm_tile_of(const Contrib& C, const Windows& W, long long p, long long a) {
+  return (W.flat(__ldg(C.idx + p), p) - a) / DM_TILE;
+}
+
+__global__ void dm_tile_bounds_kernel(const __grid_constant__ ContribTable cs, const long long* __restrict__ ranges,
+                                      long long a, long long ntiles, long long* __restrict__ bounds) {
+  const int c = blockIdx.y;
+  const Contrib& C = cs.c[c];
+  long long* bc = bounds + (long long)c * (ntiles + 1);
+  const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (C.dense) return;  // dense members are read directly by tile
+  if (lo >= hi) {       // no entries in this slice: every tile starts (and ends) at lo
+    for (long long t = tid; t <= ntiles; t += stride) bc[t] = lo;
+    return;
+  }
+  Windows W;
+  W.load(C.win);
+  for (long long p = lo + tid; p < hi; p += stride) {
+    long long tp = dm_tile_of(C, W, p, a);
+    tp = tp < 0 ? 0 : (tp > ntiles - 1 ? ntiles - 1 : tp);
+    long long tq = -1;
+    if (p > lo) {
+      tq = dm_tile_of(C, W, p - 1, a);
+      tq = tq < 0 ? 0 : (tq > ntiles - 1 ? ntiles - 1 : tq);
+    }
+    for (long long t = tq + 1; t <= tp; ++t) bc[t] = p;  // tiles starting at this entry
+    if (p == hi - 1)
+      for (long long t = tp + 1; t <= ntiles; ++t) bc[t] = hi;  // tiles after the last entry
+  }
+}
+
+__global__ void __launch_bounds__(512) dm_tile_apply_kernel(const __grid_constant__ ContribTable cs, int n,
+                                                            const long long* __restrict__ ranges,
+                                                            const long long* __restrict__ bounds, long long a,
+                                                            long long b, long long ntiles,
+                                                            const float* __restrict__ coefs, float* theta, float* mc32,
+                                                            Dests d, unsigned long long* done_dst,
+                                                            unsigned* blocks_local) {
+  extern __shared__ float tile[];  // DM_TILE floats
+  __shared__ float shc[MAX_CONTRIB];
+  if (threadIdx.x < n) shc[threadIdx.x] = coefs[threadIdx.x];
+  __syncthreads();
+  float4* tile4 = reinterpret_cast<float4*>(tile);
+  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const long long t0 = a + t * DM_TILE;
+    const long long len4 = ((b - t0) < DM_TILE ? (b - t0) : DM_TILE) / 4;  // a, b, DM_TILE multiples of 4
+    const long long len = 4 * len4;
+    // dense members first: each thread owns its float4 of the tile, no atomics
+    for (long long i4 = threadIdx.x; i4 < DM_TILE / 4; i4 += blockDim.x) {
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < n && i4 < len4; ++c) {
+        const Contrib& C = cs.c[c];
+        const float k = shc[c];
+        if (!C.dense || k == 0.f || t0 + 4 * i4 >= C.count) continue;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(C.val + t0) + i4);
+        s.x += k * v.x;
+        s.y += k * v.y;
+        s.z += k * v.z;
+        s.w += k * v.w;
+      }
+      tile4[i4] = s;
+    }
+    __syncthreads();
+    for (int c = 0; c < n; ++c) {
+      const Contrib& C = cs.c[c];
+      const float k = shc[c];
+      if (C.dense || k == 0.f) continue;
+      const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
+      const long long* bc = bounds + (long long)c * (ntiles + 1);
+      long long p0 = bc[t], p1 = bc[t + 1];
+      p0 = p0 < lo ? lo : p0;
+      p1 = p1 > hi ? hi : p1;
+      Windows W;
+      W.load(C.win);
+      for (long long q = p0 + threadIdx.x; q < p1; q += (long long)blockDim.x * MUNR) {
+        long long j[MUNR];
+        float v[MUNR];
+#pragma unroll
+        for (int u = 0; u < MUNR; ++u) {  // all loads in flight before the first shared atomic
+          const long long p = q + u * (long long)blockDim.x;
+          j[u] = p < p1 ? W.flat(__ldg(C.idx + p), p) - t0 : -1;
+          v[u] = p < p1 ? contrib_value(C, p) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < MUNR; ++u)
+          if (j[u] >= 0 && j[u] < len) atomicAdd(&tile[j[u]], k * v[u]);
+      }
+    }
+    __syncthreads();
+    for (long long i4 = threadIdx.x; i4 < len4; i4 += blockDim.x) {
+      const long long g4 = t0 / 4 + i4;
+      float4 v = reinterpret_cast<float4*>(theta)[g4];
+      const float4 u = tile4[i4];
+      v.x += u.x;
+      v.y += u.y;
+      v.z += u.z;
+      v.w += u.w;
+      reinterpret_cast<float4*>(theta)[g4] = v;
+      store_dests(mc32, d, theta, g4, v);
+    }
+    __syncthreads();
+  }
+  last_block_release(blocks_local, done_dst);
+}
+
 // Node side of a checkpoint swap: master <- stage32, p16 <- stage16 (or cast), snapshot <- master.
 // Checkpoint swap. rebase == 0: master = snap = staged fp32, p16 = staged bf16 (or its cast).
 // rebase == 1: the steps trained since the last push are carried onto the new checkpoint:
@@ -539,5 +654,34 @@ DT_API int dt_dm_broadcast(const float* theta, long long a, long long b, void* m
   dm_broadcast_kernel<<<grid_cap(n4 / MUNR + 1, 256, 148 * 4), 256, 0, st>>>(theta, a / 4, b / 4,
                                                                              reinterpret_cast<float*>(mc32), d,
                                                                              done_dst, blocks_local);
+  return (int)cudaGetLastError();
+}
+
+// Fused alternative to dt_dm_apply + dt_dm_broadcast for a slice [a, b) (multiples of 4): tile bounds per
+// sparse member into `bounds` (n * (ceil((b - a) / 8192) + 1) int64, device), then one CTA per tile.
+DT_API long long dt_dm_tile_elems() { return DM_TILE; }
+
+DT_API int dt_dm_fused(const void* contribs, int n, long long max_len, const long long* ranges, long long* bounds,
+                       long long a, long long b, const float* coefs, float* theta, void* mc32, void* const* stage32,
+                       int n_dest, unsigned long long* done_dst, unsigned* blocks_local, cudaStream_t st) {
+  if (n <= 0 || n > MAX_CONTRIB) return -13;
+  if ((a | b) & 3) return -10;
+  Dests d;
+  if (int e = make_dests(d, mc32, stage32, n_dest)) return e;
+  ContribTable tab;
+  memcpy(tab.c, contribs, sizeof(Contrib) * n);
+  const long long ntiles = (b - a + DM_TILE - 1) / DM_TILE;
+  if (ntiles > 0) {
+    dim3 g1(grid_cap(max_len / 4 + 1, 256, 148 * 4), n);
+    dm_tile_bounds_kernel<<<g1, 256, 0, st>>>(tab, ranges, a, ntiles, bounds);
+    const size_t smem = sizeof(float) * DM_TILE;  // 32 KB: under the default dynamic limit
+    const int grid = (int)(ntiles < 148 * 4 ? ntiles : 148 * 4);
+    dm_tile_apply_kernel<<<grid, 512, smem, st>>>(tab, n, ranges, bounds, a, b, ntiles, coefs, theta,
+                                                  reinterpret_cast<float*>(mc32), d, done_dst, blocks_local);
+  } else {
+    // an empty slice still reports completion
+    dm_broadcast_kernel<<<1, 32, 0, st>>>(theta, a / 4, b / 4, reinterpret_cast<float*>(mc32), d, done_dst,
+                                          blocks_local);
+  }
   return (int)cudaGetLastError();
 }

@@ -212,7 +212,8 @@ def merge_cases(iters):
 def dm_cases(iters):
     """The distributed merge's kernels on one GPU (one node owning the whole range, so no broadcast): per
     merge, the range search over 8 payloads of the tiny model and the weighted dequant scatter-add into the
-    checkpoint. Plans come from the reported statistics (no device pass over the payloads)."""
+    checkpoint (global atomics), or the fused tile pass that sums the payloads per 8192-element tile in
+    shared memory and updates the checkpoint once. Plans come from the reported statistics (no device pass over the payloads)."""
     from distrain_b200.config import preset, CompressionConfig
     from distrain_b200.models.params import ParamLayout
     from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
@@ -249,11 +250,14 @@ def dm_cases(iters):
         def run():
             dm.apply(contribs, coefs, 1.0)
             dm.stream.synchronize()
-        ms = time_it(run, iters, warmup=2)
         wire = sum(c.wire_bytes for c in contribs)
-        out.append({"kernel": "dm_range_apply", "case": f"8 x tiny {L.num_params() / 1e6:.0f}M top-k {k:.0%}",
-                    "ms": round(ms, 3), "payload_mb": round(wire / 1e6, 1),
-                    "payload_gbs": round(wire / ms / 1e6, 1)})
+        for fused in (False, True):  # scatter-add into the checkpoint, or the tile-sum pass (dt_dm_fused)
+            dm.fused = fused
+            ms = time_it(run, iters, warmup=2)
+            out.append({"kernel": "dm_fused_tiles" if fused else "dm_range_apply",
+                        "case": f"8 x tiny {L.num_params() / 1e6:.0f}M top-k {k:.0%}",
+                        "ms": round(ms, 3), "payload_mb": round(wire / 1e6, 1),
+                        "payload_gbs": round(wire / ms / 1e6, 1)})
         del comp, dm, pays, theta
     return out
 

@@ -60,7 +60,8 @@ class KernelError(RuntimeError):
 # Kernel launches issued through this library (incremented per launcher call by the number of
 # kernels that launcher starts); a CUDA-graph replay adds the count recorded at capture.
 LAUNCHES = [0]
-_KERNELS_PER_CALL = {"dt_adamw_step": 3, "dt_adamw_apply": 2, "dt_seg_sqnorm": 1, "dt_get_error": 0, "dt_clear_error": 0}
+_KERNELS_PER_CALL = {"dt_adamw_step": 3, "dt_adamw_apply": 2, "dt_seg_sqnorm": 1, "dt_get_error": 0, "dt_clear_error": 0,
+                    "dt_dm_fused": 2}
 
 
 def lib():

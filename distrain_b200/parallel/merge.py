@@ -10,6 +10,7 @@ outer (Nesterov) apply, reference coordinator/src/aggregation.rs:154-472.
 from __future__ import annotations
 
 import ctypes
+import os
 import math
 import struct
 from dataclasses import dataclass
@@ -268,7 +269,8 @@ class DistributedMerger:
     OFF_COEF, OFF_DONE, OFF_BBC, OFF_RANGES = 2048, 2624, 2816, 4096
 
     def __init__(self, rank: int, world: int, n: int, device, theta: torch.Tensor, stage_ptrs: Sequence[int],
-                 stage_mc: int, ctl: torch.Tensor, ctl_ptrs: Sequence[int], stream: Optional[torch.cuda.Stream] = None):
+                 stage_mc: int, ctl: torch.Tensor, ctl_ptrs: Sequence[int], stream: Optional[torch.cuda.Stream] = None,
+                 fused: Optional[bool] = None):
         from ..ops import _lib
         from ..ops._lib import c_int, c_void, c_ll
         self.L = _lib.lib()
@@ -277,6 +279,9 @@ class DistributedMerger:
         _lib.register("dt_dm_wait", [c_void, u64, c_int, u64, c_void])
         _lib.register("dt_dm_apply", [c_void, c_int, c_ll, c_void, c_ll, c_ll, c_void, c_void, c_int, c_int, c_void])
         _lib.register("dt_dm_broadcast", [c_void, c_ll, c_ll, c_void, c_void, c_int, c_void, c_void, c_void])
+        _lib.register("dt_dm_fused", [c_void, c_int, c_ll, c_void, c_void, c_ll, c_ll, c_void, c_void, c_void, c_void,
+                                      c_int, c_void, c_void, c_void])
+        _lib.register("dt_dm_tile_elems", [], ctypes.c_longlong)
         assert world <= 8 and ctl.numel() >= self.CTL_BYTES
         self.rank, self.world, self.n = rank, world, n
         self.device = torch.device(device)
@@ -289,6 +294,11 @@ class DistributedMerger:
         self.coef_host = torch.zeros(64, dtype=torch.float32).pin_memory()
         self.coef_dev = ctl[self.OFF_COEF:self.OFF_COEF + 256].view(torch.float32)
         self._keep = None
+        # fused tile path (dt_dm_fused): one pass over the slice that sums every member in shared memory and
+        # writes each tile once, locally and to every node; DT_DM_FUSED=1 selects it by default
+        self.fused = (os.environ.get("DT_DM_FUSED", "0") == "1") if fused is None else bool(fused)
+        self.tile = int(self.L.dt_dm_tile_elems())
+        self.bounds = torch.empty(0, dtype=torch.int64, device=self.device)
 
     def range_of(self, r: int):
         n4 = self.n // 4
@@ -320,9 +330,18 @@ class DistributedMerger:
             ranges = self.base + self.OFF_RANGES
             if has_sparse:
                 check(self.L.dt_dm_range(buf, n, self.a, self.b, ranges, sp), "dt_dm_range")
+            dests = (ctypes.c_void_p * self.world)(*self.stage_ptrs)
+            if self.fused:
+                need = n * ((self.b - self.a + self.tile - 1) // self.tile + 1)
+                if self.bounds.numel() < need:
+                    self.bounds = torch.empty(need, dtype=torch.int64, device=self.device)
+                check(self.L.dt_dm_fused(buf, n, max_len, ranges, self.bounds.data_ptr(), self.a, self.b,
+                                         self.coef_dev.data_ptr(), self.theta.data_ptr(), self.stage_mc or None, dests,
+                                         self.world, self.ctl_ptrs[0] + self.OFF_DONE, self.base + self.OFF_BBC, sp),
+                      "dt_dm_fused")
+                return
             check(self.L.dt_dm_apply(buf, n, max_len, ranges, self.a, self.b, self.coef_dev.data_ptr(),
                                      self.theta.data_ptr(), int(has_dense), int(has_sparse), sp), "dt_dm_apply")
-            dests = (ctypes.c_void_p * self.world)(*self.stage_ptrs)
             check(self.L.dt_dm_broadcast(self.theta.data_ptr(), self.a, self.b, self.stage_mc or None, dests,
                                          self.world, self.ctl_ptrs[0] + self.OFF_DONE, self.base + self.OFF_BBC, sp),
                   "dt_dm_broadcast")

@@ -266,6 +266,72 @@ def test_distributed_merger_single_node_matches_reference():
         assert info["accepted"] == 2
 
 
+@pytest.mark.parametrize("fused", [False, True])
+def test_distributed_merger_slices_on_one_gpu(fused):
+    """Three slices of one checkpoint merged one after another on one GPU (a three-node merge whose nodes
+    share one staging slot), two quantised sparse members and one raw dense member, against the fp32
+    reference: every slice boundary and (fused path) every tile boundary is crossed. The completion
+    counter is read only after all three slices finished."""
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor, dequantize_int8
+    from distrain_b200.parallel.merge import DeviceMerger, DistributedMerger, Contribution, merge_reference
+    L = _layout()
+    dev = torch.device("cuda")
+    torch.manual_seed(5)
+    theta0 = torch.randn(L.total, device=dev) * 0.02
+    cfg = CompressionConfig(top_k_fraction=0.3, quantize_int8=True, int8_block=256)
+    contribs, dense_deltas, weights, keep, stats = [], [], [], [], []
+    for i, sc in enumerate([1.0, 2.0, 1.5]):
+        comp = DeviceCompressor(L, dev, cfg)
+        d = torch.randn(L.total, device=dev) * 1e-3 * sc
+        comp.snap.copy_(theta0)
+        comp.begin(theta0 - d)
+        w = 1000.0 / (i + 1)
+        weights.append(w)
+        dense = torch.zeros(L.total)
+        if i < 2:
+            comp.finish()
+            torch.cuda.synchronize()
+            st = comp.read_stats()
+            K = st["num_params_kept"]
+            p = comp.payload
+            contribs.append(Contribution(idx_ptr=p.idx.data_ptr(), q_ptr=p.q.data_ptr(), val_ptr=p.val.data_ptr(),
+                                         scales_ptr=p.scales.data_ptr(), win_ptr=p.win.data_ptr(), count=K,
+                                         block=256, dense=False, weight=w))
+            dense[p.global_indices(K).cpu()] = dequantize_int8(p.q[:K].cpu(), p.scales[:(K + 255) // 256].cpu(), 256)
+        else:
+            out = torch.empty(L.total, device=dev)
+            comp.finish_raw(out)
+            torch.cuda.synchronize()
+            st = comp.read_stats(raw=True)
+            keep.append(out)
+            contribs.append(Contribution(idx_ptr=0, q_ptr=0, val_ptr=out.data_ptr(), scales_ptr=0, win_ptr=0,
+                                         count=L.total, block=1, dense=True, weight=w))
+            dense = out.cpu()
+        stats.append(st["wire"])
+        keep.append(comp)
+        dense_deltas.append({e.name: dense[e.offset:e.offset + e.numel] for e in L.entries})
+    theta = theta0.clone()
+    W = 3
+    ctls = [torch.zeros(DistributedMerger.CTL_BYTES, dtype=torch.uint8, device=dev) for _ in range(W)]
+    dms = [DistributedMerger(r, W, L.total, dev, theta, [theta.data_ptr()] * W, 0, ctls[r],
+                             [c.data_ptr() for c in ctls], fused=fused) for r in range(W)]
+    assert dms[0].b - dms[0].a > dms[0].tile  # every slice spans several tiles
+    torch.cuda.synchronize()
+    ck = {e.name: theta0[e.offset:e.offset + e.numel].cpu() for e in L.entries}
+    for att in (1, 2):
+        coefs, info = DeviceMerger.plan(contribs, stats)
+        for dm in dms:
+            dm.apply(contribs, coefs, 1.0)
+            dm.check()
+        dms[0].finish(att)
+        ck, _, rinfo = merge_reference(ck, dense_deltas, weights, outer_lr=1.0, outer_momentum=0.0)
+        got = theta.cpu()
+        for e in L.entries:
+            assert torch.allclose(got[e.offset:e.offset + e.numel], ck[e.name], atol=1e-7, rtol=1e-5), (att, e.name)
+        assert info["accepted"] == 3
+
+
 def test_raw_push_kernel():
     """Raw push: the dense delta + error feedback leaves as fp32, error feedback cleared, statistics of
     the whole delta."""
