@@ -388,7 +388,7 @@ __global__ void dm_broadcast_kernel(const float* __restrict__ theta, long long a
 }
 
 // ───── fused tile merge: atomic-free apply + broadcast of one slice (alternative to dm_apply_* + dm_broadcast) ─────
-// The slice [a, b) is cut into tiles of DM_TILE elements. dm_tile_bounds_kernel records, for every sparse
+// The slice [a, b) is cut into tiles of DM_TILE elements. dm_tile_bounds_kernel finds, for every sparse
 // member payload, the position where each tile's entries start (bounds[c * (ntiles + 1) + t]).
 // dm_tile_apply_kernel then gives every tile to one CTA: the CTA loads its tile of the checkpoint and of the
 // dense members into registers, sums the entries of all sparse members that fall in the tile into shared
@@ -400,36 +400,28 @@ constexpr int DM_TILE_THREADS = 256;
 constexpr int DM_TILE_R = DM_TILE / 4 / DM_TILE_THREADS;  // float4s of the tile per thread
 constexpr int DM_UNR = 8;
 
-__device__ __forceinline__ long long dm_tile_of(const Contrib& C, const Windows& W, long long p, long long a) {
-  return (W.flat(__ldg(C.idx + p), p) - a) / DM_TILE;
-}
-
+// bounds[c * (ntiles + 1) + t] = the first position of member c's slice range [lo, hi) whose flat index is at
+// least a + t * DM_TILE (hi for t = ntiles): one binary search per (member, tile boundary), all independent.
 __global__ void dm_tile_bounds_kernel(const __grid_constant__ ContribTable cs, const long long* __restrict__ ranges,
                                       long long a, long long ntiles, long long* __restrict__ bounds) {
   const int c = blockIdx.y;
   const Contrib& C = cs.c[c];
-  long long* bc = bounds + (long long)c * (ntiles + 1);
-  const long long lo = ranges[2 * c], hi = ranges[2 * c + 1];
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (C.dense) return;  // dense members are read directly by tile
-  if (lo >= hi) {       // no entries in this slice: every tile starts (and ends) at lo
-    for (long long t = tid; t <= ntiles; t += stride) bc[t] = lo;
-    return;
-  }
+  long long* bc = bounds + (long long)c * (ntiles + 1);
+  const long long lo0 = ranges[2 * c], hi0 = ranges[2 * c + 1];
   Windows W;
   W.load(C.win);
-  for (long long p = lo + tid; p < hi; p += stride) {
-    long long tp = dm_tile_of(C, W, p, a);
-    tp = tp < 0 ? 0 : (tp > ntiles - 1 ? ntiles - 1 : tp);
-    long long tq = -1;
-    if (p > lo) {
-      tq = dm_tile_of(C, W, p - 1, a);
-      tq = tq < 0 ? 0 : (tq > ntiles - 1 ? ntiles - 1 : tq);
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t <= ntiles;
+       t += (long long)gridDim.x * blockDim.x) {
+    const long long key = a + t * DM_TILE;
+    long long lo = lo0, hi = hi0 > lo0 ? hi0 : lo0;
+    if (t == ntiles) lo = hi;
+    while (lo < hi) {
+      const long long mid = lo + ((hi - lo) >> 1);
+      if (W.flat(__ldg(C.idx + mid), mid) < key) lo = mid + 1;
+      else hi = mid;
     }
-    for (long long t = tq + 1; t <= tp; ++t) bc[t] = p;  // tiles starting at this entry
-    if (p == hi - 1)
-      for (long long t = tp + 1; t <= ntiles; ++t) bc[t] = hi;  // tiles after the last entry
+    bc[t] = lo;
   }
 }
 
@@ -724,8 +716,8 @@ DT_API int dt_dm_broadcast(const float* theta, long long a, long long b, void* m
 // per tile.
 DT_API long long dt_dm_tile_elems() { return DM_TILE; }
 
-DT_API int dt_dm_fused(const void* contribs, int n, long long max_len, const long long* ranges, long long* bounds,
-                       long long a, long long b, const float* coefs, float* theta, void* mc32, void* const* stage32,
+DT_API int dt_dm_fused(const void* contribs, int n, const long long* ranges, long long* bounds, long long a,
+                       long long b, const float* coefs, float* theta, void* mc32, void* const* stage32,
                        int n_dest, unsigned long long* done_dst, unsigned* blocks_local, cudaStream_t st) {
   if (n <= 0 || n > MAX_CONTRIB) return -13;
   if ((a | b) & 3) return -10;
@@ -735,7 +727,7 @@ DT_API int dt_dm_fused(const void* contribs, int n, long long max_len, const lon
   memcpy(tab.c, contribs, sizeof(Contrib) * n);
   const long long ntiles = (b - a + DM_TILE - 1) / DM_TILE;
   if (ntiles > 0) {
-    dim3 g1(grid_cap(max_len / 4 + 1, 256, 148 * 4), n);
+    dim3 g1(grid_cap(ntiles + 1, 256, 148 * 8), n);
     dm_tile_bounds_kernel<<<g1, 256, 0, st>>>(tab, ranges, a, ntiles, bounds);
     dm_tile_apply_kernel<<<(unsigned)ntiles, DM_TILE_THREADS, 0, st>>>(tab, n, ranges, bounds, a, b, ntiles, coefs,
                                                                      theta, reinterpret_cast<float*>(mc32), d,

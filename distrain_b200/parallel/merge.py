@@ -279,8 +279,8 @@ class DistributedMerger:
         _lib.register("dt_dm_wait", [c_void, u64, c_int, u64, c_void])
         _lib.register("dt_dm_apply", [c_void, c_int, c_ll, c_void, c_ll, c_ll, c_void, c_void, c_int, c_int, c_void])
         _lib.register("dt_dm_broadcast", [c_void, c_ll, c_ll, c_void, c_void, c_int, c_void, c_void, c_void])
-        _lib.register("dt_dm_fused", [c_void, c_int, c_ll, c_void, c_void, c_ll, c_ll, c_void, c_void, c_void, c_void,
-                                      c_int, c_void, c_void, c_void])
+        _lib.register("dt_dm_fused", [c_void, c_int, c_void, c_void, c_ll, c_ll, c_void, c_void, c_void, c_void, c_int,
+                                      c_void, c_void, c_void])
         _lib.register("dt_dm_tile_elems", [], ctypes.c_longlong)
         assert world <= 8 and ctl.numel() >= self.CTL_BYTES
         self.rank, self.world, self.n = rank, world, n
@@ -335,7 +335,7 @@ class DistributedMerger:
                 need = n * ((self.b - self.a + self.tile - 1) // self.tile + 1)
                 if self.bounds.numel() < need:
                     self.bounds = torch.empty(need, dtype=torch.int64, device=self.device)
-                check(self.L.dt_dm_fused(buf, n, max_len, ranges, self.bounds.data_ptr(), self.a, self.b,
+                check(self.L.dt_dm_fused(buf, n, ranges, self.bounds.data_ptr(), self.a, self.b,
                                          self.coef_dev.data_ptr(), self.theta.data_ptr(), self.stage_mc or None, dests,
                                          self.world, self.ctl_ptrs[0] + self.OFF_DONE, self.base + self.OFF_BBC, sp),
                       "dt_dm_fused")
