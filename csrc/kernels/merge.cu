@@ -394,7 +394,7 @@ __global__ void dm_broadcast_kernel(const float* __restrict__ theta, long long a
 // ───── fused tile merge: atomic-free apply + broadcast of one slice (alternative to dm_apply_* + dm_broadcast) ─────
 // The slice [a, b) is cut into tiles of DM_TILE elements. dm_tile_bounds_kernel finds, for every sparse
 // member payload, the position where each tile's entries start (bounds[c * (ntiles + 1) + t]).
-// dm_tile_apply_kernel (persistent CTAs, one tile at a time) then loads a tile of the checkpoint and of the
+// dm_tile_apply_kernel then gives every tile to one CTA: the CTA loads its tile of the checkpoint and of the
 // dense members into registers, sums the entries of all sparse members that fall in the tile into shared
 // memory (one flat loop over the concatenation of the members' entry ranges, so every member's loads are in
 // flight together; shared atomics only), adds the sum to the checkpoint once and writes the tile to every
@@ -440,125 +440,122 @@ __global__ void __launch_bounds__(DM_TILE_THREADS) dm_tile_apply_kernel(
   __shared__ long long sh_w0[MAX_CONTRIB];                       // window offset (<< 31) at the first entry
   __shared__ float shc[MAX_CONTRIB];
   const int tid = threadIdx.x;
+  const long long t = blockIdx.x;
+  const long long t0 = a + t * DM_TILE;
+  const long long len4 = ((b - t0) < DM_TILE ? (b - t0) : DM_TILE) / 4;  // a, b, DM_TILE multiples of 4
+  const long long len = 4 * len4;
+  // (1) each member's entry range in this tile; the sparse sum starts at zero
+  if (tid < n) {
+    const Contrib& C = cs.c[tid];
+    const float k = coefs[tid];
+    shc[tid] = k;
+    long long p0 = 0, nxt = 0x7fffffffffffffffLL, w0 = 0;
+    int cnt = 0;
+    if (!C.dense && k != 0.f && t < ntiles) {
+      const long long lo = ranges[2 * tid], hi = ranges[2 * tid + 1];
+      const long long* bc = bounds + (long long)tid * (ntiles + 1);
+      long long q0 = bc[t], q1 = bc[t + 1];
+      q0 = q0 < lo ? lo : (q0 > hi ? hi : q0);
+      q1 = q1 < q0 ? q0 : (q1 > hi ? hi : q1);
+      if (q1 - q0 > DM_TILE) q1 = q0 + DM_TILE;  // a tile holds at most DM_TILE distinct indices
+      p0 = q0;
+      cnt = (int)(q1 - q0);
+      if (C.win) {
+        for (int w = 1; w < 8; ++w) {
+          const long long s = __ldg(C.win + w);
+          w0 += (p0 >= s);
+          if (s > p0 && s < nxt) nxt = s;
+        }
+      }
+    }
+    sh_p0[tid] = p0;
+    sh_nxt[tid] = nxt;
+    sh_w0[tid] = w0 << 31;
+    sh_cnt[tid] = cnt;
+  }
   float4* tile4 = reinterpret_cast<float4*>(tile);
-  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {  // persistent: one CTA per resident slot
-    const long long t0 = a + t * DM_TILE;
-    const long long len4 = ((b - t0) < DM_TILE ? (b - t0) : DM_TILE) / 4;  // a, b, DM_TILE multiples of 4
-    const long long len = 4 * len4;
-    // (1) this thread's part of the checkpoint tile (loads issued first, used last)
-    float4 th[DM_TILE_R];
+  for (int i4 = tid; i4 < DM_TILE / 4; i4 += DM_TILE_THREADS) tile4[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  // (2) this thread's part of the checkpoint tile plus the dense members, in registers
+  float4 th[DM_TILE_R];
+#pragma unroll
+  for (int r = 0; r < DM_TILE_R; ++r) {
+    const long long i4 = tid + r * DM_TILE_THREADS;
+    th[r] = i4 < len4 ? reinterpret_cast<const float4*>(theta)[t0 / 4 + i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int c = 0; c < n; ++c) {
+    const Contrib& C = cs.c[c];
+    const float k = shc[c];
+    if (!C.dense || k == 0.f) continue;
+    float4 v[DM_TILE_R];
 #pragma unroll
     for (int r = 0; r < DM_TILE_R; ++r) {
       const long long i4 = tid + r * DM_TILE_THREADS;
-      th[r] = i4 < len4 ? reinterpret_cast<const float4*>(theta)[t0 / 4 + i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[r] = (i4 < len4 && t0 + 4 * i4 < C.count) ? __ldg(reinterpret_cast<const float4*>(C.val) + t0 / 4 + i4)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // (2) each member's entry range in this tile; the sparse sum starts at zero
-    if (tid < n) {
-      const Contrib& C = cs.c[tid];
-      const float k = coefs[tid];
-      shc[tid] = k;
-      long long p0 = 0, nxt = 0x7fffffffffffffffLL, w0 = 0;
-      int cnt = 0;
-      if (!C.dense && k != 0.f) {
-        const long long lo = ranges[2 * tid], hi = ranges[2 * tid + 1];
-        const long long* bc = bounds + (long long)tid * (ntiles + 1);
-        long long q0 = bc[t], q1 = bc[t + 1];
-        q0 = q0 < lo ? lo : (q0 > hi ? hi : q0);
-        q1 = q1 < q0 ? q0 : (q1 > hi ? hi : q1);
-        if (q1 - q0 > DM_TILE) q1 = q0 + DM_TILE;  // a tile holds at most DM_TILE distinct indices
-        p0 = q0;
-        cnt = (int)(q1 - q0);
-        if (C.win) {
-          for (int w = 1; w < 8; ++w) {
-            const long long s = __ldg(C.win + w);
-            w0 += (p0 >= s);
-            if (s > p0 && s < nxt) nxt = s;
-          }
-        }
-      }
-      sh_p0[tid] = p0;
-      sh_nxt[tid] = nxt;
-      sh_w0[tid] = w0 << 31;
-      sh_cnt[tid] = cnt;
+#pragma unroll
+    for (int r = 0; r < DM_TILE_R; ++r) {
+      th[r].x += k * v[r].x;
+      th[r].y += k * v[r].y;
+      th[r].z += k * v[r].z;
+      th[r].w += k * v[r].w;
     }
-    for (int i4 = tid; i4 < DM_TILE / 4; i4 += DM_TILE_THREADS) tile4[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      for (int c = 0; c < n; ++c) {
-        sh_pre[c] = acc;
-        acc += sh_cnt[c];
-      }
-      sh_pre[n] = acc;
-    }
-    // (3) dense members into the registers
+  }
+  if (tid == 0) {
+    int acc = 0;
     for (int c = 0; c < n; ++c) {
-      const Contrib& C = cs.c[c];
-      const float k = shc[c];
-      if (!C.dense || k == 0.f) continue;
-      float4 v[DM_TILE_R];
-#pragma unroll
-      for (int r = 0; r < DM_TILE_R; ++r) {
-        const long long i4 = tid + r * DM_TILE_THREADS;
-        v[r] = (i4 < len4 && t0 + 4 * i4 < C.count) ? __ldg(reinterpret_cast<const float4*>(C.val) + t0 / 4 + i4)
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int r = 0; r < DM_TILE_R; ++r) {
-        th[r].x += k * v[r].x;
-        th[r].y += k * v[r].y;
-        th[r].z += k * v[r].z;
-        th[r].w += k * v[r].w;
-      }
+      sh_pre[c] = acc;
+      acc += sh_cnt[c];
     }
-    __syncthreads();
-    // (4) all sparse members' entries of the tile as one flat list
-    const int total = sh_pre[n];
-    for (int e0 = tid; e0 < total; e0 += DM_TILE_THREADS * DM_UNR) {
-      int j[DM_UNR];
-      float v[DM_UNR];
+    sh_pre[n] = acc;
+  }
+  __syncthreads();
+  // (3) all sparse members' entries of the tile as one flat list
+  const int total = sh_pre[n];
+  for (int e0 = tid; e0 < total; e0 += DM_TILE_THREADS * DM_UNR) {
+    int j[DM_UNR];
+    float v[DM_UNR];
 #pragma unroll
-      for (int u = 0; u < DM_UNR; ++u) {
-        const int e = e0 + u * DM_TILE_THREADS;
-        j[u] = -1;
-        v[u] = 0.f;
-        if (e < total) {
-          int lo = 0, hi = n;  // sh_pre[lo] <= e < sh_pre[hi]
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (sh_pre[mid] <= e) lo = mid;
-            else hi = mid;
-          }
-          const Contrib& C = cs.c[lo];
-          const long long p = sh_p0[lo] + (e - sh_pre[lo]);
-          const long long flat =
-              (long long)__ldg(C.idx + p) + sh_w0[lo] + (p >= sh_nxt[lo] ? (1ll << 31) : 0ll);
-          const long long jj = flat - t0;
-          j[u] = (jj >= 0 && jj < len) ? (int)jj : -1;
-          v[u] = shc[lo] * contrib_value(C, p);
+    for (int u = 0; u < DM_UNR; ++u) {
+      const int e = e0 + u * DM_TILE_THREADS;
+      j[u] = -1;
+      v[u] = 0.f;
+      if (e < total) {
+        int lo = 0, hi = n;  // sh_pre[lo] <= e < sh_pre[hi]
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (sh_pre[mid] <= e) lo = mid;
+          else hi = mid;
         }
-      }
-#pragma unroll
-      for (int u = 0; u < DM_UNR; ++u)
-        if (j[u] >= 0) atomicAdd(&tile[j[u]], v[u]);
-    }
-    __syncthreads();
-    // (5) checkpoint update and broadcast of the tile
-#pragma unroll
-    for (int r = 0; r < DM_TILE_R; ++r) {
-      const long long i4 = tid + r * DM_TILE_THREADS;
-      if (i4 < len4) {
-        const float4 s = tile4[i4];
-        float4 o = th[r];
-        o.x += s.x;
-        o.y += s.y;
-        o.z += s.z;
-        o.w += s.w;
-        reinterpret_cast<float4*>(theta)[t0 / 4 + i4] = o;
-        store_dests(mc32, d, theta, t0 / 4 + i4, o);
+        const Contrib& C = cs.c[lo];
+        const long long p = sh_p0[lo] + (e - sh_pre[lo]);
+        const long long flat =
+            (long long)__ldg(C.idx + p) + sh_w0[lo] + (p >= sh_nxt[lo] ? (1ll << 31) : 0ll);
+        const long long jj = flat - t0;
+        j[u] = (jj >= 0 && jj < len) ? (int)jj : -1;
+        v[u] = shc[lo] * contrib_value(C, p);
       }
     }
-    __syncthreads();  // the shared tile and member table are rewritten for the next tile
+#pragma unroll
+    for (int u = 0; u < DM_UNR; ++u)
+      if (j[u] >= 0) atomicAdd(&tile[j[u]], v[u]);
+  }
+  __syncthreads();
+  // (4) checkpoint update and broadcast of the tile
+#pragma unroll
+  for (int r = 0; r < DM_TILE_R; ++r) {
+    const long long i4 = tid + r * DM_TILE_THREADS;
+    if (i4 < len4) {
+      const float4 s = tile4[i4];
+      float4 o = th[r];
+      o.x += s.x;
+      o.y += s.y;
+      o.z += s.z;
+      o.w += s.w;
+      reinterpret_cast<float4*>(theta)[t0 / 4 + i4] = o;
+      store_dests(mc32, d, theta, t0 / 4 + i4, o);
+    }
   }
   last_block_release(blocks_local, done_dst);
 }
@@ -719,8 +716,8 @@ DT_API int dt_dm_broadcast(const float* theta, long long a, long long b, void* m
 }
 
 // Fused alternative to dt_dm_apply + dt_dm_broadcast for a slice [a, b) (multiples of 4): tile bounds per
-// sparse member into `bounds` (n * (ceil((b - a) / dt_dm_tile_elems()) + 1) int64, device), then the
-// tile pass.
+// sparse member into `bounds` (n * (ceil((b - a) / dt_dm_tile_elems()) + 1) int64, device), then one CTA
+// per tile.
 DT_API long long dt_dm_tile_elems() { return DM_TILE; }
 
 DT_API int dt_dm_fused(const void* contribs, int n, const long long* ranges, long long* bounds, long long a,
@@ -736,8 +733,7 @@ DT_API int dt_dm_fused(const void* contribs, int n, const long long* ranges, lon
   if (ntiles > 0) {
     dim3 g1(grid_cap(ntiles + 1, 256, 148 * 8), n);
     dm_tile_bounds_kernel<<<g1, 256, 0, st>>>(tab, ranges, a, ntiles, bounds);
-    const long long grid = ntiles < 148 * 4 ? ntiles : 148 * 4;  // 4 resident CTAs per SM (64 registers)
-    dm_tile_apply_kernel<<<(unsigned)grid, DM_TILE_THREADS, 0, st>>>(tab, n, ranges, bounds, a, b, ntiles, coefs,
+    dm_tile_apply_kernel<<<(unsigned)ntiles, DM_TILE_THREADS, 0, st>>>(tab, n, ranges, bounds, a, b, ntiles, coefs,
                                                                      theta, reinterpret_cast<float*>(mc32), d,
                                                                      done_dst, blocks_local);
   } else {
