@@ -24,7 +24,6 @@ o_proj, norm, gate|up, SwiGLU) right before its backward, with one set of block 
 """
 from __future__ import annotations
 
-import math
 from typing import Optional
 
 import torch

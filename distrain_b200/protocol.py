@@ -20,7 +20,7 @@ import time
 from dataclasses import dataclass, field, asdict
 from typing import Any, Dict, List, Optional, Tuple
 
-from .config import TrainingParams, _Json
+from .config import _Json
 
 
 # ─────────────────────────────── time helpers ───────────────────────────────

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import json
-from typing import Dict, List, Optional
+from typing import Dict, Optional
 
 import torch
 

@@ -3,7 +3,6 @@ import json
 import math
 import struct
 
-import pytest
 import torch
 
 from distrain_b200.utils import native

@@ -1,5 +1,4 @@
 """Fused compression and peer-pull merge kernels vs the CPU restatement of the reference algorithms."""
-import math
 
 import pytest
 import torch
@@ -76,7 +75,7 @@ def test_device_merge_matches_reference(momentum, in_place):
     """Merge of three compressed payloads (one an outlier that gets clipped) against the fp32 reference
     merge: in place into a staging-style buffer, into a private copy, and with Nesterov momentum."""
     from distrain_b200.config import CompressionConfig
-    from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload, dequantize_int8
+    from distrain_b200.parallel.compression import DeviceCompressor, dequantize_int8
     from distrain_b200.parallel.merge import DeviceMerger, Contribution, merge_reference
     L = _layout()
     dev = torch.device("cuda")

@@ -4,10 +4,9 @@ position, full coverage)."""
 import os
 
 import numpy as np
-import pytest
 import torch
 
-from distrain_b200.utils.data import ShardLoader, StreamingLoader, prepare_random_shards, write_shard, write_manifest
+from distrain_b200.utils.data import ShardLoader, StreamingLoader, prepare_random_shards, write_shard
 from distrain_b200.utils.storage import FsStore
 
 

@@ -12,7 +12,6 @@ import datetime as dt
 import json
 import time
 
-import pytest
 import torch
 
 from distrain_b200 import protocol as P

@@ -4,7 +4,6 @@
 CPU: chunk tables never straddle a window boundary. GPU: a ~2.2 G-parameter layout with values planted
 on both sides of the 2^31 boundary compresses to the right flat indices and merges into the right
 checkpoint entries."""
-import math
 
 import pytest
 import torch
