@@ -3,7 +3,8 @@
 Node commands mirror the reference CLI (node/cli/src/main.rs:24-122): start, bootstrap, benchmark,
 status, config, eval, gpu-stress-test, baseline, generate. Service / tooling commands: coordinator
 (the HTTP coordinator, env-configured like coordinator/src/main.rs:141-188), prepare-data (the data-prep
-script's random-shard mode), micro-cluster (coordinator + N CPU node processes on one host).
+script's random-shard mode), micro-cluster (coordinator + N CPU node processes on one host), train-box
+(every GPU of this box as one node of the in-box protocol; launched with ``torch.distributed.run``).
 """
 from __future__ import annotations
 
@@ -122,6 +123,82 @@ def cmd_start(args):
             for r in log:
                 f.write(json.dumps(r) + "\n")
     print(json.dumps(out), flush=True)
+
+
+def apply_run_overrides(run, args):
+    """Command-line overrides of a RunConfig (train-box); unset flags keep the preset's values."""
+    for flag, field_name in (("push_every", "push_every"), ("tp", "tp"), ("checkpoint_store", "checkpoint_store"),
+                             ("checkpoint_every", "checkpoint_every"), ("keep_versions", "keep_versions"),
+                             ("metrics_port", "metrics_port"), ("watchdog_secs", "watchdog_step_secs"),
+                             ("swap_mode", "swap_mode"), ("ef_on_swap", "ef_on_swap"), ("seed", "seed"),
+                             ("payload_slots", "payload_slots")):
+        v = getattr(args, flag, None)
+        if v is not None:
+            setattr(run, field_name, v)
+    for flag, field_name in (("resume", "resume"), ("loss_based_lr", "loss_based_lr"),
+                             ("bandwidth_adaptive", "bandwidth_adaptive"),
+                             ("reset_optimizer", "reset_optimizer_on_swap"),
+                             ("activation_checkpointing", "activation_checkpointing")):
+        if getattr(args, flag, False):
+            setattr(run, field_name, True)
+    if getattr(args, "top_k", None) is not None:
+        run.compression.top_k_fraction = args.top_k
+    if getattr(args, "no_int8", False):
+        run.compression.quantize_int8 = False
+    if getattr(args, "lr", None) is not None:
+        run.optim.lr = args.lr
+    if getattr(args, "batch_size", None) is not None:
+        run.micro_batch = args.batch_size
+    if getattr(args, "seq_len", None) is not None:
+        run.seq_len = args.seq_len
+        run.model.max_seq_len = max(run.model.max_seq_len, args.seq_len)
+    return run
+
+
+def cmd_train_box(args):
+    """In-box training job: one node per GPU process (rank), the compressed protocol over NVLink between
+    them, batches from local token shards (each node its deterministic share) or synthetic tokens."""
+    import torch
+    import torch.distributed as dist
+    from .config import bench_config
+    from .parallel.launch import init_box, box_node, node_batches
+    br = init_box(args.pg_timeout)
+    run = apply_run_overrides(bench_config(args.preset), args)
+    node, node_rank, n_nodes = box_node(run, br, enable_push=not args.no_push, tp_mode=args.tp_mode, sync=args.sync)
+    source, desc = node_batches(run, node_rank, n_nodes, args.data_dir, args.shards_fraction, run.seed)
+    out = open(args.output, "w") if (args.output and br.rank == 0) else None
+
+    def emit(rec):
+        if br.rank == 0:
+            print(json.dumps(rec), flush=True)
+            if out:
+                out.write(json.dumps(rec) + "\n")
+                out.flush()
+    emit({"event": "train_box_start", "preset": run.name, "nodes": n_nodes, "ranks": br.world, "tp": run.tp,
+          "micro_batch": run.micro_batch, "seq_len": run.seq_len, "push_every": run.push_every, "data": desc,
+          "resumed_version": getattr(node.sync, "resumed_version", 0)})
+    done = 0
+    tokens_per_step = run.micro_batch * (run.seq_len - 1) * n_nodes
+    while done < args.steps:
+        k = min(args.log_every, args.steps - done)
+        t0 = time.time()
+        losses = node.train_stream(source, k)
+        dt = time.time() - t0
+        done += k
+        emit({"event": "train", "step": done, "loss": sum(losses) / len(losses), "last_loss": losses[-1],
+              "tokens_per_sec": tokens_per_step * k / dt, "version": getattr(node.sync, "version", 0)})
+        if getattr(node, "hung", None):
+            emit({"event": "watchdog", "detail": str(node.hung)})
+            break
+    node.close()
+    if br.world > 1:
+        dist.barrier()
+    emit({"event": "train_box_done", "steps": done, "version": getattr(node.sync, "version", 0),
+          "merges": len(getattr(node.sync, "merges", []) or [])})
+    if out:
+        out.close()
+    if br.world > 1:
+        dist.destroy_process_group()
 
 
 def cmd_status(args):
@@ -452,6 +529,40 @@ def main(argv=None):
     p.add_argument("--port", type=int, default=18731)
     p.add_argument("--store")
     p.set_defaults(fn=cmd_micro_cluster)
+
+    p = sp.add_parser("train-box", help="in-box training: every GPU of this box is one node (torch.distributed.run)")
+    p.add_argument("--preset", default="tiny", help="micro-test | tiny | small | medium | large")
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--log-every", type=int, default=50)
+    p.add_argument("--data-dir", help="directory of shard_XXXX.bin token shards (default: synthetic tokens)")
+    p.add_argument("--shards-fraction", type=float, default=0.2, help="share of the shards each node reads")
+    p.add_argument("--batch-size", type=int)
+    p.add_argument("--seq-len", type=int)
+    p.add_argument("--push-every", type=int)
+    p.add_argument("--top-k", type=float)
+    p.add_argument("--no-int8", action="store_true")
+    p.add_argument("--bandwidth-adaptive", action="store_true")
+    p.add_argument("--lr", type=float)
+    p.add_argument("--tp", type=int)
+    p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"])
+    p.add_argument("--activation-checkpointing", action="store_true")
+    p.add_argument("--payload-slots", type=int)
+    p.add_argument("--sync", default="inbox", choices=["inbox", "nccl"])
+    p.add_argument("--no-push", action="store_true", help="train only (no protocol)")
+    p.add_argument("--checkpoint-store", help="persist merged versions here (directory or S3 endpoint)")
+    p.add_argument("--checkpoint-every", type=int)
+    p.add_argument("--keep-versions", type=int)
+    p.add_argument("--resume", action="store_true")
+    p.add_argument("--metrics-port", type=int)
+    p.add_argument("--loss-based-lr", action="store_true")
+    p.add_argument("--watchdog-secs", type=float)
+    p.add_argument("--swap-mode", choices=["rebase", "push_partial"])
+    p.add_argument("--ef-on-swap", choices=["fold", "keep", "reset"])
+    p.add_argument("--reset-optimizer", action="store_true")
+    p.add_argument("--seed", type=int)
+    p.add_argument("--output", help="JSONL log (rank 0)")
+    p.add_argument("--pg-timeout", type=float, default=300.0)
+    p.set_defaults(fn=cmd_train_box)
 
     args = ap.parse_args(argv)
     from .utils.tracing import setup_logging

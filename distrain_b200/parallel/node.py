@@ -20,6 +20,32 @@ from ..models.engine import TrainEngine
 from ..utils.tracing import nvtx
 
 
+class BatchFeed:
+    """Sequence view of a batch source for ``InBoxNode.train_steps_e2e``: reading element k fetches the
+    source's next [batch, seq] int32 batch into pinned host buffer k (of ``depth``, round robin). The loop
+    reads element i % depth at step i and waits for step i - 1 before it issues step i + 1, so a buffer is
+    refilled only after the copy that read it has completed."""
+
+    def __init__(self, source, batch: int, seq: int, depth: int = 3):
+        pin = torch.cuda.is_available()
+        self.bufs = [torch.empty(batch, seq, dtype=torch.int32) for _ in range(depth)]
+        if pin:
+            self.bufs = [b.pin_memory() for b in self.bufs]
+        self.source = source
+        self.fetched = 0
+
+    def __len__(self):
+        return len(self.bufs)
+
+    def __getitem__(self, k: int) -> torch.Tensor:
+        b = self.source()
+        if tuple(b.shape) != tuple(self.bufs[k].shape):
+            raise ValueError(f"batch source gave {tuple(b.shape)}, expected {tuple(self.bufs[k].shape)}")
+        self.bufs[k].copy_(b)
+        self.fetched += 1
+        return self.bufs[k]
+
+
 class InBoxNode:
     def __init__(self, run: RunConfig, rank: int = 0, world: int = 1, device=None, enable_push: bool = True,
                  attn_impl: str = None, tp=None, shard: int = 0, n_shards: int = 1, dp_group=None):
@@ -100,6 +126,13 @@ class InBoxNode:
         ev[(steps - 1) % 2].synchronize()
         self._observe(float(pinned_loss[(steps - 1) % 2][0]), losses)
         return losses
+
+    def train_stream(self, source, steps: int):
+        """``train_steps_e2e`` over a batch source (a callable returning [micro_batch, seq_len] int32 CPU
+        tensors, e.g. ``ShardLoader.next_batch``); returns the per-step losses."""
+        if getattr(self, "_feed", None) is None or self._feed.source is not source:
+            self._feed = BatchFeed(source, self.run.micro_batch, self.run.seq_len)
+        return self.train_steps_e2e(self._feed, steps)
 
     def _observe(self, loss: float, losses: list):
         losses.append(loss)
