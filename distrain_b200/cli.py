@@ -18,9 +18,20 @@ import sys
 import time
 
 
-def _store(path_or_url: str):
+def _store(path_or_url=None):
+    """An object store from a directory / file:// path / http(s) endpoint, or, when none is given, the S3
+    settings of the environment (R2_ENDPOINT, R2_BUCKET, R2_ACCESS_KEY_ID, R2_SECRET_ACCESS_KEY,
+    R2_REGION, as the coordinator reads them)."""
     from .utils.storage import open_store
+    if not path_or_url:
+        from .config import CoordinatorConfig
+        return open_store(CoordinatorConfig.from_env().storage)
     return open_store(path_or_url)
+
+
+def _store_from_cfg(storage_cfg):
+    from .utils.storage import open_store
+    return open_store(storage_cfg)
 
 
 def _model_cfg(preset: str, vocab=None, seq=None, theta=None):
@@ -72,7 +83,8 @@ def cmd_coordinator(args):
     cfg = CoordinatorConfig.from_env()
     if args.port is not None:
         cfg.port = args.port
-    store = _store(args.store)
+    store = _store(args.store) if args.store else _store_from_cfg(cfg.storage)
+    store.ensure_bucket()
     svc = CoordinatorService(cfg, store, merge_device=args.merge_device)
     port = svc.start(host=args.host or cfg.host)
     print(json.dumps({"event": "coordinator_started", "port": port}), flush=True)
@@ -88,9 +100,45 @@ def cmd_coordinator(args):
 
 def cmd_bootstrap(args):
     from .coordinator.service import bootstrap
+    from . import protocol as P
+    store = _store(args.store)
+    if args.if_absent and store.exists(P.checkpoint_path(0)):
+        print(json.dumps({"event": "bootstrap_skipped", "reason": "checkpoint v0 exists"}))
+        return
     m = _model_cfg(args.preset, args.vocab, args.seq_len, args.rope_theta)
-    L, _ = bootstrap(_store(args.store), m, seed=args.seed)
+    L, _ = bootstrap(store, m, seed=args.seed)
     print(json.dumps({"event": "bootstrapped", "version": 0, "params": L.num_params(), "model": m.to_dict()}))
+
+
+def _apply_node_config(args):
+    """Fill the start command's unset options from a node.toml (the reference's NodeConfig,
+    core/shared/src/config.rs:81-143): coordinator_url, [storage], gpu_device, force_batch_size /
+    batch_size, seq_len, force_cpu, min_inner_steps (steps per push). Flags win over the file; without a
+    file the storage comes from the R2_* environment."""
+    from .config import CoordinatorConfig, NodeConfig
+    nc = NodeConfig.load_toml(args.config) if args.config else None
+    if nc is None:
+        args.storage_cfg = CoordinatorConfig.from_env().storage
+    else:
+        args.storage_cfg = nc.storage
+        if not args.coordinator_url:
+            args.coordinator_url = nc.coordinator_url
+        if args.device is None and not args.cpu:
+            if nc.force_cpu:
+                args.cpu = True
+            elif nc.gpu_device >= 0:
+                args.device = f"cuda:{nc.gpu_device}"
+        if args.batch_size is None:
+            args.batch_size = nc.force_batch_size or nc.batch_size
+        if args.seq_len is None:
+            args.seq_len = nc.seq_len
+        if args.h_mini is None and nc.min_inner_steps:
+            args.h_mini = nc.min_inner_steps
+    if not args.coordinator_url:
+        raise SystemExit("start: --coordinator-url or a --config with coordinator_url is required")
+    args.batch_size = args.batch_size or 4
+    args.seq_len = args.seq_len or 512
+    args.h_mini = args.h_mini or 50
 
 
 def cmd_start(args):
@@ -99,7 +147,8 @@ def cmd_start(args):
     from .utils.checkpoint import load_safetensors_bytes
     from .coordinator.client import CoordinatorClient
     from . import protocol as P
-    store = _store(args.store)
+    _apply_node_config(args)
+    store = _store(args.store) if args.store else _store_from_cfg(args.storage_cfg)
     cl = CoordinatorClient(args.coordinator_url)
     v = cl.get_latest_checkpoint().version
     m = _infer_model_config(load_safetensors_bytes(store.get(P.checkpoint_path(v))))
@@ -413,19 +462,21 @@ def cmd_micro_cluster(args):
     print(json.dumps({"event": "micro_cluster_done", "store": root, "nodes": outs}))
 
 
-def main(argv=None):
+def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="distrain_b200")
     sp = ap.add_subparsers(dest="cmd", required=True)
 
     p = sp.add_parser("coordinator", help="run the coordinator HTTP service")
-    p.add_argument("--store", required=True, help="object store: directory / file:// path, or http(s):// S3 endpoint")
+    p.add_argument("--store", help="object store: directory / file:// path, or http(s):// S3 endpoint "
+                                    "(default: the R2_* environment)")
     p.add_argument("--host")
     p.add_argument("--port", type=int)
     p.add_argument("--merge-device", default="cpu")
     p.set_defaults(fn=cmd_coordinator)
 
     p = sp.add_parser("bootstrap", help="create and store checkpoint v0")
-    p.add_argument("--store", required=True)
+    p.add_argument("--store", help="default: the R2_* environment")
+    p.add_argument("--if-absent", action="store_true", help="do nothing when checkpoint v0 already exists")
     p.add_argument("--preset", default="tiny")
     p.add_argument("--vocab", type=int)
     p.add_argument("--seq-len", type=int)
@@ -434,15 +485,16 @@ def main(argv=None):
     p.set_defaults(fn=cmd_bootstrap)
 
     p = sp.add_parser("start", help="run a training node against a coordinator")
-    p.add_argument("--coordinator-url", required=True)
-    p.add_argument("--store", required=True)
+    p.add_argument("--config", help="node.toml (coordinator_url, [storage], gpu_device, batch size, seq_len)")
+    p.add_argument("--coordinator-url")
+    p.add_argument("--store", help="default: the config's [storage], else the R2_* environment")
     p.add_argument("--cpu", action="store_true")
     p.add_argument("--device")
     p.add_argument("--node-id")
     p.add_argument("--steps", type=int, default=1000)
-    p.add_argument("--batch-size", type=int, default=4)
-    p.add_argument("--seq-len", type=int, default=512)
-    p.add_argument("--h-mini", type=int, default=50)
+    p.add_argument("--batch-size", type=int, help="default: the config's, else 4")
+    p.add_argument("--seq-len", type=int, help="default: the config's, else 512")
+    p.add_argument("--h-mini", type=int, help="steps per push (default: the config's min_inner_steps, else 50)")
     p.add_argument("--lr", type=float, default=3e-4)
     p.add_argument("--top-k", type=float, default=0.1)
     p.add_argument("--no-int8", action="store_true")
@@ -563,8 +615,11 @@ def main(argv=None):
     p.add_argument("--output", help="JSONL log (rank 0)")
     p.add_argument("--pg-timeout", type=float, default=300.0)
     p.set_defaults(fn=cmd_train_box)
+    return ap
 
-    args = ap.parse_args(argv)
+
+def main(argv=None):
+    args = build_parser().parse_args(argv)
     from .utils.tracing import setup_logging
     setup_logging(os.environ.get("DT_LOG", "info"))
     args.fn(args)
