@@ -66,11 +66,13 @@ def setup_logging(spec: Optional[str] = None, stream=None):
         else:
             default = getattr(logging, part.upper(), logging.WARNING)
     root = logging.getLogger()
-    if not any(getattr(h, "_dt", False) for h in root.handlers):
-        h = logging.StreamHandler(stream)
-        h.setFormatter(logging.Formatter("%(asctime)s %(levelname)s %(name)s: %(message)s"))
-        h._dt = True
-        root.addHandler(h)
+    # one handler of ours at a time, on the stream of the latest call (stderr by default)
+    for old in [h for h in root.handlers if getattr(h, "_dt", False)]:
+        root.removeHandler(old)
+    h = logging.StreamHandler(stream)
+    h.setFormatter(logging.Formatter("%(asctime)s %(levelname)s %(name)s: %(message)s"))
+    h._dt = True
+    root.addHandler(h)
     root.setLevel(default)
     for name, lvl in per.items():
         logging.getLogger(name).setLevel(getattr(logging, lvl, logging.INFO))
