@@ -24,6 +24,7 @@ BUILDDIR = os.path.join(ROOT, "_build")
 
 KERNELS_SO = os.path.join(LIBDIR, "libdt_kernels.so")
 RUNTIME_SO = os.path.join(LIBDIR, "libdt_runtime.so")
+FFI_SO = os.path.join(LIBDIR, "libdistrain_c.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -121,6 +122,33 @@ def build_runtime(force: bool = False, verbose: bool = False) -> str:
     return RUNTIME_SO
 
 
+def build_ffi(force: bool = False, verbose: bool = False) -> str:
+    """``csrc/ffi/distrain_c.cpp`` -> ``libdistrain_c.so``: the C ABI over the training engine. It links
+    the runtime library (native shard assignment) and resolves Python's C API at run time; the default
+    libpython and the interpreter's site directories are recorded for C programs that start Python
+    through it."""
+    import site
+    import sysconfig
+    src = os.path.join(CSRC, "ffi", "distrain_c.cpp")
+    if not os.path.exists(src):
+        return ""
+    runtime = build_runtime(force=False, verbose=verbose)
+    deps = [src, os.path.join(CSRC, "ffi", "distrain_c.h"), runtime, __file__]
+    if not force and os.path.exists(FFI_SO) and os.path.getmtime(FFI_SO) >= _newest(deps):
+        return FFI_SO
+    libpy = os.path.join(sysconfig.get_config_var("LIBDIR") or "", sysconfig.get_config_var("INSTSONAME") or "")
+    sites = ":".join(p for p in site.getsitepackages() if os.path.isdir(p))
+    cxx = os.environ.get("CXX", "g++")
+    tmp = FFI_SO + ".tmp"
+    _run([cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I", sysconfig.get_paths()["include"],
+          f'-DDT_LIBPYTHON_DEFAULT="{libpy}"', f'-DDT_SITE_DEFAULT="{sites}"', src, "-o", tmp,
+          "-L", LIBDIR, "-ldt_runtime", "-Wl,-rpath,$ORIGIN", "-ldl"])
+    os.replace(tmp, FFI_SO)
+    if verbose:
+        print("[build] g++ C ABI library", file=sys.stderr)
+    return FFI_SO
+
+
 def sanitizer_cxx(sanitize: str):
     """The first of $CXX and g++ that compiles and links a program with -fsanitize=<sanitize> (None if
     neither does: a toolchain without the sanitizer runtime libraries)."""
@@ -181,9 +209,10 @@ def build_all(force: bool = False, verbose: bool = True):
     with cf.ThreadPoolExecutor(max_workers=2) as ex:
         a = ex.submit(build_kernels, force, verbose)
         b = ex.submit(build_runtime, force, verbose)
-        return a.result(), b.result()
+        kernels, runtime = a.result(), b.result()
+    return kernels, runtime, build_ffi(force, verbose)
 
 
 if __name__ == "__main__":
     build_all(force="--force" in sys.argv)
-    print(KERNELS_SO, RUNTIME_SO)
+    print(KERNELS_SO, RUNTIME_SO, FFI_SO)

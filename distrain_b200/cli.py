@@ -50,18 +50,28 @@ def _model_cfg(preset: str, vocab=None, seq=None, theta=None):
 
 
 def _infer_model_config(sd):
-    """Model hyper-parameters from checkpoint shapes (reference trainer.rs:837-906)."""
-    from .config import ModelConfig
+    """Model hyper-parameters from checkpoint shapes (reference trainer.rs:837-906). The shapes do not
+    determine the head count (q_proj is [heads * head_dim, hidden] for every split), so a checkpoint
+    whose hidden size, depth, FFN width and KV width match a preset takes that preset's heads (the
+    vocabulary comes from the checkpoint); otherwise head_dim is the largest of 128/64/32/16 that fits."""
+    from .config import ModelConfig, preset
     V, H = sd["embedding.embedding.weight"].shape
     L = 1 + max(int(k.split(".")[1]) for k in sd if k.startswith("layers."))
     qd = sd["layers.0.attention.q_proj.weight"].shape[0]
     kvd = sd["layers.0.attention.k_proj.weight"].shape[0]
     F = sd["layers.0.ffn.gate_proj.weight"].shape[0]
-    for d in (128, 64, 32, 16):  # head_dim used by every preset
+    bias = "layers.0.attention.q_proj.bias" in sd
+    for name in ("micro", "tiny", "small", "medium", "large"):
+        c = preset(name)
+        d = c.hidden_dim // c.num_heads
+        if (c.hidden_dim, c.num_layers, c.ffn_hidden_dim, c.num_kv_heads * d) == (H, L, F, kvd) and qd == H:
+            c.vocab_size, c.qkv_bias = V, bias
+            return c
+    for d in (128, 64, 32, 16):
         if qd % d == 0 and kvd % d == 0 and H % d == 0 and H // d == qd // d:
             break
     return ModelConfig(hidden_dim=H, num_layers=L, num_heads=qd // d, num_kv_heads=kvd // d, ffn_hidden_dim=F,
-                       vocab_size=V, qkv_bias="layers.0.attention.q_proj.bias" in sd)
+                       vocab_size=V, qkv_bias=bias)
 
 
 def _data_source(args, vocab, batch, seq, seed):
