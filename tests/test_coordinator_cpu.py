@@ -182,3 +182,19 @@ def test_merge_is_permutation_invariant_without_clipping():
         assert info["accepted"] == 4
         for k in ck:
             torch.testing.assert_close(got[k], base[k], rtol=1e-6, atol=1e-7)
+
+
+def test_nesterov_outer_step_golden_numbers():
+    """Outer Nesterov step with lr 0.7, momentum 0.9 from zero velocity: v = avg, theta -= lr * (mu * v + avg)
+    (the reference's worked example, core/model/src/training.rs:347-365), then a second step."""
+    import torch
+    from distrain_b200.parallel.merge import nesterov_step
+    ck = {"w": torch.tensor([1.0, 2.0, 3.0], dtype=torch.float64)}
+    avg = {"w": torch.tensor([0.1, 0.2, 0.3], dtype=torch.float64)}
+    ck, vel = nesterov_step(ck, avg, None, 0.7, 0.9)
+    assert torch.allclose(vel["w"], avg["w"])
+    assert torch.allclose(ck["w"], torch.tensor([0.867, 1.734, 2.601], dtype=torch.float64), atol=1e-12)
+    ck, vel = nesterov_step(ck, avg, vel, 0.7, 0.9)
+    assert torch.allclose(vel["w"], torch.tensor([0.19, 0.38, 0.57], dtype=torch.float64), atol=1e-12)
+    assert torch.allclose(ck["w"], torch.tensor([0.867 - 0.7 * 0.271, 1.734 - 0.7 * 0.542, 2.601 - 0.7 * 0.813],
+                                                dtype=torch.float64), atol=1e-12)
