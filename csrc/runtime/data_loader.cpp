@@ -193,6 +193,18 @@ DT_API void dtr_loader_seek_by_seed(void* h, unsigned long long seed) {
   L->offset = off;
 }
 
+// Position the reader at token `offset` of shard `shard` (a value saved from dtr_loader_position), so a
+// restarted reader continues where it stopped. 0 on success, -1 for a position outside the shards, -2
+// while prefetching (the prefetch thread owns the position).
+DT_API int dtr_loader_seek(void* h, long long shard, long long offset) {
+  auto* L = static_cast<Loader*>(h);
+  if (L->prefetching) return -2;
+  if (shard < 0 || (size_t)shard >= L->shards.size() || offset < 0 || (size_t)offset > L->shards[shard].n) return -1;
+  L->shard_idx = (size_t)shard;
+  L->offset = (size_t)offset;
+  return 0;
+}
+
 DT_API void dtr_loader_reset(void* h) {
   auto* L = static_cast<Loader*>(h);
   L->shard_idx = 0;

@@ -171,10 +171,12 @@ def cmd_start(args):
                     optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
                                                                                  quantize_int8=not args.no_int8),
                     device=device, node_id=args.node_id, data=data, poll_secs=args.poll_secs,
-                    bandwidth_adaptive=args.bandwidth_adaptive)
+                    bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
+                    resume_every=args.resume_every)
     node.register(gpu_model="cpu" if device == "cpu" else "B200")
     log = node.run(args.steps)
     out = {"event": "node_done", "node_id": node.node_id, "steps": len(log), "version": node.version,
+           "resumed": node.resumed, "global_step": node.global_step,
            "first_loss": log[0]["loss"] if log else None, "last_loss": log[-1]["loss"] if log else None,
            "pushes": len(node.pushes), "accepted": sum(p["accepted"] for p in node.pushes), "errors": node.errors}
     if args.metrics_out:
@@ -515,6 +517,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--rope-theta", type=float)
     p.add_argument("--poll-secs", type=float, default=5.0)
     p.add_argument("--metrics-out")
+    p.add_argument("--resume-file", help="node-local resume file: written at round boundaries, read at start "
+                                         "(same checkpoint: weights, AdamW and error feedback continue; newer: "
+                                         "identity, step count and data position continue)")
+    p.add_argument("--resume-every", type=int, default=1, help="write the resume file every N full-round pushes")
     p.set_defaults(fn=cmd_start)
 
     p = sp.add_parser("status", help="coordinator training status")

@@ -57,6 +57,16 @@ class CpuBackend:
         with torch.no_grad():
             return float(self.oracle.lm_loss(self.params, self.cfg, tokens.long()).item())
 
+    def optimizer_state(self):
+        return {"m": {k: t.clone() for k, t in self.opt.m.items()}, "v": {k: t.clone() for k, t in self.opt.v.items()},
+                "t": self.opt.t}
+
+    def load_optimizer_state(self, st):
+        for k in self.opt.m:
+            self.opt.m[k].copy_(st["m"][k])
+            self.opt.v[k].copy_(st["v"][k])
+        self.opt.t = int(st["t"])
+
     def step(self, tokens: torch.Tensor, lr: float) -> float:
         loss = self.oracle.lm_loss(self.params, self.cfg, tokens.long())
         if not math.isfinite(loss.item()):
@@ -85,6 +95,17 @@ class CudaBackend:
     def state(self):
         return self.layout.to_state_dict(self.eng.master)
 
+    def optimizer_state(self):
+        """AdamW moments and the device hyper-parameter block (step count, bias corrections)."""
+        return {"m": self.eng.m.detach().cpu().clone(), "v": self.eng.v.detach().cpu().clone(),
+                "hp": self.eng.hp.detach().cpu().clone()}
+
+    def load_optimizer_state(self, st):
+        with torch.no_grad():
+            self.eng.m.copy_(st["m"].to(self.eng.device))
+            self.eng.v.copy_(st["v"].to(self.eng.device))
+            self.eng.hp.copy_(st["hp"].to(self.eng.device))
+
     def step(self, tokens, lr):
         self.eng.set_lr(lr)
         self.eng.set_tokens(tokens.to(self.eng.device, non_blocking=True))
@@ -98,7 +119,8 @@ class HttpNode:
                  device: str = "cpu", node_id: Optional[str] = None, data: Optional[Callable[[], torch.Tensor]] = None,
                  poll_secs: float = 5.0, use_upload_proxy: bool = False, bandwidth_adaptive: bool = False,
                  heartbeat_every: int = 10, loss_based_lr: Optional[bool] = None,
-                 expected_step_secs: Optional[float] = None):
+                 expected_step_secs: Optional[float] = None, resume_path: Optional[str] = None,
+                 resume_every: int = 1):
         self.client = CoordinatorClient(coordinator_url)
         self.store = store
         self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
@@ -129,6 +151,12 @@ class HttpNode:
         self._ef_gen = 0        # bumped by the training loop at each checkpoint swap
         self._ef_gen_seen = 0   # generation the uploader's error buffer belongs to
         self._threads: List[threading.Thread] = []
+        # node-local resume file: written by the uploader after every `resume_every`-th full-round push
+        self.resume_path, self.resume_every = resume_path, max(int(resume_every), 1)
+        self.resumed: Optional[str] = None   # "exact" (same checkpoint: weights, AdamW, EF restored) / "identity"
+        self._resume_rec = self._read_resume()
+        if self.node_id is None and self._resume_rec is not None:
+            self.node_id = self._resume_rec["node_id"]  # register under the same identity
 
     # ─────────── lifecycle ───────────
     def register(self, gpu_model: str = "cpu", vram_gb: float = 0.0):
@@ -165,7 +193,7 @@ class HttpNode:
                 self.errors.append(f"upload: {e}")
 
     def _compress_upload_push(self, pkg):
-        delta, shapes, push, mean_loss, ef_generation = pkg
+        delta, shapes, push, mean_loss, ef_generation, snap = pkg
         if ef_generation != self._ef_gen_seen:   # error feedback restarts at a checkpoint boundary
             self._ef, self._ef_gen_seen = {}, ef_generation
         cfg = self.comp
@@ -201,33 +229,88 @@ class HttpNode:
         self.pushes.append({"seq": push.seq_num, "version": push.checkpoint_version, "accepted": resp.accepted,
                             "reason": resp.reason, "bytes": len(blob), "retention": stats["retention_ratio"],
                             "top_k": cfg.top_k_fraction})
+        if snap is not None:
+            self._write_resume(snap, push.seq_num)
+
+    # ─────────── node-local resume ───────────
+    def _write_resume(self, snap, seq: int):
+        """Weights and AdamW state at a round boundary, the error-feedback residual after that round's push,
+        the data position and the node's identity, written atomically."""
+        rec = dict(snap, format=1, node_id=self.node_id, seq=seq,
+                   ef={k: v.clone() for k, v in self._ef.items()})
+        tmp = self.resume_path + ".tmp"
+        torch.save(rec, tmp)
+        os.replace(tmp, self.resume_path)
+
+    def _read_resume(self):
+        if not self.resume_path or not os.path.exists(self.resume_path):
+            return None
+        try:
+            rec = torch.load(self.resume_path, weights_only=False)
+        except Exception as e:
+            self.errors.append(f"resume file unreadable: {e}")
+            return None
+        shapes = {e.name: tuple(e.shape) for e in ParamLayout(self.cfg).entries}
+        if rec.get("format") != 1 or {k: tuple(v.shape) for k, v in rec["weights"].items()} != shapes:
+            self.errors.append("resume file is for another model; ignored")
+            return None
+        return rec
+
+    def _apply_resume(self, rec, latest_version: int):
+        """Same checkpoint as when the file was written: continue exactly (weights, AdamW, EF). Newer
+        checkpoint: load it as a swap would (fresh AdamW, EF restarts) and keep identity and data position."""
+        self.seq = int(rec["seq"])
+        self.global_step = int(rec["global_step"])
+        src = getattr(self.data, "__self__", None)
+        if rec.get("data") is not None and src is not None and hasattr(src, "restore"):
+            src.restore(rec["data"])
+        if int(rec["version"]) == latest_version:
+            self.backend.load(rec["weights"])
+            self.backend.load_optimizer_state(rec["optimizer"])
+            self._ef = {k: v.clone() for k, v in rec["ef"].items()}
+            self.resumed = "exact"
+            return True
+        self.resumed = "identity"
+        return False
 
     # ─────────── training loop ───────────
-    def _build_push(self, start, steps, tokens, losses, t0):
+    def _build_push(self, start, steps, tokens, losses, t0, boundary: bool = False):
         cur = self.backend.state()
         delta = {k: (start[k].reshape(-1) - cur[k].reshape(-1)).float() for k in start}
         shapes = {k: list(v.shape) for k, v in start.items()}
         self.seq += 1
+        snap = None
+        if boundary and self.resume_path and self.seq % self.resume_every == 0:
+            src = getattr(self.data, "__self__", None)
+            snap = {"weights": {k: v.detach().float().cpu().clone() for k, v in cur.items()},
+                    "optimizer": self.backend.optimizer_state(), "global_step": self.global_step,
+                    "version": self.version,
+                    "data": src.state() if src is not None and hasattr(src, "state") else None}
         mean_loss = sum(losses) / len(losses) if losses else 0.0
         push = P.DeltaPush(node_id=self.node_id, seq_num=self.seq, checkpoint_version=self.version,
                            inner_steps=steps, delta_key=P.delta_path(self.version, self.node_id, self.seq),
                            training_loss=mean_loss, tokens_processed=tokens, training_time_secs=time.time() - t0)
-        self.up_q.put((delta, shapes, push, mean_loss, self._ef_gen))
+        self.up_q.put((delta, shapes, push, mean_loss, self._ef_gen, snap))
 
     def run(self, total_steps: int, stop_on_version: Optional[int] = None):
         """Train ``total_steps`` steps continuously (or until ``stop_on_version`` is reached)."""
+        rec = self._resume_rec if self.version < 0 else None
+        self._resume_rec = None
         if self.node_id is None:
             self.register()
+        exact = False
         if self.version < 0:
             info = self.client.get_latest_checkpoint()
             self.version = info.version
-            self.backend.load(self._load_version(info.version))
+            exact = rec is not None and self._apply_resume(rec, info.version)
+            if not exact:
+                self.backend.load(self._load_version(info.version))
         for fn in (self._ckpt_manager, self._uploader):
             t = threading.Thread(target=fn, daemon=True)
             t.start()
             self._threads.append(t)
         warm = max(int(self.h_mini * self.optim.warmup_fraction), 2)
-        first_round = True
+        first_round = rec is None  # a resumed node has had its warm-up
         start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
         loss_ema, loss_count = 0.0, 0
         ln_vocab = math.log(self.cfg.vocab_size)
@@ -255,7 +338,7 @@ class HttpNode:
                         break
                 if round_step >= self.h_mini:
                     if not (first_round and round_step <= warm):
-                        self._build_push(start, round_step, round_tokens, losses, t0)
+                        self._build_push(start, round_step, round_tokens, losses, t0, boundary=True)
                     start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
                     first_round = False
                 tokens = self.data()

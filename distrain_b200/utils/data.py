@@ -62,6 +62,7 @@ def _reg():
     register("dtr_loader_position", [v, v], ll)
     register("dtr_loader_next", [v, v, ll], i)
     register("dtr_loader_seek_by_seed", [v, ull], None)
+    register("dtr_loader_seek", [v, ll, ll], i)
     register("dtr_loader_reset", [v], None)
     register("dtr_loader_start_prefetch", [v, v, i], i)
     register("dtr_loader_acquire", [v, i], i)
@@ -117,6 +118,20 @@ class ShardLoader:
     def reset(self):
         self.L.dtr_loader_reset(self.h)
 
+    def state(self):
+        """The read position (shard, token offset), or None while prefetching (the prefetch thread reads
+        ahead of the batches handed out, so its position is not the consumer's)."""
+        if self.bufs is not None:
+            return None
+        shard, off = self.position()
+        return {"shard": shard, "offset": off}
+
+    def restore(self, st):
+        """Continue from a position saved by ``state``."""
+        rc = self.L.dtr_loader_seek(self.h, int(st["shard"]), int(st["offset"]))
+        if rc:
+            raise NativeError(f"cannot seek to {st} (rc {rc})")
+
     def position(self):
         off = ctypes.c_longlong(0)
         return int(self.L.dtr_loader_position(self.h, ctypes.byref(off))), int(off.value)
@@ -169,3 +184,9 @@ class SyntheticTokens:
 
     def next_batch(self) -> torch.Tensor:
         return torch.randint(0, self.vocab, (self.batch, self.seq_len), generator=self.g, dtype=torch.int32)
+
+    def state(self):
+        return {"generator": self.g.get_state()}
+
+    def restore(self, st):
+        self.g.set_state(st["generator"])

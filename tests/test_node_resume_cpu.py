@@ -1,0 +1,113 @@
+"""Node-local resume file of an HTTP node (CPU backend): a node stopped after a round boundary and
+restarted on the same checkpoint continues exactly (its next losses equal the ones the stopped node
+computed for the same steps: weights, AdamW moments and the data position were restored); restarted
+after the coordinator merged a newer checkpoint, it keeps its identity, sequence numbers, step count and
+data position and takes the new checkpoint."""
+import os
+import time
+
+import pytest
+import torch
+
+from distrain_b200.config import CompressionConfig, CoordinatorConfig, ModelConfig, OptimConfig
+from distrain_b200.coordinator.client import CoordinatorClient
+from distrain_b200.coordinator.service import CoordinatorService, bootstrap
+from distrain_b200.parallel.http_node import HttpNode
+from distrain_b200.utils.data import ShardLoader, SyntheticTokens, prepare_random_shards
+from distrain_b200.utils.storage import FsStore
+
+CFG = ModelConfig(hidden_dim=32, num_layers=1, num_heads=2, num_kv_heads=1, ffn_hidden_dim=64, vocab_size=64,
+                  max_seq_len=32, rope_theta=10000.0)
+
+
+def _service(tmp_path, min_contributions):
+    store = FsStore(str(tmp_path / "store"))
+    bootstrap(store, CFG, seed=0)
+    svc = CoordinatorService(CoordinatorConfig(min_contributions=min_contributions, outer_lr=1.0, outer_momentum=0.0),
+                             store, flush_interval=3600)
+    port = svc.start(host="127.0.0.1", port=0, threads=4)
+    return store, svc, f"http://127.0.0.1:{port}"
+
+
+def _node(url, store, data, resume, node_id=None):
+    return HttpNode(url, store, CFG, batch=2, seq_len=17, h_mini=5, optim=OptimConfig(lr=3e-3),
+                    compression=CompressionConfig(top_k_fraction=0.2), device="cpu", node_id=node_id, data=data,
+                    poll_secs=0.1, resume_path=resume)
+
+
+@pytest.mark.timeout(300)
+def test_restart_on_the_same_checkpoint_continues_exactly(tmp_path):
+    # more contributions required than there are nodes: no merge, the checkpoint stays at v0
+    store, svc, url = _service(tmp_path, min_contributions=10)
+    shards = tmp_path / "data"
+    prepare_random_shards(str(shards), 2, 20_000, CFG.vocab_size, seed=5)
+    paths = [str(shards / f"shard_{i:04d}.bin") for i in range(2)]
+    resume = str(tmp_path / "node.resume")
+    try:
+        a = _node(url, store, ShardLoader(paths, 17, 2).next_batch, resume)
+        a.register()
+        log_a = a.run(12)  # pushes after steps 5 and 10; the file holds the boundary after step 10
+        assert not a.errors and [p["seq"] for p in a.pushes] == [1, 2]
+        rec = torch.load(resume, weights_only=False)
+        assert (rec["seq"], rec["global_step"], rec["version"], rec["node_id"]) == (2, 10, 0, a.node_id)
+        assert rec["ef"] and rec["optimizer"]["t"] == 10
+        b = _node(url, store, ShardLoader(paths, 17, 2).next_batch, resume)
+        assert b.node_id == a.node_id  # identity from the file, before registering
+        b.register()
+        log_b = b.run(16)
+        assert b.resumed == "exact" and not b.errors
+        assert [x["step"] for x in log_b] == [11, 12, 13, 14, 15, 16]
+        # steps 11 and 12 repeat exactly what the stopped node computed from the same state and batches
+        assert [x["loss"] for x in log_b[:2]] == pytest.approx([x["loss"] for x in log_a[10:12]], rel=1e-6)
+        assert [p["seq"] for p in b.pushes] == [3]  # sequence numbers continue
+    finally:
+        svc.stop()
+
+
+@pytest.mark.timeout(300)
+def test_restart_after_a_newer_checkpoint_keeps_identity_and_position(tmp_path):
+    store, svc, url = _service(tmp_path, min_contributions=0)  # a single node's push is merged at once
+    resume = str(tmp_path / "node.resume")
+    try:
+        src_a = SyntheticTokens(CFG.vocab_size, 2, 17, seed=9)
+        a = _node(url, store, src_a.next_batch, resume, node_id="node-r")
+        a.register()
+        a.run(11)
+        assert not a.errors
+        cl = CoordinatorClient(url)
+        t0 = time.time()
+        while cl.get_latest_checkpoint().version < 1 and time.time() - t0 < 60:  # the merge is asynchronous
+            time.sleep(0.1)
+        latest = cl.get_latest_checkpoint().version
+        rec = torch.load(resume, weights_only=False)
+        assert latest > rec["version"] == 0
+        src_b = SyntheticTokens(CFG.vocab_size, 2, 17, seed=12345)  # restored from the file, not this seed
+        b = _node(url, store, src_b.next_batch, resume)
+        b.register()
+        assert b.node_id == "node-r"
+        want_next = SyntheticTokens(CFG.vocab_size, 2, 17, seed=9)
+        want_next.restore(rec["data"])
+        b.run(rec["global_step"] + 1)  # one more step
+        assert b.resumed == "identity" and b.version == latest and not b.errors
+        assert b.log[0]["step"] == rec["global_step"] + 1
+        want_next.next_batch()  # the one batch that step consumed
+        assert torch.equal(src_b.g.get_state(), want_next.g.get_state())
+    finally:
+        svc.stop()
+
+
+def test_loader_seek_roundtrip(tmp_path):
+    prepare_random_shards(str(tmp_path), 3, 5_000, 64, seed=1)
+    paths = [str(tmp_path / f"shard_{i:04d}.bin") for i in range(3)]
+    a = ShardLoader(paths, 16, 4)
+    for _ in range(90):  # crosses into the second shard
+        a.next_batch()
+    st = a.state()
+    assert st["shard"] == 1
+    want = a.next_batch()
+    b = ShardLoader(paths, 16, 4)
+    b.restore(st)
+    assert torch.equal(b.next_batch(), want)
+    with pytest.raises(Exception):
+        b.restore({"shard": 7, "offset": 0})
+    assert os.path.exists(paths[0])
