@@ -222,11 +222,15 @@ def cmd_train_box(args):
     import torch
     import torch.distributed as dist
     from .config import bench_config
-    from .parallel.launch import init_box, box_node, node_batches
+    from .parallel.launch import init_box, box_node, node_batches, node_layout, restore_data_state, save_data_state
     br = init_box(args.pg_timeout)
     run = apply_run_overrides(bench_config(args.preset), args)
     node, node_rank, n_nodes = box_node(run, br, enable_push=not args.no_push, tp_mode=args.tp_mode, sync=args.sync)
     source, desc = node_batches(run, node_rank, n_nodes, args.data_dir, args.shards_fraction, run.seed)
+    # with a checkpoint store every node also keeps its data position there (one writer per node)
+    dstore = _store(run.checkpoint_store) if run.checkpoint_store else None
+    data_resumed = bool(dstore is not None and run.resume and restore_data_state(dstore, node_rank, source))
+    writes_data = dstore is not None and br.rank % node_layout(br.world, run.tp)[0] == 0
     out = open(args.output, "w") if (args.output and br.rank == 0) else None
 
     def emit(rec):
@@ -237,7 +241,7 @@ def cmd_train_box(args):
                 out.flush()
     emit({"event": "train_box_start", "preset": run.name, "nodes": n_nodes, "ranks": br.world, "tp": run.tp,
           "micro_batch": run.micro_batch, "seq_len": run.seq_len, "push_every": run.push_every, "data": desc,
-          "resumed_version": getattr(node.sync, "resumed_version", 0)})
+          "resumed_version": getattr(node.sync, "resumed_version", 0), "data_resumed": data_resumed})
     done = 0
     tokens_per_step = run.micro_batch * (run.seq_len - 1) * n_nodes
     while done < args.steps:
@@ -246,6 +250,8 @@ def cmd_train_box(args):
         losses = node.train_stream(source, k)
         dt = time.time() - t0
         done += k
+        if writes_data:
+            save_data_state(dstore, node_rank, source)
         emit({"event": "train", "step": done, "loss": sum(losses) / len(losses), "last_loss": losses[-1],
               "tokens_per_sec": tokens_per_step * k / dt, "version": getattr(node.sync, "version", 0)})
         if getattr(node, "hung", None):

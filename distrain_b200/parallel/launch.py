@@ -89,3 +89,30 @@ def node_batches(run: RunConfig, node_rank: int, n_nodes: int, data_dir: Optiona
         list(range(len(files)))
     loader = ShardLoader([os.path.join(data_dir, files[i]) for i in idx], S, B, max_resident=max_resident)
     return loader.next_batch, f"{len(idx)} of {len(files)} shards ({[files[i] for i in idx][:4]}...)"
+
+
+def data_state_key(node_rank: int) -> str:
+    return f"state/box-data/node-{node_rank}.pt"
+
+
+def save_data_state(store, node_rank: int, source) -> bool:
+    """Store the read position of a node's batch source (``ShardLoader`` / ``SyntheticTokens`` bound
+    ``next_batch``) so that a resumed job continues the node's data instead of re-reading it."""
+    import io
+    src = getattr(source, "__self__", None)
+    st = src.state() if src is not None and hasattr(src, "state") else None
+    if st is None:
+        return False
+    buf = io.BytesIO()
+    torch.save(st, buf)
+    store.put(data_state_key(node_rank), buf.getvalue())
+    return True
+
+
+def restore_data_state(store, node_rank: int, source) -> bool:
+    import io
+    src = getattr(source, "__self__", None)
+    if src is None or not hasattr(src, "restore") or not store.exists(data_state_key(node_rank)):
+        return False
+    src.restore(torch.load(io.BytesIO(store.get(data_state_key(node_rank))), weights_only=False))
+    return True

@@ -104,3 +104,24 @@ def test_train_box_parser():
     with pytest.raises(SystemExit) as e:
         cli.main(["train-box", "--help"])
     assert e.value.code == 0
+
+
+def test_node_data_position_survives_a_restart(tmp_path):
+    """train-box keeps each node's data position in the checkpoint store; a resumed node continues."""
+    from distrain_b200.parallel.launch import restore_data_state, save_data_state
+    from distrain_b200.utils.storage import FsStore
+    store = FsStore(str(tmp_path / "ck"))
+    run = bench_config("micro-test")
+    run.micro_batch, run.seq_len = 2, 16
+    prepare_random_shards(str(tmp_path / "d"), num_shards=3, tokens_per_shard=2048, vocab_size=run.model.vocab_size)
+    for data_dir in (str(tmp_path / "d"), None):
+        a, _ = node_batches(run, 1, 2, data_dir, shards_fraction=0.5)
+        for _ in range(40):
+            a()
+        assert save_data_state(store, 1, a)
+        want = a()
+        b, _ = node_batches(run, 1, 2, data_dir, shards_fraction=0.5)
+        assert restore_data_state(store, 1, b)
+        assert torch.equal(b(), want)
+    c, _ = node_batches(run, 0, 2, None)
+    assert not restore_data_state(store, 0, c)  # nothing stored for node 0
