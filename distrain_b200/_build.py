@@ -36,10 +36,6 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found: the CUDA kernel library cannot be built")
 
 
-def _cuda_home() -> str:
-    return os.path.dirname(os.path.dirname(_nvcc()))
-
-
 def _newest(paths) -> float:
     return max((os.path.getmtime(p) for p in paths), default=0.0)
 

@@ -146,7 +146,8 @@ def _apply_node_config(args):
             args.h_mini = nc.min_inner_steps
     if not args.coordinator_url:
         raise SystemExit("start: --coordinator-url or a --config with coordinator_url is required")
-    args.batch_size = args.batch_size or 4
+    if args.batch_size is None and args.cpu:
+        args.batch_size = 4  # on a GPU an unset batch size is calibrated against the device (cmd_start)
     args.seq_len = args.seq_len or 512
     args.h_mini = args.h_mini or 50
 
@@ -166,6 +167,8 @@ def cmd_start(args):
         m.rope_theta = args.rope_theta
     m.max_seq_len = max(m.max_seq_len, args.seq_len)
     device = "cpu" if args.cpu else (args.device or "cuda:0")
+    if args.batch_size is None:
+        args.batch_size = _calibrated_batch(store.get(P.checkpoint_path(v)), args.seq_len, device)
     data = _data_source(args, m.vocab_size, args.batch_size, args.seq_len, args.seed)
     node = HttpNode(args.coordinator_url, store, m, args.batch_size, args.seq_len, h_mini=args.h_mini,
                     optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
@@ -429,6 +432,20 @@ def cmd_gpu_stress_test(args):
         ok = False
     print(json.dumps({"batch_size": args.batch_size, "seq_len": args.seq_len, "fits": ok}))
     sys.exit(0 if ok else 3)
+
+
+def _calibrated_batch(ckpt_bytes: bytes, seq_len: int, device: str) -> int:
+    """The largest batch that trains on this device (no batch size forced by flag or config, as the
+    reference node calibrates before it registers, main.rs:600-618)."""
+    import tempfile
+    with tempfile.NamedTemporaryFile(suffix=".safetensors") as f:
+        f.write(ckpt_bytes)
+        f.flush()
+        best = calibrate_batch_size(f.name, seq_len, device=device)
+    if best < 1:
+        raise SystemExit(f"start: not even batch 1 at seq_len {seq_len} fits on {device}")
+    print(json.dumps({"event": "batch_calibrated", "batch_size": best, "seq_len": seq_len}), flush=True)
+    return best
 
 
 def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 256, device="cuda:0") -> int:

@@ -388,11 +388,6 @@ def update_round_time(cs: CoordinatorPersistentState, node_id: str, now_secs: Op
     p.last_push_time = now_secs
 
 
-def merge_weights(contribs: List[ContributionMeta]) -> List[float]:
-    tot = sum(c.weight for c in contribs)
-    return [c.weight / tot if tot > 0 else 0.0 for c in contribs]
-
-
 def clip_scales(norms: List[float]) -> Tuple[List[float], List[float]]:
     """3x running-average norm clip in arrival order (aggregation.rs:310-328).
     Returns (scale per delta, effective norm per delta)."""

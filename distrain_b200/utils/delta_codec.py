@@ -84,23 +84,6 @@ def decode_dtz_dense(data: bytes) -> torch.Tensor:
     return torch.frombuffer(bytearray(raw), dtype=torch.float32)
 
 
-def payload_to_dtz(payload, count: int, total_params: int, zstd_level: int = 0) -> bytes:
-    """Serialise the first ``count`` entries of a device payload (DevicePayload) to DTZ1 bytes (flat int32
-    indices: layouts below 2^31 parameters; larger ones go through the per-tensor SparseDelta format)."""
-    if total_params >= 1 << 31:
-        raise ValueError("DTZ1 carries int32 flat indices; use payload_to_sparse_delta above 2^31 parameters")
-    blk = payload.block
-    if blk:
-        nb = (count + blk - 1) // blk
-        return encode_dtz(total_params, payload.idx[:count], payload.q[:count], payload.scales[:nb], None, blk,
-                          zstd_level)
-    return encode_dtz(total_params, payload.idx[:count], None, None, payload.val[:count], 0, zstd_level)
-
-
-def flat_to_named(dense: torch.Tensor, layout) -> Dict[str, torch.Tensor]:
-    return {e.name: dense[e.offset:e.offset + e.numel].clone() for e in layout.entries}
-
-
 def payload_to_sparse_delta(payload, count: int, layout, cfg: CompressionConfig) -> SparseDeltaT:
     """Device payload -> reference SparseDelta (per-tensor indices; dequantised values)."""
     idx = payload.global_indices(count).cpu()

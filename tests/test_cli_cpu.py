@@ -65,3 +65,22 @@ def test_bootstrap_eval_baseline_generate(tmp_path):
     r = run(["eval", ck, "--batches", "1", "--batch-size", "2", "--seq-len", "17", "--data-dir", str(tmp_path / "d"),
              "--device", "cpu"])
     assert r.returncode == 0, r.stderr
+
+
+def test_batch_calibration_binary_search(monkeypatch):
+    """Unset batch size on a GPU node: probes in child processes, binary search for the largest that fits."""
+    import subprocess as sp
+    from distrain_b200 import cli
+    probes = []
+
+    def fake_run(cmd, **kw):
+        b = int(cmd[cmd.index("--batch-size") + 1])
+        probes.append(b)
+        return sp.CompletedProcess(cmd, 0 if b <= 37 else 3)
+    monkeypatch.setattr(cli.subprocess, "run", fake_run)
+    assert cli.calibrate_batch_size("ck.safetensors", 512, device="cuda:0") == 37
+    assert len(probes) <= 9 and probes[0] == 128
+    probes.clear()
+    monkeypatch.setattr(cli.subprocess, "run", lambda cmd, **kw: sp.CompletedProcess(cmd, 3))
+    with pytest.raises(SystemExit):
+        cli._calibrated_batch(b"not used by the fake probe", 512, "cuda:0")
