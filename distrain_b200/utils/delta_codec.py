@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import json
-from typing import Dict, Optional
+from typing import Optional
 
 import torch
 
