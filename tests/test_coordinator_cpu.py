@@ -198,3 +198,21 @@ def test_nesterov_outer_step_golden_numbers():
     assert torch.allclose(vel["w"], torch.tensor([0.19, 0.38, 0.57], dtype=torch.float64), atol=1e-12)
     assert torch.allclose(ck["w"], torch.tensor([0.867 - 0.7 * 0.271, 1.734 - 0.7 * 0.542, 2.601 - 0.7 * 0.813],
                                                 dtype=torch.float64), atol=1e-12)
+
+
+def test_http_body_limits(service):
+    """The reference's 512 MB request-body cap (coordinator/src/main.rs:128): a larger Content-Length is
+    refused with 413 before any body is read; chunked uploads are refused with 411 (Content-Length only)."""
+    import socket
+    _, _, _, _, port = service
+
+    def raw(req: bytes) -> bytes:
+        with socket.create_connection(("127.0.0.1", port), timeout=10) as s:
+            s.sendall(req)
+            return s.recv(4096)
+    r = raw(b"PUT /upload/deltas/v0/x.delta.zst HTTP/1.1\r\nHost: c\r\nContent-Length: %d\r\n\r\n" % (600 << 20))
+    assert r.split(b"\r\n")[0].split()[1] == b"413"
+    r = raw(b"PUT /upload/deltas/v0/x.delta.zst HTTP/1.1\r\nHost: c\r\nTransfer-Encoding: chunked\r\n\r\n5\r\nhello\r\n0\r\n\r\n")
+    assert r.split(b"\r\n")[0].split()[1] == b"411"
+    r = raw(b"GET /health HTTP/1.1\r\nHost: c\r\nContent-Length: 0\r\n\r\n")  # the server keeps serving
+    assert r.split(b"\r\n")[0].split()[1] == b"200"
