@@ -221,6 +221,9 @@ class CoordinatorConfig(_Json):
     min_weight: float = 1.5
     max_storage_gb: int = 0
     external_storage_endpoint: Optional[str] = None
+    # GET /config hands nodes the object-store credentials, secret included, as the reference does
+    # (routes.rs:423-444); False withholds the secret for deployments whose nodes carry their own
+    publish_storage_secret: bool = True
 
     @classmethod
     def from_env(cls, env: Optional[Dict[str, str]] = None) -> "CoordinatorConfig":
@@ -244,6 +247,8 @@ class CoordinatorConfig(_Json):
             c.staleness_decay = float(e["STALENESS_DECAY"])
         if e.get("S3_EXTERNAL_ENDPOINT"):
             c.external_storage_endpoint = e["S3_EXTERNAL_ENDPOINT"]
+        if "PUBLISH_STORAGE_SECRET" in e:
+            c.publish_storage_secret = e["PUBLISH_STORAGE_SECRET"].strip().lower() not in ("0", "false", "no")
         return c
 
 

@@ -229,7 +229,8 @@ class CoordinatorService:
     def node_auto_config(self):
         s = self.cfg.storage
         return {"storage": {"endpoint": self.cfg.external_storage_endpoint or s.endpoint, "bucket": s.bucket,
-                            "access_key_id": s.access_key_id, "secret_access_key": s.secret_access_key,
+                            "access_key_id": s.access_key_id,
+                            "secret_access_key": s.secret_access_key if self.cfg.publish_storage_secret else "",
                             "region": s.region},
                 "training_params": TrainingParams().to_dict(), "coordinator_version": VERSION}
 

@@ -216,3 +216,20 @@ def test_http_body_limits(service):
     assert r.split(b"\r\n")[0].split()[1] == b"411"
     r = raw(b"GET /health HTTP/1.1\r\nHost: c\r\nContent-Length: 0\r\n\r\n")  # the server keeps serving
     assert r.split(b"\r\n")[0].split()[1] == b"200"
+
+
+def test_config_route_secret_can_be_withheld(service):
+    """GET /config gives nodes the storage credentials (the reference's behaviour); with
+    PUBLISH_STORAGE_SECRET=0 the secret is withheld and the rest of the reply is unchanged."""
+    from distrain_b200.config import CoordinatorConfig
+    from distrain_b200.coordinator.client import CoordinatorClient
+    svc, _, _, _, port = service
+    cl = CoordinatorClient(f"http://127.0.0.1:{port}")
+    full = cl.get_config()
+    assert full["storage"]["secret_access_key"] == svc.cfg.storage.secret_access_key != ""
+    svc.cfg.publish_storage_secret = CoordinatorConfig.from_env({"PUBLISH_STORAGE_SECRET": "0"}).publish_storage_secret
+    red = cl.get_config()
+    assert red["storage"]["secret_access_key"] == ""
+    assert {k: v for k, v in red["storage"].items() if k != "secret_access_key"} == \
+        {k: v for k, v in full["storage"].items() if k != "secret_access_key"}
+    assert CoordinatorConfig.from_env({}).publish_storage_secret is True
