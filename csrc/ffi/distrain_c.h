@@ -8,7 +8,9 @@
  * The engine runs on the Python interpreter already in the process (when the library is loaded
  * from Python) or on one the library starts on first use (when a C program links it; set
  * DT_LIBPYTHON to the libpython to load and DT_PYTHONPATH to extra module directories if the
- * defaults recorded at build time do not apply). Calls are serialised by one lock.
+ * defaults recorded at build time do not apply). Calls are serialised by one lock and take the
+ * interpreter lock themselves, so Python callers must not hold it across a call: ctypes.CDLL releases
+ * it during foreign calls (use that, not ctypes.PyDLL).
  * distrain_compute_shard_assignment and distrain_cosine_lr are native and need no interpreter. */
 #ifndef DISTRAIN_C_H
 #define DISTRAIN_C_H
