@@ -463,6 +463,21 @@ def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 2
     return best
 
 
+def cmd_export_hf(args):
+    """Checkpoint -> Hugging Face Qwen2ForCausalLM directory (config.json + model.safetensors)."""
+    from .utils.checkpoint import load_safetensors
+    from .utils.hf_export import export_hf
+    sd = load_safetensors(args.checkpoint)
+    cfg = _infer_model_config(sd)
+    if args.rope_theta:
+        cfg.rope_theta = args.rope_theta
+    if args.max_seq_len:
+        cfg.max_seq_len = args.max_seq_len
+    export_hf(sd, cfg, args.output_dir)
+    print(json.dumps({"event": "exported_hf", "output_dir": args.output_dir, "architecture": "Qwen2ForCausalLM",
+                      "model": cfg.to_dict()}))
+
+
 def cmd_prepare_data(args):
     from .utils.data import prepare_random_shards
     m = prepare_random_shards(args.output_dir, args.num_shards, args.tokens_per_shard, args.vocab, args.seed)
@@ -604,6 +619,13 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--seq-len", type=int, required=True)
     p.add_argument("--device")
     p.set_defaults(fn=cmd_gpu_stress_test)
+
+    p = sp.add_parser("export-hf", help="checkpoint -> Hugging Face Qwen2ForCausalLM directory")
+    p.add_argument("checkpoint")
+    p.add_argument("output_dir")
+    p.add_argument("--rope-theta", type=float)
+    p.add_argument("--max-seq-len", type=int)
+    p.set_defaults(fn=cmd_export_hf)
 
     p = sp.add_parser("prepare-data", help="write uint16 token shards + manifest (random test mode)")
     p.add_argument("--output-dir", required=True)
