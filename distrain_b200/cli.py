@@ -115,8 +115,13 @@ def cmd_bootstrap(args):
     if args.if_absent and store.exists(P.checkpoint_path(0)):
         print(json.dumps({"event": "bootstrap_skipped", "reason": "checkpoint v0 exists"}))
         return
-    m = _model_cfg(args.preset, args.vocab, args.seq_len, args.rope_theta)
-    L, _ = bootstrap(store, m, seed=args.seed)
+    init = None
+    if args.from_hf:
+        from .utils.hf_export import from_hf
+        init, m = from_hf(args.from_hf)
+    else:
+        m = _model_cfg(args.preset, args.vocab, args.seq_len, args.rope_theta)
+    L, _ = bootstrap(store, m, seed=args.seed, init_state=init)
     print(json.dumps({"event": "bootstrapped", "version": 0, "params": L.num_params(), "model": m.to_dict()}))
 
 
@@ -527,6 +532,7 @@ def build_parser() -> argparse.ArgumentParser:
     p = sp.add_parser("bootstrap", help="create and store checkpoint v0")
     p.add_argument("--store", help="default: the R2_* environment")
     p.add_argument("--if-absent", action="store_true", help="do nothing when checkpoint v0 already exists")
+    p.add_argument("--from-hf", help="start from a pretrained Hugging Face Qwen2-layout directory")
     p.add_argument("--preset", default="tiny")
     p.add_argument("--vocab", type=int)
     p.add_argument("--seq-len", type=int)

@@ -400,11 +400,17 @@ class CoordinatorService:
                 pass
 
 
-def bootstrap(store: ObjectStore, model_cfg, seed: int = 0, init_std: float = 0.02, vocab_override=None):
-    """Write checkpoint v0 + metadata + an empty accumulator (reference node/cli/src/main.rs:1247-1304)."""
+def bootstrap(store: ObjectStore, model_cfg, seed: int = 0, init_std: float = 0.02, vocab_override=None,
+              init_state=None):
+    """Write checkpoint v0 + metadata + an empty accumulator (reference node/cli/src/main.rs:1247-1304).
+    ``init_state``: start from these weights (e.g. an imported pretrained model) instead of a seeded init."""
     from ..models.params import ParamLayout, init_flat
     L = ParamLayout(model_cfg)
-    flat = init_flat(L, init_std, seed)
+    if init_state is not None:
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, init_state)
+    else:
+        flat = init_flat(L, init_std, seed)
     store.ensure_bucket()
     store.put(P.checkpoint_path(0), save_safetensors(L.to_state_dict(flat)))
     store.put_json(P.checkpoint_metadata_path(0), {"version": 0, "model_preset": "custom",

@@ -61,3 +61,44 @@ def export_hf(sd: Dict[str, torch.Tensor], cfg: ModelConfig, out_dir: str) -> st
     with open(os.path.join(out_dir, "model.safetensors"), "wb") as f:
         f.write(save_safetensors(to_hf_state_dict(sd, cfg)))
     return out_dir
+
+
+def from_hf(hf_dir: str):
+    """A Hugging Face ``Qwen2ForCausalLM``-layout directory (config.json + safetensors) -> (state dict in
+    this framework's layout, ModelConfig), e.g. to start training from a pretrained model. Requires tied
+    embeddings and head_dim = hidden / heads; the output scale is 1 (the final norm keeps the weight)."""
+    import glob
+    from .checkpoint import load_safetensors
+    with open(os.path.join(hf_dir, "config.json")) as f:
+        c = json.load(f)
+    if c.get("model_type") not in ("qwen2", None) and "Qwen2ForCausalLM" not in c.get("architectures", []):
+        raise ValueError(f"not a Qwen2-layout model: {c.get('model_type')}")
+    H, nh = int(c["hidden_size"]), int(c["num_attention_heads"])
+    if int(c.get("head_dim") or H // nh) * nh != H:
+        raise ValueError("head_dim * heads must equal the hidden size")
+    rope = c.get("rope_parameters") or {}
+    cfg = ModelConfig(hidden_dim=H, num_layers=int(c["num_hidden_layers"]), num_heads=nh,
+                      num_kv_heads=int(c.get("num_key_value_heads", nh)), ffn_hidden_dim=int(c["intermediate_size"]),
+                      vocab_size=int(c["vocab_size"]), max_seq_len=int(c.get("max_position_embeddings", 4096)),
+                      rope_theta=float(rope.get("rope_theta", c.get("rope_theta", 10000.0))),
+                      norm_eps=float(c.get("rms_norm_eps", 1e-6)), qkv_bias=True)
+    hf = {}
+    for f in sorted(glob.glob(os.path.join(hf_dir, "*.safetensors"))):
+        hf.update(load_safetensors(f))
+    if "lm_head.weight" in hf and not torch.equal(hf["lm_head.weight"], hf["model.embed_tokens.weight"]):
+        raise ValueError("untied output head: this architecture ties the head to the embedding")
+    if not c.get("tie_word_embeddings", True):
+        raise ValueError("tie_word_embeddings is false: this architecture ties the head to the embedding")
+    sd = {"embedding.embedding.weight": hf["model.embed_tokens.weight"].float(),
+          "embedding.output_scale": torch.ones(1), "final_norm.weight": hf["model.norm.weight"].float()}
+    for i in range(cfg.num_layers):
+        src, dst = f"model.layers.{i}", f"layers.{i}"
+        sd[f"{dst}.attn_norm.weight"] = hf[f"{src}.input_layernorm.weight"].float()
+        sd[f"{dst}.ffn_norm.weight"] = hf[f"{src}.post_attention_layernorm.weight"].float()
+        for proj in ("q_proj", "k_proj", "v_proj"):
+            sd[f"{dst}.attention.{proj}.weight"] = hf[f"{src}.self_attn.{proj}.weight"].float()
+            sd[f"{dst}.attention.{proj}.bias"] = hf[f"{src}.self_attn.{proj}.bias"].float()
+        sd[f"{dst}.attention.o_proj.weight"] = hf[f"{src}.self_attn.o_proj.weight"].float()
+        for proj in ("gate_proj", "up_proj", "down_proj"):
+            sd[f"{dst}.ffn.{proj}.weight"] = hf[f"{src}.mlp.{proj}.weight"].float()
+    return sd, cfg

@@ -55,3 +55,23 @@ def test_export_command(tmp_path, capsys):
     conf = json.loads((tmp_path / "out" / "config.json").read_text())
     assert (conf["num_attention_heads"], conf["num_key_value_heads"], conf["max_position_embeddings"]) == (4, 2, 256)
     assert (tmp_path / "out" / "model.safetensors").stat().st_size > 0
+
+
+def test_import_roundtrip_and_bootstrap_from_hf(tmp_path, capsys):
+    """Export -> import gives a model with the same logits (output scale now inside the final norm), and
+    bootstrap --from-hf writes it as checkpoint v0."""
+    from distrain_b200.utils.checkpoint import load_safetensors_bytes
+    from distrain_b200.utils.hf_export import from_hf
+    from distrain_b200.utils.storage import FsStore
+    from distrain_b200 import protocol as P
+    cfg = preset("micro")
+    sd = _weights(cfg, 6)
+    export_hf(sd, cfg, str(tmp_path / "hf"))
+    back, cfg2 = from_hf(str(tmp_path / "hf"))
+    assert (cfg2.num_heads, cfg2.num_kv_heads, cfg2.hidden_dim, cfg2.rope_theta) == \
+        (cfg.num_heads, cfg.num_kv_heads, cfg.hidden_dim, cfg.rope_theta)
+    ids = torch.randint(0, cfg.vocab_size, (2, 20), generator=torch.Generator().manual_seed(2))
+    assert torch.allclose(oracle.logits_fn(back, cfg2, ids), oracle.logits_fn(sd, cfg, ids), atol=1e-5, rtol=1e-5)
+    cli.main(["bootstrap", "--store", str(tmp_path / "store"), "--from-hf", str(tmp_path / "hf")])
+    v0 = load_safetensors_bytes(FsStore(str(tmp_path / "store")).get(P.checkpoint_path(0)))
+    assert all(torch.equal(v0[k], back[k]) for k in back)
