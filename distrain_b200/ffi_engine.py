@@ -117,8 +117,9 @@ class FfiEngine:
         if batch_size < 1 or seq_len < 2:
             raise ValueError("batch_size >= 1 and seq_len >= 2 are required")
         self.loader = ShardLoader([str(p) for p in paths], int(seq_len), int(batch_size))
-        if (self.batch, self.seq) != (batch_size, seq_len) and self.backend is not None:
-            state = self._state()  # the GPU engine is built for one batch shape
+        from .parallel.http_node import CudaBackend
+        if (self.batch, self.seq) != (batch_size, seq_len) and isinstance(self.backend, CudaBackend):
+            state = self._state()  # the GPU engine is built for one batch shape (the CPU model is not)
             self.backend = None
             self.params = state
         self.batch, self.seq = int(batch_size), int(seq_len)
