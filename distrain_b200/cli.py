@@ -174,15 +174,18 @@ def cmd_start(args):
     device = "cpu" if args.cpu else (args.device or "cuda:0")
     if args.batch_size is None:
         args.batch_size = _calibrated_batch(store.get(P.checkpoint_path(v)), args.seq_len, device)
-    data = _data_source(args, m.vocab_size, args.batch_size, args.seq_len, args.seed)
-    node = HttpNode(args.coordinator_url, store, m, args.batch_size, args.seq_len, h_mini=args.h_mini,
-                    optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
-                                                                                 quantize_int8=not args.no_int8),
-                    device=device, node_id=args.node_id, data=data, poll_secs=args.poll_secs,
-                    bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
-                    resume_every=args.resume_every)
-    node.register(gpu_model="cpu" if device == "cpu" else "B200")
-    log = node.run(args.steps)
+
+    def make(batch, node_id):
+        data = _data_source(args, m.vocab_size, batch, args.seq_len, args.seed)
+        node = HttpNode(args.coordinator_url, store, m, batch, args.seq_len, h_mini=args.h_mini,
+                        optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
+                                                                                     quantize_int8=not args.no_int8),
+                        device=device, node_id=node_id, data=data, poll_secs=args.poll_secs,
+                        bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
+                        resume_every=args.resume_every)
+        node.register(gpu_model="cpu" if device == "cpu" else "B200")
+        return node
+    node, log = run_with_oom_halving(make, args.batch_size, args.steps, args.node_id)
     out = {"event": "node_done", "node_id": node.node_id, "steps": len(log), "version": node.version,
            "resumed": node.resumed, "global_step": node.global_step,
            "first_loss": log[0]["loss"] if log else None, "last_loss": log[-1]["loss"] if log else None,
@@ -192,6 +195,27 @@ def cmd_start(args):
             for r in log:
                 f.write(json.dumps(r) + "\n")
     print(json.dumps(out), flush=True)
+
+
+def run_with_oom_halving(make, batch: int, steps: int, node_id=None):
+    """Build a node at `batch` and train; on a device out-of-memory error rebuild it at half the batch under
+    the same identity (its resume file carries it on), down to batch 1, after which the error stands
+    (reference main.rs:790-827, continuous.rs:919-934). Returns (node, log)."""
+    import torch
+    while True:
+        node = None
+        try:
+            node = make(batch, node_id)
+            return node, node.run(steps)
+        except torch.cuda.OutOfMemoryError:
+            if node is not None:
+                node_id = node.node_id
+            if batch <= 1:
+                raise
+            batch //= 2
+            if torch.cuda.is_available():
+                torch.cuda.empty_cache()
+            print(json.dumps({"event": "oom_halved_batch", "batch_size": batch}), flush=True)
 
 
 def apply_run_overrides(run, args):

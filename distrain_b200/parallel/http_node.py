@@ -31,6 +31,7 @@ from ..models.params import ParamLayout
 from ..utils.checkpoint import load_safetensors_bytes
 from ..utils.delta_codec import encode_sparse_delta
 from .compression import adaptive_top_k, compress_reference  # noqa: F401 (adaptive_top_k re-exported)
+from ..utils.resources import memory_pressure
 from ..utils.watchdog import StepWatchdog, watchdog_limit
 
 
@@ -120,7 +121,7 @@ class HttpNode:
                  poll_secs: float = 5.0, use_upload_proxy: bool = False, bandwidth_adaptive: bool = False,
                  heartbeat_every: int = 10, loss_based_lr: Optional[bool] = None,
                  expected_step_secs: Optional[float] = None, resume_path: Optional[str] = None,
-                 resume_every: int = 1):
+                 resume_every: int = 1, max_memory_fraction: float = 0.80):
         self.client = CoordinatorClient(coordinator_url)
         self.store = store
         self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
@@ -153,6 +154,7 @@ class HttpNode:
         self._threads: List[threading.Thread] = []
         # node-local resume file: written by the uploader after every `resume_every`-th full-round push
         self.resume_path, self.resume_every = resume_path, max(int(resume_every), 1)
+        self.max_memory_fraction = max_memory_fraction  # host memory: stop above this + 10 % used
         self.resumed: Optional[str] = None   # "exact" (same checkpoint: weights, AdamW, EF restored) / "identity"
         self._resume_rec = self._read_resume()
         if self.node_id is None and self._resume_rec is not None:
@@ -362,6 +364,10 @@ class HttpNode:
                 self.log.append({"step": self.global_step, "loss": loss, "version": self.version, "lr": lr})
                 if self.global_step % self.hb_every == 0:
                     threading.Thread(target=self._heartbeat, args=(round_step, loss), daemon=True).start()
+                    if memory_pressure(self.max_memory_fraction):  # reference main.rs:723-734
+                        self.errors.append(f"host memory pressure: above {self.max_memory_fraction + 0.1:.0%} used; "
+                                           "stopping")
+                        break
         finally:
             if wd is not None:
                 wd.close()

@@ -84,3 +84,37 @@ def test_batch_calibration_binary_search(monkeypatch):
     monkeypatch.setattr(cli.subprocess, "run", lambda cmd, **kw: sp.CompletedProcess(cmd, 3))
     with pytest.raises(SystemExit):
         cli._calibrated_batch(b"not used by the fake probe", 512, "cuda:0")
+
+
+def test_oom_halves_the_batch_under_the_same_identity():
+    import torch
+    from distrain_b200 import cli
+    built = []
+
+    class FakeNode:
+        def __init__(self, batch, node_id):
+            self.batch, self.node_id = batch, node_id or "assigned-id"
+            built.append((batch, self.node_id))
+
+        def run(self, steps):
+            if self.batch > 5:
+                raise torch.cuda.OutOfMemoryError("fake")
+            return [{"step": 1}]
+    node, log = cli.run_with_oom_halving(FakeNode, 32, 10)
+    assert [b for b, _ in built] == [32, 16, 8, 4] and node.batch == 4 and log == [{"step": 1}]
+    assert {i for _, i in built} == {"assigned-id"}
+    built.clear()
+
+    class AlwaysOom(FakeNode):
+        def run(self, steps):
+            raise torch.cuda.OutOfMemoryError("fake")
+    with pytest.raises(torch.cuda.OutOfMemoryError):
+        cli.run_with_oom_halving(AlwaysOom, 4, 10)
+    assert [b for b, _ in built] == [4, 2, 1]
+
+
+def test_host_memory_pressure_rule():
+    from distrain_b200.utils.resources import host_memory_fraction, memory_pressure
+    assert 0.0 <= host_memory_fraction() <= 1.0
+    assert memory_pressure(0.80, used_fraction=0.91) and not memory_pressure(0.80, used_fraction=0.89)
+    assert not memory_pressure(0.95, used_fraction=0.999)  # threshold capped at 100 %

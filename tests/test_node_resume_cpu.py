@@ -111,3 +111,17 @@ def test_loader_seek_roundtrip(tmp_path):
     with pytest.raises(Exception):
         b.restore({"shard": 7, "offset": 0})
     assert os.path.exists(paths[0])
+
+
+@pytest.mark.timeout(300)
+def test_node_stops_under_host_memory_pressure(tmp_path, monkeypatch):
+    from distrain_b200.parallel import http_node
+    store, svc, url = _service(tmp_path, min_contributions=10)
+    try:
+        monkeypatch.setattr(http_node, "memory_pressure", lambda frac: True)
+        n = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=1).next_batch, None)
+        n.register()
+        log = n.run(50)
+        assert len(log) == 10 and any("host memory pressure" in e for e in n.errors)  # checked every 10 steps
+    finally:
+        svc.stop()
