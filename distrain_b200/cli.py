@@ -132,6 +132,7 @@ def _apply_node_config(args):
     file the storage comes from the R2_* environment."""
     from .config import CoordinatorConfig, NodeConfig
     nc = NodeConfig.load_toml(args.config) if args.config else None
+    args.max_memory_fraction = nc.max_memory_fraction if nc is not None else NodeConfig().max_memory_fraction
     if nc is None:
         args.storage_cfg = CoordinatorConfig.from_env().storage
     else:
@@ -182,7 +183,7 @@ def cmd_start(args):
                                                                                      quantize_int8=not args.no_int8),
                         device=device, node_id=node_id, data=data, poll_secs=args.poll_secs,
                         bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
-                        resume_every=args.resume_every)
+                        resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction)
         node.register(gpu_model="cpu" if device == "cpu" else "B200")
         return node
     node, log = run_with_oom_halving(make, args.batch_size, args.steps, args.node_id)
