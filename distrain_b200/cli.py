@@ -478,15 +478,21 @@ def _calibrated_batch(ckpt_bytes: bytes, seq_len: int, device: str) -> int:
     return best
 
 
-def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 256, device="cuda:0") -> int:
+def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 256, device="cuda:0",
+                         probe_timeout: float = 300.0) -> int:
     """Binary search of the largest batch that fits, each probe in a child process so an out-of-memory
     failure cannot take down the caller (reference trainer.rs:733-834)."""
     best = 0
     while lo <= hi:
         mid = (lo + hi) // 2
-        r = subprocess.run([sys.executable, "-m", "distrain_b200", "gpu-stress-test", checkpoint, "--batch-size",
-                            str(mid), "--seq-len", str(seq_len), "--device", device], capture_output=True)
-        if r.returncode == 0:
+        try:  # a probe that does not finish in time counts as not fitting (reference trainer.rs:322-359)
+            r = subprocess.run([sys.executable, "-m", "distrain_b200", "gpu-stress-test", checkpoint, "--batch-size",
+                                str(mid), "--seq-len", str(seq_len), "--device", device], capture_output=True,
+                               timeout=probe_timeout)
+            ok = r.returncode == 0
+        except subprocess.TimeoutExpired:
+            ok = False
+        if ok:
             best, lo = mid, mid + 1
         else:
             hi = mid - 1

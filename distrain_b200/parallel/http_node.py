@@ -227,8 +227,22 @@ class HttpNode:
         self.bandwidth_bps = len(blob) / secs
         self.recommended_h_mini = int(min(max(10.0 / secs * push.inner_steps, 10), 500))
         push.compressed_bytes, push.dense_norm, push.sparse_norm = len(blob), stats["dense_norm"], stats["sparse_norm"]
-        resp = self.client.push_delta(push)
-        self.pushes.append({"seq": push.seq_num, "version": push.checkpoint_version, "accepted": resp.accepted,
+        resp, accepted = None, False
+        for attempt in range(5):   # push retries with backoff (continuous.rs:284-311)
+            try:
+                resp = self.client.push_delta(push)
+                accepted = resp.accepted
+                # a retry whose earlier attempt landed (reply lost) meets the coordinator's dedup by sequence
+                # number: that push was delivered
+                if not accepted and attempt > 0 and (resp.reason or "").startswith(
+                        f"Duplicate: existing seq_num {push.seq_num} >="):
+                    accepted = True
+                break
+            except Exception:
+                if attempt == 4:
+                    raise
+                time.sleep(2 ** attempt * 0.1)
+        self.pushes.append({"seq": push.seq_num, "version": push.checkpoint_version, "accepted": accepted,
                             "reason": resp.reason, "bytes": len(blob), "retention": stats["retention_ratio"],
                             "top_k": cfg.top_k_fraction})
         if snap is not None:

@@ -118,3 +118,17 @@ def test_host_memory_pressure_rule():
     assert 0.0 <= host_memory_fraction() <= 1.0
     assert memory_pressure(0.80, used_fraction=0.91) and not memory_pressure(0.80, used_fraction=0.89)
     assert not memory_pressure(0.95, used_fraction=0.999)  # threshold capped at 100 %
+
+
+def test_calibration_probe_timeout_counts_as_not_fitting(monkeypatch):
+    import subprocess as sp
+    from distrain_b200 import cli
+
+    def fake_run(cmd, **kw):
+        assert kw["timeout"] == 300.0
+        b = int(cmd[cmd.index("--batch-size") + 1])
+        if b > 10:
+            raise sp.TimeoutExpired(cmd, kw["timeout"])
+        return sp.CompletedProcess(cmd, 0)
+    monkeypatch.setattr(cli.subprocess, "run", fake_run)
+    assert cli.calibrate_batch_size("ck", 128) == 10
