@@ -74,6 +74,22 @@ def _infer_model_config(sd):
                        vocab_size=V, qkv_bias=bias)
 
 
+def _store_data_source(store, node_id: str, batch: int, seq: int, cache_dir: str):
+    """The reference node's data path (node/cli/src/continuous.rs:796-826): the shards listed in the store's
+    data/manifest.json, this node's share by the deterministic assignment (node id, version 0: fixed
+    across checkpoints), fetched into a local cache and read sequentially. None when the store has no
+    manifest."""
+    from . import protocol as P
+    from .config import TrainingParams
+    from .utils.data import StreamingLoader
+    from .utils.native import shard_assignment
+    if not store.exists(P.manifest_path()):
+        return None
+    total = len(store.get_json(P.manifest_path())["shards"])
+    idx = shard_assignment(node_id, 0, total, TrainingParams().shards_per_node(total))
+    return StreamingLoader(store, cache_dir, idx, seq, batch, max_resident=4, prefetch=0).next_batch
+
+
 def _data_source(args, vocab, batch, seq, seed):
     if getattr(args, "data_dir", None):
         from .utils.data import ShardLoader
@@ -150,6 +166,8 @@ def _apply_node_config(args):
             args.seq_len = nc.seq_len
         if args.h_mini is None and nc.min_inner_steps:
             args.h_mini = nc.min_inner_steps
+        if getattr(args, "cache_dir", None) is None and nc.cache_dir:
+            args.cache_dir = os.path.expanduser(nc.cache_dir)
     if not args.coordinator_url:
         raise SystemExit("start: --coordinator-url or a --config with coordinator_url is required")
     if args.batch_size is None and args.cpu:
@@ -177,14 +195,19 @@ def cmd_start(args):
         args.batch_size = _calibrated_batch(store.get(P.checkpoint_path(v)), args.seq_len, device)
 
     def make(batch, node_id):
-        data = _data_source(args, m.vocab_size, batch, args.seq_len, args.seed)
         node = HttpNode(args.coordinator_url, store, m, batch, args.seq_len, h_mini=args.h_mini,
                         optim=OptimConfig(lr=args.lr), compression=CompressionConfig(top_k_fraction=args.top_k,
                                                                                      quantize_int8=not args.no_int8),
-                        device=device, node_id=node_id, data=data, poll_secs=args.poll_secs,
+                        device=device, node_id=node_id, data=None, poll_secs=args.poll_secs,
                         bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
                         resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction)
         node.register(gpu_model="cpu" if device == "cpu" else "B200")
+        # data: local shards (--data-dir), else this node's assigned shards from the store, else synthetic
+        node.data = None if args.data_dir or args.synthetic_data else _store_data_source(
+            store, node.node_id, batch, args.seq_len, args.cache_dir or os.path.join(
+                os.path.expanduser("~"), ".distrain", "cache", node.node_id))
+        if node.data is None:
+            node.data = _data_source(args, m.vocab_size, batch, args.seq_len, args.seed)
         return node
     node, log = run_with_oom_halving(make, args.batch_size, args.steps, args.node_id)
     out = {"event": "node_done", "node_id": node.node_id, "steps": len(log), "version": node.version,
@@ -592,6 +615,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--rope-theta", type=float)
     p.add_argument("--poll-secs", type=float, default=5.0)
     p.add_argument("--metrics-out")
+    p.add_argument("--cache-dir", help="shard cache for data streamed from the store (default ~/.distrain/cache/<id>)")
+    p.add_argument("--synthetic-data", action="store_true", help="uniform random tokens even if the store has data")
     p.add_argument("--resume-file", help="node-local resume file: written at round boundaries, read at start "
                                          "(same checkpoint: weights, AdamW and error feedback continue; newer: "
                                          "identity, step count and data position continue)")

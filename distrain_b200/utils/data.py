@@ -171,6 +171,12 @@ class StreamingLoader:
     def next_batch(self):
         return self.loader.next_batch()
 
+    def state(self):
+        return self.loader.state()
+
+    def restore(self, st):
+        self.loader.restore(st)
+
     def close(self):
         self.loader.close()
 

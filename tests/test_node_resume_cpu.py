@@ -125,3 +125,28 @@ def test_node_stops_under_host_memory_pressure(tmp_path, monkeypatch):
         assert len(log) == 10 and any("host memory pressure" in e for e in n.errors)  # checked every 10 steps
     finally:
         svc.stop()
+
+
+@pytest.mark.timeout(300)
+def test_start_streams_the_nodes_assigned_shards_from_the_store(tmp_path, capsys):
+    """`start` without --data-dir reads the shards that the deterministic assignment gives this node id
+    from the store's data/ prefix (fetched into its cache), like the reference node."""
+    import json
+    from distrain_b200 import cli
+    from distrain_b200.config import TrainingParams
+    from distrain_b200.utils.native import shard_assignment
+    store, svc, url = _service(tmp_path, min_contributions=10)
+    try:
+        cli.main(["prepare-data", "--output-dir", str(tmp_path / "prep"), "--num-shards", "10",
+                  "--tokens-per-shard", "5000", "--vocab", str(CFG.vocab_size), "--upload-store",
+                  str(tmp_path / "store")])
+        cache = tmp_path / "cache"
+        cli.main(["start", "--coordinator-url", url, "--store", str(tmp_path / "store"), "--cpu", "--steps", "6",
+                  "--batch-size", "2", "--seq-len", "17", "--h-mini", "5", "--node-id", "streamer",
+                  "--cache-dir", str(cache), "--poll-secs", "0.2"])
+        out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert out["event"] == "node_done" and out["steps"] == 6 and not out["errors"]
+        want = shard_assignment("streamer", 0, 10, TrainingParams().shards_per_node(10))
+        assert sorted(os.listdir(cache)) == sorted(f"shard_{i:04d}.bin" for i in want)
+    finally:
+        svc.stop()
