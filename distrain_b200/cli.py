@@ -166,6 +166,8 @@ def _apply_node_config(args):
             args.seq_len = nc.seq_len
         if args.h_mini is None and nc.min_inner_steps:
             args.h_mini = nc.min_inner_steps
+        if args.h_mini_bounds is None:
+            args.h_mini_bounds = (nc.min_inner_steps, nc.max_inner_steps)
         if getattr(args, "cache_dir", None) is None and nc.cache_dir:
             args.cache_dir = os.path.expanduser(nc.cache_dir)
     if not args.coordinator_url:
@@ -200,7 +202,8 @@ def cmd_start(args):
                                                                                      quantize_int8=not args.no_int8),
                         device=device, node_id=node_id, data=None, poll_secs=args.poll_secs,
                         bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
-                        resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction)
+                        resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction,
+                        h_mini_bounds=args.h_mini_bounds)
         node.register(gpu_model="cpu" if device == "cpu" else "B200")
         # data: local shards (--data-dir), else this node's assigned shards from the store, else synthetic
         node.data = None if args.data_dir or args.synthetic_data else _store_data_source(
@@ -616,6 +619,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--poll-secs", type=float, default=5.0)
     p.add_argument("--metrics-out")
     p.add_argument("--cache-dir", help="shard cache for data streamed from the store (default ~/.distrain/cache/<id>)")
+    p.add_argument("--auto-h-mini", dest="h_mini_bounds", type=lambda v: tuple(int(x) for x in v.split(",")),
+                   help="MIN,MAX: retune the steps per push at each checkpoint from the upload bandwidth "
+                        "(default with --config: its min/max_inner_steps)")
     p.add_argument("--synthetic-data", action="store_true", help="uniform random tokens even if the store has data")
     p.add_argument("--resume-file", help="node-local resume file: written at round boundaries, read at start "
                                          "(same checkpoint: weights, AdamW and error feedback continue; newer: "

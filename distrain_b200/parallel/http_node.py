@@ -121,7 +121,8 @@ class HttpNode:
                  poll_secs: float = 5.0, use_upload_proxy: bool = False, bandwidth_adaptive: bool = False,
                  heartbeat_every: int = 10, loss_based_lr: Optional[bool] = None,
                  expected_step_secs: Optional[float] = None, resume_path: Optional[str] = None,
-                 resume_every: int = 1, max_memory_fraction: float = 0.80):
+                 resume_every: int = 1, max_memory_fraction: float = 0.80,
+                 h_mini_bounds: Optional[tuple] = None):
         self.client = CoordinatorClient(coordinator_url)
         self.store = store
         self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
@@ -155,6 +156,9 @@ class HttpNode:
         # node-local resume file: written by the uploader after every `resume_every`-th full-round push
         self.resume_path, self.resume_every = resume_path, max(int(resume_every), 1)
         self.max_memory_fraction = max_memory_fraction  # host memory: stop above this + 10 % used
+        # (min, max) inner steps: at each checkpoint swap the push interval follows the bandwidth-based
+        # recommendation (steps whose delta uploads in ~10 s), clamped to these bounds (continuous.rs:936-945)
+        self.h_mini_bounds = h_mini_bounds
         self.resumed: Optional[str] = None   # "exact" (same checkpoint: weights, AdamW, EF restored) / "identity"
         self._resume_rec = self._read_resume()
         if self.node_id is None and self._resume_rec is not None:
@@ -349,6 +353,9 @@ class HttpNode:
                     self.backend.load(sd)          # fresh AdamW, like the reference's re-entered loop
                     self._ef_gen += 1
                     self.version = v
+                    if self.h_mini_bounds is not None:
+                        lo, hi = self.h_mini_bounds
+                        self.h_mini = int(min(max(self.recommended_h_mini, lo), hi))
                     start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
                     if stop_on_version is not None and v >= stop_on_version:
                         break

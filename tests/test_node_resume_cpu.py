@@ -150,3 +150,27 @@ def test_start_streams_the_nodes_assigned_shards_from_the_store(tmp_path, capsys
         assert sorted(os.listdir(cache)) == sorted(f"shard_{i:04d}.bin" for i in want)
     finally:
         svc.stop()
+
+
+@pytest.mark.timeout(300)
+def test_push_interval_follows_the_bandwidth_recommendation(tmp_path):
+    """With (min, max) inner-step bounds the push interval is retuned at each checkpoint swap from the
+    upload rate (steps that upload in ~10 s); local uploads are fast, so it rises to the maximum."""
+    store, svc, url = _service(tmp_path, min_contributions=0)
+    try:
+        n = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=3).next_batch, None, node_id="tuned")
+        n.h_mini_bounds = (5, 8)
+        n.register()
+        n.run(40)
+        assert not n.errors and n.version >= 1
+        assert n.recommended_h_mini >= 8 and n.h_mini == 8
+        assert any(e["inner_steps"] == 8 for e in _accepted(store, "tuned"))  # rounds of 8 steps after a swap
+    finally:
+        svc.stop()
+
+
+def _accepted(store, node_id):
+    import json
+    from distrain_b200 import protocol as P
+    raw = store.get(P.stats_history_path()).decode()
+    return [e for e in map(json.loads, raw.splitlines()) if e["event"] == "delta_accepted" and e["node_id"] == node_id]
