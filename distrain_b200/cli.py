@@ -74,6 +74,23 @@ def _infer_model_config(sd):
                        vocab_size=V, qkv_bias=bias)
 
 
+def _saved_node_id(cache_dir):
+    """The identity this node registered with before (kept in its cache directory, reference
+    main.rs:251-260), so a restarted node is the same node to the coordinator."""
+    path = os.path.join(cache_dir, "node_id") if cache_dir else None
+    if path and os.path.exists(path):
+        with open(path) as f:
+            return f.read().strip() or None
+    return None
+
+
+def _save_node_id(cache_dir, node_id):
+    if cache_dir and node_id:
+        os.makedirs(cache_dir, exist_ok=True)
+        with open(os.path.join(cache_dir, "node_id"), "w") as f:
+            f.write(node_id)
+
+
 def _store_data_source(store, node_id: str, batch: int, seq: int, cache_dir: str):
     """The reference node's data path (node/cli/src/continuous.rs:796-826): the shards listed in the store's
     data/manifest.json, this node's share by the deterministic assignment (node id, version 0: fixed
@@ -205,6 +222,7 @@ def cmd_start(args):
                         resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction,
                         h_mini_bounds=args.h_mini_bounds)
         node.register(gpu_model="cpu" if device == "cpu" else "B200")
+        _save_node_id(args.cache_dir, node.node_id)
         # data: local shards (--data-dir), else this node's assigned shards from the store, else synthetic
         node.data = None if args.data_dir or args.synthetic_data else _store_data_source(
             store, node.node_id, batch, args.seq_len, args.cache_dir or os.path.join(
@@ -212,7 +230,7 @@ def cmd_start(args):
         if node.data is None:
             node.data = _data_source(args, m.vocab_size, batch, args.seq_len, args.seed)
         return node
-    node, log = run_with_oom_halving(make, args.batch_size, args.steps, args.node_id)
+    node, log = run_with_oom_halving(make, args.batch_size, args.steps, args.node_id or _saved_node_id(args.cache_dir))
     out = {"event": "node_done", "node_id": node.node_id, "steps": len(log), "version": node.version,
            "resumed": node.resumed, "global_step": node.global_step,
            "first_loss": log[0]["loss"] if log else None, "last_loss": log[-1]["loss"] if log else None,

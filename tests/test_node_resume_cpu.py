@@ -147,7 +147,12 @@ def test_start_streams_the_nodes_assigned_shards_from_the_store(tmp_path, capsys
         out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
         assert out["event"] == "node_done" and out["steps"] == 6 and not out["errors"]
         want = shard_assignment("streamer", 0, 10, TrainingParams().shards_per_node(10))
-        assert sorted(os.listdir(cache)) == sorted(f"shard_{i:04d}.bin" for i in want)
+        assert sorted(f for f in os.listdir(cache) if f.endswith(".bin")) == sorted(f"shard_{i:04d}.bin" for i in want)
+        # a restart without --node-id takes the identity kept in the cache directory
+        cli.main(["start", "--coordinator-url", url, "--store", str(tmp_path / "store"), "--cpu", "--steps", "3",
+                  "--batch-size", "2", "--seq-len", "17", "--h-mini", "5", "--cache-dir", str(cache),
+                  "--poll-secs", "0.2"])
+        assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["node_id"] == "streamer"
     finally:
         svc.stop()
 
