@@ -262,6 +262,20 @@ class CoordinatorService:
         return P.HeartbeatResponse(active_nodes=active, should_abort=abort, latest_version=cur).to_dict()
 
     # ─────────── stats JSONL (stats.rs:51-77, read-modify-write) ───────────
+    def _save_outer_lr_state(self, outer_lr: float, delta_norm: float):
+        """state/outer_lr.json: the applied outer lr and momentum and the last 10 merged-delta norms
+        (the reference's OuterLrState, aggregation.rs:120-127, 214-218, 360-365)."""
+        try:
+            try:
+                st = self.store.get_json(P.outer_lr_state_path())
+            except Exception:
+                st = {}
+            norms = (list(st.get("recent_norms", [])) + [float(delta_norm)])[-10:]
+            self.store.put_json(P.outer_lr_state_path(), {"outer_lr": outer_lr, "outer_momentum": 0.0,
+                                                          "recent_norms": norms})
+        except Exception as e:  # the reference only warns when this write fails
+            log.warning("outer lr state not saved: %s", e)
+
     def _append_stats(self, entry: dict):
         try:
             try:
@@ -338,8 +352,12 @@ class CoordinatorService:
                 deltas = [{k: v.to(dev) for k, v in d.items()} for d in deltas]
                 if velocity is not None:
                     velocity = {k: v.to(dev) for k, v in velocity.items()}
-            # reference forces outer lr 1.0 and momentum 0 (aggregation.rs:141-144, 364)
-            new, velocity, info = merge_reference(flat_ck, deltas, weights, velocity=velocity, outer_lr=1.0,
+            # outer lr: 1.0 once the contributions report a training loss, the configured initial value
+            # before that; momentum 0 (aggregation.rs:141-144, 181-214, 364)
+            lw = sum(c.weight for c in snap.contributions)
+            avg_loss = sum(c.training_loss * c.weight for c in snap.contributions) / lw if lw > 0 else 0.0
+            outer_lr = 1.0 if avg_loss > 0 else float(self.cfg.outer_lr)
+            new, velocity, info = merge_reference(flat_ck, deltas, weights, velocity=velocity, outer_lr=outer_lr,
                                                   outer_momentum=0.0)
             rejected += info["rejected"]
             out = {k: new[k].reshape(shapes[k]).cpu() for k in new}
@@ -354,7 +372,8 @@ class CoordinatorService:
             self.store.put_json(P.checkpoint_metadata_path(new_version), {
                 "version": new_version, "contributions_accepted": info["accepted"], "contributions_rejected": rejected,
                 "total_weight": total_weight, "outer_delta_norm": info["outer_delta_norm"],
-                "aggregation_time_secs": elapsed, "outer_lr": 1.0})
+                "aggregation_time_secs": elapsed, "outer_lr": outer_lr})
+            self._save_outer_lr_state(outer_lr, info["outer_delta_norm"])
             st_hist: Dict[int, int] = {}
             for c in meta:
                 s = max(snap.checkpoint_version - c.checkpoint_version, 0)
@@ -362,7 +381,7 @@ class CoordinatorService:
             self._append_stats({"event": "checkpoint_produced", "timestamp": P.to_rfc3339(P.utcnow()),
                                 "version": new_version, "contributions": info["accepted"],
                                 "total_weight": total_weight, "outer_delta_norm": info["outer_delta_norm"],
-                                "aggregation_time_secs": elapsed, "outer_lr": 1.0,
+                                "aggregation_time_secs": elapsed, "outer_lr": outer_lr,
                                 "avg_loss": sum(c.training_loss for c in meta) / max(len(meta), 1),
                                 "total_tokens": sum(c.tokens_processed for c in meta),
                                 "staleness_histogram": sorted(st_hist.items()),

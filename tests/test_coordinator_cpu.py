@@ -233,3 +233,48 @@ def test_config_route_secret_can_be_withheld(service):
     assert {k: v for k, v in red["storage"].items() if k != "secret_access_key"} == \
         {k: v for k, v in full["storage"].items() if k != "secret_access_key"}
     assert CoordinatorConfig.from_env({}).publish_storage_secret is True
+
+
+def test_outer_lr_before_and_after_a_reported_loss(tmp_path):
+    """The merged delta is applied unscaled once contributions report a training loss; with no loss reported
+    the configured initial outer lr applies. state/outer_lr.json keeps the applied lr and the last norms."""
+    import time as _time
+    from distrain_b200.config import CompressionConfig, CoordinatorConfig, ModelConfig
+    from distrain_b200.coordinator.client import CoordinatorClient
+    from distrain_b200.coordinator.service import CoordinatorService, bootstrap
+    from distrain_b200.parallel.compression import compress_reference
+    from distrain_b200.utils.checkpoint import load_safetensors_bytes
+    from distrain_b200.utils.delta_codec import decode_delta, encode_sparse_delta
+    import torch
+    store = FsStore(str(tmp_path))
+    cfg = ModelConfig(hidden_dim=32, num_layers=1, num_heads=2, num_kv_heads=1, ffn_hidden_dim=64, vocab_size=64)
+    layout, flat = bootstrap(store, cfg, seed=0)
+    svc = CoordinatorService(CoordinatorConfig(min_contributions=0, outer_lr=0.25), store, flush_interval=3600)
+    port = svc.start(host="127.0.0.1", port=0, threads=4)
+    cl = CoordinatorClient(f"http://127.0.0.1:{port}")
+    try:
+        cl.register(P.RegisterRequest(gpu_model="cpu", gpu_memory_gb=0.0, bandwidth_mbps=0.0, node_id="n"))
+        cl.heartbeat(P.HeartbeatRequest(node_id="n", checkpoint_version=0))  # the one active node
+        for v, loss, want_lr in ((0, 0.0, 0.25), (1, 3.5, 1.0)):
+            ck = load_safetensors_bytes(store.get(P.checkpoint_path(v)))
+            g = torch.Generator().manual_seed(v)
+            delta = {k: torch.randn(t.numel(), generator=g) * 1e-3 for k, t in ck.items()}
+            sd, _ = compress_reference(delta, {k: list(t.shape) for k, t in ck.items()},
+                                       CompressionConfig(top_k_fraction=0.3), {})
+            blob = encode_sparse_delta(sd)
+            cl.upload(P.delta_path(v, "n", v + 1), blob)
+            assert cl.push_delta(P.DeltaPush(node_id="n", seq_num=v + 1, checkpoint_version=v, inner_steps=10,
+                                             delta_key=P.delta_path(v, "n", v + 1), training_loss=loss,
+                                             tokens_processed=100, training_time_secs=1.0)).accepted
+            t0 = _time.time()
+            while cl.get_latest_checkpoint().version < v + 1 and _time.time() - t0 < 30:
+                _time.sleep(0.05)
+            new = load_safetensors_bytes(store.get(P.checkpoint_path(v + 1)))
+            dec = decode_delta(blob)
+            for k in ck:
+                assert torch.allclose(new[k].reshape(-1), ck[k].reshape(-1) - want_lr * dec[k].reshape(-1), atol=1e-7)
+            st = store.get_json(P.outer_lr_state_path())
+            assert st["outer_lr"] == want_lr and st["outer_momentum"] == 0.0 and len(st["recent_norms"]) == v + 1
+            assert json.loads(store.get(P.checkpoint_metadata_path(v + 1)))["outer_lr"] == want_lr
+    finally:
+        svc.stop()
