@@ -166,7 +166,7 @@ def test_push_interval_follows_the_bandwidth_recommendation(tmp_path):
         n = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=3).next_batch, None, node_id="tuned")
         n.h_mini_bounds = (5, 8)
         n.register()
-        n.run(400)  # CPU steps are far faster than a merge round trip: leave room for swaps and 8-step rounds
+        n.run(150)  # CPU steps are far faster than a merge round trip: leave room for swaps and 8-step rounds
         assert not n.errors and n.version >= 1
         assert n.recommended_h_mini >= 8 and n.h_mini == 8
         assert any(e["inner_steps"] == 8 for e in _accepted(store, "tuned"))  # rounds of 8 steps after a swap
