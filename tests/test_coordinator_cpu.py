@@ -216,6 +216,9 @@ def test_http_body_limits(service):
     assert r.split(b"\r\n")[0].split()[1] == b"411"
     r = raw(b"GET /health HTTP/1.1\r\nHost: c\r\nContent-Length: 0\r\n\r\n")  # the server keeps serving
     assert r.split(b"\r\n")[0].split()[1] == b"200"
+    # permissive CORS with preflight, for browser nodes (the reference's CorsLayer::permissive)
+    r = raw(b"OPTIONS /delta HTTP/1.1\r\nHost: c\r\nOrigin: http://x\r\nAccess-Control-Request-Method: POST\r\n\r\n")
+    assert r.split(b"\r\n")[0].split()[1] in (b"200", b"204") and b"Access-Control-Allow-Origin: *" in r
 
 
 def test_config_route_secret_can_be_withheld(service):
