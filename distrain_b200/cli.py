@@ -220,7 +220,7 @@ def cmd_start(args):
                         device=device, node_id=node_id, data=None, poll_secs=args.poll_secs,
                         bandwidth_adaptive=args.bandwidth_adaptive, resume_path=args.resume_file,
                         resume_every=args.resume_every, max_memory_fraction=args.max_memory_fraction,
-                        h_mini_bounds=args.h_mini_bounds)
+                        h_mini_bounds=args.h_mini_bounds, ckpt_cache_dir=args.cache_dir)
         node.register(gpu_model="cpu" if device == "cpu" else "B200")
         _save_node_id(args.cache_dir, node.node_id)
         # data: local shards (--data-dir), else this node's assigned shards from the store, else synthetic

@@ -122,7 +122,7 @@ class HttpNode:
                  heartbeat_every: int = 10, loss_based_lr: Optional[bool] = None,
                  expected_step_secs: Optional[float] = None, resume_path: Optional[str] = None,
                  resume_every: int = 1, max_memory_fraction: float = 0.80,
-                 h_mini_bounds: Optional[tuple] = None):
+                 h_mini_bounds: Optional[tuple] = None, ckpt_cache_dir: Optional[str] = None):
         self.client = CoordinatorClient(coordinator_url)
         self.store = store
         self.cfg, self.batch, self.seq_len, self.h_mini = model_cfg, batch, seq_len, h_mini
@@ -159,6 +159,8 @@ class HttpNode:
         # (min, max) inner steps: at each checkpoint swap the push interval follows the bandwidth-based
         # recommendation (steps whose delta uploads in ~10 s), clamped to these bounds (continuous.rs:936-945)
         self.h_mini_bounds = h_mini_bounds
+        # checkpoints fetched from the store are kept here, the newest 3 (continuous.rs:966-995)
+        self.ckpt_cache_dir = ckpt_cache_dir
         self.resumed: Optional[str] = None   # "exact" (same checkpoint: weights, AdamW, EF restored) / "identity"
         self._resume_rec = self._read_resume()
         if self.node_id is None and self._resume_rec is not None:
@@ -176,7 +178,26 @@ class HttpNode:
         return r
 
     def _load_version(self, v: int):
-        return load_safetensors_bytes(self.store.get(P.checkpoint_path(v)))
+        if not self.ckpt_cache_dir:
+            return load_safetensors_bytes(self.store.get(P.checkpoint_path(v)))
+        d = os.path.join(self.ckpt_cache_dir, "checkpoints")
+        path = os.path.join(d, f"v{v}.safetensors")
+        if os.path.exists(path):
+            with open(path, "rb") as f:
+                return load_safetensors_bytes(f.read())
+        data = self.store.get(P.checkpoint_path(v))
+        os.makedirs(d, exist_ok=True)
+        with open(path + ".tmp", "wb") as f:
+            f.write(data)
+        os.replace(path + ".tmp", path)
+        cached = sorted((int(n[1:-len(".safetensors")]) for n in os.listdir(d)
+                         if n.startswith("v") and n.endswith(".safetensors")), reverse=True)
+        for old in cached[3:]:
+            try:
+                os.remove(os.path.join(d, f"v{old}.safetensors"))
+            except OSError:
+                pass
+        return load_safetensors_bytes(data)
 
     def _ckpt_manager(self):
         while not self.stop.wait(self.poll_secs):

@@ -179,3 +179,28 @@ def _accepted(store, node_id):
     from distrain_b200 import protocol as P
     raw = store.get(P.stats_history_path()).decode()
     return [e for e in map(json.loads, raw.splitlines()) if e["event"] == "delta_accepted" and e["node_id"] == node_id]
+
+
+@pytest.mark.timeout(300)
+def test_checkpoint_cache_keeps_the_newest_three(tmp_path):
+    """Checkpoints fetched from the store are cached on disk (newest 3 kept): a restarted node reads an
+    unchanged checkpoint from its cache instead of the store."""
+    store, svc, url = _service(tmp_path, min_contributions=0)
+    cache = tmp_path / "cache"
+    try:
+        n = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=4).next_batch, None, node_id="cached")
+        n.ckpt_cache_dir = str(cache)
+        n.register()
+        n.run(150)
+        assert not n.errors and n.version >= 3  # v0..v3 fetched: four checkpoints, three kept
+        kept = sorted(os.listdir(cache / "checkpoints"))
+        assert len(kept) == 3 and f"v{n.version}.safetensors" in kept
+        gets = []
+        real_get = store.get
+        store.get = lambda key: (gets.append(key), real_get(key))[1]
+        m = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=5).next_batch, None, node_id="cached")
+        m.ckpt_cache_dir = str(cache)
+        assert m._load_version(n.version) is not None
+        assert not any(k.startswith("checkpoints/") for k in gets)
+    finally:
+        svc.stop()
