@@ -68,12 +68,15 @@ class CpuBackend:
             self.opt.v[k].copy_(st["v"][k])
         self.opt.t = int(st["t"])
 
-    def step(self, tokens: torch.Tensor, lr: float) -> float:
+    def step(self, tokens: torch.Tensor, lr: float, max_loss: Optional[float] = None) -> float:
+        """One step; a non-finite loss, or one above ``max_loss`` (a spike), returns without an update."""
         loss = self.oracle.lm_loss(self.params, self.cfg, tokens.long())
         if not math.isfinite(loss.item()):
             for p in self.params.values():
                 p.grad = None
             return float("nan")
+        if max_loss is not None and loss.item() > max_loss:
+            return float(loss.item())
         loss.backward()
         self.opt.step(lr)
         return float(loss.item())
@@ -107,7 +110,9 @@ class CudaBackend:
             self.eng.v.copy_(st["v"].to(self.eng.device))
             self.eng.hp.copy_(st["hp"].to(self.eng.device))
 
-    def step(self, tokens, lr):
+    def step(self, tokens, lr, max_loss=None):
+        # the fused step updates before the loss is read: a spike is only excluded from the round's
+        # statistics here, while a non-finite loss skips the update on the device
         self.eng.set_lr(lr)
         self.eng.set_tokens(tokens.to(self.eng.device, non_blocking=True))
         self.eng.step()
@@ -159,6 +164,7 @@ class HttpNode:
         # (min, max) inner steps: at each checkpoint swap the push interval follows the bandwidth-based
         # recommendation (steps whose delta uploads in ~10 s), clamped to these bounds (continuous.rs:936-945)
         self.h_mini_bounds = h_mini_bounds
+        self.spikes_skipped = 0
         # checkpoints fetched from the store are kept here, the newest 3 (continuous.rs:966-995)
         self.ckpt_cache_dir = ckpt_cache_dir
         self.resumed: Optional[str] = None   # "exact" (same checkpoint: weights, AdamW, EF restored) / "identity"
@@ -392,11 +398,14 @@ class HttpNode:
                     lr = self.optim.lr * min(max(loss_ema / ln_vocab, 0.1), 1.0)
                 else:
                     lr = self.optim.lr
-                loss = self.backend.step(tokens, lr)
+                # a loss above both 3x and +5 of its EMA is a spike: no update (continuous.rs:607-621)
+                spike_at = max(loss_ema * 3.0, loss_ema + 5.0) if loss_count > 3 else None
+                loss = self.backend.step(tokens, lr, spike_at)
                 if not math.isfinite(loss):
-                    continue  # NaN loss: skip the update (continuous.rs:607-610)
-                if loss_count > 3 and loss > loss_ema * 3.0 and loss > loss_ema + 5.0:
-                    continue  # loss spike: skip (continuous.rs:613-621)
+                    continue  # NaN loss: the update was skipped
+                if spike_at is not None and loss > spike_at:
+                    self.spikes_skipped += 1
+                    continue
                 losses.append(loss)
                 loss_count += 1
                 loss_ema = loss if loss_count == 1 else loss_ema * 0.9 + loss * 0.1

@@ -204,3 +204,20 @@ def test_checkpoint_cache_keeps_the_newest_three(tmp_path):
         assert not any(k.startswith("checkpoints/") for k in gets)
     finally:
         svc.stop()
+
+
+def test_loss_spike_skips_the_update_on_the_cpu_backend():
+    """A step whose loss exceeds the spike bound leaves weights and optimizer untouched."""
+    from distrain_b200.config import OptimConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.parallel.http_node import CpuBackend
+    b = CpuBackend(CFG, OptimConfig(lr=1e-2))
+    L = ParamLayout(CFG)
+    b.load(L.to_state_dict(init_flat(L, 0.02, 0)))
+    toks = SyntheticTokens(CFG.vocab_size, 2, 17, seed=2).next_batch()
+    before = b.state()
+    loss = b.step(toks, 1e-2, max_loss=0.1)  # any real loss is a "spike" against this bound
+    assert loss > 0.1 and b.opt.t == 0
+    assert all(torch.equal(before[k], v) for k, v in b.state().items())
+    b.step(toks, 1e-2, max_loss=None)
+    assert b.opt.t == 1 and not all(torch.equal(before[k], v) for k, v in b.state().items())
