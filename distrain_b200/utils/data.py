@@ -158,13 +158,19 @@ class StreamingLoader:
                  max_resident: int = 4, prefetch: int = 2):
         os.makedirs(cache_dir, exist_ok=True)
         manifest = store.get_json(P.manifest_path())
-        paths = []
+        paths, self.skipped = [], []
         for i in shard_indices:
             entry = manifest["shards"][i]
             local = os.path.join(cache_dir, entry["filename"])
             if not os.path.exists(local):
-                store.download_to_file(f"data/{entry['filename']}", local)
+                try:
+                    store.download_to_file(f"data/{entry['filename']}", local)
+                except Exception as e:  # a shard that cannot be fetched is skipped (reference data.rs:392-395)
+                    self.skipped.append((entry["filename"], str(e)))
+                    continue
             paths.append(local)
+        if not paths:
+            raise NativeError(f"none of the assigned shards could be fetched: {self.skipped[:3]}")
         self.manifest = manifest
         self.loader = ShardLoader(paths, seq_len, batch_size, max_resident=max_resident, prefetch=prefetch)
 

@@ -4,6 +4,7 @@ position, full coverage)."""
 import os
 
 import numpy as np
+import pytest
 import torch
 
 from distrain_b200.utils.data import ShardLoader, StreamingLoader, prepare_random_shards, write_shard
@@ -81,3 +82,19 @@ def test_prepare_and_stream_from_store(tmp_path):
     ref = np.fromfile(os.path.join(src, "shard_0002.bin"), dtype="<u2")[:128].astype(np.int32)
     assert torch.equal(b.reshape(-1), torch.from_numpy(ref)) and int(b.max()) < 300
     s.close()
+
+
+def test_stream_skips_a_shard_that_cannot_be_fetched(tmp_path):
+    src = str(tmp_path / "prep")
+    prepare_random_shards(src, num_shards=3, tokens_per_shard=2048, vocab_size=300, seed=2)
+    store = FsStore(str(tmp_path / "obj"))
+    for f in os.listdir(src):
+        if f != "shard_0001.bin":  # listed in the manifest, missing from the store
+            store.upload_from_file(os.path.join(src, f), f"data/{f}")
+    s = StreamingLoader(store, str(tmp_path / "cache"), [1, 2], seq_len=64, batch_size=2, prefetch=0)
+    assert [f for f, _ in s.skipped] == ["shard_0001.bin"]
+    ref = np.fromfile(os.path.join(src, "shard_0002.bin"), dtype="<u2")[:128].astype(np.int32)
+    assert torch.equal(s.next_batch().reshape(-1), torch.from_numpy(ref))
+    s.close()
+    with pytest.raises(Exception):
+        StreamingLoader(store, str(tmp_path / "cache2"), [1], seq_len=64, batch_size=2)
