@@ -543,11 +543,25 @@ def calibrate_batch_size(checkpoint: str, seq_len: int, lo: int = 1, hi: int = 2
     return best
 
 
+def load_safetensors_bytes_from(store, version: int):
+    from . import protocol as P
+    from .utils.checkpoint import load_safetensors_bytes
+    return load_safetensors_bytes(store.get(P.checkpoint_path(version)))
+
+
 def cmd_export_hf(args):
     """Checkpoint -> Hugging Face Qwen2ForCausalLM directory (config.json + model.safetensors)."""
     from .utils.checkpoint import load_safetensors
     from .utils.hf_export import export_hf
-    sd = load_safetensors(args.checkpoint)
+    if args.store:  # a stored version, whole or tensor-parallel shards (model-tp{t}of{T}), gathered
+        from .parallel.inbox_ckpt import gather_checkpoint, latest_version
+        st = _store(args.store)
+        v = args.version if args.version is not None else latest_version(st, args.tp)
+        if v is None:
+            raise SystemExit(f"export-hf: no stored checkpoint for {args.tp} shard(s) in {args.store}")
+        sd = gather_checkpoint(st, v, args.tp) if args.tp > 1 else load_safetensors_bytes_from(st, v)
+    else:
+        sd = load_safetensors(args.checkpoint)
     cfg = _infer_model_config(sd)
     if args.rope_theta:
         cfg.rope_theta = args.rope_theta
@@ -707,8 +721,11 @@ def build_parser() -> argparse.ArgumentParser:
     p.set_defaults(fn=cmd_gpu_stress_test)
 
     p = sp.add_parser("export-hf", help="checkpoint -> Hugging Face Qwen2ForCausalLM directory")
-    p.add_argument("checkpoint")
+    p.add_argument("checkpoint", nargs="?", help="a safetensors file (or use --store)")
     p.add_argument("output_dir")
+    p.add_argument("--store", help="read a stored version instead (gathers tensor-parallel shard files)")
+    p.add_argument("--version", type=int, help="default: the newest stored")
+    p.add_argument("--tp", type=int, default=1, help="tensor-parallel shard files per version")
     p.add_argument("--rope-theta", type=float)
     p.add_argument("--max-seq-len", type=int)
     p.set_defaults(fn=cmd_export_hf)

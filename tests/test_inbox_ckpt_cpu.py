@@ -56,3 +56,27 @@ def test_tensor_parallel_shard_files_gather(tmp_path):
     got = gather_checkpoint(store, 4, 2)
     for k in ref:
         assert torch.equal(got[k], ref[k]), k
+
+
+def test_export_hf_from_tensor_parallel_shard_files(tmp_path):
+    """export-hf --store --tp 2 gathers the shard files of the newest version and writes a Hugging Face
+    directory whose weights are the full model's."""
+    import json
+    from distrain_b200 import cli
+    from distrain_b200.utils.checkpoint import load_safetensors
+    cfg = _cfg()
+    full = ParamLayout(cfg)
+    ref = full.to_state_dict(init_flat(full, 0.02, seed=3))
+    store = FsStore(str(tmp_path / "st"))
+    for t in range(2):
+        L = ParamLayout(cfg, t, 2)
+        lf = torch.zeros(L.total)
+        L.load_state_dict(lf, shard_state_dict(ref, cfg, t, 2))
+        w = CheckpointWriter(store, L, every=1, keep_versions=5, shard=t, n_shards=2)
+        w.snapshot(lf, 6)
+        w.close()
+    cli.main(["export-hf", "--store", str(tmp_path / "st"), "--tp", "2", str(tmp_path / "hf")])
+    hf = load_safetensors(str(tmp_path / "hf" / "model.safetensors"))
+    assert torch.equal(hf["model.layers.0.mlp.gate_proj.weight"], ref["layers.0.ffn.gate_proj.weight"])
+    assert torch.equal(hf["model.embed_tokens.weight"], ref["embedding.embedding.weight"])
+    assert json.loads((tmp_path / "hf" / "config.json").read_text())["num_hidden_layers"] == cfg.num_layers
