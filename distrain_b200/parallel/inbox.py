@@ -173,9 +173,9 @@ class InBoxSync:
         # checkpoint store: resume from its newest version before anything copies the weights
         self.store = None
         self.resumed_version = 0
-        if run.checkpoint_store:
-            from ..utils.storage import FsStore
-            self.store = FsStore(run.checkpoint_store)
+        if run.checkpoint_store:  # a directory / file:// path, or an S3 endpoint
+            from ..utils.storage import open_store
+            self.store = open_store(run.checkpoint_store)
             if run.resume:
                 v = latest_version(self.store, n_shards)
                 if v:
