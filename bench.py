@@ -14,6 +14,13 @@ timed with CUDA events on the training stream; the reported time is the max over
 step's working set (~12 GB of activations and state) is far larger than the 126 MB L2, so no L2
 flush is inserted. ``e2e`` repeats the K steps through the public node API with a pinned-host H2D
 copy of every step's tokens and a D2H read of every step's loss.
+
+Protocol inside the timed steps: before each timed region every node's round counter is phased so its
+push falls after step K/2 of the region (``InBoxNode.phase_push``); the compression, the coordinator's
+merge and broadcast, and the nodes' checkpoint swap then run during the remaining timed steps. The
+line's ``merge`` block counts the pushes and swaps that happened inside each region (the minimum over
+ranks), so one push per K steps is charged to the measured rate - more than the configured one per
+``push_every`` steps whenever K < push_every.
 """
 from __future__ import annotations
 
@@ -129,6 +136,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        # NCCL's communicator set-up lines (ranks, devices, transports) go to stderr, stdout stays the JSON line
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=300))
     run = bench_config(args.config)
@@ -198,9 +209,19 @@ def main():
         clocks.start()
         time.sleep(0.5)
 
+    def protocol_marks():
+        s = node.sync
+        return (s.seq, s.version) if s is not None else (0, 0)
+
+    def phase():
+        if node.sync is not None:
+            node.phase_push(max(args.steps // 2, 1))
+
     ops._lib.LAUNCHES[0] = 0
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    phase()
+    marks0 = protocol_marks()
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
@@ -212,9 +233,13 @@ def main():
     barrier()
     launches = ops._lib.LAUNCHES[0]
     ms = e0.elapsed_time(e1)
+    marks_dev_end = marks1 = protocol_marks()
 
     e2e_ms = None
+    marks2 = marks1
     if not args.no_e2e:
+        phase()
+        marks1 = protocol_marks()
         barrier()
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -225,13 +250,21 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_ms = f0.elapsed_time(f1)
+        marks2 = protocol_marks()
     clk = clocks.stop() if clocks else None
 
     free_b, total_b = torch.cuda.mem_get_info(dev)
     t = torch.tensor([ms, e2e_ms or 0.0, float(launches), float(total_b - free_b)], device=dev)
+    # pushes / swaps inside the device-timed and the e2e regions, negated so that the MAX reduction
+    # yields the minimum over ranks
+    t = torch.cat([t, -torch.tensor([marks_t[0] - marks_s[0] for marks_s, marks_t in
+                                     ((marks0, marks_dev_end), (marks1, marks2))] +
+                                    [marks_t[1] - marks_s[1] for marks_s, marks_t in
+                                     ((marks0, marks_dev_end), (marks1, marks2))], dtype=torch.float32, device=dev)])
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms_max, launches, mem_used = t[0].item(), t[1].item(), int(t[2].item()), t[3].item()
+    pushes_dev, pushes_e2e, swaps_dev, swaps_e2e = (int(-x) for x in t[4:8].tolist())
     if nccl_arm:
         merges = node.sync.merges
     else:
@@ -272,6 +305,9 @@ def main():
             # model FLOPs (6N + causal attention [+ recompute]) per GPU against the measured bf16 peaks
             "roofline": step_roofline(run.model, S, value, world, run.activation_checkpointing),
         }
+        if node.sync is not None and not merges:
+            out["merge"] = {"count": 0, "pushes_in_timed_steps": pushes_dev, "swaps_in_timed_steps": swaps_dev,
+                            "note": "no merge completed before the end of the run"}
         if merges:
             dev_ms = sorted(m["device_ms"] for m in merges)
             out["merge"] = {"count": len(merges), "node_version": versions,
@@ -279,6 +315,10 @@ def main():
                             "timing": ("CUDA events on rank 0's merge stream while the nodes train, host planning "
                                        "and control-bus round trips between its kernels included") if not nccl_arm else
                                       "CUDA events around the NCCL all-reduce + apply on the training stream",
+                            "pushes_in_timed_steps": pushes_dev, "swaps_in_timed_steps": swaps_dev,
+                            "pushes_in_e2e_steps": pushes_e2e if e2e_ms is not None else None,
+                            "swaps_in_e2e_steps": swaps_e2e if e2e_ms is not None else None,
+                            "push_phase": f"push after step {max(args.steps // 2, 1)} of each timed region",
                             "contributions_last": merges[-1]["n_contrib"],
                             "pulled_bytes_last": merges[-1]["pulled_bytes"],
                             "broadcast_bytes_last": merges[-1]["broadcast_bytes"],

@@ -359,7 +359,7 @@ __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ c
                                const long long* __restrict__ cstart, const long long* __restrict__ cend,
                                SegState* seg, const long long* __restrict__ eq_take,
                                const long long* __restrict__ out_off, int* __restrict__ out_idx,
-                               float* __restrict__ out_val) {
+                               float* __restrict__ out_val, long long capacity) {
   __shared__ long long sh[66];
   __shared__ float shs[32];
   const int c = blockIdx.x, s = cseg[c];
@@ -394,10 +394,15 @@ __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ c
         --allow;
       }
       if (take) {
-        out_idx[pos] = (int)((i0 + j) & kWindowMask);  // index within its 2^31 window
-        out_val[pos] = v[j];
-        ef[i0 + j] = 0.f;
-        kept_sq += v[j] * v[j];
+        if (pos < capacity) {
+          out_idx[pos] = (int)((i0 + j) & kWindowMask);  // index within its 2^31 window
+          out_val[pos] = v[j];
+          ef[i0 + j] = 0.f;
+          kept_sq += v[j] * v[j];
+        } else {
+          // the caller's output arrays are too short: keep the value in error feedback, write nothing
+          dt_set_error(DT_ERR_BOUNDS, 710);
+        }
         ++pos;
       }
     }
@@ -411,10 +416,11 @@ __global__ void compact_kernel(float* __restrict__ ef, const int* __restrict__ c
 // Per block of `blk` kept values: absmax/127 scale (1 if all zero), round-half-away int8.
 // `wire` (3 doubles): statistics of the dequantised values as they go on the wire - sum of squares,
 // max |x| (as ordered bits), non-finite blocks - which the coordinator validates and clips on.
-__global__ void quant_kernel(const float* __restrict__ val, const long long* __restrict__ total, int blk,
-                             signed char* __restrict__ q, float* __restrict__ scales, double* __restrict__ wire) {
+__global__ void quant_kernel(const float* __restrict__ val, const long long* __restrict__ total, long long capacity,
+                             int blk, signed char* __restrict__ q, float* __restrict__ scales,
+                             double* __restrict__ wire) {
   __shared__ float sh[32];
-  const long long n = *total;
+  const long long n = *total < capacity ? *total : capacity;
   const long long b = blockIdx.x;
   const long long s0 = b * blk;
   if (s0 >= n) return;
@@ -527,7 +533,9 @@ DT_API int dt_compress_begin(const float* master, float* snap, float* ef, const 
 }
 
 // Everything after pass A (side stream). Writes out_idx/out_val (capacity entries) in ascending index
-// order, int8 + per-block scales when quant_block > 0, and the kept count into the workspace.
+// order, int8 + per-block scales when quant_block > 0, and the kept count into the workspace. An entry
+// that would land at or beyond `capacity` is not written (it stays in error feedback) and sets
+// DT_ERR_BOUNDS in dt_error_word; the per-tensor budgets sum to at most ceil(n * k_fraction) + nseg.
 DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstart, const long long* cend, int nchunks,
                               int nseg, void* ws, float k_fraction, int adaptive, int* out_idx, float* out_val,
                               signed char* out_q, float* out_scales, int quant_block, long long capacity,
@@ -542,11 +550,11 @@ DT_API int dt_compress_finish(float* ef, const int* cseg, const long long* cstar
   select_level_kernel<NB3, 128><<<nseg, 128, 0, st>>>(w.seg, nseg, w.h3, 7, 1);
   count_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.gt, w.eq);
   scan_kernel<<<1, 1024, 0, st>>>(cseg, nchunks, w.seg, w.gt, w.eq, w.take, w.off, w.total);
-  compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val);
+  compact_kernel<<<nchunks, TPB, 0, st>>>(ef, cseg, cstart, cend, w.seg, w.take, w.off, out_idx, out_val, capacity);
   if (out_win) window_kernel<<<1, 32, 0, st>>>(w.off, w.total, win_chunk, nwin, nchunks, out_win);
   if (quant_block > 0 && out_q) {
     long long nblk = (capacity + quant_block - 1) / quant_block;
-    quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, quant_block, out_q, out_scales,
+    quant_kernel<<<(unsigned)nblk, 256, 0, st>>>(out_val, w.total, capacity, quant_block, out_q, out_scales,
                                                  reinterpret_cast<double*>(w.total + 1));
   }
   return (int)cudaGetLastError();
@@ -597,13 +605,23 @@ void* g_scratch_ptr[64] = {nullptr};
 
 DT_API long long dt_compress_noalloc_scratch_bytes() { return (long long)DT_COMPRESS_NOALLOC_SCRATCH_BYTES; }
 
+DT_API long long dt_compress_noalloc_min_capacity(long long n_elems, int nseg, float k_fraction) {
+  long long c = (long long)ceil((double)n_elems * (double)k_fraction) + nseg;
+  return c < n_elems ? c : n_elems;
+}
+
 DT_API int dt_compress_noalloc(const float* master, float* snap, float* ef, const int* cseg, const long long* cstart,
                                const long long* cend, int nchunks, int nseg, const long long* seg_len,
-                               float k_fraction, int adaptive, int* out_idx, float* out_val, signed char* out_q,
-                               float* out_scales, int quant_block, long long capacity, double* stats_out,
-                               cudaStream_t st) {
+                               long long n_elems, float k_fraction, int adaptive, int* out_idx, float* out_val,
+                               signed char* out_q, float* out_scales, int quant_block, long long capacity,
+                               double* stats_out, cudaStream_t st) {
+  if (nseg <= 0 || nchunks <= 0 || n_elems <= 0 || !(k_fraction > 0.f) || k_fraction > 1.f) return -10;
+  // kept indices are 32-bit flat offsets: a buffer of 2^31 elements or more needs the windowed payload
+  // of dt_compress_finish (win_chunk / out_win), which this entry point does not produce
+  if (n_elems > kWindowMask) return -22;
+  if (capacity < dt_compress_noalloc_min_capacity(n_elems, nseg, k_fraction)) return -23;
   const long long need = dt_compress_workspace_bytes(nseg, nchunks);
-  if (nseg <= 0 || nchunks <= 0 || need > (long long)DT_COMPRESS_NOALLOC_SCRATCH_BYTES) return -20;
+  if (need > (long long)DT_COMPRESS_NOALLOC_SCRATCH_BYTES) return -20;
   int dev = 0;
   DT_CUDA_RET(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return -21;
@@ -621,8 +639,7 @@ DT_API int dt_compress_noalloc(const float* master, float* snap, float* ef, cons
   // dt_compress_begin clears the whole workspace (histograms, counters) before use
   int rc = dt_compress_begin(master, snap, ef, cseg, cstart, cend, nchunks, nseg, seg_len, ws, 1, st);
   if (rc) return rc;
-  // kept indices are window-relative (see window_kernel); this entry point serves buffers below 2^31
-  // elements, where they are plain flat indices
+  // below 2^31 elements there is one index window, so the kept indices are plain flat indices
   rc = dt_compress_finish(ef, cseg, cstart, cend, nchunks, nseg, ws, k_fraction, adaptive, out_idx, out_val, out_q,
                           out_scales, quant_block, capacity, nullptr, 1, nullptr, st);
   if (rc) return rc;

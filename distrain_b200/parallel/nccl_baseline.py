@@ -34,6 +34,9 @@ class NcclDenseSync:
         self.snap = self.eng.master.clone()
         self.delta = torch.empty_like(self.snap)
         self.version = 0
+        self.seq = 0            # rounds pushed (here: all-reduced), as the in-box node counts its pushes
+        self.round_tokens = 0
+        self._lr_set = None
         self.first_round = True
         self.coord = None
         self._events: List = []
@@ -70,7 +73,9 @@ class NcclDenseSync:
         e1.record(train)
         self._events.append((e0, e1))
         self.version += 1
+        self.seq += 1
         self.node.round_step = 0
+        self.round_tokens = 0
 
     @property
     def merges(self):

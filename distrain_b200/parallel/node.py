@@ -79,6 +79,20 @@ class InBoxNode:
             self.sync = InBoxSync(self, run, rank, world, self.device, shard=shard, n_shards=n_shards,
                                   dp_group=dp_group)
 
+    def phase_push(self, steps_ahead: int):
+        """Place this node's next push ``steps_ahead`` steps from now: the round counter (and the round's
+        token count) is set as if the round had begun ``push_every - steps_ahead`` steps ago, and the
+        first round's inner-lr warm-up is ended at the full lr. A benchmark uses it so that a push, the
+        merge it triggers and the checkpoint swap fall inside its timed steps whatever their number."""
+        if self.sync is None:
+            return
+        pe = self.run.push_every
+        self.round_step = max(pe - int(steps_ahead), 0)
+        self.sync.round_tokens = self.round_step * self.run.micro_batch * self.run.seq_len
+        if self.sync.first_round:
+            self.engine.set_lr(self.run.optim.lr)
+            self.sync._lr_set = self.run.optim.lr
+
     # ── training ──
     def _ensure_graph(self):
         if not self._graph_ready:

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import logging
 import os
 from typing import List, Optional
 
@@ -21,6 +22,8 @@ import torch
 
 from .native import rt, register, NativeError
 from .. import protocol as P
+
+log = logging.getLogger("distrain_b200.data")
 
 
 def write_shard(path: str, tokens) -> int:
@@ -172,15 +175,31 @@ class StreamingLoader:
         if not paths:
             raise NativeError(f"none of the assigned shards could be fetched: {self.skipped[:3]}")
         self.manifest = manifest
+        self.files = [os.path.basename(p) for p in paths]
         self.loader = ShardLoader(paths, seq_len, batch_size, max_resident=max_resident, prefetch=prefetch)
 
     def next_batch(self):
         return self.loader.next_batch()
 
     def state(self):
-        return self.loader.state()
+        """The read position with the shard's file name: the loaded shard list depends on which shards
+        could be fetched, so an index alone would point elsewhere after a restart that fetched others."""
+        st = self.loader.state()
+        if st is not None:
+            st = dict(st, filename=self.files[st["shard"]])
+        return st
 
     def restore(self, st):
+        """Continue from ``state``: the saved shard is found by file name. When that shard was not fetched
+        this time, reading restarts at the first loaded shard (the position cannot be mapped)."""
+        st = dict(st)
+        name = st.get("filename")
+        if name is not None:
+            if name not in self.files:
+                log.warning("saved data position is in shard %s, which was not fetched; starting over", name)
+                st["shard"], st["offset"] = 0, 0
+            else:
+                st["shard"] = self.files.index(name)
         self.loader.restore(st)
 
     def close(self):

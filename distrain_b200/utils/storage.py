@@ -237,15 +237,21 @@ class S3Store(ObjectStore):
             self._request("PUT", "")
 
 
-def open_store(url_or_cfg) -> ObjectStore:
-    """``file:///path`` / plain path -> FsStore; StorageConfig / http(s) endpoint -> S3Store."""
+def open_store(url_or_cfg, env=None) -> ObjectStore:
+    """``file:///path`` / plain path -> FsStore; StorageConfig / http(s) endpoint -> S3Store.
+
+    An endpoint string takes its bucket, region and credentials from the R2_* environment (``env``, or
+    the process environment), as the coordinator does, and overrides only the endpoint."""
     if isinstance(url_or_cfg, StorageConfig):
         if url_or_cfg.endpoint.startswith("file://"):
             return FsStore(url_or_cfg.endpoint[len("file://"):], url_or_cfg.bucket)
         return S3Store(url_or_cfg)
     s = str(url_or_cfg)
     if s.startswith("http://") or s.startswith("https://"):
-        return S3Store(StorageConfig(endpoint=s))
+        from ..config import CoordinatorConfig
+        cfg = CoordinatorConfig.from_env(env).storage
+        cfg.endpoint = s
+        return S3Store(cfg)
     if s.startswith("file://"):
         s = s[len("file://"):]
     return FsStore(s)

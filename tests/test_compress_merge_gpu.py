@@ -70,6 +70,51 @@ def test_device_compress_matches_reference(k_fraction, adaptive):
     assert mx == pytest.approx(float(deq.abs().max()), rel=1e-6) and nf == 0
 
 
+def test_compress_short_capacity_writes_nothing_past_it():
+    """A capacity below the selection: entries beyond it are not written (sentinels past the capacity
+    survive), they stay in error feedback, and the device error word reports an out-of-bounds condition."""
+    from distrain_b200.config import CompressionConfig
+    from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
+    from distrain_b200 import ops
+    from distrain_b200.ops._lib import check, stream_ptr
+    L = _layout()
+    dev = torch.device("cuda")
+    torch.manual_seed(1)
+    cfg = CompressionConfig(top_k_fraction=0.1, quantize_int8=True, per_tensor_adaptive=True, int8_block=256)
+    comp = DeviceCompressor(L, dev, cfg)
+    full = comp.capacity
+    short = full // 2
+    p = DevicePayload.allocate(full, 256, dev)
+    p.idx.fill_(-7)
+    p.val.fill_(123.0)
+    p.q.fill_(77)
+    mask = torch.zeros(L.total, dtype=torch.bool, device=dev)
+    for e in L.entries:
+        mask[e.offset:e.offset + e.numel] = True
+    delta = torch.randn(L.total, device=dev) * 1e-3 * mask
+    comp.snap.zero_()
+    comp.ef.zero_()
+    ops.clear_device_error()
+    comp.begin(-delta)
+    check(comp.L.dt_compress_finish(comp.ef.data_ptr(), comp.cseg.data_ptr(), comp.cstart.data_ptr(),
+                                    comp.cend.data_ptr(), comp.nchunks, comp.nseg, comp.ws.data_ptr(), 0.1, 1,
+                                    p.idx.data_ptr(), p.val.data_ptr(), p.q.data_ptr(), p.scales.data_ptr(), 256,
+                                    short, comp.win_chunk.data_ptr(), comp.nwin, p.win.data_ptr(), stream_ptr()),
+          "dt_compress_finish")
+    torch.cuda.synchronize()
+    code, site = ops.device_error()
+    ops.clear_device_error()
+    assert code == 5 and site == 710
+    assert torch.all(p.idx[short:] == -7) and torch.all(p.val[short:] == 123.0) and torch.all(p.q[short:] == 77)
+    kept = p.idx[:short].long()
+    assert bool((kept >= 0).all()) and torch.all(kept[1:] > kept[:-1])
+    # written entries left error feedback; the selected-but-unwritten ones (and the unselected) stay there
+    written = torch.zeros(L.total, dtype=torch.bool, device=dev)
+    written[kept] = True
+    assert torch.all(comp.ef[written] == 0)
+    assert torch.equal(comp.ef[~written], delta[~written])
+
+
 @pytest.mark.parametrize("momentum,in_place", [(0.0, True), (0.0, False), (0.9, False)])
 def test_device_merge_matches_reference(momentum, in_place):
     """Merge of three compressed payloads (one an outlier that gets clipped) against the fp32 reference

@@ -98,3 +98,27 @@ def test_stream_skips_a_shard_that_cannot_be_fetched(tmp_path):
     s.close()
     with pytest.raises(Exception):
         StreamingLoader(store, str(tmp_path / "cache2"), [1], seq_len=64, batch_size=2)
+
+
+def test_stream_resume_maps_the_position_by_shard_name(tmp_path):
+    """A position saved while a shard was unavailable resumes in the same shard file once that shard can be
+    fetched again (the loaded shard list, and so the shard index, differs between the two runs)."""
+    src = str(tmp_path / "prep")
+    prepare_random_shards(src, num_shards=3, tokens_per_shard=2048, vocab_size=300, seed=3)
+    store = FsStore(str(tmp_path / "obj"))
+    for f in os.listdir(src):
+        if f != "shard_0001.bin":
+            store.upload_from_file(os.path.join(src, f), f"data/{f}")
+    s = StreamingLoader(store, str(tmp_path / "cache"), [1, 2], seq_len=64, batch_size=2, prefetch=0)
+    for _ in range(3):
+        s.next_batch()
+    st = s.state()
+    assert st["filename"] == "shard_0002.bin" and st["shard"] == 0
+    expect = s.next_batch()
+    s.close()
+    store.upload_from_file(os.path.join(src, "shard_0001.bin"), "data/shard_0001.bin")
+    s2 = StreamingLoader(store, str(tmp_path / "cache2"), [1, 2], seq_len=64, batch_size=2, prefetch=0)
+    assert s2.files == ["shard_0001.bin", "shard_0002.bin"]
+    s2.restore(st)
+    assert torch.equal(s2.next_batch(), expect)
+    s2.close()

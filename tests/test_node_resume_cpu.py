@@ -193,14 +193,16 @@ def test_checkpoint_cache_keeps_the_newest_three(tmp_path):
         n.register()
         n.run(150)
         assert not n.errors and n.version >= 3  # v0..v3 fetched: four checkpoints, three kept
-        kept = sorted(os.listdir(cache / "checkpoints"))
-        assert len(kept) == 3 and f"v{n.version}.safetensors" in kept
+        # the checkpoint thread may have fetched versions newer than the one the node last swapped to
+        kept = sorted(os.listdir(cache / "checkpoints"), key=lambda f: int(f[1:].split(".")[0]))
+        newest = int(kept[-1][1:].split(".")[0])
+        assert len(kept) == 3 and newest >= n.version
         gets = []
         real_get = store.get
         store.get = lambda key: (gets.append(key), real_get(key))[1]
         m = _node(url, store, SyntheticTokens(CFG.vocab_size, 2, 17, seed=5).next_batch, None, node_id="cached")
         m.ckpt_cache_dir = str(cache)
-        assert m._load_version(n.version) is not None
+        assert m._load_version(newest) is not None
         assert not any(k.startswith("checkpoints/") for k in gets)
     finally:
         svc.stop()

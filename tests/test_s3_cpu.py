@@ -136,3 +136,24 @@ def test_s3store_end_to_end_with_signed_requests(s3):
     with pytest.raises(S.StorageError):
         s3.get("deltas/v1/big.delta.zst")
     assert not _FakeS3.bad_sigs, _FakeS3.bad_sigs
+
+
+def test_open_store_endpoint_uses_r2_environment(monkeypatch):
+    """An S3 endpoint given as a string (a node's checkpoint store) signs with the R2_* credentials and
+    writes into the R2_BUCKET bucket, not the built-in defaults."""
+    srv = http.server.ThreadingHTTPServer(("127.0.0.1", 0), _FakeS3)
+    t = threading.Thread(target=srv.serve_forever, daemon=True)
+    t.start()
+    try:
+        _FakeS3.objects.clear(), _FakeS3.bad_sigs.clear(), _FakeS3.requests.clear()
+        monkeypatch.setattr(_FakeS3, "access", "AKIDOTHER")
+        monkeypatch.setattr(_FakeS3, "secret", "OTHERSECRET")
+        env = {"R2_ACCESS_KEY_ID": "AKIDOTHER", "R2_SECRET_ACCESS_KEY": "OTHERSECRET", "R2_BUCKET": "runbucket",
+               "R2_REGION": "us-east-1", "R2_ENDPOINT": "http://unused.invalid"}
+        store = S.open_store(f"http://127.0.0.1:{srv.server_address[1]}", env=env)
+        store.put("checkpoints/v3/model.safetensors", b"w3")
+        assert store.get("checkpoints/v3/model.safetensors") == b"w3"
+        assert ("PUT", "/runbucket/checkpoints/v3/model.safetensors", {}) in _FakeS3.requests
+        assert not _FakeS3.bad_sigs, _FakeS3.bad_sigs
+    finally:
+        srv.shutdown()

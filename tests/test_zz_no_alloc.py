@@ -17,9 +17,11 @@ def _sym():
     L = _lib.lib()
     f = L.dt_compress_noalloc
     v, i, ll, fl = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float
-    f.argtypes = [v, v, v, v, v, v, i, i, v, fl, i, v, v, v, v, i, ll, v, v]
+    f.argtypes = [v, v, v, v, v, v, i, i, v, ll, fl, i, v, v, v, v, i, ll, v, v]
     f.restype = ctypes.c_int
     L.dt_compress_noalloc_scratch_bytes.restype = ll
+    L.dt_compress_noalloc_min_capacity.argtypes = [ll, i, fl]
+    L.dt_compress_noalloc_min_capacity.restype = ll
     return f, L
 
 
@@ -53,7 +55,8 @@ def test_noalloc_matches_allocating_entry_point_twice():
         ref.begin(master)
         ref.finish()
         rc = f(master.data_ptr(), snap.data_ptr(), ef.data_ptr(), ref.cseg.data_ptr(), ref.cstart.data_ptr(),
-               ref.cend.data_ptr(), ref.nchunks, ref.nseg, ref.seg_len.data_ptr(), 0.1, 1, out.idx.data_ptr(),
+               ref.cend.data_ptr(), ref.nchunks, ref.nseg, ref.seg_len.data_ptr(), layout.total, 0.1, 1,
+               out.idx.data_ptr(),
                out.val.data_ptr(), out.q.data_ptr(), out.scales.data_ptr(), 256, cap, stats.data_ptr(), stream)
         assert rc == 0
         torch.cuda.synchronize()
@@ -76,7 +79,22 @@ def test_noalloc_matches_allocating_entry_point_twice():
 
 def test_noalloc_rejects_oversized_problem():
     f, L = _sym()
+    s = torch.cuda.current_stream().cuda_stream
     big_nseg = 1 << 16  # histograms alone would exceed the 32 MiB scratch
-    rc = f(None, None, None, None, None, None, 1, big_nseg, None, 0.1, 1, None, None, None, None, 256, 1, None,
-           torch.cuda.current_stream().cuda_stream)
+    n = 1 << 20
+    rc = f(None, None, None, None, None, None, 1, big_nseg, None, n, 0.1, 1, None, None, None, None, 256, n, None, s)
     assert rc == -20
+    # 2^31 elements or more: 32-bit flat indices cannot address them
+    big = 1 << 31
+    rc = f(None, None, None, None, None, None, 1, 4, None, big, 0.1, 1, None, None, None, None, 256, big, None, s)
+    assert rc == -22
+    # output arrays shorter than the largest possible selection
+    need = L.dt_compress_noalloc_min_capacity(n, 4, 0.1)
+    assert need == -(-n // 10) + 4
+    rc = f(None, None, None, None, None, None, 1, 4, None, n, 0.1, 1, None, None, None, None, 256, need - 1, None, s)
+    assert rc == -23
+    # invalid arguments
+    for nseg, nchunks, nel, k in ((0, 1, n, 0.1), (4, 0, n, 0.1), (4, 1, 0, 0.1), (4, 1, n, 0.0), (4, 1, n, 1.5)):
+        rc = f(None, None, None, None, None, None, nchunks, nseg, None, nel, k, 1, None, None, None, None, 256, n,
+               None, s)
+        assert rc == -10
