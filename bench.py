@@ -44,6 +44,7 @@ def _parse():
     ap.add_argument("--config", default="tiny")
     ap.add_argument("--impl", default="dt", choices=["dt", "reference"])
     ap.add_argument("--push-every", type=int, default=None)
+    ap.add_argument("--grad-accum", type=int, default=None, help="micro-batches per optimizer step")
     ap.add_argument("--tp", type=int, default=None, help="tensor-parallel size per node (default: the preset's)")
     ap.add_argument("--clocks-csv", default=None,
                     help="keep the nvidia-smi clock samples of the timed region in this CSV (default: a temp file)")
@@ -145,6 +146,8 @@ def main():
     run = bench_config(args.config)
     if args.push_every:
         run.push_every = args.push_every
+    if args.grad_accum:
+        run.grad_accum_steps = max(args.grad_accum, 1)
     if args.tp:
         run.tp = args.tp
     nccl_arm = args.sync == "nccl" and not args.no_push
@@ -177,11 +180,11 @@ def main():
     if nccl_arm:
         from distrain_b200.parallel.nccl_baseline import NcclDenseSync
         node.sync = NcclDenseSync(node, run, node_rank, n_nodes, dev, group=dp_group)
-    B, S = run.micro_batch, run.seq_len
+    B, S, A = run.micro_batch, run.seq_len, run.grad_accum_steps
 
     # synthetic uniform-random tokens, per-node seed (the ranks of one tensor-parallel node share them)
     g = torch.Generator().manual_seed(1000 + node_rank)
-    ring = [torch.randint(0, run.model.vocab_size, (B, S), generator=g, dtype=torch.int32).pin_memory()
+    ring = [torch.randint(0, run.model.vocab_size, (A * B, S), generator=g, dtype=torch.int32).pin_memory()
             for _ in range(4)]
     dev_batches = [r.to(dev) for r in ring]
 
@@ -271,7 +274,7 @@ def main():
         merges = list(node.sync.coord.merges) if (node.sync is not None and node.sync.coord is not None) else []
     versions = node.sync.version if node.sync is not None else 0
     node.close()
-    tokens_per_step = B * S
+    tokens_per_step = A * B * S
     value = tokens_per_step * n_nodes * args.steps / (ms / 1e3)
     if rank == 0:
         out = {
@@ -288,7 +291,8 @@ def main():
             "dtype": "bf16",
             "data": "synthetic (uniform-random token ids, per-rank seeds; random-init N(0,0.02) weights)",
             "config": {"model": f"{run.name} preset ({run.model.param_count()/1e6:.1f}M params)",
-                       "global_batch": B * n_nodes, "seq_len": S,
+                       "global_batch": A * B * n_nodes, "seq_len": S,
+                       "micro_batch": B, "grad_accum_steps": A,
                        "parallelism": ((f"tp{tp_size} ({args.tp_mode} exchange) x " if tp_size > 1 else "") +
                                        (f"sync-dp{n_nodes} (NCCL all-reduce of dense fp32 deltas every push)"
                                         if nccl_arm else f"async-dp{n_nodes} (1 node per GPU)")),
@@ -322,12 +326,13 @@ def main():
                             "contributions_last": merges[-1]["n_contrib"],
                             "pulled_bytes_last": merges[-1]["pulled_bytes"],
                             "broadcast_bytes_last": merges[-1]["broadcast_bytes"],
-                            "multicast": merges[-1]["multicast"]}
+                            "multicast": merges[-1]["multicast"],
+                            "phases_ms_last": merges[-1].get("phases_ms")}
             if nccl_arm:
                 out["merge"]["allreduce_bytes"] = merges[-1]["allreduce_bytes"]
         if e2e_ms is not None:
             out["e2e"] = {"value": round(tokens_per_step * n_nodes * args.steps / (e2e_ms_max / 1e3), 1),
-                          "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 4}
+                          "unit": "tokens/s", "h2d_bytes_per_step": A * B * S * 4, "d2h_bytes_per_step": 4}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()

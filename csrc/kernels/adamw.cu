@@ -8,14 +8,16 @@
 //
 // Everything the step needs lives on the device (hyper-parameter block, step counter, skip flag), so
 // the whole train step can be replayed from a CUDA graph: the host only rewrites hp[HP_LR].
-// The update also writes the bf16 compute copy of every parameter used by the GEMMs.
+// The update also writes the bf16 compute copy of every parameter used by the GEMMs, and with
+// hp[HP_ZERO_GRAD] != 0 it clears every gradient it has read (also on a skipped step), so the next
+// step's backward - whose weight-gradient GEMMs accumulate - starts from zero without a separate pass.
 #include "common.cuh"
 
 namespace {
 
 enum HP : int {
   HP_LR = 0, HP_B1 = 1, HP_B2 = 2, HP_EPS = 3, HP_WD = 4, HP_BC1 = 5, HP_BC2 = 6, HP_MAXNORM = 7,
-  HP_CLIP_GLOBAL = 8, HP_STEP = 9, HP_DO_UPDATE = 10, HP_COUNT = 16
+  HP_CLIP_GLOBAL = 8, HP_STEP = 9, HP_DO_UPDATE = 10, HP_ZERO_GRAD = 11, HP_COUNT = 16
 };
 
 // chunk i covers [cstart[i], cend[i]) of segment cseg[i]
@@ -51,13 +53,19 @@ __global__ void adam_prepare_kernel(float* hp, const float* loss_flag) {
   hp[HP_DO_UPDATE] = 1.f;
 }
 
-__global__ void adamw_update_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+__global__ void adamw_update_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
                                     float* __restrict__ v, __nv_bfloat16* __restrict__ p16, const int* __restrict__ cseg,
                                     const long long* __restrict__ cstart, const long long* __restrict__ cend,
                                     const float* __restrict__ norms, int nseg, const float* __restrict__ hp) {
-  if (hp[HP_DO_UPDATE] == 0.f) return;
+  const bool upd = hp[HP_DO_UPDATE] != 0.f, zero = hp[HP_ZERO_GRAD] != 0.f;
   const int c = blockIdx.x;
   const long long s = cstart[c], e = cend[c];
+  if (!upd) {
+    if (zero)
+      for (long long i = s + threadIdx.x * 4; i < e; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(g + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
   const float lr = hp[HP_LR], b1 = hp[HP_B1], b2 = hp[HP_B2], eps = hp[HP_EPS], wd = hp[HP_WD];
   const float bc1 = hp[HP_BC1], bc2 = hp[HP_BC2], maxn = hp[HP_MAXNORM];
   float coef = 1.f;
@@ -76,6 +84,7 @@ __global__ void adamw_update_kernel(float* __restrict__ p, const float* __restri
   for (long long i = s + threadIdx.x * 4; i < e; i += blockDim.x * 4) {
     float4 pp = *reinterpret_cast<float4*>(p + i);
     float4 gg = *reinterpret_cast<const float4*>(g + i);
+    if (zero) *reinterpret_cast<float4*>(g + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 mm = *reinterpret_cast<float4*>(m + i);
     float4 vv = *reinterpret_cast<float4*>(v + i);
     float* pa = &pp.x; const float* ga = &gg.x; float* ma = &mm.x; float* va = &vv.x;
@@ -120,7 +129,7 @@ __global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
 
 // Chunk tables (cseg/cstart/cend, `nchunks` entries) are device arrays built once by the host; chunk
 // bounds must be multiples of 4 elements and every buffer 16-byte aligned.
-DT_API int dt_adamw_step(float* p, const float* g, float* m, float* v, void* p16, const int* cseg,
+DT_API int dt_adamw_step(float* p, float* g, float* m, float* v, void* p16, const int* cseg,
                          const long long* cstart, const long long* cend, int nchunks, float* norms, int nseg,
                          float* hp, const float* loss_flag, cudaStream_t st) {
   DT_CUDA_RET(cudaMemsetAsync(norms, 0, sizeof(float) * nseg, st));
@@ -135,7 +144,7 @@ DT_API int dt_adamw_step(float* p, const float* g, float* m, float* v, void* p16
 
 // Prepare + update only: `norms` already holds the per-segment squared gradient norms (e.g. summed over a
 // tensor-parallel group after dt_seg_sqnorm).
-DT_API int dt_adamw_apply(float* p, const float* g, float* m, float* v, void* p16, const int* cseg,
+DT_API int dt_adamw_apply(float* p, float* g, float* m, float* v, void* p16, const int* cseg,
                           const long long* cstart, const long long* cend, int nchunks, const float* norms, int nseg,
                           float* hp, const float* loss_flag, cudaStream_t st) {
   adam_prepare_kernel<<<1, 1, 0, st>>>(hp, loss_flag);

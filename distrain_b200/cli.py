@@ -287,6 +287,8 @@ def apply_run_overrides(run, args):
         run.optim.lr = args.lr
     if getattr(args, "batch_size", None) is not None:
         run.micro_batch = args.batch_size
+    if getattr(args, "grad_accum", None) is not None:
+        run.grad_accum_steps = max(int(args.grad_accum), 1)
     if getattr(args, "seq_len", None) is not None:
         run.seq_len = args.seq_len
         run.model.max_seq_len = max(run.model.max_seq_len, args.seq_len)
@@ -317,10 +319,11 @@ def cmd_train_box(args):
                 out.write(json.dumps(rec) + "\n")
                 out.flush()
     emit({"event": "train_box_start", "preset": run.name, "nodes": n_nodes, "ranks": br.world, "tp": run.tp,
-          "micro_batch": run.micro_batch, "seq_len": run.seq_len, "push_every": run.push_every, "data": desc,
+          "micro_batch": run.micro_batch, "grad_accum_steps": run.grad_accum_steps, "seq_len": run.seq_len,
+          "push_every": run.push_every, "data": desc,
           "resumed_version": getattr(node.sync, "resumed_version", 0), "data_resumed": data_resumed})
     done = 0
-    tokens_per_step = run.micro_batch * (run.seq_len - 1) * n_nodes
+    tokens_per_step = run.grad_accum_steps * run.micro_batch * (run.seq_len - 1) * n_nodes
     while done < args.steps:
         k = min(args.log_every, args.steps - done)
         t0 = time.time()
@@ -753,6 +756,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--data-dir", help="directory of shard_XXXX.bin token shards (default: synthetic tokens)")
     p.add_argument("--shards-fraction", type=float, default=0.2, help="share of the shards each node reads")
     p.add_argument("--batch-size", type=int)
+    p.add_argument("--grad-accum", type=int, help="micro-batches per optimizer step (gradient accumulation)")
     p.add_argument("--seq-len", type=int)
     p.add_argument("--push-every", type=int)
     p.add_argument("--top-k", type=float)

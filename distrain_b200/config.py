@@ -287,6 +287,9 @@ class RunConfig(_Json):
     model: ModelConfig = field(default_factory=lambda: preset("tiny"))
     seq_len: int = 1024
     micro_batch: int = 32
+    # micro-batches per optimizer step: gradients of grad_accum_steps x micro_batch sequences are summed
+    # before one clip + AdamW update (the effective batch); push_every counts optimizer steps
+    grad_accum_steps: int = 1
     push_every: int = 50
     optim: OptimConfig = field(default_factory=OptimConfig)
     compression: CompressionConfig = field(default_factory=lambda: CompressionConfig(

@@ -16,6 +16,14 @@ Per step (all on the current stream):
 The step mirrors the reference's continuous-loop step (node/cli/src/continuous.rs:598-637): loss on
 tokens[:, :-1] -> tokens[:, 1:], a NaN loss skips the optimiser update (decided on the device).
 
+Gradient accumulation (``grad_accum`` = A > 1): one step takes A micro-batches of B sequences
+(``ids`` is [A*B, S]); forward + backward run once per micro-batch on the same activation buffers, the
+weight-gradient GEMMs accumulate into the fp32 gradients, the loss is the mean over all A*B*T tokens,
+and clipping + AdamW run once per step. This is the accumulation the reference's trainer intends
+(node/cli/src/trainer.rs:592-630), where the optimiser instead steps after every micro-batch.
+Gradients are cleared by the AdamW kernel after it has read them (also on a skipped step), so no
+separate zeroing pass runs inside a step.
+
 Options: ``tp`` (a ``parallel.tensor_parallel.TensorParallel``) runs this replica split over a
 tensor-parallel group (local heads / FFN rows; all-reduces after the row-parallel GEMMs in the forward
 and the column-parallel data-gradient GEMMs in the backward; group-summed clip norms). ``act_ckpt``
@@ -34,13 +42,15 @@ from ..config import ModelConfig, OptimConfig
 from .params import ParamLayout, init_flat
 from .oracle import rope_tables
 
-HP_LR, HP_B1, HP_B2, HP_EPS, HP_WD, HP_BC1, HP_BC2, HP_MAXNORM, HP_CLIP_GLOBAL, HP_STEP, HP_DO_UPDATE = range(11)
+HP_LR, HP_B1, HP_B2, HP_EPS, HP_WD, HP_BC1, HP_BC2, HP_MAXNORM, HP_CLIP_GLOBAL, HP_STEP, HP_DO_UPDATE, \
+    HP_ZERO_GRAD = range(12)
 
 
 class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
-                 lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False):
+                 lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False,
+                 grad_accum: int = 1):
         self.cfg = cfg
         self.tp = tp
         self.act_ckpt = act_ckpt
@@ -48,6 +58,7 @@ class TrainEngine:
         self.optim = optim or OptimConfig()
         self.device = torch.device(device)
         self.B, self.S = batch, seq_len
+        self.A = max(int(grad_accum), 1)
         self.T = seq_len - 1
         self.M = self.B * self.T
         self.attn_impl = attn_impl
@@ -70,7 +81,7 @@ class TrainEngine:
         self.hp = torch.zeros(16, dtype=f32, device=dev)
         self._hp_host = torch.zeros(16, dtype=f32).pin_memory() if dev.type == "cuda" else torch.zeros(16)
         # ── inputs / outputs ──
-        self.ids = torch.zeros(batch, seq_len, dtype=torch.int32, device=dev)
+        self.ids = torch.zeros(self.A * batch, seq_len, dtype=torch.int32, device=dev)
         self.loss = torch.zeros(4, dtype=f32, device=dev)  # [mean loss, nonfinite flag, -, -]
         cos, sin = rope_tables(cfg, self.T)
         self.cos, self.sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
@@ -99,7 +110,7 @@ class TrainEngine:
         self.xs = torch.empty(M, H, dtype=bf16, device=dev)
         self.lm_chunk = min(lm_chunk_rows, M)
         self.logits = torch.empty(self.lm_chunk, V, dtype=bf16, device=dev)
-        self.loss_rows = torch.empty(M, dtype=f32, device=dev)
+        self.loss_rows = torch.empty(self.A * M, dtype=f32, device=dev)
         # ── backward scratch ──
         self.br = torch.empty(M, H, dtype=bf16, device=dev)
         self.dresid = torch.empty(M, H, dtype=f32, device=dev)
@@ -187,27 +198,36 @@ class TrainEngine:
         h[HP_B1], h[HP_B2], h[HP_EPS], h[HP_WD] = o.beta1, o.beta2, o.eps, o.weight_decay
         h[HP_MAXNORM] = o.grad_clip_norm
         h[HP_CLIP_GLOBAL] = 1.0 if o.clip_global else 0.0
-        # copy only the configuration slots; step/bias-correction slots are device-owned
+        h[HP_ZERO_GRAD] = 1.0
+        # copy only the configuration slots; step/bias-correction/skip slots are device-owned
         self.hp[:HP_BC1].copy_(h[:HP_BC1], non_blocking=True)
         self.hp[HP_MAXNORM:HP_STEP].copy_(h[HP_MAXNORM:HP_STEP], non_blocking=True)
+        self.hp[HP_ZERO_GRAD:HP_ZERO_GRAD + 1].copy_(h[HP_ZERO_GRAD:HP_ZERO_GRAD + 1], non_blocking=True)
 
     def set_lr(self, lr: float):
         self._write_hp(lr)
 
     def set_tokens(self, tokens: torch.Tensor):
+        """[A*B, S] int32 token ids of one step (A micro-batches of B sequences)."""
         self.ids.copy_(tokens, non_blocking=True)
 
     # ───────────────────────── the step ─────────────────────────
-    def forward_backward(self):
+    def forward_backward(self, micro: int = 0, zero_grad: bool = True):
+        """Forward + backward of micro-batch ``micro`` (rows [micro*B, (micro+1)*B) of ``ids``), adding its
+        gradients into ``grad`` (cleared first when ``zero_grad``); the loss of the step is reduced after
+        the last micro-batch."""
         cfg = self.cfg
         M, H, F, T, S, W, d, nh, nkv, V = self.M, self.H, self.F, self.T, self.S, self.W, self.d, self.nh, self.nkv, self.V
         eps = cfg.norm_eps
         Lr = cfg.num_layers
         if self._tp_active() and self.tp.fused:
             self.tp.begin_step(4 * Lr + ((Lr - 1) if self.act_ckpt else 0))
-        self.grad.zero_()
+        if zero_grad:
+            self.grad.zero_()
+        ids = self.ids[micro * self.B:(micro + 1) * self.B]
+        loss_rows = self.loss_rows[micro * M:(micro + 1) * M]
         # ── forward ──
-        ops.add_rmsnorm_fwd(emb=self.E, ids=self.ids, T=T, S=S, w=self.pv[0]["attn_norm"], out_resid=self.resid_in[0],
+        ops.add_rmsnorm_fwd(emb=self.E, ids=ids, T=T, S=S, w=self.pv[0]["attn_norm"], out_resid=self.resid_in[0],
                             y=self.xn1[0], rstd=self.rstd1[0], eps=eps, M=M, H=H)
         for l in range(Lr):
             pv, wv = self.pv[l], self.wv[l]
@@ -227,18 +247,19 @@ class TrainEngine:
                 self._row_parallel_add_norm(self.hact[l], wv["down_w"], x=self.resid_mid[l], w=self.fnorm,
                                             scale=self.oscale, out_resid=self.resid_fin, y=self.xs, rstd=self.rstd_f)
         # ── tied LM head + cross-entropy, chunked over rows; backward of the head fused per chunk ──
-        inv_m = 1.0 / M
+        inv_m = 1.0 / (M * self.A)
         for r0 in range(0, M, self.lm_chunk):
             rows = min(self.lm_chunk, M - r0)
             xs_c = self.xs[r0:r0 + rows]
             lg = self.logits[:rows]
             ops.gemm(xs_c, self.E16, lg, M=rows, N=V, K=H)
-            ops.ce_fwd_bwd(lg, self.ids, self.loss_rows[r0:r0 + rows], T=T, S=S, r0=r0, rows=rows, V=V,
+            ops.ce_fwd_bwd(lg, ids, loss_rows[r0:r0 + rows], T=T, S=S, r0=r0, rows=rows, V=V,
                            grad_scale=inv_m)
             ops.gemm(lg, self.E16, self.dxs[r0:r0 + rows], M=rows, N=H, K=V, b_mn=True, ldb=H)
             ops.gemm(lg, xs_c, self.gE, M=V, N=H, K=rows, a_mn=True, lda=V, b_mn=True, ldb=H, ldc=H,
                      epi=ops.EPI_F32_ATOMIC)
-        ops.loss_reduce(self.loss_rows, M, inv_m, self.loss)
+        if micro == self.A - 1:
+            ops.loss_reduce(self.loss_rows, self.A * M, inv_m, self.loss)
         # ── backward ──
         ops.rmsnorm_bwd(dy=self.dxs, x=self.resid_fin, rstd=self.rstd_f, w=self.fnorm, scale=self.oscale,
                         dresid_out=self.dresid, dresid16=self.g16, dw=self.g_fnorm, dscale=self.g_oscale, M=M, H=H)
@@ -264,7 +285,7 @@ class TrainEngine:
                 self.dqkv, wv["qkv_w"], lambda: ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"]),
                 x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"], dresid_in=self.dresid,
                 dresid_out=self.dresid, dresid16=self.g16 if l > 0 else None, dw=gv["attn_norm"])
-        ops.embedding_bwd(self.dresid, self.ids, self.gE, T=T, S=S, M=M, H=H)
+        ops.embedding_bwd(self.dresid, ids, self.gE, T=T, S=S, M=M, H=H)
 
     def _tp_active(self) -> bool:
         return self.tp is not None and self.tp.size > 1
@@ -334,7 +355,9 @@ class TrainEngine:
                        self.norms, self.hp, self.loss)
 
     def step_kernels(self):
-        self.forward_backward()
+        # gradients are zero here: cleared at allocation and by every optimizer step
+        for a in range(self.A):
+            self.forward_backward(a, zero_grad=False)
         self.optimizer_step()
 
     # ───────────────────────── CUDA graph ─────────────────────────
@@ -352,9 +375,10 @@ class TrainEngine:
         # the update exactly as for a NaN step (no copies of the state: large presets have no room)
         with torch.cuda.stream(s):
             for _ in range(warmup):
-                self.forward_backward()
+                for a in range(self.A):
+                    self.forward_backward(a, zero_grad=False)
                 self.loss[1].fill_(1.0)
-                self.optimizer_step()
+                self.optimizer_step()  # skipped update; clears the gradients
         torch.cuda.current_stream().wait_stream(s)
         g = torch.cuda.CUDAGraph()
         from ..ops import _lib
@@ -381,4 +405,4 @@ class TrainEngine:
         return self.layout.to_state_dict(self.master)
 
     def flops_per_step(self) -> float:
-        return self.cfg.flops_per_token(self.T) * self.M
+        return self.cfg.flops_per_token(self.T) * self.M * self.A

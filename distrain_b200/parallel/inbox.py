@@ -279,7 +279,7 @@ class InBoxSync:
         self.loss_ema = loss if self.loss_count == 1 else self.loss_ema * 0.9 + loss * 0.1
 
     def after_step(self):
-        self.round_tokens += self.run.micro_batch * self.run.seq_len
+        self.round_tokens += self.run.grad_accum_steps * self.run.micro_batch * self.run.seq_len
         if self.node.round_step >= self.run.push_every:
             warm = max(int(self.run.push_every * self.run.optim.warmup_fraction), 2)
             if self.first_round and self.node.round_step <= warm:

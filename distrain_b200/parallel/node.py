@@ -26,23 +26,27 @@ class BatchFeed:
     reads element i % depth at step i and waits for step i - 1 before it issues step i + 1, so a buffer is
     refilled only after the copy that read it has completed."""
 
-    def __init__(self, source, batch: int, seq: int, depth: int = 3):
+    def __init__(self, source, batch: int, seq: int, depth: int = 3, accum: int = 1):
         pin = torch.cuda.is_available()
-        self.bufs = [torch.empty(batch, seq, dtype=torch.int32) for _ in range(depth)]
+        self.bufs = [torch.empty(accum * batch, seq, dtype=torch.int32) for _ in range(depth)]
         if pin:
             self.bufs = [b.pin_memory() for b in self.bufs]
         self.source = source
+        self.batch, self.accum = batch, accum
         self.fetched = 0
 
     def __len__(self):
         return len(self.bufs)
 
     def __getitem__(self, k: int) -> torch.Tensor:
-        b = self.source()
-        if tuple(b.shape) != tuple(self.bufs[k].shape):
-            raise ValueError(f"batch source gave {tuple(b.shape)}, expected {tuple(self.bufs[k].shape)}")
-        self.bufs[k].copy_(b)
-        self.fetched += 1
+        # one step's batch: `accum` consecutive source batches (the micro-batches of the step)
+        for a in range(self.accum):
+            b = self.source()
+            want = (self.batch, self.bufs[k].shape[1])
+            if tuple(b.shape) != want:
+                raise ValueError(f"batch source gave {tuple(b.shape)}, expected {want}")
+            self.bufs[k][a * self.batch:(a + 1) * self.batch].copy_(b)
+            self.fetched += 1
         return self.bufs[k]
 
 
@@ -62,7 +66,7 @@ class InBoxNode:
         # `n_shards` over `dp_group` (the ranks that hold that shard on every node)
         self.engine = TrainEngine(run.model, run.micro_batch, run.seq_len, optim=run.optim, device=self.device,
                                   seed=run.seed, init_std=run.init_std, attn_impl=attn_impl, tp=tp,
-                                  act_ckpt=run.activation_checkpointing)
+                                  act_ckpt=run.activation_checkpointing, grad_accum=run.grad_accum_steps)
         self.enable_push = enable_push
         self.watchdog = None
         if run.watchdog_step_secs > 0:
@@ -88,7 +92,7 @@ class InBoxNode:
             return
         pe = self.run.push_every
         self.round_step = max(pe - int(steps_ahead), 0)
-        self.sync.round_tokens = self.round_step * self.run.micro_batch * self.run.seq_len
+        self.sync.round_tokens = self.round_step * self.run.grad_accum_steps * self.run.micro_batch * self.run.seq_len
         if self.sync.first_round:
             self.engine.set_lr(self.run.optim.lr)
             self.sync._lr_set = self.run.optim.lr
@@ -100,7 +104,8 @@ class InBoxNode:
             self._graph_ready = True
 
     def train_step_device(self, tokens_dev: torch.Tensor):
-        """One training step on tokens already resident on the device (no host sync)."""
+        """One training step on tokens already resident on the device (no host sync): [A*B, S] int32 with
+        A = ``grad_accum_steps`` micro-batches of B = ``micro_batch`` sequences."""
         self._ensure_graph()
         with nvtx("step"):
             if self.sync is not None:
@@ -143,9 +148,10 @@ class InBoxNode:
 
     def train_stream(self, source, steps: int):
         """``train_steps_e2e`` over a batch source (a callable returning [micro_batch, seq_len] int32 CPU
-        tensors, e.g. ``ShardLoader.next_batch``); returns the per-step losses."""
+        tensors, e.g. ``ShardLoader.next_batch``; a step takes ``grad_accum_steps`` of them); returns the
+        per-step losses."""
         if getattr(self, "_feed", None) is None or self._feed.source is not source:
-            self._feed = BatchFeed(source, self.run.micro_batch, self.run.seq_len)
+            self._feed = BatchFeed(source, self.run.micro_batch, self.run.seq_len, accum=self.run.grad_accum_steps)
         return self.train_steps_e2e(self._feed, steps)
 
     def _observe(self, loss: float, losses: list):

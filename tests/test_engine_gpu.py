@@ -58,3 +58,49 @@ def test_engine_graph_training_decreases_loss():
         eng.step()
         losses.append(eng.loss[0].item())
     assert losses[-1] < losses[0] - 1.0, losses
+
+
+def test_grad_accumulation_equals_one_large_batch():
+    """2 micro-batches of B/2 accumulate to the gradients (and loss, and update) of one batch of B: same
+    weights, same tokens, gradients summed in fp32 by the weight-gradient GEMMs, one AdamW step; the
+    optimizer clears the gradients it has read."""
+    from distrain_b200.models.engine import TrainEngine
+    from distrain_b200.config import OptimConfig
+    from distrain_b200 import ops
+    torch.manual_seed(3)
+    cfg = _small_cfg()
+    B, S = 4, 65
+    tokens = torch.randint(0, cfg.vocab_size, (B, S), dtype=torch.int32).cuda()
+    one = TrainEngine(cfg, B, S, optim=OptimConfig(lr=1e-3), device="cuda", seed=5)
+    acc = TrainEngine(cfg, B // 2, S, optim=OptimConfig(lr=1e-3), device="cuda", seed=5, grad_accum=2)
+    assert torch.equal(one.master, acc.master)
+    one.set_tokens(tokens)
+    acc.set_tokens(tokens)
+    one.forward_backward()
+    acc.forward_backward(0, zero_grad=True)
+    acc.forward_backward(1, zero_grad=False)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert abs(one.loss[0].item() - acc.loss[0].item()) < 1e-5
+    ga, gb = one.layout.views(one.grad), acc.layout.views(acc.grad)
+    for k in ga:
+        rel = ((ga[k].double() - gb[k].double()).norm() / (ga[k].double().norm() + 1e-12)).item()
+        assert rel < 1e-4, (k, rel)
+    # full steps: one AdamW update each, gradients cleared afterwards
+    one.grad.zero_()
+    acc.grad.zero_()
+    one.step_kernels()
+    acc.step_kernels()
+    torch.cuda.synchronize()
+    assert int(one.grad.count_nonzero()) == 0 and int(acc.grad.count_nonzero()) == 0
+    rel = ((one.master - acc.master).norm() / one.master.norm()).item()
+    assert rel < 1e-5, rel
+    assert abs(one.loss[0].item() - acc.loss[0].item()) < 1e-5
+    # second step through the captured graph: the cleared gradients keep the two in step
+    one.capture()
+    acc.capture()
+    one.step()
+    acc.step()
+    torch.cuda.synchronize()
+    assert abs(one.loss[0].item() - acc.loss[0].item()) < 1e-4
+    assert ((one.master - acc.master).norm() / one.master.norm()).item() < 1e-5

@@ -20,7 +20,8 @@ def _args(**kw):
     base = dict(push_every=None, tp=None, checkpoint_store=None, checkpoint_every=None, keep_versions=None,
                 metrics_port=None, watchdog_secs=None, swap_mode=None, ef_on_swap=None, seed=None, payload_slots=None,
                 resume=False, loss_based_lr=False, bandwidth_adaptive=False, reset_optimizer=False,
-                activation_checkpointing=False, top_k=None, no_int8=False, lr=None, batch_size=None, seq_len=None)
+                activation_checkpointing=False, top_k=None, no_int8=False, lr=None, batch_size=None, seq_len=None,
+                grad_accum=None)
     base.update(kw)
     return argparse.Namespace(**base)
 
@@ -98,6 +99,21 @@ def test_batch_feed_round_robin_and_shape_check():
     bad = BatchFeed(lambda: torch.zeros(1, 3, dtype=torch.int32), 2, 3)
     with pytest.raises(ValueError):
         bad[0]
+
+
+def test_batch_feed_gathers_the_micro_batches_of_a_step():
+    """With gradient accumulation a step's buffer holds `accum` consecutive source batches."""
+    n = [0]
+
+    def src():
+        n[0] += 1
+        return torch.full((2, 3), n[0], dtype=torch.int32)
+    feed = BatchFeed(src, 2, 3, depth=2, accum=3)
+    b = feed[0]
+    assert b.shape == (6, 3) and feed.fetched == 3
+    assert [int(b[r, 0]) for r in range(6)] == [1, 1, 2, 2, 3, 3]
+    run = cli.apply_run_overrides(bench_config("tiny"), _args(grad_accum=4))
+    assert run.grad_accum_steps == 4 and run.micro_batch == 32
 
 
 def test_train_box_parser():
