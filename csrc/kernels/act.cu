@@ -122,6 +122,60 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   }
 }
 
+// Cross-entropy from the LM-head GEMM's fp32 softmax statistics (dt_gemm_logits_lse): one block per row
+// combines the row's `np` partial (max, sum exp) pairs into the log-sum-exp, writes
+// loss_row[r] = lse - target logit (both fp32), then replaces the bf16 logits of the row with
+// grad_scale * (softmax - onehot(target)) in one read + write pass.
+__global__ void ce_lse_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long ld, const float2* __restrict__ part,
+                                  int np, long long rows, const float* __restrict__ tgt_logit,
+                                  const int* __restrict__ ids, int T, int S, long long r0,
+                                  float* __restrict__ loss_row, int V, float grad_scale) {
+  __shared__ float sh[32];
+  __shared__ float sh_m[32];
+  const long long r = blockIdx.x;
+  const long long grow = r0 + r;
+  const long long b = grow / T, t = grow - b * T;
+  const int tgt = ids[b * S + t + 1];
+  float m = -INFINITY, s = 0.f;
+  for (int k = threadIdx.x; k < np; k += blockDim.x) {
+    const float2 p = part[(long long)k * rows + r];
+    if (p.x == -INFINITY) continue;
+    const float nm = fmaxf(m, p.x);
+    s = s * __expf(m - nm) + p.y * __expf(p.x - nm);
+    m = nm;
+  }
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float wm = warp_max(m);
+  float ws = warp_sum(m == -INFINITY ? 0.f : s * __expf(m - wm));
+  if (lane == 0) { sh_m[wid] = wm; sh[wid] = ws; }
+  __syncthreads();
+  int nw = blockDim.x >> 5;
+  if (wid == 0) {
+    float mm = lane < nw ? sh_m[lane] : -INFINITY;
+    float ss = lane < nw ? sh[lane] : 0.f;
+    float gm = warp_max(mm);
+    float gs = warp_sum((lane < nw && mm != -INFINITY) ? ss * __expf(mm - gm) : 0.f);
+    if (lane == 0) { sh_m[0] = gm; sh[0] = gs; }
+  }
+  __syncthreads();
+  const float lse = sh_m[0] + __logf(sh[0]);
+  if (threadIdx.x == 0) loss_row[r] = lse - tgt_logit[r];
+  __nv_bfloat16* z = logits + r * ld;
+  for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
+    uint4 q = *reinterpret_cast<const uint4*>(z + c);
+    uint32_t qq[4] = {q.x, q.y, q.z, q.w}, o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = unpack_bf16(qq[k]);
+      float p0 = __expf(f.x - lse), p1 = __expf(f.y - lse);
+      if (c + 2 * k == tgt) p0 -= 1.f;
+      if (c + 2 * k + 1 == tgt) p1 -= 1.f;
+      o[k] = pack_bf16(p0 * grad_scale, p1 * grad_scale);
+    }
+    *reinterpret_cast<uint4*>(z + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // out[0] = sum(loss_row[0:n]) * scale  (single block); out[1] = 1 if non-finite;
 // out[2] += out[0] and out[3] += 1 when finite (running round sums read at push time).
 __global__ void loss_reduce_kernel(const float* __restrict__ loss_row, long long n, float scale, float* out) {
@@ -175,5 +229,15 @@ DT_API int dt_ce_fwd_bwd(void* logits, long long ld, const int* ids, int T, int 
 
 DT_API int dt_loss_reduce(const float* loss_row, long long n, float scale, float* out, cudaStream_t st) {
   loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_row, n, scale, out);
+  return (int)cudaGetLastError();
+}
+
+DT_API int dt_ce_lse_bwd(void* logits, long long ld, const void* part, int np, long long rows, const float* tgt_logit,
+                         const int* ids, int T, int S, long long r0, float* loss_row, int V, float grad_scale,
+                         cudaStream_t st) {
+  if (V % 8 || ld % 8 || rows <= 0) return rows <= 0 ? 0 : -10;
+  ce_lse_bwd_kernel<<<(unsigned)rows, 512, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld,
+                                                    reinterpret_cast<const float2*>(part), np, rows, tgt_logit, ids,
+                                                    T, S, r0, loss_row, V, grad_scale);
   return (int)cudaGetLastError();
 }

@@ -84,7 +84,6 @@ __global__ void adamw_update_kernel(float* __restrict__ p, float* __restrict__ g
   for (long long i = s + threadIdx.x * 4; i < e; i += blockDim.x * 4) {
     float4 pp = *reinterpret_cast<float4*>(p + i);
     float4 gg = *reinterpret_cast<const float4*>(g + i);
-    if (zero) *reinterpret_cast<float4*>(g + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 mm = *reinterpret_cast<float4*>(m + i);
     float4 vv = *reinterpret_cast<float4*>(v + i);
     float* pa = &pp.x; const float* ga = &gg.x; float* ma = &mm.x; float* va = &vv.x;
@@ -100,6 +99,7 @@ __global__ void adamw_update_kernel(float* __restrict__ p, float* __restrict__ g
     *reinterpret_cast<float4*>(p + i) = pp;
     *reinterpret_cast<float4*>(m + i) = mm;
     *reinterpret_cast<float4*>(v + i) = vv;
+    if (zero) *reinterpret_cast<float4*>(g + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p16) {
       uint2 o;
       o.x = pack_bf16(pp.x, pp.y);

@@ -11,6 +11,21 @@
 //   staging box and write it with a TMA store (bf16 / fp32) or a TMA reduce-add (fp32 accumulation,
 //   used for split-K and gradient accumulation), so global writes are full-line and asynchronous.
 // * Tiles are visited by a persistent grid (one CTA per SM) in grouped order for L2 reuse.
+// * Fused SwiGLU (reference model.rs:292-296, h = silu(x Wg^T) * (x Wu^T)):
+//     forward (MODE 1): one 256-wide tile holds 128 gate columns and the 128 matching up columns (the B
+//       stage is filled from the gate rows and the up rows of the [2F, K] weight by two TMA loads); the
+//       epilogue stores gate and up (bf16, kept for the backward) and h = silu(g) * u from the fp32
+//       accumulators, so no separate activation pass reads the [M, 2F] product back;
+//     backward (MODE 2): the down-projection data gradient dh = dY Wd is never stored - the epilogue
+//       reads the saved gate / up values of its rows and writes dgate = dh * u * silu'(g) and
+//       dup = dh * silu(g) straight into the [M, 2F] gradient the gate/up GEMMs consume.
+// * LM head with softmax statistics (MODE 4, reference model.rs:323-339 and 804-811): besides the bf16
+//   logits, the epilogue keeps, per row and half tile, the running max and sum of exp of the fp32
+//   accumulators and the fp32 logit of the row's target token, so the cross-entropy's log-sum-exp and
+//   loss come from fp32 values and need no pass over the logits.
+// * Fused QKV bias + rotary embedding (MODE 3, reference model.rs:193-201 and 66-122): the QKV GEMM's
+//   epilogue adds the bias and applies the rotate-half rotation of every q / k head (position = row mod
+//   T, fp32 cos/sin tables [T, d/2]) before the single bf16 store; v heads get the bias only.
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its in-flight TMA loads and
 // MMAs, frees TMEM and returns with dt_error_word set.
 #include "common.cuh"
@@ -22,13 +37,29 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;                        // two per TMEM lane quadrant
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int GROUP_M = 16;
 
 enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ATOMIC = 2 };
 
 struct GemmArgs {
   int M, N, K;
+  // fused SwiGLU backward: the saved [M, 2F] gate|up product (row stride ld_gu), F = N
+  const __nv_bfloat16* gu;
+  long long ld_gu;
+  // fused QKV bias + RoPE: tables [T, hd/2], bias [N] (nullable), columns [0, rot_cols) are rotated heads
+  const float* cosT;
+  const float* sinT;
+  const float* bias;
+  int T, hd, rot_cols;
+  // logits + softmax statistics (MODE 4): per (row, tile column half) max and sum of exp of the fp32
+  // logits, and the fp32 logit of the row's target token (ids[b*S + t + 1], global row r0 + row)
+  float2* lse_part;
+  float* tgt_logit;
+  const int* ids;
+  int S;
+  long long r0;
   int num_kb;
   int split_k, kb_per_split;
   int tiles_m, tiles_n;
@@ -44,15 +75,19 @@ struct GemmArgs {
   unsigned* done_ctas;      // local scratch counter, returns to 0 after every launch
 };
 
-template <int BN>
+template <int BN, int MODE = 0>
 struct Cfg {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = 4 * 4096;  // one 4 KB staging box per epilogue warp
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  static constexpr int BOXES = (MODE == 0 || MODE == 4) ? 1 : 2;  // 4 KB staging boxes per epilogue warp
+  static constexpr int EPI_BYTES = EPI_WARPS * BOXES * 4096;
+  static constexpr int FIXED = EPI_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  // as many operand stages as fit next to the staging boxes (at most 6)
+  static constexpr int STAGES = (232448 - FIXED) / STAGE_BYTES < 6 ? (232448 - FIXED) / STAGE_BYTES : 6;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + FIXED;
+  static_assert(STAGES >= 3, "operand ring");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -65,11 +100,24 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = within / gm;
 }
 
-template <int BN, int A_MN, int B_MN>
+// logistic function with the hardware exponential and reciprocal (the activations are rounded to bf16)
+__device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(1.f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
+// 16-byte chunk `ch` (8 bf16) of row `lane` of a 32-row x 128-byte staging box in the TMA 128-byte
+// swizzle layout (chunk k of row r stored at k ^ (r & 7)), so the 32 lanes' stores spread over all banks
+__device__ __forceinline__ void box_put(uint8_t* box, int lane, int ch, uint4 v) {
+  *reinterpret_cast<uint4*>(box + lane * 128 + ((ch ^ (lane & 7)) * 16)) = v;
+}
+
+template <int BN, int A_MN, int B_MN, int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmCp, GemmArgs args) {
-  using C = Cfg<BN>;
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmCp,
+               const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC2,
+               const __grid_constant__ CUtensorMap tmC3, GemmArgs args) {
+  static_assert(MODE != 1 || (BN == 256 && !A_MN && !B_MN), "fused SwiGLU forward: 128 gate + 128 up columns");
+  using C = Cfg<BN, MODE>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -81,7 +129,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* tfull = bars + 2 * C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* gbar = drain + 1;  // [EPI_WARPS] per-warp operand loads of the SwiGLU backward epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;
 
@@ -95,9 +144,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * EPI_WARPS);
     }
     mbar_init(drain, 1);
+    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&gbar[w], 1);
     *abort_flag = 0;
     *consumed = 0;
     fence_barrier_init();
@@ -107,6 +157,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
+    if (MODE == 1 || MODE == 2) {
+      tma_prefetch_desc(&tmC2);
+      tma_prefetch_desc(&tmB2);
+      tma_prefetch_desc(&tmC3);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -129,7 +184,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         int s = unit % args.split_k, tile = unit / args.split_k;
         int mb, nb;
         tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
-        int m0 = mb * BM, n0 = nb * BN;
+        int m0 = mb * BM, n0 = nb * (MODE == 1 ? BN / 2 : BN);
         int kb0 = s * args.kb_per_split, kb1 = min(kb0 + args.kb_per_split, args.num_kb);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, DT_ERR_TIMEOUT_EMPTY, 100, abort_flag)) {
@@ -145,7 +200,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           } else {
             tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, m0);
           }
-          if (B_MN) {
+          if (MODE == 1) {
+            // gate rows [n0, n0+128) then the matching up rows: two 128-row boxes, the same swizzled
+            // layout as one 256-row box
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
+            tma_load_2d(b_dst + (BN / 2) * BK * 2, &tmB2, &full[stage], kb * BK, n0);
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * j, kb * BK);
           } else {
@@ -212,15 +272,99 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   } else {
-    // ───────────── Epilogue: warps 2..5 ─────────────
-    // TMEM -> registers (tcgen05.ld, this warp's 32 lanes = 32 tile rows) -> 4 KB shared staging box ->
-    // TMA store (bf16 / fp32) or TMA reduce-add (fp32 accumulate); the tensor map clips the M/N tails.
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    uint8_t* stage = sEpi + quad * 4096;
-    const bool is_bf16 = args.epi == EPI_BF16;
-    const int cols_per_box = is_bf16 ? 64 : 32;  // 32 rows x 128 B (bf16) / 32 rows x 128 B (fp32)
+    // ───────────── Epilogue: warps 2..9 ─────────────
+    // Two warps per TMEM lane quadrant (warp w may read lanes 32*(w%4)..+31), each draining half of the
+    // tile's columns: TMEM -> registers (tcgen05.ld) -> swizzled 4 KB shared staging box(es) -> TMA store
+    // or TMA reduce-add (fp32 accumulation); the tensor maps clip the M / N tails.
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int hsel = ew >> 2;  // which half of the tile's columns this warp drains
+    uint8_t* stage = sEpi + ew * (C::BOXES * 4096);
     int local = 0;
     bool pending = false;
+    if constexpr (MODE == 2) {
+      // SwiGLU backward: this warp's 32 rows x 64 columns of the saved gate / up values arrive by TMA in
+      // its two staging boxes (issued one tile ahead), are overwritten in place with dgate / dup and
+      // stored from there.
+      uint64_t* gb = &gbar[ew];
+      auto prefetch = [&](int u) {
+        int mb, nb;
+        tile_coords(u / args.split_k, args.tiles_m, args.tiles_n, mb, nb);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(gb, 8192);
+          tma_load_2d(stage, &tmB2, gb, nb * BN + hsel * 64, mb * BM + quad * 32);
+          tma_load_2d(stage + 4096, &tmC3, gb, nb * BN + hsel * 64, mb * BM + quad * 32);
+        }
+        __syncwarp();
+      };
+      bool inflight = false;
+      if (blockIdx.x < total_units) {
+        prefetch(blockIdx.x);
+        inflight = true;
+      }
+      for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
+        int mb, nb;
+        tile_coords(unit / args.split_k, args.tiles_m, args.tiles_n, mb, nb);
+        const int acc = local & 1;
+        if (!mbar_wait_bounded(&tfull[acc], (local >> 1) & 1, DT_ERR_TIMEOUT_TMEM, 300, abort_flag)) break;
+        if (!mbar_wait_bounded(gb, local & 1, DT_ERR_TIMEOUT_FULL, 301, abort_flag)) break;
+        inflight = false;
+        tc_fence_after();
+        const int row0 = mb * BM + quad * 32;
+        const int gcol = nb * BN + hsel * 64;
+        const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + hsel * 64;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t d[32];
+          tmem_ld_32x32b_x32(t_row + 32 * half, d);
+          tmem_ld_wait();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const int off = lane * 128 + (((half * 4 + ch) ^ (lane & 7)) * 16);
+            uint4* pg = reinterpret_cast<uint4*>(stage + off);
+            uint4* pu = reinterpret_cast<uint4*>(stage + 4096 + off);
+            const uint4 gv = *pg, uv = *pu;
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+            const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+            uint32_t og[4], ou[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 a = unpack_bf16(gw[e]), b = unpack_bf16(uw[e]);
+              const float d0 = __uint_as_float(d[ch * 8 + 2 * e]), d1 = __uint_as_float(d[ch * 8 + 2 * e + 1]);
+              const float s0 = sigmoid_f(a.x), s1 = sigmoid_f(a.y);
+              const float ds0 = s0 * (1.f + a.x * (1.f - s0)), ds1 = s1 * (1.f + a.y * (1.f - s1));
+              og[e] = pack_bf16(d0 * b.x * ds0, d1 * b.y * ds1);
+              ou[e] = pack_bf16(d0 * a.x * s0, d1 * a.y * s1);
+            }
+            *pg = make_uint4(og[0], og[1], og[2], og[3]);
+            *pu = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);  // this warp's TMEM columns are read
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (gcol < args.N && row0 < args.M) {
+            tma_store_2d(&tmC, stage, gcol, row0);          // dgate -> dgu[:, gcol]
+            tma_store_2d(&tmC2, stage + 4096, gcol, row0);  // dup -> dgu[:, F + gcol]
+            bulk_commit();
+          }
+          bulk_wait_read0();  // the boxes take the next tile's gate / up values
+        }
+        __syncwarp();
+        if (unit + (int)gridDim.x < total_units) {
+          prefetch(unit + gridDim.x);
+          inflight = true;
+        }
+      }
+      if (inflight) {  // an aborted run: let the last prefetch land before the CTA exits
+        uint64_t t0 = dt_globaltimer();
+        while (!mbar_try_wait(gb, local & 1)) if (dt_globaltimer() - t0 > 20000000ull) break;
+      }
+    } else {
+    const bool is_bf16 = args.epi == EPI_BF16;
+    const int cols_per_box = is_bf16 ? 64 : 32;  // 32 rows x 128 B (bf16) / 32 rows x 128 B (fp32)
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
       int tile = unit / args.split_k;
       int mb, nb;
@@ -231,14 +375,234 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const int row0 = mb * BM + quad * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      if constexpr (MODE == 1) {
+        // TMEM columns [0, 128): gate, [128, 256): up, for output columns nb*128 + [0, 128); this warp
+        // takes output columns [hsel*64, hsel*64 + 64)
+        uint8_t* boxA = stage;
+        uint8_t* boxB = stage + 4096;
+        const int c0 = hsel * 64;
+        const int gcol = nb * (BN / 2) + c0;
+        const bool live = (gcol < args.N) && (row0 < args.M);
+        if (pending) {  // both boxes of the previous tile must have been read out of shared memory
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          pending = false;
+        }
+        uint32_t hh[2][16];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c0 + 32 * half, g);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c0 + 32 * half, u);
+          tmem_ld_wait();
+          if (live) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              const uint32_t* gs = g + ch * 8;
+              const uint32_t* us = u + ch * 8;
+              uint4 vg, vu;
+              vg.x = pack_bf16(__uint_as_float(gs[0]), __uint_as_float(gs[1]));
+              vg.y = pack_bf16(__uint_as_float(gs[2]), __uint_as_float(gs[3]));
+              vg.z = pack_bf16(__uint_as_float(gs[4]), __uint_as_float(gs[5]));
+              vg.w = pack_bf16(__uint_as_float(gs[6]), __uint_as_float(gs[7]));
+              vu.x = pack_bf16(__uint_as_float(us[0]), __uint_as_float(us[1]));
+              vu.y = pack_bf16(__uint_as_float(us[2]), __uint_as_float(us[3]));
+              vu.z = pack_bf16(__uint_as_float(us[4]), __uint_as_float(us[5]));
+              vu.w = pack_bf16(__uint_as_float(us[6]), __uint_as_float(us[7]));
+              box_put(boxA, lane, half * 4 + ch, vg);
+              box_put(boxB, lane, half * 4 + ch, vu);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                hh[half][ch * 4 + e] =
+                    pack_bf16(silu_f(__uint_as_float(gs[2 * e])) * __uint_as_float(us[2 * e]),
+                              silu_f(__uint_as_float(gs[2 * e + 1])) * __uint_as_float(us[2 * e + 1]));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);  // TMEM read; the stores below overlap the next tile's products
+        if (live) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, boxA, gcol, row0);   // gate -> gu[:, gcol]
+            bulk_commit();
+            tma_store_2d(&tmC2, boxB, gcol, row0);  // up -> gu[:, F + gcol]
+            bulk_commit();
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // box A free again
+          }
+          __syncwarp();
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch)
+              box_put(boxA, lane, half * 4 + ch,
+                      make_uint4(hh[half][ch * 4], hh[half][ch * 4 + 1], hh[half][ch * 4 + 2], hh[half][ch * 4 + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC3, boxA, gcol, row0);  // h -> h[:, gcol]
+            bulk_commit();
+          }
+          pending = true;
+        }
+        continue;
+      }
+      if constexpr (MODE == 3) {
+        const int row = row0 + lane;
+        const int t = row % args.T;
+        const int D = args.hd;
+        const float* crow = args.cosT + (long long)t * (D / 2);
+        const float* srow = args.sinT + (long long)t * (D / 2);
+        // this warp's heads: the half of the tile's columns given by hsel (a whole head when D > BN/2
+        // goes to hsel 0)
+        const int span = (D <= BN / 2) ? BN / 2 : BN;
+        const int h_lo = (D <= BN / 2) ? hsel * span : (hsel ? BN : 0);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += cols_per_box) {
+        for (int hc0 = h_lo; hc0 < h_lo + span && hc0 < BN; hc0 += D) {
+          const int hc = nb * BN + hc0;  // first output column of this head
+          const bool live = (hc < args.N) && (row0 < args.M);
+          if (pending) {
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            pending = false;
+          }
+          if (!live) continue;
+          if (hc < args.rot_cols) {
+            // rotate-half pairs (j, j + D/2): 32 pairs per pass
+#pragma unroll 1
+            for (int j0 = 0; j0 < D / 2; j0 += 32) {
+              uint32_t x1[32], x2[32];
+              tmem_ld_32x32b_x32(t_row + hc0 + j0, x1);
+              tmem_ld_32x32b_x32(t_row + hc0 + D / 2 + j0, x2);
+              tmem_ld_wait();
+#pragma unroll
+              for (int ch = 0; ch < 4; ++ch) {
+                const int e0 = j0 + ch * 8;
+                const float4 c0 = *reinterpret_cast<const float4*>(crow + e0);
+                const float4 c1 = *reinterpret_cast<const float4*>(crow + e0 + 4);
+                const float4 s0 = *reinterpret_cast<const float4*>(srow + e0);
+                const float4 s1 = *reinterpret_cast<const float4*>(srow + e0 + 4);
+                const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                float b1[8], b2[8];
+                if (args.bias) {
+                  const float4 p0 = *reinterpret_cast<const float4*>(args.bias + hc + e0);
+                  const float4 p1 = *reinterpret_cast<const float4*>(args.bias + hc + e0 + 4);
+                  const float4 q0 = *reinterpret_cast<const float4*>(args.bias + hc + D / 2 + e0);
+                  const float4 q1 = *reinterpret_cast<const float4*>(args.bias + hc + D / 2 + e0 + 4);
+                  b1[0] = p0.x; b1[1] = p0.y; b1[2] = p0.z; b1[3] = p0.w;
+                  b1[4] = p1.x; b1[5] = p1.y; b1[6] = p1.z; b1[7] = p1.w;
+                  b2[0] = q0.x; b2[1] = q0.y; b2[2] = q0.z; b2[3] = q0.w;
+                  b2[4] = q1.x; b2[5] = q1.y; b2[6] = q1.z; b2[7] = q1.w;
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) b1[e] = b2[e] = 0.f;
+                }
+                uint32_t y1[4], y2[4];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                  const float a0 = __uint_as_float(x1[ch * 8 + e]) + b1[e];
+                  const float a1 = __uint_as_float(x1[ch * 8 + e + 1]) + b1[e + 1];
+                  const float q0 = __uint_as_float(x2[ch * 8 + e]) + b2[e];
+                  const float q1 = __uint_as_float(x2[ch * 8 + e + 1]) + b2[e + 1];
+                  y1[e / 2] = pack_bf16(a0 * cs[e] - q0 * sn[e], a1 * cs[e + 1] - q1 * sn[e + 1]);
+                  y2[e / 2] = pack_bf16(a0 * sn[e] + q0 * cs[e], a1 * sn[e + 1] + q1 * cs[e + 1]);
+                }
+                box_put(stage + (e0 / 64) * 4096, lane, (e0 % 64) / 8, make_uint4(y1[0], y1[1], y1[2], y1[3]));
+                box_put(stage + ((D / 2 + e0) / 64) * 4096, lane, ((D / 2 + e0) % 64) / 8,
+                        make_uint4(y2[0], y2[1], y2[2], y2[3]));
+              }
+            }
+          } else {
+            // v head: bias only
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+              uint32_t x[32];
+              tmem_ld_32x32b_x32(t_row + hc0 + c, x);
+              tmem_ld_wait();
+#pragma unroll
+              for (int ch = 0; ch < 4; ++ch) {
+                float b[8];
+                if (args.bias) {
+                  const float4 p0 = *reinterpret_cast<const float4*>(args.bias + hc + c + ch * 8);
+                  const float4 p1 = *reinterpret_cast<const float4*>(args.bias + hc + c + ch * 8 + 4);
+                  b[0] = p0.x; b[1] = p0.y; b[2] = p0.z; b[3] = p0.w; b[4] = p1.x; b[5] = p1.y; b[6] = p1.z; b[7] = p1.w;
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) b[e] = 0.f;
+                }
+                uint32_t y[4];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2)
+                  y[e / 2] = pack_bf16(__uint_as_float(x[ch * 8 + e]) + b[e], __uint_as_float(x[ch * 8 + e + 1]) + b[e + 1]);
+                box_put(stage + (c / 64) * 4096, lane, (c % 64) / 8 + ch, make_uint4(y[0], y[1], y[2], y[3]));
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stage, hc, row0);
+            if (D == 128) tma_store_2d(&tmC, stage + 4096, hc + 64, row0);
+            bulk_commit();
+          }
+          pending = true;
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      if constexpr (MODE == 0 || MODE == 4) {
+      // MODE 4: running softmax statistics of this row over this warp's columns (base-2 exponent)
+      float st_m = -INFINITY, st_s = 0.f, st_t = 0.f;
+      bool st_has_t = false;
+      int tgt = -1;
+      if constexpr (MODE == 4) {
+        const int row = row0 + lane;
+        if (row < args.M) {
+          const long long grow = args.r0 + row;
+          const long long b = grow / args.T, t = grow - b * args.T;
+          tgt = args.ids[b * args.S + t + 1];
+        }
+      }
+#pragma unroll 1
+      for (int c0 = hsel * (BN / 2); c0 < (hsel + 1) * (BN / 2); c0 += cols_per_box) {
         uint32_t r[2][32];
         tmem_ld_32x32b_x32(t_row + c0, r[0]);
         if (is_bf16) tmem_ld_32x32b_x32(t_row + c0 + 32, r[1]);
         tmem_ld_wait();
         const int gcol = nb * BN + c0;
         const bool live = (gcol < args.N) && (row0 < args.M);
+        if constexpr (MODE == 4) {
+          const int nv = min(64, args.N - gcol);  // valid columns of this box
+          float mx = -INFINITY;
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const float v = __uint_as_float(r[e >> 5][e & 31]);
+            mx = (e < nv) ? fmaxf(mx, v) : mx;
+          }
+          if (mx > -INFINITY) {
+            const float mn = fmaxf(st_m, mx);
+            const float ml2 = mn * 1.4426950408889634f;
+            float acc = 0.f;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) {
+              const float v = __uint_as_float(r[e >> 5][e & 31]);
+              acc += (e < nv) ? ex2_approx(fmaf(v, 1.4426950408889634f, -ml2)) : 0.f;
+            }
+            st_s = st_s * ex2_approx((st_m - mn) * 1.4426950408889634f) + acc;
+            st_m = mn;
+          }
+          const int tc = tgt - gcol;
+          if (tc >= 0 && tc < 64 && tc < nv) {
+            float tv = 0.f;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) tv = (e == tc) ? __uint_as_float(r[e >> 5][e & 31]) : tv;
+            st_t = tv;
+            st_has_t = true;
+          }
+        }
         if (pending) {  // previous box of this warp must have been read out of shared memory
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
@@ -279,6 +643,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if constexpr (MODE == 4) {
+        const int row = row0 + lane;
+        if (row < args.M) {
+          args.lse_part[(long long)(nb * 2 + hsel) * args.M + row] = make_float2(st_m, st_s);
+          if (st_has_t) args.tgt_logit[row] = st_t;
+        }
+      }
+      }
+    }
     }
     if (lane == 0) bulk_wait0();
     __syncwarp();
@@ -333,18 +706,29 @@ int make_map(CUtensorMap* m, const void* ptr, long long inner, long long outer, 
 
 int g_num_sms = 0;
 
-template <int BN, int A_MN, int B_MN>
+template <int BN, int A_MN, int B_MN, int MODE = 0>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tcp,
-           const GemmArgs& a, int grid, cudaStream_t st) {
-  using C = Cfg<BN>;
-  auto k = gemm_tc_kernel<BN, A_MN, B_MN>;
+           const GemmArgs& a, int grid, cudaStream_t st, const CUtensorMap* tb2 = nullptr,
+           const CUtensorMap* tc2 = nullptr, const CUtensorMap* tc3 = nullptr) {
+  using C = Cfg<BN, MODE>;
+  static_assert(C::SMEM_BYTES <= 232448, "shared memory per CTA");
+  auto k = gemm_tc_kernel<BN, A_MN, B_MN, MODE>;
   static bool attr_set = false;
   if (!attr_set) {
     DT_CUDA_RET(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, tcp, a);
+  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, tcp, tb2 ? *tb2 : tb, tc2 ? *tc2 : tc, tc3 ? *tc3 : tc, a);
   return (int)cudaGetLastError();
+}
+
+int num_sms() {
+  if (!g_num_sms) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
 }
 
 }  // namespace
@@ -371,7 +755,7 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
     // accumulate / split-K problems fill the machine through K splits instead: keep the wide tile
     if (epi == EPI_F32_ATOMIC && N > 128 && tm * ((N + 255) / 256) < g_num_sms) bn = 256;
   }
-  GemmArgs a;
+  GemmArgs a = {};
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + BK - 1) / BK;
   a.tiles_m = (M + BM - 1) / BM;
@@ -460,3 +844,167 @@ DT_API int dt_gemm_bf16_peer(const void* A, int a_mn, long long lda, const void*
   return gemm_impl(A, a_mn, lda, B, b_mn, ldb, Cp, ldc, M, N, K, EPI_BF16, alpha, 1, bn, Cpeer, peer_arrivals,
                    done_ctas, stream);
 }
+
+// ───────────────────────────── fused SwiGLU ─────────────────────────────
+// Forward: X [M, K] (row stride ldx) times the gate|up weight Wgu [2F, K] (row stride ldw; gate rows
+// [0, F), up rows [F, 2F)). Writes gu [M, 2F] (gate | up, bf16, for the backward) and h = silu(gate) * up
+// [M, F] (bf16, computed from the fp32 accumulators). F must be a multiple of 64.
+DT_API int dt_gemm_swiglu_fwd(const void* X, long long ldx, const void* Wgu, long long ldw, void* gu, void* h,
+                              int M, int F, int K, cudaStream_t stream) {
+  if (M <= 0 || F <= 0 || K <= 0) return 0;
+  if ((F % 64) || (ldx % 8) || (ldw % 8) ||
+      ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(Wgu) | reinterpret_cast<uintptr_t>(gu) |
+        reinterpret_cast<uintptr_t>(h)) & 15))
+    return -10;
+  GemmArgs a = {};
+  a.M = M; a.N = F; a.K = K;
+  a.num_kb = (K + BK - 1) / BK;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (F + 127) / 128;
+  a.split_k = 1;
+  a.kb_per_split = a.num_kb;
+  a.epi = EPI_BF16;
+  a.alpha = 1.f;
+  a.C = gu;
+  a.ldc = 2LL * F;
+  const __nv_bfloat16* wup = reinterpret_cast<const __nv_bfloat16*>(Wgu) + (long long)F * ldw;
+  __nv_bfloat16* gu_up = reinterpret_cast<__nv_bfloat16*>(gu) + F;
+  CUtensorMap ta, tb, tb2, tc, tc2, tc3;
+  int rc;
+  if ((rc = make_map(&ta, X, K, M, ldx, BK, BM))) return rc;
+  if ((rc = make_map(&tb, Wgu, K, F, ldw, BK, 128))) return rc;
+  if ((rc = make_map(&tb2, wup, K, F, ldw, BK, 128))) return rc;
+  if ((rc = make_map(&tc, gu, F, M, 2LL * F, 64, 32))) return rc;
+  if ((rc = make_map(&tc2, gu_up, F, M, 2LL * F, 64, 32))) return rc;
+  if ((rc = make_map(&tc3, h, F, M, F, 64, 32))) return rc;
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  return launch<256, 0, 0, 1>(ta, tb, tc, tc, a, grid, stream, &tb2, &tc2, &tc3);
+}
+
+// Backward through SwiGLU and the down projection's input: dh = dY [M, K] . Wd [K, F] (row stride ldw),
+// never stored; with the saved gu [M, 2F] of the forward, writes dgu[:, :F] = dh * up * silu'(gate) and
+// dgu[:, F:] = dh * silu(gate) (bf16). F must be a multiple of 64; 128-wide tiles (`bn` is ignored).
+DT_API int dt_gemm_swiglu_bwd(const void* dY, long long ldy, const void* Wd, long long ldw, const void* gu, void* dgu,
+                              int M, int F, int K, int bn, cudaStream_t stream) {
+  (void)bn;
+  if (M <= 0 || F <= 0 || K <= 0) return 0;
+  if ((F % 64) || (ldy % 8) || (ldw % 8) ||
+      ((reinterpret_cast<uintptr_t>(dY) | reinterpret_cast<uintptr_t>(Wd) | reinterpret_cast<uintptr_t>(gu) |
+        reinterpret_cast<uintptr_t>(dgu)) & 15))
+    return -10;
+  constexpr int kBN = 128;
+  GemmArgs a = {};
+  a.M = M; a.N = F; a.K = K;
+  a.num_kb = (K + BK - 1) / BK;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (F + kBN - 1) / kBN;
+  a.split_k = 1;
+  a.kb_per_split = a.num_kb;
+  a.epi = EPI_BF16;
+  a.alpha = 1.f;
+  a.C = dgu;
+  a.ldc = 2LL * F;
+  const __nv_bfloat16* gu_up = reinterpret_cast<const __nv_bfloat16*>(gu) + F;
+  __nv_bfloat16* dgu_up = reinterpret_cast<__nv_bfloat16*>(dgu) + F;
+  CUtensorMap ta, tb, tc, tc2, tg, tu;
+  int rc;
+  if ((rc = make_map(&ta, dY, K, M, ldy, BK, BM))) return rc;
+  if ((rc = make_map(&tb, Wd, F, K, ldw, 64, BK))) return rc;  // B(n, k) = Wd[k * ldw + n]: MN-major
+  if ((rc = make_map(&tc, dgu, F, M, 2LL * F, 64, 32))) return rc;
+  if ((rc = make_map(&tc2, dgu_up, F, M, 2LL * F, 64, 32))) return rc;
+  if ((rc = make_map(&tg, gu, F, M, 2LL * F, 64, 32))) return rc;      // saved gate, read by the epilogue
+  if ((rc = make_map(&tu, gu_up, F, M, 2LL * F, 64, 32))) return rc;   // saved up
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  return launch<kBN, 0, 1, 2>(ta, tb, tc, tc, a, grid, stream, &tg, &tc2, &tu);
+}
+
+// ───────────────────────────── fused QKV bias + RoPE ─────────────────────────────
+// out[M, N] = X [M, K] . Wqkv [N, K]^T + bias, then the rotate-half rotary embedding of every head whose
+// first column is below rot_cols (the q and k heads), position = row mod T, tables cos / sin [T, hd/2]
+// fp32; hd 64 or 128 and N a multiple of hd. bias may be null. bn 128 / 256 (0 = choose).
+DT_API int dt_gemm_qkv_rope(const void* X, long long ldx, const void* Wqkv, long long ldw, const float* bias,
+                            const float* cosT, const float* sinT, void* out, int M, int N, int K, int T, int hd,
+                            int rot_cols, int bn, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((hd != 64 && hd != 128) || (N % hd) || (rot_cols % hd) || T <= 0 || (ldx % 8) || (ldw % 8) ||
+      ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(Wqkv) | reinterpret_cast<uintptr_t>(out) |
+        reinterpret_cast<uintptr_t>(cosT) | reinterpret_cast<uintptr_t>(sinT) | reinterpret_cast<uintptr_t>(bias)) & 15))
+    return -10;
+  if (bn != 128 && bn != 256) {
+    const long long tm = (M + BM - 1) / BM;
+    const long long w256 = (tm * ((N + 255) / 256) + num_sms() - 1) / num_sms();
+    const long long w128 = (tm * ((N + 127) / 128) + num_sms() - 1) / num_sms();
+    bn = (N <= 128 || w128 * 65 < w256 * 100) ? 128 : 256;
+  }
+  if (hd == 128) bn = 256;  // one 128-wide head per epilogue warp pair half
+  GemmArgs a = {};
+  a.M = M; a.N = N; a.K = K;
+  a.num_kb = (K + BK - 1) / BK;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (N + bn - 1) / bn;
+  a.split_k = 1;
+  a.kb_per_split = a.num_kb;
+  a.epi = EPI_BF16;
+  a.alpha = 1.f;
+  a.C = out;
+  a.ldc = N;
+  a.cosT = cosT;
+  a.sinT = sinT;
+  a.bias = bias;
+  a.T = T;
+  a.hd = hd;
+  a.rot_cols = rot_cols;
+  CUtensorMap ta, tb, tc;
+  int rc;
+  if ((rc = make_map(&ta, X, K, M, ldx, BK, BM))) return rc;
+  if ((rc = make_map(&tb, Wqkv, K, N, ldw, BK, bn))) return rc;
+  if ((rc = make_map(&tc, out, N, M, N, 64, 32))) return rc;
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  if (bn == 256) return launch<256, 0, 0, 3>(ta, tb, tc, tc, a, grid, stream);
+  return launch<128, 0, 0, 3>(ta, tb, tc, tc, a, grid, stream);
+}
+
+// ───────────────────────────── LM head with softmax statistics ─────────────────────────────
+// logits[rows, V] (bf16, row stride ldc) = X [rows, K] . E [V, K]^T, plus lse_part[(2 * tile_n + half) *
+// rows + row] = (max, sum exp(x - max)) of the fp32 logits over each half of each 256-wide column tile and
+// tgt_logit[row] = the fp32 logit of ids[b*S + t + 1] for global row r0 + row (b, t = divmod(r0 + row, T)).
+// lse_part needs 2 * ceil(V / 256) * rows entries. Returns that count through *n_part when non-null.
+DT_API int dt_gemm_logits_lse(const void* X, long long ldx, const void* E, long long lde, void* logits, long long ldc,
+                              int rows, int V, int K, float2* lse_part, float* tgt_logit, const int* ids, int T, int S,
+                              long long r0, cudaStream_t stream) {
+  if (rows <= 0 || V <= 0 || K <= 0) return 0;
+  if ((ldx % 8) || (lde % 8) || (ldc % 8) || !lse_part || !tgt_logit || !ids || T <= 0 || S <= T ||
+      ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(E) | reinterpret_cast<uintptr_t>(logits)) & 15))
+    return -10;
+  constexpr int kBN = 256;
+  GemmArgs a = {};
+  a.M = rows; a.N = V; a.K = K;
+  a.num_kb = (K + BK - 1) / BK;
+  a.tiles_m = (rows + BM - 1) / BM;
+  a.tiles_n = (V + kBN - 1) / kBN;
+  a.split_k = 1;
+  a.kb_per_split = a.num_kb;
+  a.epi = EPI_BF16;
+  a.alpha = 1.f;
+  a.C = logits;
+  a.ldc = ldc;
+  a.lse_part = lse_part;
+  a.tgt_logit = tgt_logit;
+  a.ids = ids;
+  a.T = T;
+  a.S = S;
+  a.r0 = r0;
+  CUtensorMap ta, tb, tc;
+  int rc;
+  if ((rc = make_map(&ta, X, K, rows, ldx, BK, BM))) return rc;
+  if ((rc = make_map(&tb, E, K, V, lde, BK, kBN))) return rc;
+  if ((rc = make_map(&tc, logits, V, rows, ldc, 64, 32))) return rc;
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  return launch<kBN, 0, 0, 4>(ta, tb, tc, tc, a, grid, stream);
+}
+
+DT_API long long dt_logits_lse_parts(int rows, int V) { return 2LL * ((V + 255) / 256) * rows; }

@@ -1,6 +1,6 @@
 """Kernel microbenchmarks: CUDA-event timing of the hot sm_100a kernels on the tiny/small preset shapes.
 
-    python -m distrain_b200.bench_kernels [--only gemm|attn|norm|compress|merge|all] [--case SUBSTR] [--iters N]
+    python -m distrain_b200.bench_kernels [--only gemm|attn|norm|fused|compress|merge|all] [--case SUBSTR] [--iters N]
                                           [--warmup W] [--json]
 
 ``--case`` keeps only the cases whose name contains SUBSTR (e.g. ``gate_up_fwd``, ``attn_fwd_d64``,
@@ -146,6 +146,77 @@ def norm_cases(iters):
     return out
 
 
+def fused_cases(iters):
+    """Fused epilogues against the separate kernels they replace, on the tiny preset's layer shapes:
+    gate|up GEMM + SwiGLU, down data-gradient + SwiGLU backward, QKV GEMM + bias + RoPE; and AdamW."""
+    from distrain_b200 import ops
+    from distrain_b200.config import preset
+    from distrain_b200.models.oracle import rope_tables
+    pk = peaks()
+    out = []
+    M, H, F, T = 32736, 768, 2048, 1023
+    x = torch.randn(M, H, device="cuda").bfloat16()
+    wgu = (torch.randn(2 * F, H, device="cuda") * 0.03).bfloat16()
+    gu = torch.empty(M, 2 * F, device="cuda", dtype=torch.bfloat16)
+    h = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+
+    def rec(name, ms, flops=None, byt=None):
+        r = {"kernel": name, "case": "tiny layer", "ms": round(ms, 4)}
+        if flops:
+            r["tflops"] = round(flops / ms / 1e9, 1)
+        if byt:
+            r["gbs"] = round(byt / ms / 1e6, 1)
+            r[f"frac_of_{pk['src']}_hbm"] = round(byt / ms / 1e6 / pk["hbm_gbs"], 3)
+        out.append(r)
+    fl = 2.0 * M * 2 * F * H
+    if want("swiglu_fwd"):
+        rec("gemm_swiglu_fwd (fused)", time_it(lambda: ops.gemm_swiglu_fwd(x, wgu, gu, h), iters), fl)
+        rec("linear_fwd + swiglu_fwd (separate)",
+            time_it(lambda: (ops.linear_fwd(x, wgu, gu), ops.swiglu_fwd(gu, h, M=M, F=F)), iters), fl)
+    if want("swiglu_bwd"):
+        dy = torch.randn(M, H, device="cuda").bfloat16()
+        wd = (torch.randn(H, F, device="cuda") * 0.03).bfloat16()
+        dgu = torch.empty_like(gu)
+        dh = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+        fb = 2.0 * M * F * H
+        rec("gemm_swiglu_bwd (fused)", time_it(lambda: ops.gemm_swiglu_bwd(dy, wd, gu, dgu), iters), fb)
+        rec("linear_dgrad + swiglu_bwd (separate)",
+            time_it(lambda: (ops.linear_dgrad(dy, wd, dh), ops.swiglu_bwd(dh, gu, dgu, M=M, F=F)), iters), fb)
+    if want("qkv_rope"):
+        cfg = preset("tiny")
+        nh, nkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim()
+        W = (nh + 2 * nkv) * d
+        wq = (torch.randn(W, H, device="cuda") * 0.03).bfloat16()
+        b = torch.zeros(W, device="cuda")
+        cos, sin = rope_tables(cfg, T)
+        cos, sin = cos.cuda().contiguous(), sin.cuda().contiguous()
+        q = torch.empty(M, W, device="cuda", dtype=torch.bfloat16)
+        fq = 2.0 * M * W * H
+        rec("gemm_qkv_rope (fused)", time_it(lambda: ops.gemm_qkv_rope(x, wq, b, cos, sin, q, T=T, d=d,
+                                                                     rot_cols=(nh + nkv) * d), iters), fq)
+        rec("linear_fwd + rope_fwd (separate)",
+            time_it(lambda: (ops.linear_fwd(x, wq, q), ops.rope_fwd(q, b, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d)),
+                    iters), fq)
+    if want("adamw"):
+        from distrain_b200.models.params import ParamLayout
+        L = ParamLayout(preset("tiny"))
+        n = L.total
+        p32 = torch.randn(n, device="cuda") * 0.02
+        g = torch.randn(n, device="cuda") * 1e-3
+        m = torch.zeros(n, device="cuda")
+        v = torch.zeros(n, device="cuda")
+        p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+        cseg, cstart, cend, nseg = L.chunk_tables(torch.device("cuda"))
+        norms = torch.zeros(nseg, device="cuda")
+        hp = torch.tensor([3e-4, 0.9, 0.999, 1e-5, 0.1, 0, 0, 1.0, 0, 0, 0, 1.0, 0, 0, 0, 0], device="cuda")
+        rec("adamw_step (clears gradients)", time_it(lambda: ops.adamw_step(p32, g, m, v, p16, cseg, cstart, cend, norms,
+                                                                            hp), iters), None, 34 * n)
+        hp[11] = 0.0
+        rec("adamw_step (keeps gradients)", time_it(lambda: ops.adamw_step(p32, g, m, v, p16, cseg, cstart, cend, norms,
+                                                                           hp), iters), None, 30 * n)
+    return out
+
+
 def compress_cases(iters):
     from distrain_b200.config import preset, CompressionConfig
     from distrain_b200.models.params import ParamLayout
@@ -281,6 +352,8 @@ def main():
         res += attn_cases(a.iters)
     if "all" in sel or "norm" in sel:
         res += norm_cases(a.iters)
+    if "all" in sel or "fused" in sel:
+        res += fused_cases(a.iters)
     if "all" in sel or "compress" in sel:
         res += compress_cases(a.iters)
     if "all" in sel or "merge" in sel:

@@ -576,8 +576,14 @@ def cmd_export_hf(args):
 
 
 def cmd_prepare_data(args):
-    from .utils.data import prepare_random_shards
-    m = prepare_random_shards(args.output_dir, args.num_shards, args.tokens_per_shard, args.vocab, args.seed)
+    from .utils.data import prepare_random_shards, iter_text_documents, tokenize_to_shards
+    if args.input:
+        if not args.tokenizer:
+            raise SystemExit("prepare-data --input needs --tokenizer (a tokenizers JSON file)")
+        m = tokenize_to_shards(iter_text_documents(args.input, args.text_column, args.max_samples), args.output_dir,
+                               args.tokenizer, args.vocab, args.tokens_per_shard)
+    else:
+        m = prepare_random_shards(args.output_dir, args.num_shards, args.tokens_per_shard, args.vocab, args.seed)
     if args.upload_store:
         st = _store(args.upload_store)
         for f in os.listdir(args.output_dir):
@@ -733,8 +739,13 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--max-seq-len", type=int)
     p.set_defaults(fn=cmd_export_hf)
 
-    p = sp.add_parser("prepare-data", help="write uint16 token shards + manifest (random test mode)")
+    p = sp.add_parser("prepare-data", help="write uint16 token shards + manifest: tokenized local text files "
+                                           "(--input, --tokenizer) or uniform-random tokens (test mode)")
     p.add_argument("--output-dir", required=True)
+    p.add_argument("--input", nargs="+", help=".txt (a document per line), .jsonl or .parquet files to tokenize")
+    p.add_argument("--tokenizer", help="tokenizers JSON file (e.g. the Mistral v0.3 tokenizer, 32768 ids)")
+    p.add_argument("--text-column", default="text", help="document field of .jsonl / .parquet inputs")
+    p.add_argument("--max-samples", type=int, help="stop after this many documents")
     p.add_argument("--num-shards", type=int, default=4)
     p.add_argument("--tokens-per-shard", type=int, default=10_000_000)
     p.add_argument("--vocab", type=int, default=32768)

@@ -112,6 +112,54 @@ def rope_bwd(dqkv, dbias, cos, sin, *, M, T, nh, nkv, d, stream=None):
           "dt_rope_bwd")
 
 
+def gemm_qkv_rope(x, w, bias, cos, sin, out, *, T, d, rot_cols, stream=None):
+    """out[M, N] = rope(x[M, K] @ w[N, K]^T + bias) in one tcgen05 GEMM: the epilogue adds the bias and
+    rotates every head whose columns lie below ``rot_cols`` (q and k heads) by the position row % T
+    (fp32 cos / sin tables [T, d/2]); d = 64 or 128."""
+    M, K = x.shape
+    N = w.shape[0]
+    check(lib().dt_gemm_qkv_rope(ptr(x), K, ptr(w), K, ptr(bias), ptr(cos), ptr(sin), ptr(out), M, N, K, T, d,
+                                 rot_cols, 0, stream_ptr(stream)), "dt_gemm_qkv_rope")
+
+
+def gemm_swiglu_fwd(x, w_gu, gu, h, stream=None):
+    """gu[M, 2F] = x[M, K] @ w_gu[2F, K]^T (gate | up, bf16) and h[M, F] = silu(gate) * up in the same
+    tcgen05 GEMM (its epilogue), from the fp32 accumulators. F a multiple of 64."""
+    M, K = x.shape
+    F = h.shape[1]
+    assert w_gu.shape == (2 * F, K) and gu.shape == (M, 2 * F) and h.shape == (M, F)
+    check(lib().dt_gemm_swiglu_fwd(ptr(x), K, ptr(w_gu), K, ptr(gu), ptr(h), M, F, K, stream_ptr(stream)),
+          "dt_gemm_swiglu_fwd")
+
+
+def gemm_swiglu_bwd(dy, w_down, gu, dgu, stream=None):
+    """dgu[M, 2F] = SwiGLU backward of dh = dy[M, K] @ w_down[K, F] against the saved gu (dh itself is
+    never stored): dgate = dh * up * silu'(gate), dup = dh * silu(gate). F a multiple of 64."""
+    M, K = dy.shape
+    F = w_down.shape[1]
+    assert w_down.shape == (K, F) and gu.shape == (M, 2 * F) and dgu.shape == (M, 2 * F)
+    check(lib().dt_gemm_swiglu_bwd(ptr(dy), K, ptr(w_down), F, ptr(gu), ptr(dgu), M, F, K, 0, stream_ptr(stream)),
+          "dt_gemm_swiglu_bwd")
+
+
+def rope_bwd_stream_scratch(M: int, W: int) -> int:
+    """fp32 elements of the scratch buffer ``rope_bwd_stream`` needs for an [M, W] gradient."""
+    return ((M + 127) // 128) * W
+
+
+def rope_bwd_stream(dqkv, dbias, cos, sin, scratch, *, M, T, nh, nkv, d, stream=None):
+    """In-place inverse rotation of the q / k heads of dqkv and dbias += its column sums (one read and one
+    write of dqkv; per-block column partials in ``scratch``, no atomics). d = 64 / 128, W % 256 == 0."""
+    check(lib().dt_rope_bwd_stream(ptr(dqkv), ptr(dbias), ptr(cos), ptr(sin), M, T, nh, nkv, d, ptr(scratch),
+                                   stream_ptr(stream)), "dt_rope_bwd_stream")
+
+
+def colsum_bf16(x, out, stream=None):
+    """out[c] += sum over rows of x[:, c] (x bf16 [M, W], out fp32 [W]): the QKV bias gradient."""
+    M, W = x.shape
+    check(lib().dt_colsum_bf16(ptr(x), M, W, ptr(out), stream_ptr(stream)), "dt_colsum_bf16")
+
+
 def swiglu_fwd(gu, h, *, M, F, stream=None):
     check(lib().dt_swiglu_fwd(ptr(gu), ptr(h), M, F, stream_ptr(stream)), "dt_swiglu_fwd")
 
@@ -123,6 +171,28 @@ def swiglu_bwd(dh, gu, dgu, *, M, F, stream=None):
 def ce_fwd_bwd(logits, ids, loss_rows, *, T, S, r0, rows, V, ld=None, grad_scale=1.0, stream=None):
     check(lib().dt_ce_fwd_bwd(ptr(logits), V if ld is None else ld, ptr(ids), T, S, r0, rows, ptr(loss_rows), V,
                               float(grad_scale), stream_ptr(stream)), "dt_ce_fwd_bwd")
+
+
+def lse_parts(rows: int, V: int) -> int:
+    """float2 entries of the softmax-statistics buffer ``gemm_logits_lse`` fills for ``rows`` rows."""
+    return 2 * ((V + 255) // 256) * rows
+
+
+def gemm_logits_lse(x, emb, logits, part, tgt_logit, ids, *, rows, V, K, T, S, r0, stream=None):
+    """logits[rows, V] = x[rows, K] @ emb[V, K]^T (bf16) and, from the fp32 accumulators, the per-row
+    softmax statistics (``part``: fp32 pairs, ``lse_parts(rows, V)`` of them) and the fp32 logit of each
+    row's target token (``tgt_logit``); target of global row r0 + r = ids[b*S + t + 1]."""
+    check(lib().dt_gemm_logits_lse(ptr(x), x.stride(0), ptr(emb), emb.stride(0), ptr(logits), logits.stride(0), rows,
+                                   V, K, ptr(part), ptr(tgt_logit), ptr(ids), T, S, r0, stream_ptr(stream)),
+          "dt_gemm_logits_lse")
+
+
+def ce_lse_bwd(logits, part, tgt_logit, ids, loss_rows, *, rows, V, T, S, r0, grad_scale, stream=None):
+    """Cross-entropy of ``rows`` rows from ``gemm_logits_lse``'s statistics: loss_rows = lse - target logit
+    (fp32) and the logits replaced in place by grad_scale * (softmax - onehot)."""
+    np_ = lse_parts(1, V)
+    check(lib().dt_ce_lse_bwd(ptr(logits), logits.stride(0), ptr(part), np_, rows, ptr(tgt_logit), ptr(ids), T, S, r0,
+                              ptr(loss_rows), V, float(grad_scale), stream_ptr(stream)), "dt_ce_lse_bwd")
 
 
 def loss_reduce(loss_rows, n, scale, out, stream=None):

@@ -118,6 +118,104 @@ class CudaBackend:
         self.eng.step()
         return float(self.eng.loss[0].item())
 
+    # ── round deltas compressed on the device (reference continuous.rs:190-219 semantics) ──
+    # The round-start snapshot and the error-feedback residual live on the GPU (DeviceCompressor); a push
+    # forms delta + EF, selects the exact per-tensor top-k and compacts it there, and only the kept
+    # (index, value) pairs cross to the host (8 bytes per kept entry), where the reference's per-tensor
+    # INT8 step and the JSON/zstd encoding run on k values instead of the whole model.
+    def enable_device_compression(self, cfg: CompressionConfig, max_fraction: float = 1.0):
+        from .compression import DeviceCompressor, DevicePayload
+        self.dcfg = CompressionConfig(top_k_fraction=cfg.top_k_fraction, quantize_int8=False,
+                                      per_tensor_adaptive=cfg.per_tensor_adaptive, int8_block=0,
+                                      zstd_level=cfg.zstd_level)
+        cap = DeviceCompressor.capacity_for(self.layout, max_fraction)
+        self.dcomp = DeviceCompressor(self.layout, self.eng.device, self.dcfg,
+                                      payload=DevicePayload.allocate(cap, 0, self.eng.device))
+        self.dcomp.reset(self.eng.master)
+        self.cstream = torch.cuda.Stream(device=self.eng.device)
+        self._payload_free = None      # event: the host has copied the previous payload out
+        self._host_idx = self._host_val = None
+        self.d2h_bytes_last = 0
+        offs = [(e.offset, e.numel, e.name, list(e.shape)) for e in self.layout.entries]
+        self._entries = sorted(offs)
+        self._starts = torch.tensor([o for o, _, _, _ in self._entries], dtype=torch.int64)
+
+    def round_reset(self, clear_ef: bool = False):
+        """New round start at the current weights (snapshot <- master); ``clear_ef`` also restarts the error
+        feedback (a checkpoint boundary)."""
+        if clear_ef:
+            self.dcomp.reset(self.eng.master)
+        else:
+            self.dcomp.snap.copy_(self.eng.master)
+
+    def compress_round(self, k_fraction: float):
+        """Delta (snapshot - master) + error feedback -> exact top-k on the device; returns a handle the
+        uploader thread passes to ``collect``. The snapshot becomes the current weights."""
+        train = torch.cuda.current_stream(self.eng.device)
+        if self._payload_free is not None:
+            self.cstream.wait_event(self._payload_free)   # the previous payload has been read out
+        self.dcomp.begin(self.eng.master, stream=train)     # pass A: ordered with the training steps
+        ev = torch.cuda.Event()
+        ev.record(train)
+        self.cstream.wait_event(ev)
+        self.dcomp.finish(stream=self.cstream, k_fraction=k_fraction, quant_block=0)
+        done = torch.cuda.Event()
+        done.record(self.cstream)
+        return done, k_fraction
+
+    def collect(self, handle, cfg: CompressionConfig, want_ef: bool = False):
+        """(SparseDeltaT, stats[, EF state dict]) of a ``compress_round`` handle, on the calling thread."""
+        from .compression import SparseDeltaT, quantize_int8, dequantize_int8
+        done, kf = handle
+        done.synchronize()
+        st = self.dcomp.read_stats(raw=False, quantized=False)
+        k = int(st["num_params_kept"])
+        if self._host_idx is None or self._host_idx.numel() < k:
+            n = max(k, 1)
+            self._host_idx = torch.empty(n, dtype=torch.int32).pin_memory()
+            self._host_val = torch.empty(n, dtype=torch.float32).pin_memory()
+        p = self.dcomp.payload
+        with torch.cuda.stream(self.cstream):
+            self._host_idx[:k].copy_(p.idx[:k], non_blocking=True)
+            self._host_val[:k].copy_(p.val[:k], non_blocking=True)
+            ef = None
+            if want_ef:
+                ef = {e.name: self.dcomp.ef[e.offset:e.offset + e.numel].view(e.shape).float().cpu()
+                      for e in self.layout.entries}
+            freed = torch.cuda.Event()
+            freed.record(self.cstream)
+        freed.synchronize()
+        self._payload_free = freed
+        self.d2h_bytes_last = 8 * k
+        flat = self._host_idx[:k].to(torch.int64)
+        vals = self._host_val[:k].clone()
+        pos = torch.searchsorted(self._starts, flat, right=True) - 1
+        bounds = torch.searchsorted(pos, torch.arange(len(self._entries) + 1), right=False)
+        idxs, values, shapes, scales = {}, {}, {}, ({} if cfg.quantize_int8 else None)
+        for j, (off, numel, name, shape) in enumerate(self._entries):
+            a, b = int(bounds[j]), int(bounds[j + 1])
+            shapes[name] = shape
+            idxs[name] = flat[a:b] - off
+            v = vals[a:b]
+            if cfg.quantize_int8:   # the reference's per-tensor scale, values shipped dequantised
+                q, s = quantize_int8(v, 0)
+                v = dequantize_int8(q, s, 0)
+                scales[name] = float(s[0])
+            values[name] = v
+        sd = SparseDeltaT(indices=idxs, values=values, shapes=shapes, scales=scales,
+                          config=CompressionConfig(top_k_fraction=kf, quantize_int8=cfg.quantize_int8,
+                                                   per_tensor_adaptive=cfg.per_tensor_adaptive,
+                                                   zstd_level=cfg.zstd_level))
+        stats = {"dense_norm": st["dense_norm"], "sparse_norm": st["sparse_norm"],
+                 "retention_ratio": st["retention_ratio"], "top_k_fraction": kf,
+                 "num_params_total": st["num_params_total"], "num_params_kept": k,
+                 "raw_param_bytes": 4 * st["num_params_total"]}
+        return (sd, stats, ef) if want_ef else (sd, stats)
+
+    def load_ef(self, ef):
+        for e in self.layout.entries:
+            self.dcomp.ef[e.offset:e.offset + e.numel].copy_(ef[e.name].reshape(-1).to(self.eng.device))
+
 
 class HttpNode:
     def __init__(self, coordinator_url: str, store, model_cfg: ModelConfig, batch: int, seq_len: int,
@@ -136,6 +234,11 @@ class HttpNode:
         self.dev = device
         self.backend = CpuBackend(model_cfg, self.optim) if device == "cpu" else \
             CudaBackend(model_cfg, self.optim, batch, seq_len, device)
+        # a GPU node compresses its round deltas on the device: only the kept entries leave the GPU
+        self.device_comp = isinstance(self.backend, CudaBackend)
+        if self.device_comp:
+            self.backend.enable_device_compression(self.comp, 1.0 if bandwidth_adaptive else
+                                                   max(self.comp.top_k_fraction, 0.0))
         self.data = data
         self.poll_secs, self.use_proxy, self.bw_adaptive = poll_secs, use_upload_proxy, bandwidth_adaptive
         self.hb_every = heartbeat_every
@@ -225,8 +328,30 @@ class HttpNode:
             except Exception as e:
                 self.errors.append(f"upload: {e}")
 
+    def _push_fraction(self, mean_loss: float):
+        """(top-k fraction, quantise) of the next device-compressed push: the configured top-k, or with
+        the bandwidth-adaptive policy the decision of ``adaptive_push_mode`` from the measured upload
+        bandwidth and the raw delta size (4 bytes per parameter; no trial compression)."""
+        from .compression import adaptive_push_mode
+        n = self.backend.layout.num_params()
+        kind, kf, qb = adaptive_push_mode(self.bw_adaptive, self.bandwidth_bps, 4 * n, mean_loss, self.comp)
+        if kind == "raw":
+            return 1.0, False
+        return kf, (self.comp.quantize_int8 and (not self.bw_adaptive or self.bandwidth_bps <= 0))
+
     def _compress_upload_push(self, pkg):
         delta, shapes, push, mean_loss, ef_generation, snap = pkg
+        if isinstance(delta, tuple) and delta and delta[0] == "device":
+            _, handle, quant = delta
+            cfg = CompressionConfig(top_k_fraction=handle[1], quantize_int8=quant,
+                                    per_tensor_adaptive=self.comp.per_tensor_adaptive, zstd_level=self.comp.zstd_level)
+            if snap is not None:
+                sd, stats, ef = self.backend.collect(handle, cfg, want_ef=True)
+                self._ef = ef
+            else:
+                sd, stats = self.backend.collect(handle, cfg)
+            self._upload_and_push(sd, cfg, stats, push, snap)
+            return
         if ef_generation != self._ef_gen_seen:   # error feedback restarts at a checkpoint boundary
             self._ef, self._ef_gen_seen = {}, ef_generation
         cfg = self.comp
@@ -241,6 +366,9 @@ class HttpNode:
                 cfg = CompressionConfig(top_k_fraction=adaptive_top_k(mean_loss, budget, raw_bytes),
                                         quantize_int8=False, zstd_level=cfg.zstd_level)
         sd, stats = compress_reference(delta, shapes, cfg, self._ef)
+        self._upload_and_push(sd, cfg, stats, push, snap)
+
+    def _upload_and_push(self, sd, cfg, stats, push, snap):
         blob = encode_sparse_delta(sd, cfg.zstd_level)
         t0 = time.time()
         for attempt in range(5):   # 5 retries with backoff (continuous.rs:244-283)
@@ -315,25 +443,42 @@ class HttpNode:
             self.backend.load(rec["weights"])
             self.backend.load_optimizer_state(rec["optimizer"])
             self._ef = {k: v.clone() for k, v in rec["ef"].items()}
+            if self.device_comp:
+                self.backend.round_reset()
+                self.backend.load_ef(self._ef)
             self.resumed = "exact"
             return True
         self.resumed = "identity"
         return False
 
     # ─────────── training loop ───────────
+    def _round_start(self, boundary: bool = False):
+        """Round-start weights: a host copy (CPU backend) or, compressing on the device, the device
+        snapshot (``boundary``: a new checkpoint, the error feedback restarts too)."""
+        if self.device_comp:
+            self.backend.round_reset(clear_ef=boundary)
+            return None
+        return self.backend.state()
+
     def _build_push(self, start, steps, tokens, losses, t0, boundary: bool = False):
-        cur = self.backend.state()
-        delta = {k: (start[k].reshape(-1) - cur[k].reshape(-1)).float() for k in start}
-        shapes = {k: list(v.shape) for k, v in start.items()}
+        mean_loss = sum(losses) / len(losses) if losses else 0.0
+        want_snap = boundary and self.resume_path and (self.seq + 1) % self.resume_every == 0
+        if self.device_comp:
+            kf, quant = self._push_fraction(mean_loss)
+            delta, shapes = ("device", self.backend.compress_round(kf), quant), None
+            cur = self.backend.state() if want_snap else None
+        else:
+            cur = self.backend.state()
+            delta = {k: (start[k].reshape(-1) - cur[k].reshape(-1)).float() for k in start}
+            shapes = {k: list(v.shape) for k, v in start.items()}
         self.seq += 1
         snap = None
-        if boundary and self.resume_path and self.seq % self.resume_every == 0:
+        if want_snap:
             src = getattr(self.data, "__self__", None)
             snap = {"weights": {k: v.detach().float().cpu().clone() for k, v in cur.items()},
                     "optimizer": self.backend.optimizer_state(), "global_step": self.global_step,
                     "version": self.version,
                     "data": src.state() if src is not None and hasattr(src, "state") else None}
-        mean_loss = sum(losses) / len(losses) if losses else 0.0
         push = P.DeltaPush(node_id=self.node_id, seq_num=self.seq, checkpoint_version=self.version,
                            inner_steps=steps, delta_key=P.delta_path(self.version, self.node_id, self.seq),
                            training_loss=mean_loss, tokens_processed=tokens, training_time_secs=time.time() - t0)
@@ -358,7 +503,7 @@ class HttpNode:
             self._threads.append(t)
         warm = max(int(self.h_mini * self.optim.warmup_fraction), 2)
         first_round = rec is None  # a resumed node has had its warm-up
-        start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+        start, round_step, round_tokens, losses, t0 = self._round_start(boundary=not exact), 0, 0, [], time.time()
         loss_ema, loss_count = 0.0, 0
         ln_vocab = math.log(self.cfg.vocab_size)
         wd = None
@@ -383,13 +528,16 @@ class HttpNode:
                     if self.h_mini_bounds is not None:
                         lo, hi = self.h_mini_bounds
                         self.h_mini = int(min(max(self.recommended_h_mini, lo), hi))
-                    start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+                    start, round_step, round_tokens, losses, t0 = self._round_start(boundary=True), 0, 0, [], time.time()
                     if stop_on_version is not None and v >= stop_on_version:
                         break
                 if round_step >= self.h_mini:
                     if not (first_round and round_step <= warm):
                         self._build_push(start, round_step, round_tokens, losses, t0, boundary=True)
-                    start, round_step, round_tokens, losses, t0 = self.backend.state(), 0, 0, [], time.time()
+                    if first_round and round_step <= warm and self.device_comp:
+                        self.backend.round_reset()  # the skipped warm-up round's steps are not pushed
+                    start = None if self.device_comp else self.backend.state()
+                    round_step, round_tokens, losses, t0 = 0, 0, [], time.time()
                     first_round = False
                 tokens = self.data()
                 if first_round and round_step < warm:

@@ -1,5 +1,7 @@
 """Training data: uint16 token shards + manifest (reference node/cli/src/data.rs, scripts/prepare_data.py).
 
+* ``tokenize_to_shards`` - text documents (local .txt / .jsonl / .parquet files) through a
+  ``tokenizers`` JSON tokenizer into the same shard format (the reference's tokenize-and-shard step).
 * ``write_shard`` / ``write_manifest`` / ``prepare_random_shards`` - the data-prep format: flat LE
   uint16 files ``shard_XXXX.bin`` and ``manifest.json`` = {num_shards, vocab_size, shards[{filename,
   num_tokens, size_bytes}], total_tokens}.
@@ -55,6 +57,90 @@ def prepare_random_shards(out_dir: str, num_shards: int, tokens_per_shard: int, 
         write_shard(os.path.join(out_dir, f), rng.integers(0, vocab_size, tokens_per_shard, dtype=np.uint16))
         files.append(f)
     return write_manifest(out_dir, files, vocab_size)
+
+
+def iter_text_documents(paths: List[str], text_column: str = "text", max_docs: Optional[int] = None):
+    """Documents of local files: ``.jsonl`` (one JSON object per line, its ``text_column`` field),
+    ``.parquet`` (the ``text_column`` column, read in record batches) or plain text (one document per
+    non-empty line)."""
+    n = 0
+    for path in paths:
+        if path.endswith(".parquet"):
+            import pyarrow.parquet as pq
+            pf = pq.ParquetFile(path)
+            for rb in pf.iter_batches(columns=[text_column], batch_size=1024):
+                for t in rb.column(0).to_pylist():
+                    if max_docs is not None and n >= max_docs:
+                        return
+                    n += 1
+                    yield t or ""
+            continue
+        with open(path, encoding="utf-8") as fh:
+            for line in fh:
+                if max_docs is not None and n >= max_docs:
+                    return
+                if path.endswith(".jsonl") or path.endswith(".json"):
+                    line = line.strip()
+                    if not line:
+                        continue
+                    t = json.loads(line).get(text_column, "")
+                else:
+                    t = line.rstrip("\n")
+                n += 1
+                yield t
+
+
+def tokenize_to_shards(texts, out_dir: str, tokenizer_path: str, vocab_size: Optional[int] = None,
+                       tokens_per_shard: int = 10_000_000, batch_docs: int = 1000) -> dict:
+    """Tokenize documents (an iterable of strings) into ``shard_XXXX.bin`` files of ``tokens_per_shard``
+    uint16 ids and write the manifest (reference scripts/prepare_data.py:106-167).
+
+    Empty documents are skipped; documents are encoded in batches and their ids concatenated without
+    separators; every full shard is written as it fills; the remainder becomes a final shard only when it
+    holds at least a tenth of a shard, otherwise it is dropped. The tokenizer's vocabulary must fit
+    uint16 and, when ``vocab_size`` is given, match it (the model's embedding size)."""
+    from tokenizers import Tokenizer
+    tok = Tokenizer.from_file(tokenizer_path)
+    v = tok.get_vocab_size()
+    if v > 65536:
+        raise ValueError(f"tokenizer vocabulary {v} does not fit uint16 token ids")
+    if vocab_size is not None and v != vocab_size:
+        raise ValueError(f"tokenizer vocabulary {v} != model vocabulary {vocab_size}")
+    os.makedirs(out_dir, exist_ok=True)
+    files: List[str] = []
+    buf = np.empty(0, dtype=np.uint16)
+    dropped = 0
+
+    def emit(arr):
+        f = f"shard_{len(files):04d}.bin"
+        write_shard(os.path.join(out_dir, f), arr)
+        files.append(f)
+
+    def encode(batch):
+        nonlocal buf
+        ids = [np.asarray(e.ids, dtype=np.uint16) for e in tok.encode_batch(batch)]
+        buf = np.concatenate([buf] + ids) if ids else buf
+        while buf.size >= tokens_per_shard:
+            emit(buf[:tokens_per_shard])
+            buf = buf[tokens_per_shard:]
+
+    batch: List[str] = []
+    for t in texts:
+        if not t or not t.strip():
+            continue
+        batch.append(t)
+        if len(batch) >= batch_docs:
+            encode(batch)
+            batch = []
+    if batch:
+        encode(batch)
+    if buf.size and buf.size >= tokens_per_shard // 10:
+        emit(buf)
+    else:
+        dropped = int(buf.size)
+    m = write_manifest(out_dir, files, vocab_size if vocab_size is not None else v)
+    m["dropped_tail_tokens"] = dropped
+    return m
 
 
 def _reg():

@@ -1,6 +1,7 @@
 """Data loading: shard format, sequential wrap-around batches, seek_by_seed, resident window, prefetch,
 streaming from a store (restates the reference's data_tests.rs regressions: no repeats, advancing
 position, full coverage)."""
+import json
 import os
 
 import numpy as np
@@ -122,3 +123,52 @@ def test_stream_resume_maps_the_position_by_shard_name(tmp_path):
     s2.restore(st)
     assert torch.equal(s2.next_batch(), expect)
     s2.close()
+
+
+def _word_tokenizer(tmp_path, words):
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import Whitespace
+    vocab = {"[UNK]": 0}
+    for w in words:
+        vocab.setdefault(w, len(vocab))
+    tok = Tokenizer(WordLevel(vocab, unk_token="[UNK]"))
+    tok.pre_tokenizer = Whitespace()
+    path = str(tmp_path / "tok.json")
+    tok.save(path)
+    return path, tok, len(vocab)
+
+
+def test_tokenize_to_shards_from_text_jsonl_and_parquet(tmp_path):
+    """Documents from .txt, .jsonl and .parquet inputs are encoded in order, concatenated and cut into
+    full shards; a remainder of at least a tenth of a shard becomes the final shard."""
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+    from distrain_b200.utils.data import iter_text_documents, tokenize_to_shards
+    from distrain_b200 import cli
+    words = [f"w{i}" for i in range(50)]
+    tok_path, tok, V = _word_tokenizer(tmp_path, words)
+    rng = np.random.default_rng(0)
+    docs = [" ".join(rng.choice(words, size=int(rng.integers(3, 30)))) for _ in range(120)]
+    (tmp_path / "a.txt").write_text("\n".join(docs[:40]) + "\n\n")
+    with open(tmp_path / "b.jsonl", "w") as fh:
+        for d in docs[40:80]:
+            fh.write(json.dumps({"text": d, "id": 1}) + "\n")
+    pq.write_table(pa.table({"text": docs[80:]}), str(tmp_path / "c.parquet"))
+    inputs = [str(tmp_path / f) for f in ("a.txt", "b.jsonl", "c.parquet")]
+    got = list(iter_text_documents(inputs))
+    assert [g for g in got if g] == docs
+    want = np.concatenate([np.asarray(tok.encode(d).ids, dtype=np.uint16) for d in docs])
+    per = 300
+    m = tokenize_to_shards(iter_text_documents(inputs), str(tmp_path / "out"), tok_path, V, per, batch_docs=7)
+    full = want.size // per
+    rem = want.size - full * per
+    assert m["num_shards"] == full + (1 if rem >= per // 10 else 0) and m["vocab_size"] == V
+    back = np.concatenate([np.fromfile(str(tmp_path / "out" / s["filename"]), dtype="<u2") for s in m["shards"]])
+    assert np.array_equal(back, want[:back.size]) and back.size in (want.size, full * per)
+    with pytest.raises(ValueError):
+        tokenize_to_shards(docs, str(tmp_path / "bad"), tok_path, V + 1, per)
+    # the CLI entry point
+    cli.main(["prepare-data", "--output-dir", str(tmp_path / "cli"), "--input", inputs[1], "--tokenizer", tok_path,
+              "--vocab", str(V), "--tokens-per-shard", "100"])
+    assert json.load(open(tmp_path / "cli" / "manifest.json"))["num_shards"] >= 1

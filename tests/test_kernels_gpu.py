@@ -205,6 +205,147 @@ def test_swiglu_fwd_bwd():
     assert _rel(dgu[:, F:], u.grad) < 1e-2
 
 
+@pytest.mark.parametrize("B,T,nh,nkv,d,K,bias", [(3, 65, 4, 2, 64, 160, True), (2, 1023, 12, 4, 64, 768, True),
+                                                  (2, 100, 4, 2, 128, 256, False), (1, 300, 2, 1, 128, 64, True)])
+def test_gemm_qkv_rope_fused(B, T, nh, nkv, d, K, bias):
+    """QKV GEMM with bias + rotate-half RoPE in its epilogue vs fp32 torch (GEMM, bias, rotation by
+    position row % T with the engine's fp32 tables)."""
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.oracle import rope_tables
+    ops = _ops()
+    torch.manual_seed(13)
+    M, W = B * T, (nh + 2 * nkv) * d
+    cfg = ModelConfig(hidden_dim=nh * d, num_layers=1, num_heads=nh, num_kv_heads=nkv, ffn_hidden_dim=64,
+                      vocab_size=64, max_seq_len=T, rope_theta=10000.0)
+    cos, sin = rope_tables(cfg, T)
+    cos, sin = cos.cuda().contiguous(), sin.cuda().contiguous()
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    w = (torch.randn(W, K, device="cuda") / K ** 0.5).bfloat16()
+    b = torch.randn(W, device="cuda") * 0.1 if bias else None
+    out = torch.full((M, W), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_qkv_rope(x, w, b, cos, sin, out, T=T, d=d, rot_cols=(nh + nkv) * d)
+    torch.cuda.synchronize()
+    z = x.float() @ w.float().t() + (b if bias else 0.0)
+    t = torch.arange(M, device="cuda") % T
+    c, s_ = cos[t], sin[t]  # [M, d/2]
+    ref = z.clone()
+    half = d // 2
+    for h in range(nh + nkv):
+        a, q = z[:, h * d:h * d + half], z[:, h * d + half:(h + 1) * d]
+        ref[:, h * d:h * d + half] = a * c - q * s_
+        ref[:, h * d + half:(h + 1) * d] = a * s_ + q * c
+    assert _rel(out, ref) < 5e-3
+    assert _rel(out[:, (nh + nkv) * d:], ref[:, (nh + nkv) * d:]) < 5e-3
+
+
+@pytest.mark.parametrize("B,T,nh,nkv,d", [(3, 65, 4, 2, 64), (2, 1023, 12, 4, 64), (2, 100, 16, 4, 128)])
+def test_rope_bwd_stream(B, T, nh, nkv, d):
+    """Streaming RoPE backward (in-place inverse rotation of the q / k heads + QKV bias gradient from
+    per-block partials) vs fp32 torch autograd through the rotation."""
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.oracle import rope_tables
+    ops = _ops()
+    torch.manual_seed(17)
+    M, W = B * T, (nh + 2 * nkv) * d
+    cfg = ModelConfig(hidden_dim=nh * d, num_layers=1, num_heads=nh, num_kv_heads=nkv, ffn_hidden_dim=64,
+                      vocab_size=64, max_seq_len=T, rope_theta=10000.0)
+    cos, sin = rope_tables(cfg, T)
+    cos, sin = cos.cuda().contiguous(), sin.cuda().contiguous()
+    z = torch.randn(M, W, device="cuda", requires_grad=True)
+    t = torch.arange(M, device="cuda") % T
+    c, s_ = cos[t], sin[t]
+    half = d // 2
+    parts = []
+    for h in range(nh + 2 * nkv):
+        zz = z[:, h * d:(h + 1) * d]
+        if h < nh + nkv:
+            a, q = zz[:, :half], zz[:, half:]
+            zz = torch.cat([a * c - q * s_, a * s_ + q * c], dim=1)
+        parts.append(zz)
+    rot = torch.cat(parts, dim=1)
+    g = torch.randn(M, W, device="cuda").bfloat16()
+    rot.backward(g.float())
+    dq = g.clone()
+    db = torch.full((W,), 0.5, device="cuda")
+    scratch = torch.empty(ops.rope_bwd_stream_scratch(M, W), device="cuda")
+    ops.rope_bwd_stream(dq, db, cos, sin, scratch, M=M, T=T, nh=nh, nkv=nkv, d=d)
+    torch.cuda.synchronize()
+    assert _rel(dq, z.grad) < 8e-3
+    assert _rel(db - 0.5, dq.float().sum(0)) < 1e-4
+    assert _rel(db - 0.5, z.grad.sum(0)) < 8e-3
+
+
+@pytest.mark.parametrize("M,F,K", [(129, 192, 160), (300, 256, 768), (1000, 2048, 768), (64, 64, 64)])
+def test_gemm_swiglu_fwd_fused(M, F, K):
+    """gate|up GEMM with the SwiGLU activation in its epilogue vs fp32 torch (partial row, column and
+    K tiles included)."""
+    ops = _ops()
+    torch.manual_seed(11)
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    w = (torch.randn(2 * F, K, device="cuda") / K ** 0.5).bfloat16()
+    gu = torch.full((M, 2 * F), 7.0, device="cuda", dtype=torch.bfloat16)
+    h = torch.full((M, F), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_swiglu_fwd(x, w, gu, h)
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    g, u = ref[:, :F], ref[:, F:]
+    assert _rel(gu, ref) < 5e-3
+    assert _rel(h, torch.nn.functional.silu(g) * u) < 8e-3
+
+
+@pytest.mark.parametrize("M,F,K", [(129, 192, 160), (300, 256, 768), (1000, 2048, 768), (64, 64, 64)])
+def test_gemm_swiglu_bwd_fused(M, F, K):
+    """down-projection data gradient with the SwiGLU backward in its epilogue (dh never stored) vs fp32
+    torch autograd through silu(g) * u."""
+    ops = _ops()
+    torch.manual_seed(12)
+    dy = torch.randn(M, K, device="cuda").bfloat16()
+    wd = (torch.randn(K, F, device="cuda") / K ** 0.5).bfloat16()
+    gu = torch.randn(M, 2 * F, device="cuda").bfloat16()
+    dgu = torch.full((M, 2 * F), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_swiglu_bwd(dy, wd, gu, dgu)
+    torch.cuda.synchronize()
+    dh = dy.float() @ wd.float()
+    g, u = gu.float()[:, :F].requires_grad_(), gu.float()[:, F:].requires_grad_()
+    (torch.nn.functional.silu(g) * u).backward(dh)
+    assert _rel(dgu[:, :F], g.grad) < 1e-2
+    assert _rel(dgu[:, F:], u.grad) < 1e-2
+
+
+@pytest.mark.parametrize("rows,V,K,T", [(300, 512, 128, 64), (1023, 32768, 768, 1023), (200, 1000, 64, 50)])
+def test_logits_lse_and_cross_entropy(rows, V, K, T):
+    """LM-head GEMM with fp32 softmax statistics in its epilogue + the cross-entropy pass that uses them:
+    the loss per row equals the fp32 log-sum-exp minus the fp32 target logit of the same product (no bf16
+    rounding of the logits enters the loss), the logits are replaced by the scaled softmax - onehot."""
+    ops = _ops()
+    torch.manual_seed(21)
+    S = T + 1
+    nb = (rows + T - 1) // T
+    ids = torch.randint(0, V, (nb, S), device="cuda", dtype=torch.int32)
+    x = (torch.randn(rows, K, device="cuda") * 0.5).bfloat16()
+    e = (torch.randn(V, K, device="cuda") / K ** 0.5 * 3).bfloat16()
+    logits = torch.empty(rows, V, device="cuda", dtype=torch.bfloat16)
+    part = torch.empty(2 * ops.lse_parts(rows, V), device="cuda")
+    tl = torch.empty(rows, device="cuda")
+    loss = torch.empty(rows, device="cuda")
+    r0 = 0
+    ops.gemm_logits_lse(x, e, logits, part, tl, ids, rows=rows, V=V, K=K, T=T, S=S, r0=r0)
+    ref = x.float() @ e.float().t()
+    torch.cuda.synchronize()
+    assert _rel(logits, ref) < 5e-3
+    g = torch.arange(rows, device="cuda") + r0
+    tgt = ids[g // T, g % T + 1].long()
+    ref_tl = ref.gather(1, tgt[:, None])[:, 0]
+    assert torch.allclose(tl, ref_tl, rtol=1e-4, atol=1e-4)
+    ops.ce_lse_bwd(logits, part, tl, ids, loss, rows=rows, V=V, T=T, S=S, r0=r0, grad_scale=0.5)
+    torch.cuda.synchronize()
+    ref_loss = torch.logsumexp(ref, dim=1) - ref_tl
+    assert (loss - ref_loss).abs().max().item() < 1e-4
+    p = torch.softmax(ref, dim=1)
+    p[torch.arange(rows), tgt] -= 1.0
+    assert _rel(logits, 0.5 * p) < 2e-2
+
+
 @pytest.mark.parametrize("V", [32768, 512, 256])
 def test_cross_entropy(V):
     ops = _ops()
