@@ -137,9 +137,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        # NCCL's communicator set-up lines (ranks, devices, transports) go to stderr, stdout stays the JSON line
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # NCCL's communicator set-up lines (ranks, devices, transports) stay on, on stderr, so the ranks and
+        # GPUs of the run can be checked; stdout stays the one JSON line
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ["NCCL_DEBUG_SUBSYS"] = os.environ.get("NCCL_DEBUG_SUBSYS") or "INIT"
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=300))

@@ -10,7 +10,9 @@
 // precomputed descriptors, and two CTAs share an SM where TMEM allows (two issuers). The softmax side
 // is bound by the exp2 unit (16 results / clock / SM).
 //
-// Forward. One CTA = 128 query rows of one (batch, head); 10 warps:
+// Forward. Persistent: CTAS x SMs CTAs loop over tiles of 128 query rows of one (batch, head), heaviest
+// (longest causal) query blocks first; the next tile's Q (double-buffered) and K/V loads and its first
+// product overlap the current tile's last softmax and epilogue. 10 warps:
 //   warp 0     TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring (3-D tensor map
 //              [B, T, W] so rows past T are zero-filled per sequence; no cluster multicast)
 //   warp 1     single-thread tcgen05.mma issuer: S = Q K^T (N = 128) into TMEM; O += P V with P a TMEM
@@ -136,13 +138,35 @@ struct FCfg {
   static constexpr int CTAS = (D == 64) ? 2 : 1;   // CTAs per SM
   static constexpr int ST = 2;                     // K / V stages
   static constexpr int TT = 128 * D * 2;           // one [128][D] bf16 tile
-  static constexpr int SMEM = TT + ST * 2 * TT + 4 * 128 * 4 + 2 * 128 * 4 + 256;
+  // Q double-buffered (the next tile's Q arrives while this tile runs) + K/V ring + max/sum exchange
+  static constexpr int SMEM = 2 * TT + ST * 2 * TT + 4 * 128 * 4 + 2 * 128 * 4 + 256;
   static constexpr int TMEM_COLS = (D == 64) ? 256 : 512;
   static constexpr int C_O = 128, C_P = 128 + D;
   static_assert(C_P + 64 <= TMEM_COLS, "forward TMEM budget");
 };
 static_assert(2 * (FCfg<64>::SMEM + 1024) <= 233472 && FCfg<128>::SMEM <= 232448, "forward shared memory");
 
+// Work unit (tile) t of the forward: heaviest query blocks first across all (batch, head) pairs
+// (a longest-processing-time-first order for the persistent CTAs).
+struct FwdTile {
+  int b, h, qb, g, nkb;
+};
+__device__ __forceinline__ FwdTile fwd_tile(int t, int B, int nh, int nkv, int nqb) {
+  FwdTile w;
+  const int bh_count = B * nh;
+  w.qb = nqb - 1 - t / bh_count;
+  const int bh = t % bh_count;
+  w.h = bh % nh;
+  w.b = bh / nh;
+  w.g = w.h / (nh / nkv);
+  w.nkb = w.qb + 1;  // causal: key blocks 0..qb (BKV == BQ)
+  return w;
+}
+
+// Persistent forward: a grid of CTAS x SMs CTAs, each looping over tiles blockIdx.x, +gridDim.x, ...
+// All warps walk the same tile sequence; barrier phases follow a global key-block counter `jg` (K/V ring,
+// S / P / O hand-offs, max exchange) and a tile counter `tl` (Q buffers, sum exchange), so the next
+// tile's Q and K/V loads and its first S = Q K^T overlap this tile's last softmax and epilogue.
 template <int D>
 __global__ void __launch_bounds__(FWD_THREADS, FCfg<D>::CTAS)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __restrict__ out,
@@ -154,16 +178,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
     if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 499);
     return;
   }
-  uint8_t* sQ = smem_raw;
-  uint8_t* sK = sQ + C::TT;             // [ST][TT]
+  uint8_t* sQ = smem_raw;               // [2][TT]
+  uint8_t* sK = sQ + 2 * C::TT;         // [ST][TT]
   uint8_t* sV = sK + C::ST * C::TT;     // [ST][TT]
   float* sMax = reinterpret_cast<float*>(sV + C::ST * C::TT);  // [2 parity][2 halves][128 rows]
   float* sL = sMax + 4 * 128;                                  // [2 halves][128 rows]
   uint64_t* bar = reinterpret_cast<uint64_t*>(sL + 2 * 128);
-  uint64_t* q_full = bar;
-  uint64_t* kv_full = bar + 1;           // [ST]
-  uint64_t* kv_empty = bar + 1 + C::ST;  // [ST]
-  uint64_t* s_full = bar + 1 + 2 * C::ST;
+  uint64_t* q_full = bar;                // [2]
+  uint64_t* q_empty = bar + 2;           // [2]
+  uint64_t* kv_full = bar + 4;           // [ST]
+  uint64_t* kv_empty = bar + 4 + C::ST;  // [ST]
+  uint64_t* s_full = bar + 4 + 2 * C::ST;
   uint64_t* s_free = s_full + 1;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = s_full + 3;
@@ -174,14 +199,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = (T + BQ - 1) / BQ;
-  const int qb = nqb - 1 - (blockIdx.x % nqb);  // heavy (long) query blocks first
-  const int bh = blockIdx.x / nqb;
-  const int h = bh % nh, b = bh / nh;
-  const int g = h / (nh / nkv);
-  const int nkb = qb + 1;  // causal: key blocks 0..qb (BKV == BQ)
+  const int ntiles = B * nh * nqb;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
     for (int i = 0; i < C::ST; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
     mbar_init(s_full, 1);
     mbar_init(s_free, FWD_SM_WARPS);
@@ -205,62 +226,101 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
   CTA_TRACE(1);
 
   if (warp == 0) {
+    // ───── TMA producer: per tile its Q (double buffer), then its K/V blocks into the ring ─────
     if (lane == 0) {
       tma_prefetch_desc(&tmQKV);
-      const int xq = h * D, xk = (nh + g) * D, xv = (nh + nkv + g) * D;
-      mbar_arrive_expect_tx(q_full, C::TT);
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_3d(sQ + c * (BQ * 128), &tmQKV, q_full, xq + 64 * c, qb * BQ, b);
-      for (int j = 0; j < nkb; ++j) {
-        const int st = j % C::ST;
-        if (j >= C::ST &&
-            !mbar_wait_bounded(&kv_empty[st], ((j / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag))
+      int jg = 0, tl = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tl) {
+        const FwdTile w = fwd_tile(t, B, nh, nkv, nqb);
+        const int qbuf = tl & 1;
+        if (tl >= 2 &&
+            !mbar_wait_bounded(&q_empty[qbuf], ((tl >> 1) - 1) & 1, DT_ERR_TIMEOUT_EMPTY, 401, abort_flag)) {
+          ok = false;
           break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * C::TT);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sK + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xk + 64 * c, j * BKV, b);
-          tma_load_3d(sV + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xv + 64 * c, j * BKV, b);
         }
+        mbar_arrive_expect_tx(&q_full[qbuf], C::TT);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sQ + qbuf * C::TT + c * (BQ * 128), &tmQKV, &q_full[qbuf], w.h * D + 64 * c, w.qb * BQ, w.b);
+        const int xk = (nh + w.g) * D, xv = (nh + nkv + w.g) * D;
+        for (int j = 0; j < w.nkb; ++j, ++jg) {
+          const int st = jg % C::ST;
+          if (jg >= C::ST &&
+              !mbar_wait_bounded(&kv_empty[st], ((jg / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * C::TT);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_3d(sK + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xk + 64 * c, j * BKV, w.b);
+            tma_load_3d(sV + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xv + 64 * c, j * BKV, w.b);
+          }
+        }
+      }
+      if (!ok) {
+        // an aborted run: let the loads already issued land before the CTA exits (bounded)
+        uint64_t t0 = dt_globaltimer();
+        for (int k = (jg > C::ST ? jg - C::ST : 0); k < jg; ++k)
+          while (!mbar_try_wait(&kv_full[k % C::ST], (k / C::ST) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
+        for (int k = (tl > 2 ? tl - 2 : 0); k <= tl && k >= 0; ++k)
+          while (!mbar_try_wait(&q_full[k & 1], (k >> 1) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
       }
     }
   } else if (warp == 1) {
+    // ───── single-thread tcgen05.mma issuer ─────
     if (lane == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(BQ, BKV, 0, 0);
       constexpr uint32_t idO = umma_idesc_bf16(BQ, D, 0, 1);
       constexpr uint64_t STG = (uint64_t)(C::TT >> 4);
       const uint64_t dQ0 = kdesc0(smem_u32(sQ)), dK0 = kdesc0(smem_u32(sK)), mV0 = mndesc0(smem_u32(sV));
       bool issued = false;
-      auto issue_s = [&](int j) -> bool {  // S = Q K^T of key block j
-        if (!mbar_wait_bounded(&kv_full[j % C::ST], (j / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 411, abort_flag))
+      // S = Q K^T of global key block jg (of a tile whose Q sits in buffer qbuf, tile counter tl)
+      auto issue_s = [&](int jg, int qbuf, int tl, bool first_of_tile) -> bool {
+        if (first_of_tile &&
+            !mbar_wait_bounded(&q_full[qbuf], (tl >> 1) & 1, DT_ERR_TIMEOUT_FULL, 410, abort_flag))
+          return false;
+        if (!mbar_wait_bounded(&kv_full[jg % C::ST], (jg / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 411, abort_flag))
           return false;
         tc_fence_after();
-        const uint64_t kk = dK0 + (uint64_t)(j % C::ST) * STG;
+        const uint64_t qq = dQ0 + (uint64_t)qbuf * STG;
+        const uint64_t kk = dK0 + (uint64_t)(jg % C::ST) * STG;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, dQ0 + koff(k), kk + koff(k), idS, k > 0 ? 1u : 0u);
+        for (int k = 0; k < D / 16; ++k) umma_bf16(tS, qq + koff(k), kk + koff(k), idS, k > 0 ? 1u : 0u);
         umma_commit(s_full);
-        ATTN_TRACE(0, j);
+        ATTN_TRACE(0, jg);
         issued = true;
         return true;
       };
-      bool ok = mbar_wait_bounded(q_full, 0, DT_ERR_TIMEOUT_FULL, 410, abort_flag) && issue_s(0);
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j % C::ST;
-        if (j + 1 < nkb) {
-          // S of the next block once the softmax warps have read this block's S out of TMEM
-          if (!mbar_wait_bounded(s_free, j & 1, DT_ERR_TIMEOUT_TMEM, 412, abort_flag) || !issue_s(j + 1)) {
-            ok = false;
-            break;
+      int jg = 0, tl = 0;
+      int t = blockIdx.x;
+      bool ok = t < ntiles;
+      FwdTile w = fwd_tile(t < ntiles ? t : 0, B, nh, nkv, nqb);
+      if (ok) ok = issue_s(0, 0, 0, true);
+      for (; t < ntiles && ok; t += gridDim.x, ++tl) {
+        const int qbuf = tl & 1;
+        const int tn = t + gridDim.x;  // next tile of this CTA
+        for (int j = 0; j < w.nkb && ok; ++j, ++jg) {
+          const int st = jg % C::ST;
+          const bool last = j + 1 == w.nkb;
+          if (!last || tn < ntiles) {
+            // S of the next key block (this tile's, or the next tile's first) once S(jg) has been read
+            if (!mbar_wait_bounded(s_free, jg & 1, DT_ERR_TIMEOUT_TMEM, 412, abort_flag)) { ok = false; break; }
+            if (last) umma_commit(&q_empty[qbuf]);  // every S of this tile is issued: its Q may be replaced
+            if (!issue_s(jg + 1, last ? qbuf ^ 1 : qbuf, last ? tl + 1 : tl, last)) { ok = false; break; }
           }
-        }
-        if (!mbar_wait_bounded(p_full, j & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) { ok = false; break; }
-        ATTN_TRACE(1, j);
-        tc_fence_after();
-        const uint64_t vv = mV0 + (uint64_t)st * STG;
+          if (!mbar_wait_bounded(p_full, jg & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) { ok = false; break; }
+          ATTN_TRACE(1, jg);
+          tc_fence_after();
+          const uint64_t vv = mV0 + (uint64_t)st * STG;
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k) umma_bf16_ts(tO, tP + k * 8, vv + mnoff(k), idO, (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
+          for (int k = 0; k < BKV / 16; ++k)
+            umma_bf16_ts(tO, tP + k * 8, vv + mnoff(k), idO, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(pv_done);
+          umma_commit(&kv_empty[st]);
+        }
+        if (tn < ntiles) w = fwd_tile(tn, B, nh, nkv, nqb);
       }
       if (!ok && issued) {
         umma_commit(drain);
@@ -272,95 +332,101 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
     // ───── softmax warps: row r = TMEM lane r, key columns [cg*64, cg*64+64) of each block ─────
     const int sw = warp - 2, quad = warp & 3, cg = sw >> 2;
     const int r = quad * 32 + lane;
-    const int q = qb * BQ + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = scale * LOG2E_F;
     const uint64_t sl2v = f2_pack(sl2, sl2);
-    float m_run = -INFINITY, l_part = 0.f;
     WarpWait wwait{abort_flag, lane};
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
-      if (!wwait(s_full, j & 1, 420)) { ok = false; break; }
-      if (warp == 2 && lane == 0) ATTN_TRACE(2, j);
-      tc_fence_after();
-      uint32_t sv[64];
-      tmem_ld_32x32b_x32(tS + lane_off + cg * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(tS + lane_off + cg * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      warp_arrive(s_free, lane);
-      const int key0 = j * BKV + cg * 64;
-      const bool need_mask = (j == qb) || (j + 1) * BKV > T;
-      // valid columns e < hi (causal key <= q, key < T); rows q >= T have none
-      const int hi = need_mask ? (q < T ? min(q - key0 + 1, T - key0) : 0) : 64;
-      float mx = -INFINITY;
-      if (need_mask) {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) mx = (e < hi) ? fmaxf(mx, __uint_as_float(sv[e])) : mx;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
-      }
-      // row max over both halves (partner warp: same lane quarter, other column half)
-      float* mbuf = sMax + (j & 1) * 256;
-      mbuf[cg * 128 + r] = mx;
-      warp_arrive(&xch[quad * 3 + (j & 1)], lane);
-      if (!wwait(&xch[quad * 3 + (j & 1)], (j >> 1) & 1, 423)) { ok = false; break; }
-      mx = fmaxf(mx, mbuf[(cg ^ 1) * 128 + r]);
-      if (warp == 2 && lane == 0) ATTN_TRACE(3, j);
-      const float m_new = mx * sl2;  // -inf when the row has no valid key yet
-      // stale-max policy: raise the reference max only when it grows by more than the threshold
-      float m_use = m_run;
-      bool resc = false;
-      if (m_new > m_run + RESCALE_THRESHOLD || m_run == -INFINITY) {
-        m_use = m_new;
-        resc = (m_run != -INFINITY);
-      }
-      const float m_safe = (m_use == -INFINITY) ? 0.f : m_use;
-      const float alpha = resc ? ex2_approx(m_run - m_use) : 1.f;
-      const uint64_t nm = f2_pack(-m_safe, -m_safe);
-      uint32_t pk[32];
-      uint64_t rs2 = f2_pack(0.f, 0.f);
-#pragma unroll
-      for (int e = 0; e < 64; e += 2) {
-        const float2 x = f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2v, nm));
-        float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+    int jg = 0, tl = 0;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tl) {
+      const FwdTile w = fwd_tile(t, B, nh, nkv, nqb);
+      const int q = w.qb * BQ + r;
+      float m_run = -INFINITY, l_part = 0.f;
+      for (int j = 0; j < w.nkb; ++j, ++jg) {
+        if (!wwait(s_full, jg & 1, 420)) { ok = false; break; }
+        if (warp == 2 && lane == 0) ATTN_TRACE(2, jg);
+        tc_fence_after();
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(tS + lane_off + cg * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(tS + lane_off + cg * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        warp_arrive(s_free, lane);
+        const int key0 = j * BKV + cg * 64;
+        const bool need_mask = (j == w.qb) || (j + 1) * BKV > T;
+        // valid columns e < hi (causal key <= q, key < T); rows q >= T have none
+        const int hi = need_mask ? (q < T ? min(q - key0 + 1, T - key0) : 0) : 64;
+        float mx = -INFINITY;
         if (need_mask) {
-          p0 = (e < hi) ? p0 : 0.f;
-          p1 = (e + 1 < hi) ? p1 : 0.f;
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mx = (e < hi) ? fmaxf(mx, __uint_as_float(sv[e])) : mx;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
         }
-        rs2 = f2_add(rs2, f2_pack(p0, p1));
-        pk[e / 2] = pack_bf16(p0, p1);
+        // row max over both halves (partner warp: same lane quarter, other column half)
+        float* mbuf = sMax + (jg & 1) * 256;
+        mbuf[cg * 128 + r] = mx;
+        warp_arrive(&xch[quad * 3 + (jg & 1)], lane);
+        if (!wwait(&xch[quad * 3 + (jg & 1)], (jg >> 1) & 1, 423)) { ok = false; break; }
+        mx = fmaxf(mx, mbuf[(cg ^ 1) * 128 + r]);
+        if (warp == 2 && lane == 0) ATTN_TRACE(3, jg);
+        const float m_new = mx * sl2;  // -inf when the row has no valid key yet
+        // stale-max policy: raise the reference max only when it grows by more than the threshold
+        float m_use = m_run;
+        bool resc = false;
+        if (m_new > m_run + RESCALE_THRESHOLD || m_run == -INFINITY) {
+          m_use = m_new;
+          resc = (m_run != -INFINITY);
+        }
+        const float m_safe = (m_use == -INFINITY) ? 0.f : m_use;
+        const float alpha = resc ? ex2_approx(m_run - m_use) : 1.f;
+        const uint64_t nm = f2_pack(-m_safe, -m_safe);
+        uint32_t pk[32];
+        uint64_t rs2 = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const float2 x = f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2v, nm));
+          float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+          if (need_mask) {
+            p0 = (e < hi) ? p0 : 0.f;
+            p1 = (e + 1 < hi) ? p1 : 0.f;
+          }
+          rs2 = f2_add(rs2, f2_pack(p0, p1));
+          pk[e / 2] = pack_bf16(p0, p1);
+        }
+        const float2 rs = f2_unpack(rs2);
+        l_part = l_part * alpha + (rs.x + rs.y);
+        m_run = m_use;
+        if (warp == 2 && lane == 0) ATTN_TRACE(4, jg);
+        // P and O are busy until the previous P V of this tile has completed (the previous tile's last
+        // P V was waited for by its epilogue)
+        if (j > 0 && !wwait(pv_done, (jg - 1) & 1, 421)) { ok = false; break; }
+        if (warp == 2 && lane == 0) ATTN_TRACE(5, jg);
+        tc_fence_after();
+        if (j > 0 && __any_sync(0xffffffffu, resc)) tmem_row_scale(tO + lane_off + cg * (D / 2), D / 2, alpha);
+        tmem_st_32x32b_x16(tP + lane_off + cg * 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+        tmem_st_32x32b_x16(tP + lane_off + cg * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        warp_arrive(p_full, lane);
+        if (warp == 2 && lane == 0) ATTN_TRACE(6, jg);
       }
-      const float2 rs = f2_unpack(rs2);
-      l_part = l_part * alpha + (rs.x + rs.y);
-      m_run = m_use;
-      if (warp == 2 && lane == 0) ATTN_TRACE(4, j);
-      // P and O are busy until the previous P V has completed
-      if (j > 0 && !wwait(pv_done, (j - 1) & 1, 421)) { ok = false; break; }
-      if (warp == 2 && lane == 0) ATTN_TRACE(5, j);
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, resc)) tmem_row_scale(tO + lane_off + cg * (D / 2), D / 2, alpha);
-      tmem_st_32x32b_x16(tP + lane_off + cg * 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-      tmem_st_32x32b_x16(tP + lane_off + cg * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      warp_arrive(p_full, lane);
-      if (warp == 2 && lane == 0) ATTN_TRACE(6, j);
-    }
-    // epilogue: O / l -> bf16 rows of `out` (this half's D/2 columns), lse
-    if (ok && wwait(pv_done, (nkb - 1) & 1, 422)) {
+      if (!ok) break;
+      // epilogue: O / l -> bf16 rows of `out` (this half's D/2 columns), lse
+      if (!wwait(pv_done, (jg - 1) & 1, 422)) { ok = false; break; }
       tc_fence_after();
       sL[cg * 128 + r] = l_part;
       warp_arrive(&xch[quad * 3 + 2], lane);
-      ok = wwait(&xch[quad * 3 + 2], 0, 424);
-    }
-    if (ok) {
+      if (!wwait(&xch[quad * 3 + 2], tl & 1, 424)) { ok = false; break; }
       const float l = l_part + sL[(cg ^ 1) * 128 + r];
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = out + ((long long)b * T + q) * ((long long)nh * D) + h * D + cg * (D / 2);
+      __nv_bfloat16* orow = out + ((long long)w.b * T + q) * ((long long)nh * D) + w.h * D + cg * (D / 2);
       tmem_row_to_bf16(tO + lane_off + cg * (D / 2), D / 2, inv, q < T, orow);
-      if (cg == 0 && q < T) lse[((long long)b * nh + h) * ((T + 3) & ~3) + q] = (m_run + log2f(l)) * LN2_F;
+      if (cg == 0 && q < T) lse[((long long)w.b * nh + w.h) * ((T + 3) & ~3) + q] = (m_run + log2f(l)) * LN2_F;
+      // the partner reads sL before either warp writes it for the next tile: the next tile's first
+      // max exchange (which both must pass) orders it
+      tc_fence_before();
     }
   }
 
@@ -406,9 +472,17 @@ int fwd_tc_launch(const void* qkv, void* out, float* lse, int B, int T, int nh, 
     DT_CUDA_RET(cudaFuncSetAttribute(attn_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     set = true;
   }
-  int nqb = (T + BQ - 1) / BQ;
-  attn_fwd_tc_kernel<D><<<B * nh * nqb, FWD_THREADS, C::SMEM, st>>>(m, reinterpret_cast<__nv_bfloat16*>(out), lse, B,
-                                                                     T, nh, nkv, scale);
+  const int nqb = (T + BQ - 1) / BQ;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    DT_CUDA_RET(cudaGetDevice(&dev));
+    DT_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const long long tiles = (long long)B * nh * nqb;
+  const int grid = (int)(tiles < (long long)C::CTAS * sms ? tiles : (long long)C::CTAS * sms);  // persistent
+  attn_fwd_tc_kernel<D><<<grid, FWD_THREADS, C::SMEM, st>>>(m, reinterpret_cast<__nv_bfloat16*>(out), lse, B, T, nh,
+                                                             nkv, scale);
   return (int)cudaGetLastError();
 }
 

@@ -7,9 +7,10 @@
 // * One elected thread of warp 1 issues tcgen05.mma (M=128, N=BN, K=16, fp32 accumulate) into one
 //   of two TMEM accumulators; tcgen05.commit releases shared-memory stages and hands finished
 //   accumulators to the epilogue, so the epilogue of tile i overlaps the main loop of tile i+1.
-// * Warps 2..5 drain TMEM with tcgen05.ld (32 lanes x 32 columns per load) into a swizzled shared
-//   staging box and write it with a TMA store (bf16 / fp32) or a TMA reduce-add (fp32 accumulation,
-//   used for split-K and gradient accumulation), so global writes are full-line and asynchronous.
+// * Warps 2..9 (two per TMEM lane quadrant, each half of the tile's columns) drain TMEM with tcgen05.ld
+//   (32 lanes x 32 columns per load) into swizzled shared staging boxes and write them with a TMA store
+//   (bf16 / fp32) or a TMA reduce-add (fp32 accumulation, used for split-K and gradient accumulation), so
+//   global writes are full-line and asynchronous.
 // * Tiles are visited by a persistent grid (one CTA per SM) in grouped order for L2 reuse.
 // * Fused SwiGLU (reference model.rs:292-296, h = silu(x Wg^T) * (x Wu^T)):
 //     forward (MODE 1): one 256-wide tile holds 128 gate columns and the 128 matching up columns (the B

@@ -128,9 +128,6 @@ class TrainEngine:
         # 64 KB of gate / up cannot be double-buffered beside the operand ring. It stays selectable.
         self.fused_swiglu = F % 64 == 0
         self.fused_swiglu_bwd = False
-        # streaming RoPE backward (head dims 64 / 128, QKV width a multiple of 256)
-        self.rope_scratch = (torch.empty(ops.rope_bwd_stream_scratch(M, self.W), dtype=f32, device=dev)
-                             if d in (64, 128) and self.W % 256 == 0 else None)
         self.dh = None if self.fused_swiglu_bwd else torch.empty(M, F, dtype=bf16, device=dev)
         self.dgu = torch.empty(M, 2 * F, dtype=bf16, device=dev)
         self.dattn = torch.empty(M, nh * d, dtype=bf16, device=dev)
@@ -298,11 +295,7 @@ class TrainEngine:
             ops.linear_wgrad(self.g16, self.attn[l], gv["o_w"])
             attn_ops.attention_bwd(self.qkv[l], self.attn[l], self.dattn, self.lse[l], self.dqkv, self.dq_acc,
                                    self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl)
-            if self.rope_scratch is not None:  # one streaming pass: inverse rotation + bias gradient
-                ops.rope_bwd_stream(self.dqkv, gv["qkv_b"], self.cos, self.sin, self.rope_scratch, M=M, T=T, nh=nh,
-                                    nkv=nkv, d=d)
-            else:
-                ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+            ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
             self._col_parallel_dgrad_norm_bwd(
                 self.dqkv, wv["qkv_w"], lambda: ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"]),
                 x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"], dresid_in=self.dresid,

@@ -142,24 +142,6 @@ def gemm_swiglu_bwd(dy, w_down, gu, dgu, stream=None):
           "dt_gemm_swiglu_bwd")
 
 
-def rope_bwd_stream_scratch(M: int, W: int) -> int:
-    """fp32 elements of the scratch buffer ``rope_bwd_stream`` needs for an [M, W] gradient."""
-    return ((M + 127) // 128) * W
-
-
-def rope_bwd_stream(dqkv, dbias, cos, sin, scratch, *, M, T, nh, nkv, d, stream=None):
-    """In-place inverse rotation of the q / k heads of dqkv and dbias += its column sums (one read and one
-    write of dqkv; per-block column partials in ``scratch``, no atomics). d = 64 / 128, W % 256 == 0."""
-    check(lib().dt_rope_bwd_stream(ptr(dqkv), ptr(dbias), ptr(cos), ptr(sin), M, T, nh, nkv, d, ptr(scratch),
-                                   stream_ptr(stream)), "dt_rope_bwd_stream")
-
-
-def colsum_bf16(x, out, stream=None):
-    """out[c] += sum over rows of x[:, c] (x bf16 [M, W], out fp32 [W]): the QKV bias gradient."""
-    M, W = x.shape
-    check(lib().dt_colsum_bf16(ptr(x), M, W, ptr(out), stream_ptr(stream)), "dt_colsum_bf16")
-
-
 def swiglu_fwd(gu, h, *, M, F, stream=None):
     check(lib().dt_swiglu_fwd(ptr(gu), ptr(h), M, F, stream_ptr(stream)), "dt_swiglu_fwd")
 

@@ -40,8 +40,6 @@ _SIGS = {
     "dt_embedding_bwd": [c_void, c_void, c_int, c_int, c_void, c_int, c_int, c_void],
     "dt_rope_fwd": [c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void],
     "dt_rope_bwd": [c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void],
-    "dt_colsum_bf16": [c_void, c_ll, c_int, c_void, c_void],
-    "dt_rope_bwd_stream": [c_void, c_void, c_void, c_void, c_ll, c_int, c_int, c_int, c_int, c_void, c_void],
     "dt_swiglu_fwd": [c_void, c_void, c_ll, c_int, c_void],
     "dt_gemm_qkv_rope": [c_void, c_ll, c_void, c_ll, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
                          c_int, c_int, c_int, c_void],
