@@ -229,28 +229,32 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const __nv_bfloat16* __res
 }
 
 // ─────────────────────────────── backward ───────────────────────────────
-// delta[b,h,q] = sum_d dO * O   (one thread per (row, head), 16-byte loads)
+// delta[b,h,q] = sum_d dO * O. Thread = 8 consecutive elements of one row (16-byte loads, a warp reads 512
+// contiguous bytes of each operand); the D/8 threads of one (row, head) sit in consecutive lanes and sum
+// by shuffles, the first writes delta.
 __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ dout,
                                     float* __restrict__ delta, int B, int T, int nh, int D) {
-  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  const long long total = (long long)B * T * nh;
-  if (i >= total) return;
-  const long long row = i / nh;
-  const int h = (int)(i % nh);
-  const uint4* o = reinterpret_cast<const uint4*>(out + row * nh * D + h * D);
-  const uint4* d = reinterpret_cast<const uint4*>(dout + row * nh * D + h * D);
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;  // 8-element chunk
+  const int cpr = nh * D / 8;                                             // chunks per row
+  const long long total = (long long)B * T * cpr;
   float acc = 0.f;
-  for (int c = 0; c < D / 8; ++c) {
-    uint4 a = o[c], e = d[c];
-    uint32_t aa[4] = {a.x, a.y, a.z, a.w}, ee[4] = {e.x, e.y, e.z, e.w};
+  if (i < total) {
+    const uint4 a = reinterpret_cast<const uint4*>(out)[i], e = reinterpret_cast<const uint4*>(dout)[i];
+    const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, ee[4] = {e.x, e.y, e.z, e.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      float2 x = unpack_bf16(aa[k]), y = unpack_bf16(ee[k]);
+      const float2 x = unpack_bf16(aa[k]), y = unpack_bf16(ee[k]);
       acc += x.x * y.x + x.y * y.y;
     }
   }
-  const long long b = row / T, t = row % T;
-  delta[(b * nh + h) * ((T + 3) & ~3) + t] = acc;
+  const int g = D / 8;  // lanes per (row, head): divides 32, so a group never straddles warps
+  for (int o = g >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (i < total && (threadIdx.x & (g - 1)) == 0) {
+    const long long row = i / cpr;
+    const int h = (int)((i - row * cpr) / g);
+    const long long b = row / T, t = row - b * T;
+    delta[(b * nh + h) * ((T + 3) & ~3) + t] = acc;
+  }
 }
 
 template <int D>
@@ -456,7 +460,7 @@ DT_API int dt_attn_bwd(const void* qkv, const void* out, const void* dout, const
   auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv);
   long long M = (long long)B * T;
   DT_CUDA_RET(cudaMemsetAsync(dq_acc, 0, sizeof(float) * M * nh * D, st));
-  long long items = M * nh;
+  long long items = M * nh * (D / 8);
   attn_bwd_pre_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(o, d, delta, B, T, nh, D);
   int rc;
   if (D == 64) rc = bwd_launch<64>(q, d, lse, delta, dq, dq_acc, B, T, nh, nkv, scale, st);
@@ -475,8 +479,8 @@ DT_API int dt_attn_bwd(const void* qkv, const void* out, const void* dout, const
 // delta = rowsum(dO * O) per (row, head) into [B, nh, Tp] (the tcgen05 backward's pre-pass).
 DT_API int dt_attn_bwd_delta(const void* out, const void* dout, float* delta, int B, int T, int nh, int D,
                              cudaStream_t st) {
-  if (D % 8) return -10;
-  long long items = (long long)B * T * nh;
+  if (D % 8 || 32 % (D / 8)) return -10;
+  long long items = (long long)B * T * nh * (D / 8);
   attn_bwd_pre_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), delta, B, T, nh, D);
   return (int)cudaGetLastError();

@@ -520,12 +520,13 @@ namespace {
 constexpr int BW_EW_WARPS = 16;
 constexpr int BW_THREADS = 64 + 32 * BW_EW_WARPS;  // warp 0 TMA, warp 1 MMA, warps 2..17 element-wise
 
-template <int D>
+template <int D, bool DS = false>
 struct KVCfg {
   static constexpr int NSB = (D == 64) ? 2 : 1;  // S^T buffers in TMEM
-  static constexpr int ST = (D == 64) ? 4 : 2;   // Q / dO stages
+  static constexpr int ST = (D == 64) ? (DS ? 3 : 4) : 2;   // Q / dO stages
   static constexpr int TT = 128 * D * 2;         // one [128][D] bf16 tile
-  static constexpr int SMEM = 2 * TT + ST * 2 * TT + ST * 2 * 512 + 256;
+  static constexpr int DS_BYTES = DS ? 2 * 128 * 128 * 2 : 0;  // two dS^T staging tiles (TMA-stored)
+  static constexpr int SMEM = 2 * TT + ST * 2 * TT + ST * 2 * 512 + DS_BYTES + 512;
   // TMEM columns
   static constexpr int C_DP = NSB * 128, C_DV = C_DP + 128, C_DK = C_DV + D;
   static_assert(C_DK + D <= 512, "kv TMEM budget");
@@ -541,7 +542,8 @@ struct QCfg {
   static_assert(C_DO + D / 2 <= 512, "q TMEM budget");
 };
 
-static_assert(KVCfg<64>::SMEM <= 232448 && KVCfg<128>::SMEM <= 232448, "kv backward shared memory");
+static_assert(KVCfg<64>::SMEM <= 232448 && KVCfg<128>::SMEM <= 232448 && KVCfg<64, true>::SMEM <= 232448,
+              "kv backward shared memory");
 static_assert(QCfg<64>::SMEM <= 232448 && QCfg<128>::SMEM <= 232448, "q backward shared memory");
 
 // TMEM A operand of K-step k of a bf16 tile written by the element-wise threads: thread group cg holds
@@ -626,12 +628,18 @@ __device__ __forceinline__ void q_block_math(const uint32_t (&sv)[32], const uin
   }
 }
 
-template <int D>
+// DS: also store each (query block, key block) pair's dS^T tile (bf16, 128 keys x 128 queries) for the dQ
+// kernel: the element-wise warps write it into one of two shared staging tiles (the 128-byte swizzled
+// [64-column chunk][128 rows][128 B] layout), and one thread TMA-stores the tile once all 16 warps have
+// arrived; the two tiles alternate, a tile being rewritten only after its previous store has read it
+// (bounded mbarrier hand-offs both ways).
+template <int D, bool DS>
 __global__ void __launch_bounds__(BW_THREADS, 1)
 attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
                       const __grid_constant__ CUtensorMap tmLSE, const __grid_constant__ CUtensorMap tmDEL,
-                      __nv_bfloat16* __restrict__ dqkv, int B, int T, int nh, int nkv, float scale) {
-  using C = KVCfg<D>;
+                      const __grid_constant__ CUtensorMap tmDS, __nv_bfloat16* __restrict__ dqkv, int B, int T,
+                      int nh, int nkv, float scale) {
+  using C = KVCfg<D, DS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023) {
     if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 599);
@@ -643,7 +651,8 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
   uint8_t* sDO = sQ + C::ST * C::TT;    // [ST][TT]
   float* sLSE = reinterpret_cast<float*>(sDO + C::ST * C::TT);  // [ST][128]
   float* sDEL = sLSE + C::ST * 128;                             // [ST][128]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sDEL + C::ST * 128);
+  uint8_t* sDS = reinterpret_cast<uint8_t*>(sDEL + C::ST * 128);  // [2][128 x 128 bf16] (DS only)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sDS + C::DS_BYTES);
   uint64_t* kv_full = bar;
   uint64_t* qd_full = bar + 1;               // [ST]
   uint64_t* qd_empty = bar + 1 + C::ST;      // [ST]
@@ -653,7 +662,9 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
   uint64_t* dp_free = s_full + 5;            // dP^T read by the element-wise warps
   uint64_t* mm_done = s_full + 6;
   uint64_t* drain = s_full + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 8);
+  uint64_t* ds_ready = s_full + 8;           // [2] all element-wise warps wrote a staging tile
+  uint64_t* ds_free = s_full + 10;           // [2] a staging tile's previous TMA store has read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -676,6 +687,10 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
     mbar_init(dp_free, BW_EW_WARPS);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ds_ready[i], BW_EW_WARPS);
+      mbar_init(&ds_free[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -825,6 +840,38 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
           kv_block_math<false>(sv, dv, lse_s, del_s, sl2, 0, 32, pk, dk);
         }
       }
+      if constexpr (DS) {
+        // dS^T of this (query block i, key block kb) pair: row = key r, query columns cg*32..+32
+        const int db = it & 1;
+        if (it >= 2 && !wwait(&ds_free[db], ((it >> 1) - 1) & 1, 530)) { ok = false; break; }
+        uint8_t* tile = sDS + db * (128 * 128 * 2) + (cg >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(tile + ((((cg & 1) * 4 + v) ^ (r & 7)) << 4)) =
+              make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]);
+        fence_proxy_async_smem();
+        warp_arrive(&ds_ready[db], lane);
+        if (warp == 2 && lane == 0) {
+          if (!mbar_wait_bounded(&ds_ready[db], (it >> 1) & 1, DT_ERR_TIMEOUT_FULL, 531, abort_flag)) {
+            ok = false;
+          } else {
+            if (it >= 1) {  // the other tile's store (issued one block ago) has read it: free for block it+1
+              bulk_wait_read0();
+              mbar_arrive(&ds_free[db ^ 1]);
+            }
+            const int hh = it / nper, h = g * G + hh;
+            const long long pair =
+                ((long long)b * nh + h) * ((long long)nkb * (nkb + 1) / 2) + (long long)i * (i + 1) / 2 + kb;
+            uint8_t* t0 = sDS + db * (128 * 128 * 2);
+            tma_store_2d(&tmDS, t0, 0, (int)(pair * 128));
+            tma_store_2d(&tmDS, t0 + 128 * 128, 64, (int)(pair * 128));
+            bulk_commit();
+          }
+        }
+        __syncwarp();
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      }
       tmem_st_32x32b_x16(tS, pk);
       tmem_st_32x32b_x16(tS + 16, dk);
       tmem_st_wait();
@@ -841,6 +888,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
       tmem_row_to_bf16(tDK + lane_off + cg * (D / 4), D / 4, scale, key < T, krow);
       tmem_row_to_bf16(tDV + lane_off + cg * (D / 4), D / 4, 1.f, key < T, vrow);
     }
+    if (DS && warp == 2 && lane == 0) bulk_wait0();  // the dS^T stores have completed
   }
   tc_fence_before();
   __syncthreads();
@@ -1056,6 +1104,153 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// dQ from the stored dS^T tiles: dQ[q, :] = scale * sum over causal key blocks j of dS[q, keys of j] K[keys of j, :].
+// A batched GEMM with no exponentials (the kv kernel formed dS once): persistent CTAs over (batch, head,
+// query block) tiles, heaviest first; warp 0 streams the dS^T tile (as the MN-major A operand) and the K
+// tile (MN-major B) of each pair through a TMA ring, warp 1 issues tcgen05.mma into one of two TMEM
+// accumulators, warps 2..5 scale and store the finished dQ rows while the next tile accumulates.
+template <int D>
+struct DQCfg {
+  static constexpr int A_BYTES = 128 * 128 * 2;   // dS^T tile
+  static constexpr int B_BYTES = 128 * D * 2;     // K tile
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int ST = (232448 - 1024 - 256) / STAGE < 4 ? (232448 - 1024 - 256) / STAGE : 4;
+  static constexpr int SMEM = ST * STAGE + 256;
+  static constexpr int TMEM_COLS = 2 * D;
+};
+constexpr int DQ_THREADS = 192;
+
+template <int D>
+__global__ void __launch_bounds__(DQ_THREADS, 1)
+attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDS,
+                      __nv_bfloat16* __restrict__ dqkv, int B, int T, int nh, int nkv, float scale) {
+  using C = DQCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 699);
+    return;
+  }
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + C::ST * C::STAGE);
+  uint64_t* full = bar;                 // [ST]
+  uint64_t* empty = bar + C::ST;        // [ST]
+  uint64_t* tfull = bar + 2 * C::ST;    // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = (T + 127) / 128;
+  const int ntiles = B * nh * nqb;
+  const long long P = (long long)nqb * (nqb + 1) / 2;  // stored pairs per (batch, head)
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto tile_of = [&](int t, int& b, int& h, int& qb) {
+    const int bh_count = B * nh;
+    qb = nqb - 1 - t / bh_count;
+    const int bh = t % bh_count;
+    h = bh % nh;
+    b = bh / nh;
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQKV);
+      tma_prefetch_desc(&tmDS);
+      int stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int b, h, qb;
+        tile_of(t, b, h, qb);
+        const int g = h / (nh / nkv);
+        const long long pair0 = ((long long)b * nh + h) * P + (long long)qb * (qb + 1) / 2;
+        for (int j = 0; j <= qb; ++j) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, DT_ERR_TIMEOUT_EMPTY, 640, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE);
+          uint8_t* a = smem_raw + stage * C::STAGE;
+          uint8_t* kb = a + C::A_BYTES;
+          tma_load_2d(a, &tmDS, &full[stage], 0, (int)((pair0 + j) * 128));
+          tma_load_2d(a + 128 * 128, &tmDS, &full[stage], 64, (int)((pair0 + j) * 128));
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(kb + c * (128 * 128), &tmQKV, &full[stage], (nh + g) * D + 64 * c, j * 128, b);
+          ++issued;
+          if (++stage == C::ST) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        uint64_t t0 = dt_globaltimer();
+        for (int k = (issued > C::ST ? issued - C::ST : 0); k < issued; ++k)
+          while (!mbar_try_wait(&full[k % C::ST], (k / C::ST) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, D, 1, 1);
+      int stage = 0, phase = 0, local = 0;
+      bool ok = true, issued_any = false;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++local) {
+        int b, h, qb;
+        tile_of(t, b, h, qb);
+        const int acc = local & 1;
+        if (!mbar_wait_bounded(&tempty[acc], ((local >> 1) & 1) ^ 1, DT_ERR_TIMEOUT_TMEM, 641, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tacc = tmem + acc * D;
+        for (int j = 0; j <= qb; ++j) {
+          if (!mbar_wait_bounded(&full[stage], phase, DT_ERR_TIMEOUT_FULL, 642, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem_raw + stage * C::STAGE);
+          const uint64_t mA = mndesc0(a), mB = umma_smem_desc_sw128(a + C::A_BYTES, 128 * 128, 1024);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) umma_bf16(tacc, mA + mnoff(k), mB + mnoff(k), idesc, (j > 0 || k > 0) ? 1u : 0u);
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == C::ST) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok && issued_any) {
+        umma_commit(drain);
+        uint64_t t0 = dt_globaltimer();
+        while (!mbar_try_wait(drain, 0)) if (dt_globaltimer() - t0 > 20000000ull) break;
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const long long W = (long long)(nh + 2 * nkv) * D;
+    int local = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+      int b, h, qb;
+      tile_of(t, b, h, qb);
+      const int acc = local & 1;
+      if (!mbar_wait_bounded(&tfull[acc], (local >> 1) & 1, DT_ERR_TIMEOUT_TMEM, 643, abort_flag)) break;
+      tc_fence_after();
+      const int q = qb * 128 + quad * 32 + lane;
+      __nv_bfloat16* qrow = dqkv + ((long long)b * T + q) * W + h * D;
+      tmem_row_to_bf16(tmem + ((uint32_t)(quad * 32) << 16) + acc * D, D, scale, q < T, qrow);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
 // fp32 [rows, Tp] map with a {128, 1} box (LSE / delta slices of one query block).
 int rowvec_map(CUtensorMap* m, const float* p, long long rows, long long Tp) {
   if (!g_enc) return -2;
@@ -1071,7 +1266,7 @@ int rowvec_map(CUtensorMap* m, const float* p, long long rows, long long Tp) {
 
 template <int D>
 int bwd_tc_launch(const void* qkv, const void* dout, const float* lse, const float* delta, void* dqkv, int B, int T,
-                  int nh, int nkv, float scale, cudaStream_t st) {
+                  int nh, int nkv, float scale, cudaStream_t st, void* ds_buf = nullptr) {
   long long W = (long long)(nh + 2 * nkv) * D;
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(lse) |
        reinterpret_cast<uintptr_t>(delta)) & 15)
@@ -1085,13 +1280,46 @@ int bwd_tc_launch(const void* qkv, const void* dout, const float* lse, const flo
   if (rc) return rc;
   static bool set = false;
   if (!set) {
-    DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, KVCfg<D>::SMEM));
+    DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     KVCfg<D>::SMEM));
+    if (D == 64)
+      DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<D, D == 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       KVCfg<D, D == 64>::SMEM));
     DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_q_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<D>::SMEM));
+    DT_CUDA_RET(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DQCfg<D>::SMEM));
     set = true;
   }
   const int nb = (T + 127) / 128;
   auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv);
-  attn_bwd_kv_tc_kernel<D><<<B * nkv * nb, BW_THREADS, KVCfg<D>::SMEM, st>>>(mq, mdo, ml, md, dq, B, T, nh, nkv, scale);
+  if (ds_buf && D == 64) {
+    // dQ from the stored dS^T tiles: no second pass over the exponentials
+    const long long rows = (long long)B * nh * ((long long)nb * (nb + 1) / 2) * 128;
+    if (rows > 0x7fffffffLL) return -12;
+    CUtensorMap mds;
+    cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {256};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t estr[2] = {1, 1};
+    if (g_enc(&mds, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ds_buf, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return -3;
+    attn_bwd_kv_tc_kernel<D, D == 64><<<B * nkv * nb, BW_THREADS, KVCfg<D, D == 64>::SMEM, st>>>(
+        mq, mdo, ml, md, mds, dq, B, T, nh, nkv, scale);
+    DT_CUDA_RET(cudaGetLastError());
+    static int sms = 0;
+    if (!sms) {
+      int dev = 0;
+      DT_CUDA_RET(cudaGetDevice(&dev));
+      DT_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    const int tiles = B * nh * nb;
+    attn_bwd_dq_tc_kernel<D><<<tiles < sms ? tiles : sms, DQ_THREADS, DQCfg<D>::SMEM, st>>>(mq, mds, dq, B, T, nh, nkv,
+                                                                                          scale);
+    return (int)cudaGetLastError();
+  }
+  attn_bwd_kv_tc_kernel<D, false><<<B * nkv * nb, BW_THREADS, KVCfg<D>::SMEM, st>>>(mq, mdo, ml, md, md, dq, B, T, nh,
+                                                                                   nkv, scale);
   DT_CUDA_RET(cudaGetLastError());
   attn_bwd_q_tc_kernel<D><<<B * nh * nb, BW_THREADS, QCfg<D>::SMEM, st>>>(mq, mdo, lse, delta, dq, B, T, nh, nkv, scale);
   return (int)cudaGetLastError();
@@ -1105,5 +1333,23 @@ DT_API int dt_attn_bwd_tc(const void* qkv, const void* dout, const float* lse, c
   if (nh % nkv) return -10;
   if (D == 64) return bwd_tc_launch<64>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st);
   if (D == 128) return bwd_tc_launch<128>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st);
+  return -11;
+}
+
+// Bytes of the dS^T buffer dt_attn_bwd_tc_ds needs: one 128 x 128 bf16 tile per causal (query block, key block)
+// pair of every (batch, head).
+DT_API long long dt_attn_ds_bytes(int B, int T, int nh) {
+  const long long nb = (T + 127) / 128;
+  return (long long)B * nh * (nb * (nb + 1) / 2) * 128 * 128 * 2;
+}
+
+// tcgen05 backward whose kv kernel also stores dS^T (bf16) into ds_buf (dt_attn_ds_bytes, 16-byte aligned), from
+// which a GEMM-like kernel forms dQ without recomputing S and P.
+// (Head dim 128 keeps the recomputing dQ kernel: its key-block kernel has no room for the staging tiles.)
+DT_API int dt_attn_bwd_tc_ds(const void* qkv, const void* dout, const float* lse, const float* delta, void* dqkv,
+                             void* ds_buf, int B, int T, int nh, int nkv, int D, float scale, cudaStream_t st) {
+  if (nh % nkv || !ds_buf || (reinterpret_cast<uintptr_t>(ds_buf) & 15)) return -10;
+  if (D == 64) return bwd_tc_launch<64>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st, ds_buf);
+  if (D == 128) return bwd_tc_launch<128>(qkv, dout, lse, delta, dqkv, B, T, nh, nkv, scale, st, ds_buf);
   return -11;
 }

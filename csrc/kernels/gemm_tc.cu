@@ -82,6 +82,10 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int TMEM_ALLOC = TMEM_COLS <= 256 ? 256 : 512;  // allocations are powers of two
+  // columns of a tile drained by the first epilogue warp of a lane quadrant (the second takes the rest)
+  static constexpr int COL_SPLIT = BN == 192 ? 128 : BN / 2;
+  static_assert(COL_SPLIT % 64 == 0 && (BN - COL_SPLIT) % 64 == 0, "epilogue boxes are 64 bf16 / 32 fp32 wide");
   static constexpr int BOXES = (MODE == 0 || MODE == 4) ? 1 : 2;  // 4 KB staging boxes per epilogue warp
   static constexpr int EPI_BYTES = EPI_WARPS * BOXES * 4096;
   static constexpr int FIXED = EPI_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
@@ -165,7 +169,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_alloc(tmem_slot, C::TMEM_ALLOC);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -568,7 +572,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
 #pragma unroll 1
-      for (int c0 = hsel * (BN / 2); c0 < (hsel + 1) * (BN / 2); c0 += cols_per_box) {
+      for (int c0 = hsel ? C::COL_SPLIT : 0; c0 < (hsel ? BN : C::COL_SPLIT); c0 += cols_per_box) {
         uint32_t r[2][32];
         tmem_ld_32x32b_x32(t_row + c0, r[0]);
         if (is_bf16) tmem_ld_32x32b_x32(t_row + c0 + 32, r[1]);
@@ -661,7 +665,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_ALLOC);
   if (args.peer && threadIdx.x == 0) {
     // every epilogue warp has waited for its bulk stores (wait_group 0) before the barrier above
     asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -746,13 +750,14 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  if (bn != 128 && bn != 256) {
-    // pick the N tile by wave quantisation; a 128-wide tile costs ~0.65 of a 256-wide one (the A tile
-    // and the per-tile epilogue are the same size), measured on the tiny-preset shapes
+  if (bn != 128 && bn != 192 && bn != 256) {
+    // pick the N tile by wave quantisation: rounds of the persistent grid x the relative cost of one tile
+    // (128 wide ~0.65, 192 wide ~0.82 of a 256-wide one: the A tile and the per-tile fixed work stay)
     long long tm = (M + BM - 1) / BM;
-    long long w256 = (tm * ((N + 255) / 256) + g_num_sms - 1) / g_num_sms;
-    long long w128 = (tm * ((N + 127) / 128) + g_num_sms - 1) / g_num_sms;
-    bn = (N <= 128 || w128 * 65 < w256 * 100) ? 128 : 256;
+    auto rounds = [&](int w) { return (tm * ((N + w - 1) / w) + g_num_sms - 1) / g_num_sms; };
+    const long long c256 = rounds(256) * 100, c128 = rounds(128) * 65;
+    const long long c192 = (N >= 384 && N % 192 == 0 && !Cpeer) ? rounds(192) * 82 : (1LL << 60);
+    bn = N <= 128 ? 128 : (c128 < c256 && c128 < c192 ? 128 : (c192 < c256 ? 192 : 256));
     // accumulate / split-K problems fill the machine through K splits instead: keep the wide tile
     if (epi == EPI_F32_ATOMIC && N > 128 && tm * ((N + 255) / 256) < g_num_sms) bn = 256;
   }
@@ -815,6 +820,11 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
     if (!a_mn && b_mn) return launch<256, 0, 1>(ta, tb, tcm, tcp, a, grid, stream);
     if (a_mn && !b_mn) return launch<256, 1, 0>(ta, tb, tcm, tcp, a, grid, stream);
     return launch<256, 1, 1>(ta, tb, tcm, tcp, a, grid, stream);
+  } else if (bn == 192) {
+    if (!a_mn && !b_mn) return launch<192, 0, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    if (!a_mn && b_mn) return launch<192, 0, 1>(ta, tb, tcm, tcp, a, grid, stream);
+    if (a_mn && !b_mn) return launch<192, 1, 0>(ta, tb, tcm, tcp, a, grid, stream);
+    return launch<192, 1, 1>(ta, tb, tcm, tcp, a, grid, stream);
   } else {
     if (!a_mn && !b_mn) return launch<128, 0, 0>(ta, tb, tcm, tcp, a, grid, stream);
     if (!a_mn && b_mn) return launch<128, 0, 1>(ta, tb, tcm, tcp, a, grid, stream);
@@ -828,7 +838,7 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
 //   a_mn = 0: A(m,k) at A[m*lda + k];  a_mn = 1: A(m,k) at A[k*lda + m]
 //   b_mn = 0: B(n,k) at B[n*ldb + k];  b_mn = 1: B(n,k) at B[k*ldb + n]
 //   epi: 0 bf16 store, 1 fp32 store, 2 fp32 atomic add;  split_k > 1 requires epi == 2.
-//   bn: 128 or 256 (0 = choose).  Returns 0 or a CUDA / argument error code.
+//   bn: 128, 192 or 256 (0 = choose).  Returns 0 or a CUDA / argument error code.
 DT_API int dt_gemm_bf16(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, void* Cp,
                         long long ldc, int M, int N, int K, int epi, float alpha, int split_k, int bn,
                         cudaStream_t stream) {

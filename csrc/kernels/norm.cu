@@ -281,6 +281,55 @@ __global__ void embedding_bwd_kernel(const float* __restrict__ g, const int* __r
     atomicAdd(reinterpret_cast<float4*>(dst + c), *reinterpret_cast<const float4*>(src + c));
 }
 
+// Warp-per-row form of the forward (no block barrier, no shared memory): lane l holds float4 chunks
+// l, l+32, ..., the row sum of squares is a warp reduction; grid-stride over rows. V = H / 128.
+template <int V>
+__global__ void __launch_bounds__(256) add_rmsnorm_fwd_warp_kernel(
+    const float* __restrict__ x, const __nv_bfloat16* __restrict__ br, const float* __restrict__ emb,
+    const int* __restrict__ ids, int T, int S, const float* __restrict__ w, const float* __restrict__ scale,
+    float* __restrict__ out_resid, __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, long long M, int H,
+    float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+  const float s = scale ? *scale : 1.f;
+  for (long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < M; row += nw) {
+    const float* src;
+    if (emb) {
+      const long long b = row / T, t = row - b * T;
+      src = emb + (long long)ids[b * S + t] * H;
+    } else {
+      src = x + row * H;
+    }
+    float4 v[V];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = (lane + 32 * i) * 4;
+      float4 a = *reinterpret_cast<const float4*>(src + c);
+      if (br) {
+        const uint2 bb = *reinterpret_cast<const uint2*>(br + row * H + c);
+        const float2 b0 = unpack_bf16(bb.x), b1 = unpack_bf16(bb.y);
+        a.x += b0.x; a.y += b0.y; a.z += b1.x; a.w += b1.y;
+      }
+      v[i] = a;
+      ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+      if (out_resid) *reinterpret_cast<float4*>(out_resid + row * H + c) = a;
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)H + eps);
+    if (lane == 0 && rstd_out) rstd_out[row] = r;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = (lane + 32 * i) * 4;
+      const float4 ww = *reinterpret_cast<const float4*>(w + c);
+      uint2 o;
+      o.x = pack_bf16(v[i].x * r * ww.x * s, v[i].y * r * ww.y * s);
+      o.y = pack_bf16(v[i].z * r * ww.z * s, v[i].w * r * ww.w * s);
+      *reinterpret_cast<uint2*>(y + row * H + c) = o;
+    }
+  }
+}
+
 int threads_for(int H, int vpt) {
   int n = (H / 4 + vpt - 1) / vpt;
   n = ((n + 31) / 32) * 32;
@@ -298,6 +347,22 @@ int add_rmsnorm_impl(const float* x, const void* br, const void* br2, const floa
   const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(br);
   const __nv_bfloat16* b2 = reinterpret_cast<const __nv_bfloat16*>(br2);
   __nv_bfloat16* yy = reinterpret_cast<__nv_bfloat16*>(y);
+  if (!b2 && !pw.arrivals && H % 128 == 0 && H <= 2048) {
+    long long blocks = ((long long)M + 7) / 8;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    switch (H / 128) {
+#define DT_RMS_FWD_WARP(V)                                                                                          \
+  case V:                                                                                                          \
+    add_rmsnorm_fwd_warp_kernel<V><<<(unsigned)blocks, 256, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, \
+                                                                     rstd, M, H, eps);                             \
+    return (int)cudaGetLastError();
+      DT_RMS_FWD_WARP(1) DT_RMS_FWD_WARP(2) DT_RMS_FWD_WARP(3) DT_RMS_FWD_WARP(4)
+      DT_RMS_FWD_WARP(5) DT_RMS_FWD_WARP(6) DT_RMS_FWD_WARP(7) DT_RMS_FWD_WARP(8)
+      DT_RMS_FWD_WARP(10) DT_RMS_FWD_WARP(12) DT_RMS_FWD_WARP(16)
+#undef DT_RMS_FWD_WARP
+      default: break;
+    }
+  }
   if (H <= 4096) {
     int th = threads_for(H, 1);
     add_rmsnorm_fwd_kernel<1><<<M, th, 0, st>>>(x, b, emb, ids, T, S, w, scale, out_resid, yy, rstd, H, eps, b2, pw);

@@ -90,7 +90,7 @@ def attn_cases(iters):
     out = []
     for (B, T, nh, nkv, d) in [(32, 1023, 12, 4, 64), (8, 2047, 16, 4, 128)]:
         do_f, do_b = want(f"attn_fwd_d{d}"), want(f"attn_bwd_d{d}")
-        if not (do_f or do_b):
+        if not (do_f or do_b or want(f"attn_bwd_ds_d{d}")):
             continue
         W = (nh + 2 * nkv) * d
         qkv = torch.randn(B * T, W, device="cuda").bfloat16()
@@ -105,7 +105,13 @@ def attn_cases(iters):
         ms_f = time_it(lambda: A.attention_fwd(qkv, o, lse, B=B, T=T, nh=nh, nkv=nkv, d=d), iters) if do_f else None
         ms_b = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d),
                        iters) if do_b else None
-        for nm, ms, f in (("fwd", ms_f, fl), ("bwd", ms_b, 2.5 * fl)):
+        ms_bd = None
+        if want(f"attn_bwd_ds_d{d}"):  # dS^T stored once, dQ from it (the engine's path)
+            dsb = torch.empty(A.ds_bytes(B, T, nh), dtype=torch.uint8, device="cuda")
+            ms_bd = time_it(lambda: A.attention_bwd(qkv, o, do, lse, dqkv, dqa, de, B=B, T=T, nh=nh, nkv=nkv, d=d,
+                                                    ds_buf=dsb), iters)
+            del dsb
+        for nm, ms, f in (("fwd", ms_f, fl), ("bwd", ms_b, 2.5 * fl), ("bwd_ds", ms_bd, 2.5 * fl)):
             if ms is None:
                 continue
             tf = f / (ms * 1e-3) / 1e12

@@ -134,6 +134,11 @@ class TrainEngine:
         self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
         self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
         self.delta = torch.empty(batch, nh, Tp, dtype=f32, device=dev)
+        # dS^T tiles of one layer's attention backward (tcgen05 path): dQ is formed from them by a GEMM-like
+        # kernel instead of a second pass over S, P and dP
+        self.ds_buf = None
+        if attn_ops.bwd_kernel_for(d, attn_impl) == "tc" and d in (64, 128) and dev.type == "cuda":
+            self.ds_buf = torch.empty(attn_ops.ds_bytes(batch, self.T, nh), dtype=torch.uint8, device=dev)
         if tp is not None:
             from ..parallel.tensor_parallel import norm_weights
             self.norm_w = norm_weights(L, dev)
@@ -294,7 +299,8 @@ class TrainEngine:
             ops.linear_dgrad(self.g16, wv["o_w"], self.dattn)
             ops.linear_wgrad(self.g16, self.attn[l], gv["o_w"])
             attn_ops.attention_bwd(self.qkv[l], self.attn[l], self.dattn, self.lse[l], self.dqkv, self.dq_acc,
-                                   self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl)
+                                   self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl,
+                                   ds_buf=self.ds_buf)
             ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
             self._col_parallel_dgrad_norm_bwd(
                 self.dqkv, wv["qkv_w"], lambda: ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"]),

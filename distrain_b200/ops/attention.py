@@ -13,6 +13,8 @@ from __future__ import annotations
 
 import torch
 
+import ctypes
+
 from ._lib import lib, check, stream_ptr, ptr, register, c_int, c_void, c_float
 
 _registered = False
@@ -34,6 +36,9 @@ def _reg():
     register("dt_attn_bwd_delta", [c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_void])
     register("dt_attn_bwd_tc", [c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_float,
                                 c_void])
+    register("dt_attn_bwd_tc_ds", [c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int,
+                                   c_float, c_void])
+    register("dt_attn_ds_bytes", [c_int, c_int, c_int], restype=ctypes.c_longlong)
     _registered = True
 
 
@@ -70,9 +75,19 @@ def attention_fwd(qkv, out, lse, *, B, T, nh, nkv, d, impl="dt", stream=None):
           "dt_attn_fwd")
 
 
-def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, *, B, T, nh, nkv, d, impl="dt", stream=None):
+def ds_bytes(B: int, T: int, nh: int) -> int:
+    """Size of the dS^T buffer of the tcgen05 backward: one 128 x 128 bf16 tile per causal (query block,
+    key block) pair of every (batch, head)."""
+    _reg()
+    return int(lib().dt_attn_ds_bytes(B, T, nh))
+
+
+def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, *, B, T, nh, nkv, d, impl="dt", stream=None,
+                  ds_buf=None):
     """dqkv <- gradients of q, k, v (same layout as qkv). ``dq_acc`` ([B*T, nh*d] fp32) and ``delta``
-    ([B, nh, T] fp32) are caller-provided scratch."""
+    ([B, nh, T] fp32) are caller-provided scratch. With ``ds_buf`` (``ds_bytes`` bytes) the tcgen05 path
+    stores dS^T once in the key-block kernel and forms dQ from it with a GEMM-like kernel instead of
+    recomputing S, P and dP in a second attention kernel."""
     scale = d ** -0.5
     if impl == "torch":
         dq, dk, dv = _torch_bwd(qkv, dout, B, T, nh, nkv, d)
@@ -86,6 +101,10 @@ def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, *, B, T, nh, nkv, d,
     if bwd_kernel_for(d, impl) == "tc" and d in (64, 128):
         sp = stream_ptr(stream)
         check(lib().dt_attn_bwd_delta(ptr(out), ptr(dout), ptr(delta), B, T, nh, d, sp), "dt_attn_bwd_delta")
+        if ds_buf is not None:
+            check(lib().dt_attn_bwd_tc_ds(ptr(qkv), ptr(dout), ptr(lse), ptr(delta), ptr(dqkv), ptr(ds_buf), B, T, nh,
+                                          nkv, d, float(scale), sp), "dt_attn_bwd_tc_ds")
+            return
         check(lib().dt_attn_bwd_tc(ptr(qkv), ptr(dout), ptr(lse), ptr(delta), ptr(dqkv), B, T, nh, nkv, d,
                                    float(scale), sp), "dt_attn_bwd_tc")
         return

@@ -60,7 +60,7 @@ def test_attention_fwd_tcgen05(B, T, nh, nkv, d):
 
 @pytest.mark.parametrize("B,T,nh,nkv,d", [(2, 128, 4, 2, 64), (2, 100, 4, 1, 64), (1, 1023, 12, 4, 64),
                                           (2, 300, 16, 4, 128), (1, 257, 8, 8, 128), (3, 64, 4, 2, 64)])
-@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("impl", ["tc", "mma", "tc-ds"])
 def test_attention_bwd_impls(B, T, nh, nkv, d, impl):
     from distrain_b200.ops import attention as A
     from distrain_b200 import ops
@@ -75,7 +75,11 @@ def test_attention_bwd_impls(B, T, nh, nkv, d, impl):
     dqkv = torch.full_like(qkv, 3.0)
     dq_acc = torch.empty(B * T, nh * d, device="cuda")
     delta = torch.zeros(B, nh, A.lse_stride(T), device="cuda")
-    A.attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, B=B, T=T, nh=nh, nkv=nkv, d=d, impl=impl)
+    ds = None
+    if impl == "tc-ds":  # dS^T stored by the key-block kernel, dQ from it
+        impl = "tc"
+        ds = torch.full((A.ds_bytes(B, T, nh),), 77, dtype=torch.uint8, device="cuda")
+    A.attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, delta, B=B, T=T, nh=nh, nkv=nkv, d=d, impl=impl, ds_buf=ds)
     dq, dk, dv = A._torch_bwd(qkv, dout, B, T, nh, nkv, d)
     torch.cuda.synchronize()
     assert ops.device_error()[0] == 0

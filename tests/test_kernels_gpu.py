@@ -26,6 +26,29 @@ def _no_device_error():
     assert code == 0, f"device error {code} at site {site}"
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_192_wide_tiles(a_mn, b_mn, epi):
+    """192-wide output tiles (chosen for N = 768-like widths by wave quantisation) for every operand layout
+    and epilogue, with partial M / K tiles."""
+    ops = _ops()
+    torch.manual_seed(5)
+    M, N, K = 304, 576, 136  # M a multiple of 8: the row stride of an M-contiguous A
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    ref = A.float() @ B.float().t()
+    a_store = A.t().contiguous() if a_mn else A
+    b_store = B.t().contiguous() if b_mn else B
+    if epi == 0:
+        C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    else:
+        C = torch.full((M, N), 0.5 if epi == 2 else 0.0, device="cuda")
+    ops.gemm(a_store, b_store, C, M=M, N=N, K=K, a_mn=bool(a_mn), b_mn=bool(b_mn), epi=epi, bn=192)
+    torch.cuda.synchronize()
+    want = ref + 0.5 if epi == 2 else ref
+    assert _rel(C, want) < (5e-3 if epi == 0 else 1e-5)
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 200, 136), (1000, 768, 768), (256, 1280, 768),
                                    (64, 40, 24)])
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
