@@ -289,6 +289,8 @@ def apply_run_overrides(run, args):
         run.micro_batch = args.batch_size
     if getattr(args, "grad_accum", None) is not None:
         run.grad_accum_steps = max(int(args.grad_accum), 1)
+    if getattr(args, "merge_sms", None) is not None:
+        run.merge_sms = max(int(args.merge_sms), 0)
     if getattr(args, "seq_len", None) is not None:
         run.seq_len = args.seq_len
         run.model.max_seq_len = max(run.model.max_seq_len, args.seq_len)
@@ -768,6 +770,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--shards-fraction", type=float, default=0.2, help="share of the shards each node reads")
     p.add_argument("--batch-size", type=int)
     p.add_argument("--grad-accum", type=int, help="micro-batches per optimizer step (gradient accumulation)")
+    p.add_argument("--merge-sms", type=int,
+                   help="SMs reserved for the merge kernels on each GPU (green-context partition; 0 = priority stream)")
     p.add_argument("--seq-len", type=int)
     p.add_argument("--push-every", type=int)
     p.add_argument("--top-k", type=float)

@@ -325,6 +325,10 @@ class RunConfig(_Json):
     keep_versions: int = 10
     resume: bool = False
     metrics_port: int = -1  # in-box coordinator's Prometheus /metrics (-1 = off, 0 = any free port)
+    # SMs of the green-context partition every GPU's merge kernels run in (the driver rounds up to its
+    # granularity, 8 on this architecture); training keeps the whole GPU and the merge never takes more
+    # than the partition. 0 = a top-priority stream over the whole device
+    merge_sms: int = 16
     # inner lr: constant (default) or loss-based, lr_max * clamp(loss_ema / ln(vocab), 0.1, 1)
     # (reference continuous.rs:586-596, LR_MODE=loss_based)
     loss_based_lr: bool = False

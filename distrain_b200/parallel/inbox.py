@@ -43,6 +43,7 @@ from ..utils.tracing import PhaseTimer, nvtx
 from .compression import DeviceCompressor, DevicePayload, adaptive_push_mode
 from .inbox_ckpt import CheckpointWriter, latest_version, resume_flat
 from .merge import Contribution, DeviceMerger, DistributedMerger
+from .partition import merge_stream
 
 
 log = logging.getLogger("distrain_b200.inbox")
@@ -194,7 +195,7 @@ class InBoxSync:
             self.stage_view().copy_(eng.master)
             self.dm = DistributedMerger(rank, world, self.n, self.device, self.stage_view(), self.stage_ptrs,
                                         self.stage_mc, self.ctl, self.ctl_ptrs,
-                                        stream=torch.cuda.Stream(device=self.device, priority=-100))
+                                        stream=merge_stream(self.device, run.merge_sms))
         multi = world * n_shards > 1
         self.bus = StoreBus(f"dtinbox/s{shard}/" if n_shards > 1 else "dtinbox/") if multi else LocalBus()
         self.shared = self.bus if n_shards == 1 else StoreBus("dtinbox/shared/")
@@ -526,7 +527,7 @@ class InBoxCoordinator:
         # merger has its own such stream)
         self.merger = None
         if sync.dm is None:
-            stream = torch.cuda.Stream(device=sync.device, priority=-100)
+            stream = merge_stream(sync.device, run.merge_sms)
             self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
                                        theta_buffer=sync.stage_view())
         self.version = sync.resumed_version
@@ -821,7 +822,7 @@ class ShardFollower:
         self.sync, self.run, self.world = sync, run, world
         self.bus = StoreBus(sync.bus.prefix)
         self.shared = StoreBus("dtinbox/shared/")
-        stream = torch.cuda.Stream(device=sync.device, priority=-100)
+        stream = merge_stream(sync.device, run.merge_sms)
         self.merger = DeviceMerger(sync.n, sync.device, sync.eng.master, momentum=0.0, stream=stream,
                                    theta_buffer=sync.stage_view())
         self.ckpt = None

@@ -13,8 +13,12 @@ def _layout():
     return ParamLayout(cfg)
 
 
-@pytest.mark.parametrize("k_fraction,adaptive", [(0.1, True), (0.01, True), (0.99, True), (0.1, False)])
-def test_device_compress_matches_reference(k_fraction, adaptive):
+@pytest.mark.parametrize("k_fraction,adaptive,flat", [(0.1, True, False), (0.01, True, False), (0.99, True, False),
+                                                      (0.1, False, False), (0.1, True, True), (0.3, False, True)])
+def test_device_compress_matches_reference(k_fraction, adaptive, flat):
+    """flat: the largest tensor's deltas all have one magnitude, so a whole 32768-element chunk falls in the
+    boundary bin - more than a chunk's candidate slot holds - and the selection takes the full-buffer
+    passes; ties are broken by ascending index as in the reference."""
     from distrain_b200.config import CompressionConfig
     from distrain_b200.parallel.compression import DeviceCompressor, sparsify_topk, quantize_int8
     L = _layout()
@@ -32,6 +36,11 @@ def test_device_compress_matches_reference(k_fraction, adaptive):
         delta[e.offset:e.offset + e.numel] *= (1 + i % 5)
     delta[L.entries[3].offset:L.entries[3].offset + 8] = 0.5
     ef0 = torch.randn(L.total, device=dev) * 1e-4 * mask
+    if flat:
+        big = max(L.entries, key=lambda e: e.numel)
+        sl = slice(big.offset, big.offset + big.numel)
+        delta[sl] = torch.where(torch.rand(big.numel, device=dev) < 0.5, -2e-3, 2e-3)
+        ef0[sl] = 0.0
     comp.snap.copy_(snap)
     comp.ef.copy_(ef0)
     master = snap - delta
@@ -173,11 +182,14 @@ def test_device_merge_matches_reference(momentum, in_place):
         assert float(merger.acc.abs().max()) == 0.0
 
 
-def test_inbox_single_gpu_protocol():
-    """One node + coordinator on one GPU: pushes, merges, version swaps, loss decreases."""
+@pytest.mark.parametrize("merge_sms", [0, 16])
+def test_inbox_single_gpu_protocol(merge_sms):
+    """One node + coordinator on one GPU: pushes, merges, version swaps, loss decreases; the merge on a
+    priority stream over the whole GPU, or in a 16-SM green-context partition."""
     from distrain_b200.config import bench_config
     from distrain_b200.parallel.node import InBoxNode
     run = bench_config("micro")
+    run.merge_sms = merge_sms
     run.model.vocab_size = 512
     run.push_every = 6
     run.optim.lr = 3e-3

@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, port, out_dir):
+def _rank(rank, port, out_dir, merge_sms=0):
     import datetime
     import torch.distributed as dist
     from distrain_b200.config import CompressionConfig, preset
@@ -30,6 +30,7 @@ def _rank(rank, port, out_dir):
     from distrain_b200.parallel.compression import DeviceCompressor, DevicePayload
     from distrain_b200.parallel.inbox import _symm_alloc
     from distrain_b200.parallel.merge import Contribution, DeviceMerger, DistributedMerger
+    from distrain_b200.parallel.partition import merge_stream
     from distrain_b200 import ops
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -62,7 +63,8 @@ def _rank(rank, port, out_dir):
     theta = stage_buf[:n * 4].view(torch.float32)
     theta.copy_(theta0)
     ctl, ctl_ptrs, _, _h3 = _symm_alloc(DistributedMerger.CTL_BYTES, dev, W)
-    dm = DistributedMerger(rank, W, n, dev, theta, stage_ptrs, stage_mc, ctl, ctl_ptrs)
+    dm = DistributedMerger(rank, W, n, dev, theta, stage_ptrs, stage_mc, ctl, ctl_ptrs,
+                           stream=merge_stream(dev, merge_sms))
     base = pay_buf.data_ptr()
     weights = [1000.0, 800.0 * 0.9]
     contribs = []
@@ -99,12 +101,14 @@ def _rank(rank, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_distributed_merge_two_gpus(tmp_path):
+@pytest.mark.parametrize("merge_sms", [0, 16])
+def test_distributed_merge_two_gpus(tmp_path, merge_sms):
+    """merge_sms 16: every node's slice merge and broadcast run in a 16-SM green-context partition."""
     import torch.multiprocessing as mp
     from distrain_b200.config import preset
     from distrain_b200.models.params import ParamLayout
     from distrain_b200.parallel.merge import merge_reference
-    mp.spawn(_rank, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank, args=(_free_port(), str(tmp_path), merge_sms), nprocs=2, join=True)
     res = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(2)]
     assert res[0]["err"] == 0 and res[1]["err"] == 0
     L = ParamLayout(preset("micro"))
