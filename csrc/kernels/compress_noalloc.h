@@ -32,7 +32,8 @@
 //    written, stay in error feedback, and dt_error_word is set to 5 (out of bounds).
 //  * Returns 0, a CUDA error code, or -10 (invalid argument: nseg, nchunks or n_elems <= 0, k_fraction
 //    outside (0, 1]), -20 (workspace exceeds the scratch), -21 (device ordinal >= 64), -22 (n_elems >=
-//    2^31), -23 (capacity below the minimum). Nothing runs when an error code is returned.
+//    2^31), -23 (capacity below the minimum), -24 (quant_block > 0 and not a multiple of 32 up to 512).
+//    Nothing runs when an error code is returned.
 #pragma once
 #include <cuda_runtime.h>
 

@@ -203,6 +203,18 @@ def fused_cases(iters):
         rec("linear_fwd + rope_fwd (separate)",
             time_it(lambda: (ops.linear_fwd(x, wq, q), ops.rope_fwd(q, b, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d)),
                     iters), fq)
+    if want("rope_bwd"):
+        cfg = preset("tiny")
+        nh, nkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim()
+        W = (nh + 2 * nkv) * d
+        cos, sin = rope_tables(cfg, T)
+        cos, sin = cos.cuda().contiguous(), sin.cuda().contiguous()
+        dq = (torch.randn(M, W, device="cuda") * 0.1).bfloat16()
+        db = torch.zeros(W, device="cuda")
+        ms = time_it(lambda: ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d), iters)
+        gbs = 2 * M * W * 2 / ms / 1e6
+        out.append({"kernel": "rope_bwd", "case": f"M{M} W{W} (inverse rotation + bias gradient)", "ms": round(ms, 4),
+                    "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)})
     if want("adamw"):
         from distrain_b200.models.params import ParamLayout
         L = ParamLayout(preset("tiny"))

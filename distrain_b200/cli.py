@@ -435,31 +435,33 @@ def cmd_baseline(args):
 
 def cmd_generate(args):
     """Greedy / temperature sampling by full re-forward (the reference has no KV cache, main.rs:1416-1548)."""
-    import torch
-    from .models import oracle
-    from .utils.checkpoint import load_safetensors
-    sd = load_safetensors(args.checkpoint)
-    cfg = _infer_model_config(sd)
-    if args.rope_theta:
-        cfg.rope_theta = args.rope_theta
-    cfg.max_seq_len = max(cfg.max_seq_len, args.max_tokens + 64)
+    from .serve import load_model, sample
+    sd, cfg = load_model(args.checkpoint, getattr(args, "device", None) or "cpu", args.rope_theta,
+                         min_len=args.max_tokens + 64)
     ids = [int(x) for x in args.prompt_ids.split(",")] if args.prompt_ids else [1]
     tok = None
     if args.tokenizer:
         from tokenizers import Tokenizer
         tok = Tokenizer.from_file(args.tokenizer)
         ids = tok.encode(args.prompt).ids
-    g = torch.Generator().manual_seed(args.seed)
-    with torch.no_grad():
-        for _ in range(args.max_tokens):
-            x = torch.tensor([ids[-cfg.max_seq_len:]])
-            z = oracle.logits_fn(sd, cfg, x)[0, -1]
-            if args.temperature <= 0:
-                nxt = int(z.argmax())
-            else:
-                nxt = int(torch.multinomial(torch.softmax(z / args.temperature, -1), 1, generator=g))
-            ids.append(nxt)
+    new, _ = sample(sd, cfg, ids, args.max_tokens, args.temperature, args.seed)
+    ids = ids + new
     print(json.dumps({"ids": ids, "text": tok.decode(ids) if tok else None}))
+
+
+def cmd_serve(args):
+    """OpenAI-style completion server for one checkpoint (the reference's scripts/serve.py:16,32-37)."""
+    import time as _time
+    from .serve import CompletionServer
+    srv = CompletionServer(args.checkpoint, args.device or "cpu", args.tokenizer, args.rope_theta,
+                           max_tokens_cap=args.max_tokens_cap)
+    port = srv.start(args.host, args.port)
+    print(json.dumps({"serving": args.checkpoint, "port": port, "model": srv.model}), flush=True)
+    try:
+        while True:
+            _time.sleep(3600)
+    except KeyboardInterrupt:
+        srv.stop()
 
 
 def cmd_benchmark(args):
@@ -714,7 +716,18 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--temperature", type=float, default=0.0)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--rope-theta", type=float)
+    p.add_argument("--device", help="torch device for the forward (default cpu)")
     p.set_defaults(fn=cmd_generate)
+
+    p = sp.add_parser("serve", help="OpenAI-style completion server for a checkpoint (/v1/completions)")
+    p.add_argument("checkpoint")
+    p.add_argument("--tokenizer", help="tokenizer JSON (text prompts); token-id prompts work without one")
+    p.add_argument("--host", default="0.0.0.0")
+    p.add_argument("--port", type=int, default=8000)
+    p.add_argument("--device", help="torch device for the forward (default cpu)")
+    p.add_argument("--max-tokens-cap", type=int, default=1024)
+    p.add_argument("--rope-theta", type=float)
+    p.set_defaults(fn=cmd_serve)
 
     p = sp.add_parser("benchmark", help="step time / throughput of this device")
     p.add_argument("--preset", default="tiny")

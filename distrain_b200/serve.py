@@ -1,0 +1,159 @@
+"""Text generation from a checkpoint: the sampler behind ``cli.py generate`` and an OpenAI-style
+completion server (``cli.py serve``) on the native HTTP server.
+
+The reference's node samples by re-running the full forward for every new token (no KV cache,
+``node/cli/src/main.rs:1416-1548``); its serving script (``scripts/serve.py:16,32-37``) exposes an
+OpenAI-style API but imports a package that is not in its repository. Here both use the model's
+plain PyTorch formulation (``models/oracle.py``) on the chosen device.
+
+Routes: ``POST /v1/completions`` with {"prompt": text or [token ids], "max_tokens", "temperature",
+"seed", "stop_token"} -> {"id", "object": "text_completion", "created", "model", "choices": [{"text",
+"token_ids", "index", "finish_reason"}], "usage": {"prompt_tokens", "completion_tokens",
+"total_tokens"}}; ``GET /v1/models``; ``GET /health``. Text prompts need a tokenizer file.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import threading
+import time
+import uuid
+from typing import List, Optional, Tuple
+
+import torch
+
+
+def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, seed: int = 0,
+           stop_token: Optional[int] = None) -> Tuple[List[int], str]:
+    """Appends up to ``max_tokens`` tokens to ``ids`` (greedy at temperature <= 0, else softmax sampling
+    from a generator seeded with ``seed``); returns the new tokens and the finish reason ("length" or
+    "stop")."""
+    from .models import oracle
+    dev = next(iter(sd.values())).device
+    g = torch.Generator(device="cpu").manual_seed(int(seed))
+    seq = list(ids) if ids else [1]
+    out: List[int] = []
+    with torch.no_grad():
+        for _ in range(int(max_tokens)):
+            x = torch.tensor([seq[-cfg.max_seq_len:]], device=dev)
+            z = oracle.logits_fn(sd, cfg, x)[0, -1].float().cpu()
+            if temperature <= 0:
+                nxt = int(z.argmax())
+            else:
+                nxt = int(torch.multinomial(torch.softmax(z / temperature, -1), 1, generator=g))
+            seq.append(nxt)
+            out.append(nxt)
+            if stop_token is not None and nxt == stop_token:
+                return out, "stop"
+    return out, "length"
+
+
+def load_model(checkpoint: str, device: str = "cpu", rope_theta: Optional[float] = None, min_len: int = 0):
+    """Checkpoint (safetensors) -> (weights on ``device``, ModelConfig inferred from the shapes)."""
+    from .cli import _infer_model_config
+    from .utils.checkpoint import load_safetensors
+    sd = load_safetensors(checkpoint)
+    cfg = _infer_model_config(sd)
+    if rope_theta:
+        cfg.rope_theta = rope_theta
+    cfg.max_seq_len = max(cfg.max_seq_len, min_len)
+    sd = {k: v.to(device) for k, v in sd.items()}
+    return sd, cfg
+
+
+class CompletionServer:
+    """OpenAI-style completions for one checkpoint; requests are served one at a time (the model's
+    forward is not re-entrant on one device)."""
+
+    def __init__(self, checkpoint: str, device: str = "cpu", tokenizer: Optional[str] = None,
+                 rope_theta: Optional[float] = None, model_name: Optional[str] = None, max_tokens_cap: int = 1024):
+        self.sd, self.cfg = load_model(checkpoint, device, rope_theta, min_len=max_tokens_cap + 64)
+        self.tok = None
+        if tokenizer:
+            from tokenizers import Tokenizer
+            self.tok = Tokenizer.from_file(tokenizer)
+        self.model = model_name or checkpoint.rsplit("/", 1)[-1]
+        self.cap = max_tokens_cap
+        self._lock = threading.Lock()
+        self.handle = None
+        self.port = None
+
+    # ── request handling (pure: testable without sockets) ──
+    def complete(self, req: dict) -> Tuple[int, dict]:
+        prompt = req.get("prompt", "")
+        if isinstance(prompt, list) and len(prompt) == 1 and isinstance(prompt[0], (str, list)):
+            prompt = prompt[0]
+        if isinstance(prompt, list):
+            ids = [int(t) for t in prompt]
+        elif self.tok is not None:
+            ids = self.tok.encode(str(prompt)).ids
+        else:
+            return 400, {"error": {"message": "text prompts need a tokenizer (start with --tokenizer) or a list "
+                                              "of token ids", "type": "invalid_request_error"}}
+        n = int(req.get("max_tokens", 16))
+        if n < 0 or n > self.cap:
+            return 400, {"error": {"message": f"max_tokens must be in [0, {self.cap}]",
+                                   "type": "invalid_request_error"}}
+        bad = [t for t in ids if t < 0 or t >= self.cfg.vocab_size]
+        if bad:
+            return 400, {"error": {"message": f"token id {bad[0]} outside the vocabulary",
+                                   "type": "invalid_request_error"}}
+        stop = req.get("stop_token")
+        with self._lock:
+            new, reason = sample(self.sd, self.cfg, ids, n, float(req.get("temperature", 0.0)),
+                                 int(req.get("seed", 0)), int(stop) if stop is not None else None)
+        text = self.tok.decode(new) if self.tok is not None else None
+        return 200, {"id": f"cmpl-{uuid.uuid4().hex[:24]}", "object": "text_completion", "created": int(time.time()),
+                     "model": self.model,
+                     "choices": [{"text": text, "token_ids": new, "index": 0, "finish_reason": reason}],
+                     "usage": {"prompt_tokens": len(ids), "completion_tokens": len(new),
+                               "total_tokens": len(ids) + len(new)}}
+
+    def handle_request(self, method: str, path: str, body: bytes) -> Tuple[int, dict]:
+        route = path.split("?", 1)[0]
+        if method == "GET" and route == "/health":
+            return 200, {"status": "ok"}
+        if method == "GET" and route == "/v1/models":
+            return 200, {"object": "list", "data": [{"id": self.model, "object": "model", "owned_by": "distrain"}]}
+        if method == "POST" and route == "/v1/completions":
+            try:
+                req = json.loads(body or b"{}")
+            except ValueError:
+                return 400, {"error": {"message": "body is not JSON", "type": "invalid_request_error"}}
+            return self.complete(req)
+        return 404, {"error": {"message": f"no route {method} {route}", "type": "not_found"}}
+
+    # ── native HTTP server ──
+    def start(self, host: str = "0.0.0.0", port: int = 8000, threads: int = 4) -> int:
+        from .utils import native
+        handler_t = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_void_p,
+                                     ctypes.c_longlong, ctypes.c_void_p)
+        L = native.rt()
+        native.register("dtr_http_start", [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, handler_t,
+                                           ctypes.c_void_p], ctypes.c_void_p)
+        native.register("dtr_http_port", [ctypes.c_void_p], ctypes.c_int)
+        native.register("dtr_http_stop", [ctypes.c_void_p], None)
+        native.register("dtr_http_respond", [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_void_p,
+                                             ctypes.c_longlong], None)
+
+        def on_request(ctx, method, path, body, blen, resp):
+            try:
+                data = ctypes.string_at(body, blen) if blen else b""
+                status, obj = self.handle_request(method.decode(), path.decode(), data)
+            except Exception as e:  # the server thread must answer whatever happens
+                status, obj = 500, {"error": {"message": str(e), "type": "server_error"}}
+            out = json.dumps(obj).encode()
+            L.dtr_http_respond(resp, status, b"application/json", out, len(out))
+
+        self._cb = handler_t(on_request)
+        self.handle = L.dtr_http_start(host.encode(), port, threads, 1 << 20, self._cb, None)
+        if not self.handle:
+            raise RuntimeError(f"serve: cannot bind {host}:{port}")
+        self.port = L.dtr_http_port(self.handle)
+        return self.port
+
+    def stop(self):
+        if self.handle:
+            from .utils import native
+            native.rt().dtr_http_stop(self.handle)
+            self.handle = None

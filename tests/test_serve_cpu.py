@@ -1,0 +1,65 @@
+"""OpenAI-style completion server on CPU: request validation, greedy output equal to the sampler (and to
+``cli.py generate``), seeded sampling, and one round trip over the native HTTP server."""
+import json
+import urllib.request
+
+import pytest
+import torch
+
+
+@pytest.fixture(scope="module")
+def ckpt(tmp_path_factory):
+    from distrain_b200.config import preset
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.utils.checkpoint import save_safetensors
+    cfg = preset("micro")
+    L = ParamLayout(cfg)
+    flat = init_flat(L, seed=3)
+    path = str(tmp_path_factory.mktemp("ck") / "model.safetensors")
+    save_safetensors(L.to_state_dict(flat), path)
+    return path
+
+
+def test_completions_validate_and_match_the_sampler(ckpt):
+    from distrain_b200.serve import CompletionServer, sample
+    srv = CompletionServer(ckpt, "cpu", max_tokens_cap=64)
+    st, out = srv.handle_request("POST", "/v1/completions", json.dumps({"prompt": [1, 2, 3], "max_tokens": 6}).encode())
+    assert st == 200, out
+    ch = out["choices"][0]
+    assert out["object"] == "text_completion" and ch["finish_reason"] == "length" and len(ch["token_ids"]) == 6
+    assert out["usage"] == {"prompt_tokens": 3, "completion_tokens": 6, "total_tokens": 9}
+    ref, _ = sample(srv.sd, srv.cfg, [1, 2, 3], 6)
+    assert ch["token_ids"] == ref
+    # seeded sampling is reproducible; a stop token ends the completion early
+    body = {"prompt": [5, 6], "max_tokens": 8, "temperature": 1.0, "seed": 11}
+    a = srv.handle_request("POST", "/v1/completions", json.dumps(body).encode())[1]["choices"][0]["token_ids"]
+    b = srv.handle_request("POST", "/v1/completions", json.dumps(body).encode())[1]["choices"][0]["token_ids"]
+    assert a == b
+    body["stop_token"] = a[2]
+    c = srv.handle_request("POST", "/v1/completions", json.dumps(body).encode())[1]["choices"][0]
+    assert c["finish_reason"] == "stop" and c["token_ids"] == a[:a.index(a[2]) + 1]
+    # invalid requests: text without a tokenizer, too many tokens, ids outside the vocabulary, bad JSON
+    assert srv.handle_request("POST", "/v1/completions", b'{"prompt": "hi"}')[0] == 400
+    assert srv.handle_request("POST", "/v1/completions", b'{"prompt": [1], "max_tokens": 65}')[0] == 400
+    assert srv.handle_request("POST", "/v1/completions", json.dumps({"prompt": [srv.cfg.vocab_size]}).encode())[0] == 400
+    assert srv.handle_request("POST", "/v1/completions", b"{not json")[0] == 400
+    assert srv.handle_request("GET", "/nope", b"")[0] == 404
+    models = srv.handle_request("GET", "/v1/models", b"")[1]
+    assert models["data"][0]["id"] == srv.model
+
+
+def test_server_round_trip(ckpt):
+    from distrain_b200.serve import CompletionServer
+    srv = CompletionServer(ckpt, "cpu", max_tokens_cap=16)
+    port = srv.start("127.0.0.1", 0, threads=2)
+    try:
+        req = urllib.request.Request(f"http://127.0.0.1:{port}/v1/completions", method="POST",
+                                     data=json.dumps({"prompt": [[1, 2]], "max_tokens": 3}).encode(),
+                                     headers={"Content-Type": "application/json"})
+        with urllib.request.urlopen(req, timeout=60) as r:
+            out = json.loads(r.read())
+        assert len(out["choices"][0]["token_ids"]) == 3
+        with urllib.request.urlopen(f"http://127.0.0.1:{port}/health", timeout=10) as r:
+            assert json.loads(r.read())["status"] == "ok"
+    finally:
+        srv.stop()
