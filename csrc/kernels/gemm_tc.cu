@@ -12,6 +12,11 @@
 //   (bf16 / fp32) or a TMA reduce-add (fp32 accumulation, used for split-K and gradient accumulation), so
 //   global writes are full-line and asynchronous.
 // * Tiles are visited by a persistent grid (one CTA per SM) in grouped order for L2 reuse.
+// * The plain GEMM's 256-wide tiles run on CTA pairs (clusters of two SMs, tcgen05 cta_group::2): a pair computes a
+//   256 x 256 tile with M = 256 MMAs issued by its even CTA; each CTA stages its own 128 rows of A and
+//   128 of the 256 B rows, so per output it reads 3/4 of the operand bytes of a single-CTA 128 x 256
+//   tile. Operand loads of both CTAs complete on the even CTA's barriers; the MMA commits arrive on both
+//   CTAs' barriers; both CTAs' epilogues hand TMEM back to the even CTA. No load uses multicast.
 // * Fused SwiGLU (reference model.rs:292-296, h = silu(x Wg^T) * (x Wu^T)):
 //     forward (MODE 1): one 256-wide tile holds 128 gate columns and the 128 matching up columns (the B
 //       stage is filled from the gate rows and the up rows of the [2F, K] weight by two TMA loads); the
@@ -33,6 +38,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <cstdlib>
 
 namespace {
 
@@ -76,10 +82,10 @@ struct GemmArgs {
   unsigned* done_ctas;      // local scratch counter, returns to 0 after every launch
 };
 
-template <int BN, int MODE = 0>
+template <int BN, int MODE = 0, bool PAIR = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a CTA of a pair holds half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int TMEM_ALLOC = TMEM_COLS <= 256 ? 256 : 512;  // allocations are powers of two
@@ -115,14 +121,18 @@ __device__ __forceinline__ void box_put(uint8_t* box, int lane, int ch, uint4 v)
   *reinterpret_cast<uint4*>(box + lane * 128 + ((ch ^ (lane & 7)) * 16)) = v;
 }
 
-template <int BN, int A_MN, int B_MN, int MODE>
+// PAIR: the kernel runs as clusters of two CTAs on two SMs, each pair computing 256 x BN tiles with
+// cta_group::2 MMAs (M = 256): each CTA loads its 128 rows of A and BN/2 rows (columns of the product)
+// of B, so a CTA reads (128 + BN/2) x K operand elements per 128 x BN outputs instead of (128 + BN) x K.
+template <int BN, int A_MN, int B_MN, int MODE, bool PAIR = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmCp,
                const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC2,
                const __grid_constant__ CUtensorMap tmC3, GemmArgs args) {
   static_assert(MODE != 1 || (BN == 256 && !A_MN && !B_MN), "fused SwiGLU forward: 128 gate + 128 up columns");
-  using C = Cfg<BN, MODE>;
+  static_assert(!PAIR || ((BN == 128 || BN == 256) && MODE != 2), "CTA pairs: 128- or 256-wide tiles, not MODE 2");
+  using C = Cfg<BN, MODE, PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -149,7 +159,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 32 * EPI_WARPS);
+      mbar_init(&tempty[a], (PAIR ? 2 : 1) * 32 * EPI_WARPS);
     }
     mbar_init(drain, 1);
     for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&gbar[w], 1);
@@ -169,15 +179,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_ALLOC);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_ALLOC);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_ALLOC);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair's CTAs signal each other's barriers: both must have initialised theirs first
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int crank = PAIR ? (int)cluster_ctarank() : 0;
+  // a pair's MMAs write both CTAs' TMEM at the even CTA's address: both allocations must agree, else
+  // nothing runs and the error word is set
+  bool pair_ok = true;
+  if constexpr (PAIR) {
+    pair_ok = ld_shared_cluster_u32(mapa_shared(smem_u32(tmem_slot), crank ^ 1)) == tmem_base;
+    if (!pair_ok && threadIdx.x == 0) dt_set_error(DT_ERR_BAD_ARG, 150);
+  }
 
-  const int total_units = args.tiles_m * args.tiles_n * args.split_k;
+  const int total_units = pair_ok ? args.tiles_m * args.tiles_n * args.split_k : 0;
+  // persistent walk: a CTA (or a pair of CTAs) takes units first, first + step, ...
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int TM = PAIR ? 2 * BM : BM;  // rows of a tile (a pair's tile spans both CTAs)
+  const int mrow = crank * BM;        // this CTA's rows within the tile
+  // barriers of the even CTA, where a pair's operand loads complete and its epilogues hand TMEM back
+  auto lead = [&](uint64_t* b) -> uint32_t { return PAIR ? mapa_shared(smem_u32(b), 0) : smem_u32(b); };
+  // an epilogue thread has read its TMEM columns of accumulator `acc`
+  auto arrive_tempty = [&](int acc) {
+    if constexpr (PAIR) mbar_arrive_remote(lead(&tempty[acc]));
+    else mbar_arrive(&tempty[acc]);
+  };
 
   if (warp == 0) {
     // ───────────── TMA producer ─────────────
@@ -185,20 +222,44 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+      for (int unit = unit0; unit < total_units && ok; unit += ustep) {
         int s = unit % args.split_k, tile = unit / args.split_k;
         int mb, nb;
         tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
-        int m0 = mb * BM, n0 = nb * (MODE == 1 ? BN / 2 : BN);
+        int m0 = mb * TM + mrow, n0 = nb * (MODE == 1 ? BN / 2 : BN);
         int kb0 = s * args.kb_per_split, kb1 = min(kb0 + args.kb_per_split, args.num_kb);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, DT_ERR_TIMEOUT_EMPTY, 100, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
           uint8_t* b_dst = sB + stage * C::B_BYTES;
+          if constexpr (PAIR) {
+            // both CTAs' loads complete on the even CTA's barrier, which expects the pair's bytes
+            const uint32_t fb = lead(&full[stage]);
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            if (A_MN) {
+#pragma unroll
+              for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * (64 * BK * 2), &tmA, fb, m0 + 64 * j, kb * BK);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, m0);
+            }
+            if (MODE == 1) {
+              // the even CTA holds the tile's 128 gate rows of B, the odd one the matching up rows
+              tma_load_2d_pair(b_dst, crank ? &tmB2 : &tmB, fb, kb * BK, n0);
+            } else if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_2d_pair(b_dst + j * (64 * BK * 2), &tmB, fb, n0 + crank * (BN / 2) + 64 * j, kb * BK);
+            } else {
+              tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, n0 + crank * (BN / 2));
+            }
+            ++issued;
+            if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * (64 * BK * 2), &tmA, &full[stage], m0 + 64 * j, kb * BK);
@@ -220,8 +281,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      if (*abort_flag) {
-        // Drain: wait (bounded) for every issued-but-unconsumed stage so no TMA write lands after exit.
+      if (*abort_flag && crank == 0) {
+        // Drain: wait (bounded) for every issued-but-unconsumed stage so no TMA write lands after exit (a
+        // pair's loads all complete on the even CTA's barriers; the final cluster barrier holds the odd
+        // CTA until then).
         for (int i = *consumed; i < issued; ++i) {
           uint64_t t0 = dt_globaltimer();
           while (!mbar_try_wait(&full[i % C::STAGES], (i / C::STAGES) & 1)) {
@@ -231,14 +294,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   } else if (warp == 1) {
-    // ───────────── MMA issuer ─────────────
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    // ───────────── MMA issuer (the even CTA of a pair issues for both) ─────────────
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(PAIR ? 2 * BM : BM, BN, A_MN, B_MN);
       uint32_t stage = 0, phase = 0;
       int local = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x, ++local) {
+      // commit to a barrier of this CTA and, for a pair, to the same barrier of the odd CTA
+      auto commit_both = [&](uint64_t* b) {
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(b));
+          umma_commit_pair(mapa_shared(smem_u32(b), 1));
+        } else {
+          umma_commit(b);
+        }
+      };
+      for (int unit = unit0; unit < total_units && ok; unit += ustep, ++local) {
         int s = unit % args.split_k;
         int kb0 = s * args.kb_per_split, kb1 = min(kb0 + args.kb_per_split, args.num_kb);
         int acc = local & 1;
@@ -258,18 +330,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                : umma_smem_desc_sw128(a_addr + k * 32, 16, 1024);
             uint64_t bd = B_MN ? umma_smem_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
                                : umma_smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           issued_any = true;
-          umma_commit(&empty[stage]);
+          commit_both(&empty[stage]);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        commit_both(&tfull[acc]);
       }
       if (!ok && issued_any) {
         // Make sure every issued MMA has retired before TMEM is released.
-        umma_commit(drain);
+        if constexpr (PAIR) umma_commit_pair(smem_u32(drain));
+        else umma_commit(drain);
         uint64_t t0 = dt_globaltimer();
         while (!mbar_try_wait(drain, 0)) {
           if (dt_globaltimer() - t0 > 20000000ull) break;
@@ -297,17 +371,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tile_coords(u / args.split_k, args.tiles_m, args.tiles_n, mb, nb);
         if (lane == 0) {
           mbar_arrive_expect_tx(gb, 8192);
-          tma_load_2d(stage, &tmB2, gb, nb * BN + hsel * 64, mb * BM + quad * 32);
-          tma_load_2d(stage + 4096, &tmC3, gb, nb * BN + hsel * 64, mb * BM + quad * 32);
+          tma_load_2d(stage, &tmB2, gb, nb * BN + hsel * 64, mb * TM + mrow + quad * 32);
+          tma_load_2d(stage + 4096, &tmC3, gb, nb * BN + hsel * 64, mb * TM + mrow + quad * 32);
         }
         __syncwarp();
       };
       bool inflight = false;
-      if (blockIdx.x < total_units) {
-        prefetch(blockIdx.x);
+      if (unit0 < total_units) {
+        prefetch(unit0);
         inflight = true;
       }
-      for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
+      for (int unit = unit0; unit < total_units; unit += ustep, ++local) {
         int mb, nb;
         tile_coords(unit / args.split_k, args.tiles_m, args.tiles_n, mb, nb);
         const int acc = local & 1;
@@ -315,7 +389,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait_bounded(gb, local & 1, DT_ERR_TIMEOUT_FULL, 301, abort_flag)) break;
         inflight = false;
         tc_fence_after();
-        const int row0 = mb * BM + quad * 32;
+        const int row0 = mb * TM + mrow + quad * 32;
         const int gcol = nb * BN + hsel * 64;
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + hsel * 64;
 #pragma unroll
@@ -346,7 +420,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);  // this warp's TMEM columns are read
+        arrive_tempty(acc);  // this warp's TMEM columns are read
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -358,8 +432,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           bulk_wait_read0();  // the boxes take the next tile's gate / up values
         }
         __syncwarp();
-        if (unit + (int)gridDim.x < total_units) {
-          prefetch(unit + gridDim.x);
+        if (unit + ustep < total_units) {
+          prefetch(unit + ustep);
           inflight = true;
         }
       }
@@ -370,7 +444,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else {
     const bool is_bf16 = args.epi == EPI_BF16;
     const int cols_per_box = is_bf16 ? 64 : 32;  // 32 rows x 128 B (bf16) / 32 rows x 128 B (fp32)
-    for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++local) {
+    for (int unit = unit0; unit < total_units; unit += ustep, ++local) {
       int tile = unit / args.split_k;
       int mb, nb;
       tile_coords(tile, args.tiles_m, args.tiles_n, mb, nb);
@@ -378,7 +452,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&tfull[acc], acc_phase, DT_ERR_TIMEOUT_TMEM, 300, abort_flag)) break;
       tc_fence_after();
-      const int row0 = mb * BM + quad * 32;
+      const int row0 = mb * TM + mrow + quad * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
       if constexpr (MODE == 1) {
         // TMEM columns [0, 128): gate, [128, 256): up, for output columns nb*128 + [0, 128); this warp
@@ -425,7 +499,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);  // TMEM read; the stores below overlap the next tile's products
+        arrive_tempty(acc);  // TMEM read; the stores below overlap the next tile's products
         if (live) {
           fence_proxy_async_smem();
           __syncwarp();
@@ -555,7 +629,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           pending = true;
         }
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        arrive_tempty(acc);
         continue;
       }
       if constexpr (MODE == 0 || MODE == 4) {
@@ -647,7 +721,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      arrive_tempty(acc);
       if constexpr (MODE == 4) {
         const int row = row0 + lane;
         if (row < args.M) {
@@ -664,8 +738,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   tc_fence_before();
   __syncthreads();
+  // a pair: neither CTA releases TMEM or exits while the other may still signal its barriers or the
+  // even CTA's MMAs may still write the odd CTA's TMEM
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_ALLOC);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_ALLOC);
+    else tmem_dealloc(tmem_base, C::TMEM_ALLOC);
+  }
   if (args.peer && threadIdx.x == 0) {
     // every epilogue warp has waited for its bulk stores (wait_group 0) before the barrier above
     asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -711,21 +791,56 @@ int make_map(CUtensorMap* m, const void* ptr, long long inner, long long outer, 
 
 int g_num_sms = 0;
 
-template <int BN, int A_MN, int B_MN, int MODE = 0>
+template <int BN, int A_MN, int B_MN, int MODE = 0, bool PAIR = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tcp,
            const GemmArgs& a, int grid, cudaStream_t st, const CUtensorMap* tb2 = nullptr,
            const CUtensorMap* tc2 = nullptr, const CUtensorMap* tc3 = nullptr) {
-  using C = Cfg<BN, MODE>;
+  using C = Cfg<BN, MODE, PAIR>;
   static_assert(C::SMEM_BYTES <= 232448, "shared memory per CTA");
-  auto k = gemm_tc_kernel<BN, A_MN, B_MN, MODE>;
+  auto k = gemm_tc_kernel<BN, A_MN, B_MN, MODE, PAIR>;
   static bool attr_set = false;
   if (!attr_set) {
     DT_CUDA_RET(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, tcp, tb2 ? *tb2 : tb, tc2 ? *tc2 : tc, tc3 ? *tc3 : tc, a);
-  return (int)cudaGetLastError();
+  if constexpr (PAIR) {
+    // clusters of two CTAs (grid even); the pair's SMs share one tile
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    DT_CUDA_RET(cudaLaunchKernelEx(&cfg, k, ta, tb, tc, tcp, tb2 ? *tb2 : tb, tc2 ? *tc2 : tc, tc3 ? *tc3 : tc, a));
+    return 0;
+  } else {
+    k<<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tc, tcp, tb2 ? *tb2 : tb, tc2 ? *tc2 : tc, tc3 ? *tc3 : tc, a);
+    return (int)cudaGetLastError();
+  }
 }
+
+// CTA pairs (256-row tiles on two SMs) serve the plain GEMM's 256-wide tiles by default. DT_GEMM_PAIR=0
+// turns them off, =1 also routes its 128-wide tiles to pairs (a test setting: slower on every shape of
+// the tiny preset). Measured on B200 (256-wide tiles, pairs against single CTAs): LM-head-shaped
+// product 0.331 vs 0.358 ms, gate|up-shaped 0.167 vs 0.177, down data-gradient 0.087 vs 0.093, QKV-shaped
+// 0.058 vs 0.060, 8192^3 0.765 vs 0.793; N = 768 products unchanged. The fused epilogues (SwiGLU,
+// QKV + RoPE, LM head + softmax statistics) stay on single CTAs: paired, a tile waits for the slower of
+// two heavy epilogues before its accumulator is reused (SwiGLU forward 0.253 vs 0.222 ms).
+int pair_mode() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DT_GEMM_PAIR");
+    v = e ? atoi(e) : 2;
+  }
+  return v;
+}
+bool use_pair(int bn) { return bn == 256 ? pair_mode() >= 1 : (bn == 128 && pair_mode() == 1); }
 
 int num_sms() {
   if (!g_num_sms) {
@@ -734,6 +849,10 @@ int num_sms() {
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
   }
   return g_num_sms;
+}
+int pair_grid(int units) {
+  const int pairs = units < num_sms() / 2 ? units : num_sms() / 2;
+  return 2 * pairs;
 }
 
 }  // namespace
@@ -761,10 +880,11 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
     // accumulate / split-K problems fill the machine through K splits instead: keep the wide tile
     if (epi == EPI_F32_ATOMIC && N > 128 && tm * ((N + 255) / 256) < g_num_sms) bn = 256;
   }
+  const bool pair = use_pair(bn);
   GemmArgs a = {};
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + BK - 1) / BK;
-  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_m = (M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   a.tiles_n = (N + bn - 1) / bn;
   int tiles = a.tiles_m * a.tiles_n;
   if (split_k <= 0) {
@@ -773,9 +893,10 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
     // one, the split with the best fill. A power-of-two rule lands e.g. 96 tiles on 192 units = 1.3 waves.
     split_k = 1;
     if (epi == EPI_F32_ATOMIC) {
+      const int slots = pair ? g_num_sms / 2 : g_num_sms;
       auto fill = [&](int sk) {
         const long long u = (long long)tiles * sk;
-        return (double)u / (double)(((u + g_num_sms - 1) / g_num_sms) * g_num_sms);
+        return (double)u / (double)(((u + slots - 1) / slots) * slots);
       };
       int best = 1;
       double best_fill = fill(1);
@@ -810,10 +931,23 @@ int gemm_impl(const void* A, int a_mn, long long lda, const void* B, int b_mn, l
   if (a.peer && (rc = make_map(&tcp, Cpeer, N, M, ldc, 64, 32, false, true))) return rc;
   rc = a_mn ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
   if (rc) return rc;
-  rc = b_mn ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
+  rc = b_mn ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, pair ? bn / 2 : bn);
   if (rc) return rc;
 
   int units = tiles * a.split_k;
+  if (pair) {
+    const int grid2 = pair_grid(units);
+    if (bn == 256) {
+      if (!a_mn && !b_mn) return launch<256, 0, 0, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+      if (!a_mn && b_mn) return launch<256, 0, 1, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+      if (a_mn && !b_mn) return launch<256, 1, 0, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+      return launch<256, 1, 1, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+    }
+    if (!a_mn && !b_mn) return launch<128, 0, 0, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+    if (!a_mn && b_mn) return launch<128, 0, 1, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+    if (a_mn && !b_mn) return launch<128, 1, 0, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+    return launch<128, 1, 1, 0, true>(ta, tb, tcm, tcp, a, grid2, stream);
+  }
   int grid = units < g_num_sms ? units : g_num_sms;
   if (bn == 256) {
     if (!a_mn && !b_mn) return launch<256, 0, 0>(ta, tb, tcm, tcp, a, grid, stream);

@@ -15,8 +15,7 @@ constexpr int RY_MAX = 4, ROWS_F = 16, ROWS_B = 64;
 
 // Work items per row, in units of 8 elements: P8 = (nh+nkv) * d/16 rotation groups (8 pairs each),
 // then V8 = nkv * d/8 groups of v elements.
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  uint4 u = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
   uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -65,13 +64,23 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
   }
   const int rows = BWD ? ROWS_B : ROWS_F;
   const long long r0 = (long long)blockIdx.x * rows;
+  // the next row's two 16-byte groups are loaded (kept packed, 8 registers) before this row is worked on
+  uint4 na = make_uint4(0, 0, 0, 0), nb = na;
+  auto fetch = [&](long long row) {
+    const __nv_bfloat16* q = qkv + row * W_;
+    na = *reinterpret_cast<const uint4*>(q + c0);
+    if (c1 >= 0) nb = *reinterpret_cast<const uint4*>(q + c1);
+  };
+  if (active && r0 + y < M && y < rows) fetch(r0 + y);
   for (int rr = y; rr < rows && active; rr += RY) {
     const long long row = r0 + rr;
     if (row >= M) break;
     const int t = (int)(row % T);
     __nv_bfloat16* p = qkv + row * W_;
+    const uint4 ua = na, ub = nb;
+    if (rr + RY < rows && row + RY < M) fetch(row + RY);
     float a[8];
-    load8(p + c0, a);
+    unpack8(ua, a);
     if (c1 < 0) {
       if (BWD) {
 #pragma unroll
@@ -84,7 +93,7 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
       continue;
     }
     float b[8];
-    load8(p + c1, b);
+    unpack8(ub, b);
     const float4* cp = reinterpret_cast<const float4*>(cosT + (long long)t * half + i0);
     const float4* sp = reinterpret_cast<const float4*>(sinT + (long long)t * half + i0);
     float4 ca = cp[0], cb = cp[1], sa = sp[0], sb = sp[1];

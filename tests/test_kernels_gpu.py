@@ -396,3 +396,43 @@ def test_adamw_matches_reference():
     ops.adamw_step(p, grads, m, v, p16, cseg, cstart, cend, norms, hp, loss)
     torch.cuda.synchronize()
     assert torch.equal(before, p)
+
+
+_PAIR_SCRIPT = r"""
+import sys, torch
+from distrain_b200 import ops
+torch.manual_seed(7)
+out = {}
+for (M, N, K, a_mn, b_mn, epi) in [(300, 512, 768, 0, 0, 0), (1000, 768, 136, 1, 1, 1), (257, 1280, 512, 0, 1, 2)]:
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    C = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16 if epi == 0 else torch.float32)
+    ops.gemm(a, b, C, M=M, N=N, K=K, a_mn=bool(a_mn), b_mn=bool(b_mn), epi=epi, bn=256)
+    out[(M, N, K)] = C.float().cpu()
+torch.cuda.synchronize()
+assert ops.device_error()[0] == 0
+torch.save(out, sys.argv[1])
+"""
+
+
+@pytest.mark.parametrize("mode", ["0", "2"])
+def test_gemm_256_wide_single_cta_and_pair_paths(tmp_path, mode):
+    """256-wide tiles run on CTA pairs by default (DT_GEMM_PAIR unset / 2); DT_GEMM_PAIR=0 keeps them on
+    single CTAs. Both paths (in child processes, the mode is read once) against the fp32 product."""
+    import os
+    import subprocess
+    import sys
+    path = str(tmp_path / f"out{mode}.pt")
+    env = dict(os.environ, DT_GEMM_PAIR=mode)
+    r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, path], env=env, capture_output=True, text=True,
+                       timeout=300, cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = torch.load(path)
+    torch.manual_seed(7)
+    for (M, N, K, a_mn, b_mn, epi) in [(300, 512, 768, 0, 0, 0), (1000, 768, 136, 1, 1, 1), (257, 1280, 512, 0, 1, 2)]:
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        B = torch.randn(N, K, device="cuda").bfloat16()
+        ref = (A.float() @ B.float().t()).cpu()
+        assert _rel(out[(M, N, K)], ref) < (1e-2 if epi == 0 else 1e-4), (M, N, K, mode)
