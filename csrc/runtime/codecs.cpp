@@ -230,6 +230,21 @@ DT_API unsigned long long dtr_siphash13(const void* data, long long n) {
 
 DT_API unsigned long long dtr_splitmix64(unsigned long long s) { return splitmix64(s); }
 
+// Gaussian test matrix of the low-rank compressor (reference lowrank.rs:54-80): n x r values (row-major),
+// state = m * 0x9e3779b97f4a7c15 + n + r, each draw replaces the state by splitmix64 of it; pairs of
+// draws give u1 = lo32 / 2^32 + 1e-10, u2 = lo32 / 2^32 and the value sqrt(-2 ln u1) cos(2 pi u2) (f64).
+DT_API void dtr_lowrank_omega(long long m, long long n, long long r, double* out) {
+  uint64_t st = (uint64_t)m * 0x9e3779b97f4a7c15ULL + (uint64_t)n + (uint64_t)r;
+  const long long cnt = n * r;
+  for (long long i = 0; i < cnt; ++i) {
+    st = splitmix64(st);
+    const double u1 = (double)(st & 0xFFFFFFFFULL) / 4294967296.0 + 1e-10;
+    st = splitmix64(st);
+    const double u2 = (double)(st & 0xFFFFFFFFULL) / 4294967296.0;
+    out[i] = std::sqrt(-2.0 * std::log(u1)) * std::cos(2.0 * M_PI * u2);
+  }
+}
+
 // Rust `format!("{}:{}", version, node_id).hash()` / `version.hash()` on DefaultHasher (SipHash-1-3,
 // keys 0,0): a str hashes its bytes followed by 0xff, a u64 its 8 little-endian bytes.
 DT_API unsigned long long dtr_hash_str(const char* s) {

@@ -3,6 +3,10 @@
 Per 2-D tensor: randomized range finder with a Gaussian test matrix drawn from splitmix64 + Box-Muller
 (same seeds as the reference: m * 0x9e3779b97f4a7c15 + n + r), one pass, modified Gram-Schmidt in
 float64, D ~= Q (Q^T D); the residual goes to the error buffer. 1-D tensors pass through exactly.
+Runs where the delta lives: CUDA tensors are compressed on the GPU (the test matrix comes from the
+native runtime - the draws form one sequential chain, each state being the previous output - and is
+copied over; the products and the Gram-Schmidt run on the device in float64), and only the factors cross
+to the host for the JSON payload.
 JSON shape: {"tensors": {name: {u, v, m, n, rank}}, "rank": r}.
 """
 from __future__ import annotations
@@ -23,7 +27,8 @@ def _splitmix64(s: int) -> int:
     return z ^ (z >> 31)
 
 
-def _omega(m: int, n: int, r: int) -> torch.Tensor:
+def _omega_loop(m: int, n: int, r: int) -> torch.Tensor:
+    """The test matrix draw by draw (the reference's loop, lowrank.rs:54-80); kept as the oracle."""
     rng = ((m * 0x9e3779b97f4a7c15) & _M64)
     rng = (rng + n + r) & _M64
     vals = []
@@ -36,9 +41,17 @@ def _omega(m: int, n: int, r: int) -> torch.Tensor:
     return torch.tensor(vals, dtype=torch.float64).view(n, r)
 
 
+def _omega(m: int, n: int, r: int, device="cpu") -> torch.Tensor:
+    """The test matrix from the native runtime (the same draws as ``_omega_loop``), on ``device``."""
+    from ..utils import native
+    out = torch.empty(n, r, dtype=torch.float64)
+    native.rt().dtr_lowrank_omega(m, n, r, out.data_ptr())
+    return out.to(device)
+
+
 def truncated_svd(mat: torch.Tensor, m: int, n: int, r: int) -> Tuple[torch.Tensor, torch.Tensor]:
     D = mat.reshape(m, n).double()
-    Y = D @ _omega(m, n, r).to(D.device)
+    Y = D @ _omega(m, n, r, D.device)
     for j in range(r):  # modified Gram-Schmidt, as the reference
         Y[:, j] /= Y[:, j].norm().clamp_min(1e-15)
         if j + 1 < r:

@@ -23,6 +23,7 @@ _SIGS = {
     "dtr_zstd_decompress": ([c_void, c_ll], c_void),
     "dtr_siphash13": ([c_void, c_ll], c_ull),
     "dtr_splitmix64": ([c_ull], c_ull),
+    "dtr_lowrank_omega": ([c_ll, c_ll, c_ll, c_void], None),
     "dtr_hash_str": ([c_char_p], c_ull),
     "dtr_hash_u64": ([c_ull], c_ull),
     "dtr_shard_assignment": ([c_char_p, c_ull, c_ll, c_ll, c_void], c_ll),

@@ -30,3 +30,11 @@ def test_roundtrip_passthrough_and_error_feedback():
     lr2, _ = compress_lowrank({"w": torch.zeros(32 * 40), "b": torch.zeros(40)}, shapes, 8, ef)
     out2 = decompress_lowrank(lr2)
     assert float(out2["w"].norm()) > 0.0
+
+
+def test_native_test_matrix_equals_the_draw_by_draw_loop():
+    from distrain_b200.parallel.lowrank import _omega, _omega_loop
+    for m, n, r in [(64, 48, 4), (768, 256, 8), (3, 5, 2)]:
+        a, b = _omega(m, n, r), _omega_loop(m, n, r)
+        assert a.shape == b.shape == (n, r)
+        assert torch.equal(a, b)  # the same libm on both sides
