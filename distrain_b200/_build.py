@@ -47,6 +47,24 @@ def _run(cmd):
     return r.stdout
 
 
+class _BuildLock:
+    """Exclusive lock on ``_build/.lock`` for one build step: the ranks of a multi-process launch that find
+    the libraries stale build them one at a time (the first builds, the others then find them current)
+    instead of racing on the same object and output files."""
+
+    def __enter__(self):
+        import fcntl
+        os.makedirs(BUILDDIR, exist_ok=True)
+        self.f = open(os.path.join(BUILDDIR, ".lock"), "w")
+        fcntl.flock(self.f, fcntl.LOCK_EX)
+        return self
+
+    def __exit__(self, *exc):
+        import fcntl
+        fcntl.flock(self.f, fcntl.LOCK_UN)
+        self.f.close()
+
+
 def _compile_many(jobs, workers):
     with cf.ThreadPoolExecutor(max_workers=workers) as ex:
         futs = [ex.submit(_run, j) for j in jobs]
@@ -54,7 +72,7 @@ def _compile_many(jobs, workers):
             f.result()
 
 
-def build_kernels(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
+def _build_kernels(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
     srcs = sorted(glob.glob(os.path.join(CSRC, "kernels", "*.cu")))
     hdrs = glob.glob(os.path.join(CSRC, "kernels", "*.cuh")) + glob.glob(os.path.join(CSRC, "kernels", "*.h"))
     os.makedirs(LIBDIR, exist_ok=True)
@@ -78,13 +96,13 @@ def build_kernels(force: bool = False, verbose: bool = False, extra_flags=None) 
             print(f"[build] nvcc {len(jobs)} kernel sources", file=sys.stderr)
         _compile_many(jobs, min(len(jobs), os.cpu_count() or 4))
     if jobs or force or not os.path.exists(KERNELS_SO) or os.path.getmtime(KERNELS_SO) < _newest(objs):
-        tmp = KERNELS_SO + ".tmp"
+        tmp = f"{KERNELS_SO}.{os.getpid()}.tmp"
         _run([nvcc] + ARCH_FLAGS + ["-shared", "-rdc=true", "-Xcompiler", "-fPIC", "-o", tmp] + objs)
         os.replace(tmp, KERNELS_SO)
     return KERNELS_SO
 
 
-def build_runtime(force: bool = False, verbose: bool = False) -> str:
+def _build_runtime(force: bool = False, verbose: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cpp")))
     hdrs = glob.glob(os.path.join(CSRC, "runtime", "*.h")) + glob.glob(os.path.join(CSRC, "runtime", "*.hpp"))
     os.makedirs(LIBDIR, exist_ok=True)
@@ -109,13 +127,23 @@ def build_runtime(force: bool = False, verbose: bool = False) -> str:
             print(f"[build] g++ {len(jobs)} runtime sources", file=sys.stderr)
         _compile_many(jobs, min(len(jobs), os.cpu_count() or 4))
     if jobs or force or not os.path.exists(RUNTIME_SO) or os.path.getmtime(RUNTIME_SO) < _newest(objs):
-        tmp = RUNTIME_SO + ".tmp"
+        tmp = f"{RUNTIME_SO}.{os.getpid()}.tmp"
         link = [cxx, "-shared", "-pthread", "-o", tmp] + objs + ["-ldl"]
         if os.environ.get("DT_SANITIZE"):
             link.insert(1, "-fsanitize=" + os.environ["DT_SANITIZE"])
         _run(link)
         os.replace(tmp, RUNTIME_SO)
     return RUNTIME_SO
+
+
+def build_kernels(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
+    with _BuildLock():
+        return _build_kernels(force, verbose, extra_flags)
+
+
+def build_runtime(force: bool = False, verbose: bool = False) -> str:
+    with _BuildLock():
+        return _build_runtime(force, verbose)
 
 
 def build_ffi(force: bool = False, verbose: bool = False) -> str:
