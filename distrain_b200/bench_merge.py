@@ -9,6 +9,9 @@ snapshot minus the master weights) and an error-feedback buffer of the same dist
 uniformly from {0, 1, 2, 3} and token counts uniformly from [1e5, 1e6], giving the merge weights
 tokens * 0.9^staleness.
 
+With ``--per-rank K`` every GPU pushes K deltas (K payload buffers, each compressed from its own
+snapshot), so the merge has GPUs x K contributors; compress_ms is then one compression.
+
 Per (model, top-k), every iteration:
   1. every rank compresses its delta (+ error feedback) into its symmetric (peer-mapped) payload buffer:
      pass A + radix top-k + ordered compaction + INT8 block 256 (or, for "raw", pass A and the dense fp32
@@ -51,7 +54,7 @@ def _max_over_ranks(x: float, dev) -> float:
     return float(t.item())
 
 
-def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, dev):
+def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, dev, per_rank: int = 1):
     from .config import preset, CompressionConfig
     from .models.params import ParamLayout
     from .parallel.compression import DeviceCompressor, DevicePayload
@@ -63,11 +66,14 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     n = L.total
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     master = torch.randn(n, device=dev, generator=g) * 0.02
-    snap = master + torch.randn(n, device=dev, generator=g) * 1e-4
+    # per_rank deltas per GPU (contributor j = rank * per_rank + k pushes snaps[k] - master)
+    snaps = [master + torch.randn(n, device=dev, generator=g) * 1e-4 for _ in range(per_rank)]
+    snap = snaps[0]
     ef0 = torch.randn(n, device=dev, generator=g) * 1e-4
+    nc = world * per_rank  # contributors
     hg = torch.Generator().manual_seed(4321)  # same draws on every rank
-    stale = torch.randint(0, 4, (world,), generator=hg).tolist()
-    tokens = torch.randint(100_000, 1_000_001, (world,), generator=hg).tolist()
+    stale = torch.randint(0, 4, (nc,), generator=hg).tolist()
+    tokens = torch.randint(100_000, 1_000_001, (nc,), generator=hg).tolist()
     weights = [t * 0.9 ** s for t, s in zip(tokens, stale)]
     ks = [k for k in topks if k != "raw"]
     cap_max = DeviceCompressor.capacity_for(L, max(ks)) if ks else 1
@@ -75,7 +81,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     if "raw" in topks:
         need = max(need, 4 * n)
     pay_bytes = (need + 4095) // 4096 * 4096
-    pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes, dev, world)
+    pay_buf, pay_ptrs, _, _pay_h = _symm_alloc(pay_bytes * per_rank, dev, world)
     stage_bytes = (n * 4 + 4095) // 4096 * 4096
     stage_buf, stage_ptrs, stage_mc, _stage_h = _symm_alloc(stage_bytes, dev, world)
     p32 = [p for p in stage_ptrs]
@@ -95,49 +101,58 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
     for k in topks:
         raw = k == "raw"
         cap = DeviceCompressor.capacity_for(L, 0.01 if raw else k)
-        payload = DevicePayload(pay_buf[:DevicePayload.nbytes(cap, 256)], cap, 256)
+        payloads = [DevicePayload(pay_buf[q * pay_bytes:q * pay_bytes + DevicePayload.nbytes(cap, 256)], cap, 256)
+                    for q in range(per_rank)]
         comp = DeviceCompressor(L, dev, CompressionConfig(top_k_fraction=0.01 if raw else k, int8_block=256),
-                                payload=payload)
-        raw_view = pay_buf[:4 * n].view(torch.float32) if raw else None
+                                payload=payloads[0])
+        raw_views = [pay_buf[q * pay_bytes:q * pay_bytes + 4 * n].view(torch.float32) for q in range(per_rank)] \
+            if raw else None
         t_comp, t_merge, t_single, pulled, infos = [], [], [], 0, None
         for it in range(warmup + iters):
-            comp.snap.copy_(snap)
-            comp.ef.copy_(ef0)
-            torch.cuda.synchronize()
-            barrier()
-            c0, c1 = _events()
-            c0.record()
-            comp.begin(master)
-            if raw:
-                comp.finish_raw(raw_view)
-            else:
-                comp.finish()
-            c1.record()
-            torch.cuda.synchronize()
-            kept = n if raw else int(comp.stats_host[comp.nseg * 6].item())
-            wire = comp.read_stats(raw=raw)["wire"]
-            cnt = torch.tensor([kept] + wire, device=dev, dtype=torch.float64)
+            rows = []
+            for q in range(per_rank):
+                comp.snap.copy_(snaps[q])
+                comp.ef.copy_(ef0)
+                torch.cuda.synchronize()
+                barrier()
+                c0, c1 = _events()
+                c0.record()
+                comp.begin(master)
+                if raw:
+                    comp.finish_raw(raw_views[q])
+                else:
+                    comp.finish(payload=payloads[q])
+                c1.record()
+                torch.cuda.synchronize()
+                if q == 0 and it >= warmup:
+                    t_comp.append(c0.elapsed_time(c1))
+                kept = n if raw else int(comp.stats_host[comp.nseg * 6].item())
+                rows.append([kept] + comp.read_stats(raw=raw)["wire"])
+            cnt = torch.tensor(rows, device=dev, dtype=torch.float64)  # [per_rank, 4]
             got = [torch.zeros_like(cnt) for _ in range(world)]
             if world > 1:
                 dist.all_gather(got, cnt)
             else:
                 got = [cnt]
-            counts = [int(g[0].item()) for g in got]
-            stats = [g[1:].tolist() for g in got]  # what each node reports with its push
+            counts = [int(g[q, 0].item()) for g in got for q in range(per_rank)]
+            stats = [g[q, 1:].tolist() for g in got for q in range(per_rank)]  # what each push reports
             base = pay_buf.data_ptr()
             contribs = []
             for r in range(world):
-                off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
-                if raw:
-                    contribs.append(Contribution(idx_ptr=0, q_ptr=0, val_ptr=off(raw_view), scales_ptr=0, count=n,
-                                                 block=0, dense=True, weight=weights[r], node_id=f"node-{r:02d}",
-                                                 wire_bytes=4 * n))
-                    continue
-                contribs.append(Contribution(idx_ptr=off(payload.idx), q_ptr=off(payload.q), win_ptr=off(payload.win),
-                                             val_ptr=off(payload.val), scales_ptr=off(payload.scales),
-                                             count=counts[r], block=256, dense=False, weight=weights[r],
-                                             node_id=f"node-{r:02d}", wire_bytes=payload.wire_bytes(counts[r])))
-            pulled = sum(c.wire_bytes for c in contribs[1:])
+                for q in range(per_rank):
+                    j = r * per_rank + q
+                    off = lambda t, r=r: t.data_ptr() - base + pay_ptrs[r]
+                    if raw:
+                        contribs.append(Contribution(idx_ptr=0, q_ptr=0, val_ptr=off(raw_views[q]), scales_ptr=0,
+                                                     count=n, block=0, dense=True, weight=weights[j],
+                                                     node_id=f"node-{j:02d}", wire_bytes=4 * n))
+                        continue
+                    pq = payloads[q]
+                    contribs.append(Contribution(idx_ptr=off(pq.idx), q_ptr=off(pq.q), win_ptr=off(pq.win),
+                                                 val_ptr=off(pq.val), scales_ptr=off(pq.scales), count=counts[j],
+                                                 block=256, dense=False, weight=weights[j], node_id=f"node-{j:02d}",
+                                                 wire_bytes=pq.wire_bytes(counts[j])))
+            pulled = sum(c.wire_bytes for c in contribs[per_rank:])
             # distributed merge: every rank plans from the reported statistics (the same on every rank),
             # merges its slice and broadcasts it; rank 0 checks that every slice landed
             coefs, infos = DeviceMerger.plan(contribs, stats)
@@ -166,7 +181,6 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                 sms = s0.elapsed_time(s1)
             barrier()
             if it >= warmup:
-                t_comp.append(c0.elapsed_time(c1))
                 t_merge.append(mms)
                 t_single.append(sms)
         cms = _max_over_ranks(sorted(t_comp)[len(t_comp) // 2], dev)
@@ -175,9 +189,9 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         if rank == 0:
             from .roofline import distributed_merge_roofline
             per_member = sum(c.wire_bytes for c in contribs) / len(contribs)
-            roof = distributed_merge_roofline(n, per_member, world, mms, multicast=bool(mc32))
+            roof = distributed_merge_roofline(n, per_member * per_rank, world, mms, multicast=bool(mc32))
             results.append({"bench": "compress_merge_broadcast", "model": name, "params": L.num_params(),
-                            "merge_roofline": roof,
+                            "merge_roofline": roof, "contributors": nc, "payloads_per_gpu": per_rank,
                             "n_nodes": world, "top_k": k, "compress_ms": round(cms, 3), "merge_ms": round(mms, 3),
                             "total_ms": round(cms + mms, 3), "merge": f"distributed over {world} GPUs",
                             "single_coordinator_merge_ms": round(sms, 3), "accepted": infos["accepted"],
@@ -185,7 +199,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
                             "checkpoint_bytes_broadcast": n * 4, "broadcast": "nvls multimem" if mc32 else "per-peer",
                             "staleness": stale, "tokens": tokens,
                             "timing": "CUDA events, median of iters, max over ranks"})
-        del comp, payload
+        del comp, payloads
     # comparison arm: dense fp32 all-reduce of the same deltas
     delta = torch.empty_like(master)
     p16t = torch.empty(n, device=dev, dtype=torch.bfloat16)
@@ -197,7 +211,7 @@ def run_model(name: str, topks, iters: int, warmup: int, rank: int, world: int, 
         e0, e1 = _events()
         e0.record()
         torch.sub(snap, master, out=delta)
-        delta.mul_(weights[rank] / sum(weights))  # the same staleness x tokens weights, then a plain sum
+        delta.mul_(weights[rank * per_rank] / sum(weights[::per_rank]))  # the same staleness x tokens weights, then a plain sum
         if world > 1:
             dist.all_reduce(delta, op=dist.ReduceOp.SUM)
         theta.copy_(snap).sub_(delta)
@@ -224,6 +238,8 @@ def main():
                          "when it fits the upload budget, as it always does over NVLink)")
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--per-rank", type=int, default=1,
+                    help="payloads pushed per GPU (contributors = GPUs x this): 8 contributors on 4 GPUs with 2")
     a = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -235,7 +251,7 @@ def main():
                                 timeout=datetime.timedelta(seconds=300))
     topks = [x if x == "raw" else float(x) for x in a.topk.split(",")]
     for m in a.models.split(","):
-        for r in run_model(m, topks, a.iters, a.warmup, rank, world, dev):
+        for r in run_model(m, topks, a.iters, a.warmup, rank, world, dev, max(a.per_rank, 1)):
             print(json.dumps(r), flush=True)
         torch.cuda.empty_cache()
     if world > 1:
