@@ -125,17 +125,22 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
 // Cross-entropy from the LM-head GEMM's fp32 softmax statistics (dt_gemm_logits_lse): one block per row
 // combines the row's `np` partial (max, sum exp) pairs into the log-sum-exp, writes
 // loss_row[r] = lse - target logit (both fp32), then replaces the bf16 logits of the row with
-// grad_scale * (softmax - onehot(target)) in one read + write pass.
+// grad_scale * (softmax - onehot(target)) in one read + write pass. With per-row weights `row_w`
+// (indexed like the rows of `ids`, i.e. by r0 + r; may be negative) the row's gradient is scaled by its
+// weight as well: a loss mask (fine-tuning on response tokens) or a signed preference coefficient. The
+// loss row stays the unweighted cross-entropy; dt_loss_reduce applies the same weights.
 __global__ void ce_lse_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long ld, const float2* __restrict__ part,
                                   int np, long long rows, const float* __restrict__ tgt_logit,
                                   const int* __restrict__ ids, int T, int S, long long r0,
-                                  float* __restrict__ loss_row, int V, float grad_scale) {
+                                  float* __restrict__ loss_row, int V, float grad_scale,
+                                  const float* __restrict__ row_w) {
   __shared__ float sh[32];
   __shared__ float sh_m[32];
   const long long r = blockIdx.x;
   const long long grow = r0 + r;
   const long long b = grow / T, t = grow - b * T;
   const int tgt = ids[b * S + t + 1];
+  if (row_w) grad_scale *= row_w[grow];
   float m = -INFINITY, s = 0.f;
   for (int k = threadIdx.x; k < np; k += blockDim.x) {
     const float2 p = part[(long long)k * rows + r];
@@ -176,12 +181,17 @@ __global__ void ce_lse_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   }
 }
 
-// out[0] = sum(loss_row[0:n]) * scale  (single block); out[1] = 1 if non-finite;
-// out[2] += out[0] and out[3] += 1 when finite (running round sums read at push time).
-__global__ void loss_reduce_kernel(const float* __restrict__ loss_row, long long n, float scale, float* out) {
+// out[0] = sum(w[i] * loss_row[i], i < n) * scale, w = 1 without weights (single block); out[1] = 1 if
+// non-finite; out[2] += out[0] and out[3] += 1 when finite (running round sums read at push time).
+__global__ void loss_reduce_kernel(const float* __restrict__ loss_row, long long n, float scale, float* out,
+                                   const float* __restrict__ w) {
   __shared__ float sh[32];
   float s = 0.f;
-  for (long long i = threadIdx.x; i < n; i += blockDim.x) s += loss_row[i];
+  for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+    // a zero weight drops its row even when that row's loss is not finite (padding)
+    if (w) s += w[i] != 0.f ? w[i] * loss_row[i] : 0.f;
+    else s += loss_row[i];
+  }
   float tot = block_sum(s, sh);
   if (threadIdx.x == 0) {
     float l = tot * scale;
@@ -227,17 +237,18 @@ DT_API int dt_ce_fwd_bwd(void* logits, long long ld, const int* ids, int T, int 
   return (int)cudaGetLastError();
 }
 
-DT_API int dt_loss_reduce(const float* loss_row, long long n, float scale, float* out, cudaStream_t st) {
-  loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_row, n, scale, out);
+DT_API int dt_loss_reduce(const float* loss_row, long long n, float scale, float* out, const float* w,
+                          cudaStream_t st) {
+  loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_row, n, scale, out, w);
   return (int)cudaGetLastError();
 }
 
 DT_API int dt_ce_lse_bwd(void* logits, long long ld, const void* part, int np, long long rows, const float* tgt_logit,
                          const int* ids, int T, int S, long long r0, float* loss_row, int V, float grad_scale,
-                         cudaStream_t st) {
+                         const float* row_w, cudaStream_t st) {
   if (V % 8 || ld % 8 || rows <= 0) return rows <= 0 ? 0 : -10;
   ce_lse_bwd_kernel<<<(unsigned)rows, 512, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld,
                                                     reinterpret_cast<const float2*>(part), np, rows, tgt_logit, ids,
-                                                    T, S, r0, loss_row, V, grad_scale);
+                                                    T, S, r0, loss_row, V, grad_scale, row_w);
   return (int)cudaGetLastError();
 }

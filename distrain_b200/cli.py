@@ -464,6 +464,87 @@ def cmd_serve(args):
         srv.stop()
 
 
+def _posttrain_model(args, checkpoint):
+    """(ModelConfig, flat fp32 weights) of a post-training run: a checkpoint, or a random model of
+    ``--model-size``."""
+    import torch
+    from .models.params import ParamLayout, init_flat
+    if checkpoint:
+        from .utils.checkpoint import load_safetensors
+        sd = load_safetensors(checkpoint)
+        cfg = _infer_model_config(sd)
+        L = ParamLayout(cfg)
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, sd)
+    else:
+        cfg = _model_cfg(args.model_size, vocab=args.vocab)
+        flat = init_flat(ParamLayout(cfg), seed=args.seed)
+    if args.rope_theta:
+        cfg.rope_theta = args.rope_theta
+    cfg.max_seq_len = max(cfg.max_seq_len, args.max_seq_len)
+    return cfg, flat
+
+
+def _posttrain_tokenizer(args, cfg):
+    from .alignment import ByteTokenizer, FileTokenizer
+    tok = FileTokenizer(args.tokenizer) if args.tokenizer else ByteTokenizer()
+    if tok.vocab_size > cfg.vocab_size:
+        raise SystemExit(f"tokenizer vocabulary {tok.vocab_size} > model vocabulary {cfg.vocab_size}")
+    return tok
+
+
+def _posttrain_done(event, m, keys):
+    print(json.dumps({"event": event, **{k: m[k] for k in keys}}))
+
+
+def cmd_sft(args):
+    """Supervised fine-tuning on chat data, loss on the assistant turns (the reference's scripts/run_sft.py)."""
+    from .alignment import SFTConfig, SFTTrainer, load_chat_jsonl, synthetic_conversations, tokenize_conversation
+    if args.use_lora:
+        raise SystemExit("sft: LoRA is not provided; fine-tuning updates every weight")
+    cfg, flat = _posttrain_model(args, args.base_model)
+    tok = _posttrain_tokenizer(args, cfg)
+    if args.synthetic:
+        convs = synthetic_conversations(args.max_examples or 100)
+    elif args.datasets:
+        convs = load_chat_jsonl([d.strip() for d in args.datasets.split(",")], args.max_examples)
+    else:
+        raise SystemExit("sft: give --datasets (JSONL files) or --synthetic")
+    examples = [tokenize_conversation(c, tok, args.template, args.max_seq_len) for c in convs]
+    c = SFTConfig(learning_rate=args.lr, num_epochs=args.epochs, batch_size=args.batch_size,
+                  gradient_accumulation_steps=args.grad_accum, max_seq_len=args.max_seq_len,
+                  save_every_n_steps=args.save_every, log_every_n_steps=args.log_every, output_dir=args.output,
+                  seed=args.seed)
+    m = SFTTrainer(cfg, flat, examples, c, pad_id=tok.pad_id, device=args.device).train()
+    _posttrain_done("sft_done", m, ("steps", "examples", "response_tokens", "first_loss", "final_loss",
+                                    "tokens_per_sec", "checkpoint"))
+
+
+def cmd_dpo(args):
+    """Direct preference optimisation against the frozen starting model (the reference's scripts/run_dpo.py)."""
+    from .alignment import DPOConfig, DPOTrainer, load_preference_jsonl, synthetic_preferences
+    if args.use_lora:
+        raise SystemExit("dpo: LoRA is not provided; fine-tuning updates every weight")
+    cfg, flat = _posttrain_model(args, args.sft_model)
+    pad_id = 0
+    if args.synthetic:  # token ids 1..48, no tokenizer
+        pairs = synthetic_preferences(args.max_examples or 50)
+    elif args.datasets:
+        tok = _posttrain_tokenizer(args, cfg)
+        pad_id = tok.pad_id
+        pairs = load_preference_jsonl([d.strip() for d in args.datasets.split(",")], tok, args.template,
+                                      args.max_examples)
+    else:
+        raise SystemExit("dpo: give --datasets (JSONL files) or --synthetic")
+    c = DPOConfig(beta=args.beta, learning_rate=args.lr, num_epochs=args.epochs, batch_size=args.batch_size,
+                  gradient_accumulation_steps=args.grad_accum, max_seq_len=args.max_seq_len,
+                  save_every_n_steps=args.save_every, log_every_n_steps=args.log_every, output_dir=args.output,
+                  seed=args.seed)
+    m = DPOTrainer(cfg, flat, pairs, c, pad_id=pad_id, device=args.device).train()
+    _posttrain_done("dpo_done", m, ("steps", "pairs", "first_loss", "final_loss", "final_reward_accuracy",
+                                    "pairs_per_sec", "checkpoint"))
+
+
 def cmd_benchmark(args):
     """Measure this device's training step time and the largest batch that fits (calibration)."""
     import torch
@@ -728,6 +809,40 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--max-tokens-cap", type=int, default=1024)
     p.add_argument("--rope-theta", type=float)
     p.set_defaults(fn=cmd_serve)
+
+    for name, fn in (("sft", cmd_sft), ("dpo", cmd_dpo)):
+        sft = name == "sft"
+        p = sp.add_parser(name, help="supervised fine-tuning on chat data (loss on assistant turns)" if sft
+                          else "direct preference optimisation against the frozen starting model")
+        if sft:
+            p.add_argument("--base-model", help="starting checkpoint (safetensors); default: a random model")
+        else:
+            p.add_argument("--sft-model", help="starting checkpoint (safetensors); default: a random model")
+        p.add_argument("--model-size", default="125m", help="preset of the random model (125m, 1b, 7b, 13b, ...)")
+        p.add_argument("--vocab", type=int, help="vocabulary of the random model")
+        p.add_argument("--device", default="cuda:0")
+        p.add_argument("--datasets", help="comma-separated JSONL files")
+        p.add_argument("--synthetic", action="store_true", help="the built-in synthetic data")
+        p.add_argument("--max-examples", type=int, help="at most this many examples per file")
+        p.add_argument("--max-seq-len", type=int, default=512 if sft else 256)
+        p.add_argument("--template", default="chatml", choices=["chatml", "llama", "zephyr"])
+        p.add_argument("--tokenizer", help="tokenizer JSON; default: UTF-8 bytes")
+        p.add_argument("--epochs", type=int, default=3 if sft else 1)
+        p.add_argument("--lr", type=float, default=2e-5 if sft else 5e-7)
+        p.add_argument("--batch-size", type=int, default=4 if sft else 2,
+                       help="sequences per micro-batch" if sft else "preference pairs per micro-batch")
+        p.add_argument("--grad-accum", type=int, default=8 if sft else 16)
+        if not sft:
+            p.add_argument("--beta", type=float, default=0.1)
+        p.add_argument("--use-lora", action="store_true", help="not provided (fine-tuning updates every weight)")
+        p.add_argument("--lora-rank", type=int, default=64)
+        p.add_argument("--lora-alpha", type=int, default=128)
+        p.add_argument("--output", default=f"models/{name}")
+        p.add_argument("--save-every", type=int, default=500 if sft else 200)
+        p.add_argument("--log-every", type=int, default=10)
+        p.add_argument("--seed", type=int, default=0)
+        p.add_argument("--rope-theta", type=float)
+        p.set_defaults(fn=fn)
 
     p = sp.add_parser("benchmark", help="step time / throughput of this device")
     p.add_argument("--preset", default="tiny")

@@ -51,7 +51,7 @@ class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
                  lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False,
-                 grad_accum: int = 1):
+                 grad_accum: int = 1, loss_weights: bool = False):
         self.cfg = cfg
         self.tp = tp
         self.act_ckpt = act_ckpt
@@ -116,6 +116,10 @@ class TrainEngine:
         self.lse_part = torch.empty(ops.lse_parts(self.lm_chunk, V) * 2, dtype=f32, device=dev)
         self.tgt_logit = torch.empty(self.lm_chunk, dtype=f32, device=dev)
         self.loss_rows = torch.empty(self.A * M, dtype=f32, device=dev)
+        # per-row loss weights of the step (fine-tuning masks, preference coefficients): the loss is
+        # sum_r w_r * ce_r over all micro-batches and each row's gradient is scaled by w_r, so the weights
+        # carry the normalisation. Without them the loss is the mean over rows.
+        self.loss_w = torch.zeros(self.A * M, dtype=f32, device=dev) if loss_weights else None
         # ── backward scratch ──
         self.br = torch.empty(M, H, dtype=bf16, device=dev)
         self.dresid = torch.empty(M, H, dtype=f32, device=dev)
@@ -228,22 +232,49 @@ class TrainEngine:
         """[A*B, S] int32 token ids of one step (A micro-batches of B sequences)."""
         self.ids.copy_(tokens, non_blocking=True)
 
+    def set_loss_weights(self, w: torch.Tensor):
+        """Per-row loss weights of one step: [A*B, S-1] (weight of predicting token t+1 of a sequence) or
+        flat [A*M]. Needs an engine built with ``loss_weights=True``."""
+        if self.loss_w is None:
+            raise RuntimeError("engine built without loss_weights=True")
+        self.loss_w.copy_(w.reshape(-1).to(torch.float32), non_blocking=True)
+
     # ───────────────────────── the step ─────────────────────────
     def forward_backward(self, micro: int = 0, zero_grad: bool = True):
         """Forward + backward of micro-batch ``micro`` (rows [micro*B, (micro+1)*B) of ``ids``), adding its
         gradients into ``grad`` (cleared first when ``zero_grad``); the loss of the step is reduced after
         the last micro-batch."""
-        cfg = self.cfg
-        M, H, F, T, S, W, d, nh, nkv, V = self.M, self.H, self.F, self.T, self.S, self.W, self.d, self.nh, self.nkv, self.V
-        eps = cfg.norm_eps
-        Lr = cfg.num_layers
+        M, Lr = self.M, self.cfg.num_layers
         if self._tp_active() and self.tp.fused:
             self.tp.begin_step(4 * Lr + ((Lr - 1) if self.act_ckpt else 0))
         if zero_grad:
             self.grad.zero_()
         ids = self.ids[micro * self.B:(micro + 1) * self.B]
-        loss_rows = self.loss_rows[micro * M:(micro + 1) * M]
-        # ── forward ──
+        self._forward(ids)
+        self._lm_head_loss(micro, ids, backward=True)
+        if micro == self.A - 1:
+            if self.loss_w is None:
+                ops.loss_reduce(self.loss_rows, self.A * M, 1.0 / (M * self.A), self.loss)
+            else:
+                ops.loss_reduce(self.loss_rows, self.A * M, 1.0, self.loss, w=self.loss_w)
+        self._backward(ids)
+
+    def forward_loss(self, micro: int = 0) -> torch.Tensor:
+        """Forward only: the unweighted cross-entropy of every row of micro-batch ``micro`` ([B*(S-1)] fp32
+        view, predicting token t+1 of each sequence), e.g. for sequence log-probabilities. Parameters,
+        gradients and the step's loss are left alone."""
+        if self._tp_active():
+            raise NotImplementedError("forward_loss runs on engines without tensor parallelism")
+        ids = self.ids[micro * self.B:(micro + 1) * self.B]
+        self._forward(ids)
+        self._lm_head_loss(micro, ids, backward=False)
+        return self.loss_rows[micro * self.M:(micro + 1) * self.M]
+
+    def _forward(self, ids):
+        cfg = self.cfg
+        M, H, T, S, d, nh, nkv = self.M, self.H, self.T, self.S, self.d, self.nh, self.nkv
+        eps = cfg.norm_eps
+        Lr = cfg.num_layers
         ops.add_rmsnorm_fwd(emb=self.E, ids=ids, T=T, S=S, w=self.pv[0]["attn_norm"], out_resid=self.resid_in[0],
                             y=self.xn1[0], rstd=self.rstd1[0], eps=eps, M=M, H=H)
         for l in range(Lr):
@@ -261,8 +292,13 @@ class TrainEngine:
             else:
                 self._row_parallel_add_norm(self.hact[l], wv["down_w"], x=self.resid_mid[l], w=self.fnorm,
                                             scale=self.oscale, out_resid=self.resid_fin, y=self.xs, rstd=self.rstd_f)
-        # ── tied LM head + cross-entropy, chunked over rows; backward of the head fused per chunk ──
-        inv_m = 1.0 / (M * self.A)
+
+    def _lm_head_loss(self, micro: int, ids, backward: bool):
+        """Tied LM head + cross-entropy, chunked over rows; the head's backward is fused per chunk."""
+        M, H, T, S, V = self.M, self.H, self.T, self.S, self.V
+        loss_rows = self.loss_rows[micro * M:(micro + 1) * M]
+        row_w = None if self.loss_w is None else self.loss_w[micro * M:(micro + 1) * M]
+        scale = 1.0 / (M * self.A) if row_w is None else 1.0
         for r0 in range(0, M, self.lm_chunk):
             rows = min(self.lm_chunk, M - r0)
             xs_c = self.xs[r0:r0 + rows]
@@ -270,13 +306,16 @@ class TrainEngine:
             part = self.lse_part[:2 * ops.lse_parts(rows, V)]
             ops.gemm_logits_lse(xs_c, self.E16, lg, part, self.tgt_logit, ids, rows=rows, V=V, K=H, T=T, S=S, r0=r0)
             ops.ce_lse_bwd(lg, part, self.tgt_logit, ids, loss_rows[r0:r0 + rows], rows=rows, V=V, T=T, S=S, r0=r0,
-                           grad_scale=inv_m)
+                           grad_scale=scale, row_w=row_w)
+            if not backward:
+                continue
             ops.gemm(lg, self.E16, self.dxs[r0:r0 + rows], M=rows, N=H, K=V, b_mn=True, ldb=H)
             ops.gemm(lg, xs_c, self.gE, M=V, N=H, K=rows, a_mn=True, lda=V, b_mn=True, ldb=H, ldc=H,
                      epi=ops.EPI_F32_ATOMIC)
-        if micro == self.A - 1:
-            ops.loss_reduce(self.loss_rows, self.A * M, inv_m, self.loss)
-        # ── backward ──
+
+    def _backward(self, ids):
+        M, H, F, T, S, d, nh, nkv = self.M, self.H, self.F, self.T, self.S, self.d, self.nh, self.nkv
+        Lr = self.cfg.num_layers
         ops.rmsnorm_bwd(dy=self.dxs, x=self.resid_fin, rstd=self.rstd_f, w=self.fnorm, scale=self.oscale,
                         dresid_out=self.dresid, dresid16=self.g16, dw=self.g_fnorm, dscale=self.g_oscale, M=M, H=H)
         for l in reversed(range(Lr)):

@@ -169,16 +169,19 @@ def gemm_logits_lse(x, emb, logits, part, tgt_logit, ids, *, rows, V, K, T, S, r
           "dt_gemm_logits_lse")
 
 
-def ce_lse_bwd(logits, part, tgt_logit, ids, loss_rows, *, rows, V, T, S, r0, grad_scale, stream=None):
+def ce_lse_bwd(logits, part, tgt_logit, ids, loss_rows, *, rows, V, T, S, r0, grad_scale, row_w=None, stream=None):
     """Cross-entropy of ``rows`` rows from ``gemm_logits_lse``'s statistics: loss_rows = lse - target logit
-    (fp32) and the logits replaced in place by grad_scale * (softmax - onehot)."""
+    (fp32) and the logits replaced in place by grad_scale * (softmax - onehot), times ``row_w[r0 + r]``
+    when per-row weights are given (fp32, indexed like the rows of ``ids``)."""
     np_ = lse_parts(1, V)
     check(lib().dt_ce_lse_bwd(ptr(logits), logits.stride(0), ptr(part), np_, rows, ptr(tgt_logit), ptr(ids), T, S, r0,
-                              ptr(loss_rows), V, float(grad_scale), stream_ptr(stream)), "dt_ce_lse_bwd")
+                              ptr(loss_rows), V, float(grad_scale), ptr(row_w), stream_ptr(stream)), "dt_ce_lse_bwd")
 
 
-def loss_reduce(loss_rows, n, scale, out, stream=None):
-    check(lib().dt_loss_reduce(ptr(loss_rows), n, float(scale), ptr(out), stream_ptr(stream)), "dt_loss_reduce")
+def loss_reduce(loss_rows, n, scale, out, w=None, stream=None):
+    """out[0] = scale * sum(loss_rows[:n]) (weighted by ``w[:n]`` when given; zero-weight rows are dropped)."""
+    check(lib().dt_loss_reduce(ptr(loss_rows), n, float(scale), ptr(out), ptr(w), stream_ptr(stream)),
+          "dt_loss_reduce")
 
 
 def adamw_step(p, g, m, v, p16, cseg, cstart, cend, norms, hp, loss_flag=None, stream=None):

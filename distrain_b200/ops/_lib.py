@@ -47,11 +47,11 @@ _SIGS = {
     "dt_gemm_swiglu_bwd": [c_void, c_ll, c_void, c_ll, c_void, c_void, c_int, c_int, c_int, c_int, c_void],
     "dt_swiglu_bwd": [c_void, c_void, c_void, c_ll, c_int, c_void],
     "dt_ce_fwd_bwd": [c_void, c_ll, c_void, c_int, c_int, c_ll, c_ll, c_void, c_int, c_float, c_void],
-    "dt_loss_reduce": [c_void, c_ll, c_float, c_void, c_void],
+    "dt_loss_reduce": [c_void, c_ll, c_float, c_void, c_void, c_void],
     "dt_gemm_logits_lse": [c_void, c_ll, c_void, c_ll, c_void, c_ll, c_int, c_int, c_int, c_void, c_void, c_void,
                            c_int, c_int, c_ll, c_void],
     "dt_ce_lse_bwd": [c_void, c_ll, c_void, c_int, c_ll, c_void, c_void, c_int, c_int, c_ll, c_void, c_int, c_float,
-                      c_void],
+                      c_void, c_void],
     "dt_adamw_step": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_void, c_int, c_void,
                       c_void, c_void],
     "dt_adamw_apply": [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_void, c_int, c_void,

@@ -1,0 +1,158 @@
+"""Post-training data and loss weights (SFT / DPO) on the fp64 oracle model, no GPU.
+
+The engine runs both methods as a cross-entropy backward with per-row weights; these tests pin that the
+weights are right: the weighted loss's gradient equals the autograd gradient of the method's own loss."""
+import json
+
+import pytest
+import torch
+
+from distrain_b200 import alignment as al
+
+
+def _cfg():
+    from distrain_b200.config import ModelConfig
+    return ModelConfig(hidden_dim=32, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=64, vocab_size=64,
+                       max_seq_len=64, rope_theta=10000.0)
+
+
+def _params(cfg, seed):
+    from distrain_b200.models.params import ParamLayout, init_flat
+    L = ParamLayout(cfg)
+    flat = init_flat(L, 0.2, seed)
+    return {k: v.detach().double().clone().requires_grad_() for k, v in L.views(flat).items()}
+
+
+def _row_ce(p, cfg, ids):
+    """[n, S-1] cross-entropy of predicting token t+1 of every sequence."""
+    from distrain_b200.models import oracle
+    ids = ids.long()
+    z = oracle.logits_fn(p, cfg, ids[:, :-1], mask_value=None)
+    lp = torch.log_softmax(z, dim=-1)
+    return -lp.gather(-1, ids[:, 1:, None])[..., 0]
+
+
+def test_templates_mark_assistant_turns():
+    tok = al.ByteTokenizer()
+    conv = [al.Message("system", "sys"), al.Message("user", "hi"), al.Message("assistant", "hello")]
+    for template, trained_text in (("chatml", "hello<|im_end|>\n"), ("zephyr", "hello</s>\n"),
+                                   ("llama", " hello </s>")):
+        ex = al.tokenize_conversation(conv, tok, template, 512)
+        assert len(ex.ids) == len(ex.trained)
+        got = tok.decode([i for i, t in zip(ex.ids, ex.trained) if t])
+        assert got == trained_text, (template, got)
+        text = tok.decode(ex.ids)
+        assert "sys" in text and "hi" in text and text.endswith(trained_text)
+    llama = tok.decode(al.tokenize_conversation(conv, tok, "llama").ids)
+    assert llama.startswith("<s>[INST] <<SYS>>\nsys\n<</SYS>>\n\nhi [/INST]")
+    assert tok.decode(al.tokenize_conversation(conv, tok, "chatml").ids).startswith("<|im_start|>system\nsys")
+    with pytest.raises(ValueError):
+        al.render_chat(conv, "alpaca")
+    cut = al.tokenize_conversation(conv, tok, "chatml", max_seq_len=10)
+    assert len(cut.ids) == 10 and len(cut.trained) == 10
+
+
+def test_pack_rows_mask_is_shifted_trained_flags():
+    seqs = [[5, 6, 7, 8], [9, 10]]
+    trained = [[False, False, True, True], [False, True]]
+    ids, mask = al.pack_rows(seqs, trained, seq_len=6, pad_id=0)
+    assert ids.tolist() == [[5, 6, 7, 8, 0, 0], [9, 10, 0, 0, 0, 0]]
+    # row t predicts token t+1: trained when token t+1 is
+    assert mask.tolist() == [[0, 1, 1, 0, 0], [1, 0, 0, 0, 0]]
+    w = al.sft_weights(mask)
+    assert abs(float(w.sum()) - 1.0) < 1e-7 and float(w[0, 0]) == 0.0
+
+
+def test_sft_weighted_loss_is_masked_mean():
+    cfg = _cfg()
+    p = _params(cfg, 1)
+    g = torch.Generator().manual_seed(0)
+    seqs = [torch.randint(3, 64, (n,), generator=g).tolist() for n in (20, 13, 17)]
+    trained = [[j >= n // 2 for j in range(n)] for n in (20, 13, 17)]
+    ids, mask = al.pack_rows(seqs, trained, 24, 0)
+    ce = _row_ce(p, cfg, ids)
+    loss = (al.sft_weights(mask).double() * ce).sum()
+    ref = ce[mask.bool()].mean()
+    assert abs(loss.item() - ref.item()) < 1e-6 * abs(ref.item())  # fp32 weights
+
+
+def test_dpo_weights_give_the_dpo_gradient():
+    """sum_r w_r * ce_r with the DPO weights (computed from detached log-probabilities) has the same
+    gradient as the DPO loss itself, against a reference model that differs from the policy."""
+    cfg = _cfg()
+    pol, ref_p = _params(cfg, 2), _params(cfg, 3)
+    g = torch.Generator().manual_seed(1)
+    pairs = []
+    for _ in range(3):
+        prompt = torch.randint(3, 64, (7,), generator=g).tolist()
+        c = prompt + torch.randint(3, 64, (9,), generator=g).tolist()
+        r = prompt + torch.randint(3, 64, (5,), generator=g).tolist()
+        pairs.append(al.PreferencePair(prompt, c, r))
+    ids, mask = al.pair_rows(pairs, 20, 0)
+    assert mask[0].sum() == 9 and mask[1].sum() == 5 and mask[0, :6].sum() == 0 and mask[0, 6] == 1
+    beta = 0.5
+    with torch.no_grad():
+        ref_lp = al.sequence_logps(_row_ce(ref_p, cfg, ids), mask)
+    # the DPO loss by autograd
+    lp = al.sequence_logps(_row_ce(pol, cfg, ids), mask)
+    z = beta * ((lp[0::2] - ref_lp[0::2]) - (lp[1::2] - ref_lp[1::2]))
+    dpo = torch.nn.functional.softplus(-z).mean()
+    dpo.backward()
+    want = {k: v.grad.clone() for k, v in pol.items()}
+    for v in pol.values():
+        v.grad = None
+    # the weighted cross-entropy
+    w, st = al.dpo_weights(lp.detach(), ref_lp, mask, beta)
+    assert abs(st["loss"] - dpo.item()) < 1e-12
+    assert st["reward_accuracy"] == float((z > 0).double().mean())
+    (w.double() * _row_ce(pol, cfg, ids)).sum().backward()
+    for k, v in pol.items():
+        # the weights are stored in fp32
+        rel = ((v.grad - want[k]).norm() / (want[k].norm() + 1e-30)).item()
+        assert rel < 1e-6, (k, rel)
+
+
+def test_step_order_covers_every_item_each_epoch():
+    order = al.step_order(10, 4, 2, seed=3)
+    assert len(order) == 6 and all(len(s) == 4 for s in order)
+    for e in range(2):
+        seen = set(sum(order[3 * e:3 * e + 3], []))
+        assert seen == set(range(10))
+    with pytest.raises(ValueError):
+        al.step_order(0, 4, 1, 0)
+
+
+def test_synthetic_data_matches_reference_scripts():
+    convs = al.synthetic_conversations(7)
+    assert len(convs) == 7 and [m.role for m in convs[0]] == ["system", "user", "assistant"]
+    assert convs[5][1].content == convs[0][1].content
+    pairs = al.synthetic_preferences(3)
+    assert pairs[0].prompt_ids == list(range(1, 17))
+    assert pairs[0].chosen_ids[16:] == list(range(17, 33)) and pairs[0].rejected_ids[16:] == list(range(33, 49))
+
+
+def test_jsonl_loaders(tmp_path):
+    chat = tmp_path / "chat.jsonl"
+    chat.write_text(json.dumps({"messages": [{"role": "user", "content": "q"},
+                                             {"role": "assistant", "content": "a"}]}) + "\n\n"
+                    + json.dumps({"instruction": "do", "output": "done"}) + "\n")
+    convs = al.load_chat_jsonl([str(chat)])
+    assert [[m.role for m in c] for c in convs] == [["user", "assistant"]] * 2
+    assert convs[1][1].content == "done"
+    assert len(al.load_chat_jsonl([str(chat)], max_examples=1)) == 1
+    pref = tmp_path / "pref.jsonl"
+    pref.write_text(json.dumps({"prompt": "p", "chosen": "good", "rejected": "bad"}) + "\n")
+    tok = al.ByteTokenizer()
+    (pp,) = al.load_preference_jsonl([str(pref)], tok, "chatml")
+    assert pp.chosen_ids[:len(pp.prompt_ids)] == pp.prompt_ids
+    assert tok.decode(pp.chosen_ids[len(pp.prompt_ids):]) == "good<|im_end|>\n"
+    assert tok.decode(pp.rejected_ids[len(pp.prompt_ids):]) == "bad<|im_end|>\n"
+    assert tok.decode(pp.prompt_ids).endswith("<|im_start|>assistant\n")
+
+
+def test_cli_rejects_lora_and_missing_data():
+    from distrain_b200.cli import main
+    with pytest.raises(SystemExit, match="LoRA"):
+        main(["sft", "--synthetic", "--use-lora"])
+    with pytest.raises(SystemExit, match="datasets"):
+        main(["dpo", "--model-size", "micro", "--device", "cpu"])
