@@ -211,7 +211,8 @@ def fused_cases(iters):
         cos, sin = cos.cuda().contiguous(), sin.cuda().contiguous()
         dq = (torch.randn(M, W, device="cuda") * 0.1).bfloat16()
         db = torch.zeros(W, device="cuda")
-        ms = time_it(lambda: ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d), iters)
+        part = torch.empty(ops.rope_bwd_scratch(M, nh, nkv, d), device="cuda")
+        ms = time_it(lambda: ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d, part=part), iters)
         gbs = 2 * M * W * 2 / ms / 1e6
         out.append({"kernel": "rope_bwd", "case": f"M{M} W{W} (inverse rotation + bias gradient)", "ms": round(ms, 4),
                     "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)})

@@ -138,6 +138,9 @@ class TrainEngine:
         self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
         self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
         self.delta = torch.empty(batch, nh, Tp, dtype=f32, device=dev)
+        # per-block column sums of the QKV bias gradient (RoPE backward)
+        self.rope_part = (torch.empty(ops.rope_bwd_scratch(M, nh, nkv, d), dtype=f32, device=dev)
+                          if cfg.qkv_bias and dev.type == "cuda" else None)
         # dS^T tiles of one layer's attention backward (tcgen05 path): dQ is formed from them by a GEMM-like
         # kernel instead of a second pass over S, P and dP
         self.ds_buf = None
@@ -340,7 +343,8 @@ class TrainEngine:
             attn_ops.attention_bwd(self.qkv[l], self.attn[l], self.dattn, self.lse[l], self.dqkv, self.dq_acc,
                                    self.delta, B=self.B, T=T, nh=nh, nkv=nkv, d=d, impl=self.attn_impl,
                                    ds_buf=self.ds_buf)
-            ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
+            ops.rope_bwd(self.dqkv, gv["qkv_b"], self.cos, self.sin, M=M, T=T, nh=nh, nkv=nkv, d=d,
+                         part=self.rope_part)
             self._col_parallel_dgrad_norm_bwd(
                 self.dqkv, wv["qkv_w"], lambda: ops.linear_wgrad(self.dqkv, self.xn1[l], gv["qkv_w"]),
                 x=self.resid_in[l], rstd=self.rstd1[l], w=pv["attn_norm"], dresid_in=self.dresid,

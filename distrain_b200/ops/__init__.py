@@ -107,9 +107,23 @@ def rope_fwd(qkv, bias, cos, sin, *, M, T, nh, nkv, d, stream=None):
           "dt_rope_fwd")
 
 
-def rope_bwd(dqkv, dbias, cos, sin, *, M, T, nh, nkv, d, stream=None):
-    check(lib().dt_rope_bwd(ptr(dqkv), ptr(dbias), ptr(cos), ptr(sin), M, T, nh, nkv, d, stream_ptr(stream)),
-          "dt_rope_bwd")
+def rope_bwd_scratch(M, nh, nkv, d) -> int:
+    """fp32 elements of the ``part`` scratch of ``rope_bwd`` for M rows."""
+    from ._lib import register
+    import ctypes
+    f = register("dt_rope_bwd_scratch", [ctypes.c_int] * 4, restype=ctypes.c_longlong)
+    return int(f(M, nh, nkv, d))
+
+
+def rope_bwd(dqkv, dbias, cos, sin, *, M, T, nh, nkv, d, part=None, stream=None):
+    """Inverse rotation of the QKV gradient in place; dbias += its column sums. With ``part``
+    (``rope_bwd_scratch`` fp32 elements) the sums go through per-block scratch rows and one reduction
+    kernel instead of atomics on the same addresses from every block."""
+    check(lib().dt_rope_bwd(ptr(dqkv), ptr(dbias), ptr(part), ptr(cos), ptr(sin), M, T, nh, nkv, d,
+                            stream_ptr(stream)), "dt_rope_bwd")
+    if part is not None and dbias is not None:
+        from . import _lib
+        _lib.LAUNCHES[0] += 1  # the column-sum reduction
 
 
 def gemm_qkv_rope(x, w, bias, cos, sin, out, *, T, d, rot_cols, stream=None):

@@ -39,7 +39,7 @@ _SIGS = {
                        c_void],
     "dt_embedding_bwd": [c_void, c_void, c_int, c_int, c_void, c_int, c_int, c_void],
     "dt_rope_fwd": [c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void],
-    "dt_rope_bwd": [c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void],
+    "dt_rope_bwd": [c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void],
     "dt_swiglu_fwd": [c_void, c_void, c_ll, c_int, c_void],
     "dt_gemm_qkv_rope": [c_void, c_ll, c_void, c_ll, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
                          c_int, c_int, c_int, c_void],

@@ -201,12 +201,14 @@ def test_rope_fwd_bwd(nh, nkv, d):
     y = torch.cat([apply_rope(y[:, :, :nh + nkv], cos, sin), y[:, :, nh + nkv:]], dim=2).reshape(M, W)
     g = torch.randn(M, W, device="cuda").bfloat16()
     y.backward(g.float())
-    dq = g.clone()
-    db = torch.zeros(W, device="cuda")
-    ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d)
-    torch.cuda.synchronize()
-    assert _rel(dq, xx.grad.reshape(M, W)) < 8e-3
-    assert _rel(db, bb.grad) < 1e-4
+    # bias gradient by atomics and by per-block scratch rows + one reduction; both add into dbias
+    for part in (None, torch.full((ops.rope_bwd_scratch(M, nh, nkv, d),), float("nan"), device="cuda")):
+        dq = g.clone()
+        db = torch.full((W,), 0.5, device="cuda")
+        ops.rope_bwd(dq, db, cos, sin, M=M, T=T, nh=nh, nkv=nkv, d=d, part=part)
+        torch.cuda.synchronize()
+        assert _rel(dq, xx.grad.reshape(M, W)) < 8e-3
+        assert _rel(db - 0.5, bb.grad) < 1e-4
 
 
 def test_swiglu_fwd_bwd():
