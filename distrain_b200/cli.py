@@ -545,6 +545,50 @@ def cmd_dpo(args):
                                     "pairs_per_sec", "checkpoint"))
 
 
+def cmd_evals(args):
+    """Multiple-choice benchmark scores of checkpoints from local task files (the reference's
+    scripts/run_evals.py)."""
+    from .evaluation import (FULL_TASKS, QUICK_TASKS, evaluate_checkpoint, find_checkpoint, save_result,
+                             summary_table)
+    tasks = QUICK_TASKS if args.quick else ([t.strip() for t in args.tasks.split(",")] if args.tasks else FULL_TASKS)
+    if args.checkpoint:
+        todo = [(args.checkpoint, None)]
+    else:
+        if not args.versions:
+            raise SystemExit("evals: --versions is required with --checkpoint-dir")
+        todo = []
+        for v in (int(x) for x in args.versions.split(",")):
+            try:
+                todo.append((find_checkpoint(args.checkpoint_dir, v), v))
+            except FileNotFoundError as e:
+                print(f"warning: {e}", file=sys.stderr)
+    results = []
+    for ck, v in todo:
+        r = evaluate_checkpoint(ck, tasks, args.task_dir, args.model_size, args.device, args.batch_size,
+                                args.seq_len, args.limit, args.tokenizer, v, args.vocab, args.seed)
+        path = save_result(r, args.output_dir)
+        results.append(r)
+        print(summary_table(r), file=sys.stderr)
+        print(json.dumps({"event": "evals", "checkpoint": ck, "version": v, "results": r["results"],
+                          "output": path}))
+    if args.plot and len(results) > 1:
+        try:
+            import matplotlib
+            matplotlib.use("Agg")
+            import matplotlib.pyplot as plt
+        except ImportError:
+            print("warning: matplotlib is not installed; no plot", file=sys.stderr)
+            return
+        fig, ax = plt.subplots(figsize=(10, 6))
+        for task in tasks:
+            pts = sorted((r["version"], x["acc"]) for r in results for x in r["results"] if x["task"] == task)
+            ax.plot([p[0] for p in pts], [p[1] for p in pts], marker="o", label=task)
+        ax.set_xlabel("checkpoint version")
+        ax.set_ylabel("acc")
+        ax.legend()
+        fig.savefig(os.path.join(args.output_dir, "eval_curves.png"), dpi=150)
+
+
 def cmd_benchmark(args):
     """Measure this device's training step time and the largest batch that fits (calibration)."""
     import torch
@@ -809,6 +853,26 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--max-tokens-cap", type=int, default=1024)
     p.add_argument("--rope-theta", type=float)
     p.set_defaults(fn=cmd_serve)
+
+    p = sp.add_parser("evals", help="multiple-choice benchmark scores of checkpoints (local JSONL task files)")
+    g = p.add_mutually_exclusive_group(required=True)
+    g.add_argument("--checkpoint", help="a safetensors file, or 'random' for an untrained model")
+    g.add_argument("--checkpoint-dir", help="directory of versioned checkpoints (with --versions)")
+    p.add_argument("--versions", help="comma-separated versions under --checkpoint-dir")
+    p.add_argument("--tasks", help="comma-separated task names (default: mmlu, hellaswag, arc_challenge, arc_easy)")
+    p.add_argument("--quick", action="store_true", help="hellaswag only")
+    p.add_argument("--task-dir", default="eval_data", help="directory holding <task>.jsonl files")
+    p.add_argument("--model-size", default="125m", help="preset of the random model")
+    p.add_argument("--vocab", type=int, help="vocabulary of the random model")
+    p.add_argument("--device", default="cuda:0")
+    p.add_argument("--batch-size", type=int, default=8)
+    p.add_argument("--seq-len", type=int, default=512, help="scoring window (longer inputs lose their left end)")
+    p.add_argument("--limit", type=int, help="at most this many examples per task")
+    p.add_argument("--tokenizer", help="tokenizer JSON; default: UTF-8 bytes")
+    p.add_argument("--output-dir", default="eval_results")
+    p.add_argument("--plot", action="store_true", help="accuracy curves over versions (needs matplotlib)")
+    p.add_argument("--seed", type=int, default=0)
+    p.set_defaults(fn=cmd_evals)
 
     for name, fn in (("sft", cmd_sft), ("dpo", cmd_dpo)):
         sft = name == "sft"

@@ -1,0 +1,32 @@
+"""Benchmark scoring on the CUDA engine's forward-only loss pass against the fp32 oracle scorer."""
+import json
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_engine_scores_match_oracle(tmp_path):
+    from distrain_b200 import evaluation as ev
+    from distrain_b200.alignment import ByteTokenizer
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    cfg = ModelConfig(hidden_dim=128, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=256, vocab_size=512,
+                      max_seq_len=128, rope_theta=10000.0)
+    flat = init_flat(ParamLayout(cfg), 0.05, 3)
+    g = torch.Generator().manual_seed(1)
+    seqs = [torch.randint(3, 259, (n,), generator=g).tolist() for n in (40, 65, 9, 100, 64, 12, 77)]
+    starts = [10, 30, 2, 90, 1, 11, 40]
+    gpu = ev.Scorer(cfg, flat, device="cuda:0", batch_size=4, seq_len=65).score(seqs, starts)
+    cpu = ev.Scorer(cfg, flat, device="cpu", batch_size=4, seq_len=65).score(seqs, starts)
+    for a, b, s, st in zip(gpu, cpu, seqs, starts):
+        n = min(len(s), 65) - max(st - max(len(s) - 65, 0), 1)
+        assert abs(a - b) < 0.02 * n + 0.05, (a, b, n)
+    # the same through the command's entry point on a task file
+    (tmp_path / "arc_easy.jsonl").write_text("".join(json.dumps(
+        {"question": f"q{i}", "choices": {"text": ["a", "bb"], "label": ["A", "B"]}, "answerKey": "AB"[i % 2]}) + "\n"
+        for i in range(6)))
+    r_gpu = ev.evaluate_tasks(ev.Scorer(cfg, flat, "cuda:0", 4, 65), ByteTokenizer(), ["arc_easy"], str(tmp_path))
+    r_cpu = ev.evaluate_tasks(ev.Scorer(cfg, flat, "cpu", 4, 65), ByteTokenizer(), ["arc_easy"], str(tmp_path))
+    assert r_gpu[0]["n"] == 6 and abs(r_gpu[0]["acc"] - r_cpu[0]["acc"]) <= 1 / 6 + 1e-9
