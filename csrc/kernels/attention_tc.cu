@@ -186,9 +186,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
   uint64_t* bar = reinterpret_cast<uint64_t*>(sL + 2 * 128);
   uint64_t* q_full = bar;                // [2]
   uint64_t* q_empty = bar + 2;           // [2]
-  uint64_t* kv_full = bar + 4;           // [ST]
-  uint64_t* kv_empty = bar + 4 + C::ST;  // [ST]
-  uint64_t* s_full = bar + 4 + 2 * C::ST;
+  // K and V have rings of their own: a K stage is free once its S = Q K^T has completed, a V stage once
+  // its P V has, so the next K loads start about one softmax phase earlier than with shared stages
+  uint64_t* kv_full = bar + 4;           // [ST] K
+  uint64_t* kv_empty = bar + 4 + C::ST;  // [ST] K
+  uint64_t* v_full = bar + 4 + 2 * C::ST;
+  uint64_t* v_empty = bar + 4 + 3 * C::ST;
+  uint64_t* s_full = bar + 4 + 4 * C::ST;
   uint64_t* s_free = s_full + 1;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = s_full + 3;
@@ -203,7 +207,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
-    for (int i = 0; i < C::ST; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < C::ST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(s_free, FWD_SM_WARPS);
     mbar_init(p_full, FWD_SM_WARPS);
@@ -226,11 +235,26 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
   CTA_TRACE(1);
 
   if (warp == 0) {
-    // ───── TMA producer: per tile its Q (double buffer), then its K/V blocks into the ring ─────
+    // ───── TMA producer: per tile its Q (double buffer), then its K blocks into the K ring; each block's
+    // V follows one step behind its K (V is needed only by P V, after that block's softmax) ─────
     if (lane == 0) {
       tma_prefetch_desc(&tmQKV);
-      int jg = 0, tl = 0;
-      bool ok = true;
+      int nk = 0, nv = 0, tl = 0;  // K / V loads issued, tile counter
+      int v_x = 0, v_j = 0, v_b = 0;
+      bool ok = true, v_pending = false;
+      auto load_v = [&]() -> bool {  // V of global block nv at (column v_x, key block v_j, batch v_b)
+        const int st = nv % C::ST;
+        if (nv >= C::ST &&
+            !mbar_wait_bounded(&v_empty[st], ((nv / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 402, abort_flag))
+          return false;
+        mbar_arrive_expect_tx(&v_full[st], C::TT);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sV + st * C::TT + c * (BKV * 128), &tmQKV, &v_full[st], v_x + 64 * c, v_j * BKV, v_b);
+        ++nv;
+        v_pending = false;
+        return true;
+      };
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tl) {
         const FwdTile w = fwd_tile(t, B, nh, nkv, nqb);
         const int qbuf = tl & 1;
@@ -244,26 +268,31 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
         for (int c = 0; c < D / 64; ++c)
           tma_load_3d(sQ + qbuf * C::TT + c * (BQ * 128), &tmQKV, &q_full[qbuf], w.h * D + 64 * c, w.qb * BQ, w.b);
         const int xk = (nh + w.g) * D, xv = (nh + nkv + w.g) * D;
-        for (int j = 0; j < w.nkb; ++j, ++jg) {
-          const int st = jg % C::ST;
-          if (jg >= C::ST &&
-              !mbar_wait_bounded(&kv_empty[st], ((jg / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag)) {
+        for (int j = 0; j < w.nkb; ++j) {
+          const int st = nk % C::ST;
+          if (nk >= C::ST &&
+              !mbar_wait_bounded(&kv_empty[st], ((nk / C::ST) & 1) ^ 1, DT_ERR_TIMEOUT_EMPTY, 400, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[st], 2 * C::TT);
+          mbar_arrive_expect_tx(&kv_full[st], C::TT);
 #pragma unroll
-          for (int c = 0; c < D / 64; ++c) {
+          for (int c = 0; c < D / 64; ++c)
             tma_load_3d(sK + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xk + 64 * c, j * BKV, w.b);
-            tma_load_3d(sV + st * C::TT + c * (BKV * 128), &tmQKV, &kv_full[st], xv + 64 * c, j * BKV, w.b);
-          }
+          ++nk;
+          if (v_pending && !load_v()) { ok = false; break; }
+          v_x = xv; v_j = j; v_b = w.b;
+          v_pending = true;
         }
       }
+      if (ok && v_pending) ok = load_v();
       if (!ok) {
         // an aborted run: let the loads already issued land before the CTA exits (bounded)
         uint64_t t0 = dt_globaltimer();
-        for (int k = (jg > C::ST ? jg - C::ST : 0); k < jg; ++k)
+        for (int k = (nk > C::ST ? nk - C::ST : 0); k < nk; ++k)
           while (!mbar_try_wait(&kv_full[k % C::ST], (k / C::ST) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
+        for (int k = (nv > C::ST ? nv - C::ST : 0); k < nv; ++k)
+          while (!mbar_try_wait(&v_full[k % C::ST], (k / C::ST) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
         for (int k = (tl > 2 ? tl - 2 : 0); k <= tl && k >= 0; ++k)
           while (!mbar_try_wait(&q_full[k & 1], (k >> 1) & 1) && dt_globaltimer() - t0 < 20000000ull) {}
       }
@@ -289,6 +318,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) umma_bf16(tS, qq + koff(k), kk + koff(k), idS, k > 0 ? 1u : 0u);
         umma_commit(s_full);
+        umma_commit(&kv_empty[jg % C::ST]);  // this K stage is free once S has read it
         ATTN_TRACE(0, jg);
         issued = true;
         return true;
@@ -311,6 +341,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
             if (!issue_s(jg + 1, last ? qbuf ^ 1 : qbuf, last ? tl + 1 : tl, last)) { ok = false; break; }
           }
           if (!mbar_wait_bounded(p_full, jg & 1, DT_ERR_TIMEOUT_FULL, 413, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_bounded(&v_full[st], (jg / C::ST) & 1, DT_ERR_TIMEOUT_FULL, 414, abort_flag)) {
+            ok = false;
+            break;
+          }
           ATTN_TRACE(1, jg);
           tc_fence_after();
           const uint64_t vv = mV0 + (uint64_t)st * STG;
@@ -318,7 +352,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __r
           for (int k = 0; k < BKV / 16; ++k)
             umma_bf16_ts(tO, tP + k * 8, vv + mnoff(k), idO, (j > 0 || k > 0) ? 1u : 0u);
           umma_commit(pv_done);
-          umma_commit(&kv_empty[st]);
+          umma_commit(&v_empty[st]);
         }
         if (tn < ntiles) w = fwd_tile(tn, B, nh, nkv, nqb);
       }
