@@ -9,7 +9,8 @@ lines and behaviour are kept: base / SFT checkpoint or a random model of a prese
 conversations; ``run_dpo.py:40-55``: a 16-token prompt with fixed 16-token chosen and rejected
 continuations), epochs, learning rate, batch size, gradient accumulation, save / log cadence, and a
 ``metrics.json`` in the output directory. Local JSONL files take the place of hub dataset names (no
-network). LoRA (``--use-lora``) is not provided: fine-tuning updates every weight.
+network). ``--use-lora`` trains low-rank adapters on the frozen model (``models/lora.py``) and saves the
+merged model plus the adapters.
 
 Both run on ``TrainEngine`` with per-row loss weights (``loss_weights=True``); the engine's fused
 LM-head / cross-entropy kernel scales each row's gradient by its weight, so neither needs a kernel of
@@ -302,7 +303,10 @@ class SFTConfig:
     log_every_n_steps: int = 10
     output_dir: str = "models/sft"
     seed: int = 0
-    cuda_graph: bool = True  # replay each step as one captured CUDA graph
+    cuda_graph: bool = True  # replay each step as one captured CUDA graph (full fine-tuning)
+    use_lora: bool = False  # train rank-r adapters on the frozen weights instead
+    lora_rank: int = 64
+    lora_alpha: float = 128.0
 
 
 @dataclass
@@ -322,6 +326,9 @@ class DPOConfig:
     output_dir: str = "models/dpo"
     seed: int = 0
     cuda_graph: bool = True
+    use_lora: bool = False
+    lora_rank: int = 64
+    lora_alpha: float = 128.0
 
 
 def step_order(n_items: int, per_step: int, epochs: int, seed: int) -> List[List[int]]:
@@ -354,6 +361,11 @@ class _EngineTrainer:
                                                  grad_clip_norm=c.grad_clip_norm),
                                loss_weights=True)
         self.dev = self.eng.device
+        self.lora = None
+        if c.use_lora:
+            from .models.lora import LoraAdapters
+            self.lora = LoraAdapters(self.eng, c.lora_rank, c.lora_alpha, lr=c.learning_rate,
+                                     weight_decay=c.weight_decay, grad_clip_norm=c.grad_clip_norm, seed=c.seed)
         self.history: List[dict] = []
         os.makedirs(c.output_dir, exist_ok=True)
 
@@ -364,8 +376,12 @@ class _EngineTrainer:
                          c.learning_rate * c.min_lr_fraction)
 
     def _run_step(self, k: int, total: int, weights: torch.Tensor):
-        self.eng.set_lr(self._lr(k, total))
         self.eng.set_loss_weights(weights.to(self.dev))
+        if self.lora is not None:
+            self.lora.set_lr(self._lr(k, total))
+            self.lora.step()
+            return
+        self.eng.set_lr(self._lr(k, total))
         if k == 0 and self.c.cuda_graph and self.dev.type == "cuda":
             self.eng.capture()
         self.eng.step()
@@ -374,13 +390,21 @@ class _EngineTrainer:
         return k == 0 or k + 1 == total or (k + 1) % max(self.c.log_every_n_steps, 1) == 0
 
     def save(self, name: str) -> str:
+        """The model (adapters folded in when training LoRA, whose adapters go to ``adapter_<name>``)."""
         from .utils.checkpoint import save_safetensors
         path = os.path.join(self.c.output_dir, name)
-        save_safetensors(self.eng.state_dict(), path)
+        if self.lora is not None:
+            save_safetensors(self.lora.merged_state_dict(), path)
+            save_safetensors(self.lora.adapter_state_dict(), os.path.join(self.c.output_dir, "adapter_" + name))
+        else:
+            save_safetensors(self.eng.state_dict(), path)
         return path
 
     def _finish(self, metrics: dict) -> dict:
         metrics["checkpoint"] = self.save("model.safetensors")
+        if self.lora is not None:
+            metrics["adapter"] = os.path.join(self.c.output_dir, "adapter_model.safetensors")
+            metrics["trainable_params"] = self.lora.total
         metrics["config"] = asdict(self.c)
         with open(os.path.join(self.c.output_dir, "metrics.json"), "w") as f:
             json.dump(metrics, f, indent=2)

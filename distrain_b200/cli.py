@@ -500,8 +500,6 @@ def _posttrain_done(event, m, keys):
 def cmd_sft(args):
     """Supervised fine-tuning on chat data, loss on the assistant turns (the reference's scripts/run_sft.py)."""
     from .alignment import SFTConfig, SFTTrainer, load_chat_jsonl, synthetic_conversations, tokenize_conversation
-    if args.use_lora:
-        raise SystemExit("sft: LoRA is not provided; fine-tuning updates every weight")
     cfg, flat = _posttrain_model(args, args.base_model)
     tok = _posttrain_tokenizer(args, cfg)
     if args.synthetic:
@@ -514,7 +512,7 @@ def cmd_sft(args):
     c = SFTConfig(learning_rate=args.lr, num_epochs=args.epochs, batch_size=args.batch_size,
                   gradient_accumulation_steps=args.grad_accum, max_seq_len=args.max_seq_len,
                   save_every_n_steps=args.save_every, log_every_n_steps=args.log_every, output_dir=args.output,
-                  seed=args.seed)
+                  seed=args.seed, use_lora=args.use_lora, lora_rank=args.lora_rank, lora_alpha=args.lora_alpha)
     m = SFTTrainer(cfg, flat, examples, c, pad_id=tok.pad_id, device=args.device).train()
     _posttrain_done("sft_done", m, ("steps", "examples", "response_tokens", "first_loss", "final_loss",
                                     "tokens_per_sec", "checkpoint"))
@@ -523,8 +521,6 @@ def cmd_sft(args):
 def cmd_dpo(args):
     """Direct preference optimisation against the frozen starting model (the reference's scripts/run_dpo.py)."""
     from .alignment import DPOConfig, DPOTrainer, load_preference_jsonl, synthetic_preferences
-    if args.use_lora:
-        raise SystemExit("dpo: LoRA is not provided; fine-tuning updates every weight")
     cfg, flat = _posttrain_model(args, args.sft_model)
     pad_id = 0
     if args.synthetic:  # token ids 1..48, no tokenizer
@@ -539,7 +535,7 @@ def cmd_dpo(args):
     c = DPOConfig(beta=args.beta, learning_rate=args.lr, num_epochs=args.epochs, batch_size=args.batch_size,
                   gradient_accumulation_steps=args.grad_accum, max_seq_len=args.max_seq_len,
                   save_every_n_steps=args.save_every, log_every_n_steps=args.log_every, output_dir=args.output,
-                  seed=args.seed)
+                  seed=args.seed, use_lora=args.use_lora, lora_rank=args.lora_rank, lora_alpha=args.lora_alpha)
     m = DPOTrainer(cfg, flat, pairs, c, pad_id=pad_id, device=args.device).train()
     _posttrain_done("dpo_done", m, ("steps", "pairs", "first_loss", "final_loss", "final_reward_accuracy",
                                     "pairs_per_sec", "checkpoint"))
@@ -898,9 +894,9 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("--grad-accum", type=int, default=8 if sft else 16)
         if not sft:
             p.add_argument("--beta", type=float, default=0.1)
-        p.add_argument("--use-lora", action="store_true", help="not provided (fine-tuning updates every weight)")
+        p.add_argument("--use-lora", action="store_true", help="train low-rank adapters on the frozen model")
         p.add_argument("--lora-rank", type=int, default=64)
-        p.add_argument("--lora-alpha", type=int, default=128)
+        p.add_argument("--lora-alpha", type=float, default=128.0)
         p.add_argument("--output", default=f"models/{name}")
         p.add_argument("--save-every", type=int, default=500 if sft else 200)
         p.add_argument("--log-every", type=int, default=10)

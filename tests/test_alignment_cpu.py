@@ -150,9 +150,29 @@ def test_jsonl_loaders(tmp_path):
     assert tok.decode(pp.prompt_ids).endswith("<|im_start|>assistant\n")
 
 
-def test_cli_rejects_lora_and_missing_data():
+def test_cli_rejects_missing_data():
     from distrain_b200.cli import main
-    with pytest.raises(SystemExit, match="LoRA"):
-        main(["sft", "--synthetic", "--use-lora"])
+    with pytest.raises(SystemExit, match="datasets"):
+        main(["sft", "--model-size", "micro", "--vocab", "512", "--device", "cpu", "--use-lora"])
     with pytest.raises(SystemExit, match="datasets"):
         main(["dpo", "--model-size", "micro", "--device", "cpu"])
+
+
+def test_lora_gradients_from_the_weight_gradient():
+    """For y = x W_eff^T with W_eff = W + s B A ([N, K], [N, r], [r, K]) the adapters' gradients are
+    dA = s B^T dW_eff and dB = s dW_eff A^T, the products the LoRA step forms from the engine's weight
+    gradient."""
+    torch.manual_seed(0)
+    N, K, r, s, M = 24, 40, 4, 2.5, 7
+    x = torch.randn(M, K, dtype=torch.float64)
+    W = torch.randn(N, K, dtype=torch.float64)
+    A = torch.randn(r, K, dtype=torch.float64, requires_grad=True)
+    B = torch.randn(N, r, dtype=torch.float64, requires_grad=True)
+    t = torch.randn(M, N, dtype=torch.float64)
+    loss = lambda Weff: ((x @ Weff.t()).tanh() * t).sum()
+    loss(W + s * B @ A).backward()
+    Weff = (W + s * B.detach() @ A.detach()).requires_grad_()
+    loss(Weff).backward()
+    dW = Weff.grad
+    assert torch.allclose(A.grad, s * B.detach().t() @ dW, rtol=1e-12, atol=1e-12)
+    assert torch.allclose(B.grad, s * dW @ A.detach().t(), rtol=1e-12, atol=1e-12)

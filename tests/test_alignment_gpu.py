@@ -114,3 +114,36 @@ def test_dpo_trainer_prefers_the_chosen_response(tmp_path):
     assert m["steps"] == 40
     assert abs(h[0]["loss"] - math.log(2.0)) < 1e-3  # the policy starts as the reference
     assert m["final_reward_accuracy"] == 1.0 and m["final_loss"] < math.log(2.0) - 0.1, h[-1]
+
+
+def test_lora_sft_trains_adapters_on_frozen_weights(tmp_path):
+    """LoRA on the engine: the loss falls, the frozen fp32 weights do not move, the GEMMs' bf16 weights
+    are W + s B A, and the saved model is the merged one (adapters saved beside it)."""
+    from distrain_b200 import alignment as al
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.utils.checkpoint import load_safetensors
+    cfg = _small_cfg()
+    tok = al.ByteTokenizer()
+    ex = [al.tokenize_conversation(c, tok, "chatml", 256) for c in al.synthetic_conversations(20)]
+    c = al.SFTConfig(learning_rate=5e-3, num_epochs=6, batch_size=4, gradient_accumulation_steps=1,
+                     max_seq_len=256, warmup_fraction=0.0, log_every_n_steps=5, save_every_n_steps=0,
+                     output_dir=str(tmp_path), use_lora=True, lora_rank=8, lora_alpha=16.0)
+    flat = init_flat(ParamLayout(cfg), 0.02, 0)
+    tr = al.SFTTrainer(cfg, flat, ex, c, pad_id=tok.pad_id)
+    master0 = tr.eng.master.clone()
+    m = tr.train(log=lambda s: None)
+    assert m["final_loss"] < 0.9 * m["first_loss"], m["history"]
+    assert torch.equal(tr.eng.master, master0)
+    lo = tr.lora
+    l, name, W, A, B, _, _ = lo.items[0]
+    assert B.abs().max().item() > 0
+    exact = W + lo.s * B @ A
+    err = (tr.eng.wv[l][name].float() - exact).abs()
+    assert bool((err <= exact.abs() * 2 ** -8 + 1e-7).all())  # bf16 rounding of W + s B A
+    sd = load_safetensors(m["checkpoint"])
+    merged = lo.merged_state_dict()
+    assert all(torch.equal(sd[k], merged[k]) for k in merged)
+    ad = load_safetensors(m["adapter"])
+    assert set(ad) == {f"layers.{i}.{t}.lora_{x}" for i in range(cfg.num_layers)
+                       for t in ("qkv_w", "o_w", "gu_w", "down_w") for x in "AB"}
+    assert m["trainable_params"] == lo.total and tr.eng.m.numel() == 0
