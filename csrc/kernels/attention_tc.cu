@@ -703,8 +703,11 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_co
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (T + 127) / 128;
-  const int kb = blockIdx.x % nkb;  // key block 0 has the most query blocks: scheduled first
-  const int bg = blockIdx.x / nkb;
+  // level-major order: every (batch, kv head)'s key block 0 (the most query blocks) is dispatched first,
+  // then all key blocks 1, ..., so the last CTAs to start are the shortest (one CTA per SM, not persistent)
+  const int nbg = B * nkv;
+  const int kb = blockIdx.x / nbg;
+  const int bg = blockIdx.x % nbg;
   const int g = bg % nkv, b = bg / nkv;
   const int G = nh / nkv;
   const int nper = nkb - kb;  // causal query blocks kb..nkb-1
@@ -961,8 +964,10 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_con
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = (T + 127) / 128;
-  const int qb = nqb - 1 - (blockIdx.x % nqb);  // long (late) query blocks first
-  const int bh = blockIdx.x / nqb;
+  // level-major order: the last query block (the most key blocks) of every (batch, head) first
+  const int nbh = B * nh;
+  const int qb = nqb - 1 - blockIdx.x / nbh;
+  const int bh = blockIdx.x % nbh;
   const int h = bh % nh, b = bh / nh;
   const int g = h / (nh / nkv);
   const int njb = qb + 1;  // causal key blocks 0..qb
