@@ -77,7 +77,7 @@ class Scorer:
         self.dev = torch.device(device)
         if self.dev.type == "cuda":
             from .models.engine import TrainEngine
-            self.eng = TrainEngine(cfg, batch_size, seq_len, device=device, flat_init=flat)
+            self.eng = TrainEngine(cfg, batch_size, seq_len, device=device, flat_init=flat, inference=True)
         else:
             self.eng = None
             self.params = {k: v.float() for k, v in ParamLayout(cfg).views(flat).items()}

@@ -51,8 +51,11 @@ class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
                  lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False,
-                 grad_accum: int = 1, loss_weights: bool = False):
+                 grad_accum: int = 1, loss_weights: bool = False, inference: bool = False):
+        """``inference``: forward-only engine (``forward_loss``): no gradients, optimizer state or
+        backward scratch, and one set of per-block activation buffers shared by all blocks."""
         self.cfg = cfg
+        self.inference = inference
         self.tp = tp
         self.act_ckpt = act_ckpt
         tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
@@ -74,9 +77,9 @@ class TrainEngine:
         # ── parameters / optimizer state ──
         self.master = torch.zeros(n, dtype=f32, device=dev)
         self.p16 = torch.zeros(n, dtype=bf16, device=dev)
-        self.grad = torch.zeros(n, dtype=f32, device=dev)
-        self.m = torch.zeros(n, dtype=f32, device=dev)
-        self.v = torch.zeros(n, dtype=f32, device=dev)
+        self.grad = None if inference else torch.zeros(n, dtype=f32, device=dev)
+        self.m = None if inference else torch.zeros(n, dtype=f32, device=dev)
+        self.v = None if inference else torch.zeros(n, dtype=f32, device=dev)
         self.cseg, self.cstart, self.cend, self.nseg = L.chunk_tables(dev)
         self.norms = torch.zeros(self.nseg, dtype=f32, device=dev)
         self.hp = torch.zeros(16, dtype=f32, device=dev)
@@ -89,12 +92,12 @@ class TrainEngine:
         # ── activations (saved for backward) ──
         M, Lr = self.M, cfg.num_layers
         Tp = attn_ops.lse_stride(self.T)
-        # with activation checkpointing every block shares one set of buffers (index 0)
-        nb = 1 if act_ckpt else Lr
+        # with activation checkpointing (or forward only) every block shares one set of buffers (index 0)
+        nb = 1 if (act_ckpt or inference) else Lr
 
         def per_block(make):
             bufs = [make() for _ in range(nb)]
-            return bufs * Lr if act_ckpt else bufs
+            return bufs * Lr if nb == 1 else bufs
         self.resid_in = [torch.empty(M, H, dtype=f32, device=dev) for _ in range(Lr)]
         self.resid_mid = per_block(lambda: torch.empty(M, H, dtype=f32, device=dev))
         self.rstd1 = per_block(lambda: torch.empty(M, dtype=f32, device=dev))
@@ -121,10 +124,12 @@ class TrainEngine:
         # carry the normalisation. Without them the loss is the mean over rows.
         self.loss_w = torch.zeros(self.A * M, dtype=f32, device=dev) if loss_weights else None
         # ── backward scratch ──
-        self.br = torch.empty(M, H, dtype=bf16, device=dev)
-        self.dresid = torch.empty(M, H, dtype=f32, device=dev)
-        self.g16 = torch.empty(M, H, dtype=bf16, device=dev)
-        self.dxs = torch.empty(M, H, dtype=bf16, device=dev)
+        bwd_empty = (lambda *shape, dtype=f32: torch.empty(*shape, dtype=dtype, device=dev)) if not inference \
+            else (lambda *shape, dtype=f32: None)
+        self.br = torch.empty(M, H, dtype=bf16, device=dev)  # also the forward's row-parallel GEMM output
+        self.dresid = bwd_empty(M, H)
+        self.g16 = bwd_empty(M, H, dtype=bf16)
+        self.dxs = bwd_empty(M, H, dtype=bf16)
         # SwiGLU fused into the gate/up GEMM's epilogue when F is a multiple of 64 (else a separate
         # activation kernel). The backward's fused form (dh kept in the down-projection data-gradient
         # GEMM, whose epilogue reads the saved gate / up tile by TMA) measured 0.260 ms per tiny layer
@@ -132,19 +137,20 @@ class TrainEngine:
         # 64 KB of gate / up cannot be double-buffered beside the operand ring. It stays selectable.
         self.fused_swiglu = F % 64 == 0
         self.fused_swiglu_bwd = False
-        self.dh = None if self.fused_swiglu_bwd else torch.empty(M, F, dtype=bf16, device=dev)
-        self.dgu = torch.empty(M, 2 * F, dtype=bf16, device=dev)
-        self.dattn = torch.empty(M, nh * d, dtype=bf16, device=dev)
-        self.dqkv = torch.empty(M, self.W, dtype=bf16, device=dev)
-        self.dq_acc = torch.empty(M, nh * d, dtype=f32, device=dev)
-        self.delta = torch.empty(batch, nh, Tp, dtype=f32, device=dev)
+        self.dh = None if self.fused_swiglu_bwd else bwd_empty(M, F, dtype=bf16)
+        self.dgu = bwd_empty(M, 2 * F, dtype=bf16)
+        self.dattn = bwd_empty(M, nh * d, dtype=bf16)
+        self.dqkv = bwd_empty(M, self.W, dtype=bf16)
+        self.dq_acc = bwd_empty(M, nh * d)
+        self.delta = bwd_empty(batch, nh, Tp)
         # per-block column sums of the QKV bias gradient (RoPE backward)
-        self.rope_part = (torch.empty(ops.rope_bwd_scratch(M, nh, nkv, d), dtype=f32, device=dev)
+        self.rope_part = (bwd_empty(ops.rope_bwd_scratch(M, nh, nkv, d))
                           if cfg.qkv_bias and dev.type == "cuda" else None)
         # dS^T tiles of one layer's attention backward (tcgen05 path): dQ is formed from them by a GEMM-like
         # kernel instead of a second pass over S, P and dP
         self.ds_buf = None
-        if attn_ops.bwd_kernel_for(d, attn_impl) == "tc" and d in (64, 128) and dev.type == "cuda":
+        if (not inference and attn_ops.bwd_kernel_for(d, attn_impl) == "tc" and d in (64, 128)
+                and dev.type == "cuda"):
             self.ds_buf = torch.empty(attn_ops.ds_bytes(batch, self.T, nh), dtype=torch.uint8, device=dev)
         if tp is not None:
             from ..parallel.tensor_parallel import norm_weights
@@ -177,7 +183,7 @@ class TrainEngine:
                 "ffn_norm": L.view(self.master, f"{p}.ffn_norm.weight"),
                 "qkv_b": L.group_view(self.master, f"{p}.qkv_b") if cfg.qkv_bias else None,
             }
-            gr = {
+            gr = None if self.grad is None else {
                 "attn_norm": L.view(self.grad, f"{p}.attn_norm.weight"),
                 "ffn_norm": L.view(self.grad, f"{p}.ffn_norm.weight"),
                 "qkv_b": L.group_view(self.grad, f"{p}.qkv_b") if cfg.qkv_bias else None,
@@ -197,11 +203,12 @@ class TrainEngine:
             self.wv.append(w16)
         self.E = L.view(self.master, "embedding.embedding.weight")
         self.E16 = L.view(self.p16, "embedding.embedding.weight")
-        self.gE = L.view(self.grad, "embedding.embedding.weight")
         self.oscale = L.view(self.master, "embedding.output_scale")
-        self.g_oscale = L.view(self.grad, "embedding.output_scale")
         self.fnorm = L.view(self.master, "final_norm.weight")
-        self.g_fnorm = L.view(self.grad, "final_norm.weight")
+        if self.grad is not None:
+            self.gE = L.view(self.grad, "embedding.embedding.weight")
+            self.g_oscale = L.view(self.grad, "embedding.output_scale")
+            self.g_fnorm = L.view(self.grad, "final_norm.weight")
 
     # ───────────────────────── state management ─────────────────────────
     def load_flat(self, flat: torch.Tensor, reset_optimizer: bool = True):
@@ -209,7 +216,7 @@ class TrainEngine:
         with torch.no_grad():
             self.master.copy_(flat.to(self.device, non_blocking=True))
             ops.cast_bf16(self.master, self.p16)
-            if reset_optimizer:
+            if reset_optimizer and self.m is not None:
                 self.m.zero_()
                 self.v.zero_()
                 self.hp.zero_()
@@ -247,6 +254,8 @@ class TrainEngine:
         """Forward + backward of micro-batch ``micro`` (rows [micro*B, (micro+1)*B) of ``ids``), adding its
         gradients into ``grad`` (cleared first when ``zero_grad``); the loss of the step is reduced after
         the last micro-batch."""
+        if self.inference:
+            raise RuntimeError("forward_backward on a forward-only (inference) engine")
         M, Lr = self.M, self.cfg.num_layers
         if self._tp_active() and self.tp.fused:
             self.tp.begin_step(4 * Lr + ((Lr - 1) if self.act_ckpt else 0))

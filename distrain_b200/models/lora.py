@@ -24,9 +24,10 @@ from typing import Dict, List, Tuple
 import torch
 
 from .. import ops
+from .engine import (HP_B1 as _HP_B1, HP_B2 as _HP_B2, HP_CLIP_GLOBAL as _HP_CLIP_GLOBAL, HP_EPS as _HP_EPS,
+                     HP_LR as _HP_LR, HP_MAXNORM as _HP_MAXNORM, HP_WD as _HP_WD, HP_ZERO_GRAD as _HP_ZERO_GRAD)
 
 TARGETS = ("qkv_w", "o_w", "gu_w", "down_w")
-_HP_LR, _HP_B1, _HP_B2, _HP_EPS, _HP_WD, _HP_MAXNORM, _HP_CLIP_GLOBAL, _HP_ZERO_GRAD = 0, 1, 2, 3, 4, 7, 8, 11
 
 
 class LoraAdapters:
@@ -38,7 +39,8 @@ class LoraAdapters:
             raise NotImplementedError("LoRA runs on engines without tensor parallelism")
         self.eng, self.r, self.s = eng, int(rank), float(alpha) / float(rank)
         L, dev = eng.layout, eng.device
-        self.items: List[Tuple[int, str, torch.Tensor, torch.Tensor, torch.Tensor, int, int]] = []
+        # (layer, name, frozen W, A, B, dA, dB) per adapted weight
+        self.items: List[Tuple[int, str, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]] = []
         shapes = []
         for l in range(eng.cfg.num_layers):
             for name in targets:
@@ -57,7 +59,8 @@ class LoraAdapters:
         self.m = torch.zeros(off, dtype=f32, device=dev)
         self.v = torch.zeros(off, dtype=f32, device=dev)
         gen = torch.Generator().manual_seed(seed)
-        segs, starts, ends = [], [], []
+        segs, starts, ends = [], [], []  # AdamW chunk tables: one segment (clipping unit) per A and per B
+        nseg = 0
         for (l, name, N, K), (a, b) in zip(shapes, offs):
             A, B = self.p[a:a + self.r * K].view(self.r, K), self.p[b:b + N * self.r].view(N, self.r)
             gA, gB = self.g[a:a + self.r * K].view(self.r, K), self.g[b:b + N * self.r].view(N, self.r)
@@ -65,17 +68,17 @@ class LoraAdapters:
             W = L.group_view(eng.master, f"layers.{l}.{name}", (N, K))
             self.items.append((l, name, W, A, B, gA, gB))
             for lo, n in ((a, self.r * K), (b, N * self.r)):
-                sid = len(segs) and segs[-1] + 1
                 i = lo
                 while i < lo + n:  # chunks of <= 32768 elements, 4-aligned starts
                     j = min(i + 32768, lo + n)
-                    segs.append(sid)
+                    segs.append(nseg)
                     starts.append(i)
                     ends.append(j)
                     i = j
+                nseg += 1
         t = lambda x, dt: torch.tensor(x, dtype=dt, device=dev)
         self.cseg, self.cstart, self.cend = t(segs, torch.int32), t(starts, torch.int64), t(ends, torch.int64)
-        self.norms = torch.zeros(segs[-1] + 1, dtype=f32, device=dev)
+        self.norms = torch.zeros(nseg, dtype=f32, device=dev)
         self.hp = torch.zeros(16, dtype=f32, device=dev)
         o = eng.optim
         hp = [0.0] * 16
@@ -83,9 +86,8 @@ class LoraAdapters:
         hp[_HP_MAXNORM], hp[_HP_CLIP_GLOBAL], hp[_HP_ZERO_GRAD] = grad_clip_norm, 0.0, 1.0
         hp[_HP_LR] = lr
         self.hp.copy_(torch.tensor(hp))
-        # the frozen weights need no AdamW moments
-        eng.m = torch.zeros(0, dtype=f32, device=dev)
-        eng.v = torch.zeros(0, dtype=f32, device=dev)
+        # the frozen weights need no AdamW moments (the engine's own optimizer step is not used)
+        eng.m = eng.v = None
         self.merge()
 
     def set_lr(self, lr: float):

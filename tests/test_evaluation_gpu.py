@@ -30,3 +30,25 @@ def test_engine_scores_match_oracle(tmp_path):
     r_gpu = ev.evaluate_tasks(ev.Scorer(cfg, flat, "cuda:0", 4, 65), ByteTokenizer(), ["arc_easy"], str(tmp_path))
     r_cpu = ev.evaluate_tasks(ev.Scorer(cfg, flat, "cpu", 4, 65), ByteTokenizer(), ["arc_easy"], str(tmp_path))
     assert r_gpu[0]["n"] == 6 and abs(r_gpu[0]["acc"] - r_cpu[0]["acc"]) <= 1 / 6 + 1e-9
+
+
+def test_inference_engine_matches_training_engine():
+    """The forward-only engine (no gradients, optimizer state or backward scratch; one set of block
+    buffers) gives the training engine's per-row losses bit for bit and refuses a backward."""
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.engine import TrainEngine
+    from distrain_b200.models.params import ParamLayout, init_flat
+    cfg = ModelConfig(hidden_dim=128, num_layers=3, num_heads=4, num_kv_heads=2, ffn_hidden_dim=256, vocab_size=512,
+                      max_seq_len=128, rope_theta=10000.0)
+    flat = init_flat(ParamLayout(cfg), 0.05, 4)
+    tokens = torch.randint(0, 512, (4, 65), dtype=torch.int32).cuda()
+    full = TrainEngine(cfg, 4, 65, device="cuda", flat_init=flat)
+    inf = TrainEngine(cfg, 4, 65, device="cuda", flat_init=flat, inference=True)
+    assert inf.grad is None and inf.m is None and inf.dgu is None and inf.qkv[0] is inf.qkv[2]
+    full.set_tokens(tokens)
+    inf.set_tokens(tokens)
+    a = full.forward_loss(0).clone()
+    b = inf.forward_loss(0).clone()
+    assert torch.equal(a, b)
+    with pytest.raises(RuntimeError):
+        inf.forward_backward()
