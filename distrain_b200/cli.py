@@ -433,6 +433,10 @@ def cmd_baseline(args):
     print(json.dumps({"event": "baseline_done", "steps": args.steps, "output": args.output}))
 
 
+def torch_device_is_cuda(device) -> bool:
+    return bool(device) and str(device).startswith("cuda")
+
+
 def cmd_generate(args):
     """Greedy / temperature sampling by full re-forward (the reference has no KV cache, main.rs:1416-1548)."""
     from .serve import load_model, sample
@@ -444,7 +448,11 @@ def cmd_generate(args):
         from tokenizers import Tokenizer
         tok = Tokenizer.from_file(args.tokenizer)
         ids = tok.encode(args.prompt).ids
-    new, _ = sample(sd, cfg, ids, args.max_tokens, args.temperature, args.seed)
+    lm = None
+    if torch_device_is_cuda(getattr(args, "device", None)):
+        from .serve import EngineLM
+        lm = EngineLM(sd, cfg, args.device, window=len(ids) + args.max_tokens)
+    new, _ = sample(sd, cfg, ids, args.max_tokens, args.temperature, args.seed, lm=lm)
     ids = ids + new
     print(json.dumps({"ids": ids, "text": tok.decode(ids) if tok else None}))
 

@@ -282,6 +282,14 @@ class TrainEngine:
         self._lm_head_loss(micro, ids, backward=False)
         return self.loss_rows[micro * self.M:(micro + 1) * self.M]
 
+    def forward_hidden(self, micro: int = 0) -> torch.Tensor:
+        """Forward only, up to the LM head's input: [B*(S-1), H] bf16 rows (final RMSNorm times the output
+        scale), row b*(S-1) + t for position t of sequence b; logits = rows @ E^T (tied embedding)."""
+        if self._tp_active():
+            raise NotImplementedError("forward_hidden runs on engines without tensor parallelism")
+        self._forward(self.ids[micro * self.B:(micro + 1) * self.B])
+        return self.xs
+
     def _forward(self, ids):
         cfg = self.cfg
         M, H, T, S, d, nh, nkv = self.M, self.H, self.T, self.S, self.d, self.nh, self.nkv

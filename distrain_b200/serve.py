@@ -3,8 +3,11 @@ completion server (``cli.py serve``) on the native HTTP server.
 
 The reference's node samples by re-running the full forward for every new token (no KV cache,
 ``node/cli/src/main.rs:1416-1548``); its serving script (``scripts/serve.py:16,32-37``) exposes an
-OpenAI-style API but imports a package that is not in its repository. Here both use the model's
-plain PyTorch formulation (``models/oracle.py``) on the chosen device.
+OpenAI-style API but imports a package that is not in its repository. Here both re-run the forward
+per token as well: on a GPU through the CUDA engine (``EngineLM``: a forward-only engine over a fixed
+window, the logits of the last real position from its final hidden row and the tied embedding; causal
+attention makes the padding after that position irrelevant), on the CPU through the model's plain
+PyTorch formulation (``models/oracle.py``).
 
 Routes: ``POST /v1/completions`` with {"prompt": text or [token ids], "max_tokens", "temperature",
 "seed", "stop_token"} -> {"id", "object": "text_completion", "created", "model", "choices": [{"text",
@@ -23,11 +26,37 @@ from typing import List, Optional, Tuple
 import torch
 
 
+class EngineLM:
+    """Next-token logits from the CUDA forward of a forward-only engine (one sequence, ``window`` input
+    positions). Longer contexts keep their last ``window`` tokens."""
+
+    def __init__(self, sd, cfg, device: str = "cuda:0", window: int = 1024):
+        from .models.engine import TrainEngine
+        from .models.params import ParamLayout
+        L = ParamLayout(cfg)
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, {k: v.detach().float().cpu() for k, v in sd.items()})
+        cfg.max_seq_len = max(cfg.max_seq_len, window + 1)
+        self.window = int(window)
+        self.eng = TrainEngine(cfg, 1, self.window + 1, device=device, flat_init=flat, inference=True)
+        self.row = torch.zeros(1, self.window + 1, dtype=torch.int32)
+
+    def next_logits(self, seq: List[int]) -> torch.Tensor:
+        """fp32 logits (CPU) of the token after ``seq``."""
+        ctx = seq[-self.window:]
+        self.row.zero_()
+        self.row[0, :len(ctx)] = torch.tensor(ctx, dtype=torch.int32)
+        self.eng.set_tokens(self.row.to(self.eng.device))
+        xs = self.eng.forward_hidden(0)
+        with torch.no_grad():
+            return (xs[len(ctx) - 1:len(ctx)].float() @ self.eng.E.t())[0].cpu()
+
+
 def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, seed: int = 0,
-           stop_token: Optional[int] = None) -> Tuple[List[int], str]:
+           stop_token: Optional[int] = None, lm: Optional[EngineLM] = None) -> Tuple[List[int], str]:
     """Appends up to ``max_tokens`` tokens to ``ids`` (greedy at temperature <= 0, else softmax sampling
     from a generator seeded with ``seed``); returns the new tokens and the finish reason ("length" or
-    "stop")."""
+    "stop"). With ``lm`` the logits come from the CUDA engine, else from the PyTorch formulation."""
     from .models import oracle
     dev = next(iter(sd.values())).device
     g = torch.Generator(device="cpu").manual_seed(int(seed))
@@ -35,8 +64,11 @@ def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, s
     out: List[int] = []
     with torch.no_grad():
         for _ in range(int(max_tokens)):
-            x = torch.tensor([seq[-cfg.max_seq_len:]], device=dev)
-            z = oracle.logits_fn(sd, cfg, x)[0, -1].float().cpu()
+            if lm is not None:
+                z = lm.next_logits(seq)
+            else:
+                x = torch.tensor([seq[-cfg.max_seq_len:]], device=dev)
+                z = oracle.logits_fn(sd, cfg, x)[0, -1].float().cpu()
             if temperature <= 0:
                 nxt = int(z.argmax())
             else:
@@ -68,6 +100,9 @@ class CompletionServer:
     def __init__(self, checkpoint: str, device: str = "cpu", tokenizer: Optional[str] = None,
                  rope_theta: Optional[float] = None, model_name: Optional[str] = None, max_tokens_cap: int = 1024):
         self.sd, self.cfg = load_model(checkpoint, device, rope_theta, min_len=max_tokens_cap + 64)
+        # on a GPU the forward runs on the CUDA engine; its window covers the longest request
+        self.lm = (EngineLM(self.sd, self.cfg, device, window=self.cfg.max_seq_len)
+                   if torch.device(device).type == "cuda" else None)
         self.tok = None
         if tokenizer:
             from tokenizers import Tokenizer
@@ -101,7 +136,7 @@ class CompletionServer:
         stop = req.get("stop_token")
         with self._lock:
             new, reason = sample(self.sd, self.cfg, ids, n, float(req.get("temperature", 0.0)),
-                                 int(req.get("seed", 0)), int(stop) if stop is not None else None)
+                                 int(req.get("seed", 0)), int(stop) if stop is not None else None, lm=self.lm)
         text = self.tok.decode(new) if self.tok is not None else None
         return 200, {"id": f"cmpl-{uuid.uuid4().hex[:24]}", "object": "text_completion", "created": int(time.time()),
                      "model": self.model,
