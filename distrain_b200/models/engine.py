@@ -51,9 +51,12 @@ class TrainEngine:
     def __init__(self, cfg: ModelConfig, batch: int, seq_len: int, optim: Optional[OptimConfig] = None,
                  device="cuda", flat_init: Optional[torch.Tensor] = None, seed: int = 0, init_std: float = 0.02,
                  lm_chunk_rows: int = 32768, attn_impl: str = "dt", tp=None, act_ckpt: bool = False,
-                 grad_accum: int = 1, loss_weights: bool = False, inference: bool = False):
+                 grad_accum: int = 1, loss_weights: bool = False, inference: bool = False,
+                 weights_from: Optional["TrainEngine"] = None):
         """``inference``: forward-only engine (``forward_loss``): no gradients, optimizer state or
-        backward scratch, and one set of per-block activation buffers shared by all blocks."""
+        backward scratch, and one set of per-block activation buffers shared by all blocks.
+        ``weights_from``: an engine of the same model whose fp32 and bf16 weights this one uses (not
+        copies; ``flat_init`` is ignored), e.g. forward-only engines of several sequence lengths."""
         self.cfg = cfg
         self.inference = inference
         self.tp = tp
@@ -75,8 +78,13 @@ class TrainEngine:
         f32, bf16 = torch.float32, torch.bfloat16
         n = L.total
         # ── parameters / optimizer state ──
-        self.master = torch.zeros(n, dtype=f32, device=dev)
-        self.p16 = torch.zeros(n, dtype=bf16, device=dev)
+        if weights_from is not None:
+            if weights_from.layout.total != n or weights_from.device != dev:
+                raise ValueError("weights_from: an engine of another model layout or device")
+            self.master, self.p16 = weights_from.master, weights_from.p16
+        else:
+            self.master = torch.zeros(n, dtype=f32, device=dev)
+            self.p16 = torch.zeros(n, dtype=bf16, device=dev)
         self.grad = None if inference else torch.zeros(n, dtype=f32, device=dev)
         self.m = None if inference else torch.zeros(n, dtype=f32, device=dev)
         self.v = None if inference else torch.zeros(n, dtype=f32, device=dev)
@@ -157,13 +165,16 @@ class TrainEngine:
             self.norm_w = norm_weights(L, dev)
         # ── named views ──
         self._bind_views()
-        if flat_init is None:
-            if tp is not None and tp.size > 1:
-                from ..parallel.tensor_parallel import init_flat_tp
-                flat_init = init_flat_tp(L, init_std, seed, device=dev)
-            else:
-                flat_init = init_flat(L, init_std, seed)
-        self.load_flat(flat_init)
+        if weights_from is not None:
+            self._write_hp(self.optim.lr)
+        else:
+            if flat_init is None:
+                if tp is not None and tp.size > 1:
+                    from ..parallel.tensor_parallel import init_flat_tp
+                    flat_init = init_flat_tp(L, init_std, seed, device=dev)
+                else:
+                    flat_init = init_flat(L, init_std, seed)
+            self.load_flat(flat_init)
         self.graph = None
         self.kernels_per_step = 0
 

@@ -27,8 +27,12 @@ import torch
 
 
 class EngineLM:
-    """Next-token logits from the CUDA forward of a forward-only engine (one sequence, ``window`` input
-    positions). Longer contexts keep their last ``window`` tokens."""
+    """Next-token logits from the CUDA forward of forward-only engines (one sequence each). Each context
+    runs on the smallest of the power-of-two windows (128 .. ``window`` input positions) that holds it,
+    so a token costs a forward over about its context, not over the longest one; the engines are made on
+    first use and share one copy of the weights. Longer contexts keep their last ``window`` tokens."""
+
+    MIN_WINDOW = 128
 
     def __init__(self, sd, cfg, device: str = "cuda:0", window: int = 1024):
         from .models.engine import TrainEngine
@@ -37,19 +41,36 @@ class EngineLM:
         flat = torch.zeros(L.total)
         L.load_state_dict(flat, {k: v.detach().float().cpu() for k, v in sd.items()})
         cfg.max_seq_len = max(cfg.max_seq_len, window + 1)
-        self.window = int(window)
-        self.eng = TrainEngine(cfg, 1, self.window + 1, device=device, flat_init=flat, inference=True)
-        self.row = torch.zeros(1, self.window + 1, dtype=torch.int32)
+        self.cfg, self.device, self.window = cfg, device, int(window)
+        self.windows = []
+        w = min(self.MIN_WINDOW, self.window)
+        while w < self.window:
+            self.windows.append(w)
+            w *= 2
+        self.windows.append(self.window)
+        # the largest engine holds the weights; the others are made when a context first fits them
+        self.engines = {self.window: TrainEngine(cfg, 1, self.window + 1, device=device, flat_init=flat,
+                                                 inference=True)}
+        self.eng = self.engines[self.window]
+
+    def _engine(self, n: int):
+        w = next(w for w in self.windows if w >= n)
+        if w not in self.engines:
+            from .models.engine import TrainEngine
+            self.engines[w] = TrainEngine(self.cfg, 1, w + 1, device=self.device, inference=True,
+                                          weights_from=self.eng)
+        return self.engines[w]
 
     def next_logits(self, seq: List[int]) -> torch.Tensor:
         """fp32 logits (CPU) of the token after ``seq``."""
         ctx = seq[-self.window:]
-        self.row.zero_()
-        self.row[0, :len(ctx)] = torch.tensor(ctx, dtype=torch.int32)
-        self.eng.set_tokens(self.row.to(self.eng.device))
-        xs = self.eng.forward_hidden(0)
+        eng = self._engine(len(ctx))
+        row = torch.zeros(1, eng.S, dtype=torch.int32)
+        row[0, :len(ctx)] = torch.tensor(ctx, dtype=torch.int32)
+        eng.set_tokens(row.to(eng.device))
+        xs = eng.forward_hidden(0)
         with torch.no_grad():
-            return (xs[len(ctx) - 1:len(ctx)].float() @ self.eng.E.t())[0].cpu()
+            return (xs[len(ctx) - 1:len(ctx)].float() @ eng.E.t())[0].cpu()
 
 
 def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, seed: int = 0,

@@ -23,15 +23,20 @@ def test_engine_logits_match_oracle(tmp_path):
     from distrain_b200.models import oracle
     from distrain_b200.serve import EngineLM
     cfg, sd, _ = _model(tmp_path)
-    lm = EngineLM(sd, cfg, "cuda:0", window=96)
+    W = 300  # windows 128, 256 and 300
+    lm = EngineLM(sd, cfg, "cuda:0", window=W)
     g = torch.Generator().manual_seed(0)
-    for n in (1, 7, 64, 96, 130):  # 130 > window: the last 96 tokens are the context
+    for n in (1, 7, 128, 130, 256, 300, 400):  # 400 > window: the last 300 tokens are the context
         seq = torch.randint(0, 512, (n,), generator=g).tolist()
         z = lm.next_logits(seq)
-        ctx = torch.tensor([seq[-96:]])
+        ctx = torch.tensor([seq[-W:]])
         ref = oracle.logits_fn({k: v.float() for k, v in sd.items()}, cfg, ctx, mask_value=None)[0, -1]
         rel = ((z - ref).norm() / ref.norm()).item()
         assert rel < 3e-2, (n, rel)
+    # one engine per window, all on the same weights
+    assert sorted(lm.engines) == [128, 256, 300]
+    assert all(e.master.data_ptr() == lm.eng.master.data_ptr() and e.p16.data_ptr() == lm.eng.p16.data_ptr()
+               for e in lm.engines.values())
 
 
 def test_completion_server_on_gpu(tmp_path):
