@@ -42,16 +42,20 @@ class EngineLM:
         L.load_state_dict(flat, {k: v.detach().float().cpu() for k, v in sd.items()})
         cfg.max_seq_len = max(cfg.max_seq_len, window + 1)
         self.cfg, self.device, self.window = cfg, device, int(window)
-        self.windows = []
-        w = min(self.MIN_WINDOW, self.window)
-        while w < self.window:
-            self.windows.append(w)
-            w *= 2
-        self.windows.append(self.window)
+        self.windows = self.window_sizes(self.window)
         # the largest engine holds the weights; the others are made when a context first fits them
         self.engines = {self.window: TrainEngine(cfg, 1, self.window + 1, device=device, flat_init=flat,
                                                  inference=True)}
         self.eng = self.engines[self.window]
+
+    @classmethod
+    def window_sizes(cls, window: int) -> List[int]:
+        """Powers of two from MIN_WINDOW below ``window``, then ``window`` itself."""
+        out, w = [], min(cls.MIN_WINDOW, window)
+        while w < window:
+            out.append(w)
+            w *= 2
+        return out + [window]
 
     def _engine(self, n: int):
         w = next(w for w in self.windows if w >= n)

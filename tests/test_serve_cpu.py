@@ -63,3 +63,12 @@ def test_server_round_trip(ckpt):
             assert json.loads(r.read())["status"] == "ok"
     finally:
         srv.stop()
+
+
+def test_engine_window_ladder():
+    """Forward windows of the GPU sampler: powers of two from 128 up to the longest context."""
+    from distrain_b200.serve import EngineLM
+    assert EngineLM.window_sizes(300) == [128, 256, 300]
+    assert EngineLM.window_sizes(128) == [128]
+    assert EngineLM.window_sizes(100) == [100]
+    assert EngineLM.window_sizes(4096) == [128, 256, 512, 1024, 2048, 4096]
