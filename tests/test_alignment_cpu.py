@@ -176,3 +176,56 @@ def test_lora_gradients_from_the_weight_gradient():
     dW = Weff.grad
     assert torch.allclose(A.grad, s * B.detach().t() @ dW, rtol=1e-12, atol=1e-12)
     assert torch.allclose(B.grad, s * dW @ A.detach().t(), rtol=1e-12, atol=1e-12)
+
+
+def test_lora_tables_merge_and_checkpoint_on_cpu():
+    """LoRA bookkeeping without a GPU, on a stand-in engine built from the parameter layout: the AdamW
+    chunk tables cover every adapter exactly once (4-aligned starts, one clipping segment per A and per
+    B), merge() writes bf16(W + s B A) into the weights the GEMMs read while the fp32 weights stay, and
+    the saved model is W + s B A."""
+    import types
+    from distrain_b200.config import OptimConfig
+    from distrain_b200.models.lora import TARGETS, LoraAdapters
+    from distrain_b200.models.params import ParamLayout, init_flat
+    cfg = _cfg()
+    L = ParamLayout(cfg)
+    master = init_flat(L, 0.02, 0)
+    p16 = master.bfloat16()
+    grad = torch.zeros_like(master)
+    H, F, d = cfg.hidden_dim, cfg.ffn_hidden_dim, cfg.head_dim()
+    W = (cfg.num_heads + 2 * cfg.num_kv_heads) * d
+    shp = {"qkv_w": (W, H), "o_w": (H, cfg.num_heads * d), "gu_w": (2 * F, H), "down_w": (H, F)}
+    views = lambda buf: [{t: L.group_view(buf, f"layers.{i}.{t}", shp[t]) for t in TARGETS}
+                         for i in range(cfg.num_layers)]
+    eng = types.SimpleNamespace(tp=None, layout=L, device=torch.device("cpu"), cfg=cfg, optim=OptimConfig(),
+                                master=master, p16=p16, gv=views(grad), wv=views(p16), m=None, v=None)
+    r = 4
+    lo = LoraAdapters(eng, rank=r, alpha=8.0, seed=1)
+    assert lo.s == 2.0 and len(lo.items) == cfg.num_layers * len(TARGETS)
+    # chunk tables: disjoint, 4-aligned, covering exactly the A and B ranges, one segment each
+    covered = torch.zeros(lo.total, dtype=torch.int32)
+    for s0, e0 in zip(lo.cstart.tolist(), lo.cend.tolist()):
+        assert s0 % 4 == 0 and e0 > s0 and e0 - s0 <= 32768
+        covered[s0:e0] += 1
+    want = torch.zeros(lo.total, dtype=torch.int32)
+    for _, _, Wt, A, B, _, _ in lo.items:
+        for t in (A, B):
+            off = t.data_ptr() // 4 - lo.p.data_ptr() // 4
+            want[off:off + t.numel()] = 1
+    assert torch.equal(covered, want)
+    assert lo.norms.numel() == 2 * len(lo.items) == int(lo.cseg.max()) + 1
+    # merge with non-zero B: bf16 weights of the GEMMs = W + s B A; fp32 weights unchanged
+    m0 = master.clone()
+    for _, _, _, A, B, _, _ in lo.items:
+        B.copy_(torch.randn(B.shape) * 0.1)
+    lo.merge()
+    assert torch.equal(master, m0)
+    for l, name, Wt, A, B, _, _ in lo.items:
+        assert torch.equal(eng.wv[l][name], torch.addmm(Wt, B, A, alpha=lo.s).bfloat16())
+    sd = lo.merged_state_dict()
+    ref = L.to_state_dict(m0)
+    changed = [k for k in sd if not torch.equal(sd[k], ref[k])]
+    assert changed and all(any(t in k for t in ("q_proj", "k_proj", "v_proj", "o_proj", "gate", "up", "down"))
+                           for k in changed), changed
+    ad = lo.adapter_state_dict()
+    assert len(ad) == 2 * len(lo.items) and ad["layers.0.qkv_w.lora_A"].shape == (r, H)
