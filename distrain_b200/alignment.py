@@ -386,6 +386,10 @@ class _EngineTrainer:
             self.eng.capture()
         self.eng.step()
 
+    def _sync(self):
+        if self.dev.type == "cuda":
+            torch.cuda.synchronize(self.dev)
+
     def _want_log(self, k: int, total: int) -> bool:
         return k == 0 or k + 1 == total or (k + 1) % max(self.c.log_every_n_steps, 1) == 0
 
@@ -436,7 +440,7 @@ class SFTTrainer(_EngineTrainer):
                 log(json.dumps({"event": "sft", **rec}))
             if c.save_every_n_steps and (k + 1) % c.save_every_n_steps == 0:
                 self.save(f"step_{k + 1}.safetensors")
-        torch.cuda.synchronize(self.dev) if self.dev.type == "cuda" else None
+        self._sync()
         dt = time.perf_counter() - t0
         return self._finish({"steps": total, "epochs": c.num_epochs, "examples": len(self.examples),
                              "response_tokens": resp, "tokens_per_sec": total * self.B * self.A * self.S / dt,
@@ -494,7 +498,7 @@ class DPOTrainer(_EngineTrainer):
                 log(json.dumps({"event": "dpo", **rec}))
             if c.save_every_n_steps and (k + 1) % c.save_every_n_steps == 0:
                 self.save(f"step_{k + 1}.safetensors")
-        torch.cuda.synchronize(self.dev) if self.dev.type == "cuda" else None
+        self._sync()
         dt = time.perf_counter() - t0
         return self._finish({"steps": total, "epochs": c.num_epochs, "pairs": len(self.pairs),
                              "pairs_per_sec": total * self.per_step / dt,
