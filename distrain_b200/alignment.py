@@ -345,9 +345,74 @@ def step_order(n_items: int, per_step: int, epochs: int, seed: int) -> List[List
     return out
 
 
+class OracleEngine:
+    """The subset of ``TrainEngine`` the trainers use, on the CPU: the fp32 PyTorch formulation of the
+    model (``models/oracle.py``) with autograd and the reference optimiser's AdamW (per-tensor
+    clipping), the same per-row loss weights and the same forward-only per-row losses. The reference's
+    post-training scripts default to the CPU for their synthetic smoke runs; this keeps ``sft`` / ``dpo``
+    usable there (slowly)."""
+
+    def __init__(self, cfg, batch: int, seq_len: int, optim, flat_init: torch.Tensor, grad_accum: int = 1,
+                 loss_weights: bool = True):
+        from .models.oracle import AdamWRef
+        from .models.params import ParamLayout
+        self.cfg, self.B, self.S, self.A, self.T = cfg, batch, seq_len, max(int(grad_accum), 1), seq_len - 1
+        self.device = torch.device("cpu")
+        self.params = {k: v.detach().clone().float().requires_grad_() for k, v in
+                       ParamLayout(cfg).views(flat_init).items()}
+        self.opt = AdamWRef(self.params, lr=optim.lr, betas=(optim.beta1, optim.beta2), eps=optim.eps,
+                            weight_decay=optim.weight_decay, clip=optim.grad_clip_norm,
+                            clip_global=optim.clip_global)
+        self.lr = optim.lr
+        self.ids = torch.zeros(self.A * batch, seq_len, dtype=torch.int32)
+        self.loss_w = torch.zeros(self.A * batch * self.T) if loss_weights else None
+        self.loss = torch.zeros(4)
+        self.graph = None
+
+    def set_tokens(self, tokens: torch.Tensor):
+        self.ids.copy_(tokens)
+
+    def set_loss_weights(self, w: torch.Tensor):
+        self.loss_w.copy_(w.reshape(-1).float())
+
+    def set_lr(self, lr: float):
+        self.lr = lr
+
+    def _row_ce(self, micro: int) -> torch.Tensor:
+        from .models import oracle
+        ids = self.ids[micro * self.B:(micro + 1) * self.B].long()
+        z = oracle.logits_fn(self.params, self.cfg, ids[:, :-1], mask_value=None)
+        return -torch.log_softmax(z.float(), dim=-1).gather(-1, ids[:, 1:, None])[..., 0]
+
+    def forward_loss(self, micro: int = 0) -> torch.Tensor:
+        with torch.no_grad():
+            return self._row_ce(micro).reshape(-1)
+
+    def step(self):
+        n = self.B * self.T
+        total = 0.0
+        for a in range(self.A):
+            w = (self.loss_w[a * n:(a + 1) * n].view(self.B, self.T) if self.loss_w is not None
+                 else torch.full((self.B, self.T), 1.0 / (n * self.A)))
+            ce = self._row_ce(a)
+            l = (w * torch.where(w != 0, ce, torch.zeros_like(ce))).sum()
+            l.backward()
+            total += float(l.detach())
+        finite = math.isfinite(total)
+        self.loss[0], self.loss[1] = total, 0.0 if finite else 1.0
+        if finite:
+            self.opt.step(self.lr)
+        else:  # skipped like a non-finite step on the GPU
+            for q in self.params.values():
+                q.grad = None
+
+    def state_dict(self) -> Dict[str, torch.Tensor]:
+        return {k: v.detach().float().cpu().clone() for k, v in self.params.items()}
+
+
 class _EngineTrainer:
-    """What both trainers share: a TrainEngine with per-row loss weights, the learning-rate schedule,
-    checkpoints and the metrics file."""
+    """What both trainers share: a TrainEngine with per-row loss weights (``OracleEngine`` on the CPU),
+    the learning-rate schedule, checkpoints and the metrics file."""
 
     def __init__(self, model_cfg, flat: torch.Tensor, batch: int, c, device: str):
         from .config import OptimConfig
@@ -356,10 +421,14 @@ class _EngineTrainer:
             model_cfg.max_seq_len = c.max_seq_len
         self.cfg, self.c, self.B, self.A = model_cfg, c, batch, c.gradient_accumulation_steps
         self.S = c.max_seq_len
-        self.eng = TrainEngine(model_cfg, batch, self.S, device=device, flat_init=flat, grad_accum=self.A,
-                               optim=OptimConfig(lr=c.learning_rate, weight_decay=c.weight_decay,
-                                                 grad_clip_norm=c.grad_clip_norm),
-                               loss_weights=True)
+        optim = OptimConfig(lr=c.learning_rate, weight_decay=c.weight_decay, grad_clip_norm=c.grad_clip_norm)
+        if torch.device(device).type == "cpu":
+            if c.use_lora:
+                raise ValueError("LoRA adapters train on the CUDA engine: use a cuda device")
+            self.eng = OracleEngine(model_cfg, batch, self.S, optim, flat, grad_accum=self.A)
+        else:
+            self.eng = TrainEngine(model_cfg, batch, self.S, device=device, flat_init=flat, grad_accum=self.A,
+                                   optim=optim, loss_weights=True)
         self.dev = self.eng.device
         self.lora = None
         if c.use_lora:

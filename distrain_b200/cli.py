@@ -888,7 +888,7 @@ def build_parser() -> argparse.ArgumentParser:
             p.add_argument("--sft-model", help="starting checkpoint (safetensors); default: a random model")
         p.add_argument("--model-size", default="125m", help="preset of the random model (125m, 1b, 7b, 13b, ...)")
         p.add_argument("--vocab", type=int, help="vocabulary of the random model")
-        p.add_argument("--device", default="cuda:0")
+        p.add_argument("--device", default="cuda:0", help="cuda:N (the CUDA engine) or cpu (the fp32 formulation)")
         p.add_argument("--datasets", help="comma-separated JSONL files")
         p.add_argument("--synthetic", action="store_true", help="the built-in synthetic data")
         p.add_argument("--max-examples", type=int, help="at most this many examples per file")

@@ -229,3 +229,38 @@ def test_lora_tables_merge_and_checkpoint_on_cpu():
                            for k in changed), changed
     ad = lo.adapter_state_dict()
     assert len(ad) == 2 * len(lo.items) and ad["layers.0.qkv_w.lora_A"].shape == (r, H)
+
+
+def test_sft_and_dpo_run_on_the_cpu(tmp_path):
+    """The trainers on the CPU engine (fp32 formulation, autograd, the reference AdamW): SFT lowers the
+    response loss, DPO starts at log 2 and learns to prefer the chosen continuation, and both write
+    their checkpoint and metrics."""
+    import math
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.utils.checkpoint import load_safetensors
+    cfg = ModelConfig(hidden_dim=32, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=64, vocab_size=260,
+                      max_seq_len=256, rope_theta=10000.0)
+    tok = al.ByteTokenizer()
+    ex = [al.tokenize_conversation(c, tok, "zephyr", 96) for c in al.synthetic_conversations(4)]
+    c = al.SFTConfig(learning_rate=1e-2, num_epochs=8, batch_size=2, gradient_accumulation_steps=2, max_seq_len=96,
+                     warmup_fraction=0.0, log_every_n_steps=1, save_every_n_steps=0,
+                     output_dir=str(tmp_path / "sft"))
+    tr = al.SFTTrainer(cfg, init_flat(ParamLayout(cfg), 0.05, 0), ex, c, pad_id=tok.pad_id, device="cpu")
+    m = tr.train(log=lambda s: None)
+    assert m["steps"] == 8 and m["final_loss"] < 0.8 * m["first_loss"], m["history"]
+    sd = load_safetensors(m["checkpoint"])
+    assert set(sd) == set(ParamLayout(cfg).shapes())
+    d = al.DPOConfig(beta=0.5, learning_rate=1e-2, num_epochs=6, batch_size=2, gradient_accumulation_steps=1,
+                     max_seq_len=40, warmup_fraction=0.0, log_every_n_steps=1, save_every_n_steps=0,
+                     output_dir=str(tmp_path / "dpo"))
+    cfg2 = ModelConfig(hidden_dim=32, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=64, vocab_size=64,
+                       max_seq_len=64, rope_theta=10000.0)
+    dp = al.DPOTrainer(cfg2, init_flat(ParamLayout(cfg2), 0.05, 1), al.synthetic_preferences(4), d, device="cpu")
+    m2 = dp.train(log=lambda s: None)
+    h = m2["history"]
+    assert abs(h[0]["loss"] - math.log(2.0)) < 1e-6
+    assert m2["final_reward_accuracy"] == 1.0 and m2["final_loss"] < math.log(2.0), h[-1]
+    with pytest.raises(ValueError, match="LoRA"):
+        al.SFTTrainer(cfg, init_flat(ParamLayout(cfg), 0.05, 0), ex,
+                      al.SFTConfig(use_lora=True, max_seq_len=96, output_dir=str(tmp_path / "x")), device="cpu")
