@@ -157,10 +157,25 @@ def synthetic_conversations(num_examples: int = 100) -> List[List[Message]]:
     return out
 
 
+_ROLES = {"system": "system", "user": "user", "human": "user", "assistant": "assistant", "gpt": "assistant"}
+
+
+def _messages(turns) -> List[Message]:
+    """Turns as ``{"role", "content"}`` or ShareGPT-style ``{"from": "system" | "human" | "gpt", "value"}``."""
+    out = []
+    for m in turns:
+        role = m.get("role", m.get("from"))
+        if role not in _ROLES:
+            raise ValueError(f"unknown role {role!r}")
+        out.append(Message(_ROLES[role], m.get("content", m.get("value"))))
+    return out
+
+
 def load_chat_jsonl(paths: Sequence[str], max_examples: Optional[int] = None) -> List[List[Message]]:
-    """Conversations from JSONL files, one per line: ``{"messages": [{"role", "content"}, ...]}`` or
-    ``{"prompt": ..., "response": ...}`` (also ``instruction`` / ``output``), at most ``max_examples``
-    per file."""
+    """Conversations from JSONL files, one per line: ``{"messages": [{"role", "content"}, ...]}``,
+    ShareGPT-style ``{"conversations": [{"from": "system" | "human" | "gpt", "value"}, ...]}`` (the
+    layout of OpenHermes-2.5 and SlimOrca dumps) or ``{"prompt": ..., "response": ...}`` (also
+    ``instruction`` / ``output``), at most ``max_examples`` per file."""
     out: List[List[Message]] = []
     for p in paths:
         n = 0
@@ -169,8 +184,8 @@ def load_chat_jsonl(paths: Sequence[str], max_examples: Optional[int] = None) ->
                 if not line.strip():
                     continue
                 r = json.loads(line)
-                if "messages" in r:
-                    conv = [Message(m["role"], m["content"]) for m in r["messages"]]
+                if "messages" in r or "conversations" in r:
+                    conv = _messages(r.get("messages", r.get("conversations")))
                 else:
                     prompt = r.get("prompt", r.get("instruction"))
                     resp = r.get("response", r.get("output"))
@@ -201,10 +216,32 @@ def synthetic_preferences(num_examples: int = 50) -> List[PreferencePair]:
             for _ in range(num_examples)]
 
 
+def _preference_turns(r: dict) -> Tuple[List[Message], str, str]:
+    """(context turns, chosen response, rejected response) of one preference line."""
+    ch, rj = r["chosen"], r["rejected"]
+    if isinstance(ch, list):  # whole conversations ending in the two assistant answers
+        cm, rm = _messages(ch), _messages(rj)
+        if not cm or cm[-1].role != "assistant" or not rm or rm[-1].role != "assistant":
+            raise ValueError("chosen / rejected conversations must end with an assistant turn")
+        return cm[:-1], cm[-1].content, rm[-1].content
+    prompt = r["prompt"]
+    context = _messages(prompt) if isinstance(prompt, list) else [Message("user", prompt)]
+    return context, ch, rj
+
+
+def _preference_ids(context: List[Message], resp: str, tok, template: str) -> Tuple[List[int], List[int]]:
+    """(prompt ids: everything the template renders before the final answer, answer ids)."""
+    segs = render_chat(list(context) + [Message("assistant", resp)], template)
+    last = max(i for i, (_, tr) in enumerate(segs) if tr)
+    return sum((tok.encode(t) for t, _ in segs[:last]), []), tok.encode(segs[last][0])
+
+
 def load_preference_jsonl(paths: Sequence[str], tok, template: str = "chatml",
                           max_examples: Optional[int] = None) -> List[PreferencePair]:
-    """Pairs from JSONL lines ``{"prompt": str, "chosen": str, "rejected": str}``: the prompt rendered as
-    a user turn of the chat template, each response as the assistant turn that follows it."""
+    """Pairs from JSONL lines ``{"prompt": str | [turns], "chosen": str, "rejected": str}`` (the prompt
+    as the context turns of the chat template, each response as the assistant turn that follows) or
+    ``{"chosen": [turns], "rejected": [turns]}`` whose two conversations share all but their last,
+    assistant, turn (the layout of binarized preference sets)."""
     out: List[PreferencePair] = []
     for p in paths:
         n = 0
@@ -212,14 +249,10 @@ def load_preference_jsonl(paths: Sequence[str], tok, template: str = "chatml",
             for line in f:
                 if not line.strip():
                     continue
-                r = json.loads(line)
-                segs = render_chat([Message("user", r["prompt"]), Message("assistant", "")], template)
-                prompt = sum((tok.encode(t) for t, tr in segs if not tr), [])
-
-                def full(resp):
-                    s = render_chat([Message("user", r["prompt"]), Message("assistant", resp)], template)
-                    return prompt + sum((tok.encode(t) for t, tr in s if tr), [])
-                out.append(PreferencePair(prompt, full(r["chosen"]), full(r["rejected"])))
+                context, chosen, rejected = _preference_turns(json.loads(line))
+                prompt, c_ids = _preference_ids(context, chosen, tok, template)
+                _, r_ids = _preference_ids(context, rejected, tok, template)
+                out.append(PreferencePair(prompt, prompt + c_ids, prompt + r_ids))
                 n += 1
                 if max_examples is not None and n >= max_examples:
                     break

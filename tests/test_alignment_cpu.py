@@ -264,3 +264,31 @@ def test_sft_and_dpo_run_on_the_cpu(tmp_path):
     with pytest.raises(ValueError, match="LoRA"):
         al.SFTTrainer(cfg, init_flat(ParamLayout(cfg), 0.05, 0), ex,
                       al.SFTConfig(use_lora=True, max_seq_len=96, output_dir=str(tmp_path / "x")), device="cpu")
+
+
+def test_sharegpt_and_conversation_preference_layouts(tmp_path):
+    tok = al.ByteTokenizer()
+    chat = tmp_path / "hermes.jsonl"
+    chat.write_text(json.dumps({"conversations": [{"from": "system", "value": "s"}, {"from": "human", "value": "q"},
+                                                  {"from": "gpt", "value": "a"}]}) + "\n")
+    (conv,) = al.load_chat_jsonl([str(chat)])
+    assert [(m.role, m.content) for m in conv] == [("system", "s"), ("user", "q"), ("assistant", "a")]
+    bad = tmp_path / "bad.jsonl"
+    bad.write_text(json.dumps({"conversations": [{"from": "robot", "value": "x"}]}) + "\n")
+    with pytest.raises(ValueError, match="robot"):
+        al.load_chat_jsonl([str(bad)])
+    # binarized layout: two conversations sharing a multi-turn context, different last answers
+    ctx = [{"role": "user", "content": "hi"}, {"role": "assistant", "content": "hello"},
+           {"role": "user", "content": "more"}]
+    pref = tmp_path / "pref.jsonl"
+    pref.write_text(json.dumps({"chosen": ctx + [{"role": "assistant", "content": "good"}],
+                                "rejected": ctx + [{"role": "assistant", "content": "bad"}]}) + "\n"
+                    + json.dumps({"prompt": ctx, "chosen": "good", "rejected": "bad"}) + "\n")
+    a, b = al.load_preference_jsonl([str(pref)], tok, "chatml")
+    assert a == b
+    text = tok.decode(a.prompt_ids)
+    assert "hello" in text and text.endswith("more<|im_end|>\n<|im_start|>assistant\n")  # earlier answer is context
+    assert tok.decode(a.chosen_ids[len(a.prompt_ids):]) == "good<|im_end|>\n"
+    assert tok.decode(a.rejected_ids[len(a.prompt_ids):]) == "bad<|im_end|>\n"
+    ids, mask = al.pair_rows([a], 256, 0)
+    assert int(mask[0].sum()) == len(a.chosen_ids) - len(a.prompt_ids)
