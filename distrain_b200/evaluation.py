@@ -8,7 +8,8 @@ untrained model of ``--model-size``), or ``--checkpoint-dir`` with ``--versions`
 summary table. Task data are local JSONL files (``<task-dir>/<task>.jsonl``) in place of hub downloads:
 one example per line, in the generic form ``{"context", "choices", "label"}`` or in the field layouts of
 the usual sources (HellaSwag: ctx / endings / label; ARC: question / choices{text, label} / answerKey;
-MMLU: question / choices / answer).
+MMLU: question / choices / answer; PIQA: goal / sol1 / sol2 / label; Winogrande: sentence / option1 /
+option2 / answer, scored by the sentence's remainder after each option fills its blank).
 
 Scoring follows the usual log-likelihood protocol: each choice is appended, after a space, to the
 context and scored by the sum of its tokens' log-probabilities; ``acc`` is the argmax of that sum,
@@ -41,16 +42,32 @@ def normalize_example(r: dict) -> Tuple[str, List[str], int]:
     if "question" in r and "choices" in r and "answer" in r:  # MMLU
         a = r["answer"]
         return f"{r['question']}\nAnswer:", list(r["choices"]), "ABCDEFGH".index(a) if isinstance(a, str) else int(a)
+    if "goal" in r and "sol1" in r:  # PIQA
+        return f"Question: {r['goal']}\nAnswer:", [r["sol1"], r["sol2"]], int(r["label"])
     raise ValueError(f"unrecognised task line (keys {sorted(r)})")
 
 
-def load_task(task_dir: str, task: str, limit: Optional[int] = None) -> List[Tuple[str, List[str], int]]:
+def example_pairs(r: dict) -> Tuple[List[str], List[str], int]:
+    """(context per choice, scored continuation per choice, correct index) of one task line. Most layouts
+    share one context and score " " + choice; Winogrande (sentence with a blank "_", option1 / option2,
+    answer "1" / "2") puts each option into the blank and scores the rest of the sentence after it."""
+    if "sentence" in r and "option1" in r:
+        i = r["sentence"].index("_")
+        before, after = r["sentence"][:i], r["sentence"][i + 1:]
+        opts = [r["option1"], r["option2"]]
+        return [before + o for o in opts], [after] * 2, int(r["answer"]) - 1
+    ctx, choices, label = normalize_example(r)
+    return [ctx] * len(choices), [" " + c for c in choices], label
+
+
+def load_task(task_dir: str, task: str, limit: Optional[int] = None) -> List[Tuple[List[str], List[str], int]]:
+    """``example_pairs`` of the first ``limit`` lines of ``<task_dir>/<task>.jsonl``."""
     path = os.path.join(task_dir, f"{task}.jsonl")
     out = []
     with open(path) as f:
         for line in f:
             if line.strip():
-                out.append(normalize_example(json.loads(line)))
+                out.append(example_pairs(json.loads(line)))
                 if limit is not None and len(out) >= limit:
                     break
     return out
@@ -121,14 +138,13 @@ def evaluate_tasks(scorer: Scorer, tok, tasks: Sequence[str], task_dir: str, lim
     for task in tasks:
         examples = load_task(task_dir, task, limit)
         seqs, starts, nbytes, spans = [], [], [], []
-        for ctx, choices, _ in examples:
-            c = tok.encode(ctx)
-            spans.append((len(seqs), len(choices)))
-            for ch in choices:
-                t = tok.encode(" " + ch)
+        for ctxs, conts, _ in examples:
+            spans.append((len(seqs), len(conts)))
+            for ctx, cont in zip(ctxs, conts):
+                c, t = tok.encode(ctx), tok.encode(cont)
                 seqs.append(c + t)
                 starts.append(len(c))
-                nbytes.append(max(len((" " + ch).encode("utf-8")), 1))
+                nbytes.append(max(len(cont.encode("utf-8")), 1))
         lps = scorer.score(seqs, starts)
         acc = acc_norm = 0
         for (first, k), (_, _, label) in zip(spans, examples):

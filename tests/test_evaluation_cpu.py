@@ -102,3 +102,22 @@ def test_evals_command_on_versions(tmp_path, capsys):
         saved = json.loads((tmp_path / "out" / f"v{v}.json").read_text())
         (r,) = saved["results"]
         assert r["task"] == "hellaswag" and r["n"] == 5 and 0.0 <= r["acc"] <= 1.0
+
+
+def test_piqa_and_winogrande_layouts(tmp_path):
+    ctxs, conts, label = ev.example_pairs({"goal": "g", "sol1": "a", "sol2": "b", "label": 1})
+    assert ctxs == ["Question: g\nAnswer:"] * 2 and conts == [" a", " b"] and label == 1
+    ctxs, conts, label = ev.example_pairs({"sentence": "The cup fell because _ was slippery.", "option1": "the cup",
+                                           "option2": "the table", "answer": "2"})
+    assert ctxs == ["The cup fell because the cup", "The cup fell because the table"]
+    assert conts == [" was slippery."] * 2 and label == 1
+    # scoring: each option is judged by the log-likelihood of the shared remainder in its own context
+    tok = ByteTokenizer()
+
+    class PrefersTable:
+        def score(self, seqs, starts):
+            return [0.0 if "table" in tok.decode(s[:st]) else -1.0 for s, st in zip(seqs, starts)]
+    (tmp_path / "winogrande.jsonl").write_text(json.dumps(
+        {"sentence": "It fell off _ today.", "option1": "the cup", "option2": "the table", "answer": "2"}) + "\n")
+    (r,) = ev.evaluate_tasks(PrefersTable(), tok, ["winogrande"], str(tmp_path))
+    assert r["acc"] == 1.0 and r["n"] == 1
