@@ -462,7 +462,7 @@ def cmd_serve(args):
     import time as _time
     from .serve import CompletionServer
     srv = CompletionServer(args.checkpoint, args.device or "cpu", args.tokenizer, args.rope_theta,
-                           max_tokens_cap=args.max_tokens_cap)
+                           model_name=args.model_name, max_tokens_cap=args.max_tokens_cap, template=args.template)
     port = srv.start(args.host, args.port)
     print(json.dumps({"serving": args.checkpoint, "port": port, "model": srv.model}), flush=True)
     try:
@@ -848,9 +848,13 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--device", help="torch device for the forward (default cpu)")
     p.set_defaults(fn=cmd_generate)
 
-    p = sp.add_parser("serve", help="OpenAI-style completion server for a checkpoint (/v1/completions)")
-    p.add_argument("checkpoint")
-    p.add_argument("--tokenizer", help="tokenizer JSON (text prompts); token-id prompts work without one")
+    p = sp.add_parser("serve", help="OpenAI-style server for a checkpoint (/v1/completions, /v1/chat/completions)")
+    p.add_argument("checkpoint", help="a safetensors file, or a directory holding model.safetensors")
+    p.add_argument("--tokenizer", help="tokenizer JSON, or 'bytes' (UTF-8 bytes, as the post-training commands "
+                                       "use without one); token-id prompts work without a tokenizer")
+    p.add_argument("--model-name", help="the model id the API reports (default: the file name)")
+    p.add_argument("--template", default="chatml", choices=["chatml", "llama", "zephyr"],
+                   help="chat template of /v1/chat/completions")
     p.add_argument("--host", default="0.0.0.0")
     p.add_argument("--port", type=int, default=8000)
     p.add_argument("--device", help="torch device for the forward (default cpu)")

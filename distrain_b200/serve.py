@@ -12,7 +12,12 @@ PyTorch formulation (``models/oracle.py``).
 Routes: ``POST /v1/completions`` with {"prompt": text or [token ids], "max_tokens", "temperature",
 "seed", "stop_token"} -> {"id", "object": "text_completion", "created", "model", "choices": [{"text",
 "token_ids", "index", "finish_reason"}], "usage": {"prompt_tokens", "completion_tokens",
-"total_tokens"}}; ``GET /v1/models``; ``GET /health``. Text prompts need a tokenizer file.
+"total_tokens"}}; ``POST /v1/chat/completions`` with {"messages": [{"role", "content"}], "max_tokens",
+"temperature", "seed", "template"} -> {"object": "chat.completion", "choices": [{"message": {"role":
+"assistant", "content"}, "finish_reason"}], "usage"}: the conversation is rendered with the chat
+template the model was fine-tuned with (chatml by default) and generation stops at the template's end
+marker; ``GET /v1/models``; ``GET /health``. Text needs a tokenizer (a file, or ``bytes`` for the UTF-8
+byte tokenizer of the post-training commands).
 """
 from __future__ import annotations
 
@@ -21,7 +26,7 @@ import json
 import threading
 import time
 import uuid
-from typing import List, Optional, Tuple
+from typing import Callable, List, Optional, Tuple
 
 import torch
 
@@ -78,10 +83,12 @@ class EngineLM:
 
 
 def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, seed: int = 0,
-           stop_token: Optional[int] = None, lm: Optional[EngineLM] = None) -> Tuple[List[int], str]:
+           stop_token: Optional[int] = None, lm: Optional[EngineLM] = None,
+           stop_fn: Optional[Callable[[List[int]], bool]] = None) -> Tuple[List[int], str]:
     """Appends up to ``max_tokens`` tokens to ``ids`` (greedy at temperature <= 0, else softmax sampling
     from a generator seeded with ``seed``); returns the new tokens and the finish reason ("length" or
-    "stop"). With ``lm`` the logits come from the CUDA engine, else from the PyTorch formulation."""
+    "stop": ``stop_token`` sampled, or ``stop_fn(new tokens)`` true). With ``lm`` the logits come from
+    the CUDA engine, else from the PyTorch formulation."""
     from .models import oracle
     dev = next(iter(sd.values())).device
     g = torch.Generator(device="cpu").manual_seed(int(seed))
@@ -100,7 +107,7 @@ def sample(sd, cfg, ids: List[int], max_tokens: int, temperature: float = 0.0, s
                 nxt = int(torch.multinomial(torch.softmax(z / temperature, -1), 1, generator=g))
             seq.append(nxt)
             out.append(nxt)
-            if stop_token is not None and nxt == stop_token:
+            if (stop_token is not None and nxt == stop_token) or (stop_fn is not None and stop_fn(out)):
                 return out, "stop"
     return out, "length"
 
@@ -123,15 +130,23 @@ class CompletionServer:
     forward is not re-entrant on one device)."""
 
     def __init__(self, checkpoint: str, device: str = "cpu", tokenizer: Optional[str] = None,
-                 rope_theta: Optional[float] = None, model_name: Optional[str] = None, max_tokens_cap: int = 1024):
+                 rope_theta: Optional[float] = None, model_name: Optional[str] = None, max_tokens_cap: int = 1024,
+                 template: str = "chatml"):
+        import os
+        if os.path.isdir(checkpoint):  # a model directory, as the reference's serve script takes
+            checkpoint = os.path.join(checkpoint, "model.safetensors")
         self.sd, self.cfg = load_model(checkpoint, device, rope_theta, min_len=max_tokens_cap + 64)
+        self.template = template
         # on a GPU the forward runs on the CUDA engine; its window covers the longest request
         self.lm = (EngineLM(self.sd, self.cfg, device, window=self.cfg.max_seq_len)
                    if torch.device(device).type == "cuda" else None)
         self.tok = None
-        if tokenizer:
-            from tokenizers import Tokenizer
-            self.tok = Tokenizer.from_file(tokenizer)
+        if tokenizer == "bytes":
+            from .alignment import ByteTokenizer
+            self.tok = ByteTokenizer()
+        elif tokenizer:
+            from .alignment import FileTokenizer
+            self.tok = FileTokenizer(tokenizer)
         self.model = model_name or checkpoint.rsplit("/", 1)[-1]
         self.cap = max_tokens_cap
         self._lock = threading.Lock()
@@ -146,7 +161,7 @@ class CompletionServer:
         if isinstance(prompt, list):
             ids = [int(t) for t in prompt]
         elif self.tok is not None:
-            ids = self.tok.encode(str(prompt)).ids
+            ids = self.tok.encode(str(prompt))
         else:
             return 400, {"error": {"message": "text prompts need a tokenizer (start with --tokenizer) or a list "
                                               "of token ids", "type": "invalid_request_error"}}
@@ -169,18 +184,56 @@ class CompletionServer:
                      "usage": {"prompt_tokens": len(ids), "completion_tokens": len(new),
                                "total_tokens": len(ids) + len(new)}}
 
+    def chat(self, req: dict) -> Tuple[int, dict]:
+        """Chat completion: the messages rendered with the chat template, the answer generated up to the
+        template's end marker (or max_tokens)."""
+        from .alignment import Message, render_chat
+        bad = lambda msg: (400, {"error": {"message": msg, "type": "invalid_request_error"}})
+        if self.tok is None:
+            return bad("chat needs a tokenizer (start with --tokenizer FILE, or --tokenizer bytes)")
+        msgs = req.get("messages")
+        if not isinstance(msgs, list) or not msgs or not all(
+                isinstance(m, dict) and m.get("role") in ("system", "user", "assistant") and
+                isinstance(m.get("content"), str) for m in msgs):
+            return bad("messages must be a non-empty list of {role: system | user | assistant, content}")
+        try:
+            segs = render_chat([Message(m["role"], m["content"]) for m in msgs] + [Message("assistant", "")],
+                               req.get("template", self.template))
+        except ValueError as e:
+            return bad(str(e))
+        end = segs[-1][0].strip()  # what the template appends to an (empty) answer: its end marker
+        ids = self.tok.encode("".join(t for t, _ in segs[:-1]))
+        n = int(req.get("max_tokens", 64))
+        if n < 0 or n > self.cap:
+            return bad(f"max_tokens must be in [0, {self.cap}]")
+        if any(t >= self.cfg.vocab_size for t in ids):
+            return bad("the tokenizer's ids do not fit the model's vocabulary")
+        with self._lock:
+            new, reason = sample(self.sd, self.cfg, ids, n, float(req.get("temperature", 0.0)),
+                                 int(req.get("seed", 0)), lm=self.lm,
+                                 stop_fn=lambda out: end in self.tok.decode(out[-64:]))
+        text = self.tok.decode(new)
+        if end in text:
+            text, reason = text[:text.index(end)], "stop"
+        return 200, {"id": f"chatcmpl-{uuid.uuid4().hex[:24]}", "object": "chat.completion",
+                     "created": int(time.time()), "model": self.model,
+                     "choices": [{"index": 0, "message": {"role": "assistant", "content": text.strip()},
+                                  "finish_reason": reason}],
+                     "usage": {"prompt_tokens": len(ids), "completion_tokens": len(new),
+                               "total_tokens": len(ids) + len(new)}}
+
     def handle_request(self, method: str, path: str, body: bytes) -> Tuple[int, dict]:
         route = path.split("?", 1)[0]
         if method == "GET" and route == "/health":
             return 200, {"status": "ok"}
         if method == "GET" and route == "/v1/models":
             return 200, {"object": "list", "data": [{"id": self.model, "object": "model", "owned_by": "distrain"}]}
-        if method == "POST" and route == "/v1/completions":
+        if method == "POST" and route in ("/v1/completions", "/v1/chat/completions"):
             try:
                 req = json.loads(body or b"{}")
             except ValueError:
                 return 400, {"error": {"message": "body is not JSON", "type": "invalid_request_error"}}
-            return self.complete(req)
+            return self.complete(req) if route == "/v1/completions" else self.chat(req)
         return 404, {"error": {"message": f"no route {method} {route}", "type": "not_found"}}
 
     # ── native HTTP server ──

@@ -72,3 +72,51 @@ def test_engine_window_ladder():
     assert EngineLM.window_sizes(128) == [128]
     assert EngineLM.window_sizes(100) == [100]
     assert EngineLM.window_sizes(4096) == [128, 256, 512, 1024, 2048, 4096]
+
+
+def test_chat_completions(tmp_path, monkeypatch):
+    """/v1/chat/completions: the conversation goes through the chat template, the answer stops at the
+    template's end marker, and the server takes a model directory and a model name."""
+    from distrain_b200 import serve
+    from distrain_b200.alignment import ByteTokenizer
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.utils.checkpoint import save_safetensors
+    cfg = ModelConfig(hidden_dim=32, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=64, vocab_size=260,
+                      max_seq_len=256, rope_theta=10000.0)
+    L = ParamLayout(cfg)
+    save_safetensors(L.to_state_dict(init_flat(L, seed=2)), str(tmp_path / "model.safetensors"))
+    srv = serve.CompletionServer(str(tmp_path), "cpu", tokenizer="bytes", model_name="tiny-chat", max_tokens_cap=64)
+    assert srv.model == "tiny-chat"
+    body = {"messages": [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}],
+            "max_tokens": 5}
+    st, out = srv.handle_request("POST", "/v1/chat/completions", json.dumps(body).encode())
+    assert st == 200, out
+    assert out["object"] == "chat.completion" and out["choices"][0]["message"]["role"] == "assistant"
+    assert out["usage"]["completion_tokens"] == 5 and out["choices"][0]["finish_reason"] == "length"
+    # the prompt is the chatml rendering up to the assistant header
+    tok = ByteTokenizer()
+    want = "<|im_start|>system\nbe brief<|im_end|>\n<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n"
+    assert out["usage"]["prompt_tokens"] == len(tok.encode(want))
+    # generation stops at the end marker, which is cut from the answer
+    reply = tok.encode("Hello!<|im_end|>\nextra")
+
+    def fake_sample(sd, cfg, ids, n, temperature=0.0, seed=0, stop_token=None, lm=None, stop_fn=None):
+        assert tok.decode(ids) == want
+        out_ids = []
+        for t in reply[:n]:
+            out_ids.append(t)
+            if stop_fn is not None and stop_fn(out_ids):
+                return out_ids, "stop"
+        return out_ids, "length"
+    monkeypatch.setattr(serve, "sample", fake_sample)
+    st, out = srv.handle_request("POST", "/v1/chat/completions", json.dumps(dict(body, max_tokens=40)).encode())
+    assert out["choices"][0]["message"]["content"] == "Hello!" and out["choices"][0]["finish_reason"] == "stop"
+    assert out["usage"]["completion_tokens"] == len(tok.encode("Hello!<|im_end|>"))
+    # invalid: no messages, unknown role, unknown template
+    for bad in ({"messages": []}, {"messages": [{"role": "robot", "content": "x"}]},
+                {"messages": [{"role": "user", "content": "x"}], "template": "alpaca"}):
+        assert srv.handle_request("POST", "/v1/chat/completions", json.dumps(bad).encode())[0] == 400
+    # without a tokenizer chat is refused
+    srv2 = serve.CompletionServer(str(tmp_path / "model.safetensors"), "cpu", max_tokens_cap=8)
+    assert srv2.handle_request("POST", "/v1/chat/completions", json.dumps(body).encode())[0] == 400
