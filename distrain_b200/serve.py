@@ -161,7 +161,10 @@ class CompletionServer:
         if isinstance(prompt, list):
             ids = [int(t) for t in prompt]
         elif self.tok is not None:
-            ids = self.tok.encode(str(prompt))
+            # plain prompts are tokenized like the pretraining shards (with the tokenizer's own special
+            # tokens, e.g. a leading BOS); chat prompts like the fine-tuning commands (without)
+            raw = getattr(self.tok, "tok", None)
+            ids = raw.encode(str(prompt)).ids if raw is not None else self.tok.encode(str(prompt))
         else:
             return 400, {"error": {"message": "text prompts need a tokenizer (start with --tokenizer) or a list "
                                               "of token ids", "type": "invalid_request_error"}}
