@@ -444,7 +444,11 @@ def cmd_generate(args):
                          min_len=args.max_tokens + 64)
     ids = [int(x) for x in args.prompt_ids.split(",")] if args.prompt_ids else [1]
     tok = None
-    if args.tokenizer:
+    if args.tokenizer == "bytes":  # the UTF-8 byte tokenizer of the post-training commands
+        from .alignment import ByteTokenizer
+        tok = ByteTokenizer()
+        ids = tok.encode(args.prompt)
+    elif args.tokenizer:
         from tokenizers import Tokenizer
         tok = Tokenizer.from_file(args.tokenizer)
         ids = tok.encode(args.prompt).ids
@@ -840,7 +844,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("checkpoint")
     p.add_argument("--prompt", default="The")
     p.add_argument("--prompt-ids")
-    p.add_argument("--tokenizer")
+    p.add_argument("--tokenizer", help="tokenizer JSON, or 'bytes' (UTF-8 bytes)")
     p.add_argument("--max-tokens", type=int, default=32)
     p.add_argument("--temperature", type=float, default=0.0)
     p.add_argument("--seed", type=int, default=0)

@@ -132,3 +132,21 @@ def test_calibration_probe_timeout_counts_as_not_fitting(monkeypatch):
         return sp.CompletedProcess(cmd, 0)
     monkeypatch.setattr(cli.subprocess, "run", fake_run)
     assert cli.calibrate_batch_size("ck", 128) == 10
+
+
+def test_generate_with_byte_tokenizer(tmp_path):
+    """generate --tokenizer bytes: the prompt's UTF-8 bytes (ids 3 + byte) and the decoded text."""
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    from distrain_b200.utils.checkpoint import save_safetensors
+    cfg = ModelConfig(hidden_dim=32, num_layers=1, num_heads=4, num_kv_heads=2, ffn_hidden_dim=64, vocab_size=260,
+                      max_seq_len=64)
+    L = ParamLayout(cfg)
+    ck = str(tmp_path / "m.safetensors")
+    save_safetensors(L.to_state_dict(init_flat(L, seed=1)), ck)
+    p = run(["generate", ck, "--prompt", "hi", "--tokenizer", "bytes", "--max-tokens", "3"])
+    assert p.returncode == 0, p.stderr
+    r = json.loads(p.stdout.strip().splitlines()[-1])
+    assert r["ids"][:2] == [3 + ord("h"), 3 + ord("i")] and len(r["ids"]) == 5
+    assert isinstance(r["text"], str) and r["text"].startswith("hi")
+
