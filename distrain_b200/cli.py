@@ -5,6 +5,8 @@ status, config, eval, gpu-stress-test, baseline, generate. Service / tooling com
 (the HTTP coordinator, env-configured like coordinator/src/main.rs:141-188), prepare-data (the data-prep
 script's random-shard mode), micro-cluster (coordinator + N CPU node processes on one host), train-box
 (every GPU of this box as one node of the in-box protocol; launched with ``torch.distributed.run``).
+The reference's post-training scripts (scripts/run_sft.py, run_dpo.py, run_evals.py, export_hf.py,
+serve.py) are the commands sft, dpo, evals, export-hf and serve.
 """
 from __future__ import annotations
 
@@ -365,8 +367,23 @@ def cmd_config(args):
 
 
 def _eval_loss(sd, cfg, batches, device):
+    """Mean next-token loss over ``batches`` ([B, S] token ids each): on a GPU through the CUDA engine's
+    forward-only pass, else through the fp32 formulation."""
     import torch
     from .models import oracle
+    if torch.device(device).type == "cuda" and batches:
+        from .models.engine import TrainEngine
+        from .models.params import ParamLayout
+        L = ParamLayout(cfg)
+        flat = torch.zeros(L.total)
+        L.load_state_dict(flat, {k: v.detach().float().cpu() for k, v in sd.items()})
+        B, S = batches[0].shape
+        eng = TrainEngine(cfg, B, S, device=device, flat_init=flat, inference=True)
+        tot = 0.0
+        for b in batches:
+            eng.set_tokens(b.to(device).int())
+            tot += float(eng.forward_loss(0).double().mean())
+        return tot / len(batches)
     p = {k: v.to(device) for k, v in sd.items()}
     tot = 0.0
     with torch.no_grad():

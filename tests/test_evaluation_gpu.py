@@ -52,3 +52,19 @@ def test_inference_engine_matches_training_engine():
     assert torch.equal(a, b)
     with pytest.raises(RuntimeError):
         inf.forward_backward()
+
+
+def test_held_out_loss_on_the_engine():
+    """cli eval's loss on a GPU (forward-only engine) against the fp32 formulation on the CPU."""
+    from distrain_b200.cli import _eval_loss
+    from distrain_b200.config import ModelConfig
+    from distrain_b200.models.params import ParamLayout, init_flat
+    cfg = ModelConfig(hidden_dim=128, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_dim=256, vocab_size=512,
+                      max_seq_len=128, rope_theta=10000.0)
+    L = ParamLayout(cfg)
+    sd = L.to_state_dict(init_flat(L, 0.05, 6))
+    g = torch.Generator().manual_seed(2)
+    batches = [torch.randint(0, 512, (3, 65), generator=g, dtype=torch.int32) for _ in range(2)]
+    gpu = _eval_loss(sd, cfg, batches, "cuda:0")
+    cpu = _eval_loss(sd, cfg, batches, "cpu")
+    assert abs(gpu - cpu) < 5e-3, (gpu, cpu)
